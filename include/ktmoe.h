@@ -1,0 +1,133 @@
+/*
+ * ktmoe — tritify's exact-integer Mixture-of-Experts FFN layer on NVIDIA B200 (sm_100a), behind a plain C ABI.
+ *
+ * Every entry point returns an int status (KTMOE_OK = 0) and never aborts; results come back through out-parameters.
+ * Pointers are plain host pointers unless the name says "dev". No CUDA or torch type appears in a signature: streams
+ * are passed as `void*` (a cudaStream_t, or NULL for the context's own stream).
+ *
+ * Reference interfaces replaced (paths within the tritify project):
+ *   LinearBackend::linear / linear_weights   crates/01-engine/kt-core/src/backend.rs:46-59
+ *   kt-cuda's C ABI (kt_cuda_*)              crates/02-runtime/kt-cuda/src/digit_gemm.cu:86-147, device.rs:9-38
+ *   Module::forward_int of MoeMlp            crates/01-engine/kt-core/src/layers.rs:1061-1073
+ *   MoeMlp::route                            layers.rs:826-862
+ *   QuantLinear::from_weights / with_bias    layers.rs:225-257
+ *   IntTensor::from_reals                    crates/01-engine/kt-core/src/tensor.rs:106-116
+ *   SigmoidScore::new (coded bias)           crates/01-engine/kt-core/src/router.rs:37-51
+ *   Scale {mant, shift}                      crates/00-kernels/kt-int/src/lib.rs:175-178
+ */
+#ifndef KTMOE_H
+#define KTMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define KTMOE_OK 0
+#define KTMOE_ERR_CUDA 1          /* a CUDA runtime/driver call failed (ktmoe_last_error has the message) */
+#define KTMOE_ERR_ARG 2           /* an argument is invalid (null, negative, inconsistent shape) */
+#define KTMOE_ERR_RANGE 3         /* a code lies outside +-WLEVELS (265720): the digit planes cannot hold it */
+#define KTMOE_ERR_KERNEL 4        /* a kernel reported a bounded wait that expired (no result was produced) */
+#define KTMOE_ERR_UNSUPPORTED 5   /* a configuration outside what this build implements */
+#define KTMOE_ERR_NO_DEVICE 6     /* no sm_100 device, or the device index does not exist */
+#define KTMOE_ERR_STATE 7         /* the layer is incomplete (a weight not set) */
+
+/* A non-negative fixed-point scale mant * 2^-shift (kt-int Scale; mant == 0 means exactly zero). */
+typedef struct ktmoe_scale {
+    int64_t mant;
+    int32_t shift;
+} ktmoe_scale;
+
+typedef struct ktmoe_ctx ktmoe_ctx;     /* one device, its stream and resident-weight cache */
+typedef struct ktmoe_layer ktmoe_layer; /* one MoE layer's resident weights and scratch */
+
+/* Layer shape and knobs (MoeMlp: layers.rs:661-674; MoeArch wiring: crates/03-models/kt-model-moe/src/lib.rs:456-501). */
+typedef struct ktmoe_layer_config {
+    int32_t d_model;        /* dim: router in_features */
+    int32_t n_experts;      /* E: router out_features (1..512) */
+    int32_t d_ff;           /* routed expert hidden size */
+    int32_t top_k;          /* 1..min(E, 16) */
+    int32_t norm_topk_prob; /* 1: normalise over the top-k codes; 0: over all E (softmax) or 2^20 (sigmoid) */
+    int32_t router_score;   /* 0: softmax (OLMoE, Mixtral, Qwen-MoE); 1: sigmoid with selection bias (GLM-4.5) */
+    int32_t shared_d_ff;    /* hidden size of the unweighted shared expert, 0 for none */
+} ktmoe_layer_config;
+
+/* ── devices and contexts (kt_cuda_device_count / kt_cuda_device_info) ── */
+int ktmoe_device_count(int* n);
+int ktmoe_open(int device, ktmoe_ctx** out);
+int ktmoe_close(ktmoe_ctx* ctx);
+const char* ktmoe_error_string(int status);
+/* The last error message recorded on this context (never NULL). */
+const char* ktmoe_last_error(const ktmoe_ctx* ctx);
+/* The context's CUDA stream (a cudaStream_t), for callers that order their own work with it. */
+void* ktmoe_stream(ktmoe_ctx* ctx);
+
+/* ── LinearBackend (backend.rs:46-59): Y[r,o] = sum_k x[r*k+i]*w[o*k+i], i64, x rows x k, w out x k ──
+ * Host pointers; synchronous. Codes beyond +-WLEVELS return KTMOE_ERR_RANGE (the reference hands such calls to its
+ * Portable CPU kernel, counted; this library has no CPU path). Any k >= 1 is exact: long k is split into chunks whose
+ * int32 plane sums cannot overflow, added in int64. */
+int ktmoe_linear(ktmoe_ctx* ctx, const int32_t* x, const int32_t* w, int64_t rows, int64_t out, int64_t k, int64_t* y);
+/* The same, with the weights kept resident on the device under `weight_id` (WeightId, backend.rs:22-35). The codes
+ * behind an id must never change. */
+int ktmoe_linear_weights(ktmoe_ctx* ctx, uint64_t weight_id, const int32_t* x, const int32_t* w, int64_t rows,
+                         int64_t out, int64_t k, int64_t* y);
+/* Resident-weight budget in bytes (LRU eviction; a weight larger than the budget is used once and dropped). */
+int ktmoe_set_weight_budget(ktmoe_ctx* ctx, uint64_t bytes);
+int ktmoe_resident_bytes(ktmoe_ctx* ctx, uint64_t* bytes);
+
+/* ── the MoE layer (MoeMlp) ── */
+int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_layer** out);
+int ktmoe_layer_destroy(ktmoe_layer* layer);
+/* Router codes [E][d_model] (QuantLinear w_codes, row-major) and w_scale; bias_codes [E] + bias_scale from
+ * QuantLinear::with_bias, or NULL for no bias. */
+int ktmoe_layer_set_router(ktmoe_layer* layer, const int32_t* codes, ktmoe_scale w_scale, const int64_t* bias_codes,
+                           ktmoe_scale bias_scale);
+/* Sigmoid router only: the coded selection bias [E], round(bias * 2^20) (SigmoidScore::new). */
+int ktmoe_layer_set_sigmoid_bias(ktmoe_layer* layer, const int64_t* bias_codes);
+/* Expert e's SwiGLU: gate [d_ff][d_model], up [d_ff][d_model], down [d_model][d_ff] codes and scales. */
+int ktmoe_layer_set_expert(ktmoe_layer* layer, int32_t e, const int32_t* gate, ktmoe_scale gate_scale,
+                           const int32_t* up, ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale);
+/* The shared expert (layers.rs:741-745): gate/up [shared_d_ff][d_model], down [d_model][shared_d_ff]. */
+int ktmoe_layer_set_shared(ktmoe_layer* layer, const int32_t* gate, ktmoe_scale gate_scale, const int32_t* up,
+                           ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale);
+/* Module::forward_int: x [rows][d_model] at x_scale -> y [rows][d_model] at *y_scale. Host buffers; synchronous. */
+int ktmoe_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                  ktmoe_scale* y_scale);
+/* The same on device buffers, ordered on `stream` (NULL: the context stream) and not synchronised: x_dev and y_dev
+ * hold rows x d_model int32, x_scale_dev and y_scale_dev one ktmoe_scale each. Kernel errors surface on the next
+ * ktmoe_sync. */
+int ktmoe_forward_dev(ktmoe_layer* layer, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
+                      int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream);
+/* Wait for the context's stream (and `stream` if not NULL); reports a kernel error word if one was raised. */
+int ktmoe_sync(ktmoe_ctx* ctx, void* stream);
+/* MoeMlp::route for each row: experts [rows][top_k] (top-k order), ec [rows][top_k] codes, sumc [rows]. */
+int ktmoe_route(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* experts,
+                int64_t* ec, int64_t* sumc);
+/* Kernel launches of this library on the context since open (the device work is all this library's own kernels). */
+int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
+
+/* Diagnostics: copy an internal buffer of the last forward or route (which = 0: router logits [rows][E] int32,
+ * 1: their scales [rows], 2: per-token combine outputs [rows][d_model] int32, 3: their scales [rows]). */
+int ktmoe_layer_debug_fetch(ktmoe_layer* layer, int32_t which, void* host, int64_t bytes);
+
+/* ── host-side, offline preparation (f64, as the reference does it once on the host) ── */
+int ktmoe_quantize_weights(const float* w, int64_t n, int32_t* codes, ktmoe_scale* scale);
+/* Returns KTMOE_OK; *has_bias = 0 when the bias is all zero (the reference then keeps none). */
+int ktmoe_quantize_bias(const float* b, int64_t n, int64_t* codes, ktmoe_scale* scale, int32_t* has_bias);
+int ktmoe_code_sigmoid_bias(const float* b, int64_t n, int64_t* codes);
+int ktmoe_from_reals(const float* v, int64_t n, int32_t* data, ktmoe_scale* scale);
+/* The three code tables: kind 0 router exp, 1 SiLU, 2 sigmoid; codes has 65536 entries. */
+int ktmoe_table(int32_t kind, int64_t* codes, ktmoe_scale* inv_step, int64_t* lo_index, ktmoe_scale* code_scale);
+/* Synthetic inputs defined by this build: elements [offset, offset + n) of the N(0, sigma) stream `seed` (splitmix64
+ * + Box-Muller in f64, cast to f32), and the reference's LCG uniform integers in [lo, hi]. */
+int ktmoe_synth_normal(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out);
+int ktmoe_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, int64_t n, int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KTMOE_H */

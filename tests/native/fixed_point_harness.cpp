@@ -1,0 +1,37 @@
+// TEST HARNESS: compiles the product's host+device fixed-point header (tritify_b200/csrc/fixed_point.cuh) for the
+// host, so its exact arithmetic can be compared with the oracle on the CPU. Exposes a C API for ctypes.
+#include "fixed_point.cuh"
+
+extern "C" {
+typedef struct {
+    int64_t mant;
+    int32_t shift;
+} fp_scale;
+
+static inline kt::Scale S(fp_scale s) { return kt::Scale{s.mant, s.shift}; }
+static inline fp_scale C(kt::Scale s) { return fp_scale{s.mant, s.shift}; }
+
+fp_scale fp_from_ratio(uint64_t nh, uint64_t nl, uint64_t dh, uint64_t dl) {
+    return C(kt::from_ratio(((kt::u128)nh << 64) | nl, ((kt::u128)dh << 64) | dl));
+}
+int fp_ge(fp_scale a, fp_scale b) { return kt::scale_ge(S(a), S(b)) ? 1 : 0; }
+fp_scale fp_mul(fp_scale a, fp_scale b) { return C(kt::scale_mul(S(a), S(b))); }
+int64_t fp_apply(fp_scale s, int64_t v) { return kt::scale_apply(S(s), v); }
+fp_scale fp_recip(fp_scale s) { return C(kt::scale_recip(S(s))); }
+int32_t fp_requant_act(int64_t v, int64_t den) { return kt::requant_act(v, den); }
+int32_t fp_requant_dyn(int64_t v, int64_t lvl, int64_t den) { return kt::requant_dyn(v, lvl, den); }
+int32_t fp_quant_to(int32_t d, int64_t xmax) { return kt::quant_to(d, xmax); }
+void fp_split(int32_t v, int8_t* d) { kt::split_digits(v, d[0], d[1], d[2]); }
+int64_t fp_recombine(int32_t a, int32_t b, int32_t c, int32_t d, int32_t e) { return kt::recombine(a, b, c, d, e); }
+
+// Batched forms for speed.
+void fp_requant_act_n(const int64_t* v, const int64_t* den, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::requant_act(v[i], den[i]);
+}
+void fp_quant_to_n(const int32_t* d, const int64_t* xmax, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::quant_to(d[i], xmax[i]);
+}
+void fp_apply_n(const fp_scale* s, const int64_t* v, int64_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::scale_apply(S(s[i]), v[i]);
+}
+}

@@ -1,0 +1,119 @@
+"""The product's exact fixed-point source (tritify_b200/csrc/fixed_point.cuh, the same header the kernels include),
+compiled for the host and compared with the oracle's restatement of kt-int and kt-core on seeded inputs."""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+class FpScale(ctypes.Structure):
+    _fields_ = [("mant", ctypes.c_int64), ("shift", ctypes.c_int32)]
+
+
+@pytest.fixture(scope="module")
+def fp(tmp_path_factory):
+    out = str(tmp_path_factory.mktemp("fp") / "libfp.so")
+    src = os.path.join(ROOT, "tests", "native", "fixed_point_harness.cpp")
+    subprocess.run(["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-x", "c++", "-I",
+                    os.path.join(ROOT, "tritify_b200", "csrc"), src, "-o", out], check=True)
+    L = ctypes.CDLL(out)
+    P = ctypes.POINTER
+    L.fp_from_ratio.argtypes = [ctypes.c_uint64] * 4
+    L.fp_from_ratio.restype = FpScale
+    L.fp_ge.argtypes = [FpScale, FpScale]
+    L.fp_mul.argtypes = [FpScale, FpScale]
+    L.fp_mul.restype = FpScale
+    L.fp_apply.argtypes = [FpScale, ctypes.c_int64]
+    L.fp_apply.restype = ctypes.c_int64
+    L.fp_recip.argtypes = [FpScale]
+    L.fp_recip.restype = FpScale
+    L.fp_requant_act.argtypes = [ctypes.c_int64, ctypes.c_int64]
+    L.fp_requant_act.restype = ctypes.c_int32
+    L.fp_quant_to.argtypes = [ctypes.c_int32, ctypes.c_int64]
+    L.fp_quant_to.restype = ctypes.c_int32
+    L.fp_split.argtypes = [ctypes.c_int32, P(ctypes.c_int8)]
+    L.fp_requant_act_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    L.fp_quant_to_n.argtypes = [P(ctypes.c_int32), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    return L
+
+
+def _t(s):
+    return (int(s.mant), int(s.shift))
+
+
+def _lcg(seed):
+    s = seed
+    while True:
+        s = (s * 6364136223846793005 + 1442695040888963407) & ((1 << 64) - 1)
+        yield s
+
+
+def test_from_ratio_mul_recip_ge_apply_equal_the_oracle(fp, oracle):
+    g = _lcg(0x5CA1E)
+    M = (1 << 64) - 1
+    for i in range(6000):
+        bits_n = 1 + next(g) % 100
+        bits_d = 1 + next(g) % 90
+        num = (next(g) | (next(g) << 64)) & ((1 << bits_n) - 1) or 1
+        den = (next(g) | (next(g) << 64)) & ((1 << bits_d) - 1) or 1
+        a = fp.fp_from_ratio(num >> 64, num & M, den >> 64, den & M)
+        assert _t(a) == oracle.from_ratio(num, den), (num, den)
+        b = oracle.from_ratio(next(g) % (1 << 50) + 1, next(g) % (1 << 40) + 1)
+        bs = FpScale(*b)
+        assert _t(fp.fp_mul(a, bs)) == oracle.mul(_t(a), b)
+        assert bool(fp.fp_ge(a, bs)) == oracle.ge(_t(a), b)
+        assert bool(fp.fp_ge(bs, a)) == oracle.ge(b, _t(a))
+        if a.mant:  # the reference asserts a non-zero scale in recip (kt-int lib.rs:276)
+            assert _t(fp.fp_recip(a)) == oracle.recip(_t(a))
+        v = (next(g) >> 1) - (1 << 62)
+        v >>= next(g) % 60
+        assert fp.fp_apply(a, v) == oracle.apply(_t(a), v), (a.mant, a.shift, v)
+    # equal values with different representations compare equal both ways
+    assert fp.fp_ge(FpScale(2, 1), FpScale(1, 0)) and fp.fp_ge(FpScale(1, 0), FpScale(2, 1))
+    assert fp.fp_ge(FpScale(0, 0), FpScale(0, 5)) and not fp.fp_ge(FpScale(0, 0), FpScale(1, 0))
+
+
+def test_requant_act_and_quant_to_equal_the_oracle(fp, oracle):
+    rng = np.random.default_rng(7)
+    n = 200000
+    den = rng.integers(1, 1 << 62, size=n, dtype=np.int64) >> rng.integers(0, 61, size=n)
+    den = np.maximum(den, 1)
+    v = (rng.integers(-(1 << 62), 1 << 62, size=n, dtype=np.int64) % (den + 1)) * rng.choice([-1, 1], size=n)
+    v[:1000] = den[:1000]  # the extremes: |v| == den maps to exactly ±2^28
+    v[1000:2000] = -den[1000:2000]
+    v[2000:2100] = 0
+    out = np.empty(n, dtype=np.int32)
+    P = ctypes.POINTER
+    fp.fp_requant_act_n(v.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)),
+                        out.ctypes.data_as(P(ctypes.c_int32)), n)
+    idx = rng.choice(n, 4000, replace=False)
+    want = [oracle.requant_dyn(int(v[i]), 1 << 28, int(den[i])) for i in idx]
+    assert list(out[idx]) == want
+    assert (out[:1000] == 1 << 28).all() and (out[1000:2000] == -(1 << 28)).all()
+
+    xmax = rng.integers(1, 1 << 31, size=n, dtype=np.int64)
+    d = (rng.integers(-(1 << 31), 1 << 31, size=n, dtype=np.int64) % (xmax + 1)).astype(np.int32)
+    q = np.empty(n, dtype=np.int32)
+    fp.fp_quant_to_n(d.ctypes.data_as(P(ctypes.c_int32)), xmax.ctypes.data_as(P(ctypes.c_int64)),
+                     q.ctypes.data_as(P(ctypes.c_int32)), n)
+    for i in idx[:2000]:
+        assert q[i] == oracle.quant_to(np.array([d[i]]), int(xmax[i]))[0]
+    assert np.abs(q).max() <= 265720
+
+
+def test_digit_split_covers_every_code(fp):
+    """kt-cuda/src/tests.rs:21-33: every code in ±WLEVELS is three digits |d| <= 40 and back."""
+    d = (ctypes.c_int8 * 3)()
+    for v in list(range(-265720, -265000)) + list(range(-3000, 3000)) + list(range(265000, 265721)):
+        fp.fp_split(v, d)
+        assert all(abs(x) <= 40 for x in d)
+        assert d[0] + 81 * d[1] + 6561 * d[2] == v
+    fp.fp_split(265720, d)
+    assert list(d) == [40, 40, 40]
+    fp.fp_split(-265720, d)
+    assert list(d) == [-40, -40, -40]

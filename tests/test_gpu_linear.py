@@ -1,0 +1,96 @@
+"""LinearBackend on the B200 (ktmoe_linear / ktmoe_linear_weights) against the reference's equality and residency
+gates (crates/02-runtime/kt-runtime/src/gate.rs:26-140): the corpus must hash to the reference's own SHA-256."""
+
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import tritify_b200 as tb
+from tritify_b200 import _native
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIT = json.load(open(os.path.join(HERE, "golden", "golden.json")))["reference_literals"]
+WL = tb.WLEVELS
+
+
+def test_doc_example(ctx):
+    ex = LIT["linear_doc_example"]["value"]
+    assert list(ctx.linear(ex["x"], ex["w"], ex["rows"], ex["out"], ex["k"])) == ex["y"]
+
+
+def test_corpus_hash_is_the_references(ctx, oracle):
+    h = hashlib.sha256()
+    diverged = []
+    for (label, r, o, k, x, w) in oracle.corpus():
+        y = ctx.linear(x, w, r, o, k)
+        if not (y == oracle.linear(x, w, r, o, k)).all():
+            diverged.append(label)
+        h.update(y.astype("<i8").tobytes())
+    assert not diverged, f"cases that differ from the CPU path: {diverged}"
+    assert h.hexdigest() == LIT["corpus_sha256"]["value"]
+
+
+def test_the_bound_case_beyond_one_flush(ctx):
+    """gate.rs:61-66: k = (KT_FLUSH + 1)·16, every code +WLEVELS, one weight row +WLEVELS and one -WLEVELS."""
+    k = LIT["k_beyond_flush"]["value"]
+    x = np.full(k, WL, np.int32)
+    w = np.concatenate([np.full(k, WL, np.int32), np.full(k, -WL, np.int32)])
+    want = k * WL * WL
+    assert list(ctx.linear(x, w, 1, 2, k)) == [want, -want]
+
+
+def test_long_k_beyond_one_exact_chunk(ctx, oracle):
+    """K above the kernel's single-pass bound (447,392) is split and the int64 partials added."""
+    k = 600_001
+    rng = np.random.default_rng(1)
+    x = rng.integers(-WL, WL + 1, size=2 * k, dtype=np.int32)
+    w = rng.integers(-WL, WL + 1, size=3 * k, dtype=np.int32)
+    assert (ctx.linear(x, w, 2, 3, k) == oracle.linear(x, w, 2, 3, k)).all()
+    xe = np.full(k, WL, np.int32)
+    assert list(ctx.linear(xe, np.concatenate([xe, -xe]), 1, 2, k)) == [k * WL * WL, -k * WL * WL]
+
+
+@pytest.mark.parametrize("rows,out,k", [(1, 1, 1), (17, 33, 50), (16, 128, 128), (64, 256, 2048), (65, 129, 129),
+                                        (200, 300, 1000), (3, 1408, 2048), (97, 2048, 1408)])
+def test_random_shapes_equal_the_cpu_path(ctx, oracle, rows, out, k):
+    rng = np.random.default_rng(rows * 1000 + out)
+    x = rng.integers(-WL, WL + 1, size=rows * k, dtype=np.int32)
+    w = rng.integers(-WL, WL + 1, size=out * k, dtype=np.int32)
+    got = ctx.linear(x, w, rows, out, k)
+    want = oracle.linear(x, w, rows, out, k)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, f"{bad.size} of {got.size} differ; first at {bad[:5]}: {got[bad[:5]]} vs {want[bad[:5]]}"
+
+
+def test_residency_gate(oracle):
+    """gate.rs:109-140: the corpus twice, then two weights of one shape interleaved; and with a 1-byte budget."""
+    for budget in [None, 1]:
+        c = tb.Context(0)
+        if budget:
+            c.set_weight_budget(budget)
+        corpus = oracle.corpus()
+        for p in range(2):
+            for i, (label, r, o, k, x, w) in enumerate(corpus):
+                assert (c.linear(x, w, r, o, k, weight_id=100 + i) == oracle.linear(x, w, r, o, k)).all(), (p, label)
+        x = corpus[3][4]
+        t0 = tb.lcg_uniform(11, -WL, WL, 64 * 1023)
+        t1 = tb.lcg_uniform(12, -WL, WL, 64 * 1023)
+        for _ in range(4):
+            for wid, w in [(1, t0), (2, t1)]:
+                assert (c.linear(x, w, 4, 64, 1023, weight_id=wid) == oracle.linear(x, w, 4, 64, 1023)).all()
+        assert (c.resident_bytes() > 0) == (budget is None)
+        c.close()
+
+
+def test_codes_outside_wlevels_fail_loudly(ctx):
+    with pytest.raises(tb.KtmoeError) as e:
+        ctx.linear(np.array([WL + 1, 2], np.int32), np.array([3, 4], np.int32), 1, 1, 2)
+    assert e.value.status == _native.ERR_RANGE
+    with pytest.raises(tb.KtmoeError):
+        ctx.linear(np.array([1, 2], np.int32), np.array([np.iinfo(np.int32).min, 4], np.int32), 1, 1, 2)
+    # the context stays usable
+    assert list(ctx.linear(np.array([1, 2], np.int32), np.array([3, 4], np.int32), 1, 1, 2)) == [11]

@@ -1,0 +1,137 @@
+"""The CPU oracle (test infrastructure) pinned to the reference's own golden vectors and properties."""
+
+import hashlib
+import json
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "golden.json")))
+LIT = GOLDEN["reference_literals"]
+
+
+def test_corpus_hash_is_the_references(oracle):
+    """kt-runtime/src/tests_cuda.rs:9: SHA-256 over every i64 accumulator of the equality-gate corpus."""
+    h = hashlib.sha256()
+    for (_, r, o, k, x, w) in oracle.corpus():
+        h.update(oracle.linear(x, w, r, o, k).astype("<i8").tobytes())
+    assert h.hexdigest() == LIT["corpus_sha256"]["value"]
+
+
+def test_kt_int_doc_examples(oracle):
+    """kt-int/src/lib.rs:35-39."""
+    three_q = oracle.from_ratio(3, 4)
+    assert oracle.apply(three_q, 8) == LIT["from_ratio_3_4_apply_8"]["value"]
+    assert oracle.apply(oracle.mul(three_q, oracle.from_ratio(4, 3)), 9) == \
+        LIT["three_quarters_times_four_thirds_apply_9"]["value"]
+    assert oracle.isqrt_u128(144) == LIT["isqrt_144"]["value"]
+    # kt-int lib.rs:246-252
+    assert oracle.apply(oracle.from_ratio(0, 5), 123) == 0
+    assert oracle.apply((0, 0), 999) == 0
+    four = oracle.from_ratio(4, 1)
+    for v in [-7, 0, 1, 1000, 1_000_000_000]:
+        assert oracle.apply(four, v) == 4 * v
+
+
+def test_backend_doc_example(oracle):
+    """kt-core/src/backend.rs:12-15."""
+    ex = LIT["linear_doc_example"]["value"]
+    y = oracle.linear(np.array(ex["x"]), np.array(ex["w"]), ex["rows"], ex["out"], ex["k"])
+    assert list(y) == ex["y"]
+
+
+def test_digit_bounds_are_the_references():
+    """kt-cuda/src/digits.rs:20-23 and tests.rs:68, :88."""
+    WL = 265720
+    assert 40 * (1 + 81 + 81 * 81) == WL
+    kt_flush = (2**31 - 1) // (16 * 40 * 40)
+    assert (kt_flush + 1) * 16 == LIT["k_beyond_flush"]["value"]
+    assert (2**63 - 1) // (WL * WL) == LIT["k_max"]["value"]
+
+
+def test_scale_ops_track_f64(oracle):
+    """kt-int lib.rs:570-621: from_ratio, mul, apply and recip within their stated f64 bounds."""
+    rng = np.random.default_rng(5)
+    for _ in range(2000):
+        num, den = int(rng.integers(1, 1 << 50)), int(rng.integers(1, 1 << 50))
+        m, s = oracle.from_ratio(num, den)
+        assert abs(m * 2.0 ** -s - num / den) <= 1e-8 * num / den
+        a = oracle.from_f64(1e-6 + rng.random())
+        b = oracle.from_f64(1e-3 + rng.random())
+        p = oracle.mul(a, b)
+        want = a[0] * 2.0 ** -a[1] * b[0] * 2.0 ** -b[1]
+        assert abs(p[0] * 2.0 ** -p[1] - want) <= 1e-8 * want
+        v = int(rng.integers(-(1 << 39), 1 << 39))
+        assert abs(oracle.apply(p, v) - round(v * p[0] * 2.0 ** -p[1])) <= 1
+        x = 1e-7 + rng.random() * 100
+        r = oracle.recip(oracle.from_f64(x))
+        assert abs(r[0] * 2.0 ** -r[1] - 1 / x) <= 1e-8 / x
+
+
+def test_tables_match_golden_and_end_codes(oracle):
+    for kind, name in enumerate(["exp", "silu", "sigmoid"]):
+        codes, inv_step, lo_index, code_scale = oracle.table(kind)
+        g = GOLDEN["tables"][name]
+        assert hashlib.sha256(codes.astype("<i8").tobytes()).hexdigest() == g["codes_sha256"]
+        assert list(inv_step) == g["inv_step"] and lo_index == g["lo_index"] and list(code_scale) == g["code_scale"]
+    exp_codes = oracle.table(0)[0]
+    assert exp_codes[-1] == 1 << 20  # exp(0)·2^20
+    sig = oracle.table(2)[0]
+    assert [int(sig[0]), int(sig[-1])] == [0, 1 << 20] == LIT["sigmoid_end_codes"]["value"]
+
+
+@pytest.mark.parametrize("name", ["tiny_softmax", "tiny_softmax_norm_one_row", "tiny_softmax_37rows",
+                                  "tiny_router_bias", "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row",
+                                  "small_shared_softmax"])
+def test_oracle_reproduces_golden_cases(oracle, name):
+    import cases
+
+    c = cases.CASES[name]
+    g = GOLDEN["cases"][name]
+    x = cases.make_x(c)
+    assert cases.sha(x) == g["x_f32_sha256"], "the generator's bytes changed"
+    xi, xs = oracle.from_reals_f32(x)
+    m = cases.build_oracle(c, oracle)
+    y, ys = m.forward(xi, xs)
+    assert cases.out_hashes(y, ys) == g["output"]
+
+
+@pytest.mark.parametrize("rows", [1, 5])
+def test_the_seam_is_a_numeric_no_op(oracle, rows):
+    """kt-core/src/tests.rs:156-181 and tests_glm.rs:225-237: forward_int_with_experts == forward_int."""
+    import cases
+
+    for name in ["tiny_softmax", "tiny_sigmoid_shared"]:
+        c = cases.CASES[name]
+        m = cases.build_oracle(c, oracle)
+        x = np.random.default_rng(rows).standard_normal((rows, c.d)).astype(np.float32)
+        xi, xs = oracle.from_reals_f32(x)
+        a, sa = m.forward(xi, xs)
+        b, sb = m.forward_with_local_experts(xi, xs)
+        assert (a == b).all() and sa == sb
+
+
+def test_topk_ties_go_to_the_lower_index(oracle):
+    """layers.rs:800-805: identical router rows give identical logits; the lowest indices win."""
+    d, E, f, k = 32, 8, 16, 3
+    rng = np.random.default_rng(3)
+    row = rng.standard_normal(d).astype(np.float32)
+    router_w = np.tile(row, (E, 1))
+    experts = rng.standard_normal(E * 3 * f * d).astype(np.float32)
+    m = oracle.MoeOracle(d, E, f, k, router_w, experts)
+    xi, xs = oracle.from_reals_f32(rng.standard_normal((4, d)).astype(np.float32))
+    ex, ec, sumc = m.route(xi, xs)
+    assert (ex == np.arange(k)).all()
+
+
+def test_all_zero_input_gives_zero_output(oracle):
+    import cases
+
+    c = cases.CASES["tiny_sigmoid_shared"]
+    m = cases.build_oracle(c, oracle)
+    y, ys = m.forward(np.zeros((3, c.d), np.int32), (0, 0))
+    assert (y == 0).all() and ys == (0, 0)

@@ -1,0 +1,444 @@
+"""tritify_b200 — tritify's exact-integer Mixture-of-Experts layer on NVIDIA B200.
+
+The host-side mirror of the reference's operator interfaces, over the C ABI of ``include/ktmoe.h``
+(``libktmoe.so``). Names and argument meanings follow tritify (paths relative to the reference project root):
+
+* :class:`Scale`, :class:`IntTensor`             — kt-int ``Scale`` (crates/00-kernels/kt-int/src/lib.rs:175-324),
+  kt-core ``IntTensor`` (crates/01-engine/kt-core/src/tensor.rs:10-116)
+* :class:`QuantLinear`, :class:`SwiGluMlp`,
+  :class:`MoeMlp`, :class:`MoeRoute`               — crates/01-engine/kt-core/src/layers.rs:211-1106
+* :class:`B200Linear`                             — a ``LinearBackend`` (crates/01-engine/kt-core/src/backend.rs:46-59)
+
+Every integer a forward produces comes from the sm_100a kernels in libktmoe.so; the only host arithmetic is the
+reference's own offline f64 preparation (weight and entry quantisers, code tables), done in C++ in the same library.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Sequence
+
+import numpy as np
+
+from . import _native
+from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
+
+__all__ = [
+    "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
+    "B200Linear", "Context", "DeviceLayer", "device_count", "synth_normal", "lcg_uniform", "table", "KtmoeError",
+]
+
+WLEVELS = 265720  # (3^12 - 1) / 2, layers.rs:16
+ACT_LEVELS = 1 << 28  # layers.rs:18
+ROUTER_CODE_BITS = 20  # layers.rs:659
+
+
+def _p(a: np.ndarray, ct):
+    return a.ctypes.data_as(ctypes.POINTER(ct))
+
+
+@dataclass(frozen=True)
+class Scale:
+    """A non-negative fixed-point scale ``mant · 2^-shift`` (kt-int ``Scale``)."""
+
+    mant: int
+    shift: int
+
+    ZERO = None  # set below
+
+    def to_f64(self) -> float:
+        return float(self.mant) * 2.0 ** (-self.shift)
+
+    def _c(self) -> KtmoeScale:
+        return KtmoeScale(int(self.mant), int(self.shift))
+
+    @staticmethod
+    def _of(s: KtmoeScale) -> "Scale":
+        return Scale(int(s.mant), int(s.shift))
+
+
+Scale.ZERO = Scale(0, 0)
+
+
+class IntTensor:
+    """An activation: int32 data, a shape and one :class:`Scale` (``real = data · scale``)."""
+
+    def __init__(self, data: np.ndarray, shape: Sequence[int], scale: Scale):
+        self.data = np.ascontiguousarray(data, dtype=np.int32).reshape(-1)
+        self.shape = tuple(int(s) for s in shape)
+        self.scale = scale
+
+    def __len__(self) -> int:
+        return int(self.data.size)
+
+    @staticmethod
+    def from_reals(values: np.ndarray, levels: int = ACT_LEVELS) -> "IntTensor":
+        """IntTensor::from_reals (tensor.rs:106-116) at ACT_LEVELS, on f32 values."""
+        if levels != ACT_LEVELS:
+            raise ValueError("the entry quantiser here runs at ACT_LEVELS")
+        v = np.ascontiguousarray(values, dtype=np.float32)
+        data = np.empty(v.size, dtype=np.int32)
+        s = KtmoeScale()
+        check(lib().ktmoe_from_reals(_p(v, ctypes.c_float), v.size, _p(data, ctypes.c_int32), ctypes.byref(s)))
+        return IntTensor(data, v.shape, Scale._of(s))
+
+    def to_f64(self) -> np.ndarray:
+        return self.data.astype(np.float64) * self.scale.to_f64()
+
+
+def device_count() -> int:
+    n = ctypes.c_int(0)
+    check(lib().ktmoe_device_count(ctypes.byref(n)))
+    return n.value
+
+
+class Context:
+    """One B200 device with its stream and resident-weight cache (kt-cuda's DeviceExec, device.rs:312-327)."""
+
+    def __init__(self, device: int = 0):
+        h = ctypes.c_void_p()
+        check(lib().ktmoe_open(device, ctypes.byref(h)))
+        self._h = h
+        self.device = device
+        self._lock = threading.Lock()
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self) -> None:
+        if self._h:
+            lib().ktmoe_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, status: int) -> None:
+        check(status, self._h)
+
+    def stream(self) -> int:
+        return int(lib().ktmoe_stream(self._h) or 0)
+
+    def launch_count(self) -> int:
+        n = ctypes.c_uint64()
+        self.check(lib().ktmoe_launch_count(self._h, ctypes.byref(n)))
+        return n.value
+
+    def sync(self, stream: int = 0) -> None:
+        self.check(lib().ktmoe_sync(self._h, ctypes.c_void_p(stream) if stream else None))
+
+    def linear(self, x: np.ndarray, w: np.ndarray, rows: int, out: int, k: int,
+               weight_id: Optional[int] = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        w = np.ascontiguousarray(w, dtype=np.int32).reshape(-1)
+        if x.size != rows * k or w.size != out * k:
+            raise ValueError("linear: x is not rows·k or w is not out·k")
+        y = np.empty(rows * out, dtype=np.int64)
+        if weight_id is None:
+            st = lib().ktmoe_linear(self._h, _p(x, ctypes.c_int32), _p(w, ctypes.c_int32), rows, out, k,
+                                    _p(y, ctypes.c_int64))
+        else:
+            st = lib().ktmoe_linear_weights(self._h, weight_id, _p(x, ctypes.c_int32), _p(w, ctypes.c_int32), rows,
+                                            out, k, _p(y, ctypes.c_int64))
+        self.check(st)
+        return y
+
+    def set_weight_budget(self, nbytes: int) -> None:
+        self.check(lib().ktmoe_set_weight_budget(self._h, nbytes))
+
+    def resident_bytes(self) -> int:
+        n = ctypes.c_uint64()
+        self.check(lib().ktmoe_resident_bytes(self._h, ctypes.byref(n)))
+        return n.value
+
+
+_default_ctx: Optional[Context] = None
+_default_lock = threading.Lock()
+
+
+def default_context() -> Context:
+    global _default_ctx
+    with _default_lock:
+        if _default_ctx is None:
+            _default_ctx = Context(0)
+        return _default_ctx
+
+
+class B200Linear:
+    """A tritify ``LinearBackend`` (backend.rs:46-59) on a B200: the exact i32×i32→i64 accumulate as digit-plane
+    products on the tensor cores. ``linear_weights`` keeps weights resident by id (``WeightId``)."""
+
+    def __init__(self, ctx: Optional[Context] = None):
+        self.ctx = ctx or default_context()
+
+    def name(self) -> str:
+        return f"b200:{self.ctx.device}"
+
+    def linear(self, x, w, rows: int, out: int, k: int) -> np.ndarray:
+        return self.ctx.linear(x, w, rows, out, k)
+
+    def linear_weights(self, x, weight_id: int, w, rows: int, out: int, k: int) -> np.ndarray:
+        return self.ctx.linear(x, w, rows, out, k, weight_id=weight_id)
+
+
+class QuantLinear:
+    """QuantLinear (layers.rs:211-257): per-tensor b=12 weight codes and their scale, optional bias."""
+
+    def __init__(self, name: str, codes: np.ndarray, w_scale: Scale, out_features: int, in_features: int,
+                 bias: Optional[tuple] = None):
+        self.name = name
+        self.out_features, self.in_features = int(out_features), int(in_features)
+        self.w_codes = np.ascontiguousarray(codes, dtype=np.int32).reshape(self.out_features, self.in_features)
+        self.w_scale = w_scale
+        self.bias = bias  # (codes int64 [out], Scale) or None
+
+    @staticmethod
+    def from_weights(name: str, w: np.ndarray, out_features: int, in_features: int) -> "QuantLinear":
+        w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+        if w.size != out_features * in_features:
+            raise ValueError(f"{name}: weights are not out·in")
+        codes = np.empty(w.size, dtype=np.int32)
+        s = KtmoeScale()
+        check(lib().ktmoe_quantize_weights(_p(w, ctypes.c_float), w.size, _p(codes, ctypes.c_int32), ctypes.byref(s)))
+        return QuantLinear(name, codes, Scale._of(s), out_features, in_features)
+
+    def with_bias(self, bias: Optional[np.ndarray]) -> "QuantLinear":
+        if bias is None:
+            return self
+        b = np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+        if b.size != self.out_features:
+            raise ValueError(f"{self.name}: bias len mismatch")
+        codes = np.empty(b.size, dtype=np.int64)
+        s = KtmoeScale()
+        has = ctypes.c_int32()
+        check(lib().ktmoe_quantize_bias(_p(b, ctypes.c_float), b.size, _p(codes, ctypes.c_int64), ctypes.byref(s),
+                                        ctypes.byref(has)))
+        if has.value:
+            self.bias = (codes, Scale._of(s))
+        return self
+
+
+class SwiGluMlp:
+    """SwiGluMlp (layers.rs:581-640): down(SiLU(gate(x)) ⊙ up(x)) with an integer-code SiLU table."""
+
+    def __init__(self, name: str, gate: QuantLinear, up: QuantLinear, down: QuantLinear):
+        if gate.out_features != up.out_features:
+            raise ValueError("gate/up hidden mismatch")
+        if down.in_features != gate.out_features:
+            raise ValueError("down input != hidden")
+        self.name, self.gate, self.up, self.down = name, gate, up, down
+
+
+@dataclass
+class MoeRoute:
+    """MoeRoute (layers.rs:812-821): the selected experts in top-k order, their codes and the normaliser."""
+
+    experts: List[int]
+    ec: List[int]
+    sumc: int
+
+
+class DeviceLayer:
+    """One MoE layer resident on a device (ktmoe_layer): weights as digit planes, scratch for the forward."""
+
+    def __init__(self, ctx: Context, d_model: int, n_experts: int, d_ff: int, top_k: int, norm_topk_prob: bool,
+                 sigmoid: bool, shared_d_ff: int):
+        self.ctx = ctx
+        cfg = KtmoeLayerConfig(d_model, n_experts, d_ff, top_k, 1 if norm_topk_prob else 0, 1 if sigmoid else 0,
+                               shared_d_ff)
+        h = ctypes.c_void_p()
+        ctx.check(lib().ktmoe_layer_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)))
+        self._h = h
+        self.d_model, self.n_experts, self.d_ff, self.top_k, self.shared_d_ff = d_model, n_experts, d_ff, top_k, shared_d_ff
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().ktmoe_layer_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def set_router(self, codes: np.ndarray, w_scale: Scale, bias: Optional[tuple] = None) -> None:
+        codes = np.ascontiguousarray(codes, dtype=np.int32)
+        if bias is not None:
+            bc = np.ascontiguousarray(bias[0], dtype=np.int64)
+            self.ctx.check(lib().ktmoe_layer_set_router(self._h, _p(codes, ctypes.c_int32), w_scale._c(),
+                                                        _p(bc, ctypes.c_int64), bias[1]._c()))
+        else:
+            self.ctx.check(lib().ktmoe_layer_set_router(self._h, _p(codes, ctypes.c_int32), w_scale._c(), None,
+                                                        KtmoeScale(0, 0)))
+
+    def set_sigmoid_bias(self, codes: np.ndarray) -> None:
+        codes = np.ascontiguousarray(codes, dtype=np.int64)
+        self.ctx.check(lib().ktmoe_layer_set_sigmoid_bias(self._h, _p(codes, ctypes.c_int64)))
+
+    def set_expert(self, e: int, gate: tuple, up: tuple, down: tuple) -> None:
+        g, u, d = (np.ascontiguousarray(t[0], dtype=np.int32) for t in (gate, up, down))
+        self.ctx.check(lib().ktmoe_layer_set_expert(self._h, e, _p(g, ctypes.c_int32), gate[1]._c(),
+                                                    _p(u, ctypes.c_int32), up[1]._c(), _p(d, ctypes.c_int32),
+                                                    down[1]._c()))
+
+    def set_shared(self, gate: tuple, up: tuple, down: tuple) -> None:
+        g, u, d = (np.ascontiguousarray(t[0], dtype=np.int32) for t in (gate, up, down))
+        self.ctx.check(lib().ktmoe_layer_set_shared(self._h, _p(g, ctypes.c_int32), gate[1]._c(),
+                                                    _p(u, ctypes.c_int32), up[1]._c(), _p(d, ctypes.c_int32),
+                                                    down[1]._c()))
+
+    def forward(self, x: np.ndarray, rows: int, x_scale: Scale):
+        """Host buffers in and out (synchronous): returns (y int32 [rows·d], Scale)."""
+        x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        if x.size != rows * self.d_model:
+            raise ValueError("x is not rows·d_model")
+        y = np.empty(rows * self.d_model, dtype=np.int32)
+        ys = KtmoeScale()
+        self.ctx.check(lib().ktmoe_forward(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(), _p(y, ctypes.c_int32),
+                                           ctypes.byref(ys)))
+        return y, Scale._of(ys)
+
+    def forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int, stream: int = 0) -> None:
+        """Device buffers (raw pointers), stream-ordered, not synchronised."""
+        self.ctx.check(lib().ktmoe_forward_dev(self._h, ctypes.c_void_p(x_ptr), rows, ctypes.c_void_p(x_scale_ptr),
+                                               ctypes.c_void_p(y_ptr), ctypes.c_void_p(y_scale_ptr),
+                                               ctypes.c_void_p(stream) if stream else None))
+
+    def route(self, x: np.ndarray, rows: int, x_scale: Scale):
+        x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        ex = np.empty(rows * self.top_k, dtype=np.int32)
+        ec = np.empty(rows * self.top_k, dtype=np.int64)
+        sumc = np.empty(rows, dtype=np.int64)
+        self.ctx.check(lib().ktmoe_route(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(), _p(ex, ctypes.c_int32),
+                                         _p(ec, ctypes.c_int64), _p(sumc, ctypes.c_int64)))
+        return ex.reshape(rows, self.top_k), ec.reshape(rows, self.top_k), sumc
+
+    def debug_fetch(self, which: int, rows: int):
+        """Internal buffers of the last forward (router logits / their scales / per-token outputs / their scales)."""
+        if which in (0, 2):
+            n = rows * (self.n_experts if which == 0 else self.d_model)
+            buf = np.empty(n, dtype=np.int32)
+            self.ctx.check(lib().ktmoe_layer_debug_fetch(self._h, which, buf.ctypes.data_as(ctypes.c_void_p),
+                                                         buf.nbytes))
+            return buf.reshape(rows, -1)
+        buf = (KtmoeScale * rows)()
+        self.ctx.check(lib().ktmoe_layer_debug_fetch(self._h, which, ctypes.cast(buf, ctypes.c_void_p),
+                                                     ctypes.sizeof(buf)))
+        return [Scale._of(s) for s in buf]
+
+
+class MoeMlp:
+    """MoeMlp (layers.rs:661-1106), its forward on a B200.
+
+    Built like the reference's: ``MoeMlp(name, router, experts, top_k)`` then ``with_norm_topk_prob``,
+    ``with_sigmoid_router`` and ``with_shared_expert``. The weights move to the device on the first forward.
+    """
+
+    def __init__(self, name: str, router: QuantLinear, experts: List[SwiGluMlp], top_k: int,
+                 ctx: Optional[Context] = None):
+        if not (1 <= top_k <= len(experts)):
+            raise ValueError("top_k in 1..=E")
+        if router.out_features != len(experts):
+            raise ValueError("router out_features != number of experts")
+        self.name, self.router, self.experts, self.top_k = name, router, experts, top_k
+        self.norm_topk_prob = False
+        self.sigmoid_bias_codes: Optional[np.ndarray] = None
+        self.shared: Optional[SwiGluMlp] = None
+        self._ctx = ctx
+        self._dev: Optional[DeviceLayer] = None
+
+    def with_norm_topk_prob(self, v: bool) -> "MoeMlp":
+        self.norm_topk_prob = bool(v)
+        self._dev = None
+        return self
+
+    def with_sigmoid_router(self, bias: np.ndarray) -> "MoeMlp":
+        b = np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+        if b.size != len(self.experts):
+            raise ValueError(f"{self.name}: one selection bias per expert")
+        codes = np.empty(b.size, dtype=np.int64)
+        check(lib().ktmoe_code_sigmoid_bias(_p(b, ctypes.c_float), b.size, _p(codes, ctypes.c_int64)))
+        self.sigmoid_bias_codes = codes
+        self._dev = None
+        return self
+
+    def with_shared_expert(self, shared: SwiGluMlp) -> "MoeMlp":
+        self.shared = shared
+        self._dev = None
+        return self
+
+    @property
+    def dim(self) -> int:
+        return self.router.in_features
+
+    def device_layer(self) -> DeviceLayer:
+        if self._dev is None:
+            ctx = self._ctx or default_context()
+            e0 = self.experts[0]
+            dev = DeviceLayer(ctx, self.dim, len(self.experts), e0.gate.out_features, self.top_k, self.norm_topk_prob,
+                              self.sigmoid_bias_codes is not None,
+                              self.shared.gate.out_features if self.shared else 0)
+            dev.set_router(self.router.w_codes, self.router.w_scale, self.router.bias)
+            if self.sigmoid_bias_codes is not None:
+                dev.set_sigmoid_bias(self.sigmoid_bias_codes)
+            for e, m in enumerate(self.experts):
+                dev.set_expert(e, (m.gate.w_codes, m.gate.w_scale), (m.up.w_codes, m.up.w_scale),
+                               (m.down.w_codes, m.down.w_scale))
+            if self.shared is not None:
+                s = self.shared
+                dev.set_shared((s.gate.w_codes, s.gate.w_scale), (s.up.w_codes, s.up.w_scale),
+                               (s.down.w_codes, s.down.w_scale))
+            self._dev = dev
+        return self._dev
+
+    def forward_int(self, x: IntTensor) -> IntTensor:
+        """Module::forward_int (layers.rs:1070-1073)."""
+        d = self.dim
+        if len(x) % d != 0:
+            raise ValueError(f"{self.name}: MoE input length must be a multiple of dim")
+        rows = len(x) // d
+        y, ys = self.device_layer().forward(x.data, rows, x.scale)
+        shape = (d,) if rows == 1 else (rows, d)
+        return IntTensor(y, shape, ys)
+
+    def route(self, x: IntTensor) -> List[MoeRoute]:
+        """MoeMlp::route (layers.rs:826-862) for each row of ``x``."""
+        rows = len(x) // self.dim
+        ex, ec, sumc = self.device_layer().route(x.data, rows, x.scale)
+        return [MoeRoute([int(v) for v in ex[t]], [int(v) for v in ec[t]], int(sumc[t])) for t in range(rows)]
+
+    def route_trace(self, x: IntTensor) -> List[List[int]]:
+        """Module::route_trace (layers.rs:1089-1100)."""
+        return [r.experts for r in self.route(x)]
+
+
+def synth_normal(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray:
+    """Elements [offset, offset + n) of the build-defined N(0, sigma) stream ``seed`` (splitmix64 + Box-Muller in f64,
+    cast to f32)."""
+    out = np.empty(n, dtype=np.float32)
+    check(lib().ktmoe_synth_normal(seed, sigma, offset, n, _p(out, ctypes.c_float)))
+    return out
+
+
+def lcg_uniform(seed: int, lo: int, hi: int, n: int) -> np.ndarray:
+    """Uniform integers in [lo, hi] from the reference's test LCG."""
+    out = np.empty(n, dtype=np.int32)
+    check(lib().ktmoe_lcg_uniform(seed, lo, hi, n, _p(out, ctypes.c_int32)))
+    return out
+
+
+def table(kind: int):
+    """Code table kind 0 (router exp), 1 (SiLU), 2 (sigmoid): (codes, inv_step, lo_index, code_scale)."""
+    codes = np.empty(1 << 16, dtype=np.int64)
+    a, b = KtmoeScale(), KtmoeScale()
+    lo = ctypes.c_int64()
+    check(lib().ktmoe_table(kind, _p(codes, ctypes.c_int64), ctypes.byref(a), ctypes.byref(lo), ctypes.byref(b)))
+    return codes, Scale._of(a), lo.value, Scale._of(b)

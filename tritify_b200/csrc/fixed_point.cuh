@@ -1,0 +1,222 @@
+// Exact integer fixed-point arithmetic of tritify's integer path, for host and device.
+//
+// Every function here is bit-identical to its tritify counterpart (cited file:line, relative to the reference
+// project root). The per-element hot operations (requant_dyn at ACT_LEVELS, quant_to, Scale::apply) are written so
+// the GPU never runs a 128-bit software division: a double-precision quotient estimate is corrected with exact
+// 128-bit integer remainders, which makes the result the exact floor quotient for any input (the correction loop
+// runs at most a couple of steps because the estimate is within one unit; a far-off estimate falls back to the
+// exact 128-bit division).
+#pragma once
+
+#include <stdint.h>
+
+#ifdef __CUDACC__
+#define KT_HD __host__ __device__ __forceinline__
+#else
+#define KT_HD inline
+#endif
+
+namespace kt {
+
+typedef __int128 i128;
+typedef unsigned __int128 u128;
+
+// crates/01-engine/kt-core/src/layers.rs:16-18
+constexpr int64_t WLEVELS = 265720;  // (3^12 - 1) / 2
+constexpr int64_t ACT_LEVELS = int64_t(1) << 28;
+constexpr int ACT_SHIFT = 28;
+// crates/01-engine/kt-core/src/layers.rs:659
+constexpr int ROUTER_CODE_BITS = 20;
+// Digit planes: a code v, |v| <= WLEVELS, is d0 + 81 d1 + 81^2 d2 with |di| <= 40
+// (crates/02-runtime/kt-cuda/src/digits.rs:8-36).
+constexpr int DIGIT_BASE = 81;
+constexpr int DIGIT_MAX = 40;
+
+struct Scale {
+    int64_t mant;
+    int32_t shift;
+};
+
+KT_HD Scale scale_zero() { return Scale{0, 0}; }
+
+KT_HD int clz64(uint64_t x) {
+#ifdef __CUDA_ARCH__
+    return __clzll((long long)x);
+#else
+    return x ? __builtin_clzll(x) : 64;
+#endif
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:184-186
+KT_HD int bits_u128(u128 x) {
+    uint64_t hi = (uint64_t)(x >> 64);
+    if (hi) return 128 - clz64(hi);
+    uint64_t lo = (uint64_t)x;
+    return lo ? 64 - clz64(lo) : 0;
+}
+
+KT_HD double u128_to_double(u128 x) {
+    return (double)(uint64_t)(x >> 64) * 18446744073709551616.0 + (double)(uint64_t)x;
+}
+
+// floor(n / d) for d > 0. The double estimate is exact to within one unit whenever the quotient is below 2^52;
+// the remainder is then corrected exactly in 128-bit arithmetic.
+KT_HD u128 udiv_u128(u128 n, u128 d) {
+    if ((d >> 64) == 0 && (n >> 64) == 0) return (u128)((uint64_t)n / (uint64_t)d);
+    double qe = u128_to_double(n) / u128_to_double(d);
+    if (qe < 4.0e15) {
+        int64_t q = (int64_t)qe;
+        i128 r = (i128)n - (i128)((u128)q * d);
+        int guard = 0;
+        while (r < 0 && guard < 4) {
+            --q;
+            r += (i128)d;
+            ++guard;
+        }
+        while (r >= (i128)d && guard < 8) {
+            ++q;
+            r -= (i128)d;
+            ++guard;
+        }
+        if (r >= 0 && r < (i128)d) return (u128)q;
+    }
+    return n / d;
+}
+
+// floor(n / d) for n < 2^96-ish, d < 2^63, quotient < 2^52: the hot-path divide (no 128-bit software division).
+KT_HD uint64_t udiv_small_q(u128 n, uint64_t d) {
+    double qe = u128_to_double(n) / (double)d;
+    int64_t q = (int64_t)qe;
+    i128 r = (i128)n - (i128)((u128)(uint64_t)q * d);
+    int guard = 0;
+    while (r < 0 && guard < 4) {
+        --q;
+        r += (i128)d;
+        ++guard;
+    }
+    while (r >= (i128)d && guard < 8) {
+        ++q;
+        r -= (i128)d;
+        ++guard;
+    }
+    if (r >= 0 && r < (i128)d) return (uint64_t)q;
+    return (uint64_t)(n / (u128)d);
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:191-212 — Scale::from_ratio.
+KT_HD Scale from_ratio(u128 num, u128 den) {
+    if (num == 0) return scale_zero();
+    // den > 0 is asserted by the reference; callers here never pass 0.
+    while (bits_u128(num) > 64 || bits_u128(den) > 64) {
+        num >>= 1;
+        den >>= 1;
+    }
+    if (den == 0) den = 1;
+    int s = 31 - (bits_u128(num) - bits_u128(den));
+    u128 mant;
+    if (s >= 0) {
+        u128 numer = num << s;
+        mant = udiv_u128(numer + den / 2, den);
+    } else {
+        u128 dd = den << (-s);
+        mant = udiv_u128(num + dd / 2, dd);
+    }
+    return Scale{(int64_t)mant, s};
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:227-248 — Scale::ge (exact comparison of mant·2^-shift).
+KT_HD bool scale_ge(Scale a, Scale o) {
+    if (a.mant == 0) return o.mant == 0;
+    if (o.mant == 0) return true;
+    u128 ma = (u128)(uint64_t)a.mant, mb = (u128)(uint64_t)o.mant;
+    int d = o.shift - a.shift;
+    if (d >= 0) {
+        if ((uint32_t)d + (uint32_t)bits_u128(ma) > 127) return true;
+        return (ma << d) >= mb;
+    } else {
+        uint32_t e = (uint32_t)(-d);
+        if (e + (uint32_t)bits_u128(mb) > 127) return false;
+        return ma >= (mb << e);
+    }
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:252-258 — Scale::mul (from_ratio(p, 1) needs no division).
+KT_HD Scale scale_mul(Scale a, Scale o) {
+    if (a.mant == 0 || o.mant == 0) return scale_zero();
+    u128 num = (u128)(uint64_t)a.mant * (u128)(uint64_t)o.mant;
+    // from_ratio(num, 1): num < 2^64 here (mantissas are below 2^32), den = 1
+    while (bits_u128(num) > 64) num >>= 1;  // den >> 1 == 0 -> 1, as in the reference loop
+    int s = 31 - (bits_u128(num) - 1);
+    u128 mant;
+    if (s >= 0) {
+        mant = num << s;
+    } else {
+        int sh = -s;
+        mant = (num + ((u128)1 << (sh - 1))) >> sh;
+    }
+    return Scale{(int64_t)mant, s + a.shift + o.shift};
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:261-272 — Scale::apply: round(value·mant / 2^shift), half away from zero.
+KT_HD int64_t scale_apply(Scale s, int64_t value) {
+    if (s.mant == 0) return 0;
+    i128 prod = (i128)value * (i128)s.mant;
+    if (s.shift <= 0) return (int64_t)(prod << (-s.shift));
+    if (s.shift >= 127) return 0;  // |prod| < 2^126: rounds to zero (the reference's shift never gets here)
+    i128 half = (i128)1 << (s.shift - 1);
+    i128 r = prod >= 0 ? (prod + half) >> s.shift : -(((-prod) + half) >> s.shift);
+    return (int64_t)r;
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:275-280 — Scale::recip (caller guarantees mant != 0).
+KT_HD Scale scale_recip(Scale s) {
+    Scale r = from_ratio((u128)1 << 40, (u128)(uint64_t)s.mant);
+    return Scale{r.mant, r.shift - s.shift + 40};
+}
+
+// from_ratio(v, 2^28) for 0 < v < 2^63: the output-scale factor of every dynamic requant.
+KT_HD Scale ratio_act(int64_t v) { return from_ratio((u128)(uint64_t)v, (u128)ACT_LEVELS); }
+
+// crates/01-engine/kt-core/src/layers.rs:34-39 — requant_dyn(v, ACT_LEVELS, den), den > 0.
+KT_HD int32_t requant_act(int64_t v, int64_t den) {
+    uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-(v + 1)) + 1;
+    u128 n = ((u128)av << ACT_SHIFT) + (u128)(uint64_t)(den / 2);
+    uint64_t q = udiv_small_q(n, (uint64_t)den);
+    int64_t r = v >= 0 ? (int64_t)q : -(int64_t)q;
+    return (int32_t)r;
+}
+
+// crates/01-engine/kt-core/src/layers.rs:34-39 — the general requant_dyn (any level), exact i128.
+KT_HD int32_t requant_dyn(int64_t v, int64_t num_level, int64_t den) {
+    i128 prod = (i128)v * (i128)num_level;
+    i128 half = (i128)den / 2;
+    i128 r = prod >= 0 ? (prod + half) / (i128)den : -(((-prod) + half) / (i128)den);
+    return (int32_t)r;
+}
+
+// crates/01-engine/kt-core/src/layers.rs:23-31 — quant_to: round_half_away(d·WLEVELS / xmax), xmax > 0.
+KT_HD int32_t quant_to(int32_t d, int64_t xmax) {
+    int64_t num = (int64_t)d * WLEVELS;
+    uint64_t an = num >= 0 ? (uint64_t)num : (uint64_t)(-num);
+    uint64_t n = an + (uint64_t)(xmax / 2);
+    uint64_t q = udiv_small_q((u128)n, (uint64_t)xmax);
+    return (int32_t)(num >= 0 ? (int64_t)q : -(int64_t)q);
+}
+
+// crates/02-runtime/kt-cuda/src/digits.rs:40-52 — the balanced base-81 digits of a code (|v| <= WLEVELS), low first.
+// The balanced representation is unique, so the offset form below gives the reference's digits.
+KT_HD void split_digits(int32_t v, int8_t& d0, int8_t& d1, int8_t& d2) {
+    uint32_t u = (uint32_t)(v + (int32_t)WLEVELS);
+    uint32_t q0 = u / 81u, q1 = q0 / 81u;
+    d0 = (int8_t)((int32_t)(u - q0 * 81u) - DIGIT_MAX);
+    d1 = (int8_t)((int32_t)(q0 - q1 * 81u) - DIGIT_MAX);
+    d2 = (int8_t)((int32_t)q1 - DIGIT_MAX);
+}
+
+// The recombination of the five diagonal plane sums: sum_t 81^t S_t (digit_gemm.cu:30-84 of kt-cuda recombines nine
+// plane sums with the same weights; products of equal i+j share a diagonal).
+KT_HD int64_t recombine(int32_t s0, int32_t s1, int32_t s2, int32_t s3, int32_t s4) {
+    return (int64_t)s0 + 81LL * s1 + 6561LL * s2 + 531441LL * s3 + 43046721LL * s4;
+}
+
+}  // namespace kt

@@ -1,0 +1,1121 @@
+// ktmoe: tritify's integer MoE layer and its exact linear accumulate on B200, behind the C ABI of include/ktmoe.h.
+//
+// Host side: contexts (device + stream + resident weights), TMA tensor maps, the launch sequence of one layer
+// forward, and the offline f64 preparation entry points. Device side: digit_gemm.cuh (the tcgen05 digit-plane GEMM)
+// and moe_kernels.cuh (routing, dispatch, SwiGLU/requant, combine, merge, shared expert). There is no CPU compute
+// path: every result comes from the kernels in this library, and a context on a device that is not sm_100 fails to
+// open.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <list>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "digit_gemm.cuh"
+#include "fixed_point.cuh"
+#include "host_prep.h"
+#include "ktmoe.h"
+#include "moe_kernels.cuh"
+
+using kt::Scale;
+
+namespace {
+
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+inline Scale S(ktmoe_scale s) { return Scale{s.mant, s.shift}; }
+inline ktmoe_scale C(Scale s) { return ktmoe_scale{s.mant, s.shift}; }
+inline Scale S(hp::HScale s) { return Scale{s.mant, s.shift}; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    });
+    return fn;
+}
+
+// A device buffer that only grows.
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    cudaError_t ensure(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&p, want);
+        if (e == cudaSuccess) bytes = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <class T>
+    T* as() const {
+        return (T*)p;
+    }
+};
+
+// Digit planes: [groups][3][rows_pad][k_pad] int8.
+struct Planes {
+    int8_t* ptr = nullptr;
+    int64_t groups = 1, rows_pad = 0, k = 0, k_pad = 0;
+};
+
+struct Resident {
+    DevBuf buf;
+    int64_t out = 0, k = 0, out_pad = 0, k_pad = 0;
+    uint64_t last_use = 0;
+};
+
+}  // namespace
+
+struct ktmoe_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int* d_err = nullptr;
+    std::string last_error = "";
+    uint64_t launches = 0;
+    std::mutex mu;
+    // LinearBackend scratch
+    DevBuf lin_xi, lin_wi, lin_xp, lin_wp, lin_y, lin_bad;
+    // resident weights (linear_weights)
+    std::unordered_map<uint64_t, Resident*> cache;
+    uint64_t budget = 0, resident = 0, tick = 0;
+};
+
+namespace {
+
+int fail(ktmoe_ctx* ctx, int status, const std::string& what) {
+    if (ctx) ctx->last_error = what;
+    return status;
+}
+
+int fail_cuda(ktmoe_ctx* ctx, cudaError_t e, const char* what) {
+    return fail(ctx, KTMOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define CK(expr)                                                        \
+    do {                                                                \
+        cudaError_t e__ = (expr);                                       \
+        if (e__ != cudaSuccess) return fail_cuda(ctx, e__, #expr);      \
+    } while (0)
+
+#define CKL(ctx)                                                        \
+    do {                                                                \
+        ++(ctx)->launches;                                              \
+        cudaError_t e__ = cudaGetLastError();                           \
+        if (e__ != cudaSuccess) return fail_cuda(ctx, e__, "kernel launch"); \
+    } while (0)
+
+int make_map(ktmoe_ctx* ctx, CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows_total, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(ctx, KTMOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t gdim[2] = {(cuuint64_t)k_pad, (cuuint64_t)rows_total};
+    cuuint64_t gstride[1] = {(cuuint64_t)k_pad};
+    cuuint32_t box[2] = {(cuuint32_t)dg::BK, (cuuint32_t)box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ctx, KTMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+    return KTMOE_OK;
+}
+
+template <int BN, int ST>
+int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
+                  const dg::GemmArgs& args) {
+    using Cf = dg::Cfg<BN, ST>;
+    static bool attr_set[64] = {};
+    if (!attr_set[ctx->device & 63]) {
+        CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                Cf::SMEM_BYTES));
+        attr_set[ctx->device & 63] = true;
+    }
+    dg::digit_gemm_kernel<BN, ST><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+struct GemmCall {
+    Planes A;        // weights: groups x 3 x M_pad x k_pad
+    int64_t M_valid;
+    Planes B;        // activations: 3 x R_pad x k_pad
+    int64_t* out;
+    int64_t ld_out;
+    int BN;
+    int64_t grid_y;
+    const int* tile_group = nullptr;
+    const int* tile_row0 = nullptr;
+    const int* group_end = nullptr;
+    const int* n_tiles = nullptr;
+    int64_t single_rows = 0;
+};
+
+// Launch the digit GEMM, splitting K into chunks whose int32 diagonal sums cannot overflow.
+int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
+    if (g.grid_y <= 0 || g.M_valid <= 0) return KTMOE_OK;
+    if (g.grid_y > 65535) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "too many activation tiles for one launch");
+    CUtensorMap ma, mb;
+    int r = make_map(ctx, &ma, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, dg::BM);
+    if (r) return r;
+    r = make_map(ctx, &mb, g.B.ptr, g.B.k_pad, 3 * g.B.rows_pad, g.BN);
+    if (r) return r;
+    const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
+    const int64_t chunk_kb = dg::K_EXACT_MAX / dg::BK;
+    dim3 grid((unsigned)(g.A.rows_pad / dg::BM), (unsigned)g.grid_y);
+    for (int64_t kb0 = 0; kb0 < total_kb; kb0 += chunk_kb) {
+        dg::GemmArgs a;
+        a.out = g.out;
+        a.ld_out = g.ld_out;
+        a.M_valid = (int)g.M_valid;
+        a.M_pad = (int)g.A.rows_pad;
+        a.k_block0 = (int)kb0;
+        a.num_k_blocks = (int)std::min(chunk_kb, total_kb - kb0);
+        a.R_pad = (int)g.B.rows_pad;
+        a.tile_group = g.tile_group;
+        a.tile_row0 = g.tile_row0;
+        a.group_row_end = g.group_end;
+        a.n_tiles = g.n_tiles;
+        a.single_rows = (int)g.single_rows;
+        a.accumulate = kb0 > 0 ? 1 : 0;
+        a.err = ctx->d_err;
+        switch (g.BN) {
+            case 16: r = launch_gemm_t<16, 4>(ctx, st, ma, mb, grid, a); break;
+            case 32: r = launch_gemm_t<32, 3>(ctx, st, ma, mb, grid, a); break;
+            case 64: r = launch_gemm_t<64, 3>(ctx, st, ma, mb, grid, a); break;
+            default: return fail(ctx, KTMOE_ERR_ARG, "unsupported BN");
+        }
+        if (r) return r;
+    }
+    return KTMOE_OK;
+}
+
+int pick_bn(double rows_per_group) {
+    if (rows_per_group >= 48.0) return 64;
+    if (rows_per_group >= 20.0) return 32;
+    return 16;
+}
+
+__global__ void sqx_kernel(const unsigned long long* gxmax, const Scale* x_scale, Scale* out) {
+    const int64_t xm = (int64_t)*gxmax;
+    *out = xm > 0 ? kt::scale_mul(kt::from_ratio((kt::u128)(uint64_t)xm, (kt::u128)kt::WLEVELS), *x_scale)
+                  : kt::scale_zero();
+}
+
+int set_device(ktmoe_ctx* ctx) {
+    CK(cudaSetDevice(ctx->device));
+    return KTMOE_OK;
+}
+
+int check_err_word(ktmoe_ctx* ctx) {
+    int h = 0;
+    CK(cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h != 0) {
+        CK(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        return fail(ctx, KTMOE_ERR_KERNEL, "a kernel's bounded wait expired (code " + std::to_string(h) + ")");
+    }
+    return KTMOE_OK;
+}
+
+}  // namespace
+
+// ───────────────────────────── the layer ─────────────────────────────
+
+struct ktmoe_layer {
+    ktmoe_ctx* ctx = nullptr;
+    ktmoe_layer_config cfg{};
+    int64_t d = 0, E = 0, f = 0, K = 0, fs = 0;
+    int64_t d_pad = 0, f_pad = 0, fs_pad = 0;
+    Planes w_router, w_gu, w_dn, w_sgu, w_sdn;
+    DevBuf b_router, b_gu, b_dn, b_sgu, b_sdn;
+    bool router_set = false, shared_set = false, sigbias_set = false;
+    std::vector<char> expert_set;
+    Scale router_ws{0, 0}, router_bscale{0, 0};
+    bool has_rbias = false;
+    DevBuf b_rbias, b_sigbias;
+    // device scales: [0,E) gate, [E,2E) up, [2E,3E) down, then shared gate, up, down
+    DevBuf b_wsc;
+    std::vector<Scale> h_wsc;
+    DevBuf b_luts;  // 3 x 65536 int64: exp, SiLU, sigmoid
+    hp::HTable tabs[3];
+    Scale silu_code_scale_recip{0, 0};
+    // scratch for `cap` tokens
+    int64_t cap = 0;
+    DevBuf x_in, y_out, scal;  // scal: Scales and u64 scalars
+    DevBuf tok_planes, tok_xmax, tok_sqx, router_acc, logits, logit_scale, top_e, top_ec, sumc;
+    DevBuf counts, chunk_off, expert_off, group_end, expert_count, tile_group, tile_row0, slot_row, row_assign,
+        row_expert;
+    DevBuf xg_planes, acc_gu, hq_planes, row_cd, acc_d, tok_out, tok_scale, y_routed;
+    DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
+};
+
+namespace {
+
+// Scalar slots inside layer->scal.
+enum ScalarSlot {
+    SL_XSCALE = 0,   // Scale
+    SL_YSCALE = 1,   // Scale (routed result scale when a shared expert follows)
+    SL_COMMON = 2,   // Scale[2]: common, its reciprocal
+    SL_GSQX = 4,     // Scale: the shared expert's s_qx
+    SL_ADD = 5,      // Scale[4]: add scratch
+    SL_SCD = 9,      // Scale: shared down c
+    SL_YROUTED = 10, // Scale: routed scale (with shared)
+    SL_NSCALES = 12
+};
+enum U64Slot { U_MERGE_GMAX = 0, U_GXMAX, U_SYG, U_SYU, U_SHMAX, U_SYD, U_ADDGMAX, U_NTILES_PAD, U_N };
+
+Scale* scal_scale(ktmoe_layer* L, int slot) { return L->scal.as<Scale>() + slot; }
+unsigned long long* scal_u64(ktmoe_layer* L, int slot) {
+    return (unsigned long long*)(L->scal.as<uint8_t>() + SL_NSCALES * sizeof(Scale)) + slot;
+}
+int* n_tiles_ptr(ktmoe_layer* L) { return (int*)(scal_u64(L, U_NTILES_PAD)); }
+
+int ensure_scratch(ktmoe_layer* L, int64_t T) {
+    ktmoe_ctx* ctx = L->ctx;
+    if (T <= L->cap && L->cap > 0) return KTMOE_OK;
+    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
+    const int64_t R = T * K;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
+    const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
+    const int64_t max_tiles = (R + 15) / 16 + E;
+    CK(L->x_in.ensure(T * d * 4));
+    CK(L->y_out.ensure(T * d * 4));
+    CK(L->scal.ensure(SL_NSCALES * sizeof(Scale) + U_N * 8));
+    CK(L->tok_planes.ensure(3 * T_pad * L->d_pad));
+    CK(L->tok_xmax.ensure(T * 8));
+    CK(L->tok_sqx.ensure(T * sizeof(Scale)));
+    CK(L->router_acc.ensure(T * E * 8));
+    CK(L->logits.ensure(T * E * 4));
+    CK(L->logit_scale.ensure(T * sizeof(Scale)));
+    CK(L->top_e.ensure(R * 4));
+    CK(L->top_ec.ensure(R * 8));
+    CK(L->sumc.ensure(T * 8));
+    CK(L->counts.ensure(std::max<int64_t>(nchunks, 1) * E * 4));
+    CK(L->chunk_off.ensure(std::max<int64_t>(nchunks, 1) * E * 4));
+    CK(L->expert_off.ensure(E * 4));
+    CK(L->group_end.ensure(E * 4));
+    CK(L->expert_count.ensure(E * 4));
+    CK(L->tile_group.ensure(max_tiles * 4));
+    CK(L->tile_row0.ensure(max_tiles * 4));
+    CK(L->slot_row.ensure(R * 4));
+    CK(L->row_assign.ensure(R * 4));
+    CK(L->row_expert.ensure(R * 4));
+    CK(L->xg_planes.ensure(3 * R_pad * L->d_pad));
+    CK(L->acc_gu.ensure(R * 2 * f * 8));
+    CK(L->hq_planes.ensure(3 * R_pad * L->f_pad));
+    CK(L->row_cd.ensure(R * sizeof(Scale)));
+    CK(L->acc_d.ensure(R * d * 8));
+    CK(L->tok_out.ensure(T * d * 4));
+    CK(L->tok_scale.ensure(T * sizeof(Scale)));
+    if (fs > 0) {
+        CK(L->y_routed.ensure(T * d * 4));
+        CK(L->xs_planes.ensure(3 * T_pad * L->d_pad));
+        CK(L->acc_sgu.ensure(T * 2 * fs * 8));
+        CK(L->hs_planes.ensure(3 * T_pad * L->fs_pad));
+        CK(L->acc_sd.ensure(T * d * 8));
+    }
+    L->cap = T;
+    return KTMOE_OK;
+}
+
+bool layer_complete(const ktmoe_layer* L) {
+    if (!L->router_set) return false;
+    for (char c : L->expert_set)
+        if (!c) return false;
+    if (L->fs > 0 && !L->shared_set) return false;
+    if (L->cfg.router_score == 1 && !L->sigbias_set) return false;
+    return true;
+}
+
+mk::Lut lut(const ktmoe_layer* L, int kind) {
+    mk::Lut l;
+    l.codes = L->b_luts.as<int64_t>() + (int64_t)kind * mk::LUT_N;
+    l.inv_step = S(L->tabs[kind].inv_step);
+    l.lo_index = L->tabs[kind].lo_index;
+    return l;
+}
+
+// Quantise, route (router GEMM + top-k) for T tokens already in x_in / SL_XSCALE.
+int stage_route(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, E = L->E;
+    const int64_t T_pad = round_up(T, 64);
+    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
+                                                        L->tok_planes.as<int8_t>(), L->tok_xmax.as<int64_t>(),
+                                                        L->tok_sqx.as<Scale>(), xs_dev, nullptr);
+    CKL(ctx);
+    GemmCall g;
+    g.A = L->w_router;
+    g.M_valid = E;
+    g.B = Planes{L->tok_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
+    g.out = L->router_acc.as<int64_t>();
+    g.ld_out = E;
+    g.BN = pick_bn((double)T);
+    g.grid_y = (T + g.BN - 1) / g.BN;
+    g.single_rows = T;
+    int r = run_gemm(ctx, st, g);
+    if (r) return r;
+    mk::RouteArgs ra;
+    ra.acc = L->router_acc.as<int64_t>();
+    ra.row_xmax = L->tok_xmax.as<int64_t>();
+    ra.row_sqx = L->tok_sqx.as<Scale>();
+    ra.rows = (int)T;
+    ra.E = (int)E;
+    ra.top_k = (int)L->K;
+    ra.norm_topk = L->cfg.norm_topk_prob;
+    ra.sigmoid = L->cfg.router_score == 1;
+    ra.w_scale = L->router_ws;
+    ra.bias_codes = L->has_rbias ? L->b_rbias.as<int64_t>() : nullptr;
+    ra.bias_scale = L->router_bscale;
+    ra.sig_bias = L->cfg.router_score == 1 ? L->b_sigbias.as<int64_t>() : nullptr;
+    ra.exp_lut = lut(L, 0);
+    ra.sig_lut = lut(L, 2);
+    ra.top_e = L->top_e.as<int32_t>();
+    ra.top_ec = L->top_ec.as<int64_t>();
+    ra.sumc = L->sumc.as<int64_t>();
+    ra.logits_out = L->logits.as<int32_t>();
+    ra.logit_scale_out = L->logit_scale.as<Scale>();
+    mk::route_kernel<<<(unsigned)((T + 3) / 4), 128, 0, st>>>(ra);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
+                  cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
+    const int64_t R = T * K;
+    const int64_t T_pad = round_up(T, 64), R_pad = round_up(R, 64);
+    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
+    int r = stage_route(L, T, x_dev, xs_dev, st);
+    if (r) return r;
+
+    // dispatch plan: stable counting sort of the T·K assignments by expert
+    const int BN = pick_bn((double)R / (double)E);
+    const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
+    mk::plan_count_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, E * 4, st>>>(L->top_e.as<int32_t>(), R, (int)E,
+                                                                             L->counts.as<int>());
+    CKL(ctx);
+    const int scan_threads = (int)std::min<int64_t>(1024, round_up(E, 32));
+    mk::plan_scan_kernel<<<1, scan_threads, 2 * E * 4, st>>>(
+        L->counts.as<int>(), (int)nchunks, (int)E, BN, L->chunk_off.as<int>(), L->expert_off.as<int>(),
+        L->group_end.as<int>(), L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L),
+        L->expert_count.as<int>());
+    CKL(ctx);
+    mk::plan_assign_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, (E + (mk::PLAN_THREADS / 32) * E) * 4, st>>>(
+        L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
+        L->row_assign.as<int>(), L->row_expert.as<int>());
+    CKL(ctx);
+    mk::permute_planes_kernel<<<(unsigned)R, 128, 0, st>>>(L->tok_planes.as<int8_t>(), T_pad, L->xg_planes.as<int8_t>(),
+                                                         R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
+    CKL(ctx);
+
+    // routed gate+up: one grouped GEMM over the E experts
+    const int64_t max_tiles = (R + BN - 1) / BN + E;
+    GemmCall g;
+    g.A = L->w_gu;
+    g.M_valid = 2 * f;
+    g.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
+    g.out = L->acc_gu.as<int64_t>();
+    g.ld_out = 2 * f;
+    g.BN = BN;
+    g.grid_y = max_tiles;
+    g.tile_group = L->tile_group.as<int>();
+    g.tile_row0 = L->tile_row0.as<int>();
+    g.group_end = L->group_end.as<int>();
+    g.n_tiles = n_tiles_ptr(L);
+    r = run_gemm(ctx, st, g);
+    if (r) return r;
+
+    mk::SwigluArgs sa;
+    std::memset(&sa, 0, sizeof(sa));
+    sa.acc = L->acc_gu.as<int64_t>();
+    sa.rows = (int)R;
+    sa.f = (int)f;
+    sa.f_pad = (int)L->f_pad;
+    sa.R_pad = R_pad;
+    sa.row_assign = L->row_assign.as<int>();
+    sa.row_expert = L->row_expert.as<int>();
+    sa.top_k = (int)K;
+    sa.row_sqx = L->tok_sqx.as<Scale>();
+    sa.g_sqx = nullptr;
+    sa.wscale_g = L->b_wsc.as<Scale>();
+    sa.wscale_u = L->b_wsc.as<Scale>() + E;
+    sa.wscale_d = L->b_wsc.as<Scale>() + 2 * E;
+    sa.silu = lut(L, 1);
+    sa.silu_code_scale = S(L->tabs[1].code_scale);
+    sa.silu_code_scale_recip = L->silu_code_scale_recip;
+    sa.planes = L->hq_planes.as<int8_t>();
+    sa.row_cd = L->row_cd.as<Scale>();
+    sa.phase = 0;
+    mk::swiglu_kernel<<<(unsigned)R, 256, 0, st>>>(sa);
+    CKL(ctx);
+
+    g.A = L->w_dn;
+    g.M_valid = d;
+    g.B = Planes{L->hq_planes.as<int8_t>(), 1, R_pad, f, L->f_pad};
+    g.out = L->acc_d.as<int64_t>();
+    g.ld_out = d;
+    r = run_gemm(ctx, st, g);
+    if (r) return r;
+
+    mk::CombineArgs ca;
+    ca.acc_d = L->acc_d.as<int64_t>();
+    ca.row_cd = L->row_cd.as<Scale>();
+    ca.slot_row = L->slot_row.as<int>();
+    ca.top_ec = L->top_ec.as<int64_t>();
+    ca.sumc = L->sumc.as<int64_t>();
+    ca.T = (int)T;
+    ca.top_k = (int)K;
+    ca.dim = (int)d;
+    ca.out = L->tok_out.as<int32_t>();
+    ca.out_scale = L->tok_scale.as<Scale>();
+    mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+    CKL(ctx);
+
+    int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
+    Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
+    if (T == 1) {
+        mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                                                                      (int)d, routed, routed_scale);
+        CKL(ctx);
+    } else {
+        mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON), nullptr);
+        CKL(ctx);
+        mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)T,
+                                                        (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX));
+        CKL(ctx);
+        mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)T,
+                                                          (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX),
+                                                          routed, routed_scale);
+        CKL(ctx);
+    }
+    if (fs == 0) return KTMOE_OK;
+
+    // shared expert on the whole tensor (global maxima), then add(routed, shared)
+    const int64_t n = T * d;
+    const unsigned red_blocks = (unsigned)std::min<int64_t>(1184, (n + 255) / 256);
+    mk::absmax_i32_kernel<<<red_blocks, 256, 0, st>>>(x_dev, n, scal_u64(L, U_GXMAX));
+    CKL(ctx);
+    sqx_kernel<<<1, 1, 0, st>>>(scal_u64(L, U_GXMAX), xs_dev, scal_scale(L, SL_GSQX));
+    CKL(ctx);
+    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
+                                                        L->xs_planes.as<int8_t>(), nullptr, nullptr, xs_dev,
+                                                        scal_u64(L, U_GXMAX));
+    CKL(ctx);
+    GemmCall s;
+    s.A = L->w_sgu;
+    s.M_valid = 2 * fs;
+    s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
+    s.out = L->acc_sgu.as<int64_t>();
+    s.ld_out = 2 * fs;
+    s.BN = pick_bn((double)T);
+    s.grid_y = (T + s.BN - 1) / s.BN;
+    s.single_rows = T;
+    r = run_gemm(ctx, st, s);
+    if (r) return r;
+    const unsigned rb2 = (unsigned)std::min<int64_t>(1184, (T * fs + 255) / 256);
+    mk::absmax_i64_cols_kernel<<<rb2, 256, 0, st>>>(L->acc_sgu.as<int64_t>(), (int)T, 2 * fs, 0, (int)fs,
+                                                    scal_u64(L, U_SYG));
+    CKL(ctx);
+    mk::absmax_i64_cols_kernel<<<rb2, 256, 0, st>>>(L->acc_sgu.as<int64_t>(), (int)T, 2 * fs, (int)fs, (int)fs,
+                                                    scal_u64(L, U_SYU));
+    CKL(ctx);
+    mk::SwigluArgs sh;
+    std::memset(&sh, 0, sizeof(sh));
+    sh.acc = L->acc_sgu.as<int64_t>();
+    sh.rows = (int)T;
+    sh.f = (int)fs;
+    sh.f_pad = (int)L->fs_pad;
+    sh.R_pad = T_pad;
+    sh.top_k = 1;
+    sh.g_sqx = scal_scale(L, SL_GSQX);
+    sh.wscale_g = L->b_wsc.as<Scale>() + 3 * E;
+    sh.wscale_u = L->b_wsc.as<Scale>() + 3 * E + 1;
+    sh.wscale_d = L->b_wsc.as<Scale>() + 3 * E + 2;
+    sh.silu = lut(L, 1);
+    sh.silu_code_scale = S(L->tabs[1].code_scale);
+    sh.silu_code_scale_recip = L->silu_code_scale_recip;
+    sh.planes = L->hs_planes.as<int8_t>();
+    sh.row_cd = scal_scale(L, SL_SCD);
+    sh.g_ymax_g = scal_u64(L, U_SYG);
+    sh.g_ymax_u = scal_u64(L, U_SYU);
+    sh.g_hmax = scal_u64(L, U_SHMAX);
+    sh.g_hmax_in = scal_u64(L, U_SHMAX);
+    sh.phase = 1;
+    mk::swiglu_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+    CKL(ctx);
+    sh.phase = 2;
+    mk::swiglu_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+    CKL(ctx);
+    s.A = L->w_sdn;
+    s.M_valid = d;
+    s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
+    s.out = L->acc_sd.as<int64_t>();
+    s.ld_out = d;
+    r = run_gemm(ctx, st, s);
+    if (r) return r;
+    mk::absmax_i64_cols_kernel<<<red_blocks, 256, 0, st>>>(L->acc_sd.as<int64_t>(), (int)T, d, 0, (int)d,
+                                                           scal_u64(L, U_SYD));
+    CKL(ctx);
+    mk::AddArgs aa;
+    aa.a = routed;
+    aa.a_scale = routed_scale;
+    aa.s_acc = L->acc_sd.as<int64_t>();
+    aa.s_ymax = scal_u64(L, U_SYD);
+    aa.s_cd = scal_scale(L, SL_SCD);
+    aa.n = n;
+    aa.gmax = scal_u64(L, U_ADDGMAX);
+    aa.scratch = scal_scale(L, SL_ADD);
+    aa.y = y_dev;
+    aa.y_scale = ys_dev;
+    mk::add_prepare_kernel<<<1, 1, 0, st>>>(aa);
+    CKL(ctx);
+    mk::add_max_kernel<<<red_blocks, 256, 0, st>>>(aa);
+    CKL(ctx);
+    mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+// Upload codes [groups? one matrix] rows x k (int32, row-major) into planes at (group g) of P, packed on the device.
+int upload_matrix(ktmoe_ctx* ctx, const Planes& P, int64_t g, const int32_t* codes, int64_t rows, int64_t k,
+                  int64_t row0) {
+    DevBuf tmp;
+    CK(tmp.ensure((size_t)rows * k * 4));
+    DevBuf bad;
+    CK(bad.ensure(8));
+    CK(cudaMemsetAsync(bad.p, 0, 8, ctx->stream));
+    CK(cudaMemcpyAsync(tmp.p, codes, (size_t)rows * k * 4, cudaMemcpyHostToDevice, ctx->stream));
+    int8_t* base = P.ptr + (g * 3) * P.rows_pad * P.k_pad + row0 * P.k_pad;
+    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, ctx->stream>>>(tmp.as<int32_t>(), rows, (int)k, (int)P.k_pad,
+                                                                   P.rows_pad, base, bad.as<unsigned long long>());
+    CKL(ctx);
+    unsigned long long hbad = 0;
+    CK(cudaMemcpyAsync(&hbad, bad.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    tmp.release();
+    bad.release();
+    if (hbad) return fail(ctx, KTMOE_ERR_RANGE, "a weight code lies outside +-WLEVELS");
+    return KTMOE_OK;
+}
+
+int alloc_planes(ktmoe_ctx* ctx, DevBuf& buf, Planes& P, int64_t groups, int64_t rows_valid, int64_t k) {
+    P.groups = groups;
+    P.rows_pad = round_up(rows_valid, dg::BM);
+    P.k = k;
+    P.k_pad = round_up(k, dg::BK);
+    CK(buf.ensure((size_t)(groups * 3 * P.rows_pad * P.k_pad)));
+    CK(cudaMemset(buf.p, 0, buf.bytes));
+    P.ptr = buf.as<int8_t>();
+    return KTMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ktmoe_error_string(int status) {
+    switch (status) {
+        case KTMOE_OK: return "ok";
+        case KTMOE_ERR_CUDA: return "CUDA error";
+        case KTMOE_ERR_ARG: return "invalid argument";
+        case KTMOE_ERR_RANGE: return "code outside +-WLEVELS";
+        case KTMOE_ERR_KERNEL: return "kernel bounded wait expired";
+        case KTMOE_ERR_UNSUPPORTED: return "unsupported configuration";
+        case KTMOE_ERR_NO_DEVICE: return "no sm_100 device";
+        case KTMOE_ERR_STATE: return "layer incomplete";
+        default: return "unknown status";
+    }
+}
+
+int ktmoe_device_count(int* n) {
+    if (!n) return KTMOE_ERR_ARG;
+    *n = 0;
+    cudaError_t e = cudaGetDeviceCount(n);
+    if (e != cudaSuccess) {
+        *n = 0;
+        return e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? KTMOE_OK : KTMOE_ERR_CUDA;
+    }
+    return KTMOE_OK;
+}
+
+int ktmoe_open(int device, ktmoe_ctx** out) {
+    if (!out) return KTMOE_ERR_ARG;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return KTMOE_ERR_NO_DEVICE;
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess) return KTMOE_ERR_NO_DEVICE;
+    if (p.major != 10) return KTMOE_ERR_NO_DEVICE;  // the kernels are built for sm_100a only
+    ktmoe_ctx* ctx = new ktmoe_ctx();
+    ctx->device = device;
+    if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaMalloc(&ctx->d_err, sizeof(int)) != cudaSuccess || cudaMemset(ctx->d_err, 0, sizeof(int)) != cudaSuccess) {
+        delete ctx;
+        return KTMOE_ERR_CUDA;
+    }
+    size_t free_b = 0, total_b = 0;
+    cudaMemGetInfo(&free_b, &total_b);
+    ctx->budget = free_b / 5 * 4;
+    *out = ctx;
+    return KTMOE_OK;
+}
+
+int ktmoe_close(ktmoe_ctx* ctx) {
+    if (!ctx) return KTMOE_ERR_ARG;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto& kv : ctx->cache) {
+        kv.second->buf.release();
+        delete kv.second;
+    }
+    ctx->lin_xi.release();
+    ctx->lin_wi.release();
+    ctx->lin_xp.release();
+    ctx->lin_wp.release();
+    ctx->lin_y.release();
+    ctx->lin_bad.release();
+    cudaFree(ctx->d_err);
+    cudaStreamDestroy(ctx->stream);
+    delete ctx;
+    return KTMOE_OK;
+}
+
+const char* ktmoe_last_error(const ktmoe_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "no context"; }
+void* ktmoe_stream(ktmoe_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n) {
+    if (!ctx || !n) return KTMOE_ERR_ARG;
+    *n = ctx->launches;
+    return KTMOE_OK;
+}
+
+int ktmoe_sync(ktmoe_ctx* ctx, void* stream) {
+    if (!ctx) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (stream) CK(cudaStreamSynchronize((cudaStream_t)stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    return check_err_word(ctx);
+}
+
+int ktmoe_set_weight_budget(ktmoe_ctx* ctx, uint64_t bytes) {
+    if (!ctx) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->budget = bytes;
+    return KTMOE_OK;
+}
+
+int ktmoe_resident_bytes(ktmoe_ctx* ctx, uint64_t* bytes) {
+    if (!ctx || !bytes) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    *bytes = ctx->resident;
+    return KTMOE_OK;
+}
+
+static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t* x, const int32_t* w, int64_t rows,
+                       int64_t out, int64_t k, int64_t* y) {
+    if (!ctx || rows < 0 || out < 0 || k < 0) return KTMOE_ERR_ARG;
+    if (rows == 0 || out == 0) return KTMOE_OK;
+    if (!x || !w || !y) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    cudaStream_t st = ctx->stream;
+    if (k == 0) {
+        std::memset(y, 0, (size_t)(rows * out) * 8);
+        return KTMOE_OK;
+    }
+    const int64_t k_pad = round_up(k, dg::BK);
+    const int BN = pick_bn((double)rows);
+    const int64_t rows_pad = round_up(rows, 64);
+    const int64_t out_pad = round_up(out, dg::BM);
+    CK(ctx->lin_bad.ensure(8));
+    CK(cudaMemsetAsync(ctx->lin_bad.p, 0, 8, st));
+    // weights: resident by id, else packed for this call
+    Planes W{nullptr, 1, out_pad, k, k_pad};
+    Resident* res = nullptr;
+    if (weight_id) {
+        auto it = ctx->cache.find(*weight_id);
+        if (it != ctx->cache.end() && it->second->out == out && it->second->k == k) {
+            res = it->second;
+            res->last_use = ++ctx->tick;
+        }
+    }
+    unsigned long long hbad_w = 0;
+    if (res) {
+        W.ptr = res->buf.as<int8_t>();
+    } else {
+        const size_t wbytes = (size_t)(3 * out_pad * k_pad);
+        DevBuf* target = &ctx->lin_wp;
+        Resident* fresh = nullptr;
+        if (weight_id && wbytes <= ctx->budget) {
+            // evict least recently used until the new weights fit
+            while (ctx->resident + wbytes > ctx->budget && !ctx->cache.empty()) {
+                auto lru = ctx->cache.begin();
+                for (auto it = ctx->cache.begin(); it != ctx->cache.end(); ++it)
+                    if (it->second->last_use < lru->second->last_use) lru = it;
+                ctx->resident -= lru->second->buf.bytes;
+                lru->second->buf.release();
+                delete lru->second;
+                ctx->cache.erase(lru);
+            }
+            fresh = new Resident();
+            target = &fresh->buf;
+        }
+        cudaError_t e = target->ensure(wbytes);
+        if (e != cudaSuccess) {
+            delete fresh;
+            return fail_cuda(ctx, e, "weight planes");
+        }
+        CK(cudaMemsetAsync(target->p, 0, wbytes, st));
+        CK(ctx->lin_wi.ensure((size_t)(out * k) * 4));
+        CK(cudaMemcpyAsync(ctx->lin_wi.p, w, (size_t)(out * k) * 4, cudaMemcpyHostToDevice, st));
+        mk::pack_codes_kernel<<<(unsigned)out, 128, 0, st>>>(ctx->lin_wi.as<int32_t>(), out, (int)k, (int)k_pad, out_pad,
+                                                            target->as<int8_t>(), ctx->lin_bad.as<unsigned long long>());
+        CKL(ctx);
+        CK(cudaMemcpyAsync(&hbad_w, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        if (hbad_w) {
+            delete fresh;
+            return fail(ctx, KTMOE_ERR_RANGE, "a weight code lies outside +-WLEVELS");
+        }
+        if (fresh) {
+            fresh->out = out;
+            fresh->k = k;
+            fresh->out_pad = out_pad;
+            fresh->k_pad = k_pad;
+            fresh->last_use = ++ctx->tick;
+            ctx->cache[*weight_id] = fresh;
+            ctx->resident += fresh->buf.bytes;
+        }
+        W.ptr = target->as<int8_t>();
+    }
+    CK(ctx->lin_xi.ensure((size_t)(rows * k) * 4));
+    CK(ctx->lin_xp.ensure((size_t)(3 * rows_pad * k_pad)));
+    CK(ctx->lin_y.ensure((size_t)(rows * out) * 8));
+    CK(cudaMemcpyAsync(ctx->lin_xi.p, x, (size_t)(rows * k) * 4, cudaMemcpyHostToDevice, st));
+    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, st>>>(ctx->lin_xi.as<int32_t>(), rows, (int)k, (int)k_pad, rows_pad,
+                                                         ctx->lin_xp.as<int8_t>(), ctx->lin_bad.as<unsigned long long>());
+    CKL(ctx);
+    GemmCall g;
+    g.A = W;
+    g.M_valid = out;
+    g.B = Planes{ctx->lin_xp.as<int8_t>(), 1, rows_pad, k, k_pad};
+    g.out = ctx->lin_y.as<int64_t>();
+    g.ld_out = out;
+    g.BN = BN;
+    g.grid_y = (rows + BN - 1) / BN;
+    g.single_rows = rows;
+    if (int r = run_gemm(ctx, st, g)) return r;
+    unsigned long long hbad = 0;
+    CK(cudaMemcpyAsync(y, ctx->lin_y.p, (size_t)(rows * out) * 8, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(&hbad, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (int r = check_err_word(ctx)) return r;
+    if (hbad) return fail(ctx, KTMOE_ERR_RANGE, "an activation code lies outside +-WLEVELS");
+    return KTMOE_OK;
+}
+
+int ktmoe_linear(ktmoe_ctx* ctx, const int32_t* x, const int32_t* w, int64_t rows, int64_t out, int64_t k, int64_t* y) {
+    return linear_impl(ctx, nullptr, x, w, rows, out, k, y);
+}
+
+int ktmoe_linear_weights(ktmoe_ctx* ctx, uint64_t weight_id, const int32_t* x, const int32_t* w, int64_t rows,
+                         int64_t out, int64_t k, int64_t* y) {
+    return linear_impl(ctx, &weight_id, x, w, rows, out, k, y);
+}
+
+int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_layer** out) {
+    if (!ctx || !cfg || !out) return KTMOE_ERR_ARG;
+    *out = nullptr;
+    const ktmoe_layer_config c = *cfg;
+    if (c.d_model <= 0 || c.n_experts <= 0 || c.d_ff <= 0 || c.top_k <= 0 || c.shared_d_ff < 0)
+        return fail(ctx, KTMOE_ERR_ARG, "layer dimensions must be positive");
+    if (c.top_k > c.n_experts) return fail(ctx, KTMOE_ERR_ARG, "top_k exceeds the number of experts");
+    if (c.n_experts > 512 || c.top_k > mk::COMBINE_MAX_K)
+        return fail(ctx, KTMOE_ERR_UNSUPPORTED, "at most 512 experts and top_k <= 16");
+    if (c.router_score != 0 && c.router_score != 1) return fail(ctx, KTMOE_ERR_ARG, "router_score is 0 or 1");
+    if ((int64_t)c.d_model * 8 > 200 * 1024) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "d_model above 25600");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    ktmoe_layer* L = new ktmoe_layer();
+    L->ctx = ctx;
+    L->cfg = c;
+    L->d = c.d_model;
+    L->E = c.n_experts;
+    L->f = c.d_ff;
+    L->K = c.top_k;
+    L->fs = c.shared_d_ff;
+    L->d_pad = round_up(L->d, dg::BK);
+    L->f_pad = round_up(L->f, dg::BK);
+    L->fs_pad = round_up(std::max<int64_t>(L->fs, 1), dg::BK);
+    L->expert_set.assign(L->E, 0);
+    int r = KTMOE_OK;
+    auto bail = [&](int code) {
+        delete L;
+        return code;
+    };
+    if ((r = alloc_planes(ctx, L->b_router, L->w_router, 1, L->E, L->d))) return bail(r);
+    if ((r = alloc_planes(ctx, L->b_gu, L->w_gu, L->E, 2 * L->f, L->d))) return bail(r);
+    if ((r = alloc_planes(ctx, L->b_dn, L->w_dn, L->E, L->d, L->f))) return bail(r);
+    if (L->fs > 0) {
+        if ((r = alloc_planes(ctx, L->b_sgu, L->w_sgu, 1, 2 * L->fs, L->d))) return bail(r);
+        if ((r = alloc_planes(ctx, L->b_sdn, L->w_sdn, 1, L->d, L->fs))) return bail(r);
+    }
+    L->h_wsc.assign(3 * L->E + 3, Scale{0, 0});
+    if (L->b_wsc.ensure(L->h_wsc.size() * sizeof(Scale)) != cudaSuccess) return bail(fail(ctx, KTMOE_ERR_CUDA, "scales"));
+    for (int kind = 0; kind < 3; ++kind) hp::build_table(kind, &L->tabs[kind]);
+    L->silu_code_scale_recip = kt::scale_recip(S(L->tabs[1].code_scale));
+    if (L->b_luts.ensure(3 * mk::LUT_N * 8) != cudaSuccess) return bail(fail(ctx, KTMOE_ERR_CUDA, "tables"));
+    for (int kind = 0; kind < 3; ++kind)
+        if (cudaMemcpy(L->b_luts.as<int64_t>() + kind * mk::LUT_N, L->tabs[kind].codes.data(), mk::LUT_N * 8,
+                       cudaMemcpyHostToDevice) != cudaSuccess)
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "tables"));
+    if (L->b_rbias.ensure(L->E * 8) != cudaSuccess || L->b_sigbias.ensure(L->E * 8) != cudaSuccess)
+        return bail(fail(ctx, KTMOE_ERR_CUDA, "bias"));
+    if ((size_t)L->d * 8 > 48 * 1024) {
+        if (cudaFuncSetAttribute(mk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
+            cudaSuccess)
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
+    }
+    *out = L;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_destroy(ktmoe_layer* L) {
+    if (!L) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    DevBuf* bufs[] = {&L->b_router, &L->b_gu, &L->b_dn, &L->b_sgu, &L->b_sdn, &L->b_rbias, &L->b_sigbias, &L->b_wsc,
+                      &L->b_luts, &L->x_in, &L->y_out, &L->scal, &L->tok_planes, &L->tok_xmax, &L->tok_sqx,
+                      &L->router_acc, &L->logits, &L->logit_scale, &L->top_e, &L->top_ec, &L->sumc, &L->counts,
+                      &L->chunk_off, &L->expert_off, &L->group_end, &L->expert_count, &L->tile_group, &L->tile_row0,
+                      &L->slot_row, &L->row_assign, &L->row_expert, &L->xg_planes, &L->acc_gu, &L->hq_planes,
+                      &L->row_cd, &L->acc_d, &L->tok_out, &L->tok_scale, &L->y_routed, &L->xs_planes, &L->acc_sgu,
+                      &L->hs_planes, &L->acc_sd};
+    for (DevBuf* b : bufs) b->release();
+    delete L;
+    return KTMOE_OK;
+}
+
+static int push_scales(ktmoe_layer* L) {
+    ktmoe_ctx* ctx = L->ctx;
+    CK(cudaMemcpy(L->b_wsc.p, L->h_wsc.data(), L->h_wsc.size() * sizeof(Scale), cudaMemcpyHostToDevice));
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_router(ktmoe_layer* L, const int32_t* codes, ktmoe_scale w_scale, const int64_t* bias_codes,
+                           ktmoe_scale bias_scale) {
+    if (!L || !codes) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = upload_matrix(ctx, L->w_router, 0, codes, L->E, L->d, 0)) return r;
+    L->router_ws = S(w_scale);
+    L->has_rbias = bias_codes != nullptr;
+    if (bias_codes) {
+        for (int64_t o = 0; o < L->E; ++o)
+            if (bias_codes[o] > (int64_t)INT32_MAX || bias_codes[o] < (int64_t)INT32_MIN)
+                return fail(ctx, KTMOE_ERR_RANGE, "a router bias code does not fit int32");
+        CK(cudaMemcpy(L->b_rbias.p, bias_codes, L->E * 8, cudaMemcpyHostToDevice));
+        L->router_bscale = S(bias_scale);
+    }
+    L->router_set = true;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_sigmoid_bias(ktmoe_layer* L, const int64_t* bias_codes) {
+    if (!L || !bias_codes) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->cfg.router_score != 1) return fail(ctx, KTMOE_ERR_ARG, "the layer's router is not sigmoid");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    CK(cudaMemcpy(L->b_sigbias.p, bias_codes, L->E * 8, cudaMemcpyHostToDevice));
+    L->sigbias_set = true;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_expert(ktmoe_layer* L, int32_t e, const int32_t* gate, ktmoe_scale gate_scale, const int32_t* up,
+                           ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale) {
+    if (!L || !gate || !up || !down || e < 0 || e >= L->E) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = upload_matrix(ctx, L->w_gu, e, gate, L->f, L->d, 0)) return r;
+    if (int r = upload_matrix(ctx, L->w_gu, e, up, L->f, L->d, L->f)) return r;
+    if (int r = upload_matrix(ctx, L->w_dn, e, down, L->d, L->f, 0)) return r;
+    L->h_wsc[e] = S(gate_scale);
+    L->h_wsc[L->E + e] = S(up_scale);
+    L->h_wsc[2 * L->E + e] = S(down_scale);
+    if (int r = push_scales(L)) return r;
+    L->expert_set[e] = 1;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate_scale, const int32_t* up,
+                           ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale) {
+    if (!L || !gate || !up || !down) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->fs <= 0) return fail(ctx, KTMOE_ERR_ARG, "the layer has no shared expert");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = upload_matrix(ctx, L->w_sgu, 0, gate, L->fs, L->d, 0)) return r;
+    if (int r = upload_matrix(ctx, L->w_sgu, 0, up, L->fs, L->d, L->fs)) return r;
+    if (int r = upload_matrix(ctx, L->w_sdn, 0, down, L->d, L->fs, 0)) return r;
+    L->h_wsc[3 * L->E] = S(gate_scale);
+    L->h_wsc[3 * L->E + 1] = S(up_scale);
+    L->h_wsc[3 * L->E + 2] = S(down_scale);
+    if (int r = push_scales(L)) return r;
+    L->shared_set = true;
+    return KTMOE_OK;
+}
+
+int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
+                      int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream) {
+    if (!L || !x_dev || !x_scale_dev || !y_dev || !y_scale_dev || rows <= 0) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    return stage_forward(L, rows, x_dev, (const Scale*)x_scale_dev, y_dev, (Scale*)y_scale_dev, st);
+}
+
+int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                  ktmoe_scale* y_scale) {
+    if (!L || !x || !y || !y_scale || rows <= 0) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    cudaStream_t st = ctx->stream;
+    const size_t n = (size_t)(rows * L->d);
+    Scale xs = S(x_scale);
+    CK(cudaMemcpyAsync(L->x_in.p, x, n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+    if (int r = stage_forward(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
+                              scal_scale(L, SL_YSCALE), st))
+        return r;
+    Scale ys;
+    CK(cudaMemcpyAsync(y, L->y_out.p, n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(&ys, scal_scale(L, SL_YSCALE), sizeof(Scale), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (int r = check_err_word(ctx)) return r;
+    *y_scale = C(ys);
+    return KTMOE_OK;
+}
+
+int ktmoe_route(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* experts, int64_t* ec,
+                int64_t* sumc) {
+    if (!L || !x || !experts || !ec || !sumc || rows <= 0) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!L->router_set || (L->cfg.router_score == 1 && !L->sigbias_set))
+        return fail(ctx, KTMOE_ERR_STATE, "the router is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    cudaStream_t st = ctx->stream;
+    Scale xs = S(x_scale);
+    CK(cudaMemcpyAsync(L->x_in.p, x, (size_t)(rows * L->d) * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+    if (int r = stage_route(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), st)) return r;
+    CK(cudaMemcpyAsync(experts, L->top_e.p, (size_t)(rows * L->K) * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(ec, L->top_ec.p, (size_t)(rows * L->K) * 8, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(sumc, L->sumc.p, (size_t)rows * 8, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return check_err_word(ctx);
+}
+
+// Internal buffers of the last forward, for stage-level checks: which = 0 router logits [rows][E] int32,
+// 1 logit scales [rows], 2 per-token combine outputs [rows][d] int32, 3 their scales [rows].
+int ktmoe_layer_debug_fetch(ktmoe_layer* L, int32_t which, void* host, int64_t bytes) {
+    if (!L || !host || bytes < 0) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    const DevBuf* b = which == 0 ? &L->logits : which == 1 ? &L->logit_scale : which == 2 ? &L->tok_out : &L->tok_scale;
+    if ((size_t)bytes > b->bytes) return fail(ctx, KTMOE_ERR_ARG, "debug fetch beyond the buffer");
+    CK(cudaStreamSynchronize(ctx->stream));
+    CK(cudaMemcpy(host, b->p, (size_t)bytes, cudaMemcpyDeviceToHost));
+    return KTMOE_OK;
+}
+
+// ── offline host preparation ──
+int ktmoe_quantize_weights(const float* w, int64_t n, int32_t* codes, ktmoe_scale* scale) {
+    if (n < 0 || (n > 0 && (!w || !codes)) || !scale) return KTMOE_ERR_ARG;
+    hp::HScale s;
+    hp::quantize_weights(w, (size_t)n, codes, &s);
+    *scale = ktmoe_scale{s.mant, s.shift};
+    return KTMOE_OK;
+}
+
+int ktmoe_quantize_bias(const float* b, int64_t n, int64_t* codes, ktmoe_scale* scale, int32_t* has_bias) {
+    if (!b || !codes || !scale || !has_bias || n < 0) return KTMOE_ERR_ARG;
+    hp::HScale s{0, 0};
+    *has_bias = hp::quantize_bias(b, (size_t)n, codes, &s) ? 1 : 0;
+    *scale = ktmoe_scale{s.mant, s.shift};
+    return KTMOE_OK;
+}
+
+int ktmoe_code_sigmoid_bias(const float* b, int64_t n, int64_t* codes) {
+    if (!b || !codes || n < 0) return KTMOE_ERR_ARG;
+    hp::code_sigmoid_bias(b, (size_t)n, codes);
+    return KTMOE_OK;
+}
+
+int ktmoe_from_reals(const float* v, int64_t n, int32_t* data, ktmoe_scale* scale) {
+    if (!v || !data || !scale || n < 0) return KTMOE_ERR_ARG;
+    hp::HScale s;
+    hp::from_reals(v, (size_t)n, data, &s);
+    *scale = ktmoe_scale{s.mant, s.shift};
+    return KTMOE_OK;
+}
+
+int ktmoe_table(int32_t kind, int64_t* codes, ktmoe_scale* inv_step, int64_t* lo_index, ktmoe_scale* code_scale) {
+    if (kind < 0 || kind > 2 || !codes || !inv_step || !lo_index || !code_scale) return KTMOE_ERR_ARG;
+    hp::HTable t;
+    hp::build_table(kind, &t);
+    std::memcpy(codes, t.codes.data(), t.codes.size() * 8);
+    *inv_step = ktmoe_scale{t.inv_step.mant, t.inv_step.shift};
+    *lo_index = t.lo_index;
+    *code_scale = ktmoe_scale{t.code_scale.mant, t.code_scale.shift};
+    return KTMOE_OK;
+}
+
+int ktmoe_synth_normal(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out) {
+    if (n < 0 || (n > 0 && !out)) return KTMOE_ERR_ARG;
+    hp::synth_normal(seed, sigma, offset, (size_t)n, out);
+    return KTMOE_OK;
+}
+
+int ktmoe_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, int64_t n, int32_t* out) {
+    if (n < 0 || (n > 0 && !out) || hi < lo) return KTMOE_ERR_ARG;
+    hp::lcg_uniform(seed, lo, hi, (size_t)n, out);
+    return KTMOE_OK;
+}
+
+}  // extern "C"

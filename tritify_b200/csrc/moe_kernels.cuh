@@ -1,0 +1,786 @@
+// The stages of tritify's integer MoE layer around the digit-plane GEMM, as sm_100a kernels.
+//
+// Reference semantics (paths relative to the reference project root):
+//   QuantLinear::forward_int        crates/01-engine/kt-core/src/layers.rs:275-328
+//   SwiGluMlp::forward_int          layers.rs:609-640
+//   MoeMlp::route / route_sigmoid   layers.rs:826-862, crates/01-engine/kt-core/src/router.rs:64-71
+//   MoeMlp::combine                 layers.rs:893-923
+//   forward_routed (merge)          layers.rs:988-1020
+//   add (routed + shared)           layers.rs:121-136
+// The reference runs the routed experts token by token; here every (token, slot) row that chose an expert is one
+// row of that expert's grouped GEMM. Every quantity the reference reduces per token (xmax, ymax, hmax, the scales)
+// is reduced per row here, and every tensor-global one (merge, shared expert, add) over the whole tensor.
+#pragma once
+
+#include <stdint.h>
+
+#include "fixed_point.cuh"
+
+namespace mk {
+
+using kt::Scale;
+
+constexpr int LUT_N = 1 << 16;
+
+// One table of the path (kt-int CodeLut, crates/00-kernels/kt-int/src/lib.rs:346-396): device codes + constants.
+struct Lut {
+    const int64_t* codes;
+    Scale inv_step;
+    int64_t lo_index;
+};
+
+// ───────────── block reductions ─────────────
+
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+        v = w > v ? w : v;
+    }
+    return v;
+}
+
+// Max over the block; every thread gets the result. `red` holds >= 32 entries.
+__device__ __forceinline__ uint64_t block_max_u64(uint64_t v, uint64_t* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+    v = warp_max_u64(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    uint64_t r = lane < nw ? red[lane] : 0;
+    r = warp_max_u64(r);
+    return r;
+}
+
+__device__ __forceinline__ uint64_t uabs64(int64_t v) { return v >= 0 ? (uint64_t)v : (uint64_t)(-(v + 1)) + 1; }
+
+__device__ __forceinline__ void store_digits4(int8_t* p0, int8_t* p1, int8_t* p2, const int32_t q[4]) {
+    int8_t a[4], b[4], c[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) kt::split_digits(q[j], a[j], b[j], c[j]);
+    *(char4*)p0 = make_char4(a[0], a[1], a[2], a[3]);
+    *(char4*)p1 = make_char4(b[0], b[1], b[2], b[3]);
+    *(char4*)p2 = make_char4(c[0], c[1], c[2], c[3]);
+}
+
+// ───────────── per-token quantisation of the layer input (QuantLinear::forward_int, layers.rs:279-298) ─────────────
+// For each token row: xmax = max|x|, qx = quant_to(x, xmax) written as three digit planes [3][R_pad][K_pad], and
+// s_qx = from_ratio(xmax, WLEVELS)·x.scale. Every linear that reads the row (router, each routed expert's gate and up)
+// quantises it identically, so the planes are computed once. `per_token == 0` uses one xmax for the whole tensor
+// (the shared expert, whose QuantLinear sees the whole [rows, dim] input): gxmax must hold that max.
+__global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K, int K_pad, long long R_pad,
+                                  int8_t* __restrict__ planes, int64_t* __restrict__ row_xmax, Scale* __restrict__ row_sqx,
+                                  const Scale* __restrict__ x_scale, const unsigned long long* __restrict__ gxmax) {
+    __shared__ uint64_t red[32];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int32_t* xr = x + (long long)r * K;
+    int64_t xmax;
+    if (gxmax) {
+        xmax = (int64_t)*gxmax;
+    } else {
+        uint64_t m = 0;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) m = max(m, uabs64(xr[k]));
+        xmax = (int64_t)block_max_u64(m, red);
+    }
+    int8_t* p0 = planes + (long long)r * K_pad;
+    int8_t* p1 = p0 + R_pad * K_pad;
+    int8_t* p2 = p1 + R_pad * K_pad;
+    for (int k4 = threadIdx.x * 4; k4 < K_pad; k4 += blockDim.x * 4) {
+        int32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int k = k4 + j;
+            q[j] = (k < K && xmax > 0) ? kt::quant_to(xr[k], xmax) : 0;
+        }
+        store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+    }
+    if (threadIdx.x == 0 && row_xmax) {
+        row_xmax[r] = xmax;
+        row_sqx[r] = xmax > 0 ? kt::scale_mul(kt::from_ratio((kt::u128)(uint64_t)xmax, (kt::u128)kt::WLEVELS), *x_scale)
+                              : kt::scale_zero();
+    }
+}
+
+// Global max |x| over n values (atomicMax into *out, which the caller zeroes).
+__global__ void absmax_i32_kernel(const int32_t* __restrict__ v, long long n, unsigned long long* out) {
+    __shared__ uint64_t red[32];
+    uint64_t m = 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        m = max(m, uabs64(v[i]));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(out, (unsigned long long)m);
+}
+
+// Global max |v| over the columns [c0, c0 + cols) of rows x ld int64 (atomicMax into *out).
+__global__ void absmax_i64_cols_kernel(const int64_t* __restrict__ v, int rows, long long ld, int c0, int cols,
+                                       unsigned long long* out) {
+    __shared__ uint64_t red[32];
+    uint64_t m = 0;
+    const long long n = (long long)rows * cols;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / cols, c = i % cols;
+        m = max(m, uabs64(v[r * ld + c0 + c]));
+    }
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(out, (unsigned long long)m);
+}
+
+// ───────────── routing: router logits → integer softmax / sigmoid codes → top-k (layers.rs:275-328, :800-862) ──────
+struct RouteArgs {
+    const int64_t* acc;  // [rows][E] router accumulators
+    const int64_t* row_xmax;
+    const Scale* row_sqx;
+    int rows, E, top_k, norm_topk, sigmoid;
+    Scale w_scale;
+    const int64_t* bias_codes;  // router QuantLinear bias (with_bias), or nullptr
+    Scale bias_scale;
+    const int64_t* sig_bias;  // sigmoid selection bias codes, or nullptr
+    Lut exp_lut, sig_lut;
+    int32_t* top_e;  // [rows][top_k]
+    int64_t* top_ec;
+    int64_t* sumc;
+    int32_t* logits_out;  // optional [rows][E]
+    Scale* logit_scale_out;
+};
+
+constexpr int ROUTE_MAX_PER_LANE = 16;  // E <= 512
+
+// One warp per token.
+__global__ void route_kernel(const RouteArgs a) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= a.rows) return;
+    const int E = a.E;
+    const int per = (E + 31) / 32;
+    int64_t acc[ROUTE_MAX_PER_LANE];
+    int32_t logit[ROUTE_MAX_PER_LANE];
+    const int64_t xmax = a.row_xmax[t];
+    Scale lscale = kt::scale_zero();
+    bool zero = false;
+    if (xmax == 0) {
+        // input all zero: the output is the bias codes at the bias scale, or zero (layers.rs:282-295)
+        for (int q = 0; q < per; ++q) {
+            const int o = lane + 32 * q;
+            logit[q] = (o < E && a.bias_codes) ? (int32_t)a.bias_codes[o] : 0;
+        }
+        lscale = a.bias_codes ? a.bias_scale : kt::scale_zero();
+    } else {
+        const Scale c = kt::scale_mul(a.row_sqx[t], a.w_scale);
+        if (c.mant == 0) {
+            zero = true;
+        } else {
+            Scale fb = kt::scale_zero();
+            if (a.bias_codes) fb = kt::scale_mul(a.bias_scale, kt::scale_recip(c));
+            uint64_t ymax = 0;
+            for (int q = 0; q < per; ++q) {
+                const int o = lane + 32 * q;
+                int64_t v = 0;
+                if (o < E) {
+                    v = a.acc[(long long)t * E + o];
+                    if (a.bias_codes) v += kt::scale_apply(fb, a.bias_codes[o]);
+                }
+                acc[q] = v;
+                ymax = max(ymax, uabs64(v));
+            }
+            ymax = warp_max_u64(ymax);
+            if (ymax == 0) {
+                zero = true;
+            } else {
+                for (int q = 0; q < per; ++q) logit[q] = kt::requant_act(acc[q], (int64_t)ymax);
+                lscale = kt::scale_mul(kt::ratio_act((int64_t)ymax), c);
+            }
+        }
+        if (zero)
+            for (int q = 0; q < per; ++q) logit[q] = 0;
+    }
+    if (a.logits_out) {
+        for (int q = 0; q < per; ++q) {
+            const int o = lane + 32 * q;
+            if (o < E) a.logits_out[(long long)t * E + o] = logit[q];
+        }
+        if (lane == 0) a.logit_scale_out[t] = lscale;
+    }
+
+    // Scores: softmax exp codes (layers.rs:832-840) or sigmoid codes + coded bias (router.rs:64-71).
+    int64_t code[ROUTE_MAX_PER_LANE], key[ROUTE_MAX_PER_LANE];
+    int64_t sum_all = 0;
+    if (!a.sigmoid) {
+        int32_t lmax = INT32_MIN;
+        for (int q = 0; q < per; ++q)
+            if (lane + 32 * q < E) lmax = max(lmax, logit[q]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax = max(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+        const Scale is = kt::scale_mul(lscale, a.exp_lut.inv_step);
+        for (int q = 0; q < per; ++q) {
+            const int o = lane + 32 * q;
+            int64_t ec = 0;
+            if (o < E) {
+                const int64_t idx = kt::scale_apply(is, (int64_t)(logit[q] - lmax)) - a.exp_lut.lo_index;
+                ec = idx < 0 ? 0 : a.exp_lut.codes[idx > LUT_N - 1 ? LUT_N - 1 : idx];
+            }
+            code[q] = ec;
+            key[q] = logit[q];
+            sum_all += ec;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum_all += __shfl_xor_sync(0xffffffffu, sum_all, o);
+    } else {
+        const Scale is = kt::scale_mul(lscale, a.sig_lut.inv_step);
+        for (int q = 0; q < per; ++q) {
+            const int o = lane + 32 * q;
+            int64_t c = 0, k = 0;
+            if (o < E) {
+                int64_t idx = kt::scale_apply(is, (int64_t)logit[q]) - a.sig_lut.lo_index;
+                idx = idx < 0 ? 0 : (idx > LUT_N - 1 ? LUT_N - 1 : idx);
+                c = a.sig_lut.codes[idx];
+                k = c + (a.sig_bias ? a.sig_bias[o] : 0);
+            }
+            code[q] = c;
+            key[q] = k;
+        }
+    }
+
+    // Top-k: descending key, ties to the lower index (layers.rs:800-805); k rounds of a warp arg-max.
+    unsigned taken = 0;  // bit q: this lane's candidate q was chosen
+    int64_t sel_sum = 0;
+    for (int i = 0; i < a.top_k; ++i) {
+        int64_t bk = INT64_MIN;
+        int bi = INT32_MAX;
+        for (int q = 0; q < per; ++q) {
+            const int o = lane + 32 * q;
+            if (o < E && !(taken & (1u << q))) {
+                if (key[q] > bk || (key[q] == bk && o < bi)) {
+                    bk = key[q];
+                    bi = o;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int64_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ok > bk || (ok == bk && oi < bi)) {
+                bk = ok;
+                bi = oi;
+            }
+        }
+        // the owner lane marks it and publishes its code
+        int64_t ec = 0;
+        if ((bi & 31) == lane) {
+            const int q = bi >> 5;
+            taken |= 1u << q;
+            ec = code[q];
+        }
+        ec = __shfl_sync(0xffffffffu, ec, bi & 31);
+        sel_sum += ec;
+        if (lane == 0) {
+            a.top_e[(long long)t * a.top_k + i] = bi;
+            a.top_ec[(long long)t * a.top_k + i] = ec;
+        }
+    }
+    if (lane == 0) {
+        int64_t s;
+        if (a.sigmoid)
+            s = a.norm_topk ? sel_sum : (int64_t(1) << kt::ROUTER_CODE_BITS);
+        else
+            s = a.norm_topk ? sel_sum : sum_all;
+        a.sumc[t] = s;
+    }
+}
+
+// ───────────── dispatch plan: a stable counting sort of (token, slot) by expert ─────────────
+constexpr int PLAN_CHUNK = 2048;  // assignments per chunk
+constexpr int PLAN_THREADS = 256;
+
+__global__ void plan_count_kernel(const int32_t* __restrict__ top_e, long long n_assign, int E, int* __restrict__ counts) {
+    extern __shared__ int hist[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const long long base = (long long)blockIdx.x * PLAN_CHUNK;
+    for (int j = threadIdx.x; j < PLAN_CHUNK; j += blockDim.x) {
+        const long long a = base + j;
+        if (a < n_assign) atomicAdd(&hist[top_e[a]], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(long long)blockIdx.x * E + e] = hist[e];
+}
+
+// One block: per-expert offsets, per-chunk offsets within each expert, and the n-tile table of the grouped GEMMs.
+__global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, int E, int BN, int* __restrict__ chunk_off,
+                                 int* __restrict__ expert_off, int* __restrict__ group_end, int* __restrict__ tile_group,
+                                 int* __restrict__ tile_row0, int* __restrict__ n_tiles, int* __restrict__ expert_count) {
+    extern __shared__ int sh[];
+    int* tot = sh;          // [E]
+    int* toff = sh + E;     // [E] tile offsets
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int run = 0;
+        for (int c = 0; c < n_chunks; ++c) {
+            chunk_off[(long long)c * E + e] = run;
+            run += counts[(long long)c * E + e];
+        }
+        tot[e] = run;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int off = 0, tiles = 0;
+        for (int e = 0; e < E; ++e) {
+            expert_off[e] = off;
+            expert_count[e] = tot[e];
+            off += tot[e];
+            group_end[e] = off;
+            toff[e] = tiles;
+            tiles += (tot[e] + BN - 1) / BN;
+        }
+        *n_tiles = tiles;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int nt = (tot[e] + BN - 1) / BN;
+        for (int i = 0; i < nt; ++i) {
+            tile_group[toff[e] + i] = e;
+            tile_row0[toff[e] + i] = expert_off[e] + i * BN;
+        }
+    }
+}
+
+// Stable positions: assignment a = t·k + i goes to expert_off[e] + chunk_off[chunk][e] + (rank among the same expert
+// earlier in its chunk). Rounds of blockDim assignments; warp match + per-warp counts give the rank.
+__global__ void plan_assign_kernel(const int32_t* __restrict__ top_e, long long n_assign, int E,
+                                   const int* __restrict__ chunk_off, const int* __restrict__ expert_off,
+                                   int* __restrict__ slot_row, int* __restrict__ row_assign, int* __restrict__ row_expert) {
+    extern __shared__ int sm[];
+    const int nw = blockDim.x >> 5;
+    int* running = sm;           // [E]
+    int* wcnt = sm + E;          // [nw][E]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) running[e] = 0;
+    for (int i = threadIdx.x; i < nw * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+    const long long base = (long long)blockIdx.x * PLAN_CHUNK;
+    for (int r0 = 0; r0 < PLAN_CHUNK; r0 += blockDim.x) {
+        const long long a = base + r0 + threadIdx.x;
+        const bool valid = (r0 + threadIdx.x < PLAN_CHUNK) && a < n_assign;
+        const int e = valid ? top_e[a] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const unsigned lt = (1u << lane) - 1u;
+        const int rank_w = __popc(peers & lt);
+        const bool leader = (peers & lt) == 0;
+        if (valid && leader) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (valid) {
+            int before = running[e];
+            for (int w = 0; w < warp; ++w) before += wcnt[w * E + e];
+            const int pos = expert_off[e] + chunk_off[(long long)blockIdx.x * E + e] + before + rank_w;
+            slot_row[a] = pos;
+            row_assign[pos] = (int)a;
+            row_expert[pos] = e;
+        }
+        __syncthreads();
+        for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+            int s = 0;
+            for (int w = 0; w < nw; ++w) {
+                s += wcnt[w * E + ee];
+                wcnt[w * E + ee] = 0;
+            }
+            running[ee] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// Gather: row r of the expert-sorted planes is token row_assign[r] / top_k of the token planes.
+__global__ void permute_planes_kernel(const int8_t* __restrict__ src, long long src_R_pad, int8_t* __restrict__ dst,
+                                      long long dst_R_pad, int K_pad, const int* __restrict__ row_assign, int top_k,
+                                      int n_rows) {
+    const int r = blockIdx.x;
+    if (r >= n_rows) return;
+    const int t = row_assign[r] / top_k;
+    const int n16 = K_pad / 16;
+#pragma unroll
+    for (int p = 0; p < 3; ++p) {
+        const int4* s = (const int4*)(src + (p * src_R_pad + t) * (long long)K_pad);
+        int4* d = (int4*)(dst + (p * dst_R_pad + r) * (long long)K_pad);
+        for (int i = threadIdx.x; i < n16; i += blockDim.x) d[i] = s[i];
+    }
+}
+
+// ───────────── SwiGLU + requant + down-input quantisation for routed rows (layers.rs:609-640, :279-298) ─────────────
+struct SwigluArgs {
+    int64_t* acc;  // [rows][2f]: gate in [0, f), up in [f, 2f); the gate half is overwritten by h
+    int rows, f, f_pad;
+    long long R_pad;  // rows of one plane of `planes`
+    const int* row_assign;  // routed: row -> token·top_k + slot (nullptr: row r is token r)
+    const int* row_expert;  // routed: row -> expert (nullptr: 0)
+    int top_k;
+    const Scale* row_sqx;   // per token (routed) ...
+    const Scale* g_sqx;     // ... or one scalar for the whole tensor (shared expert)
+    const Scale* wscale_g;  // [groups]
+    const Scale* wscale_u;
+    const Scale* wscale_d;
+    Lut silu;
+    Scale silu_code_scale, silu_code_scale_recip;
+    int8_t* planes;  // down-GEMM input digit planes [3][R_pad][f_pad]
+    Scale* row_cd;   // per row: s_qh·w_down (the down linear's c)
+    // tensor-global mode (shared expert): the maxima over the whole tensor, precomputed
+    const unsigned long long* g_ymax_g;
+    const unsigned long long* g_ymax_u;
+    unsigned long long* g_hmax;  // phase 1 output (atomicMax)
+    const unsigned long long* g_hmax_in;  // phase 2 input
+    int phase;  // 0: per-row (routed, all in one kernel); 1: global h pass; 2: global quantise pass
+};
+
+__global__ void swiglu_kernel(const SwigluArgs a) {
+    __shared__ uint64_t red[32];
+    __shared__ Scale sc[4];  // g scale, u scale, id_factor, index scale
+    __shared__ int64_t smax[2];
+    const int r = blockIdx.x;
+    if (r >= a.rows) return;
+    const int f = a.f;
+    int64_t* accg = a.acc + (long long)r * 2 * f;
+    const int64_t* accu = accg + f;
+    const int e = a.row_expert ? a.row_expert[r] : 0;
+    const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
+    int8_t* p0 = a.planes + (long long)r * a.f_pad;
+    int8_t* p1 = p0 + a.R_pad * a.f_pad;
+    int8_t* p2 = p1 + a.R_pad * a.f_pad;
+
+    int64_t hmax;
+    if (a.phase != 2) {
+        int64_t gmax_g, gmax_u;
+        if (a.phase == 0) {
+            uint64_t mg = 0, mu = 0;
+            for (int k = threadIdx.x; k < f; k += blockDim.x) {
+                mg = max(mg, uabs64(accg[k]));
+                mu = max(mu, uabs64(accu[k]));
+            }
+            mg = block_max_u64(mg, red);
+            __syncthreads();
+            mu = block_max_u64(mu, red);
+            gmax_g = (int64_t)mg;
+            gmax_u = (int64_t)mu;
+        } else {
+            gmax_g = (int64_t)*a.g_ymax_g;
+            gmax_u = (int64_t)*a.g_ymax_u;
+        }
+        if (threadIdx.x == 0) {
+            const Scale sqx = a.g_sqx ? *a.g_sqx : a.row_sqx[t];
+            const Scale cg = kt::scale_mul(sqx, a.wscale_g[e]);
+            const Scale cu = kt::scale_mul(sqx, a.wscale_u[e]);
+            // QuantLinear output scale: zero when c or ymax is zero (layers.rs:300-302, :321-326)
+            const Scale gs = (cg.mant == 0 || gmax_g == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_g), cg);
+            const Scale us = (cu.mant == 0 || gmax_u == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_u), cu);
+            sc[0] = gs;
+            sc[1] = us;
+            sc[2] = kt::scale_mul(gs, a.silu_code_scale_recip);  // id_factor (layers.rs:615)
+            sc[3] = kt::scale_mul(gs, a.silu.inv_step);          // CodeLut::index scale (kt-int lib.rs:383-385)
+            smax[0] = (cg.mant == 0) ? 0 : gmax_g;
+            smax[1] = (cu.mant == 0) ? 0 : gmax_u;
+        }
+        __syncthreads();
+        const Scale idf = sc[2], is = sc[3];
+        const int64_t mg = smax[0], mu = smax[1];
+        uint64_t hm = 0;
+        for (int k = threadIdx.x; k < f; k += blockDim.x) {
+            const int64_t g = mg ? (int64_t)kt::requant_act(accg[k], mg) : 0;
+            const int64_t u = mu ? (int64_t)kt::requant_act(accu[k], mu) : 0;
+            const int64_t idx = kt::scale_apply(is, g) - a.silu.lo_index;
+            int64_t code;
+            if (idx < 0)
+                code = 0;
+            else if (idx >= LUT_N)
+                code = kt::scale_apply(idf, g);  // identity right tail, in code units
+            else
+                code = a.silu.codes[idx];
+            const int64_t h = code * u;
+            accg[k] = h;
+            hm = max(hm, uabs64(h));
+        }
+        hm = block_max_u64(hm, red);
+        if (a.phase == 1) {
+            if (threadIdx.x == 0 && hm) atomicMax(a.g_hmax, (unsigned long long)hm);
+            return;
+        }
+        hmax = (int64_t)hm;
+    } else {
+        hmax = (int64_t)*a.g_hmax_in;
+        if (threadIdx.x == 0) {
+            const Scale sqx = *a.g_sqx;
+            const Scale cu = kt::scale_mul(sqx, a.wscale_u[e]);
+            const int64_t gmax_u = (int64_t)*a.g_ymax_u;
+            sc[1] = (cu.mant == 0 || gmax_u == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_u), cu);
+        }
+        __syncthreads();
+    }
+    // hint = requant_dyn(h, L, hmax); its max |.| is exactly L, so the down linear's quant_to divides by L.
+    for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
+        int32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int k = k4 + j;
+            int32_t v = 0;
+            if (k < f && hmax > 0) v = kt::quant_to(kt::requant_act(accg[k], hmax), kt::ACT_LEVELS);
+            q[j] = v;
+        }
+        store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+    }
+    if (threadIdx.x == 0 && (a.phase == 0 || r == 0)) {
+        Scale cd = kt::scale_zero();
+        if (hmax > 0) {
+            const Scale h_scale = kt::scale_mul(a.silu_code_scale, sc[1]);
+            const Scale hint_scale = kt::scale_mul(kt::ratio_act(hmax), h_scale);
+            const Scale s_qh = kt::scale_mul(kt::from_ratio((kt::u128)kt::ACT_LEVELS, (kt::u128)kt::WLEVELS), hint_scale);
+            cd = kt::scale_mul(s_qh, a.wscale_d[e]);
+        }
+        a.row_cd[a.phase == 0 ? r : 0] = cd;
+    }
+}
+
+// ───────────── combine: one token's selected experts → its output (layers.rs:893-923) ─────────────
+struct CombineArgs {
+    const int64_t* acc_d;  // [rows][dim] down accumulators (expert-sorted rows)
+    const Scale* row_cd;
+    const int* slot_row;   // [T][top_k] → row
+    const int64_t* top_ec;
+    const int64_t* sumc;
+    int T, top_k, dim;
+    int32_t* out;   // [T][dim]
+    Scale* out_scale;  // [T]
+};
+
+constexpr int COMBINE_MAX_K = 16;
+
+__global__ void combine_kernel(const CombineArgs a) {
+    extern __shared__ int64_t acc_s[];  // [dim]
+    __shared__ uint64_t red[32];
+    __shared__ int64_t ymax_s[COMBINE_MAX_K];
+    __shared__ Scale f_s[COMBINE_MAX_K];
+    __shared__ Scale common_s;
+    __shared__ int64_t ec_s[COMBINE_MAX_K];
+    __shared__ int row_s[COMBINE_MAX_K];
+    const int t = blockIdx.x;
+    if (t >= a.T) return;
+    const int K = a.top_k, D = a.dim;
+    int32_t* o = a.out + (long long)t * D;
+    const int64_t sumc = a.sumc[t];
+    if (sumc <= 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
+        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
+        return;
+    }
+    if (threadIdx.x < K) {
+        row_s[threadIdx.x] = a.slot_row[(long long)t * K + threadIdx.x];
+        ec_s[threadIdx.x] = a.top_ec[(long long)t * K + threadIdx.x];
+    }
+    __syncthreads();
+    for (int i = 0; i < K; ++i) {
+        const int64_t* y = a.acc_d + (long long)row_s[i] * D;
+        uint64_t m = 0;
+        for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(y[d]));
+        m = block_max_u64(m, red);
+        if (threadIdx.x == 0) ymax_s[i] = (int64_t)m;
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        // ys[i].scale: zero when its c or ymax is zero; common = the last of the largest (fold with ge, :898)
+        Scale ys[COMBINE_MAX_K];
+        Scale common = kt::scale_zero();
+        for (int i = 0; i < K; ++i) {
+            const Scale cd = a.row_cd[row_s[i]];
+            ys[i] = (cd.mant == 0 || ymax_s[i] == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax_s[i]), cd);
+            if (kt::scale_ge(ys[i], common)) common = ys[i];
+        }
+        common_s = common;
+        if (common.mant != 0) {
+            const Scale cinv = kt::scale_recip(common);
+            for (int i = 0; i < K; ++i) f_s[i] = kt::scale_mul(ys[i], cinv);
+        }
+    }
+    __syncthreads();
+    const Scale common = common_s;
+    if (common.mant == 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
+        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
+        return;
+    }
+    uint64_t gm = 0;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        int64_t s = 0;
+        for (int i = 0; i < K; ++i) {
+            if (f_s[i].mant == 0) continue;  // a zero-scale output contributes 0
+            const int64_t yv = (int64_t)kt::requant_act(a.acc_d[(long long)row_s[i] * D + d], ymax_s[i]);
+            s += ec_s[i] * kt::scale_apply(f_s[i], yv);
+        }
+        acc_s[d] = s;
+        gm = max(gm, uabs64(s));
+    }
+    gm = block_max_u64(gm, red);
+    const int64_t gmax = (int64_t)gm;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_act(acc_s[d], gmax) : 0;
+    if (threadIdx.x == 0) {
+        a.out_scale[t] = gmax == 0 ? kt::scale_zero()
+                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common),
+                                                   kt::from_ratio(1, (kt::u128)(uint64_t)sumc));
+    }
+}
+
+// ───────────── merge: per-token outputs → one tensor at one scale (layers.rs:1001-1019 / :866-886) ─────────────
+// The common scale is the LAST token whose scale value is maximal (fold `if b.ge(a) {b} else {a}`): a reduction over
+// (exact value, token index), larger index winning ties, gives the same token for any partition.
+struct ScaleIdx {
+    Scale s;
+    int idx;
+};
+
+__device__ __forceinline__ ScaleIdx better(ScaleIdx x, ScaleIdx y) {
+    const bool xy = kt::scale_ge(x.s, y.s), yx = kt::scale_ge(y.s, x.s);
+    if (xy && !yx) return x;
+    if (yx && !xy) return y;
+    return x.idx > y.idx ? x : y;
+}
+
+// One block: common scale over `n` scales (index offset idx0), result + its reciprocal into out[0..1].
+__global__ void common_scale_kernel(const Scale* __restrict__ scales, int n, int idx0, Scale* __restrict__ out,
+                                    int* __restrict__ out_idx) {
+    __shared__ ScaleIdx sm[1024];
+    ScaleIdx b{kt::scale_zero(), -1};
+    for (int i = threadIdx.x; i < n; i += blockDim.x) b = better(b, ScaleIdx{scales[i], idx0 + i});
+    sm[threadIdx.x] = b;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) sm[threadIdx.x] = better(sm[threadIdx.x], sm[threadIdx.x + s]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const Scale c = sm[0].s;
+        out[0] = c;
+        out[1] = c.mant ? kt::scale_recip(c) : kt::scale_zero();
+        if (out_idx) *out_idx = sm[0].idx;
+    }
+}
+
+// Pass 1 of the merge: max over all tokens of |f_t.apply(o_t[d])| (atomicMax into *gmax).
+__global__ void merge_max_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ o_scale, int T, int D,
+                                 const Scale* __restrict__ common, unsigned long long* __restrict__ gmax) {
+    __shared__ uint64_t red[32];
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const Scale cinv = common[1];
+    if (common[0].mant == 0) return;
+    const Scale f = kt::scale_mul(o_scale[t], cinv);
+    uint64_t m = 0;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(kt::scale_apply(f, o[(long long)t * D + d])));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(gmax, (unsigned long long)m);
+}
+
+// Pass 2: y = requant_dyn(f_t.apply(o_t), L, gmax); scale = from_ratio(gmax, L)·common.
+__global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ o_scale, int T, int D,
+                                   const Scale* __restrict__ common, const unsigned long long* __restrict__ gmax_p,
+                                   int32_t* __restrict__ y, Scale* __restrict__ y_scale) {
+    const int t = blockIdx.x;
+    if (t >= T) return;
+    const int64_t gmax = (int64_t)*gmax_p;
+    const bool zero = common[0].mant == 0 || gmax == 0;
+    const Scale f = zero ? kt::scale_zero() : kt::scale_mul(o_scale[t], common[1]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        y[(long long)t * D + d] = zero ? 0 : kt::requant_act(kt::scale_apply(f, o[(long long)t * D + d]), gmax);
+    if (t == 0 && threadIdx.x == 0) *y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common[0]);
+}
+
+// One token (rows == 1): the routed output is the combine output itself (layers.rs:992-994).
+__global__ void copy_row_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ os, int D, int32_t* __restrict__ y,
+                                Scale* __restrict__ ys) {
+    for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x) y[d] = o[d];
+    if (blockIdx.x == 0 && threadIdx.x == 0) *ys = os[0];
+}
+
+// ───────────── shared expert output and the final add (layers.rs:758-780, :121-136) ─────────────
+// Shared output: y_s = requant_dyn(acc, L, ymax) at scale from_ratio(ymax, L)·c_d, with ymax over the whole tensor.
+// add(routed, shared): common = routed.scale.ge(shared.scale) ? routed : shared.
+struct AddArgs {
+    const int32_t* a;  // routed [n]
+    const Scale* a_scale;
+    const int64_t* s_acc;  // shared down accumulators [n]
+    const unsigned long long* s_ymax;
+    const Scale* s_cd;  // shared down c (row_cd[0])
+    long long n;
+    unsigned long long* gmax;  // pass 1 out / pass 2 in
+    Scale* scratch;            // [0] shared scale, [1] common, [2] fa, [3] fb
+    int32_t* y;
+    Scale* y_scale;
+};
+
+__global__ void add_prepare_kernel(const AddArgs p) {
+    const int64_t ymax = (int64_t)*p.s_ymax;
+    const Scale cd = *p.s_cd;
+    const Scale ss = (cd.mant == 0 || ymax == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), cd);
+    const Scale as = *p.a_scale;
+    const Scale common = kt::scale_ge(as, ss) ? as : ss;
+    p.scratch[0] = ss;
+    p.scratch[1] = common;
+    if (common.mant) {
+        const Scale cinv = kt::scale_recip(common);
+        p.scratch[2] = kt::scale_mul(as, cinv);
+        p.scratch[3] = kt::scale_mul(ss, cinv);
+    } else {
+        p.scratch[2] = p.scratch[3] = kt::scale_zero();
+    }
+}
+
+__device__ __forceinline__ int64_t add_sum(const AddArgs& p, long long i, Scale fa, Scale fb, int64_t ymax) {
+    const int64_t sv = ymax ? (int64_t)kt::requant_act(p.s_acc[i], ymax) : 0;
+    return kt::scale_apply(fa, p.a[i]) + kt::scale_apply(fb, sv);
+}
+
+__global__ void add_max_kernel(const AddArgs p) {
+    __shared__ uint64_t red[32];
+    const Scale fa = p.scratch[2], fb = p.scratch[3];
+    const int64_t ymax = (int64_t)*p.s_ymax;
+    uint64_t m = 0;
+    if (p.scratch[1].mant)
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
+            m = max(m, uabs64(add_sum(p, i, fa, fb, ymax)));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(p.gmax, (unsigned long long)m);
+}
+
+__global__ void add_final_kernel(const AddArgs p) {
+    const Scale fa = p.scratch[2], fb = p.scratch[3], common = p.scratch[1];
+    const int64_t ymax = (int64_t)*p.s_ymax;
+    const int64_t gmax = (int64_t)*p.gmax;
+    const bool zero = common.mant == 0 || gmax == 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
+        p.y[i] = zero ? 0 : kt::requant_act(add_sum(p, i, fa, fb, ymax), gmax);
+    if (blockIdx.x == 0 && threadIdx.x == 0) *p.y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common);
+}
+
+// ───────────── LinearBackend helpers ─────────────
+// Pack int32 codes [rows][K] into three digit planes [3][R_pad][K_pad]; counts codes beyond ±WLEVELS into *bad.
+__global__ void pack_codes_kernel(const int32_t* __restrict__ codes, long long rows, int K, int K_pad, long long R_pad,
+                                  int8_t* __restrict__ planes, unsigned long long* __restrict__ bad) {
+    const long long r = blockIdx.x;
+    if (r >= rows) return;
+    const int32_t* c = codes + r * K;
+    int8_t* p0 = planes + r * K_pad;
+    int8_t* p1 = p0 + R_pad * K_pad;
+    int8_t* p2 = p1 + R_pad * K_pad;
+    unsigned nbad = 0;
+    for (int k4 = threadIdx.x * 4; k4 < K_pad; k4 += blockDim.x * 4) {
+        int32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int k = k4 + j;
+            int32_t v = k < K ? c[k] : 0;
+            if (v > (int32_t)kt::WLEVELS || v < -(int32_t)kt::WLEVELS) {
+                ++nbad;
+                v = 0;
+            }
+            q[j] = v;
+        }
+        store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+    }
+    if (nbad && bad) atomicAdd(bad, (unsigned long long)nbad);
+}
+
+}  // namespace mk
