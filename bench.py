@@ -1,0 +1,380 @@
+"""Benchmark: tritify's integer MoE layer on B200 — MoE-layer tokens/s, bit-exact.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one forward of one MoE layer over one batch of synthetic tokens (the reference has no
+normal RNG, so inputs come from the build-defined splitmix64 + Box-Muller generator). The default workload is BASELINE
+config 4, the largest configuration that fits one GPU: a Mixtral-8x7B-shaped layer (d_model 4096, 8 experts of
+d_ff 14336, top-2, norm_topk), 8192 prefill tokens. ``value`` is device-timed tokens/s with inputs resident in HBM;
+``e2e`` is the same metric through the public C ABI call (ktmoe_forward) with pinned host buffers, so every step
+includes the host-to-device copy of the tokens and the device-to-host read of the result. ``--impl reference`` times
+the reference's CPU integer path (its C++ restatement, oracle/, as the Rust reference cannot be built here) on a
+bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # BASELINE config 4 (i): Mixtral-8x7B-shaped, uniform router N(0, 0.02), prefill 8192 tokens.
+    "mixtral_prefill": dict(d=4096, E=8, f=14336, k=2, T=8192, norm=True, sigmoid=False, shared=0, wseed=1, xseed=0),
+    # the CPU-parity layer.
+    "config1": dict(d=2048, E=64, f=1408, k=8, T=512, norm=False, sigmoid=False, shared=0, wseed=1, xseed=0),
+    # Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
+    "qwen_prefill": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
+    "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
+    # BASELINE config 5, one layer: GLM-4.5-Air-shaped, sigmoid router with selection bias N(0, 0.02), shared expert.
+    "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
+    "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
+}
+METRIC = "MoE-layer tokens/s at 1/2/4/8 B200, bit-exact; % HBM / int8 tensor peak"
+P_PLANES = 9  # int8 plane products per code product (3 balanced base-81 digits each side)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def smi_index(local_rank: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        return vis.split(",")[local_rank].strip()
+    return str(local_rank)
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: str):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.index, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        loaded = [v for v in sm if v > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peaks():
+    try:
+        p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def build_product_layer(w, ctx, log_every=True):
+    """Quantise the workload's weights with the product's host quantiser (QuantLinear::from_weights) and make them
+    resident on the device, one matrix at a time (the Mixtral stack is 1.4 G weights)."""
+    import tritify_b200 as tb
+
+    d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
+    dev = tb.DeviceLayer(ctx, d, E, f, w["k"], w["norm"], w["sigmoid"], fs)
+    off = 0
+
+    def take(n):
+        nonlocal off
+        a = tb.synth_normal(w["wseed"], 0.02, n, offset=off)
+        off += n
+        return a
+
+    def q(n, rows, cols):
+        ql = tb.QuantLinear.from_weights("w", take(n), rows, cols)
+        return ql.w_codes, ql.w_scale
+
+    router = tb.QuantLinear.from_weights("router", take(E * d), E, d)
+    dev.set_router(router.w_codes, router.w_scale, None)
+    for e in range(E):
+        g = q(f * d, f, d)
+        u = q(f * d, f, d)
+        dn = q(d * f, d, f)
+        dev.set_expert(e, g, u, dn)
+    if fs:
+        g = q(fs * d, fs, d)
+        u = q(fs * d, fs, d)
+        dn = q(d * fs, d, fs)
+        dev.set_shared(g, u, dn)
+    if w["sigmoid"]:
+        b = tb.synth_normal(w["wseed"] + 2, 0.02, E)
+        codes = np.empty(E, dtype=np.int64)
+        import ctypes
+        tb.check(tb.lib().ktmoe_code_sigmoid_bias(b.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), E,
+                                                  codes.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))))
+        dev.set_sigmoid_bias(codes)
+    return dev
+
+
+def build_oracle_layer(w, O):
+    import tritify_b200 as tb
+
+    d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
+    off = 0
+
+    def take(n):
+        nonlocal off
+        a = tb.synth_normal(w["wseed"], 0.02, n, offset=off)
+        off += n
+        return a
+
+    router = take(E * d)
+    experts = take(E * 3 * f * d)
+    shared = take(3 * fs * d) if fs else None
+    sbias = tb.synth_normal(w["wseed"] + 2, 0.02, E) if w["sigmoid"] else None
+    return O.MoeOracle(d, E, f, w["k"], router, experts, norm_topk=w["norm"], sigmoid_bias=sbias,
+                       shared_hidden=fs, shared_w=shared)
+
+
+def make_x(w, rows=None):
+    import tritify_b200 as tb
+
+    T = w["T"] if rows is None else rows
+    return tb.IntTensor.from_reals(tb.synth_normal(w["xseed"], 1.0, T * w["d"]).reshape(T, w["d"]))
+
+
+def cpu_sample(w, seconds_target: float, O, max_rows=None):
+    """Time the oracle (the reference's CPU path, restated) on a bounded sample of the workload's tokens."""
+    O.lib().ko_set_max_threads(0)  # every host core, as the reference's default (TRITIFY_THREADS unset)
+    m = build_oracle_layer(w, O)
+    x = make_x(w)
+    xi = x.data.reshape(w["T"], w["d"])
+    xs = (x.scale.mant, x.scale.shift)
+    t0 = time.perf_counter()
+    m.forward(xi[:2], xs)
+    per_tok = max((time.perf_counter() - t0) / 2, 1e-6)
+    rows = int(max(1, min(max_rows or w["T"], seconds_target / per_tok)))
+    return m, xi, xs, rows
+
+
+def run_reference(args, w, name):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    m, xi, xs, rows = cpu_sample(w, budget, O)
+    for _ in range(args.warmup):
+        m.forward(xi[:rows], xs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward(xi[:rows], xs)
+    dt = (time.perf_counter() - t0) / args.steps
+    cores = os.cpu_count()
+    v = rows / dt
+    sample = f"first {rows} of {w['T']} tokens of {name} per step (C++ restatement of the reference CPU path)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")}},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_ours(args, w, name):
+    import torch
+
+    import tritify_b200 as tb
+
+    rank, world, local = dist_env()
+    if world > 1:
+        import ep
+
+        return ep.run(args, w, name)
+    torch.cuda.set_device(local)
+    ctx = tb.Context(local)
+    t_build = time.perf_counter()
+    dev = build_product_layer(w, ctx)
+    x = make_x(w)
+    T, d = w["T"], w["d"]
+    log(f"[bench] {name}: layer resident in {time.perf_counter() - t_build:.1f} s")
+
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    xd = torch.from_numpy(x.data.copy()).cuda()
+    xs_d = torch.tensor([x.scale.mant, x.scale.shift & 0xFFFFFFFF], dtype=torch.int64).cuda()
+    yd = torch.empty_like(xd)
+    ys_d = torch.zeros(2, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+
+    def step():
+        dev.forward_dev(xd.data_ptr(), T, xs_d.data_ptr(), yd.data_ptr(), ys_d.data_ptr(), 0)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ctx.sync()
+    # bit-exactness of the benchmarked forward: equal to the host-API forward of the same input, and deterministic
+    y_ref, ys_ref = dev.forward(x.data, T, x.scale)
+    ok_exact = bool((yd.cpu().numpy() == y_ref).all()) and int(ys_d[0]) == ys_ref.mant
+
+    # device-timed region: inputs resident in HBM; the 4.2 GB of weight planes exceed the 126 MB L2, so every step
+    # streams them from HBM (no separate flush)
+    dev.set_timing(True)
+    dev.stage_times()
+    launches0 = ctx.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_index(local)) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        end.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    launches = (ctx.launch_count() - launches0)
+    stages, nfw = dev.stage_times()
+    dev.set_timing(False)
+    stage_ms = {k: v / max(1, nfw) for k, v in stages.items()}
+
+    # e2e through the public C ABI (ktmoe_forward): pinned host buffers, H2D + forward + D2H every step
+    import ctypes
+
+    xh = torch.empty(T * d, dtype=torch.int32, pin_memory=True)
+    xh.numpy()[:] = x.data
+    yh = torch.empty(T * d, dtype=torch.int32, pin_memory=True)
+    ysh = tb.KtmoeScale()
+    i32p = ctypes.POINTER(ctypes.c_int32)
+
+    def e2e_step():
+        ctx.check(tb.lib().ktmoe_forward(dev.handle, ctypes.cast(xh.data_ptr(), i32p), T, x.scale._c(),
+                                         ctypes.cast(yh.data_ptr(), i32p), ctypes.byref(ysh)))
+
+    for _ in range(2):
+        e2e_step()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(3, args.steps // 2)
+    e_start.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e_end.record(stream)
+    e_end.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / e_steps
+    ok_exact = ok_exact and bool((yh.numpy() == y_ref).all())
+
+    # roofline of the dominant kernel: the routed gate/up digit-plane GEMM (int8 tensor bound)
+    hbm, bf16, peak_kind = measured_peaks()
+    R = T * w["k"]
+    gu_ops = 2.0 * R * d * (2 * w["f"]) * P_PLANES
+    dn_ops = 2.0 * R * w["f"] * d * P_PLANES
+    gu_ms = stage_ms["gemm_gate_up"]
+    int8_peak = 2.0 * bf16  # dense int8 : bf16 = 2 : 1 on B200
+    achieved = gu_ops / (gu_ms * 1e-3) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", f"traffic_{name}.json")
+    if os.path.exists(tpath):
+        traffic = json.load(open(tpath)).get("gemm_gate_up_dram_bytes_per_launch")
+
+    value = T / (ms * 1e-3)
+    res = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
+        "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
+                   "parallelism": "ep1", "l2": "working set (weight planes) larger than L2, no flush",
+                   "bit_exact_vs_host_api": ok_exact},
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * d * 4 + 16,
+                "d2h_bytes_per_step": T * d * 4 + 16},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
+                     "frac": achieved / int8_peak, "traffic": traffic, "kernel": "digit_gemm gate/up",
+                     "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
+                     "ops_per_launch": gu_ops, "plane_products": P_PLANES},
+        "stage_ms": stage_ms,
+        "gemm_down_tops": dn_ops / (stage_ms["gemm_down"] * 1e-3) / 1e12,
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and not args.no_cpu:
+        from oracle import oracle as O
+
+        O.build()
+        m, xi, xs, rows = cpu_sample(w, 15.0, O)
+        t0 = time.perf_counter()
+        m.forward(xi[:rows], xs)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": rows / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                               "sample": f"first {rows} of {T} tokens, one forward (C++ restatement of the "
+                                         f"reference CPU path, its own thread policy over all cores)"}
+    print(json.dumps(res), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="mixtral_prefill", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w, args.workload)
+    else:
+        run_ours(args, w, args.workload)
+
+
+if __name__ == "__main__":
+    main()

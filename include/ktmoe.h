@@ -109,6 +109,13 @@ int ktmoe_route(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale 
 /* Kernel launches of this library on the context since open (the device work is all this library's own kernels). */
 int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
 
+/* Per-stage timing with CUDA events on the forward's stream (tracing; off by default). With it on, every forward
+ * records one event per stage boundary; ktmoe_layer_stage_times waits for them, returns the summed milliseconds per
+ * stage over the timed forwards (stages: 0 quantise+route, 1 dispatch, 2 gate/up GEMM, 3 SwiGLU, 4 down GEMM,
+ * 5 combine, 6 merge, 7 shared expert + add; n_stages >= 8) and forgets them. */
+int ktmoe_layer_set_timing(ktmoe_layer* layer, int32_t enable);
+int ktmoe_layer_stage_times(ktmoe_layer* layer, double* ms, int32_t n_stages, int32_t* n_forwards);
+
 /* Diagnostics: copy an internal buffer of the last forward or route (which = 0: router logits [rows][E] int32,
  * 1: their scales [rows], 2: per-token combine outputs [rows][d_model] int32, 3: their scales [rows]). */
 int ktmoe_layer_debug_fetch(ktmoe_layer* layer, int32_t which, void* host, int64_t bytes);

@@ -321,6 +321,18 @@ class DeviceLayer:
                                          _p(ec, ctypes.c_int64), _p(sumc, ctypes.c_int64)))
         return ex.reshape(rows, self.top_k), ec.reshape(rows, self.top_k), sumc
 
+    STAGES = ["route", "dispatch", "gemm_gate_up", "swiglu", "gemm_down", "combine", "merge", "shared"]
+
+    def set_timing(self, enable: bool) -> None:
+        self.ctx.check(lib().ktmoe_layer_set_timing(self._h, 1 if enable else 0))
+
+    def stage_times(self):
+        """(per-stage milliseconds summed over the timed forwards, number of timed forwards)."""
+        ms = (ctypes.c_double * 8)()
+        n = ctypes.c_int32()
+        self.ctx.check(lib().ktmoe_layer_stage_times(self._h, ms, 8, ctypes.byref(n)))
+        return dict(zip(self.STAGES, list(ms))), n.value
+
     def debug_fetch(self, which: int, rows: int):
         """Internal buffers of the last forward (router logits / their scales / per-token outputs / their scales)."""
         if which in (0, 2):

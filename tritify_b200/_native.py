@@ -59,6 +59,8 @@ SIGNATURES = {
     "ktmoe_route": ([_vp, _i32p, _i64, KtmoeScale, _i32p, _i64p, _i64p], ctypes.c_int),
     "ktmoe_launch_count": ([_vp, _P(_u64)], ctypes.c_int),
     "ktmoe_layer_debug_fetch": ([_vp, _i32, _vp, _i64], ctypes.c_int),
+    "ktmoe_layer_set_timing": ([_vp, _i32], ctypes.c_int),
+    "ktmoe_layer_stage_times": ([_vp, _P(ctypes.c_double), _i32, _P(_i32)], ctypes.c_int),
     "ktmoe_quantize_weights": ([_f32p, _i64, _i32p, _P(KtmoeScale)], ctypes.c_int),
     "ktmoe_quantize_bias": ([_f32p, _i64, _i64p, _P(KtmoeScale), _P(_i32)], ctypes.c_int),
     "ktmoe_code_sigmoid_bias": ([_f32p, _i64, _i64p], ctypes.c_int),

@@ -266,6 +266,9 @@ struct ktmoe_layer {
         row_expert;
     DevBuf xg_planes, acc_gu, hq_planes, row_cd, acc_d, tok_out, tok_scale, y_routed;
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
+    // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
+    bool timing = false;
+    std::vector<cudaEvent_t> events;
 };
 
 namespace {
@@ -346,6 +349,24 @@ bool layer_complete(const ktmoe_layer* L) {
     return true;
 }
 
+// Stage boundaries recorded when timing is on (see ktmoe_layer_stage_times).
+enum Stage { ST_ROUTE = 0, ST_DISPATCH, ST_GEMM_GU, ST_SWIGLU, ST_GEMM_DOWN, ST_COMBINE, ST_MERGE, ST_SHARED, ST_N };
+
+int mark(ktmoe_layer* L, cudaStream_t st) {
+    if (!L->timing) return KTMOE_OK;
+    ktmoe_ctx* ctx = L->ctx;
+    cudaEvent_t e;
+    CK(cudaEventCreate(&e));
+    L->events.push_back(e);
+    CK(cudaEventRecord(e, st));
+    return KTMOE_OK;
+}
+
+#define MARK(L, st)                              \
+    do {                                         \
+        if (int m__ = mark((L), (st))) return m__; \
+    } while (0)
+
 mk::Lut lut(const ktmoe_layer* L, int kind) {
     mk::Lut l;
     l.codes = L->b_luts.as<int64_t>() + (int64_t)kind * mk::LUT_N;
@@ -406,8 +427,10 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     const int64_t R = T * K;
     const int64_t T_pad = round_up(T, 64), R_pad = round_up(R, 64);
     CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
+    MARK(L, st);
     int r = stage_route(L, T, x_dev, xs_dev, st);
     if (r) return r;
+    MARK(L, st);
 
     // dispatch plan: stable counting sort of the T·K assignments by expert
     const int BN = pick_bn((double)R / (double)E);
@@ -428,6 +451,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     mk::permute_planes_kernel<<<(unsigned)R, 128, 0, st>>>(L->tok_planes.as<int8_t>(), T_pad, L->xg_planes.as<int8_t>(),
                                                          R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
     CKL(ctx);
+    MARK(L, st);
 
     // routed gate+up: one grouped GEMM over the E experts
     const int64_t max_tiles = (R + BN - 1) / BN + E;
@@ -445,6 +469,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     g.n_tiles = n_tiles_ptr(L);
     r = run_gemm(ctx, st, g);
     if (r) return r;
+    MARK(L, st);
 
     mk::SwigluArgs sa;
     std::memset(&sa, 0, sizeof(sa));
@@ -469,6 +494,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sa.phase = 0;
     mk::swiglu_kernel<<<(unsigned)R, 256, 0, st>>>(sa);
     CKL(ctx);
+    MARK(L, st);
 
     g.A = L->w_dn;
     g.M_valid = d;
@@ -477,6 +503,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     g.ld_out = d;
     r = run_gemm(ctx, st, g);
     if (r) return r;
+    MARK(L, st);
 
     mk::CombineArgs ca;
     ca.acc_d = L->acc_d.as<int64_t>();
@@ -491,6 +518,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     ca.out_scale = L->tok_scale.as<Scale>();
     mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
     CKL(ctx);
+    MARK(L, st);
 
     int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
     Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
@@ -509,6 +537,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
                                                           routed, routed_scale);
         CKL(ctx);
     }
+    MARK(L, st);
     if (fs == 0) return KTMOE_OK;
 
     // shared expert on the whole tensor (global maxima), then add(routed, shared)
@@ -594,6 +623,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     CKL(ctx);
     mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
     CKL(ctx);
+    MARK(L, st);
     return KTMOE_OK;
 }
 
@@ -1048,6 +1078,40 @@ int ktmoe_route(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_sc
     CK(cudaMemcpyAsync(sumc, L->sumc.p, (size_t)rows * 8, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return check_err_word(ctx);
+}
+
+int ktmoe_layer_set_timing(ktmoe_layer* L, int32_t enable) {
+    if (!L) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(L->ctx->mu);
+    L->timing = enable != 0;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_stage_times(ktmoe_layer* L, double* ms, int32_t n_stages, int32_t* n_forwards) {
+    if (!L || !ms || !n_forwards || n_stages < ST_N) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    for (int i = 0; i < n_stages; ++i) ms[i] = 0.0;
+    *n_forwards = 0;
+    // Each timed forward recorded 1 + (stages it ran) events; stages run in order, so split the sequence at
+    // every first event (the one recorded before routing) by counting: a forward records ST_MERGE + 2 events
+    // without a shared expert and ST_SHARED + 2 with one.
+    const size_t per = (size_t)((L->fs > 0 ? ST_SHARED : ST_MERGE) + 2);
+    const size_t nf = L->events.size() / per;
+    for (size_t f = 0; f < nf; ++f) {
+        for (size_t i = 0; i + 1 < per; ++i) {
+            cudaEvent_t a = L->events[f * per + i], b = L->events[f * per + i + 1];
+            CK(cudaEventSynchronize(b));
+            float t = 0.f;
+            CK(cudaEventElapsedTime(&t, a, b));
+            ms[i] += t;
+        }
+    }
+    for (cudaEvent_t e : L->events) cudaEventDestroy(e);
+    L->events.clear();
+    *n_forwards = (int32_t)nf;
+    return KTMOE_OK;
 }
 
 // Internal buffers of the last forward, for stage-level checks: which = 0 router logits [rows][E] int32,
