@@ -24,6 +24,13 @@ int32_t fp_quant_to(int32_t d, int64_t xmax) { return kt::quant_to(d, xmax); }
 void fp_split(int32_t v, int8_t* d) { kt::split_digits(v, d[0], d[1], d[2]); }
 int64_t fp_recombine(int32_t a, int32_t b, int32_t c, int32_t d, int32_t e) { return kt::recombine(a, b, c, d, e); }
 
+int32_t fp_requant_act_fast(int64_t v, int64_t den) { return kt::requant_act_fast(v, kt::make_div((uint64_t)den)); }
+int64_t fp_apply_small(fp_scale s, int64_t v) { return kt::scale_apply_small(S(s), v); }
+int32_t fp_quant_to_act(int32_t d) { return kt::quant_to_act(d); }
+void fp_requant_act_fast_n(const int64_t* v, const int64_t* den, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::requant_act_fast(v[i], kt::make_div((uint64_t)den[i]));
+}
+
 // Batched forms for speed.
 void fp_requant_act_n(const int64_t* v, const int64_t* den, int32_t* out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = kt::requant_act(v[i], den[i]);
@@ -34,4 +41,14 @@ void fp_quant_to_n(const int32_t* d, const int64_t* xmax, int32_t* out, int64_t 
 void fp_apply_n(const fp_scale* s, const int64_t* v, int64_t* out, int64_t n) {
     for (int64_t i = 0; i < n; ++i) out[i] = kt::scale_apply(S(s[i]), v[i]);
 }
+}
+
+extern "C" {
+void fp_requant_row_n(const int64_t* v, const int64_t* den, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::requant_row(v[i], kt::make_req(den[i]));
+}
+void fp_quant_row_n(const int32_t* d, const int64_t* xmax, int32_t* out, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) out[i] = kt::quant_row(d[i], kt::make_quant(xmax[i]));
+}
+int64_t fp_apply_row(fp_scale s, int64_t v) { return kt::apply_row(kt::make_apply(S(s)), v); }
 }

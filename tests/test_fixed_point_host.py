@@ -37,6 +37,15 @@ def fp(tmp_path_factory):
     L.fp_quant_to.argtypes = [ctypes.c_int32, ctypes.c_int64]
     L.fp_quant_to.restype = ctypes.c_int32
     L.fp_split.argtypes = [ctypes.c_int32, P(ctypes.c_int8)]
+    L.fp_requant_act_fast_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    L.fp_apply_small.argtypes = [FpScale, ctypes.c_int64]
+    L.fp_apply_small.restype = ctypes.c_int64
+    L.fp_quant_to_act.argtypes = [ctypes.c_int32]
+    L.fp_quant_to_act.restype = ctypes.c_int32
+    L.fp_requant_row_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    L.fp_quant_row_n.argtypes = [P(ctypes.c_int32), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    L.fp_apply_row.argtypes = [FpScale, ctypes.c_int64]
+    L.fp_apply_row.restype = ctypes.c_int64
     L.fp_requant_act_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
     L.fp_quant_to_n.argtypes = [P(ctypes.c_int32), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
     return L
@@ -117,3 +126,63 @@ def test_digit_split_covers_every_code(fp):
     assert list(d) == [40, 40, 40]
     fp.fp_split(-265720, d)
     assert list(d) == [-40, -40, -40]
+
+
+def test_fast_paths_equal_the_exact_ones(fp, oracle):
+    """The reciprocal-estimate division, the 64-bit apply and the power-of-two quant_to give the exact results."""
+    rng = np.random.default_rng(11)
+    n = 300000
+    den = np.maximum(rng.integers(1, 1 << 62, size=n, dtype=np.int64) >> rng.integers(0, 62, size=n), 1)
+    v = (rng.integers(-(1 << 62), 1 << 62, size=n, dtype=np.int64) % (den + 1)) * rng.choice([-1, 1], size=n)
+    v[:500], v[500:1000] = den[:500], -den[500:1000]
+    a, b = np.empty(n, np.int32), np.empty(n, np.int32)
+    P = ctypes.POINTER
+    args = (v.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)))
+    fp.fp_requant_act_n(*args, a.ctypes.data_as(P(ctypes.c_int32)), n)
+    fp.fp_requant_act_fast_n(*args, b.ctypes.data_as(P(ctypes.c_int32)), n)
+    assert (a == b).all()
+    g = _lcg(99)
+    for _ in range(20000):
+        s = oracle.from_ratio(next(g) % (1 << 60) + 1, next(g) % (1 << 60) + 1)
+        s = oracle.mul(s, oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
+        val = int(next(g) % (1 << 31)) - (1 << 30)
+        assert fp.fp_apply_small(FpScale(*s), val) == oracle.apply(s, val)
+        assert fp.fp_apply_small(FpScale(s[0], s[1] % 70), val) == oracle.apply((s[0], s[1] % 70), val)
+    for d in list(range(-(1 << 28), -(1 << 28) + 3000)) + list(range(-5000, 5000)) + list(range((1 << 28) - 3000, (1 << 28) + 1)):
+        assert fp.fp_quant_to_act(d) == oracle.quant_to(np.array([d]), 1 << 28)[0]
+
+
+def test_row_plans_equal_the_exact_ones(fp, oracle):
+    """The per-row plans of the hot loops (requant_row, quant_row, apply_row) against the exact i128 forms."""
+    rng = np.random.default_rng(12)
+    P = ctypes.POINTER
+    n = 2_000_000
+    for hi in (1 << 52, 1 << 62):  # the 64-bit path and the 128-bit fallback
+        den = np.maximum(rng.integers(1, hi, size=n, dtype=np.int64) >> rng.integers(0, 52, size=n), 1)
+        v = (rng.integers(0, 1 << 62, size=n, dtype=np.int64) % (den + 1)) * rng.choice([-1, 1], size=n)
+        v[::5], v[1::5], v[2::5] = den[::5], -den[1::5], den[2::5] // 2
+        v[3::5] = -((den[3::5] + 1) // 2)
+        a, b = np.empty(n, np.int32), np.empty(n, np.int32)
+        args = (v.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)))
+        fp.fp_requant_act_n(*args, a.ctypes.data_as(P(ctypes.c_int32)), n)
+        fp.fp_requant_row_n(*args, b.ctypes.data_as(P(ctypes.c_int32)), n)
+        assert (a == b).all()
+    xmax = rng.integers(1, 1 << 31, size=n, dtype=np.int64)
+    xmax[:1000] = 1
+    d = (rng.integers(-(1 << 31), 1 << 31, size=n, dtype=np.int64) % (xmax + 1)).astype(np.int32)
+    d[1000:2000] = xmax[1000:2000]
+    d[2000:3000] = -xmax[2000:3000]
+    a, b = np.empty(n, np.int32), np.empty(n, np.int32)
+    fp.fp_quant_to_n(d.ctypes.data_as(P(ctypes.c_int32)), xmax.ctypes.data_as(P(ctypes.c_int64)),
+                     a.ctypes.data_as(P(ctypes.c_int32)), n)
+    fp.fp_quant_row_n(d.ctypes.data_as(P(ctypes.c_int32)), xmax.ctypes.data_as(P(ctypes.c_int64)),
+                      b.ctypes.data_as(P(ctypes.c_int32)), n)
+    assert (a == b).all()
+    g = _lcg(7)
+    for _ in range(40000):
+        s = oracle.mul(oracle.from_ratio(next(g) % (1 << 60) + 1, next(g) % (1 << 60) + 1),
+                       oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
+        val = int(next(g) % (1 << 32)) - (1 << 31)
+        assert fp.fp_apply_row(FpScale(*s), val) == oracle.apply(s, val)
+        s2 = (s[0], s[1] % 70 - 3)
+        assert fp.fp_apply_row(FpScale(*s2), val) == oracle.apply(s2, val)

@@ -48,26 +48,42 @@ struct GemmArgs {
     const int* tile_group;     // per n-tile: group (nullptr: single group 0)
     const int* tile_row0;      // per n-tile: first activation row (nullptr: tile * BN)
     const int* group_row_end;  // per group: end row, exclusive (nullptr: single_rows)
-    const int* n_tiles;        // device count of valid n-tiles (nullptr: gridDim.y)
+    const int* n_tiles;        // device count of valid n-tiles (nullptr: n_tiles_max)
+    int n_tiles_max;           // upper bound of n-tiles (the launch covers m_tiles x n_tiles_max, rounded up)
+    int m_tiles;               // weight tiles of one group (M_pad / BM)
+    int group_n;               // raster: GROUP_N consecutive n-tiles share each weight tile while it is in L2
     int single_rows;
     int accumulate;  // 1: out += result (the second and later K chunks)
     int* err;        // device error word (first error wins)
+    // Optional fused reduction: atomicMax of |out[r][m]| into rowmax[r * rowmax_stride + (m >= rowmax_split)]
+    // (rowmax_stride 0 reduces the whole output into one or two words). Only valid without K chunking.
+    unsigned long long* rowmax;
+    int rowmax_stride;
+    int rowmax_split;
 };
 
-__host__ __device__ constexpr int tmem_cols_for(int bn) {
-    return (NDIAG * bn <= 32) ? 32 : (NDIAG * bn <= 64) ? 64 : (NDIAG * bn <= 128) ? 128 : (NDIAG * bn <= 256) ? 256 : 512;
+// TMEM columns to allocate for `accbn` = (buffers x BN): a power of two >= 32 covering five diagonals each.
+__host__ __device__ constexpr int tmem_cols_for(int accbn) {
+    return (NDIAG * accbn <= 32)    ? 32
+           : (NDIAG * accbn <= 64)  ? 64
+           : (NDIAG * accbn <= 128) ? 128
+           : (NDIAG * accbn <= 256) ? 256
+                                    : 512;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int ACC>
 struct Cfg {
     static constexpr int A_PLANE = BM * BK;
     static constexpr int B_PLANE = BN * BK;
     static constexpr int STAGE_BYTES = 3 * (A_PLANE + B_PLANE);
-    static constexpr int TMEM_COLS = tmem_cols_for(BN);
-    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
-    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 96, "BN: a multiple of 16 in [16, 96]");
-    static_assert(NDIAG * BN <= 512, "five accumulators must fit TMEM");
+    static constexpr int ACC_COLS = NDIAG * BN;  // one accumulator buffer: five diagonals of BN columns
+    static constexpr int TMEM_COLS = tmem_cols_for(ACC * BN);
+    static constexpr int RED_BYTES = 2 * 4 * BN * 8;  // row-max staging: [slot][epilogue warp][column]
+    static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + RED_BYTES;
+    static_assert(BN % 16 == 0 && BN >= 16 && 3 * BN <= 256, "BN: a multiple of 16, 3·BN <= 256");
+    static_assert(ACC * NDIAG * BN <= 512, "the accumulator buffers must fit TMEM");
     static_assert(B_PLANE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+    static_assert(SMEM_BYTES <= 232448, "shared memory per block");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -105,6 +121,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
             return false;
         }
     }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
@@ -158,28 +178,56 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t (&r)[16]) {
         : "r"(taddr));
 }
 
-template <int BN, int STAGES>
+// The tiles of one launch, in raster order. Slot L (0 <= L < m_tiles · group_n · n_groups) is weight tile
+// m = (L mod per_group) / group_n of n-tile (L / per_group) · group_n + L mod group_n: the blocks resident at one time
+// walk group_n activation tiles for each weight tile, so both stay in L2 while they are reused.
+struct TileIter {
+    int per_group, limit, n_tiles;
+    __device__ __forceinline__ bool get(const GemmArgs& a, int L, int& tile, int& m0) const {
+        if (L >= limit) return false;
+        const int grp = L / per_group, rem = L % per_group;
+        tile = grp * a.group_n + rem % a.group_n;
+        m0 = (rem / a.group_n) * BM;
+        return true;
+    }
+};
+
+struct TileInfo {
+    int group, row0, n_valid;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int tile, int bn) {
+    TileInfo t;
+    t.group = a.tile_group ? a.tile_group[tile] : 0;
+    t.row0 = a.tile_row0 ? a.tile_row0[tile] : tile * bn;
+    const int row_end = a.group_row_end ? a.group_row_end[t.group] : a.single_rows;
+    t.n_valid = min(bn, row_end - t.row0);
+    return t;
+}
+
+// Persistent: gridDim.x blocks (at most one per SM) walk the raster with stride gridDim.x. The TMA producer and the
+// MMA issuer run ahead across tile boundaries; ACC accumulator buffers in TMEM let the epilogue of one tile overlap
+// the MMAs of the next.
+template <int BN, int STAGES, int ACC>
 __global__ void __launch_bounds__(THREADS, 1)
     digit_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
-    using C = Cfg<BN, STAGES>;
+    using C = Cfg<BN, STAGES, ACC>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * 3 * C::A_PLANE;
     uint64_t* full = (uint64_t*)(smem + STAGES * C::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
-    uint64_t* accum = empty + STAGES;
-    uint32_t* tmem_slot = (uint32_t*)(accum + 1);
+    uint64_t* acc_full = empty + STAGES;     // [ACC]: the MMAs of a tile completed into buffer b
+    uint64_t* acc_empty = acc_full + ACC;    // [ACC]: the epilogue has read buffer b (128 arrivals)
+    uint32_t* tmem_slot = (uint32_t*)(acc_empty + ACC);
+    unsigned long long* sred = (unsigned long long*)(smem + STAGES * C::STAGE_BYTES + 256);
 
-    const int tile = blockIdx.y;
-    const int n_tiles = args.n_tiles ? *args.n_tiles : (int)gridDim.y;
-    if (tile >= n_tiles) return;  // the whole CTA leaves before any barrier or allocation
-    const int group = args.tile_group ? args.tile_group[tile] : 0;
-    const int row0 = args.tile_row0 ? args.tile_row0[tile] : tile * BN;
-    const int row_end = args.group_row_end ? args.group_row_end[group] : args.single_rows;
-    const int n_valid = min(BN, row_end - row0);
-    const int m0 = blockIdx.x * BM;
+    const int n_tiles = args.n_tiles ? *args.n_tiles : args.n_tiles_max;
+    const int n_groups = (n_tiles + args.group_n - 1) / args.group_n;
+    const TileIter it{args.m_tiles * args.group_n, args.m_tiles * args.group_n * n_groups, n_tiles};
+    if ((int)blockIdx.x >= it.limit) return;  // no tile for this block: leave before any barrier or allocation
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = args.num_k_blocks;
 
@@ -188,7 +236,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(accum, 1);
+        for (int b = 0; b < ACC; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 128);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -202,87 +253,176 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 4) {
-        if (lane == 0 && n_valid > 0) {
+        if (lane == 0) {
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
-            int issued = 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-                if (!mbar_wait(&empty[s], ph ^ 1u, args.err, ERR_TIMEOUT_EMPTY)) break;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
-                const int kx = (args.k_block0 + kb) * BK;
+            int q = 0;  // k-blocks issued by this block so far (its position in the stage ring)
+            bool alive = true;
+            int tile, m0;
+            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0); L += gridDim.x) {
+                if (tile >= n_tiles) continue;
+                const TileInfo ti = tile_info(args, tile, BN);
+                if (ti.n_valid <= 0) continue;
+                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                    const int s = q % STAGES;
+                    const uint32_t ph = (uint32_t)(q / STAGES) & 1u;
+                    if (!mbar_wait(&empty[s], ph ^ 1u, args.err, ERR_TIMEOUT_EMPTY)) {
+                        alive = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
+                    const int kx = (args.k_block0 + kb) * BK;
 #pragma unroll
-                for (int p = 0; p < 3; ++p) {
-                    tma_load_2d(sA + (s * 3 + p) * C::A_PLANE, &tmA, kx, (group * 3 + p) * args.M_pad + m0, &full[s]);
-                    tma_load_2d(sB + (s * 3 + p) * C::B_PLANE, &tmB, kx, p * args.R_pad + row0, &full[s]);
-                }
-                issued = kb + 1;
-            }
-            // Let the copies still in flight land before the CTA can leave (bounded).
-            for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
-                mbar_wait(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, args.err, ERR_TIMEOUT_FULL);
-        }
-    } else if (warp == 5) {
-        if (lane == 0 && n_valid > 0) {
-            constexpr uint32_t idesc = idesc_i8(BN);
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-                if (!mbar_wait(&full[s], ph, args.err, ERR_TIMEOUT_FULL)) break;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t a_base = smem_u32(sA + s * 3 * C::A_PLANE);
-                const uint32_t b_base = smem_u32(sB + s * 3 * C::B_PLANE);
-#pragma unroll
-                for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) {
-#pragma unroll
-                        for (int j = 0; j < 3; ++j) {
-                            const uint64_t ad = smem_desc_sw128(a_base + i * C::A_PLANE + kk * UMMA_K);
-                            const uint64_t bd = smem_desc_sw128(b_base + j * C::B_PLANE + kk * UMMA_K);
-                            // The first product of each diagonal in the first K step overwrites its accumulator.
-                            const uint32_t acc = (kb > 0 || kk > 0 || !(i == 0 || j == 2)) ? 1u : 0u;
-                            umma_i8(tmem + (uint32_t)((i + j) * BN), ad, bd, idesc, acc);
-                        }
+                    for (int p = 0; p < 3; ++p) {
+                        tma_load_2d(sA + (s * 3 + p) * C::A_PLANE, &tmA, kx, (ti.group * 3 + p) * args.M_pad + m0,
+                                    &full[s]);
+                        tma_load_2d(sB + (s * 3 + p) * C::B_PLANE, &tmB, kx, p * args.R_pad + ti.row0, &full[s]);
                     }
                 }
-                umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
             }
-            umma_commit(accum);  // fires when every MMA issued above has completed
+            // Let the copies still in flight land before the block can leave (bounded).
+            for (int j = max(0, q - STAGES); j < q; ++j)
+                mbar_wait(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, args.err, ERR_TIMEOUT_FULL);
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            // The three activation planes sit back to back in shared memory, so one MMA of N = 3·BN multiplies a
+            // weight plane i by all three: its D starts at column i·BN and product (i, j) lands on diagonal i+j.
+            constexpr uint32_t id1 = idesc_i8(BN), id2 = idesc_i8(2 * BN), id3 = idesc_i8(3 * BN);
+            int q = 0, tc = 0;
+            bool alive = true;
+            int tile, m0;
+            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0); L += gridDim.x) {
+                if (tile >= n_tiles) continue;
+                const TileInfo ti = tile_info(args, tile, BN);
+                if (ti.n_valid <= 0) continue;
+                const int b = tc % ACC;
+                const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS);
+                if (!mbar_wait(&acc_empty[b], ((uint32_t)(tc / ACC) & 1u) ^ 1u, args.err, ERR_TIMEOUT_ACCUM)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                    const int s = q % STAGES;
+                    const uint32_t ph = (uint32_t)(q / STAGES) & 1u;
+                    if (!mbar_wait(&full[s], ph, args.err, ERR_TIMEOUT_FULL)) {
+                        alive = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint32_t a_base = smem_u32(sA + s * 3 * C::A_PLANE);
+                    const uint32_t b_base = smem_u32(sB + s * 3 * C::B_PLANE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        const uint64_t a0 = smem_desc_sw128(a_base + 0 * C::A_PLANE + kk * UMMA_K);
+                        const uint64_t a1 = smem_desc_sw128(a_base + 1 * C::A_PLANE + kk * UMMA_K);
+                        const uint64_t a2 = smem_desc_sw128(a_base + 2 * C::A_PLANE + kk * UMMA_K);
+                        const uint64_t b0 = smem_desc_sw128(b_base + 0 * C::B_PLANE + kk * UMMA_K);
+                        const uint64_t b2 = smem_desc_sw128(b_base + 2 * C::B_PLANE + kk * UMMA_K);
+                        if (kb == 0 && kk == 0) {
+                            // first K step: every diagonal's first product overwrites, the others accumulate
+                            umma_i8(acc + 0 * BN, a0, b0, id3, 0u);  // (0,0) (0,1) (0,2) -> diagonals 0, 1, 2
+                            umma_i8(acc + 1 * BN, a1, b0, id2, 1u);  // (1,0) (1,1)       -> diagonals 1, 2
+                            umma_i8(acc + 3 * BN, a1, b2, id1, 0u);  // (1,2)             -> diagonal 3
+                            umma_i8(acc + 2 * BN, a2, b0, id2, 1u);  // (2,0) (2,1)       -> diagonals 2, 3
+                            umma_i8(acc + 4 * BN, a2, b2, id1, 0u);  // (2,2)             -> diagonal 4
+                        } else {
+                            umma_i8(acc + 0 * BN, a0, b0, id3, 1u);
+                            umma_i8(acc + 1 * BN, a1, b0, id3, 1u);
+                            umma_i8(acc + 2 * BN, a2, b0, id3, 1u);
+                        }
+                    }
+                    umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                }
+                umma_commit(&acc_full[b]);  // fires when every MMA issued so far has completed
+                ++tc;
+            }
         }
     } else {
         // Epilogue: warp w reads TMEM lanes 32w..32w+31 (its lane quadrant); lane l holds weight row m0+32w+l.
-        bool ok = true;
-        if (n_valid > 0) ok = mbar_wait(accum, 0, args.err, ERR_TIMEOUT_ACCUM);
-        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: keep the branch warp-uniform
-        asm volatile("tcgen05.fence::after_thread_sync;");
-        const int m = m0 + warp * 32 + lane;
-        const bool m_ok = m < args.M_valid;
-        if (ok && n_valid > 0) {
-            const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+        const bool do_max = args.rowmax != nullptr;
+        int tc = 0;
+        int tile, m0;
+        for (int L = blockIdx.x; it.get(args, L, tile, m0); L += gridDim.x) {
+            if (tile >= n_tiles) continue;
+            const TileInfo ti = tile_info(args, tile, BN);
+            if (ti.n_valid <= 0) continue;
+            const int b = tc % ACC;
+            bool ok = mbar_wait(&acc_full[b], (uint32_t)(tc / ACC) & 1u, args.err, ERR_TIMEOUT_ACCUM);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: keep the branch warp-uniform
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const int m = m0 + warp * 32 + lane;
+            const bool m_ok = m < args.M_valid;
+            const int my_slot = m >= args.rowmax_split ? 1 : 0;
+            const bool one_slot = __all_sync(0xffffffffu, my_slot == __shfl_sync(0xffffffffu, my_slot, 0));
+            if (do_max) {
+                for (int i = threadIdx.x; i < 2 * 4 * BN; i += 128) sred[i] = 0;
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
+            const uint32_t lane_addr = tmem + (uint32_t)(b * C::ACC_COLS) + ((uint32_t)(warp * 32) << 16);
+            const int n_chunks = (ti.n_valid + 15) / 16;
 #pragma unroll 1
-            for (int c = 0; c < BN / 16; ++c) {
-                if (c * 16 >= n_valid) break;
+            for (int c = 0; c < n_chunks; ++c) {
                 int32_t s0[16], s1[16], s2[16], s3[16], s4[16];
-                tmem_ld16(lane_addr + 0 * BN + c * 16, s0);
-                tmem_ld16(lane_addr + 1 * BN + c * 16, s1);
-                tmem_ld16(lane_addr + 2 * BN + c * 16, s2);
-                tmem_ld16(lane_addr + 3 * BN + c * 16, s3);
-                tmem_ld16(lane_addr + 4 * BN + c * 16, s4);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (m_ok) {
+                if (ok) {
+                    tmem_ld16(lane_addr + 0 * BN + c * 16, s0);
+                    tmem_ld16(lane_addr + 1 * BN + c * 16, s1);
+                    tmem_ld16(lane_addr + 2 * BN + c * 16, s2);
+                    tmem_ld16(lane_addr + 3 * BN + c * 16, s3);
+                    tmem_ld16(lane_addr + 4 * BN + c * 16, s4);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                }
+                if (c == n_chunks - 1) {
+                    // this thread has read all of buffer b: the MMAs of a later tile may overwrite it
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    mbar_arrive(&acc_empty[b]);
+                }
+                if (!ok) continue;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int n = c * 16 + j;
-                        if (n < n_valid) {
-                            const int64_t v = kt::recombine(s0[j], s1[j], s2[j], s3[j], s4[j]);
-                            int64_t* p = args.out + (long long)(row0 + n) * args.ld_out + m;
-                            *p = args.accumulate ? *p + v : v;
+                for (int j = 0; j < 16; ++j) {
+                    const int n = c * 16 + j;
+                    int64_t v = kt::recombine(s0[j], s1[j], s2[j], s3[j], s4[j]);
+                    const bool live = m_ok && n < ti.n_valid;
+                    if (live) {
+                        int64_t* p = args.out + (long long)(ti.row0 + n) * args.ld_out + m;
+                        if (args.accumulate) v += *p;
+                        *p = v;
+                    }
+                    if (do_max) {
+                        unsigned long long av = live ? (unsigned long long)(v >= 0 ? v : -v) : 0ull;
+                        if (one_slot) {
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const unsigned long long w = __shfl_xor_sync(0xffffffffu, av, o);
+                                av = w > av ? w : av;
+                            }
+                            if (lane == 0) sred[(my_slot * 4 + warp) * BN + n] = av;
+                        } else {
+#pragma unroll
+                            for (int sl = 0; sl < 2; ++sl) {
+                                unsigned long long bv = my_slot == sl ? av : 0ull;
+#pragma unroll
+                                for (int o = 16; o > 0; o >>= 1) {
+                                    const unsigned long long w = __shfl_xor_sync(0xffffffffu, bv, o);
+                                    bv = w > bv ? w : bv;
+                                }
+                                if (lane == 0) sred[(sl * 4 + warp) * BN + n] = bv;
+                            }
                         }
                     }
                 }
             }
+            if (do_max) {
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                for (int i = threadIdx.x; i < 2 * BN; i += 128) {
+                    const int sl = i / BN, n = i % BN;
+                    unsigned long long v = 0;
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) v = max(v, sred[(sl * 4 + w) * BN + n]);
+                    if (v && n < ti.n_valid)
+                        atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, v);
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // sred is reused by the next tile
+            }
+            ++tc;
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");

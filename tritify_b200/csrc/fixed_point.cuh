@@ -103,6 +103,35 @@ KT_HD uint64_t udiv_small_q(u128 n, uint64_t d) {
     return (uint64_t)(n / (u128)d);
 }
 
+// A divisor with its reciprocal, for many divisions by one per-row value: the quotient estimate is one multiply,
+// then the same exact 128-bit remainder correction (correct for quotients below 2^52).
+struct FastDiv {
+    uint64_t d;
+    double inv;    // 1 / d
+    double inv28;  // 2^28 / d
+};
+
+KT_HD FastDiv make_div(uint64_t d) { return FastDiv{d, 1.0 / (double)d, 268435456.0 / (double)d}; }
+
+KT_HD uint64_t fdiv(u128 n, FastDiv f) {
+    const double qe = u128_to_double(n) * f.inv;
+    int64_t q = (int64_t)qe;
+    i128 r = (i128)n - (i128)((u128)(uint64_t)q * f.d);
+    int guard = 0;
+    while (r < 0 && guard < 4) {
+        --q;
+        r += (i128)f.d;
+        ++guard;
+    }
+    while (r >= (i128)f.d && guard < 8) {
+        ++q;
+        r -= (i128)f.d;
+        ++guard;
+    }
+    if (r >= 0 && r < (i128)f.d) return (uint64_t)q;
+    return (uint64_t)(n / (u128)f.d);
+}
+
 // crates/00-kernels/kt-int/src/lib.rs:191-212 — Scale::from_ratio.
 KT_HD Scale from_ratio(u128 num, u128 den) {
     if (num == 0) return scale_zero();
@@ -168,6 +197,19 @@ KT_HD int64_t scale_apply(Scale s, int64_t value) {
     return (int64_t)r;
 }
 
+// Scale::apply for |value| < 2^30 (every activation code here is within ±2^28): the product fits 64 bits, so the
+// rounding shift runs in 64-bit arithmetic; other inputs take the general path.
+KT_HD int64_t scale_apply_small(Scale s, int64_t value) {
+    if (s.mant == 0) return 0;
+    if (value >= (int64_t(1) << 30) || value <= -(int64_t(1) << 30) || s.shift <= 0 || s.mant >= (int64_t(1) << 33))
+        return scale_apply(s, value);
+    if (s.shift >= 64) return 0;  // |prod| < 2^63 <= 2^(shift-1): rounds to zero
+    const int64_t prod = value * s.mant;
+    const uint64_t ap = prod >= 0 ? (uint64_t)prod : (uint64_t)(-prod);
+    const uint64_t r = (ap + (uint64_t(1) << (s.shift - 1))) >> s.shift;
+    return prod >= 0 ? (int64_t)r : -(int64_t)r;
+}
+
 // crates/00-kernels/kt-int/src/lib.rs:275-280 — Scale::recip (caller guarantees mant != 0).
 KT_HD Scale scale_recip(Scale s) {
     Scale r = from_ratio((u128)1 << 40, (u128)(uint64_t)s.mant);
@@ -177,6 +219,46 @@ KT_HD Scale scale_recip(Scale s) {
 // from_ratio(v, 2^28) for 0 < v < 2^63: the output-scale factor of every dynamic requant.
 KT_HD Scale ratio_act(int64_t v) { return from_ratio((u128)(uint64_t)v, (u128)ACT_LEVELS); }
 
+// requant_dyn(v, ACT_LEVELS, den) with den's reciprocals precomputed (den = the row's max |v|, so |v| <= den).
+// For den < 2^52 the quotient estimate is |v|·(2^28/den) in double (|v| converts exactly) and the remainder
+// |v|·2^28 + den/2 - q·den is formed in wrapping 64-bit arithmetic: its true value lies in (-2^53, 2^54), so the
+// wrapped value is exact, and at most two unit corrections give the exact floor. Larger dens take the 128-bit path.
+KT_HD int32_t requant_act_fast(int64_t v, FastDiv den) {
+    const uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-(v + 1)) + 1;
+    uint64_t q;
+    if (den.d < (uint64_t(1) << 52) && av <= den.d) {
+        int64_t qi = (int64_t)((double)av * den.inv28);
+        int64_t r = (int64_t)((av << ACT_SHIFT) + (den.d >> 1) - (uint64_t)qi * den.d);
+        const int64_t d = (int64_t)den.d;
+        if (r < 0) {
+            --qi;
+            r += d;
+            if (r < 0) {
+                --qi;
+                r += d;
+            }
+        }
+        while (r >= d) {
+            ++qi;
+            r -= d;
+        }
+        q = (uint64_t)qi;
+    } else {
+        const u128 n = ((u128)av << ACT_SHIFT) + (u128)(den.d / 2);
+        q = fdiv(n, den);
+    }
+    return (int32_t)(v >= 0 ? (int64_t)q : -(int64_t)q);
+}
+
+// quant_to(d, 2^28): the divisor is a power of two, so round-half-away is a shift. Used for the down linear, whose
+// input (a dynamic requant to ACT_LEVELS) always has max |.| = 2^28.
+KT_HD int32_t quant_to_act(int32_t d) {
+    const int64_t num = (int64_t)d * (int64_t)(int32_t)WLEVELS;
+    const uint64_t an = num >= 0 ? (uint64_t)num : (uint64_t)(-num);
+    const uint64_t q = (an + (uint64_t(1) << (ACT_SHIFT - 1))) >> ACT_SHIFT;
+    return (int32_t)(num >= 0 ? (int64_t)q : -(int64_t)q);
+}
+
 // crates/01-engine/kt-core/src/layers.rs:34-39 — requant_dyn(v, ACT_LEVELS, den), den > 0.
 KT_HD int32_t requant_act(int64_t v, int64_t den) {
     uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-(v + 1)) + 1;
@@ -184,6 +266,90 @@ KT_HD int32_t requant_act(int64_t v, int64_t den) {
     uint64_t q = udiv_small_q(n, (uint64_t)den);
     int64_t r = v >= 0 ? (int64_t)q : -(int64_t)q;
     return (int32_t)r;
+}
+
+// ───── per-row plans for the hot loops ─────
+// The divisor of a row's requant (den = the row's max |v|, so |v| <= den) with its reciprocal, built once per row.
+struct ReqDiv {
+    int64_t d;
+    int64_t half;  // floor(d / 2)
+    double inv28;  // 2^28 / d
+    bool tight;    // d < 2^52: the 64-bit path below is exact
+};
+
+KT_HD ReqDiv make_req(int64_t d) {
+    ReqDiv r;
+    r.d = d > 0 ? d : 1;
+    r.half = r.d / 2;
+    r.inv28 = 268435456.0 / (double)r.d;
+    r.tight = r.d < (int64_t(1) << 52);
+    return r;
+}
+
+// requant_dyn(v, 2^28, den) for |v| <= den (layers.rs:34-39). x = |v|·2^28/den <= 2^28 is estimated in double to
+// within 2^-24 (|v| < 2^52 converts exactly; two roundings of relative size 2^-53), so trunc(estimate) is within one
+// of floor((|v|·2^28 + half)/den); the remainder |v|·2^28 + half - q·den lies in (-den, 2·den) and is formed exactly
+// in wrapping 64-bit arithmetic, and one signed correction gives the floor.
+KT_HD int32_t requant_row(int64_t v, const ReqDiv& r) {
+    if (!r.tight) return requant_act(v, r.d);
+    const uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-v);
+    int64_t q = (int64_t)((double)(int64_t)av * r.inv28);
+    const int64_t rem = (int64_t)((av << ACT_SHIFT) + (uint64_t)r.half - (uint64_t)q * (uint64_t)r.d);
+    q += (int64_t)(rem >= r.d) - (int64_t)(rem < 0);
+    return (int32_t)(v >= 0 ? q : -q);
+}
+
+// Scale::apply for one row's scale over values |v| < 2^31: with 0 < shift < 64 and mant < 2^32 the product is a
+// 32x32->64 multiply and the rounding shift is exact in 64 bits; other scales take the general path.
+struct ApplyPlan {
+    Scale s;
+    uint64_t half;
+    uint32_t mant;
+    uint32_t shift;
+    bool tight;
+};
+
+KT_HD ApplyPlan make_apply(Scale s) {
+    ApplyPlan p;
+    p.s = s;
+    p.tight = s.mant > 0 && s.mant < (int64_t(1) << 32) && s.shift > 0 && s.shift < 64;
+    p.mant = (uint32_t)s.mant;
+    p.shift = (uint32_t)(p.tight ? s.shift : 1);
+    p.half = uint64_t(1) << (p.shift - 1);
+    return p;
+}
+
+KT_HD int64_t apply_row(const ApplyPlan& p, int64_t v) {
+    if (!p.tight || v >= (int64_t(1) << 31) || v <= -(int64_t(1) << 31)) return scale_apply(p.s, v);
+    const uint32_t av = (uint32_t)(v >= 0 ? v : -v);
+    const uint64_t r = ((uint64_t)av * p.mant + p.half) >> p.shift;
+    return v >= 0 ? (int64_t)r : -(int64_t)r;
+}
+
+// quant_to(d, xmax) for one row (layers.rs:23-31): x = |d|·WLEVELS/xmax <= WLEVELS is estimated in double, the
+// remainder |d|·WLEVELS + xmax/2 - q·xmax (|d|·WLEVELS < 2^50) is exact in 64 bits, and one signed correction gives
+// the floor.
+struct QuantPlan {
+    int64_t xmax;
+    int64_t half;
+    double inv;  // WLEVELS / xmax
+};
+
+KT_HD QuantPlan make_quant(int64_t xmax) {
+    QuantPlan p;
+    p.xmax = xmax > 0 ? xmax : 1;
+    p.half = p.xmax / 2;
+    p.inv = (double)WLEVELS / (double)p.xmax;
+    return p;
+}
+
+KT_HD int32_t quant_row(int32_t d, const QuantPlan& p) {
+    const int64_t ad = d >= 0 ? (int64_t)d : -(int64_t)d;
+    int64_t q = (int64_t)((double)ad * p.inv);
+    const int64_t num = ad * WLEVELS;
+    const int64_t rem = num + p.half - q * p.xmax;
+    q += (int64_t)(rem >= p.xmax) - (int64_t)(rem < 0);
+    return (int32_t)(d >= 0 ? q : -q);
 }
 
 // crates/01-engine/kt-core/src/layers.rs:34-39 — the general requant_dyn (any level), exact i128.

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <list>
 #include <mutex>
@@ -90,6 +91,7 @@ struct Resident {
 
 struct ktmoe_ctx {
     int device = 0;
+    int num_sms = 148;
     cudaStream_t stream = nullptr;
     int* d_err = nullptr;
     std::string last_error = "";
@@ -140,17 +142,17 @@ int make_map(ktmoe_ctx* ctx, CUtensorMap* map, const void* base, int64_t k_pad, 
     return KTMOE_OK;
 }
 
-template <int BN, int ST>
+template <int BN, int ST, int ACC>
 int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
                   const dg::GemmArgs& args) {
-    using Cf = dg::Cfg<BN, ST>;
+    using Cf = dg::Cfg<BN, ST, ACC>;
     static bool attr_set[64] = {};
     if (!attr_set[ctx->device & 63]) {
-        CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST, ACC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 Cf::SMEM_BYTES));
         attr_set[ctx->device & 63] = true;
     }
-    dg::digit_gemm_kernel<BN, ST><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
+    dg::digit_gemm_kernel<BN, ST, ACC><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
     CKL(ctx);
     return KTMOE_OK;
 }
@@ -168,12 +170,18 @@ struct GemmCall {
     const int* group_end = nullptr;
     const int* n_tiles = nullptr;
     int64_t single_rows = 0;
+    unsigned long long* rowmax = nullptr;  // fused |max| per (row, slot); see dg::GemmArgs
+    int rowmax_stride = 0;
+    int64_t rowmax_split = 0;
 };
 
 // Launch the digit GEMM, splitting K into chunks whose int32 diagonal sums cannot overflow.
 int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (g.grid_y <= 0 || g.M_valid <= 0) return KTMOE_OK;
-    if (g.grid_y > 65535) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "too many activation tiles for one launch");
+    const int64_t group_n = std::min<int64_t>(16, g.grid_y);
+    const int64_t m_tiles = g.A.rows_pad / dg::BM;
+    const int64_t n_groups = (g.grid_y + group_n - 1) / group_n;
+    if (m_tiles * group_n * n_groups > INT32_MAX) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "too many tiles for one launch");
     CUtensorMap ma, mb;
     int r = make_map(ctx, &ma, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, dg::BM);
     if (r) return r;
@@ -181,7 +189,9 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (r) return r;
     const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
     const int64_t chunk_kb = dg::K_EXACT_MAX / dg::BK;
-    dim3 grid((unsigned)(g.A.rows_pad / dg::BM), (unsigned)g.grid_y);
+    if (g.rowmax && total_kb > chunk_kb) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "fused row max with a chunked K");
+    // persistent: at most one block per SM walks the tile raster
+    dim3 grid((unsigned)std::min<int64_t>(m_tiles * group_n * n_groups, ctx->num_sms));
     for (int64_t kb0 = 0; kb0 < total_kb; kb0 += chunk_kb) {
         dg::GemmArgs a;
         a.out = g.out;
@@ -195,13 +205,20 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.tile_row0 = g.tile_row0;
         a.group_row_end = g.group_end;
         a.n_tiles = g.n_tiles;
+        a.n_tiles_max = (int)g.grid_y;
+        a.m_tiles = (int)m_tiles;
+        a.group_n = (int)group_n;
         a.single_rows = (int)g.single_rows;
         a.accumulate = kb0 > 0 ? 1 : 0;
         a.err = ctx->d_err;
+        a.rowmax = g.rowmax;
+        a.rowmax_stride = g.rowmax_stride;
+        a.rowmax_split = (int)std::min<int64_t>(g.rowmax_split, INT32_MAX);
         switch (g.BN) {
-            case 16: r = launch_gemm_t<16, 4>(ctx, st, ma, mb, grid, a); break;
-            case 32: r = launch_gemm_t<32, 3>(ctx, st, ma, mb, grid, a); break;
-            case 64: r = launch_gemm_t<64, 3>(ctx, st, ma, mb, grid, a); break;
+            case 16: r = launch_gemm_t<16, 4, 2>(ctx, st, ma, mb, grid, a); break;
+            case 32: r = launch_gemm_t<32, 3, 2>(ctx, st, ma, mb, grid, a); break;
+            case 48: r = launch_gemm_t<48, 3, 2>(ctx, st, ma, mb, grid, a); break;
+            case 64: r = launch_gemm_t<64, 3, 1>(ctx, st, ma, mb, grid, a); break;
             default: return fail(ctx, KTMOE_ERR_ARG, "unsupported BN");
         }
         if (r) return r;
@@ -209,8 +226,16 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     return KTMOE_OK;
 }
 
+// Activation rows per tile: 48 keeps two accumulator buffers in TMEM (the epilogue overlaps the next tile's MMAs)
+// while three stacked planes still give one 144-wide MMA per weight plane. KTMOE_BN overrides it (16/32/48/64).
 int pick_bn(double rows_per_group) {
-    if (rows_per_group >= 48.0) return 64;
+    static int forced = [] {
+        const char* e = getenv("KTMOE_BN");
+        int v = e ? atoi(e) : 0;
+        return (v == 16 || v == 32 || v == 48 || v == 64) ? v : 0;
+    }();
+    if (forced) return forced;
+    if (rows_per_group >= 40.0) return 48;
     if (rows_per_group >= 20.0) return 32;
     return 16;
 }
@@ -219,6 +244,19 @@ __global__ void sqx_kernel(const unsigned long long* gxmax, const Scale* x_scale
     const int64_t xm = (int64_t)*gxmax;
     *out = xm > 0 ? kt::scale_mul(kt::from_ratio((kt::u128)(uint64_t)xm, (kt::u128)kt::WLEVELS), *x_scale)
                   : kt::scale_zero();
+}
+
+// The down GEMM's width: a long K (d_ff >= 4096) amortises a single-buffered accumulator, and a 64-row tile reads
+// the least shared memory per MMA; otherwise the same choice as the gate/up GEMM. KTMOE_BN_DOWN overrides it.
+int pick_bn_long_k(double rows_per_group, int64_t k) {
+    static int forced = [] {
+        const char* e = getenv("KTMOE_BN_DOWN");
+        int v = e ? atoi(e) : 0;
+        return (v == 16 || v == 32 || v == 48 || v == 64) ? v : 0;
+    }();
+    if (forced) return forced;
+    if (k >= 4096 && rows_per_group >= 48.0) return 64;
+    return pick_bn(rows_per_group);
 }
 
 int set_device(ktmoe_ctx* ctx) {
@@ -258,13 +296,14 @@ struct ktmoe_layer {
     DevBuf b_luts;  // 3 x 65536 int64: exp, SiLU, sigmoid
     hp::HTable tabs[3];
     Scale silu_code_scale_recip{0, 0};
+    int64_t swiglu_smem = 0;  // dynamic shared bytes holding one row's h (0: h stays in global memory)
     // scratch for `cap` tokens
     int64_t cap = 0;
     DevBuf x_in, y_out, scal;  // scal: Scales and u64 scalars
     DevBuf tok_planes, tok_xmax, tok_sqx, router_acc, logits, logit_scale, top_e, top_ec, sumc;
-    DevBuf counts, chunk_off, expert_off, group_end, expert_count, tile_group, tile_row0, slot_row, row_assign,
-        row_expert;
-    DevBuf xg_planes, acc_gu, hq_planes, row_cd, acc_d, tok_out, tok_scale, y_routed;
+    DevBuf counts, chunk_off, expert_off, group_end, expert_count, tile_group, tile_row0, tile_group2, tile_row02,
+        slot_row, row_assign, row_expert;
+    DevBuf xg_planes, acc_gu, hq_planes, row_cd, acc_d, tok_out, tok_scale, y_routed, rowmax_gu, rowmax_d;
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
     // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
     bool timing = false;
@@ -285,12 +324,14 @@ enum ScalarSlot {
     SL_NSCALES = 12
 };
 enum U64Slot { U_MERGE_GMAX = 0, U_GXMAX, U_SYG, U_SYU, U_SHMAX, U_SYD, U_ADDGMAX, U_NTILES_PAD, U_N };
+// the two n-tile counts live in the two 32-bit halves of U_NTILES_PAD
 
 Scale* scal_scale(ktmoe_layer* L, int slot) { return L->scal.as<Scale>() + slot; }
 unsigned long long* scal_u64(ktmoe_layer* L, int slot) {
     return (unsigned long long*)(L->scal.as<uint8_t>() + SL_NSCALES * sizeof(Scale)) + slot;
 }
 int* n_tiles_ptr(ktmoe_layer* L) { return (int*)(scal_u64(L, U_NTILES_PAD)); }
+int* n_tiles2_ptr(ktmoe_layer* L) { return (int*)(scal_u64(L, U_NTILES_PAD)) + 1; }
 
 int ensure_scratch(ktmoe_layer* L, int64_t T) {
     ktmoe_ctx* ctx = L->ctx;
@@ -319,6 +360,8 @@ int ensure_scratch(ktmoe_layer* L, int64_t T) {
     CK(L->expert_count.ensure(E * 4));
     CK(L->tile_group.ensure(max_tiles * 4));
     CK(L->tile_row0.ensure(max_tiles * 4));
+    CK(L->tile_group2.ensure(max_tiles * 4));
+    CK(L->tile_row02.ensure(max_tiles * 4));
     CK(L->slot_row.ensure(R * 4));
     CK(L->row_assign.ensure(R * 4));
     CK(L->row_expert.ensure(R * 4));
@@ -327,6 +370,8 @@ int ensure_scratch(ktmoe_layer* L, int64_t T) {
     CK(L->hq_planes.ensure(3 * R_pad * L->f_pad));
     CK(L->row_cd.ensure(R * sizeof(Scale)));
     CK(L->acc_d.ensure(R * d * 8));
+    CK(L->rowmax_gu.ensure(R * 2 * 8));
+    CK(L->rowmax_d.ensure(R * 8));
     CK(L->tok_out.ensure(T * d * 4));
     CK(L->tok_scale.ensure(T * sizeof(Scale)));
     if (fs > 0) {
@@ -434,15 +479,17 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
 
     // dispatch plan: stable counting sort of the T·K assignments by expert
     const int BN = pick_bn((double)R / (double)E);
+    const int BN2 = pick_bn_long_k((double)R / (double)E, f);
     const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
     mk::plan_count_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, E * 4, st>>>(L->top_e.as<int32_t>(), R, (int)E,
                                                                              L->counts.as<int>());
     CKL(ctx);
     const int scan_threads = (int)std::min<int64_t>(1024, round_up(E, 32));
-    mk::plan_scan_kernel<<<1, scan_threads, 2 * E * 4, st>>>(
-        L->counts.as<int>(), (int)nchunks, (int)E, BN, L->chunk_off.as<int>(), L->expert_off.as<int>(),
-        L->group_end.as<int>(), L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L),
-        L->expert_count.as<int>());
+    mk::plan_scan_kernel<<<1, scan_threads, 3 * E * 4, st>>>(
+        L->counts.as<int>(), (int)nchunks, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(),
+        L->group_end.as<int>(), L->expert_count.as<int>(),
+        mk::TileTable{BN, L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L)},
+        mk::TileTable{BN2, L->tile_group2.as<int>(), L->tile_row02.as<int>(), n_tiles2_ptr(L)});
     CKL(ctx);
     mk::plan_assign_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, (E + (mk::PLAN_THREADS / 32) * E) * 4, st>>>(
         L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
@@ -467,6 +514,11 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     g.tile_row0 = L->tile_row0.as<int>();
     g.group_end = L->group_end.as<int>();
     g.n_tiles = n_tiles_ptr(L);
+    g.rowmax = L->rowmax_gu.as<unsigned long long>();
+    g.rowmax_stride = 2;
+    g.rowmax_split = f;
+    CK(cudaMemsetAsync(L->rowmax_gu.p, 0, R * 2 * 8, st));
+    CK(cudaMemsetAsync(L->rowmax_d.p, 0, R * 8, st));
     r = run_gemm(ctx, st, g);
     if (r) return r;
     MARK(L, st);
@@ -491,9 +543,25 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sa.silu_code_scale_recip = L->silu_code_scale_recip;
     sa.planes = L->hq_planes.as<int8_t>();
     sa.row_cd = L->row_cd.as<Scale>();
+    sa.ymax = L->rowmax_gu.as<unsigned long long>();
+    sa.ymax_stride = 2;
     sa.phase = 0;
-    mk::swiglu_kernel<<<(unsigned)R, 256, 0, st>>>(sa);
-    CKL(ctx);
+    {
+        const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
+        const size_t sm = h_smem ? (size_t)L->swiglu_smem : 0;
+        static const int unroll = [] {
+            const char* e = getenv("KTMOE_SWIGLU_U");
+            const int v = e ? atoi(e) : 2;
+            return (v == 1 || v == 2 || v == 4) ? v : 2;
+        }();
+        if (unroll == 1)
+            mk::swiglu_rows_kernel<1><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+        else if (unroll == 4)
+            mk::swiglu_rows_kernel<4><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+        else
+            mk::swiglu_rows_kernel<2><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+        CKL(ctx);
+    }
     MARK(L, st);
 
     g.A = L->w_dn;
@@ -501,12 +569,21 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     g.B = Planes{L->hq_planes.as<int8_t>(), 1, R_pad, f, L->f_pad};
     g.out = L->acc_d.as<int64_t>();
     g.ld_out = d;
+    g.BN = BN2;
+    g.grid_y = (R + BN2 - 1) / BN2 + E;
+    g.tile_group = L->tile_group2.as<int>();
+    g.tile_row0 = L->tile_row02.as<int>();
+    g.n_tiles = n_tiles2_ptr(L);
+    g.rowmax = L->rowmax_d.as<unsigned long long>();
+    g.rowmax_stride = 1;
+    g.rowmax_split = INT32_MAX;
     r = run_gemm(ctx, st, g);
     if (r) return r;
     MARK(L, st);
 
     mk::CombineArgs ca;
     ca.acc_d = L->acc_d.as<int64_t>();
+    ca.ymax_d = L->rowmax_d.as<unsigned long long>();
     ca.row_cd = L->row_cd.as<Scale>();
     ca.slot_row = L->slot_row.as<int>();
     ca.top_ec = L->top_ec.as<int64_t>();
@@ -560,15 +637,11 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     s.BN = pick_bn((double)T);
     s.grid_y = (T + s.BN - 1) / s.BN;
     s.single_rows = T;
+    s.rowmax = scal_u64(L, U_SYG);  // [U_SYG] gate, [U_SYU] up: maxima over the whole tensor
+    s.rowmax_stride = 0;
+    s.rowmax_split = fs;
     r = run_gemm(ctx, st, s);
     if (r) return r;
-    const unsigned rb2 = (unsigned)std::min<int64_t>(1184, (T * fs + 255) / 256);
-    mk::absmax_i64_cols_kernel<<<rb2, 256, 0, st>>>(L->acc_sgu.as<int64_t>(), (int)T, 2 * fs, 0, (int)fs,
-                                                    scal_u64(L, U_SYG));
-    CKL(ctx);
-    mk::absmax_i64_cols_kernel<<<rb2, 256, 0, st>>>(L->acc_sgu.as<int64_t>(), (int)T, 2 * fs, (int)fs, (int)fs,
-                                                    scal_u64(L, U_SYU));
-    CKL(ctx);
     mk::SwigluArgs sh;
     std::memset(&sh, 0, sizeof(sh));
     sh.acc = L->acc_sgu.as<int64_t>();
@@ -586,26 +659,25 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sh.silu_code_scale_recip = L->silu_code_scale_recip;
     sh.planes = L->hs_planes.as<int8_t>();
     sh.row_cd = scal_scale(L, SL_SCD);
-    sh.g_ymax_g = scal_u64(L, U_SYG);
-    sh.g_ymax_u = scal_u64(L, U_SYU);
+    sh.ymax = scal_u64(L, U_SYG);
+    sh.ymax_stride = 0;
     sh.g_hmax = scal_u64(L, U_SHMAX);
-    sh.g_hmax_in = scal_u64(L, U_SHMAX);
     sh.phase = 1;
-    mk::swiglu_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+    mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
     CKL(ctx);
     sh.phase = 2;
-    mk::swiglu_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+    mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
     CKL(ctx);
     s.A = L->w_sdn;
     s.M_valid = d;
     s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
     s.out = L->acc_sd.as<int64_t>();
     s.ld_out = d;
+    s.rowmax = scal_u64(L, U_SYD);
+    s.rowmax_stride = 0;
+    s.rowmax_split = INT32_MAX;
     r = run_gemm(ctx, st, s);
     if (r) return r;
-    mk::absmax_i64_cols_kernel<<<red_blocks, 256, 0, st>>>(L->acc_sd.as<int64_t>(), (int)T, d, 0, (int)d,
-                                                           scal_u64(L, U_SYD));
-    CKL(ctx);
     mk::AddArgs aa;
     aa.a = routed;
     aa.a_scale = routed_scale;
@@ -704,6 +776,7 @@ int ktmoe_open(int device, ktmoe_ctx** out) {
         delete ctx;
         return KTMOE_ERR_CUDA;
     }
+    cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     size_t free_b = 0, total_b = 0;
     cudaMemGetInfo(&free_b, &total_b);
     ctx->budget = free_b / 5 * 4;
@@ -923,6 +996,19 @@ int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_laye
             return bail(fail(ctx, KTMOE_ERR_CUDA, "tables"));
     if (L->b_rbias.ensure(L->E * 8) != cudaSuccess || L->b_sigbias.ensure(L->E * 8) != cudaSuccess)
         return bail(fail(ctx, KTMOE_ERR_CUDA, "bias"));
+    // h of one row stays in shared memory only while that still leaves room for several resident blocks per SM;
+    // a wide expert (Mixtral's 14336) keeps h in place of its gate accumulators, which the block just read.
+    if (L->f * 8 <= 24 * 1024) {
+        L->swiglu_smem = L->f * 8;
+        if (L->swiglu_smem > 48 * 1024 &&
+            (cudaFuncSetAttribute(mk::swiglu_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)L->swiglu_smem) != cudaSuccess ||
+             cudaFuncSetAttribute(mk::swiglu_rows_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)L->swiglu_smem) != cudaSuccess ||
+             cudaFuncSetAttribute(mk::swiglu_rows_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)L->swiglu_smem) != cudaSuccess))
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "SwiGLU shared memory"));
+    }
     if ((size_t)L->d * 8 > 48 * 1024) {
         if (cudaFuncSetAttribute(mk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
             cudaSuccess)
@@ -941,9 +1027,9 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
     DevBuf* bufs[] = {&L->b_router, &L->b_gu, &L->b_dn, &L->b_sgu, &L->b_sdn, &L->b_rbias, &L->b_sigbias, &L->b_wsc,
                       &L->b_luts, &L->x_in, &L->y_out, &L->scal, &L->tok_planes, &L->tok_xmax, &L->tok_sqx,
                       &L->router_acc, &L->logits, &L->logit_scale, &L->top_e, &L->top_ec, &L->sumc, &L->counts,
-                      &L->chunk_off, &L->expert_off, &L->group_end, &L->expert_count, &L->tile_group, &L->tile_row0,
+                      &L->chunk_off, &L->expert_off, &L->group_end, &L->expert_count, &L->tile_group, &L->tile_row0, &L->tile_group2, &L->tile_row02,
                       &L->slot_row, &L->row_assign, &L->row_expert, &L->xg_planes, &L->acc_gu, &L->hq_planes,
-                      &L->row_cd, &L->acc_d, &L->tok_out, &L->tok_scale, &L->y_routed, &L->xs_planes, &L->acc_sgu,
+                      &L->row_cd, &L->acc_d, &L->rowmax_gu, &L->rowmax_d, &L->tok_out, &L->tok_scale, &L->y_routed, &L->xs_planes, &L->acc_sgu,
                       &L->hs_planes, &L->acc_sd};
     for (DevBuf* b : bufs) b->release();
     delete L;

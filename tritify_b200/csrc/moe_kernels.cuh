@@ -86,12 +86,13 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K
     int8_t* p0 = planes + (long long)r * K_pad;
     int8_t* p1 = p0 + R_pad * K_pad;
     int8_t* p2 = p1 + R_pad * K_pad;
+    const kt::QuantPlan qp = kt::make_quant(xmax);
     for (int k4 = threadIdx.x * 4; k4 < K_pad; k4 += blockDim.x * 4) {
         int32_t q[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int k = k4 + j;
-            q[j] = (k < K && xmax > 0) ? kt::quant_to(xr[k], xmax) : 0;
+            q[j] = (k < K && xmax > 0) ? kt::quant_row(xr[k], qp) : 0;
         }
         store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
     }
@@ -306,13 +307,22 @@ __global__ void plan_count_kernel(const int32_t* __restrict__ top_e, long long n
     for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(long long)blockIdx.x * E + e] = hist[e];
 }
 
-// One block: per-expert offsets, per-chunk offsets within each expert, and the n-tile table of the grouped GEMMs.
-__global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, int E, int BN, int* __restrict__ chunk_off,
-                                 int* __restrict__ expert_off, int* __restrict__ group_end, int* __restrict__ tile_group,
-                                 int* __restrict__ tile_row0, int* __restrict__ n_tiles, int* __restrict__ expert_count) {
+// One block: per-expert offsets, per-chunk offsets within each expert, and the n-tile tables of the grouped GEMMs
+// for two tile widths (the gate/up GEMM and the down GEMM may tile the rows differently).
+struct TileTable {
+    int BN;
+    int* tile_group;
+    int* tile_row0;
+    int* n_tiles;
+};
+
+__global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, int E, int* __restrict__ chunk_off,
+                                 int* __restrict__ expert_off, int* __restrict__ group_end,
+                                 int* __restrict__ expert_count, TileTable ta, TileTable tb) {
     extern __shared__ int sh[];
-    int* tot = sh;          // [E]
-    int* toff = sh + E;     // [E] tile offsets
+    int* tot = sh;             // [E]
+    int* toff_a = sh + E;      // [E] tile offsets, table a
+    int* toff_b = sh + 2 * E;  // [E] tile offsets, table b
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         int run = 0;
         for (int c = 0; c < n_chunks; ++c) {
@@ -323,23 +333,30 @@ __global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, i
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int off = 0, tiles = 0;
+        int off = 0, tiles_a = 0, tiles_b = 0;
         for (int e = 0; e < E; ++e) {
             expert_off[e] = off;
             expert_count[e] = tot[e];
             off += tot[e];
             group_end[e] = off;
-            toff[e] = tiles;
-            tiles += (tot[e] + BN - 1) / BN;
+            toff_a[e] = tiles_a;
+            toff_b[e] = tiles_b;
+            tiles_a += (tot[e] + ta.BN - 1) / ta.BN;
+            tiles_b += (tot[e] + tb.BN - 1) / tb.BN;
         }
-        *n_tiles = tiles;
+        *ta.n_tiles = tiles_a;
+        *tb.n_tiles = tiles_b;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int nt = (tot[e] + BN - 1) / BN;
-        for (int i = 0; i < nt; ++i) {
-            tile_group[toff[e] + i] = e;
-            tile_row0[toff[e] + i] = expert_off[e] + i * BN;
+        const int na = (tot[e] + ta.BN - 1) / ta.BN, nb = (tot[e] + tb.BN - 1) / tb.BN;
+        for (int i = 0; i < na; ++i) {
+            ta.tile_group[toff_a[e] + i] = e;
+            ta.tile_row0[toff_a[e] + i] = expert_off[e] + i * ta.BN;
+        }
+        for (int i = 0; i < nb; ++i) {
+            tb.tile_group[toff_b[e] + i] = e;
+            tb.tile_row0[toff_b[e] + i] = expert_off[e] + i * tb.BN;
         }
     }
 }
@@ -407,7 +424,7 @@ __global__ void permute_planes_kernel(const int8_t* __restrict__ src, long long 
 
 // ───────────── SwiGLU + requant + down-input quantisation for routed rows (layers.rs:609-640, :279-298) ─────────────
 struct SwigluArgs {
-    int64_t* acc;  // [rows][2f]: gate in [0, f), up in [f, 2f); the gate half is overwritten by h
+    int64_t* acc;  // [rows][2f]: gate in [0, f), up in [f, 2f); in the tensor-global mode the gate half holds h
     int rows, f, f_pad;
     long long R_pad;  // rows of one plane of `planes`
     const int* row_assign;  // routed: row -> token·top_k + slot (nullptr: row r is token r)
@@ -421,19 +438,89 @@ struct SwigluArgs {
     Lut silu;
     Scale silu_code_scale, silu_code_scale_recip;
     int8_t* planes;  // down-GEMM input digit planes [3][R_pad][f_pad]
-    Scale* row_cd;   // per row: s_qh·w_down (the down linear's c)
-    // tensor-global mode (shared expert): the maxima over the whole tensor, precomputed
-    const unsigned long long* g_ymax_g;
-    const unsigned long long* g_ymax_u;
-    unsigned long long* g_hmax;  // phase 1 output (atomicMax)
-    const unsigned long long* g_hmax_in;  // phase 2 input
-    int phase;  // 0: per-row (routed, all in one kernel); 1: global h pass; 2: global quantise pass
+    Scale* row_cd;   // per row: s_qh·w_down (the down linear's c); one word in the tensor-global mode
+    // |max| of the gate and up accumulators: per row ([rows][2], from the GEMM epilogue) or global ([2])
+    const unsigned long long* ymax;
+    int ymax_stride;  // 2 per row, 0 global
+    unsigned long long* g_hmax;  // tensor-global mode: phase 1 reduces max |h| here, phase 2 reads it
+    int phase;  // 0: per-row (routed, one kernel, h in shared memory); 1: global h pass; 2: global quantise pass
 };
 
-__global__ void swiglu_kernel(const SwigluArgs a) {
+// The SwiGLU scales of one row (or of the whole tensor): g and u output scales, SiLU index scale, identity factor,
+// as per-row plans for the element loop.
+struct SwigluScales {
+    Scale gs, us;
+    int64_t mg, mu;  // requant divisors (0: that output is all zero)
+    kt::ReqDiv rg, ru;
+    kt::ApplyPlan is, idf;
+};
+
+__device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t, int e, int64_t gmax_g, int64_t gmax_u) {
+    SwigluScales q;
+    const Scale sqx = a.g_sqx ? *a.g_sqx : a.row_sqx[t];
+    const Scale cg = kt::scale_mul(sqx, a.wscale_g[e]);
+    const Scale cu = kt::scale_mul(sqx, a.wscale_u[e]);
+    // QuantLinear output scale: zero when c or ymax is zero (layers.rs:300-302, :321-326)
+    q.gs = (cg.mant == 0 || gmax_g == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_g), cg);
+    q.us = (cu.mant == 0 || gmax_u == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_u), cu);
+    q.idf = kt::make_apply(kt::scale_mul(q.gs, a.silu_code_scale_recip));  // id_factor (layers.rs:615)
+    q.is = kt::make_apply(kt::scale_mul(q.gs, a.silu.inv_step));          // CodeLut::index (kt-int lib.rs:383-385)
+    q.mg = cg.mant == 0 ? 0 : gmax_g;
+    q.mu = cu.mant == 0 ? 0 : gmax_u;
+    q.rg = kt::make_req(q.mg);
+    q.ru = kt::make_req(q.mu);
+    return q;
+}
+
+// h = silu_code(g) · u for one element (layers.rs:618-629).
+__device__ __forceinline__ int64_t swiglu_h(const SwigluArgs& a, const SwigluScales& q, int64_t accg, int64_t accu) {
+    const int32_t g = q.mg ? kt::requant_row(accg, q.rg) : 0;
+    const int32_t u = q.mu ? kt::requant_row(accu, q.ru) : 0;
+    const int64_t idx = kt::apply_row(q.is, g) - a.silu.lo_index;
+    int64_t code;
+    if (idx < 0)
+        code = 0;
+    else if (idx >= LUT_N)
+        code = kt::apply_row(q.idf, g);  // identity right tail, in code units
+    else
+        code = __ldg(a.silu.codes + idx);
+    const int32_t c32 = (int32_t)code;
+    return c32 == code ? (int64_t)c32 * (int64_t)u : code * (int64_t)u;
+}
+
+// The down linear's c for a row whose h has max |h| = hmax (layers.rs:630-638 then :297-299 with xmax = 2^28).
+__device__ __forceinline__ Scale down_c(const SwigluArgs& a, Scale us, int64_t hmax, int e) {
+    if (hmax <= 0) return kt::scale_zero();
+    const Scale h_scale = kt::scale_mul(a.silu_code_scale, us);
+    const Scale hint_scale = kt::scale_mul(kt::ratio_act(hmax), h_scale);
+    const Scale s_qh = kt::scale_mul(kt::from_ratio((kt::u128)kt::ACT_LEVELS, (kt::u128)kt::WLEVELS), hint_scale);
+    return kt::scale_mul(s_qh, a.wscale_d[e]);
+}
+
+// hint = requant_dyn(h, L, hmax) has max |.| = L exactly, so the down linear's quant_to divides by 2^28.
+__device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, const int64_t* h, int64_t hmax) {
+    int8_t* p0 = a.planes + (long long)r * a.f_pad;
+    int8_t* p1 = p0 + a.R_pad * a.f_pad;
+    int8_t* p2 = p1 + a.R_pad * a.f_pad;
+    const kt::ReqDiv rh = kt::make_req(hmax);
+    for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
+        int32_t q[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int k = k4 + j;
+            q[j] = (k < a.f && hmax > 0) ? kt::quant_to_act(kt::requant_row(h[k], rh)) : 0;
+        }
+        store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+    }
+}
+
+// Phase 0: one block per routed row; h stays in shared memory (dynamic, f int64) when `h_smem`. U independent
+// elements per thread per step.
+template <int U>
+__global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem) {
+    extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
-    __shared__ Scale sc[4];  // g scale, u scale, id_factor, index scale
-    __shared__ int64_t smax[2];
+    __shared__ SwigluScales qs;
     const int r = blockIdx.x;
     if (r >= a.rows) return;
     const int f = a.f;
@@ -441,104 +528,70 @@ __global__ void swiglu_kernel(const SwigluArgs a) {
     const int64_t* accu = accg + f;
     const int e = a.row_expert ? a.row_expert[r] : 0;
     const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
-    int8_t* p0 = a.planes + (long long)r * a.f_pad;
-    int8_t* p1 = p0 + a.R_pad * a.f_pad;
-    int8_t* p2 = p1 + a.R_pad * a.f_pad;
+    if (threadIdx.x == 0)
+        qs = swiglu_scales(a, t, e, (int64_t)a.ymax[(long long)r * a.ymax_stride], (int64_t)a.ymax[(long long)r * a.ymax_stride + 1]);
+    __syncthreads();
+    const SwigluScales q = qs;
+    int64_t* h = h_smem ? hs : accg;
+    uint64_t hm = 0;
+    // the loads of a step are issued before its arithmetic
+    int k = threadIdx.x;
+    for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
+        int64_t gv[U], uv[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            gv[j] = accg[k + j * blockDim.x];
+            uv[j] = accu[k + j * blockDim.x];
+        }
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+            const int64_t v = swiglu_h(a, q, gv[j], uv[j]);
+            h[k + j * blockDim.x] = v;
+            hm = max(hm, uabs64(v));
+        }
+    }
+    for (; k < f; k += blockDim.x) {
+        const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
+        h[k] = v;
+        hm = max(hm, uabs64(v));
+    }
+    const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
+    write_down_planes(a, r, h, hmax);
+    if (threadIdx.x == 0) a.row_cd[r] = down_c(a, q.us, hmax, e);
+}
 
-    int64_t hmax;
-    if (a.phase != 2) {
-        int64_t gmax_g, gmax_u;
-        if (a.phase == 0) {
-            uint64_t mg = 0, mu = 0;
-            for (int k = threadIdx.x; k < f; k += blockDim.x) {
-                mg = max(mg, uabs64(accg[k]));
-                mu = max(mu, uabs64(accu[k]));
-            }
-            mg = block_max_u64(mg, red);
-            __syncthreads();
-            mu = block_max_u64(mu, red);
-            gmax_g = (int64_t)mg;
-            gmax_u = (int64_t)mu;
-        } else {
-            gmax_g = (int64_t)*a.g_ymax_g;
-            gmax_u = (int64_t)*a.g_ymax_u;
-        }
-        if (threadIdx.x == 0) {
-            const Scale sqx = a.g_sqx ? *a.g_sqx : a.row_sqx[t];
-            const Scale cg = kt::scale_mul(sqx, a.wscale_g[e]);
-            const Scale cu = kt::scale_mul(sqx, a.wscale_u[e]);
-            // QuantLinear output scale: zero when c or ymax is zero (layers.rs:300-302, :321-326)
-            const Scale gs = (cg.mant == 0 || gmax_g == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_g), cg);
-            const Scale us = (cu.mant == 0 || gmax_u == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_u), cu);
-            sc[0] = gs;
-            sc[1] = us;
-            sc[2] = kt::scale_mul(gs, a.silu_code_scale_recip);  // id_factor (layers.rs:615)
-            sc[3] = kt::scale_mul(gs, a.silu.inv_step);          // CodeLut::index scale (kt-int lib.rs:383-385)
-            smax[0] = (cg.mant == 0) ? 0 : gmax_g;
-            smax[1] = (cu.mant == 0) ? 0 : gmax_u;
-        }
-        __syncthreads();
-        const Scale idf = sc[2], is = sc[3];
-        const int64_t mg = smax[0], mu = smax[1];
+// Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase).
+__global__ void swiglu_global_kernel(const SwigluArgs a) {
+    __shared__ uint64_t red[32];
+    __shared__ SwigluScales qs;
+    const int r = blockIdx.x;
+    if (r >= a.rows) return;
+    const int f = a.f;
+    int64_t* accg = a.acc + (long long)r * 2 * f;
+    const int64_t* accu = accg + f;
+    if (threadIdx.x == 0) qs = swiglu_scales(a, 0, 0, (int64_t)a.ymax[0], (int64_t)a.ymax[1]);
+    __syncthreads();
+    const SwigluScales q = qs;
+    if (a.phase == 1) {
         uint64_t hm = 0;
         for (int k = threadIdx.x; k < f; k += blockDim.x) {
-            const int64_t g = mg ? (int64_t)kt::requant_act(accg[k], mg) : 0;
-            const int64_t u = mu ? (int64_t)kt::requant_act(accu[k], mu) : 0;
-            const int64_t idx = kt::scale_apply(is, g) - a.silu.lo_index;
-            int64_t code;
-            if (idx < 0)
-                code = 0;
-            else if (idx >= LUT_N)
-                code = kt::scale_apply(idf, g);  // identity right tail, in code units
-            else
-                code = a.silu.codes[idx];
-            const int64_t h = code * u;
-            accg[k] = h;
-            hm = max(hm, uabs64(h));
+            const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
+            accg[k] = v;
+            hm = max(hm, uabs64(v));
         }
         hm = block_max_u64(hm, red);
-        if (a.phase == 1) {
-            if (threadIdx.x == 0 && hm) atomicMax(a.g_hmax, (unsigned long long)hm);
-            return;
-        }
-        hmax = (int64_t)hm;
-    } else {
-        hmax = (int64_t)*a.g_hmax_in;
-        if (threadIdx.x == 0) {
-            const Scale sqx = *a.g_sqx;
-            const Scale cu = kt::scale_mul(sqx, a.wscale_u[e]);
-            const int64_t gmax_u = (int64_t)*a.g_ymax_u;
-            sc[1] = (cu.mant == 0 || gmax_u == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax_u), cu);
-        }
-        __syncthreads();
+        if (threadIdx.x == 0 && hm) atomicMax(a.g_hmax, (unsigned long long)hm);
+        return;
     }
-    // hint = requant_dyn(h, L, hmax); its max |.| is exactly L, so the down linear's quant_to divides by L.
-    for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
-        int32_t q[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int k = k4 + j;
-            int32_t v = 0;
-            if (k < f && hmax > 0) v = kt::quant_to(kt::requant_act(accg[k], hmax), kt::ACT_LEVELS);
-            q[j] = v;
-        }
-        store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
-    }
-    if (threadIdx.x == 0 && (a.phase == 0 || r == 0)) {
-        Scale cd = kt::scale_zero();
-        if (hmax > 0) {
-            const Scale h_scale = kt::scale_mul(a.silu_code_scale, sc[1]);
-            const Scale hint_scale = kt::scale_mul(kt::ratio_act(hmax), h_scale);
-            const Scale s_qh = kt::scale_mul(kt::from_ratio((kt::u128)kt::ACT_LEVELS, (kt::u128)kt::WLEVELS), hint_scale);
-            cd = kt::scale_mul(s_qh, a.wscale_d[e]);
-        }
-        a.row_cd[a.phase == 0 ? r : 0] = cd;
-    }
+    const int64_t hmax = (int64_t)*a.g_hmax;
+    write_down_planes(a, r, accg, hmax);
+    if (r == 0 && threadIdx.x == 0) a.row_cd[0] = down_c(a, q.us, hmax, 0);
 }
 
 // ───────────── combine: one token's selected experts → its output (layers.rs:893-923) ─────────────
 struct CombineArgs {
     const int64_t* acc_d;  // [rows][dim] down accumulators (expert-sorted rows)
+    const unsigned long long* ymax_d;  // [rows]: max |acc_d| of the row, from the GEMM epilogue
     const Scale* row_cd;
     const int* slot_row;   // [T][top_k] → row
     const int64_t* top_ec;
@@ -554,10 +607,12 @@ __global__ void combine_kernel(const CombineArgs a) {
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
     __shared__ int64_t ymax_s[COMBINE_MAX_K];
-    __shared__ Scale f_s[COMBINE_MAX_K];
+    __shared__ kt::ReqDiv ry_s[COMBINE_MAX_K];
+    __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
     __shared__ Scale common_s;
     __shared__ int64_t ec_s[COMBINE_MAX_K];
     __shared__ int row_s[COMBINE_MAX_K];
+    __shared__ int live_s;
     const int t = blockIdx.x;
     if (t >= a.T) return;
     const int K = a.top_k, D = a.dim;
@@ -569,18 +624,12 @@ __global__ void combine_kernel(const CombineArgs a) {
         return;
     }
     if (threadIdx.x < K) {
-        row_s[threadIdx.x] = a.slot_row[(long long)t * K + threadIdx.x];
+        const int row = a.slot_row[(long long)t * K + threadIdx.x];
+        row_s[threadIdx.x] = row;
         ec_s[threadIdx.x] = a.top_ec[(long long)t * K + threadIdx.x];
+        ymax_s[threadIdx.x] = (int64_t)a.ymax_d[row];
     }
     __syncthreads();
-    for (int i = 0; i < K; ++i) {
-        const int64_t* y = a.acc_d + (long long)row_s[i] * D;
-        uint64_t m = 0;
-        for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(y[d]));
-        m = block_max_u64(m, red);
-        if (threadIdx.x == 0) ymax_s[i] = (int64_t)m;
-        __syncthreads();
-    }
     if (threadIdx.x == 0) {
         // ys[i].scale: zero when its c or ymax is zero; common = the last of the largest (fold with ge, :898)
         Scale ys[COMBINE_MAX_K];
@@ -591,10 +640,20 @@ __global__ void combine_kernel(const CombineArgs a) {
             if (kt::scale_ge(ys[i], common)) common = ys[i];
         }
         common_s = common;
+        // the slots that contribute (a zero-scale output contributes 0), packed to the front
+        int n = 0;
         if (common.mant != 0) {
             const Scale cinv = kt::scale_recip(common);
-            for (int i = 0; i < K; ++i) f_s[i] = kt::scale_mul(ys[i], cinv);
+            for (int i = 0; i < K; ++i) {
+                if (ys[i].mant == 0) continue;
+                f_s[n] = kt::make_apply(kt::scale_mul(ys[i], cinv));
+                ry_s[n] = kt::make_req(ymax_s[i]);
+                row_s[n] = row_s[i];
+                ec_s[n] = ec_s[i];
+                ++n;
+            }
         }
+        live_s = n;
     }
     __syncthreads();
     const Scale common = common_s;
@@ -603,20 +662,21 @@ __global__ void combine_kernel(const CombineArgs a) {
         if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
         return;
     }
+    const int n = live_s;
     uint64_t gm = 0;
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         int64_t s = 0;
-        for (int i = 0; i < K; ++i) {
-            if (f_s[i].mant == 0) continue;  // a zero-scale output contributes 0
-            const int64_t yv = (int64_t)kt::requant_act(a.acc_d[(long long)row_s[i] * D + d], ymax_s[i]);
-            s += ec_s[i] * kt::scale_apply(f_s[i], yv);
+        for (int i = 0; i < n; ++i) {
+            const int32_t yv = kt::requant_row(a.acc_d[(long long)row_s[i] * D + d], ry_s[i]);
+            s += ec_s[i] * kt::apply_row(f_s[i], yv);
         }
         acc_s[d] = s;
         gm = max(gm, uabs64(s));
     }
     gm = block_max_u64(gm, red);
     const int64_t gmax = (int64_t)gm;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_act(acc_s[d], gmax) : 0;
+    const kt::ReqDiv rg = kt::make_req(gmax);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
     if (threadIdx.x == 0) {
         a.out_scale[t] = gmax == 0 ? kt::scale_zero()
                                    : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common),
@@ -667,9 +727,9 @@ __global__ void merge_max_kernel(const int32_t* __restrict__ o, const Scale* __r
     if (t >= T) return;
     const Scale cinv = common[1];
     if (common[0].mant == 0) return;
-    const Scale f = kt::scale_mul(o_scale[t], cinv);
+    const kt::ApplyPlan f = kt::make_apply(kt::scale_mul(o_scale[t], cinv));
     uint64_t m = 0;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(kt::scale_apply(f, o[(long long)t * D + d])));
+    for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(kt::apply_row(f, o[(long long)t * D + d])));
     m = block_max_u64(m, red);
     if (threadIdx.x == 0 && m) atomicMax(gmax, (unsigned long long)m);
 }
@@ -682,9 +742,10 @@ __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* _
     if (t >= T) return;
     const int64_t gmax = (int64_t)*gmax_p;
     const bool zero = common[0].mant == 0 || gmax == 0;
-    const Scale f = zero ? kt::scale_zero() : kt::scale_mul(o_scale[t], common[1]);
+    const kt::ApplyPlan f = kt::make_apply(zero ? kt::scale_zero() : kt::scale_mul(o_scale[t], common[1]));
+    const kt::ReqDiv rg = kt::make_req(gmax);
     for (int d = threadIdx.x; d < D; d += blockDim.x)
-        y[(long long)t * D + d] = zero ? 0 : kt::requant_act(kt::scale_apply(f, o[(long long)t * D + d]), gmax);
+        y[(long long)t * D + d] = zero ? 0 : kt::requant_row(kt::apply_row(f, o[(long long)t * D + d]), rg);
     if (t == 0 && threadIdx.x == 0) *y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common[0]);
 }
 
@@ -728,30 +789,34 @@ __global__ void add_prepare_kernel(const AddArgs p) {
     }
 }
 
-__device__ __forceinline__ int64_t add_sum(const AddArgs& p, long long i, Scale fa, Scale fb, int64_t ymax) {
-    const int64_t sv = ymax ? (int64_t)kt::requant_act(p.s_acc[i], ymax) : 0;
-    return kt::scale_apply(fa, p.a[i]) + kt::scale_apply(fb, sv);
+__device__ __forceinline__ int64_t add_sum(const AddArgs& p, long long i, const kt::ApplyPlan& fa,
+                                           const kt::ApplyPlan& fb, const kt::ReqDiv& ry, int64_t ymax) {
+    const int32_t sv = ymax ? kt::requant_row(p.s_acc[i], ry) : 0;
+    return kt::apply_row(fa, p.a[i]) + kt::apply_row(fb, sv);
 }
 
 __global__ void add_max_kernel(const AddArgs p) {
     __shared__ uint64_t red[32];
-    const Scale fa = p.scratch[2], fb = p.scratch[3];
+    const kt::ApplyPlan fa = kt::make_apply(p.scratch[2]), fb = kt::make_apply(p.scratch[3]);
     const int64_t ymax = (int64_t)*p.s_ymax;
+    const kt::ReqDiv ry = kt::make_req(ymax);
     uint64_t m = 0;
     if (p.scratch[1].mant)
         for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
-            m = max(m, uabs64(add_sum(p, i, fa, fb, ymax)));
+            m = max(m, uabs64(add_sum(p, i, fa, fb, ry, ymax)));
     m = block_max_u64(m, red);
     if (threadIdx.x == 0 && m) atomicMax(p.gmax, (unsigned long long)m);
 }
 
 __global__ void add_final_kernel(const AddArgs p) {
-    const Scale fa = p.scratch[2], fb = p.scratch[3], common = p.scratch[1];
+    const kt::ApplyPlan fa = kt::make_apply(p.scratch[2]), fb = kt::make_apply(p.scratch[3]);
+    const Scale common = p.scratch[1];
     const int64_t ymax = (int64_t)*p.s_ymax;
     const int64_t gmax = (int64_t)*p.gmax;
+    const kt::ReqDiv ry = kt::make_req(ymax), rg = kt::make_req(gmax);
     const bool zero = common.mant == 0 || gmax == 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
-        p.y[i] = zero ? 0 : kt::requant_act(add_sum(p, i, fa, fb, ymax), gmax);
+        p.y[i] = zero ? 0 : kt::requant_row(add_sum(p, i, fa, fb, ry, ymax), rg);
     if (blockIdx.x == 0 && threadIdx.x == 0) *p.y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common);
 }
 
