@@ -124,41 +124,34 @@ def measured_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def build_product_layer(w, ctx, log_every=True):
+def build_product_layer(w, ctx, ep=None):
     """Quantise the workload's weights with the product's host quantiser (QuantLinear::from_weights) and make them
-    resident on the device, one matrix at a time (the Mixtral stack is 1.4 G weights)."""
+    resident on the device, one matrix at a time (the Mixtral layer is 1.4 G weights). With ``ep = (rank, world,
+    nccl_id)`` the layer is this rank's part of an expert-parallel layer and only its experts are generated."""
+    import ctypes
+
     import tritify_b200 as tb
 
     d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
-    dev = tb.DeviceLayer(ctx, d, E, f, w["k"], w["norm"], w["sigmoid"], fs)
-    off = 0
+    dev = tb.DeviceLayer(ctx, d, E, f, w["k"], w["norm"], w["sigmoid"], fs, ep=ep)
 
-    def take(n):
-        nonlocal off
-        a = tb.synth_normal(w["wseed"], 0.02, n, offset=off)
-        off += n
-        return a
-
-    def q(n, rows, cols):
-        ql = tb.QuantLinear.from_weights("w", take(n), rows, cols)
+    def q(offset, rows, cols):
+        ql = tb.QuantLinear.from_weights("w", tb.synth_normal(w["wseed"], 0.02, rows * cols, offset=offset), rows, cols)
         return ql.w_codes, ql.w_scale
 
-    router = tb.QuantLinear.from_weights("router", take(E * d), E, d)
-    dev.set_router(router.w_codes, router.w_scale, None)
-    for e in range(E):
-        g = q(f * d, f, d)
-        u = q(f * d, f, d)
-        dn = q(d * f, d, f)
-        dev.set_expert(e, g, u, dn)
+    # one stream (seed wseed): router [E,d], then expert e's gate [f,d], up [f,d], down [d,f], then the shared expert
+    router = q(0, E, d)
+    dev.set_router(router[0], router[1], None)
+    base = E * d
+    for e in dev.experts:
+        o = base + e * 3 * f * d
+        dev.set_expert(e, q(o, f, d), q(o + f * d, f, d), q(o + 2 * f * d, d, f))
     if fs:
-        g = q(fs * d, fs, d)
-        u = q(fs * d, fs, d)
-        dn = q(d * fs, d, fs)
-        dev.set_shared(g, u, dn)
+        o = base + E * 3 * f * d
+        dev.set_shared(q(o, fs, d), q(o + fs * d, fs, d), q(o + 2 * fs * d, d, fs))
     if w["sigmoid"]:
         b = tb.synth_normal(w["wseed"] + 2, 0.02, E)
         codes = np.empty(E, dtype=np.int64)
-        import ctypes
         tb.check(tb.lib().ktmoe_code_sigmoid_bias(b.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), E,
                                                   codes.ctypes.data_as(ctypes.POINTER(ctypes.c_int64))))
         dev.set_sigmoid_bias(codes)
@@ -240,16 +233,30 @@ def run_ours(args, w, name):
     import tritify_b200 as tb
 
     rank, world, local = dist_env()
-    if world > 1:
-        import ep
-
-        return ep.run(args, w, name)
     torch.cuda.set_device(local)
+    dist = None
+    ep = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+        nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            nid.copy_(torch.frombuffer(bytearray(tb.ep_unique_id()), dtype=torch.uint8))
+        dist.broadcast(nid, 0)
+        ep = (rank, world, bytes(nid.cpu().numpy().tobytes()))
     ctx = tb.Context(local)
     t_build = time.perf_counter()
-    dev = build_product_layer(w, ctx)
-    x = make_x(w)
-    T, d = w["T"], w["d"]
+    dev = build_product_layer(w, ctx, ep=ep)
+    x_full = make_x(w)
+    T_all, d = w["T"], w["d"]
+    if T_all % world:
+        raise SystemExit(f"{T_all} tokens do not split evenly over {world} ranks")
+    T = T_all // world  # this rank's token rows (the entry quantiser ran over the whole tensor)
+    x = tb.IntTensor(x_full.data.reshape(T_all, d)[rank * T:(rank + 1) * T], (T, d), x_full.scale)
     log(f"[bench] {name}: layer resident in {time.perf_counter() - t_build:.1f} s")
 
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -262,9 +269,14 @@ def run_ours(args, w, name):
     def step():
         dev.forward_dev(xd.data_ptr(), T, xs_d.data_ptr(), yd.data_ptr(), ys_d.data_ptr(), 0)
 
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
     for _ in range(max(3, args.warmup)):
         step()
     ctx.sync()
+    barrier()
     # bit-exactness of the benchmarked forward: equal to the host-API forward of the same input, and deterministic
     y_ref, ys_ref = dev.forward(x.data, T, x.scale)
     ok_exact = bool((yd.cpu().numpy() == y_ref).all()) and int(ys_d[0]) == ys_ref.mant
@@ -276,13 +288,19 @@ def run_ours(args, w, name):
     launches0 = ctx.launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(smi_index(local)) as clk:
+        barrier()
         torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             step()
         end.record(stream)
         end.synchronize()
+        barrier()
     ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     launches = (ctx.launch_count() - launches0)
     stages, nfw = dev.stage_times()
     dev.set_timing(False)
@@ -305,17 +323,23 @@ def run_ours(args, w, name):
         e2e_step()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_steps = max(3, args.steps // 2)
+    barrier()
     e_start.record(stream)
     for _ in range(e_steps):
         e2e_step()
     e_end.record(stream)
     e_end.synchronize()
     e2e_ms = e_start.elapsed_time(e_end) / e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
     ok_exact = ok_exact and bool((yh.numpy() == y_ref).all())
 
     # roofline of the dominant kernel: the routed gate/up digit-plane GEMM (int8 tensor bound)
     hbm, bf16, peak_kind = measured_peaks()
-    R = T * w["k"]
+    # the rows one rank's GEMM processes: all rows of its experts (balanced routing assumed for the EP figure)
+    R = T_all * w["k"] // world
     gu_ops = 2.0 * R * d * (2 * w["f"]) * P_PLANES
     dn_ops = 2.0 * R * w["f"] * d * P_PLANES
     gu_ms = stage_ms["gemm_gate_up"]
@@ -326,16 +350,16 @@ def run_ours(args, w, name):
     if os.path.exists(tpath):
         traffic = json.load(open(tpath)).get("gemm_gate_up_dram_bytes_per_launch")
 
-    value = T / (ms * 1e-3)
+    value = T_all / (ms * 1e-3)
     res = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
         "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
-                   "parallelism": "ep1", "l2": "working set (weight planes) larger than L2, no flush",
+                   "parallelism": f"ep{world}", "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
                    "bit_exact_vs_host_api": ok_exact},
-        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T * d * 4 + 16,
-                "d2h_bytes_per_step": T * d * 4 + 16},
+        "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
+                "d2h_bytes_per_step": T_all * d * 4 + 16 * world},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
                      "frac": achieved / int8_peak, "traffic": traffic, "kernel": "digit_gemm gate/up",
@@ -345,7 +369,14 @@ def run_ours(args, w, name):
         "gemm_down_tops": dn_ops / (stage_ms["gemm_down"] * 1e-3) / 1e12,
         "clocks": clk.summary(),
     }
-    if rank == 0 and not args.no_cpu:
+    if dist is not None:
+        dev = None
+        ctx.sync()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    if not args.no_cpu and world == 1:
         from oracle import oracle as O
 
         O.build()
@@ -354,7 +385,7 @@ def run_ours(args, w, name):
         m.forward(xi[:rows], xs)
         dt = time.perf_counter() - t0
         res["cpu_baseline"] = {"value": rows / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-                               "sample": f"first {rows} of {T} tokens, one forward (C++ restatement of the "
+                               "sample": f"first {rows} of {T_all} tokens, one forward (C++ restatement of the "
                                          f"reference CPU path, its own thread policy over all cores)"}
     print(json.dumps(res), flush=True)
 

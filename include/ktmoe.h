@@ -81,6 +81,17 @@ int ktmoe_resident_bytes(ktmoe_ctx* ctx, uint64_t* bytes);
 /* ── the MoE layer (MoeMlp) ── */
 int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_layer** out);
 int ktmoe_layer_destroy(ktmoe_layer* layer);
+/* ── expert parallelism over NCCL (NVLink / NVSwitch) ──
+ * One process (or one context) per GPU. Rank r of `world` owns experts [r*E/world, (r+1)*E/world) and passes its own
+ * token rows to ktmoe_forward / ktmoe_forward_dev (any count, 0 included); the result is bit-identical to one
+ * ktmoe_forward over all ranks' rows concatenated in rank order. All ranks must call every forward together.
+ * The unique id (128 bytes) is made by one rank with ktmoe_ep_unique_id and handed to the others out of band. */
+int ktmoe_ep_unique_id(void* id, int64_t bytes);
+int ktmoe_layer_create_ep(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int32_t rank, int32_t world,
+                          const void* nccl_id, ktmoe_layer** out);
+/* The experts this layer holds: [*begin, *end). ktmoe_layer_set_expert takes global expert ids in that range. */
+int ktmoe_layer_experts(const ktmoe_layer* layer, int32_t* begin, int32_t* end);
+
 /* Router codes [E][d_model] (QuantLinear w_codes, row-major) and w_scale; bias_codes [E] + bias_scale from
  * QuantLinear::with_bias, or NULL for no bias. */
 int ktmoe_layer_set_router(ktmoe_layer* layer, const int32_t* codes, ktmoe_scale w_scale, const int64_t* bias_codes,

@@ -1,0 +1,106 @@
+"""Expert parallelism over NCCL (ktmoe_layer_create_ep): the rows of each rank, concatenated in rank order, must be
+bit-identical to the single-GPU forward (and so to the golden hashes of the CPU path). Needs two or more GPUs; the
+ranks run as spawned processes, one per GPU."""
+
+import json
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+import tritify_b200 as tb
+
+pytestmark = pytest.mark.gpu
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+GOLDEN = json.load(open(os.path.join(HERE, "golden", "golden.json")))
+
+import cases  # noqa: E402
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _splits(T, world, mode):
+    if mode == "even":
+        base = [T // world] * world
+        for i in range(T % world):
+            base[i] += 1
+        return base
+    if mode == "first_empty":
+        return [0] + [T // (world - 1) + (1 if i < T % (world - 1) else 0) for i in range(world - 1)]
+    raise ValueError(mode)
+
+
+def _worker(rank, world, port, name, mode, outdir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        nid.copy_(torch.frombuffer(bytearray(tb.ep_unique_id()), dtype=torch.uint8))
+    dist.broadcast(nid, 0)
+    c = cases.CASES[name]
+    ctx = tb.Context(rank)
+    m = cases.build_layer(c, ctx)  # the host mirror (quantised weights); only this rank's experts go to its device
+    dev = tb.DeviceLayer(ctx, c.d, c.E, c.f, c.k, c.norm, c.sigmoid, c.shared,
+                         ep=(rank, world, bytes(nid.cpu().numpy().tobytes())))
+    dev.set_router(m.router.w_codes, m.router.w_scale, m.router.bias)
+    if c.sigmoid:
+        dev.set_sigmoid_bias(m.sigmoid_bias_codes)
+    for e in dev.experts:
+        ex = m.experts[e]
+        dev.set_expert(e, (ex.gate.w_codes, ex.gate.w_scale), (ex.up.w_codes, ex.up.w_scale),
+                       (ex.down.w_codes, ex.down.w_scale))
+    if c.shared:
+        s = m.shared
+        dev.set_shared((s.gate.w_codes, s.gate.w_scale), (s.up.w_codes, s.up.w_scale), (s.down.w_codes, s.down.w_scale))
+    x = tb.IntTensor.from_reals(cases.make_x(c))
+    sizes = _splits(c.T, world, mode)
+    start = sum(sizes[:rank])
+    rows = sizes[rank]
+    xr = x.data.reshape(c.T, c.d)[start:start + rows]
+    for rep in range(2):  # twice: the second forward reuses every buffer
+        y, ys = dev.forward(xr, rows, x.scale)
+    np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=y, mant=ys.mant, shift=ys.shift, rows=rows)
+    dev = None
+    ctx.sync()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name,mode", [("tiny_softmax_37rows", "even"), ("small_shared_softmax", "even"),
+                                       ("tiny_sigmoid_shared", "first_empty"), ("config1", "even")])
+def test_expert_parallel_equals_one_gpu(tmp_path, name, mode):
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("expert parallelism needs two or more GPUs")
+    c = cases.CASES[name]
+    world = min(world, c.E)
+    if mode == "first_empty" and c.T < world - 1:
+        world = 2
+    mp.spawn(_worker, args=(world, _free_port(), name, mode, str(tmp_path)), nprocs=world, join=True)
+    ys, scales = [], set()
+    for r in range(world):
+        z = np.load(tmp_path / f"rank{r}.npz")
+        if int(z["rows"]) > 0:
+            ys.append(z["y"])
+            scales.add((int(z["mant"]), int(z["shift"])))
+    assert len(scales) == 1, f"ranks disagree on the output scale: {scales}"
+    y = np.concatenate(ys)
+    assert cases.out_hashes(y, scales.pop()) == GOLDEN["cases"][name]["output"]

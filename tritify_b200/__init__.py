@@ -28,6 +28,7 @@ from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 __all__ = [
     "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
     "B200Linear", "Context", "DeviceLayer", "device_count", "synth_normal", "lcg_uniform", "table", "KtmoeError",
+    "ep_unique_id",
 ]
 
 WLEVELS = 265720  # (3^12 - 1) / 2, layers.rs:16
@@ -248,14 +249,23 @@ class DeviceLayer:
     """One MoE layer resident on a device (ktmoe_layer): weights as digit planes, scratch for the forward."""
 
     def __init__(self, ctx: Context, d_model: int, n_experts: int, d_ff: int, top_k: int, norm_topk_prob: bool,
-                 sigmoid: bool, shared_d_ff: int):
+                 sigmoid: bool, shared_d_ff: int, ep: Optional[tuple] = None):
+        """``ep = (rank, world, nccl_id_bytes)`` makes this rank's part of an expert-parallel layer."""
         self.ctx = ctx
         cfg = KtmoeLayerConfig(d_model, n_experts, d_ff, top_k, 1 if norm_topk_prob else 0, 1 if sigmoid else 0,
                                shared_d_ff)
         h = ctypes.c_void_p()
-        ctx.check(lib().ktmoe_layer_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)))
+        if ep is None:
+            ctx.check(lib().ktmoe_layer_create(ctx.handle, ctypes.byref(cfg), ctypes.byref(h)))
+        else:
+            rank, world, nid = ep
+            buf = ctypes.create_string_buffer(bytes(nid), len(nid))
+            ctx.check(lib().ktmoe_layer_create_ep(ctx.handle, ctypes.byref(cfg), rank, world, buf, ctypes.byref(h)))
         self._h = h
         self.d_model, self.n_experts, self.d_ff, self.top_k, self.shared_d_ff = d_model, n_experts, d_ff, top_k, shared_d_ff
+        b, e = ctypes.c_int32(), ctypes.c_int32()
+        ctx.check(lib().ktmoe_layer_experts(self._h, ctypes.byref(b), ctypes.byref(e)))
+        self.experts = range(b.value, e.value)
 
     def __del__(self):
         try:
@@ -298,6 +308,13 @@ class DeviceLayer:
     def forward(self, x: np.ndarray, rows: int, x_scale: Scale):
         """Host buffers in and out (synchronous): returns (y int32 [rows·d], Scale)."""
         x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        if x.size == 0:
+            x = np.zeros(1, np.int32)
+            y = np.zeros(1, np.int32)
+            ys = KtmoeScale()
+            self.ctx.check(lib().ktmoe_forward(self._h, _p(x, ctypes.c_int32), 0, x_scale._c(), _p(y, ctypes.c_int32),
+                                               ctypes.byref(ys)))
+            return np.zeros(0, np.int32), Scale._of(ys)
         if x.size != rows * self.d_model:
             raise ValueError("x is not rows·d_model")
         y = np.empty(rows * self.d_model, dtype=np.int32)
@@ -430,6 +447,13 @@ class MoeMlp:
     def route_trace(self, x: IntTensor) -> List[List[int]]:
         """Module::route_trace (layers.rs:1089-1100)."""
         return [r.experts for r in self.route(x)]
+
+
+def ep_unique_id() -> bytes:
+    """A new NCCL unique id (128 bytes) for an expert-parallel layer; one rank makes it, all ranks use it."""
+    buf = ctypes.create_string_buffer(128)
+    check(lib().ktmoe_ep_unique_id(buf, 128))
+    return buf.raw
 
 
 def synth_normal(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray:

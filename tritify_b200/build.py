@@ -61,13 +61,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 cmd.insert(1, "-Xptxas=-v")
             _run(cmd, verbose)
     if force or _stale(LIB, objs):
-        _run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda" if _has_libcuda() else "", "-lpthread"], verbose)
+        _run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lnccl", "-lpthread"], verbose)
     return LIB
-
-
-def _has_libcuda() -> bool:
-    # cudaGetDriverEntryPoint is used for the tensor-map encoder, so libcuda is not a link dependency.
-    return False
 
 
 def _run(cmd: list[str], verbose: bool) -> None:

@@ -48,6 +48,7 @@ struct GemmArgs {
     const int* tile_group;     // per n-tile: group (nullptr: single group 0)
     const int* tile_row0;      // per n-tile: first activation row (nullptr: tile * BN)
     const int* group_row_end;  // per group: end row, exclusive (nullptr: single_rows)
+    const int* tile_row_end;   // per n-tile: end row, exclusive (overrides group_row_end; a group may have several runs)
     const int* n_tiles;        // device count of valid n-tiles (nullptr: n_tiles_max)
     int n_tiles_max;           // upper bound of n-tiles (the launch covers m_tiles x n_tiles_max, rounded up)
     int m_tiles;               // weight tiles of one group (M_pad / BM)
@@ -200,7 +201,7 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int tile, int b
     TileInfo t;
     t.group = a.tile_group ? a.tile_group[tile] : 0;
     t.row0 = a.tile_row0 ? a.tile_row0[tile] : tile * bn;
-    const int row_end = a.group_row_end ? a.group_row_end[t.group] : a.single_rows;
+    const int row_end = a.tile_row_end ? a.tile_row_end[tile] : a.group_row_end ? a.group_row_end[t.group] : a.single_rows;
     t.n_valid = min(bn, row_end - t.row0);
     return t;
 }

@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -168,6 +169,7 @@ struct GemmCall {
     const int* tile_group = nullptr;
     const int* tile_row0 = nullptr;
     const int* group_end = nullptr;
+    const int* tile_row_end = nullptr;
     const int* n_tiles = nullptr;
     int64_t single_rows = 0;
     unsigned long long* rowmax = nullptr;  // fused |max| per (row, slot); see dg::GemmArgs
@@ -204,6 +206,7 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.tile_group = g.tile_group;
         a.tile_row0 = g.tile_row0;
         a.group_row_end = g.group_end;
+        a.tile_row_end = g.tile_row_end;
         a.n_tiles = g.n_tiles;
         a.n_tiles_max = (int)g.grid_y;
         a.m_tiles = (int)m_tiles;
@@ -282,6 +285,14 @@ struct ktmoe_layer {
     ktmoe_ctx* ctx = nullptr;
     ktmoe_layer_config cfg{};
     int64_t d = 0, E = 0, f = 0, K = 0, fs = 0;
+    // expert parallelism: this rank owns experts [e_begin, e_end) of E (E_local = e_end - e_begin)
+    int rank = 0, world = 1;
+    int64_t e_begin = 0, e_end = 0, E_local = 0;
+    ncclComm_t comm = nullptr;
+    DevBuf ep_counts, ep_counts_all, ep_meta_send, ep_meta_recv, ep_recv_planes, ep_recv_sqx, ep_recv_row_expert,
+        ep_y_send, ep_ys_send, ep_y_back, ep_ys_back, ep_tiles, ep_runs, ep_rec, ep_recs, ep_best_idx;
+    std::vector<int> h_counts;
+    int64_t ep_tok_offset = 0, ep_tok_total = 0;
     int64_t d_pad = 0, f_pad = 0, fs_pad = 0;
     Planes w_router, w_gu, w_dn, w_sgu, w_sdn;
     DevBuf b_router, b_gu, b_dn, b_sgu, b_sdn;
@@ -333,10 +344,24 @@ unsigned long long* scal_u64(ktmoe_layer* L, int slot) {
 int* n_tiles_ptr(ktmoe_layer* L) { return (int*)(scal_u64(L, U_NTILES_PAD)); }
 int* n_tiles2_ptr(ktmoe_layer* L) { return (int*)(scal_u64(L, U_NTILES_PAD)) + 1; }
 
+// Buffers of the routed experts for `rows` expert rows (the home's rows on one rank, the received rows with EP).
+int ensure_rows(ktmoe_layer* L, int64_t rows) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t n = std::max<int64_t>(rows, 1), n_pad = round_up(n, 64);
+    CK(L->acc_gu.ensure(n * 2 * L->f * 8));
+    CK(L->hq_planes.ensure(3 * n_pad * L->f_pad));
+    CK(L->row_cd.ensure(n * sizeof(Scale)));
+    CK(L->acc_d.ensure(n * L->d * 8));
+    CK(L->rowmax_gu.ensure(n * 2 * 8));
+    CK(L->rowmax_d.ensure(n * 8));
+    return KTMOE_OK;
+}
+
 int ensure_scratch(ktmoe_layer* L, int64_t T) {
     ktmoe_ctx* ctx = L->ctx;
     if (T <= L->cap && L->cap > 0) return KTMOE_OK;
-    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
+    const int64_t d = L->d, E = L->E, K = L->K, fs = L->fs;
+    T = std::max<int64_t>(T, 1);
     const int64_t R = T * K;
     const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
     const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
@@ -366,12 +391,7 @@ int ensure_scratch(ktmoe_layer* L, int64_t T) {
     CK(L->row_assign.ensure(R * 4));
     CK(L->row_expert.ensure(R * 4));
     CK(L->xg_planes.ensure(3 * R_pad * L->d_pad));
-    CK(L->acc_gu.ensure(R * 2 * f * 8));
-    CK(L->hq_planes.ensure(3 * R_pad * L->f_pad));
-    CK(L->row_cd.ensure(R * sizeof(Scale)));
-    CK(L->acc_d.ensure(R * d * 8));
-    CK(L->rowmax_gu.ensure(R * 2 * 8));
-    CK(L->rowmax_d.ensure(R * 8));
+    if (int r = ensure_rows(L, R)) return r;
     CK(L->tok_out.ensure(T * d * 4));
     CK(L->tok_scale.ensure(T * sizeof(Scale)));
     if (fs > 0) {
@@ -465,21 +485,35 @@ int stage_route(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs
     return KTMOE_OK;
 }
 
-int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
-                  cudaStream_t st) {
-    ktmoe_ctx* ctx = L->ctx;
-    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
-    const int64_t R = T * K;
-    const int64_t T_pad = round_up(T, 64), R_pad = round_up(R, 64);
-    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
-    MARK(L, st);
-    int r = stage_route(L, T, x_dev, xs_dev, st);
-    if (r) return r;
-    MARK(L, st);
+// ── collectives of an expert-parallel layer (no-ops on one rank) ──
+int nccl_check(ktmoe_ctx* ctx, ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return KTMOE_OK;
+    return fail(ctx, KTMOE_ERR_CUDA, std::string(what) + ": " + ncclGetErrorString(r));
+}
 
-    // dispatch plan: stable counting sort of the T·K assignments by expert
-    const int BN = pick_bn((double)R / (double)E);
-    const int BN2 = pick_bn_long_k((double)R / (double)E, f);
+#define NK(expr)                                                          \
+    do {                                                                  \
+        if (int r__ = nccl_check(ctx, (expr), #expr)) return r__;         \
+    } while (0)
+
+// max over the ranks of n u64 words, in place
+int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t st) {
+    if (L->world == 1) return KTMOE_OK;
+    ktmoe_ctx* ctx = L->ctx;
+    NK(ncclAllReduce(p, p, n, ncclUint64, ncclMax, L->comm, st));
+    return KTMOE_OK;
+}
+
+// Dispatch plan of the home rank: a stable counting sort of the T·K (token, slot) rows by expert, the tile tables of
+// the grouped GEMMs (widths BN and BN2) and the rows' digit planes gathered in that order (xg_planes).
+int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t E = L->E, K = L->K, R = T * K;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
+    if (R == 0) {
+        CK(cudaMemsetAsync(L->expert_count.p, 0, E * 4, st));
+        return KTMOE_OK;
+    }
     const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
     mk::plan_count_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, E * 4, st>>>(L->top_e.as<int32_t>(), R, (int)E,
                                                                              L->counts.as<int>());
@@ -498,29 +532,51 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     mk::permute_planes_kernel<<<(unsigned)R, 128, 0, st>>>(L->tok_planes.as<int8_t>(), T_pad, L->xg_planes.as<int8_t>(),
                                                          R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
     CKL(ctx);
-    MARK(L, st);
+    return KTMOE_OK;
+}
 
-    // routed gate+up: one grouped GEMM over the E experts
-    const int64_t max_tiles = (R + BN - 1) / BN + E;
+// The routed experts over n_rows rows of digit planes `B` (R_pad rows per plane): gate/up GEMM with fused row maxima,
+// SwiGLU + requant + the down input planes, down GEMM with fused row maxima (acc_d, rowmax_d, row_cd).
+struct ExpertRows {
+    Planes B;
+    int64_t n_rows;
+    int BN, BN2;
+    int64_t grid_a, grid_b;  // n-tile bounds of the two tables
+    const int *tg_a, *tr_a, *te_a, *nt_a;  // table a: group, row0, row end (or nullptr + group_end), count
+    const int *tg_b, *tr_b, *te_b, *nt_b;
+    const int* group_end;
+    const int* row_assign;  // nullptr: row_sqx is per row
+    const int* row_expert;
+    const Scale* row_sqx;
+};
+
+int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, f = L->f, R = x.n_rows;
+    if (R == 0) {
+        MARK(L, st);
+        MARK(L, st);
+        return KTMOE_OK;
+    }
     GemmCall g;
     g.A = L->w_gu;
     g.M_valid = 2 * f;
-    g.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
+    g.B = x.B;
     g.out = L->acc_gu.as<int64_t>();
     g.ld_out = 2 * f;
-    g.BN = BN;
-    g.grid_y = max_tiles;
-    g.tile_group = L->tile_group.as<int>();
-    g.tile_row0 = L->tile_row0.as<int>();
-    g.group_end = L->group_end.as<int>();
-    g.n_tiles = n_tiles_ptr(L);
+    g.BN = x.BN;
+    g.grid_y = x.grid_a;
+    g.tile_group = x.tg_a;
+    g.tile_row0 = x.tr_a;
+    g.tile_row_end = x.te_a;
+    g.group_end = x.group_end;
+    g.n_tiles = x.nt_a;
     g.rowmax = L->rowmax_gu.as<unsigned long long>();
     g.rowmax_stride = 2;
     g.rowmax_split = f;
     CK(cudaMemsetAsync(L->rowmax_gu.p, 0, R * 2 * 8, st));
     CK(cudaMemsetAsync(L->rowmax_d.p, 0, R * 8, st));
-    r = run_gemm(ctx, st, g);
-    if (r) return r;
+    if (int r = run_gemm(ctx, st, g)) return r;
     MARK(L, st);
 
     mk::SwigluArgs sa;
@@ -529,15 +585,14 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sa.rows = (int)R;
     sa.f = (int)f;
     sa.f_pad = (int)L->f_pad;
-    sa.R_pad = R_pad;
-    sa.row_assign = L->row_assign.as<int>();
-    sa.row_expert = L->row_expert.as<int>();
-    sa.top_k = (int)K;
-    sa.row_sqx = L->tok_sqx.as<Scale>();
-    sa.g_sqx = nullptr;
+    sa.R_pad = x.B.rows_pad;
+    sa.row_assign = x.row_assign;
+    sa.row_expert = x.row_expert;
+    sa.top_k = (int)L->K;
+    sa.row_sqx = x.row_sqx;
     sa.wscale_g = L->b_wsc.as<Scale>();
-    sa.wscale_u = L->b_wsc.as<Scale>() + E;
-    sa.wscale_d = L->b_wsc.as<Scale>() + 2 * E;
+    sa.wscale_u = L->b_wsc.as<Scale>() + L->E_local;
+    sa.wscale_d = L->b_wsc.as<Scale>() + 2 * L->E_local;
     sa.silu = lut(L, 1);
     sa.silu_code_scale = S(L->tabs[1].code_scale);
     sa.silu_code_scale_recip = L->silu_code_scale_recip;
@@ -566,82 +621,353 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
 
     g.A = L->w_dn;
     g.M_valid = d;
-    g.B = Planes{L->hq_planes.as<int8_t>(), 1, R_pad, f, L->f_pad};
+    g.B = Planes{L->hq_planes.as<int8_t>(), 1, x.B.rows_pad, f, L->f_pad};
     g.out = L->acc_d.as<int64_t>();
     g.ld_out = d;
-    g.BN = BN2;
-    g.grid_y = (R + BN2 - 1) / BN2 + E;
-    g.tile_group = L->tile_group2.as<int>();
-    g.tile_row0 = L->tile_row02.as<int>();
-    g.n_tiles = n_tiles2_ptr(L);
+    g.BN = x.BN2;
+    g.grid_y = x.grid_b;
+    g.tile_group = x.tg_b;
+    g.tile_row0 = x.tr_b;
+    g.tile_row_end = x.te_b;
+    g.n_tiles = x.nt_b;
     g.rowmax = L->rowmax_d.as<unsigned long long>();
     g.rowmax_stride = 1;
     g.rowmax_split = INT32_MAX;
-    r = run_gemm(ctx, st, g);
-    if (r) return r;
+    if (int r = run_gemm(ctx, st, g)) return r;
+    return KTMOE_OK;
+}
+
+// Expert parallelism: exchange the home rank's expert-sorted rows with the experts' owners, run the local experts on
+// what arrives, return their outputs (i32 + Scale per row) and combine at home. Grouped ncclSend/ncclRecv over the
+// world; every rank takes the same collective steps.
+int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, E = L->E, K = L->K, R = T * K, G = L->world, rk = L->rank;
+    const int64_t R_pad = round_up(std::max<int64_t>(R, 1), 64);
+    const int BN = pick_bn((double)R * G / (double)E), BN2 = pick_bn_long_k((double)R * G / (double)E, L->f);
+    if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
+    // per-row s_qx for the owners, and this rank's per-expert counts (+ its token count) for everyone
+    CK(L->ep_meta_send.ensure(std::max<int64_t>(R, 1) * 16));
+    if (R > 0) {
+        mk::pack_meta_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(L->row_assign.as<int>(), (int)K,
+                                                                        L->tok_sqx.as<Scale>(), (int)R,
+                                                                        L->ep_meta_send.as<int64_t>());
+        CKL(ctx);
+    }
+    CK(L->ep_counts.ensure((E + 1) * 4));
+    CK(L->ep_counts_all.ensure(G * (E + 1) * 4));
+    CK(cudaMemcpyAsync(L->ep_counts.p, L->expert_count.p, E * 4, cudaMemcpyDeviceToDevice, st));
+    const int32_t t32 = (int32_t)T;
+    CK(cudaMemcpyAsync(L->ep_counts.as<int32_t>() + E, &t32, 4, cudaMemcpyHostToDevice, st));
+    NK(ncclAllGather(L->ep_counts.p, L->ep_counts_all.p, E + 1, ncclInt32, L->comm, st));
+    L->h_counts.resize(G * (E + 1));
+    CK(cudaMemcpyAsync(L->h_counts.data(), L->ep_counts_all.p, G * (E + 1) * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    const std::vector<int>& hc = L->h_counts;
+    auto cnt = [&](int64_t src, int64_t e) { return (int64_t)hc[src * (E + 1) + e]; };
+    auto begin_of = [&](int64_t q) { return q * E / G; };
+    std::vector<int64_t> send_rows(G), send_off(G), recv_rows(G), recv_off(G);
+    int64_t so = 0, ro = 0;
+    L->ep_tok_offset = 0;
+    L->ep_tok_total = 0;
+    for (int64_t q = 0; q < G; ++q) {
+        int64_t sr = 0, rr = 0;
+        for (int64_t e = begin_of(q); e < begin_of(q + 1); ++e) sr += cnt(rk, e);
+        for (int64_t e = L->e_begin; e < L->e_end; ++e) rr += cnt(q, e);
+        send_rows[q] = sr;
+        send_off[q] = so;
+        recv_rows[q] = rr;
+        recv_off[q] = ro;
+        so += sr;
+        ro += rr;
+        if (q < rk) L->ep_tok_offset += cnt(q, E);
+        L->ep_tok_total += cnt(q, E);
+    }
+    const int64_t Rr = ro, Rr_pad = round_up(std::max<int64_t>(Rr, 1), 64);
+    // received rows come in source order, each source's rows sorted by expert: runs (source, local expert) with
+    // their tiles for the two GEMM widths
+    std::vector<int> runs_start, runs_count, runs_group, ta_g, ta_r, ta_e, tb_g, tb_r, tb_e;
+    for (int64_t q = 0; q < G; ++q) {
+        int64_t at = recv_off[q];
+        for (int64_t e = L->e_begin; e < L->e_end; ++e) {
+            const int64_t c = cnt(q, e);
+            if (c == 0) continue;
+            runs_start.push_back((int)at);
+            runs_count.push_back((int)c);
+            runs_group.push_back((int)(e - L->e_begin));
+            for (int64_t r0 = 0; r0 < c; r0 += BN) {
+                ta_g.push_back((int)(e - L->e_begin));
+                ta_r.push_back((int)(at + r0));
+                ta_e.push_back((int)(at + c));
+            }
+            for (int64_t r0 = 0; r0 < c; r0 += BN2) {
+                tb_g.push_back((int)(e - L->e_begin));
+                tb_r.push_back((int)(at + r0));
+                tb_e.push_back((int)(at + c));
+            }
+            at += c;
+        }
+    }
+    const int64_t n_runs = (int64_t)runs_start.size(), na = (int64_t)ta_g.size(), nb = (int64_t)tb_g.size();
+    std::vector<int> tiles;  // [na | na | na | nb | nb | nb | na | nb] then runs [3][n_runs]
+    tiles.insert(tiles.end(), ta_g.begin(), ta_g.end());
+    tiles.insert(tiles.end(), ta_r.begin(), ta_r.end());
+    tiles.insert(tiles.end(), ta_e.begin(), ta_e.end());
+    tiles.insert(tiles.end(), tb_g.begin(), tb_g.end());
+    tiles.insert(tiles.end(), tb_r.begin(), tb_r.end());
+    tiles.insert(tiles.end(), tb_e.begin(), tb_e.end());
+    tiles.push_back((int)na);
+    tiles.push_back((int)nb);
+    tiles.insert(tiles.end(), runs_start.begin(), runs_start.end());
+    tiles.insert(tiles.end(), runs_count.begin(), runs_count.end());
+    tiles.insert(tiles.end(), runs_group.begin(), runs_group.end());
+    CK(L->ep_tiles.ensure(tiles.size() * 4));
+    CK(cudaMemcpyAsync(L->ep_tiles.p, tiles.data(), tiles.size() * 4, cudaMemcpyHostToDevice, st));
+    const int* td = L->ep_tiles.as<int>();
+
+    // the exchange of rows: three digit planes and the s_qx words
+    CK(L->ep_recv_planes.ensure(3 * Rr_pad * L->d_pad));
+    CK(L->ep_meta_recv.ensure(std::max<int64_t>(Rr, 1) * 16));
+    NK(ncclGroupStart());
+    for (int64_t q = 0; q < G; ++q) {
+        for (int p = 0; p < 3; ++p) {
+            if (send_rows[q])
+                NK(ncclSend(L->xg_planes.as<int8_t>() + (p * R_pad + send_off[q]) * L->d_pad, send_rows[q] * L->d_pad,
+                            ncclInt8, (int)q, L->comm, st));
+            if (recv_rows[q])
+                NK(ncclRecv(L->ep_recv_planes.as<int8_t>() + (p * Rr_pad + recv_off[q]) * L->d_pad,
+                            recv_rows[q] * L->d_pad, ncclInt8, (int)q, L->comm, st));
+        }
+        if (send_rows[q])
+            NK(ncclSend(L->ep_meta_send.as<int64_t>() + 2 * send_off[q], 2 * send_rows[q], ncclInt64, (int)q, L->comm,
+                        st));
+        if (recv_rows[q])
+            NK(ncclRecv(L->ep_meta_recv.as<int64_t>() + 2 * recv_off[q], 2 * recv_rows[q], ncclInt64, (int)q, L->comm,
+                        st));
+    }
+    NK(ncclGroupEnd());
     MARK(L, st);
 
-    mk::CombineArgs ca;
-    ca.acc_d = L->acc_d.as<int64_t>();
-    ca.ymax_d = L->rowmax_d.as<unsigned long long>();
-    ca.row_cd = L->row_cd.as<Scale>();
-    ca.slot_row = L->slot_row.as<int>();
-    ca.top_ec = L->top_ec.as<int64_t>();
-    ca.sumc = L->sumc.as<int64_t>();
-    ca.T = (int)T;
-    ca.top_k = (int)K;
-    ca.dim = (int)d;
-    ca.out = L->tok_out.as<int32_t>();
-    ca.out_scale = L->tok_scale.as<Scale>();
-    mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
-    CKL(ctx);
+    // the owner side: this rank's experts on the rows it received
+    if (int r = ensure_rows(L, Rr)) return r;
+    CK(L->ep_recv_sqx.ensure(std::max<int64_t>(Rr, 1) * sizeof(Scale)));
+    CK(L->ep_recv_row_expert.ensure(std::max<int64_t>(Rr, 1) * 4));
+    if (Rr > 0) {
+        mk::meta_to_scale_kernel<<<(unsigned)((Rr + 255) / 256), 256, 0, st>>>(L->ep_meta_recv.as<int64_t>(), (int)Rr,
+                                                                             L->ep_recv_sqx.as<Scale>());
+        CKL(ctx);
+        const int* runs = td + 3 * na + 3 * nb + 2;
+        mk::runs_to_rows_kernel<<<(unsigned)n_runs, 128, 0, st>>>(runs, runs + n_runs, runs + 2 * n_runs, (int)n_runs,
+                                                                 L->ep_recv_row_expert.as<int>());
+        CKL(ctx);
+    }
+    ExpertRows xr;
+    xr.B = Planes{L->ep_recv_planes.as<int8_t>(), 1, Rr_pad, d, L->d_pad};
+    xr.n_rows = Rr;
+    xr.BN = BN;
+    xr.BN2 = BN2;
+    xr.grid_a = std::max<int64_t>(na, 1);
+    xr.grid_b = std::max<int64_t>(nb, 1);
+    xr.tg_a = td;
+    xr.tr_a = td + na;
+    xr.te_a = td + 2 * na;
+    xr.tg_b = td + 3 * na;
+    xr.tr_b = td + 3 * na + nb;
+    xr.te_b = td + 3 * na + 2 * nb;
+    xr.nt_a = td + 3 * na + 3 * nb;
+    xr.nt_b = td + 3 * na + 3 * nb + 1;
+    xr.group_end = nullptr;
+    xr.row_assign = nullptr;
+    xr.row_expert = L->ep_recv_row_expert.as<int>();
+    xr.row_sqx = L->ep_recv_sqx.as<Scale>();
+    if (int r = run_experts(L, xr, st)) return r;
+    CK(L->ep_y_send.ensure(std::max<int64_t>(Rr, 1) * d * 4));
+    CK(L->ep_ys_send.ensure(std::max<int64_t>(Rr, 1) * sizeof(Scale)));
+    if (Rr > 0) {
+        mk::expert_out_kernel<<<(unsigned)Rr, 256, 0, st>>>(L->acc_d.as<int64_t>(), L->rowmax_d.as<unsigned long long>(),
+                                                           L->row_cd.as<Scale>(), (int)Rr, (int)d,
+                                                           L->ep_y_send.as<int32_t>(), L->ep_ys_send.as<Scale>());
+        CKL(ctx);
+    }
     MARK(L, st);
 
+    // the outputs go home, in the order the rows came
+    CK(L->ep_y_back.ensure(std::max<int64_t>(R, 1) * d * 4));
+    CK(L->ep_ys_back.ensure(std::max<int64_t>(R, 1) * sizeof(Scale)));
+    NK(ncclGroupStart());
+    for (int64_t q = 0; q < G; ++q) {
+        if (recv_rows[q]) {
+            NK(ncclSend(L->ep_y_send.as<int32_t>() + recv_off[q] * d, recv_rows[q] * d, ncclInt32, (int)q, L->comm, st));
+            NK(ncclSend(L->ep_ys_send.as<Scale>() + recv_off[q], recv_rows[q] * sizeof(Scale), ncclInt8, (int)q,
+                        L->comm, st));
+        }
+        if (send_rows[q]) {
+            NK(ncclRecv(L->ep_y_back.as<int32_t>() + send_off[q] * d, send_rows[q] * d, ncclInt32, (int)q, L->comm, st));
+            NK(ncclRecv(L->ep_ys_back.as<Scale>() + send_off[q], send_rows[q] * sizeof(Scale), ncclInt8, (int)q,
+                        L->comm, st));
+        }
+    }
+    NK(ncclGroupEnd());
+    if (T > 0) {
+        mk::CombineYArgs ca;
+        ca.y = L->ep_y_back.as<int32_t>();
+        ca.ys = L->ep_ys_back.as<Scale>();
+        ca.slot_row = L->slot_row.as<int>();
+        ca.top_ec = L->top_ec.as<int64_t>();
+        ca.sumc = L->sumc.as<int64_t>();
+        ca.T = (int)T;
+        ca.top_k = (int)K;
+        ca.dim = (int)d;
+        ca.out = L->tok_out.as<int32_t>();
+        ca.out_scale = L->tok_scale.as<Scale>();
+        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        CKL(ctx);
+    }
+    MARK(L, st);
+    return KTMOE_OK;
+}
+
+int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
+                  cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
+    const int64_t R = T * K;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
+    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
+    MARK(L, st);
+    if (T > 0) {
+        if (int r = stage_route(L, T, x_dev, xs_dev, st)) return r;
+    }
+    MARK(L, st);
+
+    int64_t T_total = T, tok_offset = 0;
+    if (L->world == 1) {
+        const int BN = pick_bn((double)R / (double)E);
+        const int BN2 = pick_bn_long_k((double)R / (double)E, f);
+        if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
+        MARK(L, st);
+        ExpertRows xr;
+        xr.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
+        xr.n_rows = R;
+        xr.BN = BN;
+        xr.BN2 = BN2;
+        xr.grid_a = (R + BN - 1) / BN + E;
+        xr.grid_b = (R + BN2 - 1) / BN2 + E;
+        xr.tg_a = L->tile_group.as<int>();
+        xr.tr_a = L->tile_row0.as<int>();
+        xr.te_a = nullptr;
+        xr.nt_a = n_tiles_ptr(L);
+        xr.tg_b = L->tile_group2.as<int>();
+        xr.tr_b = L->tile_row02.as<int>();
+        xr.te_b = nullptr;
+        xr.nt_b = n_tiles2_ptr(L);
+        xr.group_end = L->group_end.as<int>();
+        xr.row_assign = L->row_assign.as<int>();
+        xr.row_expert = L->row_expert.as<int>();
+        xr.row_sqx = L->tok_sqx.as<Scale>();
+        if (int r = run_experts(L, xr, st)) return r;
+        MARK(L, st);
+        mk::CombineArgs ca;
+        ca.acc_d = L->acc_d.as<int64_t>();
+        ca.ymax_d = L->rowmax_d.as<unsigned long long>();
+        ca.row_cd = L->row_cd.as<Scale>();
+        ca.slot_row = L->slot_row.as<int>();
+        ca.top_ec = L->top_ec.as<int64_t>();
+        ca.sumc = L->sumc.as<int64_t>();
+        ca.T = (int)T;
+        ca.top_k = (int)K;
+        ca.dim = (int)d;
+        ca.out = L->tok_out.as<int32_t>();
+        ca.out_scale = L->tok_scale.as<Scale>();
+        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        CKL(ctx);
+        MARK(L, st);
+    } else {
+        if (int r = ep_routed(L, T, st)) return r;
+        T_total = L->ep_tok_total;
+        tok_offset = L->ep_tok_offset;
+    }
+
+    // merge (layers.rs:1001-1019): one common scale and one gmax over all the layer's tokens, on every rank
     int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
     Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
-    if (T == 1) {
-        mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
-                                                                      (int)d, routed, routed_scale);
-        CKL(ctx);
+    if (T_total == 1) {
+        if (T == 1) {
+            mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(
+                L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)d, routed, routed_scale);
+            CKL(ctx);
+        }
     } else {
-        mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON), nullptr);
-        CKL(ctx);
-        mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)T,
-                                                        (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX));
-        CKL(ctx);
-        mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)T,
-                                                          (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX),
-                                                          routed, routed_scale);
-        CKL(ctx);
+        if (L->world == 1) {
+            mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON),
+                                                        nullptr);
+            CKL(ctx);
+        } else {
+            CK(L->ep_rec.ensure(3 * 8));
+            CK(L->ep_recs.ensure(L->world * 3 * 8));
+            CK(L->ep_best_idx.ensure(4));
+            if (T > 0) {
+                mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
+                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>());
+                CKL(ctx);
+                mk::scale_record_kernel<<<1, 1, 0, st>>>(scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
+                                                         L->ep_rec.as<int64_t>());
+                CKL(ctx);
+            } else {
+                const int64_t none[3] = {0, 0, -1};
+                CK(cudaMemcpyAsync(L->ep_rec.p, none, sizeof(none), cudaMemcpyHostToDevice, st));
+            }
+            NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
+            mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, scal_scale(L, SL_COMMON));
+            CKL(ctx);
+        }
+        if (T > 0) {
+            mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                                                            (int)T, (int)d, scal_scale(L, SL_COMMON),
+                                                            scal_u64(L, U_MERGE_GMAX));
+            CKL(ctx);
+        }
+        if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st)) return r;
+        if (T > 0) {
+            mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                                                              (int)T, (int)d, scal_scale(L, SL_COMMON),
+                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale);
+            CKL(ctx);
+        }
     }
     MARK(L, st);
     if (fs == 0) return KTMOE_OK;
 
     // shared expert on the whole tensor (global maxima), then add(routed, shared)
     const int64_t n = T * d;
-    const unsigned red_blocks = (unsigned)std::min<int64_t>(1184, (n + 255) / 256);
-    mk::absmax_i32_kernel<<<red_blocks, 256, 0, st>>>(x_dev, n, scal_u64(L, U_GXMAX));
-    CKL(ctx);
+    const unsigned red_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
+    if (T > 0) {
+        mk::absmax_i32_kernel<<<red_blocks, 256, 0, st>>>(x_dev, n, scal_u64(L, U_GXMAX));
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_GXMAX), 1, st)) return r;
     sqx_kernel<<<1, 1, 0, st>>>(scal_u64(L, U_GXMAX), xs_dev, scal_scale(L, SL_GSQX));
     CKL(ctx);
-    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
-                                                        L->xs_planes.as<int8_t>(), nullptr, nullptr, xs_dev,
-                                                        scal_u64(L, U_GXMAX));
-    CKL(ctx);
     GemmCall s;
-    s.A = L->w_sgu;
-    s.M_valid = 2 * fs;
-    s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
-    s.out = L->acc_sgu.as<int64_t>();
-    s.ld_out = 2 * fs;
-    s.BN = pick_bn((double)T);
-    s.grid_y = (T + s.BN - 1) / s.BN;
-    s.single_rows = T;
-    s.rowmax = scal_u64(L, U_SYG);  // [U_SYG] gate, [U_SYU] up: maxima over the whole tensor
-    s.rowmax_stride = 0;
-    s.rowmax_split = fs;
-    r = run_gemm(ctx, st, s);
-    if (r) return r;
+    if (T > 0) {
+        mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
+                                                            L->xs_planes.as<int8_t>(), nullptr, nullptr, xs_dev,
+                                                            scal_u64(L, U_GXMAX));
+        CKL(ctx);
+        s.A = L->w_sgu;
+        s.M_valid = 2 * fs;
+        s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
+        s.out = L->acc_sgu.as<int64_t>();
+        s.ld_out = 2 * fs;
+        s.BN = pick_bn((double)T);
+        s.grid_y = (T + s.BN - 1) / s.BN;
+        s.single_rows = T;
+        s.rowmax = scal_u64(L, U_SYG);  // [U_SYG] gate, [U_SYU] up: maxima over the whole tensor
+        s.rowmax_stride = 0;
+        s.rowmax_split = fs;
+        if (int r = run_gemm(ctx, st, s)) return r;
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_SYG), 2, st)) return r;
     mk::SwigluArgs sh;
     std::memset(&sh, 0, sizeof(sh));
     sh.acc = L->acc_sgu.as<int64_t>();
@@ -651,9 +977,9 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sh.R_pad = T_pad;
     sh.top_k = 1;
     sh.g_sqx = scal_scale(L, SL_GSQX);
-    sh.wscale_g = L->b_wsc.as<Scale>() + 3 * E;
-    sh.wscale_u = L->b_wsc.as<Scale>() + 3 * E + 1;
-    sh.wscale_d = L->b_wsc.as<Scale>() + 3 * E + 2;
+    sh.wscale_g = L->b_wsc.as<Scale>() + 3 * L->E_local;
+    sh.wscale_u = L->b_wsc.as<Scale>() + 3 * L->E_local + 1;
+    sh.wscale_d = L->b_wsc.as<Scale>() + 3 * L->E_local + 2;
     sh.silu = lut(L, 1);
     sh.silu_code_scale = S(L->tabs[1].code_scale);
     sh.silu_code_scale_recip = L->silu_code_scale_recip;
@@ -663,21 +989,27 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sh.ymax_stride = 0;
     sh.g_hmax = scal_u64(L, U_SHMAX);
     sh.phase = 1;
-    mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
-    CKL(ctx);
+    if (T > 0) {
+        mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_SHMAX), 1, st)) return r;
     sh.phase = 2;
-    mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
-    CKL(ctx);
-    s.A = L->w_sdn;
-    s.M_valid = d;
-    s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
-    s.out = L->acc_sd.as<int64_t>();
-    s.ld_out = d;
-    s.rowmax = scal_u64(L, U_SYD);
-    s.rowmax_stride = 0;
-    s.rowmax_split = INT32_MAX;
-    r = run_gemm(ctx, st, s);
-    if (r) return r;
+    if (T > 0) {
+        mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
+        CKL(ctx);
+        s.A = L->w_sdn;
+        s.M_valid = d;
+        s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
+        s.out = L->acc_sd.as<int64_t>();
+        s.ld_out = d;
+        s.rowmax = scal_u64(L, U_SYD);
+        s.rowmax_stride = 0;
+        s.rowmax_split = INT32_MAX;
+        if (int r = run_gemm(ctx, st, s)) return r;
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_SYD), 1, st)) return r;
+    // a rank without tokens still needs the shared down c for nothing: only ranks with rows produce output
     mk::AddArgs aa;
     aa.a = routed;
     aa.a_scale = routed_scale;
@@ -689,12 +1021,17 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     aa.scratch = scal_scale(L, SL_ADD);
     aa.y = y_dev;
     aa.y_scale = ys_dev;
-    mk::add_prepare_kernel<<<1, 1, 0, st>>>(aa);
-    CKL(ctx);
-    mk::add_max_kernel<<<red_blocks, 256, 0, st>>>(aa);
-    CKL(ctx);
-    mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
-    CKL(ctx);
+    if (T > 0) {
+        mk::add_prepare_kernel<<<1, 1, 0, st>>>(aa);
+        CKL(ctx);
+        mk::add_max_kernel<<<red_blocks, 256, 0, st>>>(aa);
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st)) return r;
+    if (T > 0) {
+        mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
+        CKL(ctx);
+    }
     MARK(L, st);
     return KTMOE_OK;
 }
@@ -948,9 +1285,12 @@ int ktmoe_linear_weights(ktmoe_ctx* ctx, uint64_t weight_id, const int32_t* x, c
     return linear_impl(ctx, &weight_id, x, w, rows, out, k, y);
 }
 
-int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_layer** out) {
+static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank, int world, const void* nccl_id,
+                        ktmoe_layer** out) {
     if (!ctx || !cfg || !out) return KTMOE_ERR_ARG;
     *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world || (world > 1 && !nccl_id)) return fail(ctx, KTMOE_ERR_ARG, "rank/world");
+    if (cfg->n_experts < world) return fail(ctx, KTMOE_ERR_ARG, "fewer experts than ranks");
     const ktmoe_layer_config c = *cfg;
     if (c.d_model <= 0 || c.n_experts <= 0 || c.d_ff <= 0 || c.top_k <= 0 || c.shared_d_ff < 0)
         return fail(ctx, KTMOE_ERR_ARG, "layer dimensions must be positive");
@@ -972,20 +1312,25 @@ int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_laye
     L->d_pad = round_up(L->d, dg::BK);
     L->f_pad = round_up(L->f, dg::BK);
     L->fs_pad = round_up(std::max<int64_t>(L->fs, 1), dg::BK);
-    L->expert_set.assign(L->E, 0);
+    L->rank = rank;
+    L->world = world;
+    L->e_begin = (int64_t)rank * L->E / world;
+    L->e_end = (int64_t)(rank + 1) * L->E / world;
+    L->E_local = L->e_end - L->e_begin;
+    L->expert_set.assign(L->E_local, 0);
     int r = KTMOE_OK;
     auto bail = [&](int code) {
         delete L;
         return code;
     };
     if ((r = alloc_planes(ctx, L->b_router, L->w_router, 1, L->E, L->d))) return bail(r);
-    if ((r = alloc_planes(ctx, L->b_gu, L->w_gu, L->E, 2 * L->f, L->d))) return bail(r);
-    if ((r = alloc_planes(ctx, L->b_dn, L->w_dn, L->E, L->d, L->f))) return bail(r);
+    if ((r = alloc_planes(ctx, L->b_gu, L->w_gu, L->E_local, 2 * L->f, L->d))) return bail(r);
+    if ((r = alloc_planes(ctx, L->b_dn, L->w_dn, L->E_local, L->d, L->f))) return bail(r);
     if (L->fs > 0) {
         if ((r = alloc_planes(ctx, L->b_sgu, L->w_sgu, 1, 2 * L->fs, L->d))) return bail(r);
         if ((r = alloc_planes(ctx, L->b_sdn, L->w_sdn, 1, L->d, L->fs))) return bail(r);
     }
-    L->h_wsc.assign(3 * L->E + 3, Scale{0, 0});
+    L->h_wsc.assign(3 * L->E_local + 3, Scale{0, 0});
     if (L->b_wsc.ensure(L->h_wsc.size() * sizeof(Scale)) != cudaSuccess) return bail(fail(ctx, KTMOE_ERR_CUDA, "scales"));
     for (int kind = 0; kind < 3; ++kind) hp::build_table(kind, &L->tabs[kind]);
     L->silu_code_scale_recip = kt::scale_recip(S(L->tabs[1].code_scale));
@@ -1013,8 +1358,44 @@ int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_laye
         if (cudaFuncSetAttribute(mk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
             cudaSuccess)
             return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
+        if (cudaFuncSetAttribute(mk::combine_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
+            cudaSuccess)
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
+    }
+    if (world > 1) {
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        ncclResult_t nr = ncclCommInitRank(&L->comm, world, id, rank);
+        if (nr != ncclSuccess) {
+            L->comm = nullptr;
+            return bail(fail(ctx, KTMOE_ERR_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(nr)));
+        }
     }
     *out = L;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, ktmoe_layer** out) {
+    return layer_create(ctx, cfg, 0, 1, nullptr, out);
+}
+
+int ktmoe_ep_unique_id(void* id, int64_t bytes) {
+    if (!id || bytes < (int64_t)sizeof(ncclUniqueId)) return KTMOE_ERR_ARG;
+    ncclUniqueId u;
+    if (ncclGetUniqueId(&u) != ncclSuccess) return KTMOE_ERR_CUDA;
+    std::memcpy(id, &u, sizeof(u));
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_create_ep(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int32_t rank, int32_t world,
+                          const void* nccl_id, ktmoe_layer** out) {
+    return layer_create(ctx, cfg, rank, world, nccl_id, out);
+}
+
+int ktmoe_layer_experts(const ktmoe_layer* L, int32_t* begin, int32_t* end) {
+    if (!L || !begin || !end) return KTMOE_ERR_ARG;
+    *begin = (int32_t)L->e_begin;
+    *end = (int32_t)L->e_end;
     return KTMOE_OK;
 }
 
@@ -1032,6 +1413,11 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                       &L->row_cd, &L->acc_d, &L->rowmax_gu, &L->rowmax_d, &L->tok_out, &L->tok_scale, &L->y_routed, &L->xs_planes, &L->acc_sgu,
                       &L->hs_planes, &L->acc_sd};
     for (DevBuf* b : bufs) b->release();
+    DevBuf* ep_bufs[] = {&L->ep_counts, &L->ep_counts_all, &L->ep_meta_send, &L->ep_meta_recv, &L->ep_recv_planes,
+                         &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,
+                         &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
+    for (DevBuf* b : ep_bufs) b->release();
+    if (L->comm) ncclCommDestroy(L->comm);
     delete L;
     return KTMOE_OK;
 }
@@ -1075,18 +1461,19 @@ int ktmoe_layer_set_sigmoid_bias(ktmoe_layer* L, const int64_t* bias_codes) {
 
 int ktmoe_layer_set_expert(ktmoe_layer* L, int32_t e, const int32_t* gate, ktmoe_scale gate_scale, const int32_t* up,
                            ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale) {
-    if (!L || !gate || !up || !down || e < 0 || e >= L->E) return KTMOE_ERR_ARG;
+    if (!L || !gate || !up || !down || e < L->e_begin || e >= L->e_end) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     std::lock_guard<std::mutex> lk(ctx->mu);
     if (int r = set_device(ctx)) return r;
-    if (int r = upload_matrix(ctx, L->w_gu, e, gate, L->f, L->d, 0)) return r;
-    if (int r = upload_matrix(ctx, L->w_gu, e, up, L->f, L->d, L->f)) return r;
-    if (int r = upload_matrix(ctx, L->w_dn, e, down, L->d, L->f, 0)) return r;
-    L->h_wsc[e] = S(gate_scale);
-    L->h_wsc[L->E + e] = S(up_scale);
-    L->h_wsc[2 * L->E + e] = S(down_scale);
+    const int64_t le = e - L->e_begin;  // this rank's experts are stored from 0
+    if (int r = upload_matrix(ctx, L->w_gu, le, gate, L->f, L->d, 0)) return r;
+    if (int r = upload_matrix(ctx, L->w_gu, le, up, L->f, L->d, L->f)) return r;
+    if (int r = upload_matrix(ctx, L->w_dn, le, down, L->d, L->f, 0)) return r;
+    L->h_wsc[le] = S(gate_scale);
+    L->h_wsc[L->E_local + le] = S(up_scale);
+    L->h_wsc[2 * L->E_local + le] = S(down_scale);
     if (int r = push_scales(L)) return r;
-    L->expert_set[e] = 1;
+    L->expert_set[le] = 1;
     return KTMOE_OK;
 }
 
@@ -1100,9 +1487,9 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
     if (int r = upload_matrix(ctx, L->w_sgu, 0, gate, L->fs, L->d, 0)) return r;
     if (int r = upload_matrix(ctx, L->w_sgu, 0, up, L->fs, L->d, L->fs)) return r;
     if (int r = upload_matrix(ctx, L->w_sdn, 0, down, L->d, L->fs, 0)) return r;
-    L->h_wsc[3 * L->E] = S(gate_scale);
-    L->h_wsc[3 * L->E + 1] = S(up_scale);
-    L->h_wsc[3 * L->E + 2] = S(down_scale);
+    L->h_wsc[3 * L->E_local] = S(gate_scale);
+    L->h_wsc[3 * L->E_local + 1] = S(up_scale);
+    L->h_wsc[3 * L->E_local + 2] = S(down_scale);
     if (int r = push_scales(L)) return r;
     L->shared_set = true;
     return KTMOE_OK;
@@ -1110,7 +1497,8 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
 
 int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
                       int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream) {
-    if (!L || !x_dev || !x_scale_dev || !y_dev || !y_scale_dev || rows <= 0) return KTMOE_ERR_ARG;
+    if (!L || !x_scale_dev || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (rows > 0 && (!x_dev || !y_dev || !y_scale_dev)) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
     std::lock_guard<std::mutex> lk(ctx->mu);
@@ -1122,7 +1510,8 @@ int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const 
 
 int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
                   ktmoe_scale* y_scale) {
-    if (!L || !x || !y || !y_scale || rows <= 0) return KTMOE_ERR_ARG;
+    if (!L || !y_scale || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (rows > 0 && (!x || !y)) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
     std::lock_guard<std::mutex> lk(ctx->mu);
@@ -1131,13 +1520,13 @@ int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_
     cudaStream_t st = ctx->stream;
     const size_t n = (size_t)(rows * L->d);
     Scale xs = S(x_scale);
-    CK(cudaMemcpyAsync(L->x_in.p, x, n * 4, cudaMemcpyHostToDevice, st));
+    if (n) CK(cudaMemcpyAsync(L->x_in.p, x, n * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
     if (int r = stage_forward(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
                               scal_scale(L, SL_YSCALE), st))
         return r;
-    Scale ys;
-    CK(cudaMemcpyAsync(y, L->y_out.p, n * 4, cudaMemcpyDeviceToHost, st));
+    Scale ys{0, 0};
+    if (n) CK(cudaMemcpyAsync(y, L->y_out.p, n * 4, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(&ys, scal_scale(L, SL_YSCALE), sizeof(Scale), cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     if (int r = check_err_word(ctx)) return r;

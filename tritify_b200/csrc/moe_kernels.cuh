@@ -820,6 +820,147 @@ __global__ void add_final_kernel(const AddArgs p) {
     if (blockIdx.x == 0 && threadIdx.x == 0) *p.y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common);
 }
 
+// ───────────── expert parallelism: the exchange around the routed experts ─────────────
+// A home rank sends, for every (token, slot) row in expert order, the row's digit planes and its s_qx; the owner of
+// the expert returns the expert's output as the reference's seam returns it (an IntTensor: i32 data + Scale,
+// crates/01-engine/kt-core/src/layers.rs:945-984), and the home combines. combine depends only on (ec, ys, scales), so
+// the placement of the experts cannot change a bit (layers.rs:888-892).
+
+// meta[pos] = s_qx of the token of expert-sorted row pos (as {mant, shift} int64 pairs).
+__global__ void pack_meta_kernel(const int* __restrict__ row_assign, int top_k, const Scale* __restrict__ tok_sqx,
+                                 int n_rows, int64_t* __restrict__ meta) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n_rows) return;
+    const Scale s = tok_sqx[row_assign[r] / top_k];
+    meta[2 * (long long)r] = s.mant;
+    meta[2 * (long long)r + 1] = s.shift;
+}
+
+__global__ void meta_to_scale_kernel(const int64_t* __restrict__ meta, int n_rows, Scale* __restrict__ out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= n_rows) return;
+    out[r] = Scale{meta[2 * (long long)r], (int32_t)meta[2 * (long long)r + 1]};
+}
+
+// row_expert for received rows: run i covers rows [start[i], start[i] + count[i]) of local expert group[i].
+__global__ void runs_to_rows_kernel(const int* __restrict__ start, const int* __restrict__ count,
+                                    const int* __restrict__ group, int n_runs, int* __restrict__ row_expert) {
+    const int i = blockIdx.x;
+    if (i >= n_runs) return;
+    for (int j = threadIdx.x; j < count[i]; j += blockDim.x) row_expert[start[i] + j] = group[i];
+}
+
+// The expert's output as an IntTensor: y = requant_dyn(acc, L, ymax), scale = from_ratio(ymax, L)·c (layers.rs:321-327).
+__global__ void expert_out_kernel(const int64_t* __restrict__ acc, const unsigned long long* __restrict__ ymax_d,
+                                  const Scale* __restrict__ row_cd, int n_rows, int D, int32_t* __restrict__ y,
+                                  Scale* __restrict__ ys) {
+    const int r = blockIdx.x;
+    if (r >= n_rows) return;
+    const int64_t ymax = (int64_t)ymax_d[r];
+    const Scale cd = row_cd[r];
+    const bool zero = ymax == 0 || cd.mant == 0;
+    const kt::ReqDiv rq = kt::make_req(ymax);
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        y[(long long)r * D + d] = zero ? 0 : kt::requant_row(acc[(long long)r * D + d], rq);
+    if (threadIdx.x == 0) ys[r] = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), cd);
+}
+
+// combine (layers.rs:893-923) from expert outputs given as IntTensors (y rows + scales), row = slot_row[t·K + i].
+struct CombineYArgs {
+    const int32_t* y;
+    const Scale* ys;
+    const int* slot_row;
+    const int64_t* top_ec;
+    const int64_t* sumc;
+    int T, top_k, dim;
+    int32_t* out;
+    Scale* out_scale;
+};
+
+__global__ void combine_y_kernel(const CombineYArgs a) {
+    extern __shared__ int64_t acc_s[];  // [dim]
+    __shared__ uint64_t red[32];
+    __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
+    __shared__ Scale common_s;
+    __shared__ int64_t ec_s[COMBINE_MAX_K];
+    __shared__ int row_s[COMBINE_MAX_K];
+    __shared__ int live_s;
+    const int t = blockIdx.x;
+    if (t >= a.T) return;
+    const int K = a.top_k, D = a.dim;
+    int32_t* o = a.out + (long long)t * D;
+    const int64_t sumc = a.sumc[t];
+    if (sumc <= 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
+        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
+        return;
+    }
+    if (threadIdx.x == 0) {
+        Scale ys[COMBINE_MAX_K];
+        Scale common = kt::scale_zero();
+        for (int i = 0; i < K; ++i) {
+            row_s[i] = a.slot_row[(long long)t * K + i];
+            ec_s[i] = a.top_ec[(long long)t * K + i];
+            ys[i] = a.ys[row_s[i]];
+            if (kt::scale_ge(ys[i], common)) common = ys[i];
+        }
+        common_s = common;
+        int n = 0;
+        if (common.mant != 0) {
+            const Scale cinv = kt::scale_recip(common);
+            for (int i = 0; i < K; ++i) {
+                if (ys[i].mant == 0) continue;
+                f_s[n] = kt::make_apply(kt::scale_mul(ys[i], cinv));
+                row_s[n] = row_s[i];
+                ec_s[n] = ec_s[i];
+                ++n;
+            }
+        }
+        live_s = n;
+    }
+    __syncthreads();
+    const Scale common = common_s;
+    if (common.mant == 0) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
+        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
+        return;
+    }
+    const int n = live_s;
+    uint64_t gm = 0;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        int64_t s = 0;
+        for (int i = 0; i < n; ++i) s += ec_s[i] * kt::apply_row(f_s[i], a.y[(long long)row_s[i] * D + d]);
+        acc_s[d] = s;
+        gm = max(gm, uabs64(s));
+    }
+    gm = block_max_u64(gm, red);
+    const int64_t gmax = (int64_t)gm;
+    const kt::ReqDiv rg = kt::make_req(gmax);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
+    if (threadIdx.x == 0) {
+        a.out_scale[t] = gmax == 0 ? kt::scale_zero()
+                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common),
+                                                   kt::from_ratio(1, (kt::u128)(uint64_t)sumc));
+    }
+}
+
+// This rank's best (common-scale candidate, global token index) as an int64 record {mant, shift, index}.
+__global__ void scale_record_kernel(const Scale* __restrict__ best, const int* __restrict__ best_idx,
+                                    int64_t* __restrict__ rec) {
+    rec[0] = best[0].mant;
+    rec[1] = best[0].shift;
+    rec[2] = *best_idx;
+}
+
+// The common scale over the ranks' records (in rank order; the index decides ties, so the order does not matter).
+__global__ void reduce_records_kernel(const int64_t* __restrict__ recs, int n, Scale* __restrict__ out) {
+    ScaleIdx b{kt::scale_zero(), -1};
+    for (int i = 0; i < n; ++i)
+        b = better(b, ScaleIdx{Scale{recs[3 * i], (int32_t)recs[3 * i + 1]}, (int)recs[3 * i + 2]});
+    out[0] = b.s;
+    out[1] = b.s.mant ? kt::scale_recip(b.s) : kt::scale_zero();
+}
+
 // ───────────── LinearBackend helpers ─────────────
 // Pack int32 codes [rows][K] into three digit planes [3][R_pad][K_pad]; counts codes beyond ±WLEVELS into *bad.
 __global__ void pack_codes_kernel(const int32_t* __restrict__ codes, long long rows, int K, int K_pad, long long R_pad,
