@@ -74,6 +74,17 @@ int ktmoe_linear(ktmoe_ctx* ctx, const int32_t* x, const int32_t* w, int64_t row
  * behind an id must never change. */
 int ktmoe_linear_weights(ktmoe_ctx* ctx, uint64_t weight_id, const int32_t* x, const int32_t* w, int64_t rows,
                          int64_t out, int64_t k, int64_t* y);
+/* The same accumulate for callers that cannot let a library allocate device memory (a runtime that owns one fixed
+ * pool, or runs under a budget where a hidden cudaMalloc/cudaFree would break its accounting). No counterpart in the
+ * reference. x [rows][k], w [out][k] (int32 codes) and y [rows][out] (int64) are DEVICE buffers on `device`; the
+ * call allocates nothing: its scratch is a 64 MiB file-scope device array that every GPU running this entry point
+ * holds until exit; the first call on a device looks up its address and loads this entry point's kernels there
+ * (make that first call before any stream capture). Limit: 256 + 3*ceil64(rows)*ceil128(k) (rounded up to 256) + 3*ceil128(out)*ceil128(k) <= 64 MiB, else
+ * KTMOE_ERR_UNSUPPORTED. Calls on one device share the array and keep the last call's contents; calls whose GPU work
+ * overlaps on one device race, so serialise them. Synchronous: returns when the work on `stream` (NULL: the legacy
+ * default stream) is done. */
+int ktmoe_linear_noalloc(int32_t device, const int32_t* x, const int32_t* w, int64_t rows, int64_t out, int64_t k,
+                         int64_t* y, void* stream);
 /* Resident-weight budget in bytes (LRU eviction; a weight larger than the budget is used once and dropped). */
 int ktmoe_set_weight_budget(ktmoe_ctx* ctx, uint64_t bytes);
 int ktmoe_resident_bytes(ktmoe_ctx* ctx, uint64_t* bytes);

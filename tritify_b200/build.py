@@ -18,7 +18,7 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libktmoe.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-SOURCES_CU = ["ktmoe.cu"]
+SOURCES_CU = ["ktmoe.cu", "noalloc.cu"]
 SOURCES_CPP = ["host_prep.cpp"]
 HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "moe_kernels.cuh", "host_prep.h"]
 
