@@ -398,9 +398,16 @@ def main():
     ap.add_argument("--workload", default="mixtral_prefill", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--tokens", type=int, default=0, help="override the workload's token count (small profiling cases)")
+    ap.add_argument("--experts", type=int, default=0, help="override the workload's expert count (small profiling cases)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    if args.tokens:
+        w["T"] = args.tokens
+    if args.experts:
+        w["E"] = args.experts
+        w["k"] = min(w["k"], args.experts)
     if args.impl == "reference":
         run_reference(args, w, args.workload)
     else:
