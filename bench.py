@@ -345,10 +345,14 @@ def run_ours(args, w, name):
     gu_ms = stage_ms["gemm_gate_up"]
     int8_peak = 2.0 * bf16  # dense int8 : bf16 = 2 : 1 on B200
     achieved = gu_ops / (gu_ms * 1e-3) / 1e12
+    # DRAM bytes per gate/up launch from the committed ncu summary of this workload (null when none is committed)
     traffic = None
-    tpath = os.path.join(ROOT, "profiles", f"traffic_{name}.json")
-    if os.path.exists(tpath):
-        traffic = json.load(open(tpath)).get("gemm_gate_up_dram_bytes_per_launch")
+    tpath = os.path.join(ROOT, "profiles", f"digit_gemm_{name}.md")
+    if os.path.exists(tpath) and not args.tokens and not args.experts and world == 1:
+        import re
+
+        m = re.search(r"gemm_gate_up_dram_bytes_per_launch:\s*(\d+)", open(tpath).read())
+        traffic = int(m.group(1)) if m else None
 
     value = T_all / (ms * 1e-3)
     res = {

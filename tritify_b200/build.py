@@ -30,6 +30,21 @@ def _nvcc() -> str:
     raise RuntimeError("nvcc not found: the CUDA toolkit is required to build libktmoe.so")
 
 
+def _nccl() -> tuple[list[str], list[str]]:
+    """Compile and link flags for NCCL. The library uses the NCCL that PyTorch loads (the nvidia-nccl wheel) when it
+    is installed, so that a process importing both sees one NCCL: with two, whichever loads first provides the
+    symbols and the other library can fail to import. Otherwise the system NCCL."""
+    import importlib.util
+
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec and spec.submodule_search_locations:
+        base = list(spec.submodule_search_locations)[0]
+        lib, inc = os.path.join(base, "lib"), os.path.join(base, "include")
+        if os.path.exists(os.path.join(lib, "libnccl.so.2")) and os.path.exists(os.path.join(inc, "nccl.h")):
+            return ["-I", inc], ["-L", lib, "-l:libnccl.so.2", "-Xlinker", "-rpath," + lib]
+    return [], ["-lnccl"]
+
+
 def _stale(target: str, deps: list[str]) -> bool:
     if not os.path.exists(target):
         return True
@@ -42,6 +57,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     nvcc = _nvcc()
     header_deps = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", "ktmoe.h")]
+    nccl_inc, nccl_link = _nccl()
     objs = []
     for src in SOURCES_CPP:
         s = os.path.join(CSRC, src)
@@ -56,12 +72,12 @@ def build(force: bool = False, verbose: bool = False) -> str:
         objs.append(o)
         if force or _stale(o, [s] + header_deps):
             cmd = [nvcc, *ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-ffp-contract=off",
-                   "-I", os.path.join(ROOT, "include"), "-I", CSRC, "-c", s, "-o", o]
+                   "-I", os.path.join(ROOT, "include"), "-I", CSRC, *nccl_inc, "-c", s, "-o", o]
             if verbose:
                 cmd.insert(1, "-Xptxas=-v")
             _run(cmd, verbose)
     if force or _stale(LIB, objs):
-        _run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lnccl", "-lpthread"], verbose)
+        _run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, *nccl_link, "-lpthread"], verbose)
     return LIB
 
 
