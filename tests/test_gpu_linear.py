@@ -66,6 +66,23 @@ def test_random_shapes_equal_the_cpu_path(ctx, oracle, rows, out, k):
     assert bad.size == 0, f"{bad.size} of {got.size} differ; first at {bad[:5]}: {got[bad[:5]]} vs {want[bad[:5]]}"
 
 
+@pytest.mark.parametrize("rows,out,k", [(333, 1000, 4096), (64, 256, 128), (1024, 768, 3000)])
+def test_pair_and_single_sm_kernels_agree(ctx, oracle, rows, out, k, monkeypatch):
+    """Wide calls run on SM pairs (tcgen05 cta_group::2, 256 weight rows x 64 activation rows per tile); KTMOE_PAIR=0
+    keeps them on single SMs. Both must equal the CPU path."""
+    rng = np.random.default_rng(out + k)
+    x = rng.integers(-WL, WL + 1, size=rows * k, dtype=np.int32)
+    w = rng.integers(-WL, WL + 1, size=out * k, dtype=np.int32)
+    monkeypatch.setenv("KTMOE_PAIR", "1")
+    got_pair = ctx.linear(x, w, rows, out, k)
+    monkeypatch.setenv("KTMOE_PAIR", "0")
+    got_single = ctx.linear(x, w, rows, out, k)
+    want = oracle.linear(x, w, rows, out, k)
+    for got in (got_pair, got_single):
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, f"{bad.size} of {got.size} differ; first at {bad[:5]}"
+
+
 def test_residency_gate(oracle):
     """gate.rs:109-140: the corpus twice, then two weights of one shape interleaved; and with a 1-byte budget."""
     for budget in [None, 1]:

@@ -20,7 +20,7 @@ LIB = os.path.join(PKG, "libktmoe.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES_CU = ["ktmoe.cu", "noalloc.cu"]
 SOURCES_CPP = ["host_prep.cpp"]
-HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "moe_kernels.cuh", "host_prep.h"]
+HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "digit_gemm_pair.cuh", "moe_kernels.cuh", "host_prep.h"]
 
 
 def _nvcc() -> str:

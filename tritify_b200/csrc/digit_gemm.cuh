@@ -111,8 +111,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: false (and the error word set) after ~2 s.
+// Bounded wait of the pipeline: false (and the error word set) after ~2 s, or as soon as another wait of the launch
+// has failed (the error word is set), so that a failed launch ends in about one limit rather than one per tile.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255u) == 0) {
+            if (err && *(volatile int*)err != 0) return false;
+            if (globaltimer() - t0 > 2000000000ull) {
+                if (err) atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+// Bounded wait for work already issued (copies or MMAs in flight) before the block frees what they touch: ~2 s,
+// whatever the error word says.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
@@ -179,6 +197,17 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
 // The tiles of one launch, in raster order. Slot L (0 <= L < m_tiles · group_n · n_groups) is weight tile
 // m = (L mod per_group) / group_n of n-tile (L / per_group) · group_n + L mod group_n: the blocks resident at one time
 // walk group_n activation tiles for each weight tile, so both stay in L2 while they are reused.
@@ -222,7 +251,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;     // [ACC]: the MMAs of a tile completed into buffer b
     uint64_t* acc_empty = acc_full + ACC;    // [ACC]: the epilogue has read buffer b (128 arrivals)
-    uint32_t* tmem_slot = (uint32_t*)(acc_empty + ACC);
+    uint64_t* mma_done = acc_empty + ACC;    // every MMA of the block has completed (waited before TMEM is freed)
+    uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
     unsigned long long* sred = (unsigned long long*)(smem + STAGES * C::STAGE_BYTES + 256);
 
     const int n_tiles = args.n_tiles ? *args.n_tiles : args.n_tiles_max;
@@ -241,6 +271,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&acc_full[b], 1);
             mbar_init(&acc_empty[b], 128);
         }
+        mbar_init(mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -283,7 +314,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             // Let the copies still in flight land before the block can leave (bounded).
             for (int j = max(0, q - STAGES); j < q; ++j)
-                mbar_wait(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, args.err, ERR_TIMEOUT_FULL);
+                mbar_wait_drain(&full[j % STAGES], (uint32_t)(j / STAGES) & 1u, args.err, ERR_TIMEOUT_FULL);
         }
     } else if (warp == 5) {
         if (lane == 0) {
@@ -336,6 +367,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 umma_commit(&acc_full[b]);  // fires when every MMA issued so far has completed
                 ++tc;
             }
+            umma_commit(mma_done);
+            mbar_wait_drain(mma_done, 0u, args.err, ERR_TIMEOUT_ACCUM);
         }
     } else {
         // Epilogue: warp w reads TMEM lanes 32w..32w+31 (its lane quadrant); lane l holds weight row m0+32w+l.

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "digit_gemm.cuh"
+#include "digit_gemm_pair.cuh"
 #include "fixed_point.cuh"
 #include "host_prep.h"
 #include "ktmoe.h"
@@ -93,6 +94,7 @@ struct Resident {
 struct ktmoe_ctx {
     int device = 0;
     int num_sms = 148;
+    int pair_clusters = 0;  // co-resident clusters of the pair GEMM on this device (0: not yet queried)
     cudaStream_t stream = nullptr;
     int* d_err = nullptr;
     std::string last_error = "";
@@ -158,6 +160,46 @@ int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const 
     return KTMOE_OK;
 }
 
+// The pair GEMM (tcgen05 cta_group::2) is used for 64-row tiles of weights padded to 256 rows unless KTMOE_PAIR=0.
+bool pair_enabled() {
+    const char* e = getenv("KTMOE_PAIR");
+    return !(e && e[0] == '0');
+}
+
+int launch_gemm_pair(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, int64_t slots,
+                     const dg::GemmArgs& args) {
+    static bool attr_set[64] = {};
+    if (!attr_set[ctx->device & 63]) {
+        CK(cudaFuncSetAttribute(dg::digit_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                dg::pair::SMEM_BYTES));
+        attr_set[ctx->device & 63] = true;
+    }
+    if (ctx->pair_clusters == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(2 * (ctx->num_sms / 2)));
+        cfg.blockDim = dim3(dg::pair::THREADS);
+        cfg.dynamicSmemBytes = dg::pair::SMEM_BYTES;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, dg::digit_gemm_pair_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = ctx->num_sms / 2;
+        }
+        ctx->pair_clusters = std::min(n, ctx->num_sms / 2);
+    }
+    const int64_t clusters = std::min<int64_t>(slots, ctx->pair_clusters);
+    dg::digit_gemm_pair_kernel<<<dim3((unsigned)(2 * clusters)), dg::pair::THREADS, dg::pair::SMEM_BYTES, st>>>(ma, mb,
+                                                                                                              args);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
 struct GemmCall {
     Planes A;        // weights: groups x 3 x M_pad x k_pad
     int64_t M_valid;
@@ -180,14 +222,15 @@ struct GemmCall {
 // Launch the digit GEMM, splitting K into chunks whose int32 diagonal sums cannot overflow.
 int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (g.grid_y <= 0 || g.M_valid <= 0) return KTMOE_OK;
+    const bool pair = g.BN == dg::pair::BN && g.A.rows_pad % dg::pair::BM2 == 0 && pair_enabled();
     const int64_t group_n = std::min<int64_t>(16, g.grid_y);
-    const int64_t m_tiles = g.A.rows_pad / dg::BM;
+    const int64_t m_tiles = g.A.rows_pad / (pair ? dg::pair::BM2 : dg::BM);
     const int64_t n_groups = (g.grid_y + group_n - 1) / group_n;
     if (m_tiles * group_n * n_groups > INT32_MAX) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "too many tiles for one launch");
     CUtensorMap ma, mb;
     int r = make_map(ctx, &ma, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, dg::BM);
     if (r) return r;
-    r = make_map(ctx, &mb, g.B.ptr, g.B.k_pad, 3 * g.B.rows_pad, g.BN);
+    r = make_map(ctx, &mb, g.B.ptr, g.B.k_pad, 3 * g.B.rows_pad, pair ? dg::pair::BOX_ROWS : g.BN);
     if (r) return r;
     const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
     const int64_t chunk_kb = dg::K_EXACT_MAX / dg::BK;
@@ -217,6 +260,11 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.rowmax = g.rowmax;
         a.rowmax_stride = g.rowmax_stride;
         a.rowmax_split = (int)std::min<int64_t>(g.rowmax_split, INT32_MAX);
+        if (pair) {
+            r = launch_gemm_pair(ctx, st, ma, mb, m_tiles * group_n * n_groups, a);
+            if (r) return r;
+            continue;
+        }
         switch (g.BN) {
             case 16: r = launch_gemm_t<16, 4, 2>(ctx, st, ma, mb, grid, a); break;
             case 32: r = launch_gemm_t<32, 3, 2>(ctx, st, ma, mb, grid, a); break;
@@ -229,15 +277,18 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     return KTMOE_OK;
 }
 
-// Activation rows per tile: 48 keeps two accumulator buffers in TMEM (the epilogue overlaps the next tile's MMAs)
-// while three stacked planes still give one 144-wide MMA per weight plane. KTMOE_BN overrides it (16/32/48/64).
-int pick_bn(double rows_per_group) {
+// Activation rows per tile. With weights padded to 256 rows and at least 64 rows per group, 64-row tiles on the SM
+// pair (each SM reads half of the stacked activation tile). Otherwise, on one SM, 48 keeps two accumulator buffers
+// in TMEM (the epilogue overlaps the next tile's MMAs) while three stacked planes still give one 144-wide MMA per
+// weight plane. KTMOE_BN overrides it (16/32/48/64).
+int pick_bn(double rows_per_group, bool pair_ok = false) {
     static int forced = [] {
         const char* e = getenv("KTMOE_BN");
         int v = e ? atoi(e) : 0;
         return (v == 16 || v == 32 || v == 48 || v == 64) ? v : 0;
     }();
     if (forced) return forced;
+    if (pair_ok && rows_per_group >= 64.0 && pair_enabled()) return 64;
     if (rows_per_group >= 40.0) return 48;
     if (rows_per_group >= 20.0) return 32;
     return 16;
@@ -251,7 +302,7 @@ __global__ void sqx_kernel(const unsigned long long* gxmax, const Scale* x_scale
 
 // The down GEMM's width: a long K (d_ff >= 4096) amortises a single-buffered accumulator, and a 64-row tile reads
 // the least shared memory per MMA; otherwise the same choice as the gate/up GEMM. KTMOE_BN_DOWN overrides it.
-int pick_bn_long_k(double rows_per_group, int64_t k) {
+int pick_bn_long_k(double rows_per_group, int64_t k, bool pair_ok = false) {
     static int forced = [] {
         const char* e = getenv("KTMOE_BN_DOWN");
         int v = e ? atoi(e) : 0;
@@ -259,7 +310,7 @@ int pick_bn_long_k(double rows_per_group, int64_t k) {
     }();
     if (forced) return forced;
     if (k >= 4096 && rows_per_group >= 48.0) return 64;
-    return pick_bn(rows_per_group);
+    return pick_bn(rows_per_group, pair_ok);
 }
 
 int set_device(ktmoe_ctx* ctx) {
@@ -644,7 +695,7 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t d = L->d, E = L->E, K = L->K, R = T * K, G = L->world, rk = L->rank;
     const int64_t R_pad = round_up(std::max<int64_t>(R, 1), 64);
-    const int BN = pick_bn((double)R * G / (double)E), BN2 = pick_bn_long_k((double)R * G / (double)E, L->f);
+    const int BN = pick_bn((double)R * G / (double)E, true), BN2 = pick_bn_long_k((double)R * G / (double)E, L->f, true);
     if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
     // per-row s_qx for the owners, and this rank's per-expert counts (+ its token count) for everyone
     CK(L->ep_meta_send.ensure(std::max<int64_t>(R, 1) * 16));
@@ -842,8 +893,8 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
 
     int64_t T_total = T, tok_offset = 0;
     if (L->world == 1) {
-        const int BN = pick_bn((double)R / (double)E);
-        const int BN2 = pick_bn_long_k((double)R / (double)E, f);
+        const int BN = pick_bn((double)R / (double)E, true);
+        const int BN2 = pick_bn_long_k((double)R / (double)E, f, true);
         if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
         MARK(L, st);
         ExpertRows xr;
@@ -959,7 +1010,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
         s.out = L->acc_sgu.as<int64_t>();
         s.ld_out = 2 * fs;
-        s.BN = pick_bn((double)T);
+        s.BN = pick_bn((double)T, true);
         s.grid_y = (T + s.BN - 1) / s.BN;
         s.single_rows = T;
         s.rowmax = scal_u64(L, U_SYG);  // [U_SYG] gate, [U_SYU] up: maxima over the whole tensor
@@ -1060,7 +1111,7 @@ int upload_matrix(ktmoe_ctx* ctx, const Planes& P, int64_t g, const int32_t* cod
 
 int alloc_planes(ktmoe_ctx* ctx, DevBuf& buf, Planes& P, int64_t groups, int64_t rows_valid, int64_t k) {
     P.groups = groups;
-    P.rows_pad = round_up(rows_valid, dg::BM);
+    P.rows_pad = rows_valid > dg::BM ? round_up(rows_valid, dg::pair::BM2) : dg::BM;  // 256-row pair tiles
     P.k = k;
     P.k_pad = round_up(k, dg::BK);
     CK(buf.ensure((size_t)(groups * 3 * P.rows_pad * P.k_pad)));
@@ -1186,9 +1237,10 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
         return KTMOE_OK;
     }
     const int64_t k_pad = round_up(k, dg::BK);
-    const int BN = pick_bn((double)rows);
+    // weights of more than one 128-row tile are padded to 256 rows, so that wide calls can use the pair GEMM
+    const int64_t out_pad = out > dg::BM ? round_up(out, dg::pair::BM2) : dg::BM;
+    const int BN = pick_bn((double)rows, out_pad % dg::pair::BM2 == 0);
     const int64_t rows_pad = round_up(rows, 64);
-    const int64_t out_pad = round_up(out, dg::BM);
     CK(ctx->lin_bad.ensure(8));
     CK(cudaMemsetAsync(ctx->lin_bad.p, 0, 8, st));
     // weights: resident by id, else packed for this call
