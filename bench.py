@@ -31,6 +31,10 @@ sys.path.insert(0, ROOT)
 WORKLOADS = {
     # BASELINE config 4 (i): Mixtral-8x7B-shaped, uniform router N(0, 0.02), prefill 8192 tokens.
     "mixtral_prefill": dict(d=4096, E=8, f=14336, k=2, T=8192, norm=True, sigmoid=False, shared=0, wseed=1, xseed=0),
+    # BASELINE config 4 (ii): the same layer with a router bias (QuantLinear::with_bias on the router) fitted so that
+    # the top-2 selections follow Zipf(1.2) over the experts; with one expert per GPU the hottest GPU bounds the step.
+    "mixtral_zipf": dict(d=4096, E=8, f=14336, k=2, T=8192, norm=True, sigmoid=False, shared=0, wseed=1, xseed=0,
+                         zipf=1.2),
     # the CPU-parity layer.
     "config1": dict(d=2048, E=64, f=1408, k=8, T=512, norm=False, sigmoid=False, shared=0, wseed=1, xseed=0),
     # Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
@@ -124,6 +128,30 @@ def measured_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+def zipf_router_bias(w, tokens=2048, iters=300):
+    """A router bias (f32, one per expert) under which the top-k selections of the workload's tokens are distributed
+    as Zipf(s) over the experts: expert e is chosen with frequency proportional to (e + 1)^-s. Fitted on the float
+    logits of the first ``tokens`` tokens (x·W_router^T + b, the generator's f32 values in f64 arithmetic) by repeated
+    corrections b_e += log(target_e / observed_e); deterministic. The integer path routes on the quantised codes, so
+    its frequencies follow the target closely but not exactly; the bench reports the observed load."""
+    import tritify_b200 as tb
+
+    d, E, k, s = w["d"], w["E"], w["k"], w["zipf"]
+    n = min(tokens, w["T"])
+    x = tb.synth_normal(w["xseed"], 1.0, n * d).reshape(n, d).astype(np.float64)
+    wr = tb.synth_normal(w["wseed"], 0.02, E * d).reshape(E, d).astype(np.float64)
+    logits = x @ wr.T
+    target = np.arange(1, E + 1, dtype=np.float64) ** -s
+    target /= target.sum()
+    b = np.zeros(E)
+    for _ in range(iters):
+        top = np.argsort(-(logits + b), axis=1, kind="stable")[:, :k]
+        freq = np.bincount(top.reshape(-1), minlength=E) / float(top.size)
+        b += 0.5 * (np.log(target) - np.log(np.maximum(freq, 0.5 / top.size)))
+        b -= b.mean()
+    return b.astype(np.float32)
+
+
 def build_product_layer(w, ctx, ep=None):
     """Quantise the workload's weights with the product's host quantiser (QuantLinear::from_weights) and make them
     resident on the device, one matrix at a time (the Mixtral layer is 1.4 G weights). With ``ep = (rank, world,
@@ -141,7 +169,10 @@ def build_product_layer(w, ctx, ep=None):
 
     # one stream (seed wseed): router [E,d], then expert e's gate [f,d], up [f,d], down [d,f], then the shared expert
     router = q(0, E, d)
-    dev.set_router(router[0], router[1], None)
+    rbias = None
+    if w.get("zipf"):
+        rbias = tb.QuantLinear("router", router[0], router[1], E, d).with_bias(zipf_router_bias(w)).bias
+    dev.set_router(router[0], router[1], rbias)
     base = E * d
     for e in dev.experts:
         o = base + e * 3 * f * d
@@ -174,7 +205,8 @@ def build_oracle_layer(w, O):
     experts = take(E * 3 * f * d)
     shared = take(3 * fs * d) if fs else None
     sbias = tb.synth_normal(w["wseed"] + 2, 0.02, E) if w["sigmoid"] else None
-    return O.MoeOracle(d, E, f, w["k"], router, experts, norm_topk=w["norm"], sigmoid_bias=sbias,
+    rbias = zipf_router_bias(w) if w.get("zipf") else None
+    return O.MoeOracle(d, E, f, w["k"], router, experts, router_bias=rbias, norm_topk=w["norm"], sigmoid_bias=sbias,
                        shared_hidden=fs, shared_w=shared)
 
 
@@ -281,6 +313,15 @@ def run_ours(args, w, name):
     y_ref, ys_ref = dev.forward(x.data, T, x.scale)
     ok_exact = bool((yd.cpu().numpy() == y_ref).all()) and int(ys_d[0]) == ys_ref.mant
 
+    # per-expert load of this routing (rows each expert receives), summed over the ranks
+    ex, _, _ = dev.route(x.data, T, x.scale)
+    load = np.bincount(ex.reshape(-1), minlength=w["E"]).astype(np.int64)
+    if dist is not None:
+        lt = torch.from_numpy(load).cuda()
+        dist.all_reduce(lt)
+        load = lt.cpu().numpy()
+    per_gpu = [int(load[r * w["E"] // world:(r + 1) * w["E"] // world].sum()) for r in range(world)]
+
     # device-timed region: inputs resident in HBM; the 4.2 GB of weight planes exceed the 126 MB L2, so every step
     # streams them from HBM (no separate flush)
     dev.set_timing(True)
@@ -360,6 +401,7 @@ def run_ours(args, w, name):
         "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
         "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
+                   "router_bias": f"zipf({w['zipf']})" if w.get("zipf") else None,
                    "parallelism": f"ep{world}", "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
                    "bit_exact_vs_host_api": ok_exact},
         "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
@@ -370,6 +412,8 @@ def run_ours(args, w, name):
                      "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
                      "ops_per_launch": gu_ops, "plane_products": P_PLANES},
         "stage_ms": stage_ms,
+        "expert_load": {"rows_per_expert": [int(v) for v in load], "rows_per_gpu": per_gpu,
+                        "hottest_gpu_over_mean": max(per_gpu) / (sum(per_gpu) / world)},
         "gemm_down_tops": dn_ops / (stage_ms["gemm_down"] * 1e-3) / 1e12,
         "clocks": clk.summary(),
     }

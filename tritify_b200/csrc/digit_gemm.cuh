@@ -446,13 +446,33 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             if (do_max) {
                 asm volatile("bar.sync 1, 128;" ::: "memory");
-                for (int i = threadIdx.x; i < 2 * BN; i += 128) {
-                    const int sl = i / BN, n = i % BN;
-                    unsigned long long v = 0;
+                if (args.rowmax_stride == 0) {
+                    // one word per slot for the whole output: reduce the tile's columns first (one atomic per warp)
+                    unsigned long long v[2] = {0ull, 0ull};
+                    for (int i = threadIdx.x; i < 2 * BN; i += 128) {
+                        const int sl = i / BN, n = i % BN;
+                        if (n >= ti.n_valid) continue;
 #pragma unroll
-                    for (int w = 0; w < 4; ++w) v = max(v, sred[(sl * 4 + w) * BN + n]);
-                    if (v && n < ti.n_valid)
-                        atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, v);
+                        for (int w = 0; w < 4; ++w) v[sl] = max(v[sl], sred[(sl * 4 + w) * BN + n]);
+                    }
+#pragma unroll
+                    for (int sl = 0; sl < 2; ++sl) {
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const unsigned long long w = __shfl_xor_sync(0xffffffffu, v[sl], o);
+                            v[sl] = w > v[sl] ? w : v[sl];
+                        }
+                        if (lane == 0 && v[sl]) atomicMax(args.rowmax + sl, v[sl]);
+                    }
+                } else {
+                    for (int i = threadIdx.x; i < 2 * BN; i += 128) {
+                        const int sl = i / BN, n = i % BN;
+                        unsigned long long v = 0;
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v = max(v, sred[(sl * 4 + w) * BN + n]);
+                        if (v && n < ti.n_valid)
+                            atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, v);
+                    }
                 }
                 asm volatile("bar.sync 1, 128;" ::: "memory");  // sred is reused by the next tile
             }

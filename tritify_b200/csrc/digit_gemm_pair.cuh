@@ -372,19 +372,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
             if (do_max) {
                 const int n = chalf * 32 + lane;  // the column whose maximum this lane ends up holding
                 const bool one_slot = __all_sync(0xffffffffu, my_slot == __shfl_sync(0xffffffffu, my_slot, 0));
-                if (one_slot) {
-                    const unsigned long long mx = lane_max_transpose(av, lane);
-                    if (mx && n < ti.n_valid)
-                        atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + my_slot, mx);
-                } else {
 #pragma unroll 1
-                    for (int sl = 0; sl < 2; ++sl) {
-                        unsigned long long bv[32];
+                for (int sl = 0; sl < 2; ++sl) {
+                    if (one_slot && sl != my_slot) continue;
+                    unsigned long long bv[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) bv[j] = my_slot == sl ? av[j] : 0ull;
-                        const unsigned long long mx = lane_max_transpose(bv, lane);
-                        if (mx && n < ti.n_valid)
-                            atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, mx);
+                    for (int j = 0; j < 32; ++j) bv[j] = my_slot == sl ? av[j] : 0ull;
+                    unsigned long long mx = lane_max_transpose(bv, lane);
+                    if (n >= ti.n_valid) mx = 0;
+                    if (args.rowmax_stride == 0) {
+                        // one word for the whole output: reduce the warp's columns first (one atomic per warp)
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const unsigned long long w = __shfl_xor_sync(0xffffffffu, mx, o);
+                            mx = w > mx ? w : mx;
+                        }
+                        if (lane == 0 && mx) atomicMax(args.rowmax + sl, mx);
+                    } else if (mx) {
+                        atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, mx);
                     }
                 }
             }

@@ -366,6 +366,8 @@ struct ktmoe_layer {
     DevBuf counts, chunk_off, expert_off, group_end, expert_count, tile_group, tile_row0, tile_group2, tile_row02,
         slot_row, row_assign, row_expert;
     DevBuf xg_planes, acc_gu, hq_planes, row_cd, acc_d, tok_out, tok_scale, y_routed, rowmax_gu, rowmax_d;
+    DevBuf swiglu_plans, row_hmax, shared_plan;  // per-row SwiGLU scale plans and max |h|; the shared expert's plan
+    DevBuf cp_n, cp_common, cp_row, cp_ec, cp_ry, cp_f;  // per-token combine plans
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
     // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
     bool timing = false;
@@ -405,6 +407,8 @@ int ensure_rows(ktmoe_layer* L, int64_t rows) {
     CK(L->acc_d.ensure(n * L->d * 8));
     CK(L->rowmax_gu.ensure(n * 2 * 8));
     CK(L->rowmax_d.ensure(n * 8));
+    CK(L->swiglu_plans.ensure(n * sizeof(mk::SwigluScales)));
+    CK(L->row_hmax.ensure(n * 8));
     return KTMOE_OK;
 }
 
@@ -428,6 +432,12 @@ int ensure_scratch(ktmoe_layer* L, int64_t T) {
     CK(L->logit_scale.ensure(T * sizeof(Scale)));
     CK(L->top_e.ensure(R * 4));
     CK(L->top_ec.ensure(R * 8));
+    CK(L->cp_n.ensure(T * 4));
+    CK(L->cp_common.ensure(T * sizeof(Scale)));
+    CK(L->cp_row.ensure(R * 4));
+    CK(L->cp_ec.ensure(R * 8));
+    CK(L->cp_ry.ensure(R * sizeof(kt::ReqDiv)));
+    CK(L->cp_f.ensure(R * sizeof(kt::ApplyPlan)));
     CK(L->sumc.ensure(T * 8));
     CK(L->counts.ensure(std::max<int64_t>(nchunks, 1) * E * 4));
     CK(L->chunk_off.ensure(std::max<int64_t>(nchunks, 1) * E * 4));
@@ -651,7 +661,11 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     sa.row_cd = L->row_cd.as<Scale>();
     sa.ymax = L->rowmax_gu.as<unsigned long long>();
     sa.ymax_stride = 2;
+    sa.plans = L->swiglu_plans.as<mk::SwigluScales>();
+    sa.row_hmax = L->row_hmax.as<unsigned long long>();
     sa.phase = 0;
+    mk::swiglu_plan_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
+    CKL(ctx);
     {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
         const size_t sm = h_smem ? (size_t)L->swiglu_smem : 0;
@@ -668,6 +682,8 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
             mk::swiglu_rows_kernel<2><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
         CKL(ctx);
     }
+    mk::down_c_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
+    CKL(ctx);
     MARK(L, st);
 
     g.A = L->w_dn;
@@ -930,7 +946,18 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         ca.dim = (int)d;
         ca.out = L->tok_out.as<int32_t>();
         ca.out_scale = L->tok_scale.as<Scale>();
-        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
+                                 L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
+        mk::combine_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
+        CKL(ctx);
+        if (L->K <= 2)
+            mk::combine_kernel<2><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+        else if (L->K <= 4)
+            mk::combine_kernel<4><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+        else if (L->K <= 8)
+            mk::combine_kernel<8><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+        else
+            mk::combine_kernel<16><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
         CKL(ctx);
         MARK(L, st);
     } else {
@@ -1039,7 +1066,11 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     sh.ymax = scal_u64(L, U_SYG);
     sh.ymax_stride = 0;
     sh.g_hmax = scal_u64(L, U_SHMAX);
+    CK(L->shared_plan.ensure(sizeof(mk::SwigluScales)));
+    sh.plans = L->shared_plan.as<mk::SwigluScales>();
     sh.phase = 1;
+    mk::swiglu_plan_kernel<<<1, 32, 0, st>>>(sh);
+    CKL(ctx);
     if (T > 0) {
         mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
         CKL(ctx);
@@ -1407,8 +1438,11 @@ static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank,
             return bail(fail(ctx, KTMOE_ERR_CUDA, "SwiGLU shared memory"));
     }
     if ((size_t)L->d * 8 > 48 * 1024) {
-        if (cudaFuncSetAttribute(mk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
-            cudaSuccess)
+        const int cs = (int)(L->d * 8);
+        if (cudaFuncSetAttribute(mk::combine_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
+            cudaFuncSetAttribute(mk::combine_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
+            cudaFuncSetAttribute(mk::combine_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
+            cudaFuncSetAttribute(mk::combine_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess)
             return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
         if (cudaFuncSetAttribute(mk::combine_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
             cudaSuccess)
@@ -1463,7 +1497,8 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                       &L->chunk_off, &L->expert_off, &L->group_end, &L->expert_count, &L->tile_group, &L->tile_row0, &L->tile_group2, &L->tile_row02,
                       &L->slot_row, &L->row_assign, &L->row_expert, &L->xg_planes, &L->acc_gu, &L->hq_planes,
                       &L->row_cd, &L->acc_d, &L->rowmax_gu, &L->rowmax_d, &L->tok_out, &L->tok_scale, &L->y_routed, &L->xs_planes, &L->acc_sgu,
-                      &L->hs_planes, &L->acc_sd};
+                      &L->hs_planes, &L->acc_sd, &L->swiglu_plans, &L->row_hmax, &L->shared_plan,
+                      &L->cp_n, &L->cp_common, &L->cp_row, &L->cp_ec, &L->cp_ry, &L->cp_f};
     for (DevBuf* b : bufs) b->release();
     DevBuf* ep_bufs[] = {&L->ep_counts, &L->ep_counts_all, &L->ep_meta_send, &L->ep_meta_recv, &L->ep_recv_planes,
                          &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,

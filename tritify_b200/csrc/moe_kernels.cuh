@@ -423,6 +423,15 @@ __global__ void permute_planes_kernel(const int8_t* __restrict__ src, long long 
 }
 
 // ───────────── SwiGLU + requant + down-input quantisation for routed rows (layers.rs:609-640, :279-298) ─────────────
+// The SwiGLU scales of one row (or of the whole tensor): g and u output scales, SiLU index scale, identity factor,
+// as per-row plans for the element loop.
+struct SwigluScales {
+    Scale gs, us;
+    int64_t mg, mu;  // requant divisors (0: that output is all zero)
+    kt::ReqDiv rg, ru;
+    kt::ApplyPlan is, idf;
+};
+
 struct SwigluArgs {
     int64_t* acc;  // [rows][2f]: gate in [0, f), up in [f, 2f); in the tensor-global mode the gate half holds h
     int rows, f, f_pad;
@@ -442,17 +451,10 @@ struct SwigluArgs {
     // |max| of the gate and up accumulators: per row ([rows][2], from the GEMM epilogue) or global ([2])
     const unsigned long long* ymax;
     int ymax_stride;  // 2 per row, 0 global
+    SwigluScales* plans;         // per row ([rows]) or one for the tensor-global mode, from swiglu_plan_kernel
+    unsigned long long* row_hmax;  // routed: max |h| per row, for down_c_kernel
     unsigned long long* g_hmax;  // tensor-global mode: phase 1 reduces max |h| here, phase 2 reads it
-    int phase;  // 0: per-row (routed, one kernel, h in shared memory); 1: global h pass; 2: global quantise pass
-};
-
-// The SwiGLU scales of one row (or of the whole tensor): g and u output scales, SiLU index scale, identity factor,
-// as per-row plans for the element loop.
-struct SwigluScales {
-    Scale gs, us;
-    int64_t mg, mu;  // requant divisors (0: that output is all zero)
-    kt::ReqDiv rg, ru;
-    kt::ApplyPlan is, idf;
+    int phase;  // 0: per-row (routed, one kernel); 1: global h pass; 2: global quantise pass
 };
 
 __device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t, int e, int64_t gmax_g, int64_t gmax_u) {
@@ -470,6 +472,21 @@ __device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t
     q.rg = kt::make_req(q.mg);
     q.ru = kt::make_req(q.mu);
     return q;
+}
+
+// The per-row scale plans, one thread per row (one thread in the tensor-global mode), so that the element kernels
+// start without a serial prologue.
+__global__ void swiglu_plan_kernel(const SwigluArgs a) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (a.ymax_stride == 0) {
+        if (r == 0) a.plans[0] = swiglu_scales(a, 0, 0, (int64_t)a.ymax[0], (int64_t)a.ymax[1]);
+        return;
+    }
+    if (r >= a.rows) return;
+    const int e = a.row_expert ? a.row_expert[r] : 0;
+    const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
+    a.plans[r] = swiglu_scales(a, t, e, (int64_t)a.ymax[(long long)r * a.ymax_stride],
+                               (int64_t)a.ymax[(long long)r * a.ymax_stride + 1]);
 }
 
 // h = silu_code(g) · u for one element (layers.rs:618-629).
@@ -497,6 +514,14 @@ __device__ __forceinline__ Scale down_c(const SwigluArgs& a, Scale us, int64_t h
     return kt::scale_mul(s_qh, a.wscale_d[e]);
 }
 
+// Per routed row: the down linear's c from the row's plan and max |h|, one thread per row.
+__global__ void down_c_kernel(const SwigluArgs a) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= a.rows) return;
+    const int e = a.row_expert ? a.row_expert[r] : 0;
+    a.row_cd[r] = down_c(a, a.plans[r].us, (int64_t)a.row_hmax[r], e);
+}
+
 // hint = requant_dyn(h, L, hmax) has max |.| = L exactly, so the down linear's quant_to divides by 2^28.
 __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, const int64_t* h, int64_t hmax) {
     int8_t* p0 = a.planes + (long long)r * a.f_pad;
@@ -515,23 +540,17 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
 }
 
 // Phase 0: one block per routed row; h stays in shared memory (dynamic, f int64) when `h_smem`. U independent
-// elements per thread per step.
+// elements per thread per step. The row's scales come from swiglu_plan_kernel; its max |h| goes to row_hmax.
 template <int U>
 __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem) {
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
-    __shared__ SwigluScales qs;
     const int r = blockIdx.x;
     if (r >= a.rows) return;
     const int f = a.f;
     int64_t* accg = a.acc + (long long)r * 2 * f;
     const int64_t* accu = accg + f;
-    const int e = a.row_expert ? a.row_expert[r] : 0;
-    const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
-    if (threadIdx.x == 0)
-        qs = swiglu_scales(a, t, e, (int64_t)a.ymax[(long long)r * a.ymax_stride], (int64_t)a.ymax[(long long)r * a.ymax_stride + 1]);
-    __syncthreads();
-    const SwigluScales q = qs;
+    const SwigluScales q = a.plans[r];
     int64_t* h = h_smem ? hs : accg;
     uint64_t hm = 0;
     // the loads of a step are issued before its arithmetic
@@ -557,22 +576,19 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
     }
     const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
     write_down_planes(a, r, h, hmax);
-    if (threadIdx.x == 0) a.row_cd[r] = down_c(a, q.us, hmax, e);
+    if (threadIdx.x == 0) a.row_hmax[r] = (unsigned long long)hmax;
 }
 
-// Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase).
+// Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase; one plan).
 __global__ void swiglu_global_kernel(const SwigluArgs a) {
     __shared__ uint64_t red[32];
-    __shared__ SwigluScales qs;
     const int r = blockIdx.x;
     if (r >= a.rows) return;
     const int f = a.f;
     int64_t* accg = a.acc + (long long)r * 2 * f;
     const int64_t* accu = accg + f;
-    if (threadIdx.x == 0) qs = swiglu_scales(a, 0, 0, (int64_t)a.ymax[0], (int64_t)a.ymax[1]);
-    __syncthreads();
-    const SwigluScales q = qs;
     if (a.phase == 1) {
+        const SwigluScales q = a.plans[0];
         uint64_t hm = 0;
         for (int k = threadIdx.x; k < f; k += blockDim.x) {
             const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
@@ -585,7 +601,7 @@ __global__ void swiglu_global_kernel(const SwigluArgs a) {
     }
     const int64_t hmax = (int64_t)*a.g_hmax;
     write_down_planes(a, r, accg, hmax);
-    if (r == 0 && threadIdx.x == 0) a.row_cd[0] = down_c(a, q.us, hmax, 0);
+    if (r == 0 && threadIdx.x == 0) a.row_cd[0] = down_c(a, a.plans[0].us, hmax, 0);
 }
 
 // ───────────── combine: one token's selected experts → its output (layers.rs:893-923) ─────────────
@@ -603,83 +619,119 @@ struct CombineArgs {
 
 constexpr int COMBINE_MAX_K = 16;
 
-__global__ void combine_kernel(const CombineArgs a) {
+// The per-token combine plan: live slot count (-1: the token's output is zero), the common scale, and per live slot
+// (packed to the front in slot order) its row, routing code, requant divisor and rescale to the common scale.
+struct CombinePlan {
+    int* n;             // [T]
+    Scale* common;      // [T]
+    int* row;           // [T][K]
+    int64_t* ec;        // [T][K]
+    kt::ReqDiv* ry;     // [T][K]
+    kt::ApplyPlan* f;   // [T][K]
+};
+
+// One thread per token: ys_i = ratio_act(ymax_i)·c_i (zero when c_i or ymax_i is zero, layers.rs:300-302,
+// :321-326), common = the last of the largest (fold with ge, layers.rs:898), and the live slots' plans.
+__global__ void combine_plan_kernel(const CombineArgs a, const CombinePlan p) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= a.T) return;
+    const int K = a.top_k;
+    if (a.sumc[t] <= 0) {
+        p.n[t] = -1;
+        return;
+    }
+    Scale ys[COMBINE_MAX_K];
+    Scale common = kt::scale_zero();
+    for (int i = 0; i < K; ++i) {
+        const int row = a.slot_row[(long long)t * K + i];
+        const int64_t ym = (int64_t)a.ymax_d[row];
+        const Scale cd = a.row_cd[row];
+        ys[i] = (cd.mant == 0 || ym == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ym), cd);
+        if (kt::scale_ge(ys[i], common)) common = ys[i];
+    }
+    if (common.mant == 0) {
+        p.n[t] = -1;
+        return;
+    }
+    const Scale cinv = kt::scale_recip(common);
+    int n = 0;
+    for (int i = 0; i < K; ++i) {
+        if (ys[i].mant == 0) continue;
+        const long long o = (long long)t * K + n;
+        const int row = a.slot_row[(long long)t * K + i];
+        p.row[o] = row;
+        p.ec[o] = a.top_ec[(long long)t * K + i];
+        p.ry[o] = kt::make_req((int64_t)a.ymax_d[row]);
+        p.f[o] = kt::make_apply(kt::scale_mul(ys[i], cinv));
+        ++n;
+    }
+    p.n[t] = n;
+    p.common[t] = common;
+}
+
+// One block per token, from its plan: every live slot's load of a step is in flight before its arithmetic
+// (KMAX >= top_k, a compile-time bound so the loads are unrolled).
+template <int KMAX>
+__global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a, const CombinePlan p) {
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
-    __shared__ int64_t ymax_s[COMBINE_MAX_K];
-    __shared__ kt::ReqDiv ry_s[COMBINE_MAX_K];
-    __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
-    __shared__ Scale common_s;
-    __shared__ int64_t ec_s[COMBINE_MAX_K];
-    __shared__ int row_s[COMBINE_MAX_K];
-    __shared__ int live_s;
+    __shared__ kt::ReqDiv ry_s[KMAX];
+    __shared__ kt::ApplyPlan f_s[KMAX];
+    __shared__ int64_t ec_s[KMAX];
+    __shared__ int row_s[KMAX];
     const int t = blockIdx.x;
     if (t >= a.T) return;
-    const int K = a.top_k, D = a.dim;
+    const int D = a.dim;
     int32_t* o = a.out + (long long)t * D;
-    const int64_t sumc = a.sumc[t];
-    if (sumc <= 0) {
+    const int n = p.n[t];
+    if (n < 0) {
         for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
         if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
         return;
     }
-    if (threadIdx.x < K) {
-        const int row = a.slot_row[(long long)t * K + threadIdx.x];
-        row_s[threadIdx.x] = row;
-        ec_s[threadIdx.x] = a.top_ec[(long long)t * K + threadIdx.x];
-        ymax_s[threadIdx.x] = (int64_t)a.ymax_d[row];
+    const int K = a.top_k;
+    if ((int)threadIdx.x < n) {
+        const long long q = (long long)t * K + threadIdx.x;
+        row_s[threadIdx.x] = p.row[q];
+        ec_s[threadIdx.x] = p.ec[q];
+        ry_s[threadIdx.x] = p.ry[q];
+        f_s[threadIdx.x] = p.f[q];
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // ys[i].scale: zero when its c or ymax is zero; common = the last of the largest (fold with ge, :898)
-        Scale ys[COMBINE_MAX_K];
-        Scale common = kt::scale_zero();
-        for (int i = 0; i < K; ++i) {
-            const Scale cd = a.row_cd[row_s[i]];
-            ys[i] = (cd.mant == 0 || ymax_s[i] == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax_s[i]), cd);
-            if (kt::scale_ge(ys[i], common)) common = ys[i];
+    const int64_t* base[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) base[j] = a.acc_d + (long long)row_s[j < n ? j : 0] * D;
+    uint64_t gm = 0;
+    constexpr int U = KMAX <= 4 ? 4 : 2;  // elements per thread per step
+    for (int d0 = threadIdx.x; d0 < D; d0 += U * blockDim.x) {
+        int64_t v[U][KMAX];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int d = d0 + u * blockDim.x;
+#pragma unroll
+            for (int j = 0; j < KMAX; ++j) v[u][j] = (j < n && d < D) ? __ldg(base[j] + d) : 0;
         }
-        common_s = common;
-        // the slots that contribute (a zero-scale output contributes 0), packed to the front
-        int n = 0;
-        if (common.mant != 0) {
-            const Scale cinv = kt::scale_recip(common);
-            for (int i = 0; i < K; ++i) {
-                if (ys[i].mant == 0) continue;
-                f_s[n] = kt::make_apply(kt::scale_mul(ys[i], cinv));
-                ry_s[n] = kt::make_req(ymax_s[i]);
-                row_s[n] = row_s[i];
-                ec_s[n] = ec_s[i];
-                ++n;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int d = d0 + u * blockDim.x;
+            int64_t acc = 0;
+#pragma unroll
+            for (int j = 0; j < KMAX; ++j)
+                if (j < n) acc += ec_s[j] * kt::apply_row(f_s[j], kt::requant_row(v[u][j], ry_s[j]));
+            if (d < D) {
+                acc_s[d] = acc;
+                gm = max(gm, uabs64(acc));
             }
         }
-        live_s = n;
-    }
-    __syncthreads();
-    const Scale common = common_s;
-    if (common.mant == 0) {
-        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
-        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
-        return;
-    }
-    const int n = live_s;
-    uint64_t gm = 0;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        int64_t s = 0;
-        for (int i = 0; i < n; ++i) {
-            const int32_t yv = kt::requant_row(a.acc_d[(long long)row_s[i] * D + d], ry_s[i]);
-            s += ec_s[i] * kt::apply_row(f_s[i], yv);
-        }
-        acc_s[d] = s;
-        gm = max(gm, uabs64(s));
     }
     gm = block_max_u64(gm, red);
     const int64_t gmax = (int64_t)gm;
     const kt::ReqDiv rg = kt::make_req(gmax);
     for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
     if (threadIdx.x == 0) {
+        const int64_t sumc = a.sumc[t];
         a.out_scale[t] = gmax == 0 ? kt::scale_zero()
-                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common),
+                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), p.common[t]),
                                                    kt::from_ratio(1, (kt::u128)(uint64_t)sumc));
     }
 }
