@@ -52,3 +52,7 @@ void fp_quant_row_n(const int32_t* d, const int64_t* xmax, int32_t* out, int64_t
 }
 int64_t fp_apply_row(fp_scale s, int64_t v) { return kt::apply_row(kt::make_apply(S(s)), v); }
 }
+
+extern "C" {
+int64_t fp_apply_row32(fp_scale s, int32_t v) { return kt::apply_row(kt::make_apply(S(s)), v); }
+}

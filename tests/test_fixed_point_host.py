@@ -186,3 +186,44 @@ def test_row_plans_equal_the_exact_ones(fp, oracle):
         assert fp.fp_apply_row(FpScale(*s), val) == oracle.apply(s, val)
         s2 = (s[0], s[1] % 70 - 3)
         assert fp.fp_apply_row(FpScale(*s2), val) == oracle.apply(s2, val)
+
+
+def test_certified_paths_near_integer_quotients(fp, oracle):
+    """Quotients that sit on or next to an integer, where the double estimate cannot decide and the integer path
+    must: requant_row and quant_row against the exact forms."""
+    rng = np.random.default_rng(21)
+    P = ctypes.POINTER
+    n = 600_000
+    den = rng.integers(1 << 22, 1 << 52, size=n, dtype=np.int64) >> rng.integers(0, 30, size=n)
+    den = np.maximum(den, 1 << 22)
+    q = rng.integers(0, 1 << 28, size=n, dtype=np.int64)
+    # v with v·2^28 + floor(den/2) at or just around q·den (computed exactly in Python integers)
+    v = np.array([min(int(dd), max(0, (int(qq) * int(dd) - int(dd) // 2) // (1 << 28) + int(e)))
+                  for qq, dd, e in zip(q, den, rng.integers(-1, 2, size=n))], dtype=np.int64)
+    v *= rng.choice([-1, 1], size=n)
+    a, b = np.empty(n, np.int32), np.empty(n, np.int32)
+    args = (v.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)))
+    fp.fp_requant_act_n(*args, a.ctypes.data_as(P(ctypes.c_int32)), n)
+    fp.fp_requant_row_n(*args, b.ctypes.data_as(P(ctypes.c_int32)), n)
+    assert (a == b).all()
+    xmax = rng.integers(1 << 16, 1 << 31, size=n, dtype=np.int64)
+    qd = rng.integers(0, 265721, size=n, dtype=np.int64)
+    d = np.array([min(int(xm), max(0, (int(qq) * int(xm) - int(xm) // 2) // 265720 + int(e)))
+                  for qq, xm, e in zip(qd, xmax, rng.integers(-1, 2, size=n))], dtype=np.int64)
+    d = (d * rng.choice([-1, 1], size=n)).astype(np.int32)
+    fp.fp_quant_to_n(d.ctypes.data_as(P(ctypes.c_int32)), xmax.ctypes.data_as(P(ctypes.c_int64)),
+                     a.ctypes.data_as(P(ctypes.c_int32)), n)
+    fp.fp_quant_row_n(d.ctypes.data_as(P(ctypes.c_int32)), xmax.ctypes.data_as(P(ctypes.c_int64)),
+                      b.ctypes.data_as(P(ctypes.c_int32)), n)
+    assert (a == b).all()
+
+
+def test_apply_row_on_int32_values(fp, oracle):
+    fp.fp_apply_row32.argtypes = [FpScale, ctypes.c_int32]
+    fp.fp_apply_row32.restype = ctypes.c_int64
+    g = _lcg(9)
+    for _ in range(40000):
+        s = oracle.mul(oracle.from_ratio(next(g) % (1 << 60) + 1, next(g) % (1 << 60) + 1),
+                       oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
+        for val in (int(next(g) % (1 << 32)) - (1 << 31), -(1 << 31), (1 << 31) - 1, 0, -1, 1):
+            assert fp.fp_apply_row32(FpScale(*s), val) == oracle.apply(s, val)

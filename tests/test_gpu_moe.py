@@ -141,3 +141,29 @@ def test_forward_dev_equals_forward(ctx):
     ctx.sync(torch.cuda.current_stream().cuda_stream)
     assert (yd.cpu().numpy() == y.data).all()
     assert int(ys[0]) == y.scale.mant and (int(ys[1]) & 0xFFFFFFFF) == (y.scale.shift & 0xFFFFFFFF)
+
+
+@pytest.mark.parametrize("name", ["small_shared_softmax", "tiny_softmax_37rows"])
+def test_forward_dev_with_unaligned_device_buffers(ctx, name):
+    """Caller buffers that start 4 bytes past a 16-byte boundary take the scalar paths of the vectorised kernels
+    and give the same bytes."""
+    torch = pytest.importorskip("torch")
+    c = cases.CASES[name]
+    m = cases.build_layer(c, ctx)
+    x = tb.IntTensor.from_reals(cases.make_x(c))
+    y = m.forward_int(x)
+    n = c.T * c.d
+    xbuf = torch.zeros(n + 4, dtype=torch.int32, device="cuda")
+    ybuf = torch.full((n + 4,), -7, dtype=torch.int32, device="cuda")
+    xbuf[1:n + 1] = torch.from_numpy(x.data.copy()).cuda()
+    xs = torch.tensor([x.scale.mant, x.scale.shift & 0xFFFFFFFF], dtype=torch.int64).cuda()
+    ys = torch.zeros(2, dtype=torch.int64, device="cuda")
+    dev = m.device_layer()
+    torch.cuda.synchronize()
+    dev.forward_dev(xbuf.data_ptr() + 4, c.T, xs.data_ptr(), ybuf.data_ptr() + 4, ys.data_ptr(),
+                    torch.cuda.current_stream().cuda_stream)
+    ctx.sync(torch.cuda.current_stream().cuda_stream)
+    got = ybuf.cpu().numpy()
+    assert (got[1:n + 1] == y.data).all()
+    assert got[0] == -7 and (got[n + 1:] == -7).all(), "wrote outside the output"
+    assert int(ys[0]) == y.scale.mant

@@ -269,12 +269,27 @@ KT_HD int32_t requant_act(int64_t v, int64_t den) {
 }
 
 // ───── per-row plans for the hot loops ─────
+// floor(y) for 0 <= y < 2^31 as a double and as an integer. On the device one add rounded toward minus infinity
+// of 1.5·2^52 leaves floor(y) in the low mantissa bits (FP64 pipe only, no conversion instruction).
+KT_HD double floor_split(double y, int32_t& q) {
+#ifdef __CUDA_ARCH__
+    const double m = __dadd_rd(y, 6755399441055744.0);  // 2^52 + 2^51: an ulp of 1 from 2^52 on
+    q = (int32_t)(uint32_t)__double_as_longlong(m);
+    return m - 6755399441055744.0;
+#else
+    const double f = __builtin_floor(y);
+    q = (int32_t)f;
+    return f;
+#endif
+}
+
 // The divisor of a row's requant (den = the row's max |v|, so |v| <= den) with its reciprocal, built once per row.
 struct ReqDiv {
     int64_t d;
     int64_t half;  // floor(d / 2)
     double inv28;  // 2^28 / d
     bool tight;    // d < 2^52: the 64-bit path below is exact
+    bool dbl;      // 2^22 <= d < 2^52: the certified double path applies
 };
 
 KT_HD ReqDiv make_req(int64_t d) {
@@ -283,15 +298,28 @@ KT_HD ReqDiv make_req(int64_t d) {
     r.half = r.d / 2;
     r.inv28 = 268435456.0 / (double)r.d;
     r.tight = r.d < (int64_t(1) << 52);
+    r.dbl = r.tight && r.d >= (int64_t(1) << 22);
     return r;
 }
 
-// requant_dyn(v, 2^28, den) for |v| <= den (layers.rs:34-39). x = |v|·2^28/den <= 2^28 is estimated in double to
-// within 2^-24 (|v| < 2^52 converts exactly; two roundings of relative size 2^-53), so trunc(estimate) is within one
-// of floor((|v|·2^28 + half)/den); the remainder |v|·2^28 + half - q·den lies in (-den, 2·den) and is formed exactly
-// in wrapping 64-bit arithmetic, and one signed correction gives the floor.
+// requant_dyn(v, 2^28, den) for |v| <= den (layers.rs:34-39): q = floor(t), t = (|v|·2^28 + floor(den/2)) / den,
+// then the sign of v.
+//
+// Certified double path (2^22 <= den < 2^52): y = |v|·(2^28/den) + 1/2 in double differs from t by at most
+// 2^-24 (the estimate; |v| converts exactly) + 2^-25 (the last rounding) + 1/(2·den) (floor(den/2)/den is 1/2 or
+// 1/2 - 1/(2·den)) < 2^-22. t is a multiple of 1/den, so when y lies more than 2^-21 from every integer, t and y
+// share their floor and floor(y) is exact. Otherwise (about one value in a million) the integer path decides.
+// Integer path (den < 2^52): the same estimate truncated is within one of the floor; the remainder
+// |v|·2^28 + half - q·den lies in (-den, 2·den) and is formed exactly in wrapping 64-bit arithmetic, and one signed
+// correction gives the floor.
 KT_HD int32_t requant_row(int64_t v, const ReqDiv& r) {
     if (!r.tight) return requant_act(v, r.d);
+    if (r.dbl) {
+        const double y = __builtin_fabs((double)v) * r.inv28 + 0.5;
+        int32_t q;
+        const double fr = y - floor_split(y, q);
+        if (fr > 4.76837158203125e-07 && fr < 1.0 - 4.76837158203125e-07) return v >= 0 ? q : -q;  // 2^-21
+    }
     const uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-v);
     int64_t q = (int64_t)((double)(int64_t)av * r.inv28);
     const int64_t rem = (int64_t)((av << ACT_SHIFT) + (uint64_t)r.half - (uint64_t)q * (uint64_t)r.d);
@@ -326,6 +354,14 @@ KT_HD int64_t apply_row(const ApplyPlan& p, int64_t v) {
     return v >= 0 ? (int64_t)r : -(int64_t)r;
 }
 
+// The same for an int32 value (no range check: every int32 other than -2^31 has |v| < 2^31).
+KT_HD int64_t apply_row(const ApplyPlan& p, int32_t v) {
+    if (!p.tight || v == INT32_MIN) return scale_apply(p.s, v);
+    const uint32_t av = (uint32_t)(v >= 0 ? v : -v);
+    const uint64_t r = ((uint64_t)av * p.mant + p.half) >> p.shift;
+    return v >= 0 ? (int64_t)r : -(int64_t)r;
+}
+
 // quant_to(d, xmax) for one row (layers.rs:23-31): x = |d|·WLEVELS/xmax <= WLEVELS is estimated in double, the
 // remainder |d|·WLEVELS + xmax/2 - q·xmax (|d|·WLEVELS < 2^50) is exact in 64 bits, and one signed correction gives
 // the floor.
@@ -333,6 +369,7 @@ struct QuantPlan {
     int64_t xmax;
     int64_t half;
     double inv;  // WLEVELS / xmax
+    bool dbl;    // xmax >= 2^16: the certified double path applies
 };
 
 KT_HD QuantPlan make_quant(int64_t xmax) {
@@ -340,10 +377,20 @@ KT_HD QuantPlan make_quant(int64_t xmax) {
     p.xmax = xmax > 0 ? xmax : 1;
     p.half = p.xmax / 2;
     p.inv = (double)WLEVELS / (double)p.xmax;
+    p.dbl = p.xmax >= (int64_t(1) << 16);
     return p;
 }
 
+// Certified double path as in requant_row: t = (|d|·WLEVELS + floor(xmax/2)) / xmax <= WLEVELS + 1/2, and
+// y = |d|·(WLEVELS/xmax) + 1/2 is within 2^-33 + 1/(2·xmax) <= 2^-17 + 2^-33 of it, so y more than 2^-16 from every
+// integer has t's floor. |d| <= xmax < 2^31 (int32 codes).
 KT_HD int32_t quant_row(int32_t d, const QuantPlan& p) {
+    if (p.dbl) {
+        const double y = __builtin_fabs((double)d) * p.inv + 0.5;
+        int32_t q;
+        const double fr = y - floor_split(y, q);
+        if (fr > 1.52587890625e-05 && fr < 1.0 - 1.52587890625e-05) return d >= 0 ? q : -q;  // 2^-16
+    }
     const int64_t ad = d >= 0 ? (int64_t)d : -(int64_t)d;
     int64_t q = (int64_t)((double)ad * p.inv);
     const int64_t num = ad * WLEVELS;

@@ -75,12 +75,20 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K
     const int r = blockIdx.x;
     if (r >= rows) return;
     const int32_t* xr = x + (long long)r * K;
+    const bool vec = (K & 3) == 0 && ((uintptr_t)x & 15) == 0;  // rows start 16-byte aligned: 4 codes per load
     int64_t xmax;
     if (gxmax) {
         xmax = (int64_t)*gxmax;
     } else {
         uint64_t m = 0;
-        for (int k = threadIdx.x; k < K; k += blockDim.x) m = max(m, uabs64(xr[k]));
+        if (vec) {
+            for (int k4 = threadIdx.x * 4; k4 < K; k4 += blockDim.x * 4) {
+                const int4 v = __ldg((const int4*)(xr + k4));
+                m = max(max(m, uabs64(v.x)), max(uabs64(v.y), max(uabs64(v.z), uabs64(v.w))));
+            }
+        } else {
+            for (int k = threadIdx.x; k < K; k += blockDim.x) m = max(m, uabs64(xr[k]));
+        }
         xmax = (int64_t)block_max_u64(m, red);
     }
     int8_t* p0 = planes + (long long)r * K_pad;
@@ -89,10 +97,18 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K
     const kt::QuantPlan qp = kt::make_quant(xmax);
     for (int k4 = threadIdx.x * 4; k4 < K_pad; k4 += blockDim.x * 4) {
         int32_t q[4];
+        if (vec && k4 < K && xmax > 0) {
+            const int4 v = __ldg((const int4*)(xr + k4));
+            q[0] = kt::quant_row(v.x, qp);
+            q[1] = kt::quant_row(v.y, qp);
+            q[2] = kt::quant_row(v.z, qp);
+            q[3] = kt::quant_row(v.w, qp);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int k = k4 + j;
-            q[j] = (k < K && xmax > 0) ? kt::quant_row(xr[k], qp) : 0;
+            for (int j = 0; j < 4; ++j) {
+                const int k = k4 + j;
+                q[j] = (k < K && xmax > 0) ? kt::quant_row(xr[k], qp) : 0;
+            }
         }
         store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
     }
@@ -780,8 +796,17 @@ __global__ void merge_max_kernel(const int32_t* __restrict__ o, const Scale* __r
     const Scale cinv = common[1];
     if (common[0].mant == 0) return;
     const kt::ApplyPlan f = kt::make_apply(kt::scale_mul(o_scale[t], cinv));
+    const int32_t* ot = o + (long long)t * D;
     uint64_t m = 0;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(kt::apply_row(f, o[(long long)t * D + d])));
+    if ((D & 3) == 0 && ((uintptr_t)o & 15) == 0) {
+        for (int d = threadIdx.x * 4; d < D; d += blockDim.x * 4) {
+            const int4 v = __ldg((const int4*)(ot + d));
+            m = max(max(m, uabs64(kt::apply_row(f, v.x))), uabs64(kt::apply_row(f, v.y)));
+            m = max(max(m, uabs64(kt::apply_row(f, v.z))), uabs64(kt::apply_row(f, v.w)));
+        }
+    } else {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) m = max(m, uabs64(kt::apply_row(f, ot[d])));
+    }
     m = block_max_u64(m, red);
     if (threadIdx.x == 0 && m) atomicMax(gmax, (unsigned long long)m);
 }
@@ -796,8 +821,23 @@ __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* _
     const bool zero = common[0].mant == 0 || gmax == 0;
     const kt::ApplyPlan f = kt::make_apply(zero ? kt::scale_zero() : kt::scale_mul(o_scale[t], common[1]));
     const kt::ReqDiv rg = kt::make_req(gmax);
-    for (int d = threadIdx.x; d < D; d += blockDim.x)
-        y[(long long)t * D + d] = zero ? 0 : kt::requant_row(kt::apply_row(f, o[(long long)t * D + d]), rg);
+    const int32_t* ot = o + (long long)t * D;
+    int32_t* yt = y + (long long)t * D;
+    if ((D & 3) == 0 && (((uintptr_t)o | (uintptr_t)y) & 15) == 0) {
+        for (int d = threadIdx.x * 4; d < D; d += blockDim.x * 4) {
+            int4 r = make_int4(0, 0, 0, 0);
+            if (!zero) {
+                const int4 v = __ldg((const int4*)(ot + d));
+                r.x = kt::requant_row(kt::apply_row(f, v.x), rg);
+                r.y = kt::requant_row(kt::apply_row(f, v.y), rg);
+                r.z = kt::requant_row(kt::apply_row(f, v.z), rg);
+                r.w = kt::requant_row(kt::apply_row(f, v.w), rg);
+            }
+            *(int4*)(yt + d) = r;
+        }
+    } else {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) yt[d] = zero ? 0 : kt::requant_row(kt::apply_row(f, ot[d]), rg);
+    }
     if (t == 0 && threadIdx.x == 0) *y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common[0]);
 }
 
@@ -847,15 +887,37 @@ __device__ __forceinline__ int64_t add_sum(const AddArgs& p, long long i, const 
     return kt::apply_row(fa, p.a[i]) + kt::apply_row(fb, sv);
 }
 
+// Four consecutive elements from i (i a multiple of 4; the buffers are 16-byte aligned): a as one int4, the shared
+// accumulators as two 16-byte loads.
+__device__ __forceinline__ void add_sum4(const AddArgs& p, long long i, const kt::ApplyPlan& fa,
+                                         const kt::ApplyPlan& fb, const kt::ReqDiv& ry, int64_t ymax, int64_t (&out)[4]) {
+    const int4 av = __ldg((const int4*)(p.a + i));
+    const longlong2 s0 = __ldg((const longlong2*)(p.s_acc + i));
+    const longlong2 s1 = __ldg((const longlong2*)(p.s_acc + i + 2));
+    const int64_t sv[4] = {s0.x, s0.y, s1.x, s1.y};
+    const int32_t a4[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        out[j] = kt::apply_row(fa, a4[j]) + kt::apply_row(fb, ymax ? kt::requant_row(sv[j], ry) : 0);
+}
+
 __global__ void add_max_kernel(const AddArgs p) {
     __shared__ uint64_t red[32];
     const kt::ApplyPlan fa = kt::make_apply(p.scratch[2]), fb = kt::make_apply(p.scratch[3]);
     const int64_t ymax = (int64_t)*p.s_ymax;
     const kt::ReqDiv ry = kt::make_req(ymax);
     uint64_t m = 0;
-    if (p.scratch[1].mant)
-        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
+    if (p.scratch[1].mant) {
+        const bool vec = (((uintptr_t)p.a | (uintptr_t)p.s_acc) & 15) == 0;
+        const long long n4 = vec ? p.n & ~3LL : 0, stride = (long long)gridDim.x * blockDim.x;
+        for (long long i = (blockIdx.x * (long long)blockDim.x + threadIdx.x) * 4; i < n4; i += stride * 4) {
+            int64_t v[4];
+            add_sum4(p, i, fa, fb, ry, ymax, v);
+            m = max(max(m, max(uabs64(v[0]), uabs64(v[1]))), max(uabs64(v[2]), uabs64(v[3])));
+        }
+        for (long long i = n4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += stride)
             m = max(m, uabs64(add_sum(p, i, fa, fb, ry, ymax)));
+    }
     m = block_max_u64(m, red);
     if (threadIdx.x == 0 && m) atomicMax(p.gmax, (unsigned long long)m);
 }
@@ -867,7 +929,21 @@ __global__ void add_final_kernel(const AddArgs p) {
     const int64_t gmax = (int64_t)*p.gmax;
     const kt::ReqDiv ry = kt::make_req(ymax), rg = kt::make_req(gmax);
     const bool zero = common.mant == 0 || gmax == 0;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += (long long)gridDim.x * blockDim.x)
+    const bool vec = (((uintptr_t)p.a | (uintptr_t)p.s_acc | (uintptr_t)p.y) & 15) == 0;
+    const long long n4 = vec ? p.n & ~3LL : 0, stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (blockIdx.x * (long long)blockDim.x + threadIdx.x) * 4; i < n4; i += stride * 4) {
+        int4 r = make_int4(0, 0, 0, 0);
+        if (!zero) {
+            int64_t v[4];
+            add_sum4(p, i, fa, fb, ry, ymax, v);
+            r.x = kt::requant_row(v[0], rg);
+            r.y = kt::requant_row(v[1], rg);
+            r.z = kt::requant_row(v[2], rg);
+            r.w = kt::requant_row(v[3], rg);
+        }
+        *(int4*)(p.y + i) = r;
+    }
+    for (long long i = n4 + blockIdx.x * (long long)blockDim.x + threadIdx.x; i < p.n; i += stride)
         p.y[i] = zero ? 0 : kt::requant_row(add_sum(p, i, fa, fb, ry, ymax), rg);
     if (blockIdx.x == 0 && threadIdx.x == 0) *p.y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common);
 }
