@@ -289,6 +289,10 @@ def run_ours(args, w, name):
         raise SystemExit(f"{T_all} tokens do not split evenly over {world} ranks")
     T = T_all // world  # this rank's token rows (the entry quantiser ran over the whole tensor)
     x = tb.IntTensor(x_full.data.reshape(T_all, d)[rank * T:(rank + 1) * T], (T, d), x_full.scale)
+    # the exchange of an expert-parallel layer: peer memory over NVLink (default) or NCCL (KTMOE_EP=nccl)
+    transport = os.environ.get("KTMOE_EP", "peer") if world > 1 else None
+    if transport == "peer":
+        dev.set_ep_capacity(T)
     log(f"[bench] {name}: layer resident in {time.perf_counter() - t_build:.1f} s")
 
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -402,7 +406,7 @@ def run_ours(args, w, name):
         "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
         "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
                    "router_bias": f"zipf({w['zipf']})" if w.get("zipf") else None,
-                   "parallelism": f"ep{world}", "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
+                   "parallelism": f"ep{world}", "ep_transport": transport, "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
                    "bit_exact_vs_host_api": ok_exact},
         "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
                 "d2h_bytes_per_step": T_all * d * 4 + 16 * world},

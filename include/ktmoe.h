@@ -102,6 +102,13 @@ int ktmoe_layer_create_ep(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int32_t
                           const void* nccl_id, ktmoe_layer** out);
 /* The experts this layer holds: [*begin, *end). ktmoe_layer_set_expert takes global expert ids in that range. */
 int ktmoe_layer_experts(const ktmoe_layer* layer, int32_t* begin, int32_t* end);
+/* Peer-memory transport (all ranks call it together, with the same value; at most 8 ranks): afterwards every forward
+ * passes at most max_tokens_per_rank rows on each rank, and the exchanges run as kernels that write into the other
+ * GPUs' memory over NVLink (CUDA IPC mappings) instead of NCCL calls, with no host synchronisation in the forward.
+ * Results are the same bytes. 0 returns to the NCCL exchange. Device memory per rank: the receive planes
+ * (3 * world * max * top_k * d_model bytes) and the experts' scratch for that many rows. Replaces the reference's
+ * forward_int_with_experts transport (crates/01-engine/kt-core/src/layers.rs:945-984) inside one node. */
+int ktmoe_layer_set_ep_capacity(ktmoe_layer* layer, int64_t max_tokens_per_rank);
 
 /* Router codes [E][d_model] (QuantLinear w_codes, row-major) and w_scale; bias_codes [E] + bias_scale from
  * QuantLinear::with_bias, or NULL for no bias. */

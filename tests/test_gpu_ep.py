@@ -1,6 +1,6 @@
-"""Expert parallelism over NCCL (ktmoe_layer_create_ep): the rows of each rank, concatenated in rank order, must be
-bit-identical to the single-GPU forward (and so to the golden hashes of the CPU path). Needs two or more GPUs; the
-ranks run as spawned processes, one per GPU."""
+"""Expert parallelism (ktmoe_layer_create_ep), over NCCL and over peer memory (ktmoe_layer_set_ep_capacity): the rows
+of each rank, concatenated in rank order, must be bit-identical to the single-GPU forward (and so to the golden hashes
+of the CPU path). Needs two or more GPUs; the ranks run as spawned processes, one per GPU."""
 
 import json
 import os
@@ -37,7 +37,7 @@ def _splits(T, world, mode):
     raise ValueError(mode)
 
 
-def _worker(rank, world, port, name, mode, outdir):
+def _worker(rank, world, port, name, mode, transport, outdir):
     import datetime
 
     import torch
@@ -72,7 +72,9 @@ def _worker(rank, world, port, name, mode, outdir):
     start = sum(sizes[:rank])
     rows = sizes[rank]
     xr = x.data.reshape(c.T, c.d)[start:start + rows]
-    for rep in range(2):  # twice: the second forward reuses every buffer
+    if transport == "peer":
+        dev.set_ep_capacity(max(sizes))  # collective: every rank passes the same capacity
+    for rep in range(3):  # the later forwards reuse every buffer (and, over peer memory, the flags)
         y, ys = dev.forward(xr, rows, x.scale)
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=y, mant=ys.mant, shift=ys.shift, rows=rows)
     dev = None
@@ -81,9 +83,11 @@ def _worker(rank, world, port, name, mode, outdir):
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["nccl", "peer"])
 @pytest.mark.parametrize("name,mode", [("tiny_softmax_37rows", "even"), ("small_shared_softmax", "even"),
-                                       ("tiny_sigmoid_shared", "first_empty"), ("config1", "even")])
-def test_expert_parallel_equals_one_gpu(tmp_path, name, mode):
+                                       ("tiny_sigmoid_shared", "first_empty"), ("config1", "even"),
+                                       ("tiny_sigmoid_raw_shared_one_row", "first_empty")])
+def test_expert_parallel_equals_one_gpu(tmp_path, name, mode, transport):
     import torch
     import torch.multiprocessing as mp
 
@@ -94,7 +98,7 @@ def test_expert_parallel_equals_one_gpu(tmp_path, name, mode):
     world = min(world, c.E)
     if mode == "first_empty" and c.T < world - 1:
         world = 2
-    mp.spawn(_worker, args=(world, _free_port(), name, mode, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), name, mode, transport, str(tmp_path)), nprocs=world, join=True)
     ys, scales = [], set()
     for r in range(world):
         z = np.load(tmp_path / f"rank{r}.npz")

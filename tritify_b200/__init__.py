@@ -323,6 +323,11 @@ class DeviceLayer:
                                            ctypes.byref(ys)))
         return y, Scale._of(ys)
 
+    def set_ep_capacity(self, max_tokens_per_rank: int) -> None:
+        """Expert-parallel layers: exchange over peer memory (NVLink, CUDA IPC) for forwards of at most this many rows
+        per rank; all ranks call it together with the same value (0: back to NCCL)."""
+        self.ctx.check(lib().ktmoe_layer_set_ep_capacity(self._h, int(max_tokens_per_rank)))
+
     def forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int, stream: int = 0) -> None:
         """Device buffers (raw pointers), stream-ordered, not synchronised."""
         self.ctx.check(lib().ktmoe_forward_dev(self._h, ctypes.c_void_p(x_ptr), rows, ctypes.c_void_p(x_scale_ptr),

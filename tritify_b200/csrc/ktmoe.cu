@@ -22,6 +22,7 @@
 
 #include "digit_gemm.cuh"
 #include "digit_gemm_pair.cuh"
+#include "ep_peer.cuh"
 #include "fixed_point.cuh"
 #include "host_prep.h"
 #include "ktmoe.h"
@@ -344,6 +345,16 @@ struct ktmoe_layer {
         ep_y_send, ep_ys_send, ep_y_back, ep_ys_back, ep_tiles, ep_runs, ep_rec, ep_recs, ep_best_idx;
     std::vector<int> h_counts;
     int64_t ep_tok_offset = 0, ep_tok_total = 0;
+    // the peer-memory transport (ktmoe_layer_set_ep_capacity): one IPC-shared region per rank
+    struct Peer {
+        bool on = false;
+        int64_t cap_T = 0, cap_rows = 0, cap_home = 0, bytes = 0;
+        DevBuf region;
+        void* opened[ep::MAXW] = {};
+        ep::Peers P{};
+        unsigned long long seq = 0;
+        DevBuf ctr, dst_base, rows_recv, group_end, tiles, tok_info, recv_sqx, recv_expert;
+    } peer;
     int64_t d_pad = 0, f_pad = 0, fs_pad = 0;
     Planes w_router, w_gu, w_dn, w_sgu, w_sdn;
     DevBuf b_router, b_gu, b_dn, b_sgu, b_sdn;
@@ -356,6 +367,8 @@ struct ktmoe_layer {
     DevBuf b_wsc;
     std::vector<Scale> h_wsc;
     DevBuf b_luts;  // 3 x 65536 int64: exp, SiLU, sigmoid
+    DevBuf b_silu32;  // the SiLU codes as int32 (they all fit: |silu(x)|·2^20 < 2^25 on [-30, 30])
+    bool silu32 = false;
     hp::HTable tabs[3];
     Scale silu_code_scale_recip{0, 0};
     int64_t swiglu_smem = 0;  // dynamic shared bytes holding one row's h (0: h stays in global memory)
@@ -496,6 +509,7 @@ int mark(ktmoe_layer* L, cudaStream_t st) {
 mk::Lut lut(const ktmoe_layer* L, int kind) {
     mk::Lut l;
     l.codes = L->b_luts.as<int64_t>() + (int64_t)kind * mk::LUT_N;
+    l.codes32 = (kind == 1 && L->silu32) ? L->b_silu32.as<int32_t>() : nullptr;
     l.inv_step = S(L->tabs[kind].inv_step);
     l.lo_index = L->tabs[kind].lo_index;
     return l;
@@ -558,16 +572,22 @@ int nccl_check(ktmoe_ctx* ctx, ncclResult_t r, const char* what) {
     } while (0)
 
 // max over the ranks of n u64 words, in place
-int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t st) {
+// max over the ranks of n u64 words, in place; `point` names the step for the peer transport
+int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t st, int point) {
     if (L->world == 1) return KTMOE_OK;
     ktmoe_ctx* ctx = L->ctx;
+    if (L->peer.on) {
+        ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, point, L->peer.seq, p, (int)n, nullptr, p, ctx->d_err);
+        CKL(ctx);
+        return KTMOE_OK;
+    }
     NK(ncclAllReduce(p, p, n, ncclUint64, ncclMax, L->comm, st));
     return KTMOE_OK;
 }
 
 // Dispatch plan of the home rank: a stable counting sort of the T·K (token, slot) rows by expert, the tile tables of
 // the grouped GEMMs (widths BN and BN2) and the rows' digit planes gathered in that order (xg_planes).
-int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st) {
+int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st, bool permute = true) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t E = L->E, K = L->K, R = T * K;
     const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
@@ -590,6 +610,7 @@ int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st
         L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
         L->row_assign.as<int>(), L->row_expert.as<int>());
     CKL(ctx);
+    if (!permute) return KTMOE_OK;
     mk::permute_planes_kernel<<<(unsigned)R, 128, 0, st>>>(L->tok_planes.as<int8_t>(), T_pad, L->xg_planes.as<int8_t>(),
                                                          R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
     CKL(ctx);
@@ -609,6 +630,7 @@ struct ExpertRows {
     const int* row_assign;  // nullptr: row_sqx is per row
     const int* row_expert;
     const Scale* row_sqx;
+    const int* n_rows_dev = nullptr;  // rows counted on the device (n_rows is then an upper bound)
 };
 
 int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
@@ -663,6 +685,7 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     sa.ymax_stride = 2;
     sa.plans = L->swiglu_plans.as<mk::SwigluScales>();
     sa.row_hmax = L->row_hmax.as<unsigned long long>();
+    sa.rows_dev = x.n_rows_dev;
     sa.phase = 0;
     mk::swiglu_plan_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
     CKL(ctx);
@@ -674,12 +697,14 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
             const int v = e ? atoi(e) : 2;
             return (v == 1 || v == 2 || v == 4) ? v : 2;
         }();
+        // blocks walk the rows: a few per SM cover them without a block per row
+        const unsigned grid = (unsigned)std::min<int64_t>(R, (int64_t)ctx->num_sms * 6);
         if (unroll == 1)
-            mk::swiglu_rows_kernel<1><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<1><<<grid, 256, sm, st>>>(sa, h_smem);
         else if (unroll == 4)
-            mk::swiglu_rows_kernel<4><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<4><<<grid, 256, sm, st>>>(sa, h_smem);
         else
-            mk::swiglu_rows_kernel<2><<<(unsigned)R, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<2><<<grid, 256, sm, st>>>(sa, h_smem);
         CKL(ctx);
     }
     mk::down_c_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
@@ -894,6 +919,94 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     return KTMOE_OK;
 }
 
+// Expert parallelism over peer memory (ktmoe_layer_set_ep_capacity): the counts go to every rank, each rank writes
+// its rows straight into the owners' expert-major buffers, the owners run their experts on what arrived and write the
+// outputs straight back into the home ranks' buffers; no host synchronisation and no copies through NCCL.
+int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    auto& pr = L->peer;
+    const int64_t d = L->d, E = L->E, K = L->K, R = T * K, G = L->world;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64);
+    // tile widths from the balanced estimate of the rows an owner receives
+    const int BN = pick_bn((double)R * G / (double)E, true), BN2 = pick_bn_long_k((double)R * G / (double)E, L->f, true);
+    if (R > 0) {
+        if (int r = plan_and_permute(L, T, BN, BN2, st, false)) return r;
+    } else {
+        CK(cudaMemsetAsync(L->expert_count.p, 0, E * 4, st));
+        CK(cudaMemsetAsync(L->expert_off.p, 0, E * 4, st));
+    }
+    const unsigned long long seq = pr.seq;
+    ep::counts_exchange_kernel<<<1, 256, 0, st>>>(pr.P, seq, L->expert_count.as<int>(), (int)T, ctx->d_err);
+    CKL(ctx);
+    int* tiles = pr.tiles.as<int>();
+    const int64_t tmax = pr.cap_rows / 16 + L->E_local + 1;
+    const mk::TileTable ta{BN, tiles, tiles + tmax, tiles + 4 * tmax};
+    const mk::TileTable tb{BN2, tiles + 2 * tmax, tiles + 3 * tmax, tiles + 4 * tmax + 1};
+    int* tok_info = pr.tok_info.as<int>();  // [0] this rank's first token, [1] the layer's tokens
+    ep::ep_plan_kernel<<<1, 256, 2 * E * 4, st>>>(pr.P, L->expert_off.as<int>(), pr.dst_base.as<int>(),
+                                                   pr.group_end.as<int>(), pr.rows_recv.as<int>(), ta, tb, tok_info,
+                                                   tok_info + 1, ctx->d_err);
+    CKL(ctx);
+    ep::dispatch_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(R, ctx->num_sms * 4)), 128, 0, st>>>(
+        pr.P, seq, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
+        L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(), ctx->d_err);
+    CKL(ctx);
+    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_DISPATCH, seq, ctx->d_err);
+    CKL(ctx);
+    MARK(L, st);
+
+    // the owner side: this rank's experts on the rows that arrived (their count is on the device)
+    ep::meta_unpack_kernel<<<(unsigned)std::min<int64_t>((pr.cap_rows + 255) / 256, ctx->num_sms * 4), 256, 0, st>>>(
+        pr.P, pr.rows_recv.as<int>(), pr.recv_sqx.as<Scale>(), pr.recv_expert.as<int>());
+    CKL(ctx);
+    ExpertRows xr;
+    xr.B = Planes{(int8_t*)((unsigned char*)pr.region.p + pr.P.off_planes), 1, pr.cap_rows, d, L->d_pad};
+    xr.n_rows = pr.cap_rows;
+    xr.n_rows_dev = pr.rows_recv.as<int>();
+    xr.BN = BN;
+    xr.BN2 = BN2;
+    xr.grid_a = pr.cap_rows / BN + L->E_local;
+    xr.grid_b = pr.cap_rows / BN2 + L->E_local;
+    xr.tg_a = ta.tile_group;
+    xr.tr_a = ta.tile_row0;
+    xr.te_a = nullptr;
+    xr.nt_a = ta.n_tiles;
+    xr.tg_b = tb.tile_group;
+    xr.tr_b = tb.tile_row0;
+    xr.te_b = nullptr;
+    xr.nt_b = tb.n_tiles;
+    xr.group_end = pr.group_end.as<int>();
+    xr.row_assign = nullptr;
+    xr.row_expert = pr.recv_expert.as<int>();
+    xr.row_sqx = pr.recv_sqx.as<Scale>();
+    if (int r = run_experts(L, xr, st)) return r;
+    ep::return_kernel<<<(unsigned)(ctx->num_sms * 2), 256, 0, st>>>(pr.P, seq, pr.rows_recv.as<int>(),
+                                                                   L->acc_d.as<int64_t>(),
+                                                                   L->rowmax_d.as<unsigned long long>(),
+                                                                   L->row_cd.as<Scale>(), pr.ctr.as<int>(), ctx->d_err);
+    CKL(ctx);
+    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_RETURN, seq, ctx->d_err);
+    CKL(ctx);
+    MARK(L, st);
+    if (T > 0) {
+        mk::CombineYArgs ca;
+        ca.y = (const int32_t*)((unsigned char*)pr.region.p + pr.P.off_rety);
+        ca.ys = (const Scale*)((unsigned char*)pr.region.p + pr.P.off_retys);
+        ca.slot_row = L->slot_row.as<int>();
+        ca.top_ec = L->top_ec.as<int64_t>();
+        ca.sumc = L->sumc.as<int64_t>();
+        ca.T = (int)T;
+        ca.top_k = (int)K;
+        ca.dim = (int)d;
+        ca.out = L->tok_out.as<int32_t>();
+        ca.out_scale = L->tok_scale.as<Scale>();
+        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        CKL(ctx);
+    }
+    MARK(L, st);
+    return KTMOE_OK;
+}
+
 int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
                   cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
@@ -950,21 +1063,19 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
                                  L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
         mk::combine_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
         CKL(ctx);
-        if (L->K <= 2)
-            mk::combine_kernel<2><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        else if (L->K <= 4)
-            mk::combine_kernel<4><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        else if (L->K <= 8)
-            mk::combine_kernel<8><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        else
-            mk::combine_kernel<16><<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
         CKL(ctx);
         MARK(L, st);
+    } else if (L->peer.on) {
+        ++L->peer.seq;
+        if (int r = ep_routed_peer(L, T, st)) return r;
+        T_total = -1;  // on the device (peer.tok_info): the merge kernels read it there
     } else {
         if (int r = ep_routed(L, T, st)) return r;
         T_total = L->ep_tok_total;
         tok_offset = L->ep_tok_offset;
     }
+    const int* tok_info = L->peer.on ? L->peer.tok_info.as<int>() : nullptr;  // [0] first token, [1] tokens
 
     // merge (layers.rs:1001-1019): one common scale and one gmax over all the layer's tokens, on every rank
     int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
@@ -986,7 +1097,8 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
             CK(L->ep_best_idx.ensure(4));
             if (T > 0) {
                 mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
-                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>());
+                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
+                                                            tok_info);
                 CKL(ctx);
                 mk::scale_record_kernel<<<1, 1, 0, st>>>(scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
                                                          L->ep_rec.as<int64_t>());
@@ -995,7 +1107,13 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
                 const int64_t none[3] = {0, 0, -1};
                 CK(cudaMemcpyAsync(L->ep_rec.p, none, sizeof(none), cudaMemcpyHostToDevice, st));
             }
-            NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
+            if (L->peer.on) {
+                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->peer.seq, L->ep_rec.as<unsigned long long>(),
+                                                      3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
+                CKL(ctx);
+            } else {
+                NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
+            }
             mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, scal_scale(L, SL_COMMON));
             CKL(ctx);
         }
@@ -1005,11 +1123,12 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
                                                             scal_u64(L, U_MERGE_GMAX));
             CKL(ctx);
         }
-        if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st)) return r;
+        if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st, ep::P_MERGE)) return r;
         if (T > 0) {
             mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
                                                               (int)T, (int)d, scal_scale(L, SL_COMMON),
-                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale);
+                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale,
+                                                              tok_info ? tok_info + 1 : nullptr);
             CKL(ctx);
         }
     }
@@ -1023,7 +1142,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         mk::absmax_i32_kernel<<<red_blocks, 256, 0, st>>>(x_dev, n, scal_u64(L, U_GXMAX));
         CKL(ctx);
     }
-    if (int r = allreduce_max(L, scal_u64(L, U_GXMAX), 1, st)) return r;
+    if (int r = allreduce_max(L, scal_u64(L, U_GXMAX), 1, st, ep::P_SX)) return r;
     sqx_kernel<<<1, 1, 0, st>>>(scal_u64(L, U_GXMAX), xs_dev, scal_scale(L, SL_GSQX));
     CKL(ctx);
     GemmCall s;
@@ -1045,7 +1164,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         s.rowmax_split = fs;
         if (int r = run_gemm(ctx, st, s)) return r;
     }
-    if (int r = allreduce_max(L, scal_u64(L, U_SYG), 2, st)) return r;
+    if (int r = allreduce_max(L, scal_u64(L, U_SYG), 2, st, ep::P_SYG)) return r;
     mk::SwigluArgs sh;
     std::memset(&sh, 0, sizeof(sh));
     sh.acc = L->acc_sgu.as<int64_t>();
@@ -1075,7 +1194,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
         CKL(ctx);
     }
-    if (int r = allreduce_max(L, scal_u64(L, U_SHMAX), 1, st)) return r;
+    if (int r = allreduce_max(L, scal_u64(L, U_SHMAX), 1, st, ep::P_SHMAX)) return r;
     sh.phase = 2;
     if (T > 0) {
         mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
@@ -1090,7 +1209,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         s.rowmax_split = INT32_MAX;
         if (int r = run_gemm(ctx, st, s)) return r;
     }
-    if (int r = allreduce_max(L, scal_u64(L, U_SYD), 1, st)) return r;
+    if (int r = allreduce_max(L, scal_u64(L, U_SYD), 1, st, ep::P_SYD)) return r;
     // a rank without tokens still needs the shared down c for nothing: only ranks with rows produce output
     mk::AddArgs aa;
     aa.a = routed;
@@ -1109,7 +1228,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         mk::add_max_kernel<<<red_blocks, 256, 0, st>>>(aa);
         CKL(ctx);
     }
-    if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st)) return r;
+    if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st, ep::P_ADD)) return r;
     if (T > 0) {
         mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
         CKL(ctx);
@@ -1422,6 +1541,18 @@ static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank,
         if (cudaMemcpy(L->b_luts.as<int64_t>() + kind * mk::LUT_N, L->tabs[kind].codes.data(), mk::LUT_N * 8,
                        cudaMemcpyHostToDevice) != cudaSuccess)
             return bail(fail(ctx, KTMOE_ERR_CUDA, "tables"));
+    {
+        std::vector<int32_t> c32(mk::LUT_N);
+        L->silu32 = true;
+        for (int i = 0; i < mk::LUT_N; ++i) {
+            const int64_t c = L->tabs[1].codes[i];
+            L->silu32 = L->silu32 && c == (int64_t)(int32_t)c;
+            c32[i] = (int32_t)c;
+        }
+        if (L->silu32 && (L->b_silu32.ensure(mk::LUT_N * 4) != cudaSuccess ||
+                          cudaMemcpy(L->b_silu32.p, c32.data(), mk::LUT_N * 4, cudaMemcpyHostToDevice) != cudaSuccess))
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "tables"));
+    }
     if (L->b_rbias.ensure(L->E * 8) != cudaSuccess || L->b_sigbias.ensure(L->E * 8) != cudaSuccess)
         return bail(fail(ctx, KTMOE_ERR_CUDA, "bias"));
     // h of one row stays in shared memory only while that still leaves room for several resident blocks per SM;
@@ -1439,10 +1570,7 @@ static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank,
     }
     if ((size_t)L->d * 8 > 48 * 1024) {
         const int cs = (int)(L->d * 8);
-        if (cudaFuncSetAttribute(mk::combine_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
-            cudaFuncSetAttribute(mk::combine_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
-            cudaFuncSetAttribute(mk::combine_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
-            cudaFuncSetAttribute(mk::combine_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess)
+        if (cudaFuncSetAttribute(mk::combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess)
             return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
         if (cudaFuncSetAttribute(mk::combine_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
             cudaSuccess)
@@ -1485,6 +1613,131 @@ int ktmoe_layer_experts(const ktmoe_layer* L, int32_t* begin, int32_t* end) {
     return KTMOE_OK;
 }
 
+// Min over the ranks of one int (host value; NCCL on the context stream, synchronous). Also a barrier.
+static int allreduce_min_host(ktmoe_layer* L, int v, int* out) {
+    ktmoe_ctx* ctx = L->ctx;
+    DevBuf b;
+    CK(b.ensure(4));
+    CK(cudaMemcpy(b.p, &v, 4, cudaMemcpyHostToDevice));
+    NK(ncclAllReduce(b.p, b.p, 1, ncclInt32, ncclMin, L->comm, ctx->stream));
+    CK(cudaMemcpyAsync(out, b.p, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    b.release();
+    return KTMOE_OK;
+}
+
+// Unmap the peers' regions and free this rank's. `collective`: every rank does the same now, so a barrier makes sure
+// no rank frees its region while another still has it mapped.
+static void peer_close(ktmoe_layer* L, bool collective) {
+    auto& pr = L->peer;
+    for (int q = 0; q < ep::MAXW; ++q)
+        if (pr.opened[q]) {
+            cudaIpcCloseMemHandle(pr.opened[q]);
+            pr.opened[q] = nullptr;
+        }
+    if (collective && pr.region.p) {
+        int all = 0;
+        allreduce_min_host(L, 1, &all);
+    }
+    DevBuf* bufs[] = {&pr.region, &pr.ctr, &pr.dst_base, &pr.rows_recv, &pr.group_end, &pr.tiles, &pr.tok_info,
+                      &pr.recv_sqx, &pr.recv_expert};
+    for (DevBuf* b : bufs) b->release();
+    pr.on = false;
+    pr.cap_T = pr.cap_rows = pr.cap_home = pr.bytes = 0;
+}
+
+int ktmoe_layer_set_ep_capacity(ktmoe_layer* L, int64_t max_tokens_per_rank) {
+    if (!L || max_tokens_per_rank < 0 || max_tokens_per_rank > (int64_t(1) << 24)) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->world == 1) return KTMOE_OK;
+    if (L->world > ep::MAXW) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "the peer transport serves at most 8 ranks");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    CK(cudaStreamSynchronize(ctx->stream));
+    peer_close(L, L->peer.on);
+    if (max_tokens_per_rank == 0) return KTMOE_OK;
+    auto& pr = L->peer;
+    const int64_t G = L->world, E = L->E, K = L->K, d = L->d, dp = L->d_pad;
+    auto a256 = [](int64_t x) { return (x + 255) / 256 * 256; };
+    pr.cap_T = max_tokens_per_rank;
+    pr.cap_home = pr.cap_T * K;
+    pr.cap_rows = round_up(G * pr.cap_T * K, 64);  // every rank's rows could go to one owner
+    ep::Peers& P = pr.P;
+    std::memset(&P, 0, sizeof(P));
+    P.world = (int)G;
+    P.rank = L->rank;
+    P.E = (int)E;
+    P.e_begin = (int)L->e_begin;
+    P.e_end = (int)L->e_end;
+    P.d = (int)d;
+    P.d_pad = (int)dp;
+    int64_t off = a256(sizeof(ep::Box));
+    P.off_counts = off;
+    off += a256(G * (E + 1) * 4);
+    P.off_planes = off;
+    off += a256(3 * pr.cap_rows * dp);
+    P.off_meta = off;
+    off += a256(pr.cap_rows * 32);
+    P.off_rety = off;
+    off += a256(pr.cap_home * d * 4);
+    P.off_retys = off;
+    off += a256(pr.cap_home * (int64_t)sizeof(Scale));
+    P.cap_rows = pr.cap_rows;
+    P.cap_home = pr.cap_home;
+    pr.bytes = off;
+    // every step below is taken by every rank (the collectives stay matched when one rank fails locally)
+    int ok = 1;
+    cudaIpcMemHandle_t h;
+    std::memset(&h, 0, sizeof(h));
+    if (pr.region.ensure((size_t)off) != cudaSuccess || cudaMemset(pr.region.p, 0, (size_t)off) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, pr.region.p) != cudaSuccess)
+        ok = 0;
+    const int64_t tmax = pr.cap_rows / 16 + L->E_local + 1;
+    if (ok && (pr.ctr.ensure(4) != cudaSuccess || cudaMemset(pr.ctr.p, 0, 4) != cudaSuccess ||
+               pr.dst_base.ensure(E * 4) != cudaSuccess || pr.rows_recv.ensure(4) != cudaSuccess ||
+               pr.group_end.ensure(L->E_local * 4) != cudaSuccess || pr.tiles.ensure((4 * tmax + 2) * 4) != cudaSuccess ||
+               pr.tok_info.ensure(2 * 4) != cudaSuccess || pr.recv_sqx.ensure(pr.cap_rows * sizeof(Scale)) != cudaSuccess ||
+               pr.recv_expert.ensure(pr.cap_rows * 4) != cudaSuccess || ensure_rows(L, pr.cap_rows) != KTMOE_OK))
+        ok = 0;
+    // every rank's region handle to every rank (NCCL, host-synchronous: this is set-up, not the forward)
+    DevBuf hs;
+    CK(hs.ensure((size_t)(G + 1) * sizeof(h)));
+    CK(cudaMemcpy(hs.p, &h, sizeof(h), cudaMemcpyHostToDevice));
+    NK(ncclAllGather(hs.p, (unsigned char*)hs.p + sizeof(h), sizeof(h), ncclInt8, L->comm, ctx->stream));
+    std::vector<cudaIpcMemHandle_t> all(G);
+    CK(cudaMemcpyAsync(all.data(), (unsigned char*)hs.p + sizeof(h), G * sizeof(h), cudaMemcpyDeviceToHost,
+                       ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    hs.release();
+    cudaError_t open_err = cudaSuccess;
+    for (int64_t q = 0; q < G && ok; ++q) {
+        if (q == L->rank) {
+            P.base[q] = (unsigned char*)pr.region.p;
+            continue;
+        }
+        void* ptr = nullptr;
+        open_err = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+        if (open_err != cudaSuccess) {
+            ok = 0;
+            break;
+        }
+        pr.opened[q] = ptr;
+        P.base[q] = (unsigned char*)ptr;
+    }
+    // all ranks learn whether all succeeded; this is also the barrier before anyone writes into a peer
+    int all_ok = 0;
+    if (int r = allreduce_min_host(L, ok, &all_ok)) return r;
+    if (!all_ok) {
+        peer_close(L, true);
+        if (open_err != cudaSuccess) return fail_cuda(ctx, open_err, "cudaIpcOpenMemHandle");
+        return fail(ctx, KTMOE_ERR_CUDA, ok ? "the peer transport could not be set up on another rank"
+                                            : "the peer transport could not be set up");
+    }
+    pr.seq = 0;
+    pr.on = true;
+    return KTMOE_OK;
+}
+
 int ktmoe_layer_destroy(ktmoe_layer* L) {
     if (!L) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
@@ -1492,7 +1745,7 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     DevBuf* bufs[] = {&L->b_router, &L->b_gu, &L->b_dn, &L->b_sgu, &L->b_sdn, &L->b_rbias, &L->b_sigbias, &L->b_wsc,
-                      &L->b_luts, &L->x_in, &L->y_out, &L->scal, &L->tok_planes, &L->tok_xmax, &L->tok_sqx,
+                      &L->b_luts, &L->b_silu32, &L->x_in, &L->y_out, &L->scal, &L->tok_planes, &L->tok_xmax, &L->tok_sqx,
                       &L->router_acc, &L->logits, &L->logit_scale, &L->top_e, &L->top_ec, &L->sumc, &L->counts,
                       &L->chunk_off, &L->expert_off, &L->group_end, &L->expert_count, &L->tile_group, &L->tile_row0, &L->tile_group2, &L->tile_row02,
                       &L->slot_row, &L->row_assign, &L->row_expert, &L->xg_planes, &L->acc_gu, &L->hq_planes,
@@ -1504,6 +1757,7 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                          &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,
                          &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
     for (DevBuf* b : ep_bufs) b->release();
+    peer_close(L, L->peer.on);  // an expert-parallel layer is destroyed on every rank
     if (L->comm) ncclCommDestroy(L->comm);
     delete L;
     return KTMOE_OK;
@@ -1585,6 +1839,7 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
 int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
                       int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream) {
     if (!L || !x_scale_dev || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (L->peer.on && rows > L->peer.cap_T) return fail(L->ctx, KTMOE_ERR_ARG, "more rows than the EP capacity");
     if (rows > 0 && (!x_dev || !y_dev || !y_scale_dev)) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
@@ -1598,6 +1853,7 @@ int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const 
 int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
                   ktmoe_scale* y_scale) {
     if (!L || !y_scale || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (L->peer.on && rows > L->peer.cap_T) return fail(L->ctx, KTMOE_ERR_ARG, "more rows than the EP capacity");
     if (rows > 0 && (!x || !y)) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");

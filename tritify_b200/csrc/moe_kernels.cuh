@@ -27,6 +27,7 @@ struct Lut {
     const int64_t* codes;
     Scale inv_step;
     int64_t lo_index;
+    const int32_t* codes32;  // the same codes as int32 when every one fits (half the cache footprint), else nullptr
 };
 
 // ───────────── block reductions ─────────────
@@ -471,7 +472,10 @@ struct SwigluArgs {
     unsigned long long* row_hmax;  // routed: max |h| per row, for down_c_kernel
     unsigned long long* g_hmax;  // tensor-global mode: phase 1 reduces max |h| here, phase 2 reads it
     int phase;  // 0: per-row (routed, one kernel); 1: global h pass; 2: global quantise pass
+    const int* rows_dev;  // routed rows counted on the device (rows is then an upper bound), or nullptr
 };
+
+__device__ __forceinline__ int swiglu_rows(const SwigluArgs& a) { return a.rows_dev ? *a.rows_dev : a.rows; }
 
 __device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t, int e, int64_t gmax_g, int64_t gmax_u) {
     SwigluScales q;
@@ -498,7 +502,7 @@ __global__ void swiglu_plan_kernel(const SwigluArgs a) {
         if (r == 0) a.plans[0] = swiglu_scales(a, 0, 0, (int64_t)a.ymax[0], (int64_t)a.ymax[1]);
         return;
     }
-    if (r >= a.rows) return;
+    if (r >= swiglu_rows(a)) return;
     const int e = a.row_expert ? a.row_expert[r] : 0;
     const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
     a.plans[r] = swiglu_scales(a, t, e, (int64_t)a.ymax[(long long)r * a.ymax_stride],
@@ -516,7 +520,7 @@ __device__ __forceinline__ int64_t swiglu_h(const SwigluArgs& a, const SwigluSca
     else if (idx >= LUT_N)
         code = kt::apply_row(q.idf, g);  // identity right tail, in code units
     else
-        code = __ldg(a.silu.codes + idx);
+        code = a.silu.codes32 ? (int64_t)__ldg(a.silu.codes32 + idx) : __ldg(a.silu.codes + idx);
     const int32_t c32 = (int32_t)code;
     return c32 == code ? (int64_t)c32 * (int64_t)u : code * (int64_t)u;
 }
@@ -533,7 +537,7 @@ __device__ __forceinline__ Scale down_c(const SwigluArgs& a, Scale us, int64_t h
 // Per routed row: the down linear's c from the row's plan and max |h|, one thread per row.
 __global__ void down_c_kernel(const SwigluArgs a) {
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
-    if (r >= a.rows) return;
+    if (r >= swiglu_rows(a)) return;
     const int e = a.row_expert ? a.row_expert[r] : 0;
     a.row_cd[r] = down_c(a, a.plans[r].us, (int64_t)a.row_hmax[r], e);
 }
@@ -555,44 +559,47 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
     }
 }
 
-// Phase 0: one block per routed row; h stays in shared memory (dynamic, f int64) when `h_smem`. U independent
-// elements per thread per step. The row's scales come from swiglu_plan_kernel; its max |h| goes to row_hmax.
+// Phase 0: blocks walk the routed rows (row r, r + gridDim.x, ...); h stays in shared memory (dynamic, f int64) when
+// `h_smem`. U independent elements per thread per step. The row's scales come from swiglu_plan_kernel; its max |h|
+// goes to row_hmax.
 template <int U>
 __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem) {
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
-    const int r = blockIdx.x;
-    if (r >= a.rows) return;
+    const int n = swiglu_rows(a);
     const int f = a.f;
-    int64_t* accg = a.acc + (long long)r * 2 * f;
-    const int64_t* accu = accg + f;
-    const SwigluScales q = a.plans[r];
-    int64_t* h = h_smem ? hs : accg;
-    uint64_t hm = 0;
-    // the loads of a step are issued before its arithmetic
-    int k = threadIdx.x;
-    for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
-        int64_t gv[U], uv[U];
+    for (int r = blockIdx.x; r < n; r += gridDim.x) {
+        int64_t* accg = a.acc + (long long)r * 2 * f;
+        const int64_t* accu = accg + f;
+        const SwigluScales q = a.plans[r];
+        int64_t* h = h_smem ? hs : accg;
+        uint64_t hm = 0;
+        // the loads of a step are issued before its arithmetic
+        int k = threadIdx.x;
+        for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
+            int64_t gv[U], uv[U];
 #pragma unroll
-        for (int j = 0; j < U; ++j) {
-            gv[j] = accg[k + j * blockDim.x];
-            uv[j] = accu[k + j * blockDim.x];
+            for (int j = 0; j < U; ++j) {
+                gv[j] = accg[k + j * blockDim.x];
+                uv[j] = accu[k + j * blockDim.x];
+            }
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int64_t v = swiglu_h(a, q, gv[j], uv[j]);
+                h[k + j * blockDim.x] = v;
+                hm = max(hm, uabs64(v));
+            }
         }
-#pragma unroll
-        for (int j = 0; j < U; ++j) {
-            const int64_t v = swiglu_h(a, q, gv[j], uv[j]);
-            h[k + j * blockDim.x] = v;
+        for (; k < f; k += blockDim.x) {
+            const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
+            h[k] = v;
             hm = max(hm, uabs64(v));
         }
+        const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
+        write_down_planes(a, r, h, hmax);
+        if (threadIdx.x == 0) a.row_hmax[r] = (unsigned long long)hmax;
+        __syncthreads();  // h (and red) are reused by the next row
     }
-    for (; k < f; k += blockDim.x) {
-        const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
-        h[k] = v;
-        hm = max(hm, uabs64(v));
-    }
-    const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
-    write_down_planes(a, r, h, hmax);
-    if (threadIdx.x == 0) a.row_hmax[r] = (unsigned long long)hmax;
 }
 
 // Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase; one plan).
@@ -685,16 +692,17 @@ __global__ void combine_plan_kernel(const CombineArgs a, const CombinePlan p) {
     p.common[t] = common;
 }
 
-// One block per token, from its plan: every live slot's load of a step is in flight before its arithmetic
-// (KMAX >= top_k, a compile-time bound so the loads are unrolled).
-template <int KMAX>
-__global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a, const CombinePlan p) {
+// One block per token, from its plan. A thread owns CE elements per chunk and walks the live slots: a slot's plan
+// is read from shared memory once per chunk and its CE loads are in flight together.
+constexpr int CE = 8;
+
+__global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, const CombinePlan p) {
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
-    __shared__ kt::ReqDiv ry_s[KMAX];
-    __shared__ kt::ApplyPlan f_s[KMAX];
-    __shared__ int64_t ec_s[KMAX];
-    __shared__ int row_s[KMAX];
+    __shared__ kt::ReqDiv ry_s[COMBINE_MAX_K];
+    __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
+    __shared__ int64_t ec_s[COMBINE_MAX_K];
+    __shared__ int row_s[COMBINE_MAX_K];
     const int t = blockIdx.x;
     if (t >= a.T) return;
     const int D = a.dim;
@@ -714,29 +722,31 @@ __global__ void __launch_bounds__(256) combine_kernel(const CombineArgs a, const
         f_s[threadIdx.x] = p.f[q];
     }
     __syncthreads();
-    const int64_t* base[KMAX];
-#pragma unroll
-    for (int j = 0; j < KMAX; ++j) base[j] = a.acc_d + (long long)row_s[j < n ? j : 0] * D;
     uint64_t gm = 0;
-    constexpr int U = KMAX <= 4 ? 4 : 2;  // elements per thread per step
-    for (int d0 = threadIdx.x; d0 < D; d0 += U * blockDim.x) {
-        int64_t v[U][KMAX];
+    for (int d0 = threadIdx.x; d0 < D; d0 += CE * blockDim.x) {
+        int64_t acc[CE];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const int d = d0 + u * blockDim.x;
+        for (int u = 0; u < CE; ++u) acc[u] = 0;
+        for (int j = 0; j < n; ++j) {
+            const kt::ReqDiv ry = ry_s[j];
+            const kt::ApplyPlan f = f_s[j];
+            const int64_t ec = ec_s[j];
+            const int64_t* b = a.acc_d + (long long)row_s[j] * D;
+            int64_t v[CE];
 #pragma unroll
-            for (int j = 0; j < KMAX; ++j) v[u][j] = (j < n && d < D) ? __ldg(base[j] + d) : 0;
+            for (int u = 0; u < CE; ++u) {
+                const int d = d0 + u * blockDim.x;
+                v[u] = d < D ? __ldg(b + d) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, kt::requant_row(v[u], ry));
         }
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int u = 0; u < CE; ++u) {
             const int d = d0 + u * blockDim.x;
-            int64_t acc = 0;
-#pragma unroll
-            for (int j = 0; j < KMAX; ++j)
-                if (j < n) acc += ec_s[j] * kt::apply_row(f_s[j], kt::requant_row(v[u][j], ry_s[j]));
             if (d < D) {
-                acc_s[d] = acc;
-                gm = max(gm, uabs64(acc));
+                acc_s[d] = acc[u];
+                gm = max(gm, uabs64(acc[u]));
             }
         }
     }
@@ -769,8 +779,9 @@ __device__ __forceinline__ ScaleIdx better(ScaleIdx x, ScaleIdx y) {
 
 // One block: common scale over `n` scales (index offset idx0), result + its reciprocal into out[0..1].
 __global__ void common_scale_kernel(const Scale* __restrict__ scales, int n, int idx0, Scale* __restrict__ out,
-                                    int* __restrict__ out_idx) {
+                                    int* __restrict__ out_idx, const int* __restrict__ idx0_dev = nullptr) {
     __shared__ ScaleIdx sm[1024];
+    if (idx0_dev) idx0 = *idx0_dev;
     ScaleIdx b{kt::scale_zero(), -1};
     for (int i = threadIdx.x; i < n; i += blockDim.x) b = better(b, ScaleIdx{scales[i], idx0 + i});
     sm[threadIdx.x] = b;
@@ -814,9 +825,16 @@ __global__ void merge_max_kernel(const int32_t* __restrict__ o, const Scale* __r
 // Pass 2: y = requant_dyn(f_t.apply(o_t), L, gmax); scale = from_ratio(gmax, L)·common.
 __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ o_scale, int T, int D,
                                    const Scale* __restrict__ common, const unsigned long long* __restrict__ gmax_p,
-                                   int32_t* __restrict__ y, Scale* __restrict__ y_scale) {
+                                   int32_t* __restrict__ y, Scale* __restrict__ y_scale,
+                                   const int* __restrict__ t_total = nullptr) {
     const int t = blockIdx.x;
     if (t >= T) return;
+    if (t_total && *t_total == 1) {
+        // one token in the whole layer: the routed output is its combine output (layers.rs:992-994)
+        for (int d = threadIdx.x; d < D; d += blockDim.x) y[(long long)t * D + d] = o[(long long)t * D + d];
+        if (threadIdx.x == 0) *y_scale = o_scale[t];
+        return;
+    }
     const int64_t gmax = (int64_t)*gmax_p;
     const bool zero = common[0].mant == 0 || gmax == 0;
     const kt::ApplyPlan f = kt::make_apply(zero ? kt::scale_zero() : kt::scale_mul(o_scale[t], common[1]));
