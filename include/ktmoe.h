@@ -143,6 +143,12 @@ int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
  * stage over the timed forwards (stages: 0 quantise+route, 1 dispatch, 2 gate/up GEMM, 3 SwiGLU, 4 down GEMM,
  * 5 combine, 6 merge, 7 shared expert + add; n_stages >= 8) and forgets them. */
 int ktmoe_layer_set_timing(ktmoe_layer* layer, int32_t enable);
+/* CUDA graphs for the forward (off by default): with it on, the first forward with given buffers, row count and
+ * stream runs normally and is then captured; later forwards with the same ones launch the graph (fewer launch
+ * gaps at decode sizes). Applies on one rank and with the peer transport; the NCCL exchange and per-stage timing run
+ * uncaptured. The layer's weights may change between calls (they are read in place); growing the scratch (more rows
+ * than ever before) drops the graphs. No counterpart in the reference (its CPU path launches nothing). */
+int ktmoe_layer_set_graphs(ktmoe_layer* layer, int32_t enable);
 int ktmoe_layer_stage_times(ktmoe_layer* layer, double* ms, int32_t n_stages, int32_t* n_forwards);
 
 /* Diagnostics: copy an internal buffer of the last forward or route (which = 0: router logits [rows][E] int32,

@@ -72,8 +72,10 @@ def _worker(rank, world, port, name, mode, transport, outdir):
     start = sum(sizes[:rank])
     rows = sizes[rank]
     xr = x.data.reshape(c.T, c.d)[start:start + rows]
-    if transport == "peer":
+    if transport.startswith("peer"):
         dev.set_ep_capacity(max(sizes))  # collective: every rank passes the same capacity
+    if transport == "peer_graphs":
+        dev.set_graphs(True)
     for rep in range(3):  # the later forwards reuse every buffer (and, over peer memory, the flags)
         y, ys = dev.forward(xr, rows, x.scale)
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=y, mant=ys.mant, shift=ys.shift, rows=rows)
@@ -83,7 +85,7 @@ def _worker(rank, world, port, name, mode, transport, outdir):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("transport", ["nccl", "peer"])
+@pytest.mark.parametrize("transport", ["nccl", "peer", "peer_graphs"])
 @pytest.mark.parametrize("name,mode", [("tiny_softmax_37rows", "even"), ("small_shared_softmax", "even"),
                                        ("tiny_sigmoid_shared", "first_empty"), ("config1", "even"),
                                        ("tiny_sigmoid_raw_shared_one_row", "first_empty")])

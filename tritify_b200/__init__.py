@@ -323,6 +323,10 @@ class DeviceLayer:
                                            ctypes.byref(ys)))
         return y, Scale._of(ys)
 
+    def set_graphs(self, enable: bool) -> None:
+        """Capture the forward in CUDA graphs (per buffers, rows and stream) and replay them."""
+        self.ctx.check(lib().ktmoe_layer_set_graphs(self._h, 1 if enable else 0))
+
     def set_ep_capacity(self, max_tokens_per_rank: int) -> None:
         """Expert-parallel layers: exchange over peer memory (NVLink, CUDA IPC) for forwards of at most this many rows
         per rank; all ranks call it together with the same value (0: back to NCCL)."""

@@ -53,6 +53,7 @@ SIGNATURES = {
     "ktmoe_layer_create_ep": ([_vp, _P(KtmoeLayerConfig), _i32, _i32, _vp, _P(_vp)], ctypes.c_int),
     "ktmoe_layer_experts": ([_vp, _P(_i32), _P(_i32)], ctypes.c_int),
     "ktmoe_layer_set_ep_capacity": ([_vp, _i64], ctypes.c_int),
+    "ktmoe_layer_set_graphs": ([_vp, _i32], ctypes.c_int),
     "ktmoe_layer_destroy": ([_vp], ctypes.c_int),
     "ktmoe_layer_set_router": ([_vp, _i32p, KtmoeScale, _i64p, KtmoeScale], ctypes.c_int),
     "ktmoe_layer_set_sigmoid_bias": ([_vp, _i64p], ctypes.c_int),

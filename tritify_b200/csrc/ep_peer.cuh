@@ -41,6 +41,7 @@ struct Peers {
     int d, d_pad;
     long long off_counts, off_planes, off_meta, off_rety, off_retys;
     long long cap_rows, cap_home;
+    unsigned long long* seq;  // this rank's forward counter (device memory, so a captured graph advances it too)
 
     __device__ __forceinline__ Box* box(int r) const { return (Box*)base[r]; }
     __device__ __forceinline__ int* counts(int r) const { return (int*)(base[r] + off_counts); }
@@ -95,8 +96,9 @@ __device__ __forceinline__ bool wait_flag(const Peers& P, int point, int src, un
 // Exchange up to four u64 words with every rank (one block, >= world threads): writes `src` into every rank's
 // vals[point][rank], raises the flags, waits for all ranks, then gives all ranks' words ([world][n], rank order) in
 // `all` and/or their maxima in `mx` (in place allowed: mx may equal src).
-__global__ void exchange_kernel(const Peers P, int point, unsigned long long seq, const unsigned long long* src, int n,
-                                unsigned long long* all, unsigned long long* mx, int* err) {
+__global__ void exchange_kernel(const Peers P, int point, const unsigned long long* src, int n, unsigned long long* all,
+                                unsigned long long* mx, int* err) {
+    const unsigned long long seq = *P.seq;
     __shared__ unsigned long long v[4];
     __shared__ int ok;
     const int i = threadIdx.x;
@@ -125,8 +127,8 @@ __global__ void exchange_kernel(const Peers P, int point, unsigned long long seq
 
 // Publish this rank's counts (E experts + its token count) into counts[rank] of every rank, raise P_COUNTS, wait for
 // all ranks. One block.
-__global__ void counts_exchange_kernel(const Peers P, unsigned long long seq, const int* __restrict__ expert_count,
-                                       int T, int* err) {
+__global__ void counts_exchange_kernel(const Peers P, const int* __restrict__ expert_count, int T, int* err) {
+    const unsigned long long seq = *P.seq;
     const int E1 = P.E + 1;
     for (int q = 0; q < P.world; ++q) {
         int* c = P.counts(q) + (long long)P.rank * E1;
@@ -228,10 +230,11 @@ __device__ __forceinline__ void last_block_signal(const Peers& P, int point, uns
 // Dispatch (the permute and the send in one pass): expert-sorted row r of this rank (token row_assign[r] / K, expert
 // row_expert[r]) is copied from the token's digit planes straight into its owner's receive buffer at
 // dst_base[e] + r, with its meta. Grid-stride over rows; then P_DISPATCH to every rank.
-__global__ void dispatch_kernel(const Peers P, unsigned long long seq, int R, const int* __restrict__ row_assign,
+__global__ void dispatch_kernel(const Peers P, int R, const int* __restrict__ row_assign,
                                 const int* __restrict__ row_expert, int K, const int8_t* __restrict__ tok_planes,
                                 long long T_pad, const Scale* __restrict__ tok_sqx, const int* __restrict__ dst_base,
                                 int* ctr, int* err) {
+    const unsigned long long seq = *P.seq;
     const int n16 = P.d_pad / 16;
     for (int r = blockIdx.x; r < R; r += gridDim.x) {
         const int e = row_expert[r];
@@ -261,9 +264,12 @@ __global__ void dispatch_kernel(const Peers P, unsigned long long seq, int R, co
     last_block_signal(P, P_DISPATCH, seq, ctr);
 }
 
+// A new forward: the next sequence number (one thread).
+__global__ void seq_bump_kernel(const Peers P) { *P.seq += 1; }
+
 // Wait for `point` from every rank (one block, >= world threads).
-__global__ void wait_all_kernel(const Peers P, int point, unsigned long long seq, int* err) {
-    if ((int)threadIdx.x < P.world) wait_flag(P, point, threadIdx.x, seq, err);
+__global__ void wait_all_kernel(const Peers P, int point, int* err) {
+    if ((int)threadIdx.x < P.world) wait_flag(P, point, threadIdx.x, *P.seq, err);
 }
 
 // The owner's per-row s_qx and local expert from the meta of its received rows.
@@ -280,9 +286,10 @@ __global__ void meta_unpack_kernel(const Peers P, const int* __restrict__ rows_r
 // Return (the expert output and the send in one pass): received row r's output, requant_dyn(acc, L, ymax) as i32 with
 // scale from_ratio(ymax, L)·c (the QuantLinear output the seam returns), written into its home rank's ret_y / ret_ys
 // at the home row. Grid-stride over rows; then P_RETURN to every rank.
-__global__ void return_kernel(const Peers P, unsigned long long seq, const int* __restrict__ rows_recv,
+__global__ void return_kernel(const Peers P, const int* __restrict__ rows_recv,
                               const int64_t* __restrict__ acc, const unsigned long long* __restrict__ ymax_row,
                               const Scale* __restrict__ row_cd, int* ctr, int* err) {
+    const unsigned long long seq = *P.seq;
     const int n = *rows_recv;
     const int D = P.d;
     const long long* m = P.meta(P.rank);

@@ -352,8 +352,7 @@ struct ktmoe_layer {
         DevBuf region;
         void* opened[ep::MAXW] = {};
         ep::Peers P{};
-        unsigned long long seq = 0;
-        DevBuf ctr, dst_base, rows_recv, group_end, tiles, tok_info, recv_sqx, recv_expert;
+        DevBuf seq_dev, ctr, dst_base, rows_recv, group_end, tiles, tok_info, recv_sqx, recv_expert;
     } peer;
     int64_t d_pad = 0, f_pad = 0, fs_pad = 0;
     Planes w_router, w_gu, w_dn, w_sgu, w_sdn;
@@ -384,6 +383,16 @@ struct ktmoe_layer {
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
     // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
     bool timing = false;
+    // CUDA graphs of the forward (ktmoe_layer_set_graphs), keyed by the call's pointers, rows and stream
+    struct Graph {
+        const void *x, *xs, *y, *ys;
+        int64_t T;
+        cudaStream_t st;
+        cudaGraphExec_t exec;
+        uint64_t launches;  // this library's kernels in the graph
+    };
+    bool graphs = false;
+    std::vector<Graph> graph_cache;
     std::vector<cudaEvent_t> events;
 };
 
@@ -425,9 +434,15 @@ int ensure_rows(ktmoe_layer* L, int64_t rows) {
     return KTMOE_OK;
 }
 
+void graphs_clear(ktmoe_layer* L) {
+    for (auto& g : L->graph_cache) cudaGraphExecDestroy(g.exec);
+    L->graph_cache.clear();
+}
+
 int ensure_scratch(ktmoe_layer* L, int64_t T) {
     ktmoe_ctx* ctx = L->ctx;
     if (T <= L->cap && L->cap > 0) return KTMOE_OK;
+    graphs_clear(L);  // the scratch moves: graphs that name it are stale
     const int64_t d = L->d, E = L->E, K = L->K, fs = L->fs;
     T = std::max<int64_t>(T, 1);
     const int64_t R = T * K;
@@ -577,7 +592,7 @@ int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t 
     if (L->world == 1) return KTMOE_OK;
     ktmoe_ctx* ctx = L->ctx;
     if (L->peer.on) {
-        ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, point, L->peer.seq, p, (int)n, nullptr, p, ctx->d_err);
+        ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, point, p, (int)n, nullptr, p, ctx->d_err);
         CKL(ctx);
         return KTMOE_OK;
     }
@@ -935,8 +950,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         CK(cudaMemsetAsync(L->expert_count.p, 0, E * 4, st));
         CK(cudaMemsetAsync(L->expert_off.p, 0, E * 4, st));
     }
-    const unsigned long long seq = pr.seq;
-    ep::counts_exchange_kernel<<<1, 256, 0, st>>>(pr.P, seq, L->expert_count.as<int>(), (int)T, ctx->d_err);
+    ep::counts_exchange_kernel<<<1, 256, 0, st>>>(pr.P, L->expert_count.as<int>(), (int)T, ctx->d_err);
     CKL(ctx);
     int* tiles = pr.tiles.as<int>();
     const int64_t tmax = pr.cap_rows / 16 + L->E_local + 1;
@@ -948,10 +962,10 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
                                                    tok_info + 1, ctx->d_err);
     CKL(ctx);
     ep::dispatch_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(R, ctx->num_sms * 4)), 128, 0, st>>>(
-        pr.P, seq, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
+        pr.P, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
         L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(), ctx->d_err);
     CKL(ctx);
-    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_DISPATCH, seq, ctx->d_err);
+    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_DISPATCH, ctx->d_err);
     CKL(ctx);
     MARK(L, st);
 
@@ -980,12 +994,12 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     xr.row_expert = pr.recv_expert.as<int>();
     xr.row_sqx = pr.recv_sqx.as<Scale>();
     if (int r = run_experts(L, xr, st)) return r;
-    ep::return_kernel<<<(unsigned)(ctx->num_sms * 2), 256, 0, st>>>(pr.P, seq, pr.rows_recv.as<int>(),
+    ep::return_kernel<<<(unsigned)(ctx->num_sms * 2), 256, 0, st>>>(pr.P, pr.rows_recv.as<int>(),
                                                                    L->acc_d.as<int64_t>(),
                                                                    L->rowmax_d.as<unsigned long long>(),
                                                                    L->row_cd.as<Scale>(), pr.ctr.as<int>(), ctx->d_err);
     CKL(ctx);
-    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_RETURN, seq, ctx->d_err);
+    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_RETURN, ctx->d_err);
     CKL(ctx);
     MARK(L, st);
     if (T > 0) {
@@ -1067,7 +1081,8 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         CKL(ctx);
         MARK(L, st);
     } else if (L->peer.on) {
-        ++L->peer.seq;
+        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);
+        CKL(ctx);
         if (int r = ep_routed_peer(L, T, st)) return r;
         T_total = -1;  // on the device (peer.tok_info): the merge kernels read it there
     } else {
@@ -1104,11 +1119,11 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
                                                          L->ep_rec.as<int64_t>());
                 CKL(ctx);
             } else {
-                const int64_t none[3] = {0, 0, -1};
-                CK(cudaMemcpyAsync(L->ep_rec.p, none, sizeof(none), cudaMemcpyHostToDevice, st));
+                mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
+                CKL(ctx);
             }
             if (L->peer.on) {
-                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->peer.seq, L->ep_rec.as<unsigned long long>(),
+                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->ep_rec.as<unsigned long long>(),
                                                       3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
                 CKL(ctx);
             } else {
@@ -1234,6 +1249,57 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         CKL(ctx);
     }
     MARK(L, st);
+    return KTMOE_OK;
+}
+
+// The forward through a CUDA graph when graphs are on and the forward has no host synchronisation (one rank, or the
+// peer transport): the first call with a key runs the forward, then captures the same launch sequence; later calls
+// with that key launch the graph. Timing (per-stage events) and the NCCL exchange always run uncaptured.
+int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, int32_t* y, Scale* ys, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    if (!L->graphs || L->timing || (L->world > 1 && !L->peer.on)) return stage_forward(L, T, x, xs, y, ys, st);
+    for (auto& g : L->graph_cache)
+        if (g.x == x && g.xs == xs && g.y == y && g.ys == ys && g.T == T && g.st == st) {
+            CK(cudaGraphLaunch(g.exec, st));
+            ctx->launches += g.launches;
+            return KTMOE_OK;
+        }
+    if (int r = stage_forward(L, T, x, xs, y, ys, st)) return r;
+    const uint64_t l0 = ctx->launches;
+    cudaGraph_t graph = nullptr;
+    CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    const int r = stage_forward(L, T, x, xs, y, ys, st);
+    const cudaError_t e = cudaStreamEndCapture(st, &graph);
+    ctx->launches = l0;  // nothing ran during the capture
+    if (r != KTMOE_OK || e != cudaSuccess || !graph) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        L->graphs = false;  // this forward cannot be captured here: stay uncaptured (its result is already computed)
+        return KTMOE_OK;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    uint64_t n = 0;
+    size_t nodes = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &nodes) == cudaSuccess) {
+        std::vector<cudaGraphNode_t> v(nodes);
+        if (nodes && cudaGraphGetNodes(graph, v.data(), &nodes) == cudaSuccess)
+            for (auto nd : v) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) ++n;
+            }
+    }
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+        cudaGetLastError();
+        L->graphs = false;
+        return KTMOE_OK;
+    }
+    if (L->graph_cache.size() >= 16) {
+        cudaGraphExecDestroy(L->graph_cache.front().exec);
+        L->graph_cache.erase(L->graph_cache.begin());
+    }
+    L->graph_cache.push_back({x, xs, y, ys, T, st, exec, n});
     return KTMOE_OK;
 }
 
@@ -1639,7 +1705,7 @@ static void peer_close(ktmoe_layer* L, bool collective) {
         int all = 0;
         allreduce_min_host(L, 1, &all);
     }
-    DevBuf* bufs[] = {&pr.region, &pr.ctr, &pr.dst_base, &pr.rows_recv, &pr.group_end, &pr.tiles, &pr.tok_info,
+    DevBuf* bufs[] = {&pr.region, &pr.seq_dev, &pr.ctr, &pr.dst_base, &pr.rows_recv, &pr.group_end, &pr.tiles, &pr.tok_info,
                       &pr.recv_sqx, &pr.recv_expert};
     for (DevBuf* b : bufs) b->release();
     pr.on = false;
@@ -1654,6 +1720,7 @@ int ktmoe_layer_set_ep_capacity(ktmoe_layer* L, int64_t max_tokens_per_rank) {
     std::lock_guard<std::mutex> lk(ctx->mu);
     if (int r = set_device(ctx)) return r;
     CK(cudaStreamSynchronize(ctx->stream));
+    graphs_clear(L);
     peer_close(L, L->peer.on);
     if (max_tokens_per_rank == 0) return KTMOE_OK;
     auto& pr = L->peer;
@@ -1693,7 +1760,8 @@ int ktmoe_layer_set_ep_capacity(ktmoe_layer* L, int64_t max_tokens_per_rank) {
         cudaDeviceSynchronize() != cudaSuccess || cudaIpcGetMemHandle(&h, pr.region.p) != cudaSuccess)
         ok = 0;
     const int64_t tmax = pr.cap_rows / 16 + L->E_local + 1;
-    if (ok && (pr.ctr.ensure(4) != cudaSuccess || cudaMemset(pr.ctr.p, 0, 4) != cudaSuccess ||
+    if (ok && (pr.seq_dev.ensure(8) != cudaSuccess || cudaMemset(pr.seq_dev.p, 0, 8) != cudaSuccess ||
+               pr.ctr.ensure(4) != cudaSuccess || cudaMemset(pr.ctr.p, 0, 4) != cudaSuccess ||
                pr.dst_base.ensure(E * 4) != cudaSuccess || pr.rows_recv.ensure(4) != cudaSuccess ||
                pr.group_end.ensure(L->E_local * 4) != cudaSuccess || pr.tiles.ensure((4 * tmax + 2) * 4) != cudaSuccess ||
                pr.tok_info.ensure(2 * 4) != cudaSuccess || pr.recv_sqx.ensure(pr.cap_rows * sizeof(Scale)) != cudaSuccess ||
@@ -1733,7 +1801,7 @@ int ktmoe_layer_set_ep_capacity(ktmoe_layer* L, int64_t max_tokens_per_rank) {
         return fail(ctx, KTMOE_ERR_CUDA, ok ? "the peer transport could not be set up on another rank"
                                             : "the peer transport could not be set up");
     }
-    pr.seq = 0;
+    P.seq = pr.seq_dev.as<unsigned long long>();
     pr.on = true;
     return KTMOE_OK;
 }
@@ -1757,6 +1825,7 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                          &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,
                          &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
     for (DevBuf* b : ep_bufs) b->release();
+    graphs_clear(L);
     peer_close(L, L->peer.on);  // an expert-parallel layer is destroyed on every rank
     if (L->comm) ncclCommDestroy(L->comm);
     delete L;
@@ -1847,7 +1916,7 @@ int ktmoe_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const 
     if (int r = set_device(ctx)) return r;
     if (int r = ensure_scratch(L, rows)) return r;
     cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
-    return stage_forward(L, rows, x_dev, (const Scale*)x_scale_dev, y_dev, (Scale*)y_scale_dev, st);
+    return run_forward(L, rows, x_dev, (const Scale*)x_scale_dev, y_dev, (Scale*)y_scale_dev, st);
 }
 
 int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
@@ -1865,7 +1934,7 @@ int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_
     Scale xs = S(x_scale);
     if (n) CK(cudaMemcpyAsync(L->x_in.p, x, n * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
-    if (int r = stage_forward(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
+    if (int r = run_forward(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
                               scal_scale(L, SL_YSCALE), st))
         return r;
     Scale ys{0, 0};
@@ -1896,6 +1965,16 @@ int ktmoe_route(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_sc
     CK(cudaMemcpyAsync(sumc, L->sumc.p, (size_t)rows * 8, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return check_err_word(ctx);
+}
+
+int ktmoe_layer_set_graphs(ktmoe_layer* L, int32_t enable) {
+    if (!L) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(L->ctx->mu);
+    if (int r = set_device(L->ctx)) return r;
+    cudaStreamSynchronize(L->ctx->stream);
+    graphs_clear(L);
+    L->graphs = enable != 0;
+    return KTMOE_OK;
 }
 
 int ktmoe_layer_set_timing(ktmoe_layer* L, int32_t enable) {

@@ -1098,6 +1098,13 @@ __global__ void scale_record_kernel(const Scale* __restrict__ best, const int* _
     rec[2] = *best_idx;
 }
 
+// The record of a rank without tokens: no candidate ({0, 0, -1}).
+__global__ void empty_record_kernel(int64_t* __restrict__ rec) {
+    rec[0] = 0;
+    rec[1] = 0;
+    rec[2] = -1;
+}
+
 // The common scale over the ranks' records (in rank order; the index decides ties, so the order does not matter).
 __global__ void reduce_records_kernel(const int64_t* __restrict__ recs, int n, Scale* __restrict__ out) {
     ScaleIdx b{kt::scale_zero(), -1};
