@@ -111,3 +111,18 @@ def test_codes_outside_wlevels_fail_loudly(ctx):
         ctx.linear(np.array([1, 2], np.int32), np.array([np.iinfo(np.int32).min, 4], np.int32), 1, 1, 2)
     # the context stays usable
     assert list(ctx.linear(np.array([1, 2], np.int32), np.array([3, 4], np.int32), 1, 1, 2)) == [11]
+
+
+@pytest.mark.parametrize("rows,out,k", [(1, 128, 4096), (16, 1408, 4096), (5, 300, 1000)])
+def test_split_k_equals_one_block_per_tile(ctx, oracle, rows, out, k, monkeypatch):
+    """Few rows leave most SMs idle, so blocks share each tile's K range and add their partial sums atomically
+    (exact in any order); KTMOE_SPLITK=0 keeps one block per tile. Both must equal the CPU path."""
+    rng = np.random.default_rng(rows + out + k)
+    x = rng.integers(-WL, WL + 1, size=rows * k, dtype=np.int32)
+    w = rng.integers(-WL, WL + 1, size=out * k, dtype=np.int32)
+    want = oracle.linear(x, w, rows, out, k)
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KTMOE_SPLITK", flag)
+        got = ctx.linear(x, w, rows, out, k)
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, f"KTMOE_SPLITK={flag}: {bad.size} of {got.size} differ"

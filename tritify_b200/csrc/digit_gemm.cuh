@@ -61,6 +61,9 @@ struct GemmArgs {
     unsigned long long* rowmax;
     int rowmax_stride;
     int rowmax_split;
+    // Split K: k_splits > 1 blocks share a tile, each over its own K range, and add their partial results into `out`
+    // with 64-bit atomics (integer sums: exact in any order; `out` starts at zero; no fused row maxima).
+    int k_splits;
 };
 
 // TMEM columns to allocate for `accbn` = (buffers x BN): a power of two >= 32 covering five diagonals each.
@@ -212,9 +215,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int32_t (&r)[32]) {
 // m = (L mod per_group) / group_n of n-tile (L / per_group) · group_n + L mod group_n: the blocks resident at one time
 // walk group_n activation tiles for each weight tile, so both stay in L2 while they are reused.
 struct TileIter {
-    int per_group, limit, n_tiles;
-    __device__ __forceinline__ bool get(const GemmArgs& a, int L, int& tile, int& m0) const {
-        if (L >= limit) return false;
+    int per_group, limit, n_tiles;  // limit: slots of one K split
+    int splits;
+    __device__ __forceinline__ bool get(const GemmArgs& a, int L, int& tile, int& m0, int& split) const {
+        if (L >= limit * splits) return false;
+        split = L / limit;
+        L -= split * limit;
         const int grp = L / per_group, rem = L % per_group;
         tile = grp * a.group_n + rem % a.group_n;
         m0 = (rem / a.group_n) * BM;
@@ -257,8 +263,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     const int n_tiles = args.n_tiles ? *args.n_tiles : args.n_tiles_max;
     const int n_groups = (n_tiles + args.group_n - 1) / args.group_n;
-    const TileIter it{args.m_tiles * args.group_n, args.m_tiles * args.group_n * n_groups, n_tiles};
-    if ((int)blockIdx.x >= it.limit) return;  // no tile for this block: leave before any barrier or allocation
+    const int ks = args.k_splits > 1 ? args.k_splits : 1;
+    const TileIter it{args.m_tiles * args.group_n, args.m_tiles * args.group_n * n_groups, n_tiles, ks};
+    if ((int)blockIdx.x >= it.limit * ks) return;  // no tile for this block: leave before any barrier or allocation
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = args.num_k_blocks;
 
@@ -290,12 +297,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
             int q = 0;  // k-blocks issued by this block so far (its position in the stage ring)
             bool alive = true;
-            int tile, m0;
-            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0); L += gridDim.x) {
+            int tile, m0, split;
+            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0, split); L += gridDim.x) {
                 if (tile >= n_tiles) continue;
                 const TileInfo ti = tile_info(args, tile, BN);
                 if (ti.n_valid <= 0) continue;
-                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                const int kb1 = (int)((long long)(split + 1) * nkb / ks);
+                for (int kb = (int)((long long)split * nkb / ks); kb < kb1; ++kb, ++q) {
                     const int s = q % STAGES;
                     const uint32_t ph = (uint32_t)(q / STAGES) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, args.err, ERR_TIMEOUT_EMPTY)) {
@@ -323,8 +331,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             constexpr uint32_t id1 = idesc_i8(BN), id2 = idesc_i8(2 * BN), id3 = idesc_i8(3 * BN);
             int q = 0, tc = 0;
             bool alive = true;
-            int tile, m0;
-            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0); L += gridDim.x) {
+            int tile, m0, split;
+            for (int L = blockIdx.x; alive && it.get(args, L, tile, m0, split); L += gridDim.x) {
                 if (tile >= n_tiles) continue;
                 const TileInfo ti = tile_info(args, tile, BN);
                 if (ti.n_valid <= 0) continue;
@@ -332,7 +340,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS);
                 if (!mbar_wait(&acc_empty[b], ((uint32_t)(tc / ACC) & 1u) ^ 1u, args.err, ERR_TIMEOUT_ACCUM)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;");
-                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                const int kb0 = (int)((long long)split * nkb / ks), kb1 = (int)((long long)(split + 1) * nkb / ks);
+                for (int kb = kb0; kb < kb1; ++kb, ++q) {
                     const int s = q % STAGES;
                     const uint32_t ph = (uint32_t)(q / STAGES) & 1u;
                     if (!mbar_wait(&full[s], ph, args.err, ERR_TIMEOUT_FULL)) {
@@ -349,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint64_t a2 = smem_desc_sw128(a_base + 2 * C::A_PLANE + kk * UMMA_K);
                         const uint64_t b0 = smem_desc_sw128(b_base + 0 * C::B_PLANE + kk * UMMA_K);
                         const uint64_t b2 = smem_desc_sw128(b_base + 2 * C::B_PLANE + kk * UMMA_K);
-                        if (kb == 0 && kk == 0) {
+                        if (kb == kb0 && kk == 0) {
                             // first K step: every diagonal's first product overwrites, the others accumulate
                             umma_i8(acc + 0 * BN, a0, b0, id3, 0u);  // (0,0) (0,1) (0,2) -> diagonals 0, 1, 2
                             umma_i8(acc + 1 * BN, a1, b0, id2, 1u);  // (1,0) (1,1)       -> diagonals 1, 2
@@ -374,8 +383,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Epilogue: warp w reads TMEM lanes 32w..32w+31 (its lane quadrant); lane l holds weight row m0+32w+l.
         const bool do_max = args.rowmax != nullptr;
         int tc = 0;
-        int tile, m0;
-        for (int L = blockIdx.x; it.get(args, L, tile, m0); L += gridDim.x) {
+        int tile, m0, split;
+        for (int L = blockIdx.x; it.get(args, L, tile, m0, split); L += gridDim.x) {
             if (tile >= n_tiles) continue;
             const TileInfo ti = tile_info(args, tile, BN);
             if (ti.n_valid <= 0) continue;
@@ -417,8 +426,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const bool live = m_ok && n < ti.n_valid;
                     if (live) {
                         int64_t* p = args.out + (long long)(ti.row0 + n) * args.ld_out + m;
-                        if (args.accumulate) v += *p;
-                        *p = v;
+                        if (ks > 1) {
+                            atomicAdd((unsigned long long*)p, (unsigned long long)v);
+                        } else {
+                            if (args.accumulate) v += *p;
+                            *p = v;
+                        }
                     }
                     if (do_max) {
                         unsigned long long av = live ? (unsigned long long)(v >= 0 ? v : -v) : 0ull;
@@ -484,6 +497,39 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+    }
+}
+
+// Row maxima of an output written by a K-split launch (the fused epilogue reduction needs final values):
+// rowmax[r * stride + (m >= split)] = max |out[r][m]| over m < M_valid (stride 0: one or two words for the whole
+// output). One block per row (grid-stride); the words start at zero.
+static __global__ void rowmax_kernel(const int64_t* __restrict__ out, long long ld, int rows, int M_valid, int split,
+                              unsigned long long* __restrict__ rowmax, int stride) {
+    __shared__ unsigned long long red[2][32];
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        unsigned long long v[2] = {0ull, 0ull};
+        for (int m = threadIdx.x; m < M_valid; m += blockDim.x) {
+            const int64_t x = out[(long long)r * ld + m];
+            const unsigned long long a = (unsigned long long)(x >= 0 ? x : -x);
+            const int sl = m >= split ? 1 : 0;
+            v[sl] = a > v[sl] ? a : v[sl];
+        }
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long w = __shfl_xor_sync(0xffffffffu, v[sl], o);
+                v[sl] = w > v[sl] ? w : v[sl];
+            }
+            if ((threadIdx.x & 31) == 0) red[sl][threadIdx.x >> 5] = v[sl];
+        }
+        __syncthreads();
+        if (threadIdx.x < 2) {
+            unsigned long long m = 0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = red[threadIdx.x][w] > m ? red[threadIdx.x][w] : m;
+            if (m) atomicMax(rowmax + (long long)r * stride + threadIdx.x, m);
+        }
+        __syncthreads();
     }
 }
 

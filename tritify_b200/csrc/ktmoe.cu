@@ -97,6 +97,8 @@ struct ktmoe_ctx {
     int num_sms = 148;
     int pair_clusters = 0;  // co-resident clusters of the pair GEMM on this device (0: not yet queried)
     cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // the shared expert runs here, beside the routed experts
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
     int* d_err = nullptr;
     std::string last_error = "";
     uint64_t launches = 0;
@@ -236,10 +238,23 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
     const int64_t chunk_kb = dg::K_EXACT_MAX / dg::BK;
     if (g.rowmax && total_kb > chunk_kb) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "fused row max with a chunked K");
+    // Split K when the tiles cannot fill the SMs (small row counts): one output matrix (no groups), one K chunk, the
+    // one-SM kernel; the row maxima then come from a pass over the finished output. KTMOE_SPLITK=0 turns it off.
+    const int64_t slots = m_tiles * group_n * n_groups;
+    int ks = 1;
+    {
+        const char* e = getenv("KTMOE_SPLITK");
+        const bool single = !g.tile_group && !g.group_end && !g.tile_row_end && !g.n_tiles;
+        if (!(e && e[0] == '0') && !pair && single && total_kb <= chunk_kb && 2 * slots <= ctx->num_sms) {
+            ks = (int)std::min<int64_t>({ctx->num_sms / slots, total_kb / 2, 16});
+            if (ks < 2) ks = 1;
+        }
+    }
+    if (ks > 1) CK(cudaMemsetAsync(g.out, 0, (size_t)g.single_rows * g.ld_out * 8, st));
     // persistent: at most one block per SM walks the tile raster
-    dim3 grid((unsigned)std::min<int64_t>(m_tiles * group_n * n_groups, ctx->num_sms));
+    dim3 grid((unsigned)std::min<int64_t>(slots * ks, ctx->num_sms));
     for (int64_t kb0 = 0; kb0 < total_kb; kb0 += chunk_kb) {
-        dg::GemmArgs a;
+        dg::GemmArgs a{};
         a.out = g.out;
         a.ld_out = g.ld_out;
         a.M_valid = (int)g.M_valid;
@@ -258,9 +273,10 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.single_rows = (int)g.single_rows;
         a.accumulate = kb0 > 0 ? 1 : 0;
         a.err = ctx->d_err;
-        a.rowmax = g.rowmax;
+        a.rowmax = ks > 1 ? nullptr : g.rowmax;
         a.rowmax_stride = g.rowmax_stride;
         a.rowmax_split = (int)std::min<int64_t>(g.rowmax_split, INT32_MAX);
+        a.k_splits = ks;
         if (pair) {
             r = launch_gemm_pair(ctx, st, ma, mb, m_tiles * group_n * n_groups, a);
             if (r) return r;
@@ -274,6 +290,12 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
             default: return fail(ctx, KTMOE_ERR_ARG, "unsupported BN");
         }
         if (r) return r;
+    }
+    if (ks > 1 && g.rowmax) {
+        dg::rowmax_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(g.single_rows, ctx->num_sms * 4)), 256, 0,
+                            st>>>(g.out, g.ld_out, (int)g.single_rows, (int)g.M_valid,
+                                  (int)std::min<int64_t>(g.rowmax_split, INT32_MAX), g.rowmax, g.rowmax_stride);
+        CKL(ctx);
     }
     return KTMOE_OK;
 }
@@ -1021,136 +1043,12 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     return KTMOE_OK;
 }
 
-int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
-                  cudaStream_t st) {
+// The shared expert on the whole tensor (layers.rs:758-780; its QuantLinears see the whole [rows, dim] input, so its
+// maxima are global): everything up to the down accumulators and their max, on stream `st`.
+int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
-    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
-    const int64_t R = T * K;
-    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
-    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
-    MARK(L, st);
-    if (T > 0) {
-        if (int r = stage_route(L, T, x_dev, xs_dev, st)) return r;
-    }
-    MARK(L, st);
-
-    int64_t T_total = T, tok_offset = 0;
-    if (L->world == 1) {
-        const int BN = pick_bn((double)R / (double)E, true);
-        const int BN2 = pick_bn_long_k((double)R / (double)E, f, true);
-        if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
-        MARK(L, st);
-        ExpertRows xr;
-        xr.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
-        xr.n_rows = R;
-        xr.BN = BN;
-        xr.BN2 = BN2;
-        xr.grid_a = (R + BN - 1) / BN + E;
-        xr.grid_b = (R + BN2 - 1) / BN2 + E;
-        xr.tg_a = L->tile_group.as<int>();
-        xr.tr_a = L->tile_row0.as<int>();
-        xr.te_a = nullptr;
-        xr.nt_a = n_tiles_ptr(L);
-        xr.tg_b = L->tile_group2.as<int>();
-        xr.tr_b = L->tile_row02.as<int>();
-        xr.te_b = nullptr;
-        xr.nt_b = n_tiles2_ptr(L);
-        xr.group_end = L->group_end.as<int>();
-        xr.row_assign = L->row_assign.as<int>();
-        xr.row_expert = L->row_expert.as<int>();
-        xr.row_sqx = L->tok_sqx.as<Scale>();
-        if (int r = run_experts(L, xr, st)) return r;
-        MARK(L, st);
-        mk::CombineArgs ca;
-        ca.acc_d = L->acc_d.as<int64_t>();
-        ca.ymax_d = L->rowmax_d.as<unsigned long long>();
-        ca.row_cd = L->row_cd.as<Scale>();
-        ca.slot_row = L->slot_row.as<int>();
-        ca.top_ec = L->top_ec.as<int64_t>();
-        ca.sumc = L->sumc.as<int64_t>();
-        ca.T = (int)T;
-        ca.top_k = (int)K;
-        ca.dim = (int)d;
-        ca.out = L->tok_out.as<int32_t>();
-        ca.out_scale = L->tok_scale.as<Scale>();
-        const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
-                                 L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
-        mk::combine_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
-        CKL(ctx);
-        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        CKL(ctx);
-        MARK(L, st);
-    } else if (L->peer.on) {
-        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);
-        CKL(ctx);
-        if (int r = ep_routed_peer(L, T, st)) return r;
-        T_total = -1;  // on the device (peer.tok_info): the merge kernels read it there
-    } else {
-        if (int r = ep_routed(L, T, st)) return r;
-        T_total = L->ep_tok_total;
-        tok_offset = L->ep_tok_offset;
-    }
-    const int* tok_info = L->peer.on ? L->peer.tok_info.as<int>() : nullptr;  // [0] first token, [1] tokens
-
-    // merge (layers.rs:1001-1019): one common scale and one gmax over all the layer's tokens, on every rank
-    int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
-    Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
-    if (T_total == 1) {
-        if (T == 1) {
-            mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(
-                L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)d, routed, routed_scale);
-            CKL(ctx);
-        }
-    } else {
-        if (L->world == 1) {
-            mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON),
-                                                        nullptr);
-            CKL(ctx);
-        } else {
-            CK(L->ep_rec.ensure(3 * 8));
-            CK(L->ep_recs.ensure(L->world * 3 * 8));
-            CK(L->ep_best_idx.ensure(4));
-            if (T > 0) {
-                mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
-                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
-                                                            tok_info);
-                CKL(ctx);
-                mk::scale_record_kernel<<<1, 1, 0, st>>>(scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
-                                                         L->ep_rec.as<int64_t>());
-                CKL(ctx);
-            } else {
-                mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
-                CKL(ctx);
-            }
-            if (L->peer.on) {
-                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->ep_rec.as<unsigned long long>(),
-                                                      3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
-                CKL(ctx);
-            } else {
-                NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
-            }
-            mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, scal_scale(L, SL_COMMON));
-            CKL(ctx);
-        }
-        if (T > 0) {
-            mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
-                                                            (int)T, (int)d, scal_scale(L, SL_COMMON),
-                                                            scal_u64(L, U_MERGE_GMAX));
-            CKL(ctx);
-        }
-        if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st, ep::P_MERGE)) return r;
-        if (T > 0) {
-            mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
-                                                              (int)T, (int)d, scal_scale(L, SL_COMMON),
-                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale,
-                                                              tok_info ? tok_info + 1 : nullptr);
-            CKL(ctx);
-        }
-    }
-    MARK(L, st);
-    if (fs == 0) return KTMOE_OK;
-
-    // shared expert on the whole tensor (global maxima), then add(routed, shared)
+    const int64_t d = L->d, fs = L->fs;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64);
     const int64_t n = T * d;
     const unsigned red_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
     if (T > 0) {
@@ -1225,6 +1123,157 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         if (int r = run_gemm(ctx, st, s)) return r;
     }
     if (int r = allreduce_max(L, scal_u64(L, U_SYD), 1, st, ep::P_SYD)) return r;
+    return KTMOE_OK;
+}
+
+int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
+                  cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
+    const int64_t R = T * K;
+    const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
+    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
+    if (L->peer.on) {
+        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);  // a new forward for every exchange below
+        CKL(ctx);
+    }
+    // the shared expert depends only on x: it runs on the side stream while the routed experts run on st (not with
+    // per-stage timing, and not with the NCCL exchange, whose collectives must keep one order on every rank)
+    const bool side_shared = fs > 0 && !L->timing && (L->world == 1 || L->peer.on);
+    if (side_shared) {
+        CK(cudaEventRecord(ctx->ev_fork, st));
+        CK(cudaStreamWaitEvent(ctx->side, ctx->ev_fork, 0));
+        if (int r = shared_expert(L, T, x_dev, xs_dev, ctx->side)) return r;
+        CK(cudaEventRecord(ctx->ev_join, ctx->side));
+    }
+    MARK(L, st);
+    if (T > 0) {
+        if (int r = stage_route(L, T, x_dev, xs_dev, st)) return r;
+    }
+    MARK(L, st);
+
+    int64_t T_total = T, tok_offset = 0;
+    if (L->world == 1) {
+        const int BN = pick_bn((double)R / (double)E, true);
+        const int BN2 = pick_bn_long_k((double)R / (double)E, f, true);
+        if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
+        MARK(L, st);
+        ExpertRows xr;
+        xr.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
+        xr.n_rows = R;
+        xr.BN = BN;
+        xr.BN2 = BN2;
+        xr.grid_a = (R + BN - 1) / BN + E;
+        xr.grid_b = (R + BN2 - 1) / BN2 + E;
+        xr.tg_a = L->tile_group.as<int>();
+        xr.tr_a = L->tile_row0.as<int>();
+        xr.te_a = nullptr;
+        xr.nt_a = n_tiles_ptr(L);
+        xr.tg_b = L->tile_group2.as<int>();
+        xr.tr_b = L->tile_row02.as<int>();
+        xr.te_b = nullptr;
+        xr.nt_b = n_tiles2_ptr(L);
+        xr.group_end = L->group_end.as<int>();
+        xr.row_assign = L->row_assign.as<int>();
+        xr.row_expert = L->row_expert.as<int>();
+        xr.row_sqx = L->tok_sqx.as<Scale>();
+        if (int r = run_experts(L, xr, st)) return r;
+        MARK(L, st);
+        mk::CombineArgs ca;
+        ca.acc_d = L->acc_d.as<int64_t>();
+        ca.ymax_d = L->rowmax_d.as<unsigned long long>();
+        ca.row_cd = L->row_cd.as<Scale>();
+        ca.slot_row = L->slot_row.as<int>();
+        ca.top_ec = L->top_ec.as<int64_t>();
+        ca.sumc = L->sumc.as<int64_t>();
+        ca.T = (int)T;
+        ca.top_k = (int)K;
+        ca.dim = (int)d;
+        ca.out = L->tok_out.as<int32_t>();
+        ca.out_scale = L->tok_scale.as<Scale>();
+        const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
+                                 L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
+        mk::combine_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
+        CKL(ctx);
+        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+        CKL(ctx);
+        MARK(L, st);
+    } else if (L->peer.on) {
+        if (int r = ep_routed_peer(L, T, st)) return r;
+        T_total = -1;  // on the device (peer.tok_info): the merge kernels read it there
+    } else {
+        if (int r = ep_routed(L, T, st)) return r;
+        T_total = L->ep_tok_total;
+        tok_offset = L->ep_tok_offset;
+    }
+    const int* tok_info = L->peer.on ? L->peer.tok_info.as<int>() : nullptr;  // [0] first token, [1] tokens
+
+    // merge (layers.rs:1001-1019): one common scale and one gmax over all the layer's tokens, on every rank
+    int32_t* routed = fs > 0 ? L->y_routed.as<int32_t>() : y_dev;
+    Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
+    if (T_total == 1) {
+        if (T == 1) {
+            mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(
+                L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)d, routed, routed_scale);
+            CKL(ctx);
+        }
+    } else {
+        if (L->world == 1) {
+            mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON),
+                                                        nullptr);
+            CKL(ctx);
+        } else {
+            CK(L->ep_rec.ensure(3 * 8));
+            CK(L->ep_recs.ensure(L->world * 3 * 8));
+            CK(L->ep_best_idx.ensure(4));
+            if (T > 0) {
+                mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
+                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
+                                                            tok_info);
+                CKL(ctx);
+                mk::scale_record_kernel<<<1, 1, 0, st>>>(scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
+                                                         L->ep_rec.as<int64_t>());
+                CKL(ctx);
+            } else {
+                mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
+                CKL(ctx);
+            }
+            if (L->peer.on) {
+                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->ep_rec.as<unsigned long long>(),
+                                                      3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
+                CKL(ctx);
+            } else {
+                NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
+            }
+            mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, scal_scale(L, SL_COMMON));
+            CKL(ctx);
+        }
+        if (T > 0) {
+            mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                                                            (int)T, (int)d, scal_scale(L, SL_COMMON),
+                                                            scal_u64(L, U_MERGE_GMAX));
+            CKL(ctx);
+        }
+        if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st, ep::P_MERGE)) return r;
+        if (T > 0) {
+            mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                                                              (int)T, (int)d, scal_scale(L, SL_COMMON),
+                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale,
+                                                              tok_info ? tok_info + 1 : nullptr);
+            CKL(ctx);
+        }
+    }
+    MARK(L, st);
+    if (fs == 0) return KTMOE_OK;
+
+    // add(routed, shared) (layers.rs:121-136), after the shared expert (run here, or beside the routed experts)
+    if (side_shared) {
+        CK(cudaStreamWaitEvent(st, ctx->ev_join, 0));
+    } else if (int r = shared_expert(L, T, x_dev, xs_dev, st)) {
+        return r;
+    }
+    const int64_t n = T * d;
+    const unsigned red_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
     // a rank without tokens still needs the shared down c for nothing: only ranks with rows produce output
     mk::AddArgs aa;
     aa.a = routed;
@@ -1380,6 +1429,12 @@ int ktmoe_open(int device, ktmoe_ctx** out) {
         delete ctx;
         return KTMOE_ERR_CUDA;
     }
+    if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess) {
+        delete ctx;
+        return KTMOE_ERR_CUDA;
+    }
     cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
     size_t free_b = 0, total_b = 0;
     cudaMemGetInfo(&free_b, &total_b);
@@ -1404,6 +1459,9 @@ int ktmoe_close(ktmoe_ctx* ctx) {
     ctx->lin_bad.release();
     cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->stream);
+    if (ctx->side) cudaStreamDestroy(ctx->side);
+    if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
+    if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
     delete ctx;
     return KTMOE_OK;
 }
