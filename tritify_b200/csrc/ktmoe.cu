@@ -949,7 +949,11 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         ca.dim = (int)d;
         ca.out = L->tok_out.as<int32_t>();
         ca.out_scale = L->tok_scale.as<Scale>();
-        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
+                                 L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
+        mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
+        CKL(ctx);
+        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
         CKL(ctx);
     }
     MARK(L, st);
@@ -1036,7 +1040,11 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         ca.dim = (int)d;
         ca.out = L->tok_out.as<int32_t>();
         ca.out_scale = L->tok_scale.as<Scale>();
-        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca);
+        const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
+                                 L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
+        mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
+        CKL(ctx);
+        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
         CKL(ctx);
     }
     MARK(L, st);

@@ -1023,69 +1023,102 @@ struct CombineYArgs {
     Scale* out_scale;
 };
 
-__global__ void combine_y_kernel(const CombineYArgs a) {
+// One thread per token: the plan of combine from expert outputs given as IntTensors (their scales are final, so each
+// live slot needs only its rescale to the common scale); the same CombinePlan layout (ry unused).
+__global__ void combine_y_plan_kernel(const CombineYArgs a, const CombinePlan p) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= a.T) return;
+    const int K = a.top_k;
+    if (a.sumc[t] <= 0) {
+        p.n[t] = -1;
+        return;
+    }
+    Scale common = kt::scale_zero();
+    for (int i = 0; i < K; ++i) {
+        const Scale ys = a.ys[a.slot_row[(long long)t * K + i]];
+        if (kt::scale_ge(ys, common)) common = ys;
+    }
+    if (common.mant == 0) {
+        p.n[t] = -1;
+        return;
+    }
+    const Scale cinv = kt::scale_recip(common);
+    int n = 0;
+    for (int i = 0; i < K; ++i) {
+        const int row = a.slot_row[(long long)t * K + i];
+        const Scale ys = a.ys[row];
+        if (ys.mant == 0) continue;
+        const long long o = (long long)t * K + n;
+        p.row[o] = row;
+        p.ec[o] = a.top_ec[(long long)t * K + i];
+        p.f[o] = kt::make_apply(kt::scale_mul(ys, cinv));
+        ++n;
+    }
+    p.n[t] = n;
+    p.common[t] = common;
+}
+
+// combine (layers.rs:893-923) from expert outputs given as IntTensors (y rows + scales), row = slot_row[t·K + i]: one
+// block per token from its plan, each thread CE elements per chunk, one slot's plan at a time.
+__global__ void __launch_bounds__(256, 3) combine_y_kernel(const CombineYArgs a, const CombinePlan p) {
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
     __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
-    __shared__ Scale common_s;
     __shared__ int64_t ec_s[COMBINE_MAX_K];
     __shared__ int row_s[COMBINE_MAX_K];
-    __shared__ int live_s;
     const int t = blockIdx.x;
     if (t >= a.T) return;
-    const int K = a.top_k, D = a.dim;
+    const int D = a.dim;
     int32_t* o = a.out + (long long)t * D;
-    const int64_t sumc = a.sumc[t];
-    if (sumc <= 0) {
+    const int n = p.n[t];
+    if (n < 0) {
         for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
         if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
         return;
     }
-    if (threadIdx.x == 0) {
-        Scale ys[COMBINE_MAX_K];
-        Scale common = kt::scale_zero();
-        for (int i = 0; i < K; ++i) {
-            row_s[i] = a.slot_row[(long long)t * K + i];
-            ec_s[i] = a.top_ec[(long long)t * K + i];
-            ys[i] = a.ys[row_s[i]];
-            if (kt::scale_ge(ys[i], common)) common = ys[i];
-        }
-        common_s = common;
-        int n = 0;
-        if (common.mant != 0) {
-            const Scale cinv = kt::scale_recip(common);
-            for (int i = 0; i < K; ++i) {
-                if (ys[i].mant == 0) continue;
-                f_s[n] = kt::make_apply(kt::scale_mul(ys[i], cinv));
-                row_s[n] = row_s[i];
-                ec_s[n] = ec_s[i];
-                ++n;
-            }
-        }
-        live_s = n;
+    const int K = a.top_k;
+    if ((int)threadIdx.x < n) {
+        const long long q = (long long)t * K + threadIdx.x;
+        row_s[threadIdx.x] = p.row[q];
+        ec_s[threadIdx.x] = p.ec[q];
+        f_s[threadIdx.x] = p.f[q];
     }
     __syncthreads();
-    const Scale common = common_s;
-    if (common.mant == 0) {
-        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = 0;
-        if (threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
-        return;
-    }
-    const int n = live_s;
     uint64_t gm = 0;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        int64_t s = 0;
-        for (int i = 0; i < n; ++i) s += ec_s[i] * kt::apply_row(f_s[i], a.y[(long long)row_s[i] * D + d]);
-        acc_s[d] = s;
-        gm = max(gm, uabs64(s));
+    for (int d0 = threadIdx.x; d0 < D; d0 += CE * blockDim.x) {
+        int64_t acc[CE];
+#pragma unroll
+        for (int u = 0; u < CE; ++u) acc[u] = 0;
+        for (int j = 0; j < n; ++j) {
+            const kt::ApplyPlan f = f_s[j];
+            const int64_t ec = ec_s[j];
+            const int32_t* b = a.y + (long long)row_s[j] * D;
+            int32_t v[CE];
+#pragma unroll
+            for (int u = 0; u < CE; ++u) {
+                const int d = d0 + u * blockDim.x;
+                v[u] = d < D ? __ldg(b + d) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, v[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < CE; ++u) {
+            const int d = d0 + u * blockDim.x;
+            if (d < D) {
+                acc_s[d] = acc[u];
+                gm = max(gm, uabs64(acc[u]));
+            }
+        }
     }
     gm = block_max_u64(gm, red);
     const int64_t gmax = (int64_t)gm;
     const kt::ReqDiv rg = kt::make_req(gmax);
     for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
     if (threadIdx.x == 0) {
+        const int64_t sumc = a.sumc[t];
         a.out_scale[t] = gmax == 0 ? kt::scale_zero()
-                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common),
+                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), p.common[t]),
                                                    kt::from_ratio(1, (kt::u128)(uint64_t)sumc));
     }
 }
