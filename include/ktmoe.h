@@ -132,6 +132,18 @@ int ktmoe_forward_dev(ktmoe_layer* layer, const int32_t* x_dev, int64_t rows, co
                       int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream);
 /* Wait for the context's stream (and `stream` if not NULL); reports a kernel error word if one was raised. */
 int ktmoe_sync(ktmoe_ctx* ctx, void* stream);
+/* The FFN half of a decoder block with this layer as its FFN (crates/01-engine/kt-core/src/model.rs:175-181):
+ * y = add(x, moe(rms_norm(x))), the RmsNorm of layers.rs:352-449 and the residual add of layers.rs:121-136, each
+ * reduction over the whole tensor (over every rank's rows with expert parallelism). The norm's weight codes and
+ * scale come from ktmoe_quantize_weights (RmsNorm::new quantises like QuantLinear::from_weights), eps as
+ * ktmoe_scale_from_f64(eps). Host and device entry points as for the layer. */
+int ktmoe_layer_set_norm(ktmoe_layer* layer, const int32_t* w_codes, ktmoe_scale w_scale, ktmoe_scale eps_scale);
+int ktmoe_block_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                        ktmoe_scale* y_scale);
+int ktmoe_block_forward_dev(ktmoe_layer* layer, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
+                            int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream);
+/* Scale::from_f64 (crates/00-kernels/kt-int/src/lib.rs:215-222), for offline constants such as a norm's eps. */
+int ktmoe_scale_from_f64(double x, ktmoe_scale* out);
 /* MoeMlp::route for each row: experts [rows][top_k] (top-k order), ec [rows][top_k] codes, sumc [rows]. */
 int ktmoe_route(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* experts,
                 int64_t* ec, int64_t* sumc);

@@ -164,6 +164,22 @@ struct Scale {
         Scale r = from_ratio((u128)1 << 40, (u128)(uint64_t)mant);
         return Scale{r.mant, r.shift - shift + 40};
     }
+
+    // lib.rs:285-303
+    Scale add(Scale o) const {
+        if (mant == 0) return o;
+        if (o.mant == 0) return *this;
+        const int32_t s = std::max(shift, o.shift);
+        const uint32_t da = (uint32_t)(s - shift), db = (uint32_t)(s - o.shift);
+        if (da >= 96) return *this;
+        if (db >= 96) return o;
+        const u128 sum = ((u128)(uint64_t)mant << da) + ((u128)(uint64_t)o.mant << db);
+        const Scale fr = from_ratio(sum, 1);
+        return Scale{fr.mant, fr.shift + s};
+    }
+
+    // lib.rs:307-318 (defined after isqrt_u128)
+    Scale rsqrt() const;
 };
 
 // lib.rs:327-340
@@ -176,6 +192,19 @@ static u128 isqrt_u128(u128 n) {
         if (y >= x) return x;
         x = y;
     }
+}
+
+Scale Scale::rsqrt() const {
+    if (mant <= 0) std::abort();  // the reference asserts mant > 0
+    u128 m = (u128)(uint64_t)mant;
+    int32_t s = shift;
+    if (s & 1) {
+        m <<= 1;
+        s += 1;
+    }
+    const uint32_t k = 31;
+    const u128 r = isqrt_u128(m << (2 * k));
+    return Scale{(int64_t)r, (int32_t)k + s / 2}.recip();
 }
 
 // lib.rs:346-396 — CodeLut: a pointwise nonlinearity tabulated as integer codes.
@@ -349,6 +378,66 @@ static IntTensor add(const IntTensor& a, const IntTensor& b) {
 }
 
 // layers.rs:211-328 — QuantLinear.
+// crates/01-engine/kt-core/src/layers.rs:352-449 — RmsNorm: per row C_r = x.scale·rsqrt(mean(x²)+eps)·w_scale and
+// p = x_i·wcode_i (integer); rows to the common (last largest) C, then one dynamic requant of the whole tensor.
+struct RmsNorm {
+    size_t dim = 0;
+    std::vector<int32_t> wcodes;
+    Scale w_scale, eps_scale;
+
+    RmsNorm(const float* weight, size_t dim_, double eps) : dim(dim_) {
+        double peak = 0.0;
+        for (size_t i = 0; i < dim; ++i) peak = std::max(peak, std::fabs((double)weight[i]));
+        wcodes.assign(dim, 0);
+        if (peak == 0.0) {
+            w_scale = Scale::zero();
+        } else {
+            const double step = peak / (double)WLEVELS;
+            w_scale = Scale::from_f64(step);
+            for (size_t i = 0; i < dim; ++i) {
+                int64_t c = (int64_t)std::round((double)weight[i] / step);
+                wcodes[i] = (int32_t)std::max<int64_t>(-WLEVELS, std::min<int64_t>(WLEVELS, c));
+            }
+        }
+        eps_scale = Scale::from_f64(eps);
+    }
+
+    IntTensor forward_int(const IntTensor& x) const {
+        const size_t rows = x.data.size() / dim;
+        std::vector<int64_t> p(x.data.size());
+        std::vector<Scale> c(rows);
+        for (size_t r = 0; r < rows; ++r) {
+            const int32_t* xr = x.data.data() + r * dim;
+            i128 ss = 0;
+            for (size_t i = 0; i < dim; ++i) ss += (i128)xr[i] * (i128)xr[i];
+            const Scale mean_sq = Scale::from_ratio((u128)ss, (u128)dim).mul(x.scale).mul(x.scale);
+            const Scale denom = mean_sq.add(eps_scale);
+            const Scale inv = denom.mant == 0 ? Scale::zero() : denom.rsqrt();
+            c[r] = x.scale.mul(inv).mul(w_scale);
+            for (size_t i = 0; i < dim; ++i) p[r * dim + i] = (int64_t)xr[i] * (int64_t)wcodes[i];
+        }
+        Scale common = Scale::zero();
+        for (size_t r = 0; r < rows; ++r)
+            if (c[r].ge(common)) common = c[r];
+        if (common.mant == 0) return zeros(x.data.size(), x.shape);
+        const Scale cinv = common.recip();
+        std::vector<int64_t> v(x.data.size());
+        int64_t gmax = 0;
+        for (size_t r = 0; r < rows; ++r) {
+            const Scale f = c[r].mul(cinv);
+            for (size_t i = 0; i < dim; ++i) {
+                v[r * dim + i] = f.apply(p[r * dim + i]);
+                gmax = std::max(gmax, v[r * dim + i] < 0 ? -v[r * dim + i] : v[r * dim + i]);
+            }
+        }
+        if (gmax == 0) return zeros(x.data.size(), x.shape);
+        IntTensor out{std::vector<int32_t>(x.data.size()), x.shape,
+                      Scale::from_ratio((u128)gmax, (u128)ACT_LEVELS).mul(common)};
+        for (size_t i = 0; i < v.size(); ++i) out.data[i] = requant_dyn(v[i], ACT_LEVELS, gmax);
+        return out;
+    }
+};
+
 struct QuantLinear {
     size_t out_features = 0, in_features = 0;
     std::vector<int32_t> w_codes;
@@ -940,6 +1029,23 @@ void ko_moe_expert(void* p, size_t e, const int32_t* x, ko_scale xs, int32_t* y,
 }
 
 // add (layers.rs:121-136) on two equal-length tensors.
+// RmsNorm (layers.rs:352-449) built from f32 weights and eps, applied to rows x dim codes.
+void ko_rmsnorm(const float* weight, size_t dim, double eps, const int32_t* x, size_t rows, ko_scale xs, int32_t* y,
+                ko_scale* ys, int32_t* wcodes, ko_scale* w_scale, ko_scale* eps_scale) {
+    RmsNorm nrm(weight, dim, eps);
+    IntTensor t{std::vector<int32_t>(x, x + rows * dim), {rows, dim}, from_c(xs)};
+    IntTensor o = nrm.forward_int(t);
+    std::copy(o.data.begin(), o.data.end(), y);
+    *ys = to_c(o.scale);
+    if (wcodes) std::copy(nrm.wcodes.begin(), nrm.wcodes.end(), wcodes);
+    if (w_scale) *w_scale = to_c(nrm.w_scale);
+    if (eps_scale) *eps_scale = to_c(nrm.eps_scale);
+}
+
+ko_scale ko_scale_add(ko_scale a, ko_scale b) { return to_c(from_c(a).add(from_c(b))); }
+ko_scale ko_scale_rsqrt(ko_scale a) { return to_c(from_c(a).rsqrt()); }
+ko_scale ko_scale_from_f64(double x) { return to_c(Scale::from_f64(x)); }
+
 void ko_add(const int32_t* a, ko_scale as, const int32_t* b, ko_scale bs, size_t n, int32_t* y, ko_scale* ys) {
     IntTensor ta{std::vector<int32_t>(a, a + n), {n}, from_c(as)}, tb{std::vector<int32_t>(b, b + n), {n}, from_c(bs)};
     IntTensor o = add(ta, tb);

@@ -79,6 +79,11 @@ def lib():
             "ko_moe_router_logits": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_expert": ([ctypes.c_void_p, sz, i32p, KoScale, i32p, p(KoScale)], None),
             "ko_add": ([i32p, KoScale, i32p, KoScale, sz, i32p, p(KoScale)], None),
+            "ko_rmsnorm": ([f32p, sz, ctypes.c_double, i32p, sz, KoScale, i32p, p(KoScale), i32p, p(KoScale),
+                            p(KoScale)], None),
+            "ko_scale_add": ([KoScale, KoScale], KoScale),
+            "ko_scale_rsqrt": ([KoScale], KoScale),
+            "ko_scale_from_f64": ([ctypes.c_double], KoScale),
         }
         for name, (args, res) in sigs.items():
             f = getattr(L, name)
@@ -297,3 +302,28 @@ def add(a, a_s, b, b_s):
     lib().ko_add(_p(a, ctypes.c_int32), S(a_s), _p(b, ctypes.c_int32), S(b_s), a.size, _p(y, ctypes.c_int32),
                  ctypes.byref(s))
     return y, s.tup()
+
+
+def scale_add(a, b):
+    """Scale::add (kt-int lib.rs:285-303)."""
+    return lib().ko_scale_add(S(a), S(b)).tup()
+
+
+def scale_rsqrt(a):
+    """Scale::rsqrt (kt-int lib.rs:307-318), mant > 0."""
+    return lib().ko_scale_rsqrt(S(a)).tup()
+
+
+def rmsnorm(weight: np.ndarray, eps: float, x: np.ndarray, xs):
+    """RmsNorm::new(weight, eps).forward_int (layers.rs:352-449) on rows of x codes: (y, y_scale, wcodes, w_scale,
+    eps_scale)."""
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    dim = w.size
+    rows = x.size // dim
+    y = np.empty(x.size, np.int32)
+    wc = np.empty(dim, np.int32)
+    ys, ws, es = KoScale(), KoScale(), KoScale()
+    lib().ko_rmsnorm(_p(w, ctypes.c_float), dim, float(eps), _p(x, ctypes.c_int32), rows, S(xs), _p(y, ctypes.c_int32),
+                     ctypes.byref(ys), _p(wc, ctypes.c_int32), ctypes.byref(ws), ctypes.byref(es))
+    return y.reshape(x.shape), ys.tup(), wc, ws.tup(), es.tup()

@@ -56,3 +56,17 @@ int64_t fp_apply_row(fp_scale s, int64_t v) { return kt::apply_row(kt::make_appl
 extern "C" {
 int64_t fp_apply_row32(fp_scale s, int32_t v) { return kt::apply_row(kt::make_apply(S(s)), v); }
 }
+
+extern "C" {
+fp_scale fp_scale_add(fp_scale a, fp_scale b) { return C(kt::scale_add(S(a), S(b))); }
+fp_scale fp_scale_rsqrt(fp_scale a) { return C(kt::scale_rsqrt(S(a))); }
+void fp_isqrt(uint64_t hi, uint64_t lo, uint64_t* out_hi, uint64_t* out_lo) {
+    const kt::u128 r = kt::isqrt_u128(((kt::u128)hi << 64) | lo);
+    *out_hi = (uint64_t)(r >> 64);
+    *out_lo = (uint64_t)r;
+}
+}
+
+extern "C" {
+int64_t fp_apply_row_wide(fp_scale s, int64_t v) { return kt::apply_row_wide(kt::make_apply(S(s)), v); }
+}

@@ -227,3 +227,36 @@ def test_apply_row_on_int32_values(fp, oracle):
                        oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
         for val in (int(next(g) % (1 << 32)) - (1 << 31), -(1 << 31), (1 << 31) - 1, 0, -1, 1):
             assert fp.fp_apply_row32(FpScale(*s), val) == oracle.apply(s, val)
+
+
+def test_scale_add_rsqrt_isqrt_equal_the_oracle(fp, oracle):
+    fp.fp_scale_add.argtypes = [FpScale, FpScale]
+    fp.fp_scale_add.restype = FpScale
+    fp.fp_scale_rsqrt.argtypes = [FpScale]
+    fp.fp_scale_rsqrt.restype = FpScale
+    P = ctypes.POINTER
+    fp.fp_isqrt.argtypes = [ctypes.c_uint64, ctypes.c_uint64, P(ctypes.c_uint64), P(ctypes.c_uint64)]
+    g = _lcg(31)
+    for _ in range(20000):
+        a = oracle.from_ratio(next(g) % (1 << 62) + 1, next(g) % (1 << 40) + 1)
+        b = oracle.from_ratio(next(g) % (1 << 50) + 1, next(g) % (1 << 60) + 1)
+        r = fp.fp_scale_add(FpScale(*a), FpScale(*b))
+        assert (r.mant, r.shift) == oracle.scale_add(a, b)
+        r = fp.fp_scale_rsqrt(FpScale(*a))
+        assert (r.mant, r.shift) == oracle.scale_rsqrt(a)
+        n = (next(g) << 64) | next(g)
+        hi, lo = ctypes.c_uint64(), ctypes.c_uint64()
+        fp.fp_isqrt(n >> 64, n & ((1 << 64) - 1), ctypes.byref(hi), ctypes.byref(lo))
+        assert (hi.value << 64) | lo.value == oracle.isqrt_u128(n)
+    assert oracle.scale_add((0, 0), (5, 3)) == (5, 3)
+
+
+def test_apply_row_wide_equals_the_oracle(fp, oracle):
+    fp.fp_apply_row_wide.argtypes = [FpScale, ctypes.c_int64]
+    fp.fp_apply_row_wide.restype = ctypes.c_int64
+    g = _lcg(41)
+    for _ in range(40000):
+        s = oracle.mul(oracle.from_ratio(next(g) % (1 << 60) + 1, next(g) % (1 << 60) + 1),
+                       oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
+        val = int(next(g) % (1 << 50)) - (1 << 49)
+        assert fp.fp_apply_row_wide(FpScale(*s), val) == oracle.apply(s, val)

@@ -67,6 +67,12 @@ def _worker(rank, world, port, name, mode, transport, outdir):
     if c.shared:
         s = m.shared
         dev.set_shared((s.gate.w_codes, s.gate.w_scale), (s.up.w_codes, s.up.w_scale), (s.down.w_codes, s.down.w_scale))
+    block = mode.endswith(":block")
+    mode = mode.split(":")[0]
+    if block:
+        import test_gpu_block as tgb
+
+        tgb.set_norm(dev, c)
     x = tb.IntTensor.from_reals(cases.make_x(c))
     sizes = _splits(c.T, world, mode)
     start = sum(sizes[:rank])
@@ -77,7 +83,7 @@ def _worker(rank, world, port, name, mode, transport, outdir):
     if transport == "peer_graphs":
         dev.set_graphs(True)
     for rep in range(3):  # the later forwards reuse every buffer (and, over peer memory, the flags)
-        y, ys = dev.forward(xr, rows, x.scale)
+        y, ys = dev.forward(xr, rows, x.scale, block=block)
     np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=y, mant=ys.mant, shift=ys.shift, rows=rows)
     dev = None
     ctx.sync()
@@ -110,3 +116,33 @@ def test_expert_parallel_equals_one_gpu(tmp_path, name, mode, transport):
     assert len(scales) == 1, f"ranks disagree on the output scale: {scales}"
     y = np.concatenate(ys)
     assert cases.out_hashes(y, scales.pop()) == GOLDEN["cases"][name]["output"]
+
+
+@pytest.mark.parametrize("transport", ["nccl", "peer", "peer_graphs"])
+@pytest.mark.parametrize("name,mode", [("small_shared_softmax", "even"), ("tiny_sigmoid_shared", "first_empty")])
+def test_expert_parallel_block_equals_the_oracle(tmp_path, oracle, name, mode, transport):
+    """The block x + moe(rms_norm(x)) with the layer's experts spread over the GPUs: the norm's common scale and
+    maxima and the residual add's maximum span every rank's rows."""
+    import torch
+    import torch.multiprocessing as mp
+
+    import test_gpu_block as tgb
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("expert parallelism needs two or more GPUs")
+    c = cases.CASES[name]
+    world = min(world, c.E)
+    if mode == "first_empty" and c.T < world - 1:
+        world = 2
+    mp.spawn(_worker, args=(world, _free_port(), name, mode + ":block", transport, str(tmp_path)), nprocs=world,
+             join=True)
+    want, ws = tgb.expected_block(c, oracle)
+    ys, scales = [], set()
+    for r in range(world):
+        z = np.load(tmp_path / f"rank{r}.npz")
+        if int(z["rows"]) > 0:
+            ys.append(z["y"])
+            scales.add((int(z["mant"]), int(z["shift"])))
+    assert scales == {ws}
+    assert (np.concatenate(ys) == want).all()

@@ -76,3 +76,17 @@ def test_lcg_uniform_is_the_reference_lcg():
         s = (s * 6364136223846793005 + 1442695040888963407) & ((1 << 64) - 1)
         want.append((s >> 33) % (2 * 265720 + 1) - 265720)
     assert list(v) == want
+
+
+def test_norm_codes_and_eps_equal_the_references_quantiser(oracle):
+    """RmsNorm::new (layers.rs:367-388) quantises its weight like QuantLinear::from_weights, and eps with
+    Scale::from_f64: the product's host preparation gives the oracle's codes and scales."""
+    import tritify_b200 as tb
+
+    d = 256
+    w = tb.synth_normal(63, 1.0, d)
+    _, _, wc, ws, es = oracle.rmsnorm(w, 1e-6, np.zeros(d, np.int32), (1, 0))
+    q = tb.QuantLinear.from_weights("norm", w, 1, d)
+    assert (q.w_codes.reshape(-1) == wc).all() and (q.w_scale.mant, q.w_scale.shift) == ws
+    e = tb.scale_from_f64(1e-6)
+    assert (e.mant, e.shift) == es

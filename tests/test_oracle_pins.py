@@ -135,3 +135,34 @@ def test_all_zero_input_gives_zero_output(oracle):
     m = cases.build_oracle(c, oracle)
     y, ys = m.forward(np.zeros((3, c.d), np.int32), (0, 0))
     assert (y == 0).all() and ys == (0, 0)
+
+
+def test_rsqrt_tracks_f64_like_the_reference(oracle):
+    """kt-int lib.rs:620-640 (scale_rsqrt_matches_f64): over log-uniform v in [2^-20, 2^20], Scale::rsqrt is within a
+    relative 2e-9 of 1/sqrt(v) (the reference freezes that bound)."""
+    rng = np.random.default_rng(0x1557A1)
+    worst = 0.0
+    for frac in rng.random(20000):
+        v = 2.0 ** (-20.0 + 40.0 * frac)
+        m, sh = oracle.scale_rsqrt(oracle.from_f64(v))
+        got = m * 2.0 ** (-sh)
+        worst = max(worst, abs(got - 1.0 / np.sqrt(v)) * np.sqrt(v))
+    assert worst < 2e-9
+
+
+def test_rmsnorm_tracks_float_like_the_reference(oracle):
+    """kt-core tests.rs:63-75 (rmsnorm_tracks_float_and_is_deterministic): the integer RmsNorm stays within 1% of the
+    float path's peak, and repeats bit for bit."""
+    import tritify_b200 as tb
+
+    dim, rows = 128, 3
+    w = tb.synth_normal(71, 1.0, dim)
+    xf = tb.synth_normal(72, 1.0, rows * dim)
+    xi, xs = oracle.from_reals_f32(xf)
+    y, ys, _, _, _ = oracle.rmsnorm(w, 1e-6, xi, xs)
+    y2, ys2, _, _, _ = oracle.rmsnorm(w, 1e-6, xi, xs)
+    assert (y == y2).all() and ys == ys2
+    x64 = xi.astype(np.float64).reshape(rows, dim) * xs[0] * 2.0 ** (-xs[1])
+    ref = x64 / np.sqrt((x64 ** 2).mean(axis=1, keepdims=True) + 1e-6) * w.astype(np.float64)
+    got = y.astype(np.float64).reshape(rows, dim) * ys[0] * 2.0 ** (-ys[1])
+    assert np.abs(got - ref).max() <= np.abs(ref).max() * 1e-2

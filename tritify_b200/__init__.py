@@ -305,21 +305,30 @@ class DeviceLayer:
                                                     _p(u, ctypes.c_int32), up[1]._c(), _p(d, ctypes.c_int32),
                                                     down[1]._c()))
 
-    def forward(self, x: np.ndarray, rows: int, x_scale: Scale):
+    def set_norm(self, w_codes: np.ndarray, w_scale: Scale, eps_scale: Scale) -> None:
+        """The block's FFN input RmsNorm (RmsNorm::new codes and scales) for block_forward."""
+        w = np.ascontiguousarray(w_codes, dtype=np.int32)
+        self.ctx.check(lib().ktmoe_layer_set_norm(self._h, _p(w, ctypes.c_int32), w_scale._c(), eps_scale._c()))
+
+    def block_forward(self, x: np.ndarray, rows: int, x_scale: Scale):
+        """x + moe(rms_norm(x)) (kt-core model.rs:175-181), host buffers: returns (y int32 [rows·d], Scale)."""
+        return self.forward(x, rows, x_scale, block=True)
+
+    def forward(self, x: np.ndarray, rows: int, x_scale: Scale, block: bool = False):
         """Host buffers in and out (synchronous): returns (y int32 [rows·d], Scale)."""
+        fn = lib().ktmoe_block_forward if block else lib().ktmoe_forward
         x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
         if x.size == 0:
             x = np.zeros(1, np.int32)
             y = np.zeros(1, np.int32)
             ys = KtmoeScale()
-            self.ctx.check(lib().ktmoe_forward(self._h, _p(x, ctypes.c_int32), 0, x_scale._c(), _p(y, ctypes.c_int32),
-                                               ctypes.byref(ys)))
+            self.ctx.check(fn(self._h, _p(x, ctypes.c_int32), 0, x_scale._c(), _p(y, ctypes.c_int32), ctypes.byref(ys)))
             return np.zeros(0, np.int32), Scale._of(ys)
         if x.size != rows * self.d_model:
             raise ValueError("x is not rows·d_model")
         y = np.empty(rows * self.d_model, dtype=np.int32)
         ys = KtmoeScale()
-        self.ctx.check(lib().ktmoe_forward(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(), _p(y, ctypes.c_int32),
+        self.ctx.check(fn(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(), _p(y, ctypes.c_int32),
                                            ctypes.byref(ys)))
         return y, Scale._of(ys)
 
@@ -456,6 +465,13 @@ class MoeMlp:
     def route_trace(self, x: IntTensor) -> List[List[int]]:
         """Module::route_trace (layers.rs:1089-1100)."""
         return [r.experts for r in self.route(x)]
+
+
+def scale_from_f64(x: float) -> Scale:
+    """Scale::from_f64 (kt-int lib.rs:215-222)."""
+    s = KtmoeScale()
+    check(lib().ktmoe_scale_from_f64(float(x), ctypes.byref(s)))
+    return Scale._of(s)
 
 
 def ep_unique_id() -> bytes:

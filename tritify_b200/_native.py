@@ -54,6 +54,10 @@ SIGNATURES = {
     "ktmoe_layer_experts": ([_vp, _P(_i32), _P(_i32)], ctypes.c_int),
     "ktmoe_layer_set_ep_capacity": ([_vp, _i64], ctypes.c_int),
     "ktmoe_layer_set_graphs": ([_vp, _i32], ctypes.c_int),
+    "ktmoe_layer_set_norm": ([_vp, _i32p, KtmoeScale, KtmoeScale], ctypes.c_int),
+    "ktmoe_block_forward": ([_vp, _i32p, _i64, KtmoeScale, _i32p, _P(KtmoeScale)], ctypes.c_int),
+    "ktmoe_block_forward_dev": ([_vp, _vp, _i64, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ktmoe_scale_from_f64": ([ctypes.c_double, _P(KtmoeScale)], ctypes.c_int),
     "ktmoe_layer_destroy": ([_vp], ctypes.c_int),
     "ktmoe_layer_set_router": ([_vp, _i32p, KtmoeScale, _i64p, KtmoeScale], ctypes.c_int),
     "ktmoe_layer_set_sigmoid_bias": ([_vp, _i64p], ctypes.c_int),

@@ -27,7 +27,11 @@ namespace ep {
 using kt::Scale;
 
 constexpr int MAXW = 8;
-enum Point : int { P_COUNTS = 0, P_DISPATCH, P_RETURN, P_REC, P_MERGE, P_SX, P_SYG, P_SHMAX, P_SYD, P_ADD, NPOINT };
+enum Point : int {
+    P_COUNTS = 0, P_DISPATCH, P_RETURN, P_REC, P_MERGE, P_SX, P_SYG, P_SHMAX, P_SYD, P_ADD,
+    P_TOK, P_NREC, P_NMAX, P_RADD,  // the block around the layer: row counts, the norm's record and max, the residual add
+    NPOINT
+};
 enum : int { ERR_WAIT = 21, ERR_BOUNDS = 22 };
 
 struct Box {

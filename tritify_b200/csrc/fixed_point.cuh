@@ -216,6 +216,44 @@ KT_HD Scale scale_recip(Scale s) {
     return Scale{r.mant, r.shift - s.shift + 40};
 }
 
+// crates/00-kernels/kt-int/src/lib.rs:285-303 — Scale::add (exact sum of two non-negative scales, renormalised).
+KT_HD Scale scale_add(Scale a, Scale o) {
+    if (a.mant == 0) return o;
+    if (o.mant == 0) return a;
+    const int32_t s = a.shift > o.shift ? a.shift : o.shift;
+    const uint32_t da = (uint32_t)(s - a.shift), db = (uint32_t)(s - o.shift);
+    if (da >= 96) return a;
+    if (db >= 96) return o;
+    const u128 sum = ((u128)(uint64_t)a.mant << da) + ((u128)(uint64_t)o.mant << db);
+    const Scale fr = from_ratio(sum, 1);
+    return Scale{fr.mant, fr.shift + s};
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:327-340 — floor(sqrt(n)) by Newton's method from above.
+KT_HD u128 isqrt_u128(u128 n) {
+    if (n == 0) return 0;
+    const int bits = bits_u128(n);
+    u128 x = (u128)1 << ((bits + 1) / 2);
+    for (;;) {
+        const u128 y = (x + udiv_u128(n, x)) >> 1;
+        if (y >= x) return x;
+        x = y;
+    }
+}
+
+// crates/00-kernels/kt-int/src/lib.rs:307-318 — Scale::rsqrt (mant > 0): an even exponent, an integer square root
+// with 31 fractional bits, the reciprocal.
+KT_HD Scale scale_rsqrt(Scale a) {
+    u128 m = (u128)(uint64_t)a.mant;
+    int32_t s = a.shift;
+    if (s & 1) {
+        m <<= 1;
+        s += 1;
+    }
+    const u128 r = isqrt_u128(m << 62);
+    return scale_recip(Scale{(int64_t)r, 31 + s / 2});
+}
+
 // from_ratio(v, 2^28) for 0 < v < 2^63: the output-scale factor of every dynamic requant.
 KT_HD Scale ratio_act(int64_t v) { return from_ratio((u128)(uint64_t)v, (u128)ACT_LEVELS); }
 
@@ -359,6 +397,14 @@ KT_HD int64_t apply_row(const ApplyPlan& p, int32_t v) {
     if (!p.tight || v == INT32_MIN) return scale_apply(p.s, v);
     const uint32_t av = (uint32_t)(v >= 0 ? v : -v);
     const uint64_t r = ((uint64_t)av * p.mant + p.half) >> p.shift;
+    return v >= 0 ? (int64_t)r : -(int64_t)r;
+}
+
+// Scale::apply for any int64 value with a tight plan: |v|·mant < 2^95 in 128-bit arithmetic, then the rounding shift.
+KT_HD int64_t apply_row_wide(const ApplyPlan& p, int64_t v) {
+    if (!p.tight) return scale_apply(p.s, v);
+    const uint64_t av = v >= 0 ? (uint64_t)v : (uint64_t)(-(v + 1)) + 1;
+    const u128 r = ((u128)av * p.mant + p.half) >> p.shift;
     return v >= 0 ? (int64_t)r : -(int64_t)r;
 }
 

@@ -405,6 +405,12 @@ struct ktmoe_layer {
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
     // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
     bool timing = false;
+    // the block around the layer (ktmoe_layer_set_norm): the FFN input RmsNorm and the residual add
+    bool norm_set = false;
+    DevBuf b_norm;  // int32 [d]: the norm's weight codes
+    Scale norm_ws{0, 0}, norm_eps{0, 0};
+    DevBuf blk_c, blk_xn, blk_m, blk_sc, blk_u64, blk_off;
+    int64_t blk_cap = 0;
     // CUDA graphs of the forward (ktmoe_layer_set_graphs), keyed by the call's pointers, rows and stream
     struct Graph {
         const void *x, *xs, *y, *ys;
@@ -412,6 +418,7 @@ struct ktmoe_layer {
         cudaStream_t st;
         cudaGraphExec_t exec;
         uint64_t launches;  // this library's kernels in the graph
+        bool block;         // the block forward (norm, layer, residual add) rather than the layer alone
     };
     bool graphs = false;
     std::vector<Graph> graph_cache;
@@ -1135,13 +1142,13 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
 }
 
 int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
-                  cudaStream_t st) {
+                  cudaStream_t st, bool bump = true) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t d = L->d, E = L->E, f = L->f, K = L->K, fs = L->fs;
     const int64_t R = T * K;
     const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
     CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
-    if (L->peer.on) {
+    if (L->peer.on && bump) {
         ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);  // a new forward for every exchange below
         CKL(ctx);
     }
@@ -1309,23 +1316,134 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     return KTMOE_OK;
 }
 
+__global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { *p = v; }
+
+int ensure_block(ktmoe_layer* L, int64_t T) {
+    ktmoe_ctx* ctx = L->ctx;
+    CK(L->blk_sc.ensure(8 * sizeof(Scale)));
+    CK(L->blk_u64.ensure((3 + ep::MAXW) * 8));
+    CK(L->blk_off.ensure(4));
+    CK(L->ep_rec.ensure(3 * 8));
+    CK(L->ep_recs.ensure(L->world * 3 * 8));
+    CK(L->ep_best_idx.ensure(4));
+    if (T <= L->blk_cap && L->blk_cap > 0) return KTMOE_OK;
+    graphs_clear(L);
+    const int64_t n = std::max<int64_t>(T, 1);
+    CK(L->blk_c.ensure(n * sizeof(Scale)));
+    CK(L->blk_xn.ensure(n * L->d * 4));
+    CK(L->blk_m.ensure(n * L->d * 4));
+    L->blk_cap = n;
+    return KTMOE_OK;
+}
+
+// The FFN half of a decoder block with this layer as its FFN (kt-core model.rs:175-181): y = add(x, moe(norm(x))),
+// norm the RmsNorm of ktmoe_layer_set_norm (layers.rs:352-449), add the residual add (layers.rs:121-136). Every
+// reduction over the tensor (the norm's common scale and max, the add's max) spans all ranks.
+int stage_block(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
+                cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d;
+    Scale* sc = L->blk_sc.as<Scale>();  // [0..1] the norm's common and its reciprocal, [2] x_norm, [3] moe, [4..6] add
+    unsigned long long* u = L->blk_u64.as<unsigned long long>();  // [0] norm gmax, [1] add gmax, [2] T, [3..] counts
+    Scale* c = L->blk_c.as<Scale>();
+    int32_t* xn = L->blk_xn.as<int32_t>();
+    int32_t* m = L->blk_m.as<int32_t>();
+    CK(cudaMemsetAsync(u, 0, 2 * 8, st));
+    if (L->peer.on) {
+        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);
+        CKL(ctx);
+    }
+    const int* off = nullptr;
+    if (L->world > 1) {
+        // every rank's row count, for this rank's first global row (the tie rule of the common scale)
+        set_u64_kernel<<<1, 1, 0, st>>>(u + 2, (unsigned long long)T);
+        CKL(ctx);
+        if (L->peer.on) {
+            ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_TOK, u + 2, 1, u + 3, nullptr, ctx->d_err);
+            CKL(ctx);
+        } else {
+            NK(ncclAllGather(u + 2, u + 3, 1, ncclUint64, L->comm, st));
+        }
+        mk::row_offset_kernel<<<1, 1, 0, st>>>(u + 3, L->rank, L->blk_off.as<int>());
+        CKL(ctx);
+        off = L->blk_off.as<int>();
+    }
+    if (T > 0) {
+        mk::rms_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, xs_dev, L->norm_ws, L->norm_eps, c);
+        CKL(ctx);
+    }
+    if (L->world == 1) {
+        mk::common_scale_kernel<<<1, 1024, 0, st>>>(c, (int)T, 0, sc, nullptr);
+        CKL(ctx);
+    } else {
+        if (T > 0) {
+            mk::common_scale_kernel<<<1, 1024, 0, st>>>(c, (int)T, 0, sc, L->ep_best_idx.as<int>(), off);
+            CKL(ctx);
+            mk::scale_record_kernel<<<1, 1, 0, st>>>(sc, L->ep_best_idx.as<int>(), L->ep_rec.as<int64_t>());
+            CKL(ctx);
+        } else {
+            mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
+            CKL(ctx);
+        }
+        if (L->peer.on) {
+            ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_NREC, L->ep_rec.as<unsigned long long>(), 3,
+                                                  L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
+            CKL(ctx);
+        } else {
+            NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
+        }
+        mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, sc);
+        CKL(ctx);
+    }
+    if (T > 0) {
+        mk::rms_max_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc, u);
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, u, 1, st, ep::P_NMAX)) return r;
+    if (T > 0) {
+        mk::rms_final_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc, u, xn);
+        CKL(ctx);
+    }
+    mk::gmax_scale_kernel<<<1, 1, 0, st>>>(sc, u, sc + 2);
+    CKL(ctx);
+    if (int r = stage_forward(L, T, xn, sc + 2, m, sc + 3, st, false)) return r;
+    const int64_t n = T * d;
+    const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
+    mk::add2_prepare_kernel<<<1, 1, 0, st>>>(xs_dev, sc + 3, sc + 4);
+    CKL(ctx);
+    if (T > 0) {
+        mk::add2_max_kernel<<<rb, 256, 0, st>>>(x_dev, m, n, sc + 4, u + 1);
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, u + 1, 1, st, ep::P_RADD)) return r;
+    if (T > 0) {
+        mk::add2_final_kernel<<<rb, 256, 0, st>>>(x_dev, m, n, sc + 4, u + 1, y_dev);
+        CKL(ctx);
+    }
+    mk::gmax_scale_kernel<<<1, 1, 0, st>>>(sc + 4, u + 1, ys_dev);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
 // The forward through a CUDA graph when graphs are on and the forward has no host synchronisation (one rank, or the
 // peer transport): the first call with a key runs the forward, then captures the same launch sequence; later calls
 // with that key launch the graph. Timing (per-stage events) and the NCCL exchange always run uncaptured.
-int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, int32_t* y, Scale* ys, cudaStream_t st) {
+int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, int32_t* y, Scale* ys, cudaStream_t st,
+                bool block = false) {
     ktmoe_ctx* ctx = L->ctx;
-    if (!L->graphs || L->timing || (L->world > 1 && !L->peer.on)) return stage_forward(L, T, x, xs, y, ys, st);
+    auto once = [&]() { return block ? stage_block(L, T, x, xs, y, ys, st) : stage_forward(L, T, x, xs, y, ys, st); };
+    if (!L->graphs || L->timing || (L->world > 1 && !L->peer.on)) return once();
     for (auto& g : L->graph_cache)
-        if (g.x == x && g.xs == xs && g.y == y && g.ys == ys && g.T == T && g.st == st) {
+        if (g.x == x && g.xs == xs && g.y == y && g.ys == ys && g.T == T && g.st == st && g.block == block) {
             CK(cudaGraphLaunch(g.exec, st));
             ctx->launches += g.launches;
             return KTMOE_OK;
         }
-    if (int r = stage_forward(L, T, x, xs, y, ys, st)) return r;
+    if (int r = once()) return r;
     const uint64_t l0 = ctx->launches;
     cudaGraph_t graph = nullptr;
     CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    const int r = stage_forward(L, T, x, xs, y, ys, st);
+    const int r = once();
     const cudaError_t e = cudaStreamEndCapture(st, &graph);
     ctx->launches = l0;  // nothing ran during the capture
     if (r != KTMOE_OK || e != cudaSuccess || !graph) {
@@ -1356,7 +1474,7 @@ int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, in
         cudaGraphExecDestroy(L->graph_cache.front().exec);
         L->graph_cache.erase(L->graph_cache.begin());
     }
-    L->graph_cache.push_back({x, xs, y, ys, T, st, exec, n});
+    L->graph_cache.push_back({x, xs, y, ys, T, st, exec, n, block});
     return KTMOE_OK;
 }
 
@@ -1887,6 +2005,8 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                       &L->hs_planes, &L->acc_sd, &L->swiglu_plans, &L->row_hmax, &L->shared_plan,
                       &L->cp_n, &L->cp_common, &L->cp_row, &L->cp_ec, &L->cp_ry, &L->cp_f};
     for (DevBuf* b : bufs) b->release();
+    DevBuf* blk_bufs[] = {&L->b_norm, &L->blk_c, &L->blk_xn, &L->blk_m, &L->blk_sc, &L->blk_u64, &L->blk_off};
+    for (DevBuf* b : blk_bufs) b->release();
     DevBuf* ep_bufs[] = {&L->ep_counts, &L->ep_counts_all, &L->ep_meta_send, &L->ep_meta_recv, &L->ep_recv_planes,
                          &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,
                          &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
@@ -2009,6 +2129,73 @@ int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_
     CK(cudaStreamSynchronize(st));
     if (int r = check_err_word(ctx)) return r;
     *y_scale = C(ys);
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_norm(ktmoe_layer* L, const int32_t* w_codes, ktmoe_scale w_scale, ktmoe_scale eps_scale) {
+    if (!L || !w_codes) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    for (int64_t i = 0; i < L->d; ++i)
+        if (w_codes[i] > kt::WLEVELS || w_codes[i] < -kt::WLEVELS) return fail(ctx, KTMOE_ERR_RANGE, "norm code");
+    CK(cudaStreamSynchronize(ctx->stream));
+    CK(L->b_norm.ensure(L->d * 4));
+    CK(cudaMemcpy(L->b_norm.p, w_codes, L->d * 4, cudaMemcpyHostToDevice));
+    L->norm_ws = S(w_scale);
+    L->norm_eps = S(eps_scale);
+    L->norm_set = true;
+    graphs_clear(L);  // graphs captured the old scales as kernel arguments
+    return KTMOE_OK;
+}
+
+int ktmoe_block_forward_dev(ktmoe_layer* L, const int32_t* x_dev, int64_t rows, const ktmoe_scale* x_scale_dev,
+                            int32_t* y_dev, ktmoe_scale* y_scale_dev, void* stream) {
+    if (!L || !x_scale_dev || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (L->peer.on && rows > L->peer.cap_T) return fail(L->ctx, KTMOE_ERR_ARG, "more rows than the EP capacity");
+    if (rows > 0 && (!x_dev || !y_dev || !y_scale_dev)) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!layer_complete(L) || !L->norm_set) return fail(ctx, KTMOE_ERR_STATE, "a weight of the block is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    if (int r = ensure_block(L, rows)) return r;
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    return run_forward(L, rows, x_dev, (const Scale*)x_scale_dev, y_dev, (Scale*)y_scale_dev, st, true);
+}
+
+int ktmoe_block_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                        ktmoe_scale* y_scale) {
+    if (!L || !y_scale || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (L->peer.on && rows > L->peer.cap_T) return fail(L->ctx, KTMOE_ERR_ARG, "more rows than the EP capacity");
+    if (rows > 0 && (!x || !y)) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!layer_complete(L) || !L->norm_set) return fail(ctx, KTMOE_ERR_STATE, "a weight of the block is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    if (int r = ensure_block(L, rows)) return r;
+    cudaStream_t st = ctx->stream;
+    const size_t n = (size_t)(rows * L->d);
+    Scale xs = S(x_scale);
+    if (n) CK(cudaMemcpyAsync(L->x_in.p, x, n * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+    if (int r = run_forward(L, rows, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
+                            scal_scale(L, SL_YSCALE), st, true))
+        return r;
+    Scale ys{0, 0};
+    if (n) CK(cudaMemcpyAsync(y, L->y_out.p, n * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(&ys, scal_scale(L, SL_YSCALE), sizeof(Scale), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (int r = check_err_word(ctx)) return r;
+    *y_scale = C(ys);
+    return KTMOE_OK;
+}
+
+int ktmoe_scale_from_f64(double x, ktmoe_scale* out) {
+    if (!out) return KTMOE_ERR_ARG;
+    const hp::HScale h = hp::scale_from_f64(x);
+    *out = ktmoe_scale{h.mant, h.shift};
     return KTMOE_OK;
 }
 

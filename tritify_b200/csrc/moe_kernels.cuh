@@ -966,6 +966,122 @@ __global__ void add_final_kernel(const AddArgs p) {
     if (blockIdx.x == 0 && threadIdx.x == 0) *p.y_scale = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common);
 }
 
+// ───────────── the FFN half of a decoder block: x + moe(rms_norm(x)) (kt-core model.rs:175-181) ─────────────
+// RmsNorm (layers.rs:352-449): per row C_r = x.scale·rsqrt(mean(x²)·x.scale² + eps)·w_scale, p = x_i·wcode_i; all
+// rows to the common (last largest) C, one dynamic requant over the whole tensor.
+
+// One block per row: the row's C (the sum of squares in 128 bits, as the reference's i128).
+__global__ void rms_rows_kernel(const int32_t* __restrict__ x, int rows, int dim, const Scale* __restrict__ x_scale,
+                                Scale w_scale, Scale eps_scale, Scale* __restrict__ c) {
+    __shared__ unsigned long long part[2][256];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int32_t* xr = x + (long long)r * dim;
+    kt::u128 ss = 0;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) ss += (kt::u128)((int64_t)xr[i] * (int64_t)xr[i]);
+    part[0][threadIdx.x] = (unsigned long long)ss;
+    part[1][threadIdx.x] = (unsigned long long)(ss >> 64);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        kt::u128 t = 0;
+        for (int i = 0; i < (int)blockDim.x; ++i) t += ((kt::u128)part[1][i] << 64) | part[0][i];
+        const Scale xs = *x_scale;
+        const Scale mean_sq = kt::scale_mul(kt::scale_mul(kt::from_ratio(t, (kt::u128)dim), xs), xs);
+        const Scale denom = kt::scale_add(mean_sq, eps_scale);
+        const Scale inv = denom.mant == 0 ? kt::scale_zero() : kt::scale_rsqrt(denom);
+        c[r] = kt::scale_mul(kt::scale_mul(xs, inv), w_scale);
+    }
+}
+
+// Pass 1: max over the tensor of |f_r.apply(x_i·wcode_i)|, f_r = C_r·common⁻¹ (atomicMax into *gmax).
+__global__ void rms_max_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ wcodes, int rows, int dim,
+                               const Scale* __restrict__ c, const Scale* __restrict__ common,
+                               unsigned long long* __restrict__ gmax) {
+    __shared__ uint64_t red[32];
+    const int r = blockIdx.x;
+    if (r >= rows || common[0].mant == 0) return;
+    const kt::ApplyPlan f = kt::make_apply(kt::scale_mul(c[r], common[1]));
+    const int32_t* xr = x + (long long)r * dim;
+    uint64_t m = 0;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        m = max(m, uabs64(kt::apply_row_wide(f, (int64_t)xr[i] * (int64_t)wcodes[i])));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(gmax, (unsigned long long)m);
+}
+
+// Pass 2: y = requant_dyn(f_r.apply(x_i·wcode_i), L, gmax); scale = from_ratio(gmax, L)·common.
+__global__ void rms_final_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ wcodes, int rows, int dim,
+                                 const Scale* __restrict__ c, const Scale* __restrict__ common,
+                                 const unsigned long long* __restrict__ gmax_p, int32_t* __restrict__ y) {
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int64_t gmax = (int64_t)*gmax_p;
+    const bool zero = common[0].mant == 0 || gmax == 0;
+    int32_t* yr = y + (long long)r * dim;
+    if (zero) {
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) yr[i] = 0;
+    } else {
+        const kt::ApplyPlan f = kt::make_apply(kt::scale_mul(c[r], common[1]));
+        const kt::ReqDiv rg = kt::make_req(gmax);
+        const int32_t* xr = x + (long long)r * dim;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x)
+            yr[i] = kt::requant_row(kt::apply_row_wide(f, (int64_t)xr[i] * (int64_t)wcodes[i]), rg);
+    }
+}
+
+// The scale of a dynamic requant over a whole tensor: from_ratio(gmax, L)·common (zero when either is).
+__global__ void gmax_scale_kernel(const Scale* __restrict__ common, const unsigned long long* __restrict__ gmax_p,
+                                  Scale* __restrict__ out) {
+    const int64_t gmax = (int64_t)*gmax_p;
+    *out = (common[0].mant == 0 || gmax == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common[0]);
+}
+
+// add(a, b) of two activations (layers.rs:121-136): common = a.scale.ge(b.scale) ? a : b; sum = fa.apply(a) +
+// fb.apply(b); one dynamic requant over the tensor. `plan` holds {common, fa, fb}.
+__global__ void add2_prepare_kernel(const Scale* __restrict__ a_scale, const Scale* __restrict__ b_scale,
+                                    Scale* __restrict__ plan) {
+    const Scale as = *a_scale, bs = *b_scale;
+    const Scale common = kt::scale_ge(as, bs) ? as : bs;
+    plan[0] = common;
+    if (common.mant) {
+        const Scale cinv = kt::scale_recip(common);
+        plan[1] = kt::scale_mul(as, cinv);
+        plan[2] = kt::scale_mul(bs, cinv);
+    } else {
+        plan[1] = plan[2] = kt::scale_zero();
+    }
+}
+
+__global__ void add2_max_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ b, long long n,
+                                const Scale* __restrict__ plan, unsigned long long* __restrict__ gmax) {
+    __shared__ uint64_t red[32];
+    const kt::ApplyPlan fa = kt::make_apply(plan[1]), fb = kt::make_apply(plan[2]);
+    uint64_t m = 0;
+    if (plan[0].mant)
+        for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+            m = max(m, uabs64(kt::apply_row(fa, a[i]) + kt::apply_row(fb, b[i])));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(gmax, (unsigned long long)m);
+}
+
+__global__ void add2_final_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ b, long long n,
+                                  const Scale* __restrict__ plan, const unsigned long long* __restrict__ gmax_p,
+                                  int32_t* __restrict__ y) {
+    const kt::ApplyPlan fa = kt::make_apply(plan[1]), fb = kt::make_apply(plan[2]);
+    const int64_t gmax = (int64_t)*gmax_p;
+    const bool zero = plan[0].mant == 0 || gmax == 0;
+    const kt::ReqDiv rg = kt::make_req(gmax);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        y[i] = zero ? 0 : kt::requant_row(kt::apply_row(fa, a[i]) + kt::apply_row(fb, b[i]), rg);
+}
+
+// The first global row of this rank from every rank's row count ([world] u64, rank order).
+__global__ void row_offset_kernel(const unsigned long long* __restrict__ counts, int rank, int* __restrict__ offset) {
+    int o = 0;
+    for (int q = 0; q < rank; ++q) o += (int)counts[q];
+    *offset = o;
+}
+
 // ───────────── expert parallelism: the exchange around the routed experts ─────────────
 // A home rank sends, for every (token, slot) row in expert order, the row's digit planes and its s_qx; the owner of
 // the expert returns the expert's output as the reference's seam returns it (an IntTensor: i32 data + Scale,
