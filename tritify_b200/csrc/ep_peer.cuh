@@ -233,30 +233,33 @@ __device__ __forceinline__ void last_block_signal(const Peers& P, int point, uns
 
 // Dispatch (the permute and the send in one pass): expert-sorted row r of this rank (token row_assign[r] / K, expert
 // row_expert[r]) is copied from the token's digit planes straight into its owner's receive buffer at
-// dst_base[e] + r, with its meta. Grid-stride over rows; then P_DISPATCH to every rank.
+// dst_base[e] + r, with its meta. One warp per row (16-byte loads and stores, many rows in flight per SM); then
+// P_DISPATCH to every rank.
 __global__ void dispatch_kernel(const Peers P, int R, const int* __restrict__ row_assign,
                                 const int* __restrict__ row_expert, int K, const int8_t* __restrict__ tok_planes,
                                 long long T_pad, const Scale* __restrict__ tok_sqx, const int* __restrict__ dst_base,
                                 int* ctr, int* err) {
     const unsigned long long seq = *P.seq;
     const int n16 = P.d_pad / 16;
-    for (int r = blockIdx.x; r < R; r += gridDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int warps = (int)(gridDim.x * blockDim.x) >> 5;
+    for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < R; r += warps) {
         const int e = row_expert[r];
         const int t = row_assign[r] / K;
         const int q = owner_of(P, e);
         const long long dst = (long long)dst_base[e] + r;
         if (dst < 0 || dst >= P.cap_rows) {
-            if (threadIdx.x == 0) atomicCAS(err, 0, ERR_BOUNDS);
+            if (lane == 0) atomicCAS(err, 0, ERR_BOUNDS);
             continue;
         }
         int8_t* pq = P.planes(q);
 #pragma unroll
         for (int p = 0; p < 3; ++p) {
-            const int4* s = (const int4*)(tok_planes + ((long long)p * T_pad + t) * P.d_pad);
+            const int4* src = (const int4*)(tok_planes + ((long long)p * T_pad + t) * P.d_pad);
             int4* dp = (int4*)(pq + ((long long)p * P.cap_rows + dst) * P.d_pad);
-            for (int i = threadIdx.x; i < n16; i += blockDim.x) dp[i] = __ldg(s + i);
+            for (int i = lane; i < n16; i += 32) dp[i] = __ldg(src + i);
         }
-        if (threadIdx.x == 0) {
+        if (lane == 0) {
             long long* m = P.meta(q) + dst * 4;
             const Scale sq = tok_sqx[t];
             m[0] = sq.mant;

@@ -994,7 +994,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
                                                    pr.group_end.as<int>(), pr.rows_recv.as<int>(), ta, tb, tok_info,
                                                    tok_info + 1, ctx->d_err);
     CKL(ctx);
-    ep::dispatch_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(R, ctx->num_sms * 4)), 128, 0, st>>>(
+    ep::dispatch_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, ctx->num_sms * 8)), 256, 0, st>>>(
         pr.P, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
         L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(), ctx->d_err);
     CKL(ctx);
@@ -1027,7 +1027,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     xr.row_expert = pr.recv_expert.as<int>();
     xr.row_sqx = pr.recv_sqx.as<Scale>();
     if (int r = run_experts(L, xr, st)) return r;
-    ep::return_kernel<<<(unsigned)(ctx->num_sms * 2), 256, 0, st>>>(pr.P, pr.rows_recv.as<int>(),
+    ep::return_kernel<<<(unsigned)(ctx->num_sms * 8), 256, 0, st>>>(pr.P, pr.rows_recv.as<int>(),
                                                                    L->acc_d.as<int64_t>(),
                                                                    L->rowmax_d.as<unsigned long long>(),
                                                                    L->row_cd.as<Scale>(), pr.ctr.as<int>(), ctx->d_err);
