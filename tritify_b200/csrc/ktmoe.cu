@@ -741,8 +741,9 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
             const int v = e ? atoi(e) : 2;
             return (v == 1 || v == 2 || v == 4) ? v : 2;
         }();
-        // blocks walk the rows: a few per SM cover them without a block per row
-        const unsigned grid = (unsigned)std::min<int64_t>(R, (int64_t)ctx->num_sms * 6);
+        // a block per row (rows beyond a device-side count leave at once): blocks that wait at a row's barrier
+        // are replaced by new ones, which keeps the SMs busier than blocks walking several rows (ncu: 617 vs 696 us)
+        const unsigned grid = (unsigned)R;
         if (unroll == 1)
             mk::swiglu_rows_kernel<1><<<grid, 256, sm, st>>>(sa, h_smem);
         else if (unroll == 4)
