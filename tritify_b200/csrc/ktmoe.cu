@@ -464,6 +464,8 @@ int ensure_rows(ktmoe_layer* L, int64_t rows) {
 }
 
 void graphs_clear(ktmoe_layer* L) {
+    if (L->graph_cache.empty()) return;
+    cudaStreamSynchronize(L->ctx->stream);  // no launch of these graphs is still in flight
     for (auto& g : L->graph_cache) cudaGraphExecDestroy(g.exec);
     L->graph_cache.clear();
 }
@@ -2030,6 +2032,7 @@ int ktmoe_layer_set_router(ktmoe_layer* L, const int32_t* codes, ktmoe_scale w_s
     if (!L || !codes) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);  // captured launches hold some of the layer's scales by value
     if (int r = set_device(ctx)) return r;
     if (int r = upload_matrix(ctx, L->w_router, 0, codes, L->E, L->d, 0)) return r;
     L->router_ws = S(w_scale);
@@ -2050,6 +2053,7 @@ int ktmoe_layer_set_sigmoid_bias(ktmoe_layer* L, const int64_t* bias_codes) {
     ktmoe_ctx* ctx = L->ctx;
     if (L->cfg.router_score != 1) return fail(ctx, KTMOE_ERR_ARG, "the layer's router is not sigmoid");
     std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);  // captured launches hold some of the layer's scales by value
     if (int r = set_device(ctx)) return r;
     CK(cudaMemcpy(L->b_sigbias.p, bias_codes, L->E * 8, cudaMemcpyHostToDevice));
     L->sigbias_set = true;
@@ -2061,6 +2065,7 @@ int ktmoe_layer_set_expert(ktmoe_layer* L, int32_t e, const int32_t* gate, ktmoe
     if (!L || !gate || !up || !down || e < L->e_begin || e >= L->e_end) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
     std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);  // captured launches hold some of the layer's scales by value
     if (int r = set_device(ctx)) return r;
     const int64_t le = e - L->e_begin;  // this rank's experts are stored from 0
     if (int r = upload_matrix(ctx, L->w_gu, le, gate, L->f, L->d, 0)) return r;
@@ -2080,6 +2085,7 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
     ktmoe_ctx* ctx = L->ctx;
     if (L->fs <= 0) return fail(ctx, KTMOE_ERR_ARG, "the layer has no shared expert");
     std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);  // captured launches hold some of the layer's scales by value
     if (int r = set_device(ctx)) return r;
     if (int r = upload_matrix(ctx, L->w_sgu, 0, gate, L->fs, L->d, 0)) return r;
     if (int r = upload_matrix(ctx, L->w_sgu, 0, up, L->fs, L->d, L->fs)) return r;
