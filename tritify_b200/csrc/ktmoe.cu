@@ -465,7 +465,7 @@ int ensure_rows(ktmoe_layer* L, int64_t rows) {
 
 void graphs_clear(ktmoe_layer* L) {
     if (L->graph_cache.empty()) return;
-    cudaStreamSynchronize(L->ctx->stream);  // no launch of these graphs is still in flight
+    for (auto& g : L->graph_cache) cudaStreamSynchronize(g.st);  // no launch of these graphs is still in flight
     for (auto& g : L->graph_cache) cudaGraphExecDestroy(g.exec);
     L->graph_cache.clear();
 }
