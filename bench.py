@@ -43,7 +43,11 @@ WORKLOADS = {
     # BASELINE config 5, one layer: GLM-4.5-Air-shaped, sigmoid router with selection bias N(0, 0.02), shared expert.
     "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
     "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
+    # the standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
+    # activations uniform in [-127, 127], seed 2 (1 GPU).
+    "gemm4096": dict(gemm=True, M=4096, N=4096, K=4096, seed=2),
 }
+GEMM_METRIC = "exact int64 GEMM throughput (2·M·N·K code ops/s), bit-exact; % int8 tensor peak"
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200, bit-exact; % HBM / int8 tensor peak"
 P_PLANES = 9  # int8 plane products per code product (3 balanced base-81 digits each side)
 
@@ -259,6 +263,137 @@ def run_reference(args, w, name):
     }), flush=True)
 
 
+def gemm_codes(w):
+    """x [N][K] int8-range activation codes and w [M][K] 12-bit weight codes, both from one numpy generator."""
+    rng = np.random.default_rng(w["seed"])
+    wt = rng.integers(-2048, 2048, size=w["M"] * w["K"], dtype=np.int32)
+    x = rng.integers(-127, 128, size=w["N"] * w["K"], dtype=np.int32)
+    return x, wt
+
+
+def gemm_config(w, name):
+    return {"workload": name, "M": w["M"], "N": w["N"], "K": w["K"], "weights": "uniform [-2048, 2047]",
+            "activations": "uniform [-127, 127]",
+            "l2": "each step writes the 128 MiB int64 result and the packed activations (> 126 MB L2) between GEMMs"}
+
+
+def gemm_cpu_sample(w, seconds_target, O, x, wt):
+    """Rows of the activations that the oracle's linear (the reference's Portable CPU kernel, restated) finishes in
+    about seconds_target."""
+    M, K = w["M"], w["K"]
+    t0 = time.perf_counter()
+    O.linear(x[:8 * K], wt, 8, M, K)
+    per_row = max((time.perf_counter() - t0) / 8, 1e-6)
+    return int(max(1, min(w["N"], seconds_target / per_row)))
+
+
+def run_gemm_reference(args, w, name):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    O.lib().ko_set_max_threads(0)
+    x, wt = gemm_codes(w)
+    M, K = w["M"], w["K"]
+    rows = gemm_cpu_sample(w, 150.0 / max(1, args.steps + args.warmup), O, x, wt)
+    for _ in range(args.warmup):
+        O.linear(x[:rows * K], wt, rows, M, K)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.linear(x[:rows * K], wt, rows, M, K)
+    dt = (time.perf_counter() - t0) / args.steps
+    v = 2.0 * rows * M * K / dt / 1e12
+    sample = f"first {rows} of {w['N']} activation rows per step (C++ restatement of the reference's CPU linear)"
+    print(json.dumps({
+        "impl": "reference", "metric": GEMM_METRIC, "value": v, "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": gemm_config(w, name),
+        "cpu_baseline": {"value": v, "unit": "TOPS", "cores": os.cpu_count(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_gemm_ours(args, w, name):
+    """The GEMM through the LinearBackend entry point (ktmoe_linear_weights, weights resident after the first call).
+    e2e: each step copies the host activations in, packs them, runs the GEMM and copies the int64 result back; the
+    GEMM alone is timed with CUDA events that the library records around its launches (ktmoe_linear_last_gemm)."""
+    import torch
+
+    import tritify_b200 as tb
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return  # a 1-GPU workload: other ranks idle
+    torch.cuda.set_device(local)
+    M, N, K = w["M"], w["N"], w["K"]
+    x, wt = gemm_codes(w)
+    ctx = tb.Context(local)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    launches0 = None
+    for _ in range(args.warmup):
+        y = ctx.linear(x, wt, N, M, K, weight_id=1)
+    gemm_ms, planes = [], set()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_index(local)) as clk:
+        torch.cuda.synchronize()
+        launches0 = ctx.launch_count()
+        e0.record(stream)
+        for _ in range(args.steps):
+            y = ctx.linear(x, wt, N, M, K, weight_id=1)
+            ms, p = ctx.last_gemm()
+            gemm_ms.append(ms)
+            planes.add(p)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    launches = ctx.launch_count() - launches0
+    step_ms = e0.elapsed_time(e1) / args.steps
+    g_ms = sum(gemm_ms) / len(gemm_ms)
+    # spot check: 16 output columns equal their exact dot products
+    cols = np.random.default_rng(7).choice(M, 16, replace=False)
+    Y = y.reshape(N, M)
+    X = x.reshape(N, K).astype(np.int64)
+    if not (Y[:, cols] == X @ wt.reshape(M, K)[cols].astype(np.int64).T).all():
+        raise SystemExit("gemm4096: the result differs from the exact product")
+    ops = 2.0 * M * N * K
+    _, bf16, peak_kind = measured_peaks()
+    int8_peak = 2.0 * bf16
+    pl = planes.pop() if len(planes) == 1 else -1
+    int8_ops = ops * (2 if pl == 1 else 9)  # int8 plane products per code product: (1, 2) planes or (3, 3)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", f"digit_gemm_{name}.md")
+    if os.path.exists(tpath):
+        import re
+
+        m = re.search(r"dram_bytes_per_launch:\s*(\d+)", open(tpath).read())
+        traffic = int(m.group(1)) if m else None
+    res = {
+        "metric": GEMM_METRIC, "value": ops / (g_ms * 1e-3) / 1e12, "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": g_ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": gemm_config(w, name),
+        "activation_planes": pl, "clocks": clk.summary(), "gpu_launches": launches,
+        "e2e": {"value": ops / (step_ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": step_ms,
+                "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 8},
+        "roofline": {"bound": "tensor", "achieved": int8_ops / (g_ms * 1e-3) / 1e12, "peak": int8_peak,
+                     "unit": "TOPS (int8)", "frac": int8_ops / (g_ms * 1e-3) / 1e12 / int8_peak, "traffic": traffic,
+                     "kernel": "digit_gemm", "peak_kind": f"2 x bf16 dense, {peak_kind}"},
+    }
+    if not args.no_cpu:
+        from oracle import oracle as O
+
+        O.build()
+        O.lib().ko_set_max_threads(0)
+        rows = gemm_cpu_sample(w, 15.0, O, x, wt)
+        t0 = time.perf_counter()
+        O.linear(x[:rows * K], wt, rows, M, K)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": 2.0 * rows * M * K / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count(),
+                               "kind": "port", "sample": f"first {rows} of {N} activation rows, one call (C++ "
+                                                         f"restatement of the reference's CPU linear, all cores)"}
+    print(json.dumps(res), flush=True)
+
+
 def run_ours(args, w, name):
     import torch
 
@@ -463,6 +598,9 @@ def main():
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = dict(WORKLOADS[args.workload])
+    if w.get("gemm"):
+        (run_gemm_reference if args.impl == "reference" else run_gemm_ours)(args, w, args.workload)
+        return
     if args.tokens:
         w["T"] = args.tokens
     if args.experts:

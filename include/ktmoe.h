@@ -74,6 +74,14 @@ int ktmoe_linear(ktmoe_ctx* ctx, const int32_t* x, const int32_t* w, int64_t row
  * behind an id must never change. */
 int ktmoe_linear_weights(ktmoe_ctx* ctx, uint64_t weight_id, const int32_t* x, const int32_t* w, int64_t rows,
                          int64_t out, int64_t k, int64_t* y);
+/* Small codes: when every weight code lies within +-3280 and every activation code within +-127 (int8 activations,
+ * 12-bit weights), the call runs on one raw activation plane and two weight digit planes (two int8 products per
+ * code product instead of nine); otherwise on three planes each. Same result either way. KTMOE_SMALL=0 forces the
+ * nine-plane kernel. */
+/* Tracing: the device time in milliseconds of the last successful linear call's GEMM (CUDA events on the context's
+ * stream around the GEMM launches, after the codes are packed) and the activation planes it used (1 or 3; 0 and
+ * *ms = 0 when no call has completed). No counterpart in the reference. */
+int ktmoe_linear_last_gemm(ktmoe_ctx* ctx, double* ms, int32_t* act_planes);
 /* The same accumulate for callers that cannot let a library allocate device memory (a runtime that owns one fixed
  * pool, or runs under a budget where a hidden cudaMalloc/cudaFree would break its accounting). No counterpart in the
  * reference. x [rows][k], w [out][k] (int32 codes) and y [rows][out] (int64) are DEVICE buffers on `device`; the

@@ -126,3 +126,53 @@ def test_split_k_equals_one_block_per_tile(ctx, oracle, rows, out, k, monkeypatc
         got = ctx.linear(x, w, rows, out, k)
         bad = np.nonzero(got != want)[0]
         assert bad.size == 0, f"KTMOE_SPLITK={flag}: {bad.size} of {got.size} differ"
+
+
+def _small_codes(rng, rows, out, k):
+    x = rng.integers(-127, 128, size=rows * k, dtype=np.int32)
+    w = rng.integers(-2048, 2048, size=out * k, dtype=np.int32)
+    return x, w
+
+
+@pytest.mark.parametrize("rows,out,k", [(1, 1, 1), (37, 200, 300), (64, 256, 2048), (128, 1024, 4096),
+                                        (5, 128, 4096)])
+def test_small_codes_equal_the_cpu_path(ctx, oracle, rows, out, k):
+    """int8 activations and 12-bit weights (|x| <= 127, |w| <= 3280) run on one raw activation plane and two weight
+    digit planes; a single code one past either bound sends the call back to the nine-plane kernel. All equal the
+    CPU path, for weights packed per call and resident weights."""
+    rng = np.random.default_rng(rows * 7 + out * 3 + k)
+    wid = 90_000 + rows * 7 + out * 3 + k
+    x, w = _small_codes(rng, rows, out, k)
+    x[0] = -127
+    w[-1] = 3280
+    want = oracle.linear(x, w, rows, out, k)
+    assert (ctx.linear(x, w, rows, out, k) == want).all()
+    assert ctx.last_gemm()[1] == 1
+    assert (ctx.linear(x, w, rows, out, k, weight_id=wid) == want).all()
+    assert (ctx.linear(x, w, rows, out, k, weight_id=wid) == want).all()  # resident, small
+    assert ctx.last_gemm()[1] == 1
+    x2 = x.copy()
+    x2[-1] = 128
+    want2 = oracle.linear(x2, w, rows, out, k)
+    assert (ctx.linear(x2, w, rows, out, k) == want2).all()
+    assert ctx.last_gemm()[1] == 3
+    assert (ctx.linear(x2, w, rows, out, k, weight_id=wid) == want2).all()  # resident, nine planes
+    assert ctx.last_gemm()[1] == 3
+    w2 = w.copy()
+    w2[0] = -3281
+    assert (ctx.linear(x, w2, rows, out, k) == oracle.linear(x, w2, rows, out, k)).all()
+    assert ctx.last_gemm()[1] == 3
+
+
+def test_small_codes_at_the_standalone_gemm_size(ctx):
+    """M = N = K = 4096, 12-bit weight codes uniform in [-2048, 2047] and int8 activations in [-127, 127]: every row
+    sum equals x · (sum of the weight rows), and 64 random output columns equal their exact dot products."""
+    n = 4096
+    rng = np.random.default_rng(2)
+    x, w = _small_codes(rng, n, n, n)
+    y = ctx.linear(x, w, n, n, n).reshape(n, n)
+    X = x.reshape(n, n).astype(np.int64)
+    W = w.reshape(n, n).astype(np.int64)
+    assert (y.sum(axis=1) == X @ W.sum(axis=0)).all()
+    cols = rng.choice(n, 64, replace=False)
+    assert (y[:, cols] == X @ W[cols].T).all()

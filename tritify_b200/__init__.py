@@ -150,6 +150,13 @@ class Context:
         self.check(st)
         return y
 
+    def last_gemm(self) -> tuple:
+        """(milliseconds, activation planes) of the last linear call's GEMM, timed with CUDA events on the context's
+        stream; planes is 1 for the small-code kernel, 3 for the nine-plane one, 0 before any call."""
+        ms, planes = ctypes.c_double(), ctypes.c_int32()
+        self.check(lib().ktmoe_linear_last_gemm(self._h, ctypes.byref(ms), ctypes.byref(planes)))
+        return ms.value, planes.value
+
     def set_weight_budget(self, nbytes: int) -> None:
         self.check(lib().ktmoe_set_weight_budget(self._h, nbytes))
 

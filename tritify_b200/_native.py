@@ -46,6 +46,7 @@ SIGNATURES = {
     "ktmoe_linear": ([_vp, _i32p, _i32p, _i64, _i64, _i64, _i64p], ctypes.c_int),
     "ktmoe_linear_weights": ([_vp, _u64, _i32p, _i32p, _i64, _i64, _i64, _i64p], ctypes.c_int),
     "ktmoe_linear_noalloc": ([_i32, _vp, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
+    "ktmoe_linear_last_gemm": ([_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)], ctypes.c_int),
     "ktmoe_set_weight_budget": ([_vp, _u64], ctypes.c_int),
     "ktmoe_resident_bytes": ([_vp, _P(_u64)], ctypes.c_int),
     "ktmoe_layer_create": ([_vp, _P(KtmoeLayerConfig), _P(_vp)], ctypes.c_int),

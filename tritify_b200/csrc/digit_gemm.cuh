@@ -34,6 +34,7 @@ constexpr int UMMA_K = 32;  // K of one kind::i8 MMA
 constexpr int NDIAG = 5;
 constexpr int THREADS = 192;
 constexpr int64_t K_EXACT_MAX = 447392;  // floor((2^31 - 1) / (3 · 1600)): one pass without int32 overflow
+constexpr int64_t K_EXACT_MAX_SMALL = 422733;  // floor((2^31 - 1) / (127 · 40)): the same for the (1, 2) planes
 
 enum : int { ERR_NONE = 0, ERR_TIMEOUT_FULL = 1, ERR_TIMEOUT_EMPTY = 2, ERR_TIMEOUT_ACCUM = 3 };
 
@@ -244,11 +245,18 @@ __device__ __forceinline__ TileInfo tile_info(const GemmArgs& a, int tile, int b
 // Persistent: gridDim.x blocks (at most one per SM) walk the raster with stride gridDim.x. The TMA producer and the
 // MMA issuer run ahead across tile boundaries; ACC accumulator buffers in TMEM let the epilogue of one tile overlap
 // the MMAs of the next.
-template <int BN, int STAGES, int ACC>
+//
+// PX, PW: digit planes of the activations and the weights. (3, 3) is every 12-trit code. (1, 2) serves small codes
+// (|x| <= 127 stored as one raw int8 plane, |w| <= 3280 as two base-81 digits): two MMAs of N = BN per K step, product
+// x·w_j on diagonal j, two diagonals recombined.
+template <int BN, int STAGES, int ACC, int PX = 3, int PW = 3>
 __global__ void __launch_bounds__(THREADS, 1)
     digit_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
+    static_assert((PX == 3 && PW == 3) || (PX == 1 && PW == 2), "plane counts");
+    constexpr int NDIAG_USED = PX + PW - 1;
     using C = Cfg<BN, STAGES, ACC>;
+    constexpr uint32_t TX_BYTES = (uint32_t)(PW * C::A_PLANE + PX * C::B_PLANE);  // what one stage's copies bring
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
@@ -310,14 +318,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                         alive = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)C::STAGE_BYTES);
+                    mbar_arrive_expect_tx(&full[s], TX_BYTES);
                     const int kx = (args.k_block0 + kb) * BK;
 #pragma unroll
-                    for (int p = 0; p < 3; ++p) {
+                    for (int p = 0; p < PW; ++p)
                         tma_load_2d(sA + (s * 3 + p) * C::A_PLANE, &tmA, kx, (ti.group * 3 + p) * args.M_pad + m0,
                                     &full[s]);
+#pragma unroll
+                    for (int p = 0; p < PX; ++p)
                         tma_load_2d(sB + (s * 3 + p) * C::B_PLANE, &tmB, kx, p * args.R_pad + ti.row0, &full[s]);
-                    }
                 }
             }
             // Let the copies still in flight land before the block can leave (bounded).
@@ -351,24 +360,36 @@ __global__ void __launch_bounds__(THREADS, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;");
                     const uint32_t a_base = smem_u32(sA + s * 3 * C::A_PLANE);
                     const uint32_t b_base = smem_u32(sB + s * 3 * C::B_PLANE);
+                    if constexpr (PX == 3) {
+    #pragma unroll
+                        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                            const uint64_t a0 = smem_desc_sw128(a_base + 0 * C::A_PLANE + kk * UMMA_K);
+                            const uint64_t a1 = smem_desc_sw128(a_base + 1 * C::A_PLANE + kk * UMMA_K);
+                            const uint64_t a2 = smem_desc_sw128(a_base + 2 * C::A_PLANE + kk * UMMA_K);
+                            const uint64_t b0 = smem_desc_sw128(b_base + 0 * C::B_PLANE + kk * UMMA_K);
+                            const uint64_t b2 = smem_desc_sw128(b_base + 2 * C::B_PLANE + kk * UMMA_K);
+                            if (kb == kb0 && kk == 0) {
+                                // first K step: every diagonal's first product overwrites, the others accumulate
+                                umma_i8(acc + 0 * BN, a0, b0, id3, 0u);  // (0,0) (0,1) (0,2) -> diagonals 0, 1, 2
+                                umma_i8(acc + 1 * BN, a1, b0, id2, 1u);  // (1,0) (1,1)       -> diagonals 1, 2
+                                umma_i8(acc + 3 * BN, a1, b2, id1, 0u);  // (1,2)             -> diagonal 3
+                                umma_i8(acc + 2 * BN, a2, b0, id2, 1u);  // (2,0) (2,1)       -> diagonals 2, 3
+                                umma_i8(acc + 4 * BN, a2, b2, id1, 0u);  // (2,2)             -> diagonal 4
+                            } else {
+                                umma_i8(acc + 0 * BN, a0, b0, id3, 1u);
+                                umma_i8(acc + 1 * BN, a1, b0, id3, 1u);
+                                umma_i8(acc + 2 * BN, a2, b0, id3, 1u);
+                            }
+                        }
+                    } else {
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-                        const uint64_t a0 = smem_desc_sw128(a_base + 0 * C::A_PLANE + kk * UMMA_K);
-                        const uint64_t a1 = smem_desc_sw128(a_base + 1 * C::A_PLANE + kk * UMMA_K);
-                        const uint64_t a2 = smem_desc_sw128(a_base + 2 * C::A_PLANE + kk * UMMA_K);
-                        const uint64_t b0 = smem_desc_sw128(b_base + 0 * C::B_PLANE + kk * UMMA_K);
-                        const uint64_t b2 = smem_desc_sw128(b_base + 2 * C::B_PLANE + kk * UMMA_K);
-                        if (kb == kb0 && kk == 0) {
-                            // first K step: every diagonal's first product overwrites, the others accumulate
-                            umma_i8(acc + 0 * BN, a0, b0, id3, 0u);  // (0,0) (0,1) (0,2) -> diagonals 0, 1, 2
-                            umma_i8(acc + 1 * BN, a1, b0, id2, 1u);  // (1,0) (1,1)       -> diagonals 1, 2
-                            umma_i8(acc + 3 * BN, a1, b2, id1, 0u);  // (1,2)             -> diagonal 3
-                            umma_i8(acc + 2 * BN, a2, b0, id2, 1u);  // (2,0) (2,1)       -> diagonals 2, 3
-                            umma_i8(acc + 4 * BN, a2, b2, id1, 0u);  // (2,2)             -> diagonal 4
-                        } else {
-                            umma_i8(acc + 0 * BN, a0, b0, id3, 1u);
-                            umma_i8(acc + 1 * BN, a1, b0, id3, 1u);
-                            umma_i8(acc + 2 * BN, a2, b0, id3, 1u);
+                        for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                            const uint64_t bd = smem_desc_sw128(b_base + kk * UMMA_K);
+                            const uint32_t first = (kb == kb0 && kk == 0) ? 0u : 1u;  // each MMA owns its diagonal
+#pragma unroll
+                            for (int j = 0; j < PW; ++j)
+                                umma_i8(acc + j * BN, smem_desc_sw128(a_base + j * C::A_PLANE + kk * UMMA_K), bd,
+                                        id1, first);
                         }
                     }
                     umma_commit(&empty[s]);  // frees the stage once these MMAs have read it
@@ -408,9 +429,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (ok) {
                     tmem_ld16(lane_addr + 0 * BN + c * 16, s0);
                     tmem_ld16(lane_addr + 1 * BN + c * 16, s1);
-                    tmem_ld16(lane_addr + 2 * BN + c * 16, s2);
-                    tmem_ld16(lane_addr + 3 * BN + c * 16, s3);
-                    tmem_ld16(lane_addr + 4 * BN + c * 16, s4);
+                    if constexpr (NDIAG_USED == 5) {
+                        tmem_ld16(lane_addr + 2 * BN + c * 16, s2);
+                        tmem_ld16(lane_addr + 3 * BN + c * 16, s3);
+                        tmem_ld16(lane_addr + 4 * BN + c * 16, s4);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) s2[j] = s3[j] = s4[j] = 0;
+                    }
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
                 if (c == n_chunks - 1) {

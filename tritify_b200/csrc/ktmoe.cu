@@ -87,6 +87,7 @@ struct Planes {
 struct Resident {
     DevBuf buf;
     int64_t out = 0, k = 0, out_pad = 0, k_pad = 0;
+    bool small = false;  // every code within ±3280: planes 0 and 1 hold it, plane 2 is zero
     uint64_t last_use = 0;
 };
 
@@ -99,12 +100,14 @@ struct ktmoe_ctx {
     cudaStream_t stream = nullptr;
     cudaStream_t side = nullptr;  // the shared expert runs here, beside the routed experts
     cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaEvent_t ev_g0 = nullptr, ev_g1 = nullptr;  // around the last linear call's GEMM (ktmoe_linear_last_gemm)
+    int last_gemm_planes = 0;                      // 0: no GEMM timed yet; 3: nine-plane kernel; 1: (1, 2) kernel
     int* d_err = nullptr;
     std::string last_error = "";
     uint64_t launches = 0;
     std::mutex mu;
     // LinearBackend scratch
-    DevBuf lin_xi, lin_wi, lin_xp, lin_wp, lin_y, lin_bad;
+    DevBuf lin_xi, lin_wi, lin_xp, lin_xr, lin_wp, lin_y, lin_bad;
     // resident weights (linear_weights)
     std::unordered_map<uint64_t, Resident*> cache;
     uint64_t budget = 0, resident = 0, tick = 0;
@@ -148,17 +151,17 @@ int make_map(ktmoe_ctx* ctx, CUtensorMap* map, const void* base, int64_t k_pad, 
     return KTMOE_OK;
 }
 
-template <int BN, int ST, int ACC>
+template <int BN, int ST, int ACC, int PX = 3, int PW = 3>
 int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
                   const dg::GemmArgs& args) {
     using Cf = dg::Cfg<BN, ST, ACC>;
     static bool attr_set[64] = {};
     if (!attr_set[ctx->device & 63]) {
-        CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST, ACC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                Cf::SMEM_BYTES));
+        CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST, ACC, PX, PW>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES));
         attr_set[ctx->device & 63] = true;
     }
-    dg::digit_gemm_kernel<BN, ST, ACC><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
+    dg::digit_gemm_kernel<BN, ST, ACC, PX, PW><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
     CKL(ctx);
     return KTMOE_OK;
 }
@@ -206,7 +209,8 @@ int launch_gemm_pair(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, con
 struct GemmCall {
     Planes A;        // weights: groups x 3 x M_pad x k_pad
     int64_t M_valid;
-    Planes B;        // activations: 3 x R_pad x k_pad
+    Planes B;        // activations: 3 x R_pad x k_pad (one raw plane R_pad x k_pad when `small`)
+    bool small = false;  // |x| <= 127 and |w| <= 3280: the (1, 2) plane GEMM on weight planes 0 and 1
     int64_t* out;
     int64_t ld_out;
     int BN;
@@ -225,7 +229,7 @@ struct GemmCall {
 // Launch the digit GEMM, splitting K into chunks whose int32 diagonal sums cannot overflow.
 int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (g.grid_y <= 0 || g.M_valid <= 0) return KTMOE_OK;
-    const bool pair = g.BN == dg::pair::BN && g.A.rows_pad % dg::pair::BM2 == 0 && pair_enabled();
+    const bool pair = !g.small && g.BN == dg::pair::BN && g.A.rows_pad % dg::pair::BM2 == 0 && pair_enabled();
     const int64_t group_n = std::min<int64_t>(16, g.grid_y);
     const int64_t m_tiles = g.A.rows_pad / (pair ? dg::pair::BM2 : dg::BM);
     const int64_t n_groups = (g.grid_y + group_n - 1) / group_n;
@@ -233,10 +237,10 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     CUtensorMap ma, mb;
     int r = make_map(ctx, &ma, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, dg::BM);
     if (r) return r;
-    r = make_map(ctx, &mb, g.B.ptr, g.B.k_pad, 3 * g.B.rows_pad, pair ? dg::pair::BOX_ROWS : g.BN);
+    r = make_map(ctx, &mb, g.B.ptr, g.B.k_pad, (g.small ? 1 : 3) * g.B.rows_pad, pair ? dg::pair::BOX_ROWS : g.BN);
     if (r) return r;
     const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
-    const int64_t chunk_kb = dg::K_EXACT_MAX / dg::BK;
+    const int64_t chunk_kb = (g.small ? dg::K_EXACT_MAX_SMALL : dg::K_EXACT_MAX) / dg::BK;
     if (g.rowmax && total_kb > chunk_kb) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "fused row max with a chunked K");
     // Split K when the tiles cannot fill the SMs (small row counts): one output matrix (no groups), one K chunk, the
     // one-SM kernel; the row maxima then come from a pass over the finished output. KTMOE_SPLITK=0 turns it off.
@@ -279,6 +283,17 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.k_splits = ks;
         if (pair) {
             r = launch_gemm_pair(ctx, st, ma, mb, m_tiles * group_n * n_groups, a);
+            if (r) return r;
+            continue;
+        }
+        if (g.small) {
+            switch (g.BN) {
+                case 16: r = launch_gemm_t<16, 4, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
+                case 32: r = launch_gemm_t<32, 3, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
+                case 48: r = launch_gemm_t<48, 3, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
+                case 64: r = launch_gemm_t<64, 3, 1, 1, 2>(ctx, st, ma, mb, grid, a); break;
+                default: return fail(ctx, KTMOE_ERR_ARG, "unsupported BN");
+            }
             if (r) return r;
             continue;
         }
@@ -1560,7 +1575,8 @@ int ktmoe_open(int device, ktmoe_ctx** out) {
     }
     if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess) {
+        cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreate(&ctx->ev_g0) != cudaSuccess || cudaEventCreate(&ctx->ev_g1) != cudaSuccess) {
         delete ctx;
         return KTMOE_ERR_CUDA;
     }
@@ -1583,6 +1599,7 @@ int ktmoe_close(ktmoe_ctx* ctx) {
     ctx->lin_xi.release();
     ctx->lin_wi.release();
     ctx->lin_xp.release();
+    ctx->lin_xr.release();
     ctx->lin_wp.release();
     ctx->lin_y.release();
     ctx->lin_bad.release();
@@ -1591,6 +1608,8 @@ int ktmoe_close(ktmoe_ctx* ctx) {
     if (ctx->side) cudaStreamDestroy(ctx->side);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+    if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
+    if (ctx->ev_g1) cudaEventDestroy(ctx->ev_g1);
     delete ctx;
     return KTMOE_OK;
 }
@@ -1642,10 +1661,17 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     const int64_t k_pad = round_up(k, dg::BK);
     // weights of more than one 128-row tile are padded to 256 rows, so that wide calls can use the pair GEMM
     const int64_t out_pad = out > dg::BM ? round_up(out, dg::pair::BM2) : dg::BM;
-    const int BN = pick_bn((double)rows, out_pad % dg::pair::BM2 == 0);
     const int64_t rows_pad = round_up(rows, 64);
-    CK(ctx->lin_bad.ensure(8));
-    CK(cudaMemsetAsync(ctx->lin_bad.p, 0, 8, st));
+    // counters: [0] codes beyond +-WLEVELS, [1] weight codes beyond +-3280, [2] activation codes beyond +-127
+    CK(ctx->lin_bad.ensure(24));
+    CK(cudaMemsetAsync(ctx->lin_bad.p, 0, 24, st));
+    unsigned long long* counters = ctx->lin_bad.as<unsigned long long>();
+    // Small codes (|x| <= 127, |w| <= 3280) take the (1, 2) plane GEMM unless KTMOE_SMALL=0.
+    static const bool small_enabled = [] {
+        const char* e = getenv("KTMOE_SMALL");
+        return !(e && e[0] == '0');
+    }();
+    bool small_w = false;
     // weights: resident by id, else packed for this call
     Planes W{nullptr, 1, out_pad, k, k_pad};
     Resident* res = nullptr;
@@ -1654,11 +1680,19 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
         if (it != ctx->cache.end() && it->second->out == out && it->second->k == k) {
             res = it->second;
             res->last_use = ++ctx->tick;
+        } else if (it != ctx->cache.end()) {
+            // the id now names weights of another shape: drop the old planes before packing the new ones
+            CK(cudaStreamSynchronize(st));
+            ctx->resident -= it->second->buf.bytes;
+            it->second->buf.release();
+            delete it->second;
+            ctx->cache.erase(it);
         }
     }
-    unsigned long long hbad_w = 0;
+    unsigned long long hbad_w[2] = {0, 0};
     if (res) {
         W.ptr = res->buf.as<int8_t>();
+        small_w = res->small;
     } else {
         const size_t wbytes = (size_t)(3 * out_pad * k_pad);
         DevBuf* target = &ctx->lin_wp;
@@ -1686,11 +1720,12 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
         CK(ctx->lin_wi.ensure((size_t)(out * k) * 4));
         CK(cudaMemcpyAsync(ctx->lin_wi.p, w, (size_t)(out * k) * 4, cudaMemcpyHostToDevice, st));
         mk::pack_codes_kernel<<<(unsigned)out, 128, 0, st>>>(ctx->lin_wi.as<int32_t>(), out, (int)k, (int)k_pad, out_pad,
-                                                            target->as<int8_t>(), ctx->lin_bad.as<unsigned long long>());
+                                                            target->as<int8_t>(), counters, counters + 1, 3280);
         CKL(ctx);
-        CK(cudaMemcpyAsync(&hbad_w, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(hbad_w, ctx->lin_bad.p, 16, cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
-        if (hbad_w) {
+        small_w = hbad_w[1] == 0;
+        if (hbad_w[0]) {
             delete fresh;
             return fail(ctx, KTMOE_ERR_RANGE, "a weight code lies outside +-WLEVELS");
         }
@@ -1699,6 +1734,7 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
             fresh->k = k;
             fresh->out_pad = out_pad;
             fresh->k_pad = k_pad;
+            fresh->small = small_w;
             fresh->last_use = ++ctx->tick;
             ctx->cache[*weight_id] = fresh;
             ctx->resident += fresh->buf.bytes;
@@ -1709,25 +1745,58 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     CK(ctx->lin_xp.ensure((size_t)(3 * rows_pad * k_pad)));
     CK(ctx->lin_y.ensure((size_t)(rows * out) * 8));
     CK(cudaMemcpyAsync(ctx->lin_xi.p, x, (size_t)(rows * k) * 4, cudaMemcpyHostToDevice, st));
+    // with small weights, the activations are also written as one raw plane and their range decides the kernel
+    const bool try_small = small_enabled && small_w;
+    if (try_small) CK(ctx->lin_xr.ensure((size_t)(rows_pad * k_pad)));
     mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, st>>>(ctx->lin_xi.as<int32_t>(), rows, (int)k, (int)k_pad, rows_pad,
-                                                         ctx->lin_xp.as<int8_t>(), ctx->lin_bad.as<unsigned long long>());
+                                                         ctx->lin_xp.as<int8_t>(), counters,
+                                                         try_small ? counters + 2 : nullptr, 127,
+                                                         try_small ? ctx->lin_xr.as<int8_t>() : nullptr);
     CKL(ctx);
+    bool small = false;
+    if (try_small) {
+        unsigned long long hx = 1;
+        CK(cudaMemcpyAsync(&hx, counters + 2, 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        small = hx == 0;
+    }
+    const int BN = pick_bn((double)rows, !small && out_pad % dg::pair::BM2 == 0);
     GemmCall g;
     g.A = W;
     g.M_valid = out;
-    g.B = Planes{ctx->lin_xp.as<int8_t>(), 1, rows_pad, k, k_pad};
+    g.B = small ? Planes{ctx->lin_xr.as<int8_t>(), 1, rows_pad, k, k_pad}
+                : Planes{ctx->lin_xp.as<int8_t>(), 1, rows_pad, k, k_pad};
+    g.small = small;
+    ctx->last_gemm_planes = 0;
+    CK(cudaEventRecord(ctx->ev_g0, st));
     g.out = ctx->lin_y.as<int64_t>();
     g.ld_out = out;
     g.BN = BN;
     g.grid_y = (rows + BN - 1) / BN;
     g.single_rows = rows;
     if (int r = run_gemm(ctx, st, g)) return r;
+    CK(cudaEventRecord(ctx->ev_g1, st));
     unsigned long long hbad = 0;
     CK(cudaMemcpyAsync(y, ctx->lin_y.p, (size_t)(rows * out) * 8, cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(&hbad, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     if (int r = check_err_word(ctx)) return r;
     if (hbad) return fail(ctx, KTMOE_ERR_RANGE, "an activation code lies outside +-WLEVELS");
+    ctx->last_gemm_planes = small ? 1 : 3;
+    return KTMOE_OK;
+}
+
+int ktmoe_linear_last_gemm(ktmoe_ctx* ctx, double* ms, int32_t* act_planes) {
+    if (!ctx || !ms || !act_planes) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    *ms = 0.0;
+    *act_planes = ctx->last_gemm_planes;
+    if (ctx->last_gemm_planes == 0) return KTMOE_OK;
+    CK(cudaEventSynchronize(ctx->ev_g1));
+    float t = 0.f;
+    CK(cudaEventElapsedTime(&t, ctx->ev_g0, ctx->ev_g1));
+    *ms = t;
     return KTMOE_OK;
 }
 

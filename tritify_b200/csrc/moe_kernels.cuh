@@ -1265,15 +1265,20 @@ __global__ void reduce_records_kernel(const int64_t* __restrict__ recs, int n, S
 
 // ───────────── LinearBackend helpers ─────────────
 // Pack int32 codes [rows][K] into three digit planes [3][R_pad][K_pad]; counts codes beyond ±WLEVELS into *bad.
+// Optionally counts the codes beyond ±big_lim into *big, and writes the codes as one raw int8 plane [R_pad][K_pad]
+// into `raw` (0 where |v| > 127), for the reduced-plane GEMM.
 __global__ void pack_codes_kernel(const int32_t* __restrict__ codes, long long rows, int K, int K_pad, long long R_pad,
-                                  int8_t* __restrict__ planes, unsigned long long* __restrict__ bad) {
+                                  int8_t* __restrict__ planes, unsigned long long* __restrict__ bad,
+                                  unsigned long long* __restrict__ big = nullptr, int32_t big_lim = 0,
+                                  int8_t* __restrict__ raw = nullptr) {
     const long long r = blockIdx.x;
     if (r >= rows) return;
     const int32_t* c = codes + r * K;
     int8_t* p0 = planes + r * K_pad;
     int8_t* p1 = p0 + R_pad * K_pad;
     int8_t* p2 = p1 + R_pad * K_pad;
-    unsigned nbad = 0;
+    int8_t* pr = raw ? raw + r * K_pad : nullptr;
+    unsigned nbad = 0, nbig = 0;
     for (int k4 = threadIdx.x * 4; k4 < K_pad; k4 += blockDim.x * 4) {
         int32_t q[4];
 #pragma unroll
@@ -1284,11 +1289,22 @@ __global__ void pack_codes_kernel(const int32_t* __restrict__ codes, long long r
                 ++nbad;
                 v = 0;
             }
+            nbig += (v > big_lim || v < -big_lim) ? 1u : 0u;
             q[j] = v;
         }
         store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+        if (pr) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int32_t v = (q[j] > 127 || q[j] < -127) ? 0 : q[j];
+                packed |= (uint32_t)(uint8_t)(int8_t)v << (8 * j);
+            }
+            *reinterpret_cast<uint32_t*>(pr + k4) = packed;  // K_pad is a multiple of 64: 4-byte aligned
+        }
     }
     if (nbad && bad) atomicAdd(bad, (unsigned long long)nbad);
+    if (nbig && big) atomicAdd(big, (unsigned long long)nbig);
 }
 
 }  // namespace mk
