@@ -176,3 +176,33 @@ def test_small_codes_at_the_standalone_gemm_size(ctx):
     assert (y.sum(axis=1) == X @ W.sum(axis=0)).all()
     cols = rng.choice(n, 64, replace=False)
     assert (y[:, cols] == X @ W[cols].T).all()
+
+
+@pytest.mark.parametrize("rows,out,k", [(300, 1000, 4096), (256, 256, 128), (1000, 384, 3000), (129, 130, 200)])
+def test_small_codes_pair_and_single_sm_agree(ctx, oracle, rows, out, k, monkeypatch):
+    """From 128 activation rows on, small codes run on SM pairs (256 activation rows x 128 weight rows per tile);
+    KTMOE_PAIR=0 keeps them on the one-SM (1, 2) kernel. Both equal the CPU path."""
+    rng = np.random.default_rng(rows + 3 * out + k)
+    x, w = _small_codes(rng, rows, out, k)
+    want = oracle.linear(x, w, rows, out, k)
+    for flag in ("1", "0"):
+        monkeypatch.setenv("KTMOE_PAIR", flag)
+        got = ctx.linear(x, w, rows, out, k)
+        assert ctx.last_gemm()[1] == 1
+        bad = np.nonzero(got != want)[0]
+        assert bad.size == 0, f"KTMOE_PAIR={flag}: {bad.size} of {got.size} differ; first at {bad[:5]}"
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_small_codes_beyond_one_exact_chunk(ctx, pair, monkeypatch):
+    """K = 450 000 of the largest small codes (x = ±127, w = ±3280, every digit ±40): one int32 diagonal would
+    overflow, so K is split at 422 733 and the int64 partials added."""
+    monkeypatch.setenv("KTMOE_PAIR", pair)
+    rows, out, k = 128, 2, 450_000
+    x = np.full(rows * k, 127, np.int32)
+    x[k:2 * k] = -127
+    w = np.concatenate([np.full(k, 3280, np.int32), np.full(k, -3280, np.int32)])
+    y = ctx.linear(x, w, rows, out, k).reshape(rows, out)
+    assert ctx.last_gemm()[1] == 1
+    e = k * 127 * 3280
+    assert y[0].tolist() == [e, -e] and y[1].tolist() == [-e, e] and (y[2:] == y[0]).all()

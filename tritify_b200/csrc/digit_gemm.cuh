@@ -67,26 +67,24 @@ struct GemmArgs {
     int k_splits;
 };
 
-// TMEM columns to allocate for `accbn` = (buffers x BN): a power of two >= 32 covering five diagonals each.
-__host__ __device__ constexpr int tmem_cols_for(int accbn) {
-    return (NDIAG * accbn <= 32)    ? 32
-           : (NDIAG * accbn <= 64)  ? 64
-           : (NDIAG * accbn <= 128) ? 128
-           : (NDIAG * accbn <= 256) ? 256
-                                    : 512;
-}
-
-template <int BN, int STAGES, int ACC>
+// PX, PW: digit planes of the activations and the weights per stage (3, 3 for any code; 1, 2 for small codes).
+template <int BN, int STAGES, int ACC, int PX = 3, int PW = 3>
 struct Cfg {
     static constexpr int A_PLANE = BM * BK;
     static constexpr int B_PLANE = BN * BK;
-    static constexpr int STAGE_BYTES = 3 * (A_PLANE + B_PLANE);
-    static constexpr int ACC_COLS = NDIAG * BN;  // one accumulator buffer: five diagonals of BN columns
-    static constexpr int TMEM_COLS = tmem_cols_for(ACC * BN);
+    static constexpr int STAGE_BYTES = PW * A_PLANE + PX * B_PLANE;
+    static constexpr int DIAGS = PX + PW - 1;
+    static constexpr int ACC_COLS = DIAGS * BN;  // one accumulator buffer: a diagonal of BN columns per plane sum
+    static constexpr int TMEM_COLS = ACC * ACC_COLS <= 32    ? 32
+                                     : ACC * ACC_COLS <= 64  ? 64
+                                     : ACC * ACC_COLS <= 128 ? 128
+                                     : ACC * ACC_COLS <= 256 ? 256
+                                                             : 512;
     static constexpr int RED_BYTES = 2 * 4 * BN * 8;  // row-max staging: [slot][epilogue warp][column]
     static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256 + RED_BYTES;
-    static_assert(BN % 16 == 0 && BN >= 16 && 3 * BN <= 256, "BN: a multiple of 16, 3·BN <= 256");
-    static_assert(ACC * NDIAG * BN <= 512, "the accumulator buffers must fit TMEM");
+    static_assert((PX == 3 && PW == 3) || (PX == 1 && PW == 2), "plane counts");
+    static_assert(BN % 16 == 0 && BN >= 16 && PX * BN <= 256, "BN: a multiple of 16, PX·BN <= 256 (one MMA's N)");
+    static_assert(ACC * ACC_COLS <= 512, "the accumulator buffers must fit TMEM");
     static_assert(B_PLANE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
     static_assert(SMEM_BYTES <= 232448, "shared memory per block");
 };
@@ -253,14 +251,13 @@ template <int BN, int STAGES, int ACC, int PX = 3, int PW = 3>
 __global__ void __launch_bounds__(THREADS, 1)
     digit_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
-    static_assert((PX == 3 && PW == 3) || (PX == 1 && PW == 2), "plane counts");
-    constexpr int NDIAG_USED = PX + PW - 1;
-    using C = Cfg<BN, STAGES, ACC>;
-    constexpr uint32_t TX_BYTES = (uint32_t)(PW * C::A_PLANE + PX * C::B_PLANE);  // what one stage's copies bring
+    using C = Cfg<BN, STAGES, ACC, PX, PW>;
+    constexpr int NDIAG_USED = C::DIAGS;
+    constexpr uint32_t TX_BYTES = (uint32_t)C::STAGE_BYTES;  // what one stage's copies bring
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * 3 * C::A_PLANE;
+    uint8_t* sA = smem;                              // [STAGES][PW] weight planes
+    uint8_t* sB = smem + STAGES * PW * C::A_PLANE;   // [STAGES][PX] activation planes
     uint64_t* full = (uint64_t*)(smem + STAGES * C::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;     // [ACC]: the MMAs of a tile completed into buffer b
@@ -322,11 +319,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int kx = (args.k_block0 + kb) * BK;
 #pragma unroll
                     for (int p = 0; p < PW; ++p)
-                        tma_load_2d(sA + (s * 3 + p) * C::A_PLANE, &tmA, kx, (ti.group * 3 + p) * args.M_pad + m0,
+                        tma_load_2d(sA + (s * PW + p) * C::A_PLANE, &tmA, kx, (ti.group * 3 + p) * args.M_pad + m0,
                                     &full[s]);
 #pragma unroll
                     for (int p = 0; p < PX; ++p)
-                        tma_load_2d(sB + (s * 3 + p) * C::B_PLANE, &tmB, kx, p * args.R_pad + ti.row0, &full[s]);
+                        tma_load_2d(sB + (s * PX + p) * C::B_PLANE, &tmB, kx, p * args.R_pad + ti.row0, &full[s]);
                 }
             }
             // Let the copies still in flight land before the block can leave (bounded).
@@ -337,7 +334,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             // The three activation planes sit back to back in shared memory, so one MMA of N = 3·BN multiplies a
             // weight plane i by all three: its D starts at column i·BN and product (i, j) lands on diagonal i+j.
-            constexpr uint32_t id1 = idesc_i8(BN), id2 = idesc_i8(2 * BN), id3 = idesc_i8(3 * BN);
+            constexpr uint32_t id1 = idesc_i8(BN), id2 = idesc_i8(PX * BN >= 2 * BN ? 2 * BN : BN),
+                               id3 = idesc_i8(PX * BN >= 3 * BN ? 3 * BN : BN);
             int q = 0, tc = 0;
             bool alive = true;
             int tile, m0, split;
@@ -358,10 +356,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;");
-                    const uint32_t a_base = smem_u32(sA + s * 3 * C::A_PLANE);
-                    const uint32_t b_base = smem_u32(sB + s * 3 * C::B_PLANE);
+                    const uint32_t a_base = smem_u32(sA + s * PW * C::A_PLANE);
+                    const uint32_t b_base = smem_u32(sB + s * PX * C::B_PLANE);
                     if constexpr (PX == 3) {
-    #pragma unroll
+#pragma unroll
                         for (int kk = 0; kk < BK / UMMA_K; ++kk) {
                             const uint64_t a0 = smem_desc_sw128(a_base + 0 * C::A_PLANE + kk * UMMA_K);
                             const uint64_t a1 = smem_desc_sw128(a_base + 1 * C::A_PLANE + kk * UMMA_K);

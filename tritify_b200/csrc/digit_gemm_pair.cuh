@@ -404,4 +404,227 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
     }
 }
 
+
+// ───────────── small codes on an SM pair ─────────────
+// The (1, 2) product (one raw activation plane, |x| <= 127; two weight digit planes, |w| <= 3280) with the roles of
+// the kernel above swapped: the MMA's M side is 256 activation rows (128 in each SM's shared memory and TMEM), its N
+// side the two digit planes of 128 weight rows stacked (N = 256; SM 0 holds plane 0, SM 1 plane 1). One
+// tcgen05.mma.cta_group::2 per 32-byte K step puts x·w0 into columns 0-127 and x·w1 into columns 128-255 of each SM's
+// accumulator: the two diagonals. Per K step an SM takes 8 KB from TMA and its MMA reads 8 KB of shared memory for
+// 128 tensor cycles (128 B/clk), against 224 B/clk for the one-SM (1, 2) kernel at BN = 128. Two accumulator buffers
+// of 256 columns let the epilogue of one tile overlap the MMAs of the next. A TMEM lane is an activation row, so an
+// epilogue thread writes 16 consecutive int64 outputs (128 bytes) of its row per step. No fused row maxima and no
+// split K: the LinearBackend path is its only user. No load uses cluster multicast; every wait is bounded.
+namespace pair_small {
+
+constexpr int BM_ACT = 256;                         // activation rows per pair tile (128 per SM)
+constexpr int BN_W = 128;                           // weight rows per tile
+constexpr int N = 2 * BN_W;                         // the two weight planes, stacked
+constexpr int THREADS = 192;                        // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer (CTA 0)
+constexpr int EPI_WARPS = 4;
+constexpr int STAGES = 6;
+constexpr int ACC = 2;
+constexpr int X_TILE = 128 * BK;                    // 16 KB: this SM's activation rows
+constexpr int W_TILE = BN_W * BK;                   // 16 KB: this SM's weight plane
+constexpr int CTA_STAGE_BYTES = X_TILE + W_TILE;
+constexpr int ACC_COLS = N;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = 1024 + STAGES * CTA_STAGE_BYTES + 256;
+static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+static_assert(ACC * ACC_COLS <= TMEM_COLS, "the accumulator buffers must fit TMEM");
+static_assert(X_TILE % 1024 == 0 && W_TILE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
+
+// kind::i8 instruction descriptor: D = s32, A = B = s8, K-major, M = 256, N = 256.
+__host__ __device__ constexpr uint32_t idesc() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(BM_ACT >> 4) << 24);
+}
+
+// Slot L of the raster: activation tile `at` (256 rows) and weight rows w0.. (128). group_n consecutive activation
+// tiles share each weight tile, as in the other kernels (args.m_tiles counts 128-row weight tiles here,
+// args.n_tiles_max activation tiles).
+__device__ __forceinline__ bool tile_of(const GemmArgs& a, int per_group, int limit, int L, int& at, int& w0) {
+    if (L >= limit) return false;
+    const int grp = L / per_group, rem = L % per_group;
+    at = grp * a.group_n + rem % a.group_n;
+    w0 = (rem / a.group_n) * BN_W;
+    return true;
+}
+
+}  // namespace pair_small
+
+// tmX: the activations' raw plane [R_pad][k_pad]; tmW: the weight planes [3][M_pad][k_pad] (planes 0 and 1 used).
+// out[r][m] (+= with args.accumulate) for r < single_rows, m < M_valid. Launched with clusters of 2 CTAs.
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_small::THREADS, 1)
+    digit_gemm_pair_small_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                                 const GemmArgs args) {
+    using namespace pair;
+    namespace ps = pair_small;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* sX = smem;                                  // [STAGES][128 rows][BK]
+    uint8_t* sW = smem + ps::STAGES * ps::X_TILE;        // [STAGES][128 rows][BK]
+    uint64_t* full = (uint64_t*)(smem + ps::STAGES * ps::CTA_STAGE_BYTES);
+    uint64_t* empty = full + ps::STAGES;
+    uint64_t* acc_full = empty + ps::STAGES;  // [ACC]: this CTA's accumulator half is complete (commit from CTA 0)
+    uint64_t* acc_empty = acc_full + ps::ACC;  // [ACC], CTA 0: both CTAs' epilogues have read buffer b (8 arrivals)
+    uint64_t* mma_done = acc_empty + ps::ACC;  // every MMA of the pair has completed (waited before TMEM is freed)
+    uint32_t* tmem_slot = (uint32_t*)(mma_done + 1);
+
+    const uint32_t rank = cta_rank();
+    const int cid = (int)cluster_index(), ncl = (int)cluster_count();
+    const int n_at = args.n_tiles_max;
+    const int n_groups = (n_at + args.group_n - 1) / args.group_n;
+    const int per_group = args.m_tiles * args.group_n, limit = per_group * n_groups;
+    // Both CTAs of a cluster see the same cid, so they leave together, before any barrier or allocation.
+    if (cid >= limit) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nkb = args.num_k_blocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ps::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < ps::ACC; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * ps::EPI_WARPS);
+        }
+        mbar_init(mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(ps::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        asm volatile("tcgen05.fence::before_thread_sync;");
+    }
+    __syncthreads();
+    cluster_sync_all();  // the peer's barriers are initialised before anyone signals them
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+            int q = 0;
+            bool alive = true;
+            int at, w0;
+            for (int L = cid; alive && ps::tile_of(args, per_group, limit, L, at, w0); L += ncl) {
+                if (at >= n_at) continue;
+                const int x0 = at * ps::BM_ACT + (int)rank * 128;
+                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                    const int s = q % ps::STAGES;
+                    const uint32_t ph = (uint32_t)(q / ps::STAGES) & 1u;
+                    if (!wait(&empty[s], ph ^ 1u, args.err, ERR_TIMEOUT_EMPTY)) {
+                        alive = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], (uint32_t)(2 * ps::CTA_STAGE_BYTES));
+                    const uint32_t bar = peer_addr(&full[s], 0);
+                    const int kx = (args.k_block0 + kb) * BK;
+                    tma_load_2d_to(sX + s * ps::X_TILE, &tmX, kx, x0, bar);
+                    tma_load_2d_to(sW + s * ps::W_TILE, &tmW, kx, (int)rank * args.M_pad + w0, bar);
+                }
+            }
+            // CTA 0 lets every copy still in flight (its own and the peer's) land before the pair can leave.
+            if (rank == 0)
+                for (int j = max(0, q - ps::STAGES); j < q; ++j)
+                    wait(&full[j % ps::STAGES], (uint32_t)(j / ps::STAGES) & 1u, args.err, ERR_TIMEOUT_FULL, true);
+        }
+    } else if (warp == 5) {
+        if (lane == 0 && rank == 0) {
+            constexpr uint32_t id = ps::idesc();
+            int q = 0, tc = 0;
+            bool alive = true;
+            int at, w0;
+            for (int L = cid; alive && ps::tile_of(args, per_group, limit, L, at, w0); L += ncl) {
+                if (at >= n_at) continue;
+                const int b = tc % ps::ACC;
+                const uint32_t acc = tmem + (uint32_t)(b * ps::ACC_COLS);
+                // buffer b is free once both epilogues have read its previous tile (the first use passes at once)
+                if (!wait(&acc_empty[b], ((uint32_t)(tc / ps::ACC) & 1u) ^ 1u, args.err, ERR_TIMEOUT_ACCUM)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                for (int kb = 0; kb < nkb; ++kb, ++q) {
+                    const int s = q % ps::STAGES;
+                    const uint32_t ph = (uint32_t)(q / ps::STAGES) & 1u;
+                    if (!wait(&full[s], ph, args.err, ERR_TIMEOUT_FULL)) {
+                        alive = false;
+                        break;
+                    }
+                    asm volatile("tcgen05.fence::after_thread_sync;");
+                    const uint32_t x_base = smem_u32(sX + s * ps::X_TILE);
+                    const uint32_t w_base = smem_u32(sW + s * ps::W_TILE);
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk)
+                        umma_i8_pair(acc, smem_desc_sw128(x_base + kk * UMMA_K), smem_desc_sw128(w_base + kk * UMMA_K),
+                                     id, (kb == 0 && kk == 0) ? 0u : 1u);
+                    umma_commit_both(&empty[s]);
+                }
+                umma_commit_both(&acc_full[b]);
+                ++tc;
+            }
+            umma_commit_both(mma_done);
+            wait(mma_done, 0u, args.err, ERR_TIMEOUT_ACCUM, true);
+        }
+    } else {
+        // Epilogue: warp w reads TMEM lanes 32w..32w+31; lane l holds activation row x0 + 32w + l.
+        int tc = 0;
+        int at, w0;
+        for (int L = cid; ps::tile_of(args, per_group, limit, L, at, w0); L += ncl) {
+            if (at >= n_at) continue;
+            const int b = tc % ps::ACC;
+            bool ok = wait(&acc_full[b], (uint32_t)(tc / ps::ACC) & 1u, args.err, ERR_TIMEOUT_ACCUM);
+            ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective: keep the branch warp-uniform
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t lane_base = tmem + (uint32_t)(b * ps::ACC_COLS) + ((uint32_t)(warp * 32) << 16);
+            const int r = at * ps::BM_ACT + (int)rank * 128 + warp * 32 + lane;
+            const bool r_ok = r < args.single_rows;
+            int64_t* orow = args.out + (long long)(r_ok ? r : 0) * args.ld_out;
+#pragma unroll 1
+            for (int c = 0; c < ps::BN_W / 16; ++c) {
+                int32_t s0[16], s1[16];
+                if (ok) {
+                    tmem_ld16(lane_base + c * 16, s0);
+                    tmem_ld16(lane_base + ps::BN_W + c * 16, s1);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                }
+                if (c == ps::BN_W / 16 - 1) {
+                    // this warp has read all of buffer b: the MMAs of a later tile may overwrite it
+                    asm volatile("tcgen05.fence::before_thread_sync;");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(peer_addr(&acc_empty[b], 0));
+                }
+                if (!ok || !r_ok) continue;
+                const int m = w0 + c * 16;
+                int64_t v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = (int64_t)s0[j] + 81LL * s1[j];
+                int64_t* p = orow + m;
+                if (m + 16 <= args.M_valid && !args.accumulate && ((reinterpret_cast<uintptr_t>(p) & 15u) == 0)) {
+#pragma unroll
+                    for (int j = 0; j < 16; j += 2)
+                        *reinterpret_cast<longlong2*>(p + j) = make_longlong2(v[j], v[j + 1]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (m + j >= args.M_valid) break;
+                        int64_t x = v[j];
+                        if (args.accumulate) x += p[j];
+                        p[j] = x;
+                    }
+                }
+            }
+            ++tc;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    cluster_sync_all();  // neither CTA frees TMEM or leaves while the pair's MMAs, copies or arrivals may touch it
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ps::TMEM_COLS));
+    }
+}
+
 }  // namespace dg

@@ -154,7 +154,7 @@ int make_map(ktmoe_ctx* ctx, CUtensorMap* map, const void* base, int64_t k_pad, 
 template <int BN, int ST, int ACC, int PX = 3, int PW = 3>
 int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
                   const dg::GemmArgs& args) {
-    using Cf = dg::Cfg<BN, ST, ACC>;
+    using Cf = dg::Cfg<BN, ST, ACC, PX, PW>;
     static bool attr_set[64] = {};
     if (!attr_set[ctx->device & 63]) {
         CK(cudaFuncSetAttribute(dg::digit_gemm_kernel<BN, ST, ACC, PX, PW>,
@@ -226,9 +226,95 @@ struct GemmCall {
     int64_t rowmax_split = 0;
 };
 
+// The small-code GEMM on SM pairs (dg::digit_gemm_pair_small_kernel): 256 activation rows x 128 weight rows per
+// tile, clusters of 2, one launch per K chunk.
+int launch_gemm_pair_small(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& mx, const CUtensorMap& mw,
+                           int64_t slots, const dg::GemmArgs& args) {
+    namespace ps = dg::pair_small;
+    static bool attr_set[64] = {};
+    static int clusters_of[64] = {};
+    const int dev = ctx->device & 63;
+    if (!attr_set[dev]) {
+        CK(cudaFuncSetAttribute(dg::digit_gemm_pair_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                ps::SMEM_BYTES));
+        attr_set[dev] = true;
+    }
+    if (clusters_of[dev] == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(2 * (ctx->num_sms / 2)));
+        cfg.blockDim = dim3(ps::THREADS);
+        cfg.dynamicSmemBytes = ps::SMEM_BYTES;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, dg::digit_gemm_pair_small_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = ctx->num_sms / 2;
+        }
+        clusters_of[dev] = std::min(n, ctx->num_sms / 2);
+    }
+    const int64_t clusters = std::min<int64_t>(slots, clusters_of[dev]);
+    dg::digit_gemm_pair_small_kernel<<<dim3((unsigned)(2 * clusters)), ps::THREADS, ps::SMEM_BYTES, st>>>(mx, mw,
+                                                                                                      args);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+// Small codes with at least 128 activation rows, one weight matrix and no fused row maxima go to the SM pairs
+// (KTMOE_PAIR=0 keeps them on the one-SM (1, 2) kernel).
+bool small_pair_ok(const GemmCall& g) {
+    return g.small && pair_enabled() && g.single_rows >= 128 && !g.rowmax && !g.tile_group && !g.tile_row0 &&
+           !g.group_end && !g.tile_row_end && !g.n_tiles && g.A.groups == 1 &&
+           g.A.rows_pad % dg::pair_small::BN_W == 0;
+}
+
+int run_gemm_small_pair(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
+    namespace ps = dg::pair_small;
+    const int64_t rows = g.single_rows;
+    const int64_t w_tiles = g.A.rows_pad / ps::BN_W;
+    const int64_t a_tiles = (rows + ps::BM_ACT - 1) / ps::BM_ACT;
+    const int64_t group_n = std::min<int64_t>(16, a_tiles);
+    const int64_t n_groups = (a_tiles + group_n - 1) / group_n;
+    const int64_t slots = w_tiles * group_n * n_groups;
+    if (slots > INT32_MAX) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "too many tiles for one launch");
+    CUtensorMap mx, mw;
+    int r = make_map(ctx, &mx, g.B.ptr, g.B.k_pad, g.B.rows_pad, 128);
+    if (r) return r;
+    r = make_map(ctx, &mw, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, ps::BN_W);
+    if (r) return r;
+    const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
+    const int64_t chunk_kb = dg::K_EXACT_MAX_SMALL / dg::BK;
+    for (int64_t kb0 = 0; kb0 < total_kb; kb0 += chunk_kb) {
+        dg::GemmArgs a{};
+        a.out = g.out;
+        a.ld_out = g.ld_out;
+        a.M_valid = (int)g.M_valid;
+        a.M_pad = (int)g.A.rows_pad;
+        a.k_block0 = (int)kb0;
+        a.num_k_blocks = (int)std::min(chunk_kb, total_kb - kb0);
+        a.R_pad = (int)g.B.rows_pad;
+        a.n_tiles_max = (int)a_tiles;
+        a.m_tiles = (int)w_tiles;
+        a.group_n = (int)group_n;
+        a.single_rows = (int)rows;
+        a.accumulate = kb0 > 0 ? 1 : 0;
+        a.err = ctx->d_err;
+        a.k_splits = 1;
+        r = launch_gemm_pair_small(ctx, st, mx, mw, slots, a);
+        if (r) return r;
+    }
+    return KTMOE_OK;
+}
+
 // Launch the digit GEMM, splitting K into chunks whose int32 diagonal sums cannot overflow.
 int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (g.grid_y <= 0 || g.M_valid <= 0) return KTMOE_OK;
+    if (small_pair_ok(g)) return run_gemm_small_pair(ctx, st, g);
     const bool pair = !g.small && g.BN == dg::pair::BN && g.A.rows_pad % dg::pair::BM2 == 0 && pair_enabled();
     const int64_t group_n = std::min<int64_t>(16, g.grid_y);
     const int64_t m_tiles = g.A.rows_pad / (pair ? dg::pair::BM2 : dg::BM);
@@ -292,6 +378,7 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
                 case 32: r = launch_gemm_t<32, 3, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
                 case 48: r = launch_gemm_t<48, 3, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
                 case 64: r = launch_gemm_t<64, 3, 1, 1, 2>(ctx, st, ma, mb, grid, a); break;
+                case 128: r = launch_gemm_t<128, 4, 2, 1, 2>(ctx, st, ma, mb, grid, a); break;
                 default: return fail(ctx, KTMOE_ERR_ARG, "unsupported BN");
             }
             if (r) return r;
@@ -330,6 +417,20 @@ int pick_bn(double rows_per_group, bool pair_ok = false) {
     if (rows_per_group >= 40.0) return 48;
     if (rows_per_group >= 20.0) return 32;
     return 16;
+}
+
+// Activation rows per tile of the small-code (1, 2) kernel: 128 once there are enough rows — two MMAs of N = 128
+// per K step against 48 KB of operands per 128-byte K block, with two accumulator buffers of 2·128 TMEM columns —
+// else the one-SM choice of the nine-plane kernel. KTMOE_BN_SMALL overrides it (16/32/48/64/128).
+int pick_bn_small(double rows) {
+    static int forced = [] {
+        const char* e = getenv("KTMOE_BN_SMALL");
+        int v = e ? atoi(e) : 0;
+        return (v == 16 || v == 32 || v == 48 || v == 64 || v == 128) ? v : 0;
+    }();
+    if (forced) return forced;
+    if (rows >= 96.0) return 128;
+    return pick_bn(rows, false);
 }
 
 __global__ void sqx_kernel(const unsigned long long* gxmax, const Scale* x_scale, Scale* out) {
@@ -1760,7 +1861,7 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
         CK(cudaStreamSynchronize(st));
         small = hx == 0;
     }
-    const int BN = pick_bn((double)rows, !small && out_pad % dg::pair::BM2 == 0);
+    const int BN = small ? pick_bn_small((double)rows) : pick_bn((double)rows, out_pad % dg::pair::BM2 == 0);
     GemmCall g;
     g.A = W;
     g.M_valid = out;
