@@ -44,9 +44,27 @@ WORKLOADS = {
     "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
     "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
     # the standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
-    # activations uniform in [-127, 127], seed 2 (1 GPU).
+    # activations uniform in [-127, 127] from the reference's LCG, seed 2 (1 GPU).
     "gemm4096": dict(gemm=True, M=4096, N=4096, K=4096, seed=2),
+    # The reference's LinearBackend benchmark shapes (kt-runtime/examples/cuda_bench.rs:59-66): an OLMoE-sized prefill,
+    # a Qwen decode projection, Qwen's LM head and a row sweep, full-range 12-trit codes from the test LCG.
+    "cuda_bench": dict(linear_bench=True),
 }
+LINEAR_METRIC = "LinearBackend MMAC/s over the reference's cuda_bench shapes (exact int64, resident weights)"
+
+
+def linear_bench_shapes():
+    """(rows, out, k, label) of cuda_bench.rs:59-66."""
+    shapes = [(8, 2048, 2048, "prefill 8x2048x2048"), (1, 4864, 896, "decode 1x4864x896 (Qwen MLP)"),
+              (1, 151_936, 896, "decode 1x151936x896 (Qwen LM head)")]
+    shapes += [(r, 2048, 2048, "sweep") for r in (1, 2, 4, 8, 16, 32, 64)]
+    return shapes
+
+
+def linear_bench_codes(tb, m, n, k):
+    """cuda_bench.rs:13-21: x = codes(m·k, 1 + m), w = codes(n·k, 2 + n), uniform in [-WLEVELS, WLEVELS]."""
+    lv = tb.WLEVELS
+    return tb.lcg_uniform(1 + m, -lv, lv, m * k), tb.lcg_uniform(2 + n, -lv, lv, n * k)
 GEMM_METRIC = "exact int64 GEMM throughput (2·M·N·K code ops/s), bit-exact; % int8 tensor peak"
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200, bit-exact; % HBM / int8 tensor peak"
 P_PLANES = 9  # int8 plane products per code product (3 balanced base-81 digits each side)
@@ -263,17 +281,33 @@ def run_reference(args, w, name):
     }), flush=True)
 
 
+def lcg_state_after(seed: int, n: int) -> int:
+    """The reference's test LCG (s = s·6364136223846793005 + 1442695040888963407 mod 2^64) advanced n steps, by
+    squaring the affine step."""
+    a, c, m = 6364136223846793005, 1442695040888963407, 1 << 64
+    acc_a, acc_c = 1, 0
+    while n:
+        if n & 1:
+            acc_a, acc_c = acc_a * a % m, (acc_c * a + c) % m
+        a, c = a * a % m, (c * a + c) % m
+        n >>= 1
+    return (acc_a * seed + acc_c) % m
+
+
 def gemm_codes(w):
-    """x [N][K] int8-range activation codes and w [M][K] 12-bit weight codes, both from one numpy generator."""
-    rng = np.random.default_rng(w["seed"])
-    wt = rng.integers(-2048, 2048, size=w["M"] * w["K"], dtype=np.int32)
-    x = rng.integers(-127, 128, size=w["N"] * w["K"], dtype=np.int32)
+    """One stream of the reference's test LCG with the config's seed (as gate.rs:446-459 draws its corpus): first the
+    weights w [M][K] uniform in [-2048, 2047], then the activations x [N][K] uniform in [-127, 127]."""
+    import tritify_b200 as tb
+
+    nw = w["M"] * w["K"]
+    wt = tb.lcg_uniform(w["seed"], -2048, 2047, nw)
+    x = tb.lcg_uniform(lcg_state_after(w["seed"], nw), -127, 127, w["N"] * w["K"])
     return x, wt
 
 
 def gemm_config(w, name):
     return {"workload": name, "M": w["M"], "N": w["N"], "K": w["K"], "weights": "uniform [-2048, 2047]",
-            "activations": "uniform [-127, 127]",
+            "activations": "uniform [-127, 127]", "generator": "the reference's test LCG, seed 2, weights first",
             "l2": "each step writes the 128 MiB int64 result and the packed activations (> 126 MB L2) between GEMMs"}
 
 
@@ -392,6 +426,122 @@ def run_gemm_ours(args, w, name):
                                "kind": "port", "sample": f"first {rows} of {N} activation rows, one call (C++ "
                                                          f"restatement of the reference's CPU linear, all cores)"}
     print(json.dumps(res), flush=True)
+
+
+def run_linear_bench_ours(args, w, name):
+    """Each shape through ktmoe_linear_weights (weights resident after one untimed call, as cuda_bench.rs:24-33
+    times it): `us_per_call` from CUDA events around `steps` synchronous calls from host arrays, `gemm_us` from the
+    events the library records around its GEMM launches. Every shape's result is checked against exact numpy int64
+    dot products (all of it up to 2048 outputs per row, else 256 sampled columns)."""
+    import torch
+
+    import tritify_b200 as tb
+
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    torch.cuda.set_device(local)
+    ctx = tb.Context(local)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    _, bf16, peak_kind = measured_peaks()
+    hbm, _, _ = measured_peaks()
+    rows_out, tot_mac, tot_us, tot_gemm_us, h2d, d2h = [], 0, 0.0, 0.0, 0, 0
+    launches0 = ctx.launch_count()
+    lm = None
+    with ClockSampler(smi_index(local)) as clk:
+        for i, (m, n, k, label) in enumerate(linear_bench_shapes()):
+            x, wt = linear_bench_codes(tb, m, n, k)
+            for _ in range(args.warmup):
+                y = ctx.linear(x, wt, m, n, k, weight_id=1000 + i)
+            cols = np.arange(n) if n <= 2048 else np.random.default_rng(i).choice(n, 256, replace=False)
+            want = x.reshape(m, k).astype(np.int64) @ wt.reshape(n, k)[cols].astype(np.int64).T
+            if not (y.reshape(m, n)[:, cols] == want).all():
+                raise SystemExit(f"cuda_bench {label} m={m}: the result differs from the exact product")
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g = []
+            torch.cuda.synchronize()
+            e0.record(stream)
+            for _ in range(args.steps):
+                ctx.linear(x, wt, m, n, k, weight_id=1000 + i)
+                g.append(ctx.last_gemm()[0])
+            e1.record(stream)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / args.steps
+            gus = 1e3 * sum(g) / len(g)
+            rows_out.append({"label": label, "m": m, "n": n, "k": k, "us_per_call": us, "gemm_us": gus,
+                             "mmac_s": m * n * k / us, "gemm_mmac_s": m * n * k / gus})
+            tot_mac += m * n * k
+            tot_us += us
+            tot_gemm_us += gus
+            h2d += m * k * 4
+            d2h += m * n * 8
+            if n == 151_936:
+                lm = (n, k, gus)
+    launches = ctx.launch_count() - launches0
+    n, k, gus = lm
+    wbytes = 3 * n * ((k + 127) // 128 * 128)  # the LM head's digit planes, streamed once per call
+    res = {
+        "metric": LINEAR_METRIC, "value": tot_mac / tot_gemm_us, "unit": "MMAC/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": tot_gemm_us * 1e-3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
+        "config": {"workload": name, "shapes": "cuda_bench.rs:59-66", "codes": "test LCG, full range +-WLEVELS",
+                   "l2": "the LM head's 408 MB of planes exceed L2; the smaller shapes run from L2 (as in the reference)"},
+        "shapes": rows_out, "clocks": clk.summary(), "gpu_launches": launches,
+        "e2e": {"value": tot_mac / tot_us, "unit": "MMAC/s", "ms_per_step": tot_us * 1e-3,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "achieved": wbytes / (gus * 1e-6) / 1e9, "peak": hbm, "unit": "GB/s",
+                     "frac": wbytes / (gus * 1e-6) / 1e9 / hbm, "traffic": None,
+                     "kernel": "digit_gemm, decode 1x151936x896 (LM head)", "peak_kind": peak_kind},
+    }
+    if not args.no_cpu:
+        from oracle import oracle as O
+
+        O.build()
+        O.lib().ko_set_max_threads(0)
+        mac, sec = 0, 0.0
+        for (m, n, k, label) in linear_bench_shapes():
+            x, wt = linear_bench_codes(tb, m, n, k)
+            t0 = time.perf_counter()
+            O.linear(x, wt, m, n, k)
+            sec += time.perf_counter() - t0
+            mac += m * n * k
+        res["cpu_baseline"] = {"value": mac / sec / 1e6, "unit": "MMAC/s", "cores": os.cpu_count(), "kind": "port",
+                               "sample": "every shape once (C++ restatement of the reference's Portable linear)"}
+    print(json.dumps(res), flush=True)
+
+
+def run_linear_bench_reference(args, w, name):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import tritify_b200 as tb
+    from oracle import oracle as O
+
+    O.build()
+    O.lib().ko_set_max_threads(0)
+    shapes, mac, sec = [], 0, 0.0
+    for (m, n, k, label) in linear_bench_shapes():
+        x, wt = linear_bench_codes(tb, m, n, k)
+        O.linear(x, wt, m, n, k)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            O.linear(x, wt, m, n, k)
+        us = (time.perf_counter() - t0) * 1e6 / args.steps
+        shapes.append({"label": label, "m": m, "n": n, "k": k, "us_per_call": us, "mmac_s": m * n * k / us})
+        mac += m * n * k
+        sec += us * 1e-6
+    v = mac / sec / 1e6
+    print(json.dumps({
+        "impl": "reference", "metric": LINEAR_METRIC, "value": v, "unit": "MMAC/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {"workload": name, "shapes": "cuda_bench.rs:59-66", "codes": "test LCG, full range +-WLEVELS"},
+        "shapes": shapes,
+        "cpu_baseline": {"value": v, "unit": "MMAC/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": "every shape, `steps` calls each (C++ restatement of the reference's Portable "
+                                   "linear)"},
+        "e2e": {"value": v, "unit": "MMAC/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 def run_ours(args, w, name):
@@ -600,6 +750,9 @@ def main():
     w = dict(WORKLOADS[args.workload])
     if w.get("gemm"):
         (run_gemm_reference if args.impl == "reference" else run_gemm_ours)(args, w, args.workload)
+        return
+    if w.get("linear_bench"):
+        (run_linear_bench_reference if args.impl == "reference" else run_linear_bench_ours)(args, w, args.workload)
         return
     if args.tokens:
         w["T"] = args.tokens

@@ -34,6 +34,7 @@ extern "C" {
 #define KTMOE_ERR_UNSUPPORTED 5   /* a configuration outside what this build implements */
 #define KTMOE_ERR_NO_DEVICE 6     /* no sm_100 device, or the device index does not exist */
 #define KTMOE_ERR_STATE 7         /* the layer is incomplete (a weight not set) */
+#define KTMOE_ERR_CALLBACK 8      /* the caller's experts callback returned non-zero */
 
 /* A non-negative fixed-point scale mant * 2^-shift (kt-int Scale; mant == 0 means exactly zero). */
 typedef struct ktmoe_scale {
@@ -155,6 +156,30 @@ int ktmoe_scale_from_f64(double x, ktmoe_scale* out);
 /* MoeMlp::route for each row: experts [rows][top_k] (top-k order), ec [rows][top_k] codes, sumc [rows]. */
 int ktmoe_route(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* experts,
                 int64_t* ec, int64_t* sumc);
+/* ── the expert-parallel seam: MoeMlp::forward_int_with_experts (layers.rs:945-984) with the experts elsewhere ──
+ * A layer whose routed experts live on other hosts (MoeMlp::remote, layers.rs:694-712) routes, combines, merges and
+ * adds its shared expert here, and gets the expert outputs through a callback; a worker holding experts computes
+ * those outputs with ktmoe_layer_expert_forward. Both take host pointers, are synchronous and run on a single-rank
+ * layer (world 1). The outputs cross hosts in the IntTensor wire format below (ktmoe_wire_encode/decode).
+ *
+ * The worker side: SwiGluMlp::forward_int (layers.rs:609-640) of expert ids[r·n_ids + j] on row r of x (rows x d,
+ * every row at x_scale, as the reference hands each row over with the input's scale) into y [rows][n_ids][d] and
+ * y_scale [rows][n_ids]. An id < 0 is an empty slot (zeros, zero scale); an id >= n_experts is KTMOE_ERR_ARG and an
+ * expert never set KTMOE_ERR_STATE. The router and the shared expert are not needed. */
+int ktmoe_layer_expert_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale,
+                               const int32_t* ids, int32_t n_ids, int32_t* y, ktmoe_scale* y_scale);
+/* The coordinator side's callback: for each row r, the outputs of experts ids[r·top_k + j] (the route's order) on
+ * row r of x into y [rows][top_k][d] and y_scale [rows][top_k] (both zero-filled on entry). A row whose route is empty
+ * (sumc <= 0, which the reference never hands to its callback) has ids -1 and its outputs are ignored. Return 0; any
+ * other value ends the forward with KTMOE_ERR_CALLBACK. */
+typedef int (*ktmoe_experts_fn)(void* user, int64_t rows, int32_t top_k, const int32_t* ids, const int32_t* x,
+                                ktmoe_scale x_scale, int32_t* y, ktmoe_scale* y_scale);
+/* The coordinator side: route x, call experts_fn once for all rows, then combine, merge the rows and add the shared
+ * expert exactly as ktmoe_forward does: with experts_fn returning what the layer's own experts compute, y and y_scale
+ * equal ktmoe_forward's (the reference's seam property, kt-core/src/tests.rs:156-181). The routed experts of this
+ * layer need not be set. */
+int ktmoe_layer_forward_with_experts(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale,
+                                     ktmoe_experts_fn experts_fn, void* user, int32_t* y, ktmoe_scale* y_scale);
 /* Kernel launches of this library on the context since open (the device work is all this library's own kernels). */
 int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
 
@@ -187,6 +212,20 @@ int ktmoe_table(int32_t kind, int64_t* codes, ktmoe_scale* inv_step, int64_t* lo
  * + Box-Muller in f64, cast to f32), and the reference's LCG uniform integers in [lo, hi]. */
 int ktmoe_synth_normal(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out);
 int ktmoe_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, int64_t n, int32_t* out);
+
+/* ── wire format: IntTensor::to_bytes / IntTensor::from_bytes (kt-core/src/tensor.rs:51-100) ──
+ * The reference's interchange form of an activation between workers, byte for byte, little-endian:
+ *   u32 ndim | ndim x u64 shape | i64 scale.mant | i32 scale.shift | u64 ndata | ndata x i32 codes
+ * Host-only (no device needed). ktmoe_wire_size gives the frame's bytes. ktmoe_wire_encode writes one frame into
+ * out (cap bytes) and its length into *written. ktmoe_wire_decode reads the frame at the start of b (len bytes):
+ * ndim, the shape (when shape is not NULL; shape_cap >= ndim), the scale, ndata and, when data is not NULL, the codes
+ * (data_cap >= ndata); *consumed is the frame's length, so concatenated frames are read one after another. A buffer
+ * shorter than its header declares, or a cap too small, is KTMOE_ERR_ARG (the reference panics on a short buffer). */
+int ktmoe_wire_size(int32_t ndim, int64_t ndata, uint64_t* bytes);
+int ktmoe_wire_encode(const int32_t* data, int64_t ndata, const int64_t* shape, int32_t ndim, ktmoe_scale scale,
+                      uint8_t* out, uint64_t cap, uint64_t* written);
+int ktmoe_wire_decode(const uint8_t* b, uint64_t len, int32_t* ndim, int64_t* shape, int32_t shape_cap,
+                      ktmoe_scale* scale, int64_t* ndata, int32_t* data, int64_t data_cap, uint64_t* consumed);
 
 #ifdef __cplusplus
 }

@@ -991,6 +991,33 @@ void ko_moe_forward_with_local_experts(void* p, const int32_t* x, size_t rows, k
     *ys = to_c(o.scale);
 }
 
+// The seam (layers.rs:945-984) with the expert outputs given: ye [rows][top_k][d] and yse [rows][top_k] in route order,
+// as a transport would deliver them. Rows reach the callback in order, skipping those whose route is empty.
+void ko_moe_forward_with_given_experts(void* p, const int32_t* x, size_t rows, ko_scale xs, const int32_t* ye,
+                                       const ko_scale* yse, int32_t* y, ko_scale* ys) {
+    MoeMlp* m = (MoeMlp*)p;
+    const size_t d = m->dim(), K = m->top_k;
+    IntTensor t{std::vector<int32_t>(x, x + rows * d), rows == 1 ? std::vector<size_t>{d} : std::vector<size_t>{rows, d},
+                from_c(xs)};
+    std::vector<size_t> live;
+    for (size_t r = 0; r < rows; ++r) {
+        IntTensor row{std::vector<int32_t>(x + r * d, x + (r + 1) * d), {d}, from_c(xs)};
+        if (m->route(row).sumc > 0) live.push_back(r);
+    }
+    size_t next = 0;
+    IntTensor o = m->forward_int_with_experts(t, [&](const std::vector<size_t>& ids, const IntTensor&) {
+        const size_t r = live.at(next++);
+        std::vector<IntTensor> v;
+        for (size_t j = 0; j < ids.size(); ++j) {
+            const int32_t* src = ye + (r * K + j) * d;
+            v.push_back(IntTensor{std::vector<int32_t>(src, src + d), {d}, from_c(yse[r * K + j])});
+        }
+        return v;
+    });
+    std::memcpy(y, o.data.data(), o.data.size() * 4);
+    *ys = to_c(o.scale);
+}
+
 // MoeMlp::route for each row (layers.rs:826-862).
 void ko_moe_route(void* p, const int32_t* x, size_t rows, ko_scale xs, int32_t* experts, int64_t* ec, int64_t* sumc) {
     MoeMlp* m = (MoeMlp*)p;

@@ -75,6 +75,8 @@ def lib():
             "ko_moe_forward": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_tokens": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_with_local_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
+            "ko_moe_forward_with_given_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale), i32p,
+                                                   p(KoScale)], None),
             "ko_moe_route": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, i64p, i64p], None),
             "ko_moe_router_logits": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_expert": ([ctypes.c_void_p, sz, i32p, KoScale, i32p, p(KoScale)], None),
@@ -270,6 +272,19 @@ class MoeOracle:
                                                 ctypes.byref(s))
         return y.reshape(rows, self.dim), s.tup()
 
+    def forward_with_given_experts(self, x, xs, ye, yse):
+        """The seam with the expert outputs given: ye [rows][top_k][d] int32, yse [rows][top_k] of (mant, shift)."""
+        x, rows = self._x(x)
+        ye = np.ascontiguousarray(ye, dtype=np.int32)
+        ys_arr = (KoScale * max(1, rows * self.top_k))()
+        for i, (mt, sh) in enumerate(yse):
+            ys_arr[i] = KoScale(int(mt), int(sh))
+        y = np.empty(x.size, dtype=np.int32)
+        s = KoScale()
+        lib().ko_moe_forward_with_given_experts(self._h, _p(x, ctypes.c_int32), rows, S(xs), _p(ye, ctypes.c_int32),
+                                                ys_arr, _p(y, ctypes.c_int32), ctypes.byref(s))
+        return y.reshape(rows, self.dim), s.tup()
+
     def route(self, x, xs):
         x, rows = self._x(x)
         ex = np.empty(rows * self.top_k, dtype=np.int32)
@@ -327,3 +342,26 @@ def rmsnorm(weight: np.ndarray, eps: float, x: np.ndarray, xs):
     lib().ko_rmsnorm(_p(w, ctypes.c_float), dim, float(eps), _p(x, ctypes.c_int32), rows, S(xs), _p(y, ctypes.c_int32),
                      ctypes.byref(ys), _p(wc, ctypes.c_int32), ctypes.byref(ws), ctypes.byref(es))
     return y.reshape(x.shape), ys.tup(), wc, ws.tup(), es.tup()
+
+
+def to_bytes(data: np.ndarray, shape, mant: int, shift: int) -> bytes:
+    """IntTensor::to_bytes (kt-core/src/tensor.rs:51-67): u32 ndim, ndim x u64 shape, i64 mant, i32 shift, u64 ndata,
+    ndata x i32, all little-endian."""
+    import struct
+
+    data = np.ascontiguousarray(data, dtype="<i4").reshape(-1)
+    head = struct.pack("<I", len(shape)) + b"".join(struct.pack("<Q", int(s)) for s in shape)
+    return head + struct.pack("<qiQ", int(mant), int(shift), data.size) + data.tobytes()
+
+
+def from_bytes(b: bytes):
+    """IntTensor::from_bytes (kt-core/src/tensor.rs:70-100): (data, shape, (mant, shift), bytes read)."""
+    import struct
+
+    (nd,) = struct.unpack_from("<I", b, 0)
+    shape = list(struct.unpack_from(f"<{nd}Q", b, 4))
+    c = 4 + 8 * nd
+    mant, shift, n = struct.unpack_from("<qiQ", b, c)
+    c += 20
+    data = np.frombuffer(b, dtype="<i4", count=n, offset=c).astype(np.int32)
+    return data, shape, (mant, shift), c + 4 * n

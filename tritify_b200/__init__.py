@@ -88,6 +88,34 @@ class IntTensor:
     def to_f64(self) -> np.ndarray:
         return self.data.astype(np.float64) * self.scale.to_f64()
 
+    def to_bytes(self) -> bytes:
+        """IntTensor::to_bytes (tensor.rs:51-67): the reference's interchange frame, byte for byte."""
+        shape = np.ascontiguousarray(self.shape, dtype=np.int64)
+        n = ctypes.c_uint64()
+        check(lib().ktmoe_wire_size(shape.size, self.data.size, ctypes.byref(n)))
+        out = np.empty(n.value, dtype=np.uint8)
+        check(lib().ktmoe_wire_encode(_p(self.data, ctypes.c_int32), self.data.size, _p(shape, ctypes.c_int64),
+                                      shape.size, self.scale._c(), _p(out, ctypes.c_uint8), out.size,
+                                      ctypes.byref(n)))
+        return out.tobytes()
+
+    @staticmethod
+    def from_bytes(b: bytes, with_length: bool = False):
+        """IntTensor::from_bytes (tensor.rs:70-100) of the frame at the start of `b`; with_length also returns the
+        frame's byte length (frames may be concatenated). A short or malformed buffer raises KtmoeError."""
+        buf = np.frombuffer(b, dtype=np.uint8)
+        ndim, ndata, used = ctypes.c_int32(), ctypes.c_int64(), ctypes.c_uint64()
+        s = KtmoeScale()
+        check(lib().ktmoe_wire_decode(_p(buf, ctypes.c_uint8), buf.size, ctypes.byref(ndim), None, 0, ctypes.byref(s),
+                                      ctypes.byref(ndata), None, 0, ctypes.byref(used)))
+        shape = np.empty(ndim.value, dtype=np.int64)
+        data = np.empty(ndata.value, dtype=np.int32)
+        check(lib().ktmoe_wire_decode(_p(buf, ctypes.c_uint8), buf.size, ctypes.byref(ndim), _p(shape, ctypes.c_int64),
+                                      shape.size, ctypes.byref(s), ctypes.byref(ndata), _p(data, ctypes.c_int32),
+                                      data.size, ctypes.byref(used)))
+        t = IntTensor(data, shape.tolist(), Scale._of(s))
+        return (t, used.value) if with_length else t
+
 
 def device_count() -> int:
     n = ctypes.c_int(0)
@@ -363,6 +391,59 @@ class DeviceLayer:
                                          _p(ec, ctypes.c_int64), _p(sumc, ctypes.c_int64)))
         return ex.reshape(rows, self.top_k), ec.reshape(rows, self.top_k), sumc
 
+    def expert_forward(self, x: np.ndarray, rows: int, x_scale: Scale, ids: np.ndarray):
+        """The seam's worker side (ktmoe_layer_expert_forward): SwiGluMlp::forward_int of expert ids[r][j] on row r
+        (ids < 0: empty). Returns (y int32 [rows][n_ids][d], scales [rows][n_ids] as a list of lists of Scale)."""
+        x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        ids = np.ascontiguousarray(ids, dtype=np.int32).reshape(rows, -1)
+        n_ids = ids.shape[1]
+        if x.size != rows * self.d_model:
+            raise ValueError("x is not rows·d_model")
+        y = np.empty(rows * n_ids * self.d_model, dtype=np.int32)
+        ys = (KtmoeScale * max(1, rows * n_ids))()
+        self.ctx.check(lib().ktmoe_layer_expert_forward(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(),
+                                                        _p(ids, ctypes.c_int32), n_ids, _p(y, ctypes.c_int32), ys))
+        sc = [Scale._of(ys[i]) for i in range(rows * n_ids)]
+        return y.reshape(rows, n_ids, self.d_model), [sc[r * n_ids:(r + 1) * n_ids] for r in range(rows)]
+
+    def forward_with_experts(self, x: np.ndarray, rows: int, x_scale: Scale, experts_fn: Callable):
+        """MoeMlp::forward_int_with_experts (layers.rs:945-984) on the device: route here, call
+        ``experts_fn(ids [rows][top_k] int32, x [rows][d] int32, x_scale) -> (y [rows][top_k][d], scales)`` once for
+        all rows (rows with an empty route have ids -1; scales: [rows][top_k] of Scale or (mant, shift)), then combine,
+        merge and add the shared expert. Returns (y int32 [rows·d], Scale)."""
+        x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
+        if x.size != rows * self.d_model:
+            raise ValueError("x is not rows·d_model")
+        d = self.d_model
+        failure = []
+
+        def tramp(_user, n, k, ids_p, x_p, xs_c, y_p, ys_p):
+            try:
+                ids = np.ctypeslib.as_array(ids_p, shape=(n, k)).copy()
+                xr = np.ctypeslib.as_array(x_p, shape=(n, d)).copy()
+                ye, yse = experts_fn(ids, xr, Scale._of(xs_c))
+                ye = np.ascontiguousarray(ye, dtype=np.int32).reshape(n, k, d)
+                np.ctypeslib.as_array(y_p, shape=(n * k * d,))[:] = ye.reshape(-1)
+                for r in range(n):
+                    for j in range(k):
+                        s = yse[r][j]
+                        m, sh = (s.mant, s.shift) if isinstance(s, Scale) else (int(s[0]), int(s[1]))
+                        ys_p[r * k + j] = KtmoeScale(m, sh)
+                return 0
+            except Exception as e:  # reported through KTMOE_ERR_CALLBACK; re-raised below
+                failure.append(e)
+                return 1
+
+        cb = _native.EXPERTS_FN(tramp)
+        y = np.empty(rows * d, dtype=np.int32)
+        ys = KtmoeScale()
+        status = lib().ktmoe_layer_forward_with_experts(self._h, _p(x, ctypes.c_int32), rows, x_scale._c(), cb, None,
+                                                        _p(y, ctypes.c_int32), ctypes.byref(ys))
+        if failure:
+            raise failure[0]
+        self.ctx.check(status)
+        return y, Scale._of(ys)
+
     STAGES = ["route", "dispatch", "gemm_gate_up", "swiglu", "gemm_down", "combine", "merge", "shared"]
 
     def set_timing(self, enable: bool) -> None:
@@ -402,6 +483,19 @@ class MoeMlp:
             raise ValueError("top_k in 1..=E")
         if router.out_features != len(experts):
             raise ValueError("router out_features != number of experts")
+        self._init(name, router, experts, top_k, ctx)
+
+    @staticmethod
+    def remote(name: str, router: QuantLinear, top_k: int, ctx: Optional[Context] = None) -> "MoeMlp":
+        """MoeMlp::remote (layers.rs:694-712): the routed experts are elsewhere; route, combine and the shared expert
+        run here, and the experts come only through :meth:`forward_int_with_experts`."""
+        if not (1 <= top_k <= router.out_features):
+            raise ValueError("top_k in 1..=E")
+        m = MoeMlp.__new__(MoeMlp)
+        m._init(name, router, [], top_k, ctx)
+        return m
+
+    def _init(self, name, router, experts, top_k, ctx):
         self.name, self.router, self.experts, self.top_k = name, router, experts, top_k
         self.norm_topk_prob = False
         self.sigmoid_bias_codes: Optional[np.ndarray] = None
@@ -433,11 +527,18 @@ class MoeMlp:
     def dim(self) -> int:
         return self.router.in_features
 
+    def n_experts(self) -> int:
+        return self.router.out_features
+
+    def is_remote(self) -> bool:
+        return not self.experts
+
     def device_layer(self) -> DeviceLayer:
         if self._dev is None:
             ctx = self._ctx or default_context()
-            e0 = self.experts[0]
-            dev = DeviceLayer(ctx, self.dim, len(self.experts), e0.gate.out_features, self.top_k, self.norm_topk_prob,
+            # a remote layer holds no routed experts: the smallest expert width keeps their (unused) planes small
+            d_ff = self.experts[0].gate.out_features if self.experts else 16
+            dev = DeviceLayer(ctx, self.dim, self.n_experts(), d_ff, self.top_k, self.norm_topk_prob,
                               self.sigmoid_bias_codes is not None,
                               self.shared.gate.out_features if self.shared else 0)
             dev.set_router(self.router.w_codes, self.router.w_scale, self.router.bias)
@@ -453,8 +554,46 @@ class MoeMlp:
             self._dev = dev
         return self._dev
 
+    def forward_int_with_experts(self, x: IntTensor, experts_fn: Callable) -> IntTensor:
+        """MoeMlp::forward_int_with_experts (layers.rs:945-951): route and combine here, the experts through
+        ``experts_fn(ids: list[int], row: IntTensor) -> list[IntTensor]`` (outputs in ids order), called for each row
+        whose route is not empty, in row order, as the reference does."""
+        d = self.dim
+        if len(x) % d != 0:
+            raise ValueError(f"{self.name}: MoE input length must be a multiple of dim")
+        rows = len(x) // d
+
+        def batch(ids, xr, xs):
+            n, k = ids.shape
+            y = np.zeros((n, k, d), dtype=np.int32)
+            ys = [[Scale.ZERO] * k for _ in range(n)]
+            for r in range(n):
+                if ids[r, 0] < 0:
+                    continue
+                outs = experts_fn([int(e) for e in ids[r]], IntTensor(xr[r], (d,), xs))
+                if len(outs) != k:
+                    raise ValueError(f"{self.name}: the experts callback returned {len(outs)} outputs for {k} ids")
+                for j, o in enumerate(outs):
+                    y[r, j] = np.asarray(o.data, dtype=np.int32).reshape(d)
+                    ys[r][j] = o.scale
+            return y, ys
+
+        y, ys = self.device_layer().forward_with_experts(x.data, rows, x.scale, batch)
+        return IntTensor(y, (d,) if rows == 1 else (rows, d), ys)
+
+    def expert_outputs(self, x: IntTensor, ids: np.ndarray) -> List[List[IntTensor]]:
+        """The worker side of the seam: ``SwiGluMlp::forward_int`` (layers.rs:609-640) of expert ``ids[r][j]`` on row
+        r of ``x`` (ids < 0: empty, a zero output), all rows at ``x.scale``; on the device in one batch."""
+        d = self.dim
+        rows = len(x) // d
+        y, ys = self.device_layer().expert_forward(x.data, rows, x.scale, ids)
+        return [[IntTensor(y[r, j], (d,), ys[r][j]) for j in range(y.shape[1])] for r in range(rows)]
+
     def forward_int(self, x: IntTensor) -> IntTensor:
         """Module::forward_int (layers.rs:1070-1073)."""
+        if self.is_remote():
+            raise RuntimeError(f"{self.name}: the routed experts are remote (MoeMlp::remote); compute them through "
+                               "forward_int_with_experts")
         d = self.dim
         if len(x) % d != 0:
             raise ValueError(f"{self.name}: MoE input length must be a multiple of dim")

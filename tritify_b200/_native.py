@@ -13,7 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libktmoe.so")
 
 OK = 0
-ERR_CUDA, ERR_ARG, ERR_RANGE, ERR_KERNEL, ERR_UNSUPPORTED, ERR_NO_DEVICE, ERR_STATE = 1, 2, 3, 4, 5, 6, 7
+ERR_CUDA, ERR_ARG, ERR_RANGE, ERR_KERNEL, ERR_UNSUPPORTED, ERR_NO_DEVICE, ERR_STATE, ERR_CALLBACK = (1, 2, 3, 4, 5,
+                                                                                                 6, 7, 8)
 
 
 class KtmoeScale(ctypes.Structure):
@@ -47,6 +48,12 @@ SIGNATURES = {
     "ktmoe_linear_weights": ([_vp, _u64, _i32p, _i32p, _i64, _i64, _i64, _i64p], ctypes.c_int),
     "ktmoe_linear_noalloc": ([_i32, _vp, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "ktmoe_linear_last_gemm": ([_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)], ctypes.c_int),
+    "ktmoe_wire_size": ([_i32, _i64, ctypes.POINTER(_u64)], ctypes.c_int),
+    "ktmoe_layer_expert_forward": ([_vp, _vp, _i64, KtmoeScale, _vp, _i32, _vp, _vp], ctypes.c_int),
+    "ktmoe_layer_forward_with_experts": ([_vp, _vp, _i64, KtmoeScale, _vp, _vp, _vp, _vp], ctypes.c_int),
+    "ktmoe_wire_encode": ([_vp, _i64, _vp, _i32, KtmoeScale, _vp, _u64, ctypes.POINTER(_u64)], ctypes.c_int),
+    "ktmoe_wire_decode": ([_vp, _u64, ctypes.POINTER(_i32), _vp, _i32, ctypes.POINTER(KtmoeScale), ctypes.POINTER(_i64),
+                           _vp, _i64, ctypes.POINTER(_u64)], ctypes.c_int),
     "ktmoe_set_weight_budget": ([_vp, _u64], ctypes.c_int),
     "ktmoe_resident_bytes": ([_vp, _P(_u64)], ctypes.c_int),
     "ktmoe_layer_create": ([_vp, _P(KtmoeLayerConfig), _P(_vp)], ctypes.c_int),
@@ -103,6 +110,12 @@ class KtmoeError(RuntimeError):
     def __init__(self, status: int, message: str):
         super().__init__(f"ktmoe status {status}: {message}")
         self.status = status
+
+
+# ktmoe_experts_fn: (user, rows, top_k, ids, x, x_scale, y, y_scale) -> int
+EXPERTS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+                              ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32), KtmoeScale,
+                              ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(KtmoeScale))
 
 
 def check(status: int, ctx=None) -> None:

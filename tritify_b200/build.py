@@ -19,8 +19,9 @@ LIB = os.path.join(PKG, "libktmoe.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES_CU = ["ktmoe.cu", "noalloc.cu"]
-SOURCES_CPP = ["host_prep.cpp"]
-HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "digit_gemm_pair.cuh", "moe_kernels.cuh", "host_prep.h"]
+SOURCES_CPP = ["host_prep.cpp", "wire.cpp"]
+HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "digit_gemm_pair.cuh", "moe_kernels.cuh", "ep_peer.cuh",
+           "host_prep.h"]
 
 
 def _nvcc() -> str:
@@ -64,7 +65,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
         o = os.path.join(BUILD, src + ".o")
         objs.append(o)
         if force or _stale(o, [s] + header_deps):
-            cmd = ["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-Wall", "-c", s, "-o", o]
+            cmd = ["g++", "-O3", "-std=c++17", "-fPIC", "-ffp-contract=off", "-Wall", "-I", os.path.join(ROOT, "include"),
+                   "-c", s, "-o", o]
             _run(cmd, verbose)
     for src in SOURCES_CU:
         s = os.path.join(CSRC, src)

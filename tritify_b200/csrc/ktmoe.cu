@@ -211,6 +211,7 @@ struct GemmCall {
     int64_t M_valid;
     Planes B;        // activations: 3 x R_pad x k_pad (one raw plane R_pad x k_pad when `small`)
     bool small = false;  // |x| <= 127 and |w| <= 3280: the (1, 2) plane GEMM on weight planes 0 and 1
+    cudaEvent_t ev0 = nullptr;  // when set, recorded on the stream just before the first launch (after the maps)
     int64_t* out;
     int64_t ld_out;
     int BN;
@@ -287,6 +288,7 @@ int run_gemm_small_pair(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
     if (r) return r;
     r = make_map(ctx, &mw, g.A.ptr, g.A.k_pad, g.A.groups * 3 * g.A.rows_pad, ps::BN_W);
     if (r) return r;
+    if (g.ev0) CK(cudaEventRecord(g.ev0, st));
     const int64_t total_kb = (g.A.k + dg::BK - 1) / dg::BK;
     const int64_t chunk_kb = dg::K_EXACT_MAX_SMALL / dg::BK;
     for (int64_t kb0 = 0; kb0 < total_kb; kb0 += chunk_kb) {
@@ -340,6 +342,7 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
             if (ks < 2) ks = 1;
         }
     }
+    if (g.ev0) CK(cudaEventRecord(g.ev0, st));
     if (ks > 1) CK(cudaMemsetAsync(g.out, 0, (size_t)g.single_rows * g.ld_out * 8, st));
     // persistent: at most one block per SM walks the tile raster
     dim3 grid((unsigned)std::min<int64_t>(slots * ks, ctx->num_sms));
@@ -519,6 +522,7 @@ struct ktmoe_layer {
     DevBuf swiglu_plans, row_hmax, shared_plan;  // per-row SwiGLU scale plans and max |h|; the shared expert's plan
     DevBuf cp_n, cp_common, cp_row, cp_ec, cp_ry, cp_f;  // per-token combine plans
     DevBuf xs_planes, acc_sgu, hs_planes, acc_sd;
+    DevBuf seam_y, seam_ys, seam_ids;  // the expert-output seam (ktmoe_layer_expert_forward / _forward_with_experts)
     // optional per-stage CUDA-event timing: one event per stage boundary per timed forward
     bool timing = false;
     // the block around the layer (ktmoe_layer_set_norm): the FFN input RmsNorm and the residual add
@@ -677,15 +681,22 @@ mk::Lut lut(const ktmoe_layer* L, int kind) {
     return l;
 }
 
+// Each token row's quantiser (xmax, quant_to, the digit planes, s_qx): tok_planes, tok_xmax, tok_sqx.
+int stage_quant(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)L->d, (int)L->d_pad, round_up(T, 64),
+                                                        L->tok_planes.as<int8_t>(), L->tok_xmax.as<int64_t>(),
+                                                        L->tok_sqx.as<Scale>(), xs_dev, nullptr);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
 // Quantise, route (router GEMM + top-k) for T tokens already in x_in / SL_XSCALE.
 int stage_route(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t d = L->d, E = L->E;
     const int64_t T_pad = round_up(T, 64);
-    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
-                                                        L->tok_planes.as<int8_t>(), L->tok_xmax.as<int64_t>(),
-                                                        L->tok_sqx.as<Scale>(), xs_dev, nullptr);
-    CKL(ctx);
+    if (int r = stage_quant(L, T, x_dev, xs_dev, st)) return r;
     GemmCall g;
     g.A = L->w_router;
     g.M_valid = E;
@@ -1260,6 +1271,9 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     return KTMOE_OK;
 }
 
+int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset, const int32_t* x_dev,
+                  const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev, cudaStream_t st, bool side_shared);
+
 int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev,
                   cudaStream_t st, bool bump = true) {
     ktmoe_ctx* ctx = L->ctx;
@@ -1340,6 +1354,16 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         T_total = L->ep_tok_total;
         tok_offset = L->ep_tok_offset;
     }
+    return merge_and_add(L, T, T_total, tok_offset, x_dev, xs_dev, y_dev, ys_dev, st, side_shared);
+}
+
+// The end of the forward, after each token's combine (tok_out, tok_scale): merge the rows at one scale over all the
+// layer's tokens (T_total of them, this rank's from tok_offset; -1: counted on the device by the peer transport),
+// then add the shared expert (run here unless side_shared, when it ran on the side stream).
+int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset, const int32_t* x_dev,
+                  const Scale* xs_dev, int32_t* y_dev, Scale* ys_dev, cudaStream_t st, bool side_shared) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d, fs = L->fs;
     const int* tok_info = L->peer.on ? L->peer.tok_info.as<int>() : nullptr;  // [0] first token, [1] tokens
 
     // merge (layers.rs:1001-1019): one common scale and one gmax over all the layer's tokens, on every rank
@@ -1644,6 +1668,7 @@ const char* ktmoe_error_string(int status) {
         case KTMOE_ERR_UNSUPPORTED: return "unsupported configuration";
         case KTMOE_ERR_NO_DEVICE: return "no sm_100 device";
         case KTMOE_ERR_STATE: return "layer incomplete";
+        case KTMOE_ERR_CALLBACK: return "the experts callback failed";
         default: return "unknown status";
     }
 }
@@ -1869,7 +1894,7 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
                 : Planes{ctx->lin_xp.as<int8_t>(), 1, rows_pad, k, k_pad};
     g.small = small;
     ctx->last_gemm_planes = 0;
-    CK(cudaEventRecord(ctx->ev_g0, st));
+    g.ev0 = ctx->ev_g0;
     g.out = ctx->lin_y.as<int64_t>();
     g.ld_out = out;
     g.BN = BN;
@@ -2395,6 +2420,173 @@ int ktmoe_route(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_sc
     CK(cudaMemcpyAsync(sumc, L->sumc.p, (size_t)rows * 8, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return check_err_word(ctx);
+}
+
+// ── the expert-parallel seam: MoeMlp::forward_int_with_experts (layers.rs:945-984) with the experts elsewhere ──
+
+int ktmoe_layer_expert_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale,
+                               const int32_t* ids, int32_t n_ids, int32_t* y, ktmoe_scale* y_scale) {
+    if (!L || rows < 0 || n_ids < 0) return KTMOE_ERR_ARG;
+    if (rows == 0 || n_ids == 0) return KTMOE_OK;
+    if (!x || !ids || !y || !y_scale) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->world != 1) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "the seam runs on a single-rank layer");
+    const int64_t n_req = rows * (int64_t)n_ids;
+    int32_t fill = -1;  // a set expert that stands in for empty slots (its outputs there are discarded)
+    for (int64_t i = 0; i < n_req; ++i) {
+        const int32_t e = ids[i];
+        if (e >= L->E) return fail(ctx, KTMOE_ERR_ARG, "an expert id is out of range");
+        if (e < 0) continue;
+        if (!L->expert_set[e]) return fail(ctx, KTMOE_ERR_STATE, "a requested expert is not set");
+        if (fill < 0) fill = e;
+    }
+    if (fill < 0) {  // nothing requested: every output is zero with a zero scale
+        std::memset(y, 0, (size_t)(n_req * L->d) * 4);
+        for (int64_t i = 0; i < n_req; ++i) y_scale[i] = ktmoe_scale{0, 0};
+        return KTMOE_OK;
+    }
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, rows)) return r;
+    cudaStream_t st = ctx->stream;
+    const int64_t d = L->d, E = L->E, f = L->f, K = L->K, T = rows, R = T * K;
+    const int64_t R_pad = round_up(R, 64);
+    CK(L->seam_y.ensure((size_t)(n_req * d) * 4));
+    CK(L->seam_ys.ensure((size_t)n_req * sizeof(Scale)));
+    CK(L->seam_ids.ensure((size_t)n_req * 4));
+    Scale xs = S(x_scale);
+    CK(cudaMemcpyAsync(L->x_in.p, x, (size_t)(T * d) * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(L->seam_ids.p, ids, (size_t)n_req * 4, cudaMemcpyHostToDevice, st));
+    if (int r = stage_quant(L, T, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), st)) return r;
+    // the requests in chunks of K per row, each through the layer's routed pipeline with the ids as its top-k
+    std::vector<int32_t> te((size_t)R);
+    const int BN = pick_bn((double)R / (double)E, true), BN2 = pick_bn_long_k((double)R / (double)E, f, true);
+    for (int32_t j0 = 0; j0 < n_ids; j0 += (int32_t)K) {
+        const int32_t Kc = (int32_t)std::min<int64_t>(K, n_ids - j0);
+        for (int64_t t = 0; t < T; ++t)
+            for (int64_t s = 0; s < K; ++s) {
+                const int32_t e = s < Kc ? ids[t * n_ids + j0 + s] : -1;
+                te[(size_t)(t * K + s)] = e >= 0 ? e : fill;
+            }
+        CK(cudaMemcpyAsync(L->top_e.p, te.data(), (size_t)R * 4, cudaMemcpyHostToDevice, st));
+        if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
+        ExpertRows xr;
+        xr.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
+        xr.n_rows = R;
+        xr.BN = BN;
+        xr.BN2 = BN2;
+        xr.grid_a = (R + BN - 1) / BN + E;
+        xr.grid_b = (R + BN2 - 1) / BN2 + E;
+        xr.tg_a = L->tile_group.as<int>();
+        xr.tr_a = L->tile_row0.as<int>();
+        xr.te_a = nullptr;
+        xr.nt_a = n_tiles_ptr(L);
+        xr.tg_b = L->tile_group2.as<int>();
+        xr.tr_b = L->tile_row02.as<int>();
+        xr.te_b = nullptr;
+        xr.nt_b = n_tiles2_ptr(L);
+        xr.group_end = L->group_end.as<int>();
+        xr.row_assign = L->row_assign.as<int>();
+        xr.row_expert = L->row_expert.as<int>();
+        xr.row_sqx = L->tok_sqx.as<Scale>();
+        if (int r = run_experts(L, xr, st)) return r;
+        mk::seam_out_kernel<<<(unsigned)R, 256, 0, st>>>(
+            L->acc_d.as<int64_t>(), L->rowmax_d.as<unsigned long long>(), L->row_cd.as<Scale>(),
+            L->row_assign.as<int>(), (int)R, (int)d, (int)K, Kc, n_ids, j0, L->seam_ids.as<int32_t>(),
+            L->seam_y.as<int32_t>(), L->seam_ys.as<Scale>());
+        CKL(ctx);
+        // te is reused by the next chunk: its copy must have left the host buffer first
+        CK(cudaStreamSynchronize(st));
+    }
+    std::vector<Scale> hs((size_t)n_req);
+    CK(cudaMemcpyAsync(y, L->seam_y.p, (size_t)(n_req * d) * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(hs.data(), L->seam_ys.p, (size_t)n_req * sizeof(Scale), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (int r = check_err_word(ctx)) return r;
+    for (int64_t i = 0; i < n_req; ++i) y_scale[i] = C(hs[(size_t)i]);
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_forward_with_experts(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale,
+                                     ktmoe_experts_fn experts_fn, void* user, int32_t* y, ktmoe_scale* y_scale) {
+    if (!L || !experts_fn || !y_scale || rows <= 0 || !x || !y) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->world != 1) return fail(ctx, KTMOE_ERR_UNSUPPORTED, "the seam runs on a single-rank layer");
+    if (!L->router_set || (L->cfg.router_score == 1 && !L->sigbias_set) || (L->fs > 0 && !L->shared_set))
+        return fail(ctx, KTMOE_ERR_STATE, "the router or the shared expert is not set");
+    const int64_t d = L->d, K = L->K, T = rows, R = T * K;
+    const Scale xs = S(x_scale);
+    cudaStream_t st = ctx->stream;
+    std::vector<int32_t> ids((size_t)R);
+    std::vector<int64_t> ec((size_t)R), sumc((size_t)T);
+    {
+        // route; the callback runs without the context's lock (it may call into this library, even this layer),
+        // so what the combine needs from the route is kept on the host across it
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (int r = set_device(ctx)) return r;
+        if (int r = ensure_scratch(L, T)) return r;
+        CK(cudaMemcpyAsync(L->x_in.p, x, (size_t)(T * d) * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+        if (int r = stage_route(L, T, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), st)) return r;
+        CK(cudaMemcpyAsync(ids.data(), L->top_e.p, (size_t)R * 4, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(ec.data(), L->top_ec.p, (size_t)R * 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(sumc.data(), L->sumc.p, (size_t)T * 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaStreamSynchronize(st));
+        if (int r = check_err_word(ctx)) return r;
+    }
+    // a row whose route is empty never reaches the callback in the reference: its ids are -1 here
+    for (int64_t t = 0; t < T; ++t)
+        if (sumc[(size_t)t] <= 0)
+            for (int64_t i = 0; i < K; ++i) ids[(size_t)(t * K + i)] = -1;
+    std::vector<int32_t> ye((size_t)(R * d), 0);
+    std::vector<ktmoe_scale> yse((size_t)R, ktmoe_scale{0, 0});
+    const int cb = experts_fn(user, T, (int32_t)K, ids.data(), x, x_scale, ye.data(), yse.data());
+    if (cb != 0) return fail(ctx, KTMOE_ERR_CALLBACK, "the experts callback returned " + std::to_string(cb));
+    std::vector<Scale> ys_h((size_t)R);
+    for (int64_t i = 0; i < R; ++i) ys_h[(size_t)i] = S(yse[(size_t)i]);
+
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = ensure_scratch(L, T)) return r;
+    CK(L->seam_y.ensure((size_t)(R * d) * 4));
+    CK(L->seam_ys.ensure((size_t)R * sizeof(Scale)));
+    CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
+    CK(cudaMemcpyAsync(L->x_in.p, x, (size_t)(T * d) * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(scal_scale(L, SL_XSCALE), &xs, sizeof(Scale), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(L->top_ec.p, ec.data(), (size_t)R * 8, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(L->sumc.p, sumc.data(), (size_t)T * 8, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(L->seam_y.p, ye.data(), (size_t)(R * d) * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(L->seam_ys.p, ys_h.data(), (size_t)R * sizeof(Scale), cudaMemcpyHostToDevice, st));
+    mk::iota_kernel<<<(unsigned)std::min<int64_t>((R + 255) / 256, 1024), 256, 0, st>>>(L->slot_row.as<int>(), R);
+    CKL(ctx);
+    mk::CombineYArgs ca;
+    ca.y = L->seam_y.as<int32_t>();
+    ca.ys = L->seam_ys.as<Scale>();
+    ca.slot_row = L->slot_row.as<int>();
+    ca.top_ec = L->top_ec.as<int64_t>();
+    ca.sumc = L->sumc.as<int64_t>();
+    ca.T = (int)T;
+    ca.top_k = (int)K;
+    ca.dim = (int)d;
+    ca.out = L->tok_out.as<int32_t>();
+    ca.out_scale = L->tok_scale.as<Scale>();
+    const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
+                             L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
+    mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
+    CKL(ctx);
+    mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
+    CKL(ctx);
+    if (int r = merge_and_add(L, T, T, 0, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
+                              scal_scale(L, SL_YSCALE), st, false))
+        return r;
+    Scale ys{0, 0};
+    CK(cudaMemcpyAsync(y, L->y_out.p, (size_t)(T * d) * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(&ys, scal_scale(L, SL_YSCALE), sizeof(Scale), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (int r = check_err_word(ctx)) return r;
+    *y_scale = C(ys);
+    return KTMOE_OK;
 }
 
 int ktmoe_layer_set_graphs(ktmoe_layer* L, int32_t enable) {

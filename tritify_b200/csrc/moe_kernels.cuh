@@ -1127,6 +1127,33 @@ __global__ void expert_out_kernel(const int64_t* __restrict__ acc, const unsigne
     if (threadIdx.x == 0) ys[r] = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), cd);
 }
 
+// The seam's worker side: the expert outputs of one chunk of at most K requested experts per row. Expert-sorted row
+// r is assignment a = row_assign[r] = t·K + slot; slot < Kc is request (t, j0 + slot) of the n_ids per row, written to
+// y[(t·n_ids + j0 + slot)·D ..] and ys[..] as expert_out_kernel does; a request with id < 0 (an empty slot that ran on
+// a stand-in expert) gets zeros and a zero scale.
+__global__ void seam_out_kernel(const int64_t* __restrict__ acc, const unsigned long long* __restrict__ ymax_d,
+                                const Scale* __restrict__ row_cd, const int* __restrict__ row_assign, int n_rows, int D,
+                                int K, int Kc, int n_ids, int j0, const int32_t* __restrict__ ids,
+                                int32_t* __restrict__ y, Scale* __restrict__ ys) {
+    const int r = blockIdx.x;
+    if (r >= n_rows) return;
+    const int a = row_assign[r], t = a / K, slot = a % K;
+    if (slot >= Kc) return;
+    const long long o = (long long)t * n_ids + j0 + slot;
+    const int64_t ymax = (int64_t)ymax_d[r];
+    const Scale cd = row_cd[r];
+    const bool zero = ids[o] < 0 || ymax == 0 || cd.mant == 0;
+    const kt::ReqDiv rq = kt::make_req(zero ? 1 : ymax);
+    for (int d = threadIdx.x; d < D; d += blockDim.x)
+        y[o * D + d] = zero ? 0 : kt::requant_row(acc[(long long)r * D + d], rq);
+    if (threadIdx.x == 0) ys[o] = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), cd);
+}
+
+__global__ void iota_kernel(int* __restrict__ p, long long n) {
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        p[i] = (int)i;
+}
+
 // combine (layers.rs:893-923) from expert outputs given as IntTensors (y rows + scales), row = slot_row[t·K + i].
 struct CombineYArgs {
     const int32_t* y;
