@@ -605,6 +605,21 @@ def run_ours(args, w, name):
     y_ref, ys_ref = dev.forward(x.data, T, x.scale)
     ok_exact = bool((yd.cpu().numpy() == y_ref).all()) and int(ys_d[0]) == ys_ref.mant
 
+    # verify::hash_int of the layer's whole output (all ranks' rows in rank order) and the repro hash with the scale
+    # (crates/01-engine/kt-core/src/verify.rs:35-41, kt-convert/src/repro.rs:34): the same for every GPU count
+    import hashlib
+
+    y_all = torch.from_numpy(np.ascontiguousarray(y_ref, dtype=np.int32)).cuda()
+    if dist is not None:
+        parts = [torch.empty_like(y_all) for _ in range(world)]
+        dist.all_gather(parts, y_all)
+        y_all = torch.cat(parts)
+    y_bytes = y_all.cpu().numpy().astype("<i4").tobytes()
+    out_hash = {"data_sha256": hashlib.sha256(y_bytes).hexdigest(),
+                "repro_sha256": hashlib.sha256(np.int64(ys_ref.mant).astype("<i8").tobytes()
+                                               + np.int32(ys_ref.shift).astype("<i4").tobytes() + y_bytes).hexdigest(),
+                "scale": [int(ys_ref.mant), int(ys_ref.shift)]}
+
     # per-expert load of this routing (rows each expert receives), summed over the ranks
     ex, _, _ = dev.route(x.data, T, x.scale)
     load = np.bincount(ex.reshape(-1), minlength=w["E"]).astype(np.int64)
@@ -700,7 +715,7 @@ def run_ours(args, w, name):
         "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
                    "router_bias": f"zipf({w['zipf']})" if w.get("zipf") else None,
                    "parallelism": f"ep{world}", "ep_transport": transport, "cuda_graphs": graphs, "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
-                   "bit_exact_vs_host_api": ok_exact},
+                   "bit_exact_vs_host_api": ok_exact, "output": out_hash},
         "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
                 "d2h_bytes_per_step": T_all * d * 4 + 16 * world},
         "gpu_launches": launches,

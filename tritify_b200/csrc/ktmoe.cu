@@ -103,6 +103,9 @@ struct ktmoe_ctx {
     cudaEvent_t ev_g0 = nullptr, ev_g1 = nullptr;  // around the last linear call's GEMM (ktmoe_linear_last_gemm)
     int last_gemm_planes = 0;                      // 0: no GEMM timed yet; 3: nine-plane kernel; 1: (1, 2) kernel
     int* d_err = nullptr;
+    // pinned host words for the status a linear call reads back with its result: [0..2] the packing counters, [3]
+    // the error word (one synchronisation for both, instead of a blocking copy each)
+    unsigned long long* h_status = nullptr;
     std::string last_error = "";
     uint64_t launches = 0;
     std::mutex mu;
@@ -1702,7 +1705,8 @@ int ktmoe_open(int device, ktmoe_ctx** out) {
     if (cudaStreamCreateWithFlags(&ctx->side, cudaStreamNonBlocking) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_fork, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&ctx->ev_join, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreate(&ctx->ev_g0) != cudaSuccess || cudaEventCreate(&ctx->ev_g1) != cudaSuccess) {
+        cudaEventCreate(&ctx->ev_g0) != cudaSuccess || cudaEventCreate(&ctx->ev_g1) != cudaSuccess ||
+        cudaHostAlloc((void**)&ctx->h_status, 4 * sizeof(unsigned long long), cudaHostAllocDefault) != cudaSuccess) {
         delete ctx;
         return KTMOE_ERR_CUDA;
     }
@@ -1734,6 +1738,7 @@ int ktmoe_close(ktmoe_ctx* ctx) {
     if (ctx->side) cudaStreamDestroy(ctx->side);
     if (ctx->ev_fork) cudaEventDestroy(ctx->ev_fork);
     if (ctx->ev_join) cudaEventDestroy(ctx->ev_join);
+    if (ctx->h_status) cudaFreeHost(ctx->h_status);
     if (ctx->ev_g0) cudaEventDestroy(ctx->ev_g0);
     if (ctx->ev_g1) cudaEventDestroy(ctx->ev_g1);
     delete ctx;
@@ -1881,10 +1886,9 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     CKL(ctx);
     bool small = false;
     if (try_small) {
-        unsigned long long hx = 1;
-        CK(cudaMemcpyAsync(&hx, counters + 2, 8, cudaMemcpyDeviceToHost, st));
+        CK(cudaMemcpyAsync(ctx->h_status + 2, counters + 2, 8, cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
-        small = hx == 0;
+        small = ctx->h_status[2] == 0;
     }
     const int BN = small ? pick_bn_small((double)rows) : pick_bn((double)rows, out_pad % dg::pair::BM2 == 0);
     GemmCall g;
@@ -1902,12 +1906,17 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     g.single_rows = rows;
     if (int r = run_gemm(ctx, st, g)) return r;
     CK(cudaEventRecord(ctx->ev_g1, st));
-    unsigned long long hbad = 0;
+    CK(cudaMemcpyAsync(ctx->h_status, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
+    ctx->h_status[3] = 0;
+    CK(cudaMemcpyAsync(ctx->h_status + 3, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
     CK(cudaMemcpyAsync(y, ctx->lin_y.p, (size_t)(rows * out) * 8, cudaMemcpyDeviceToHost, st));
-    CK(cudaMemcpyAsync(&hbad, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
-    if (int r = check_err_word(ctx)) return r;
-    if (hbad) return fail(ctx, KTMOE_ERR_RANGE, "an activation code lies outside +-WLEVELS");
+    if (ctx->h_status[3] != 0) {
+        const int code = (int)(uint32_t)ctx->h_status[3];
+        CK(cudaMemset(ctx->d_err, 0, sizeof(int)));
+        return fail(ctx, KTMOE_ERR_KERNEL, "a kernel's bounded wait expired (code " + std::to_string(code) + ")");
+    }
+    if (ctx->h_status[0]) return fail(ctx, KTMOE_ERR_RANGE, "an activation code lies outside +-WLEVELS");
     ctx->last_gemm_planes = small ? 1 : 3;
     return KTMOE_OK;
 }
