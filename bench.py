@@ -39,9 +39,11 @@ WORKLOADS = {
     "config1": dict(d=2048, E=64, f=1408, k=8, T=512, norm=False, sigmoid=False, shared=0, wseed=1, xseed=0),
     # Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
     "qwen_prefill": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
-    "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
+    "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0,
+                        decode=True),
     # BASELINE config 5, one layer: GLM-4.5-Air-shaped, sigmoid router with selection bias N(0, 0.02), shared expert.
-    "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
+    "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3,
+                       decode=True),
     "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
     # the standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
     # activations uniform in [-127, 127] from the reference's LCG, seed 2 (1 GPU).
@@ -68,6 +70,19 @@ def linear_bench_codes(tb, m, n, k):
 GEMM_METRIC = "exact int64 GEMM throughput (2·M·N·K code ops/s), bit-exact; % int8 tensor peak"
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200, bit-exact; % HBM / int8 tensor peak"
 P_PLANES = 9  # int8 plane products per code product (3 balanced base-81 digits each side)
+
+
+def decode_bytes(w, load, world):
+    """Algorithmic HBM bytes of one decode forward per GPU: the weight planes (3 B per code) of the experts this
+    routing actually touches on that GPU (3·d·f codes each), the replicated router (E·d) and shared expert (3·d·f_s),
+    and the tokens in and out (4 B per element each way). Returns the list over GPUs (experts in contiguous blocks)."""
+    d, E, f, fs, T = w["d"], w["E"], w["f"], w["shared"], w["T"]
+    out = []
+    for r in range(world):
+        lo, hi = r * E // world, (r + 1) * E // world
+        touched = int(np.count_nonzero(np.asarray(load[lo:hi])))
+        out.append(3 * (touched * 3 * d * f + E * d + 3 * d * fs) + 2 * (T // world) * d * 4)
+    return out
 
 
 def log(*a):
@@ -708,6 +723,19 @@ def run_ours(args, w, name):
         traffic = int(m.group(1)) if m else None
 
     value = T_all / (ms * 1e-3)
+    if w.get("decode"):
+        # decode streams each touched expert's planes once per step: HBM bound on the hottest GPU, the whole forward
+        per_gpu_bytes = decode_bytes(w, load, world)
+        hb = max(per_gpu_bytes)
+        roofline = {"bound": "hbm", "achieved": hb / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "frac": hb / (ms * 1e-3) / 1e9 / hbm, "traffic": None, "kernel": "the whole forward (decode)",
+                    "bytes_per_gpu": per_gpu_bytes, "experts_touched": int(np.count_nonzero(load)),
+                    "peak_source": f"{peak_kind} HBM copy bandwidth"}
+    else:
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
+                    "frac": achieved / int8_peak, "traffic": traffic, "kernel": "digit_gemm gate/up",
+                    "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
+                    "ops_per_launch": gu_ops, "plane_products": P_PLANES}
     res = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -719,10 +747,7 @@ def run_ours(args, w, name):
         "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
                 "d2h_bytes_per_step": T_all * d * 4 + 16 * world},
         "gpu_launches": launches,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                     "frac": achieved / int8_peak, "traffic": traffic, "kernel": "digit_gemm gate/up",
-                     "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
-                     "ops_per_launch": gu_ops, "plane_products": P_PLANES},
+        "roofline": roofline,
         "stage_ms": stage_ms,
         "expert_load": {"rows_per_expert": [int(v) for v in load], "rows_per_gpu": per_gpu,
                         "hottest_gpu_over_mean": max(per_gpu) / (sum(per_gpu) / world)},
