@@ -180,6 +180,11 @@ typedef int (*ktmoe_experts_fn)(void* user, int64_t rows, int32_t top_k, const i
  * layer need not be set. */
 int ktmoe_layer_forward_with_experts(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale,
                                      ktmoe_experts_fn experts_fn, void* user, int32_t* y, ktmoe_scale* y_scale);
+/* Failure detection, checked without a fault: runs the expert-parallel peer-exchange kernel against two regions of
+ * this GPU's own memory standing for two ranks, the second of which never takes part, so the kernel's bounded wait for
+ * it expires (about 2 s) and the call returns KTMOE_ERR_KERNEL, as a forward whose peer stopped does. The context
+ * stays usable afterwards. */
+int ktmoe_check_wait_expiry(ktmoe_ctx* ctx);
 /* Kernel launches of this library on the context since open (the device work is all this library's own kernels). */
 int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
 

@@ -178,6 +178,11 @@ class Context:
         self.check(st)
         return y
 
+    def check_wait_expiry(self) -> int:
+        """Failure detection without a fault (ktmoe_check_wait_expiry): the status a forward whose expert-parallel peer
+        stopped returns (KTMOE_ERR_KERNEL after the ~2 s bounded wait)."""
+        return int(lib().ktmoe_check_wait_expiry(self._h))
+
     def last_gemm(self) -> tuple:
         """(milliseconds, activation planes) of the last linear call's GEMM, timed with CUDA events on the context's
         stream; planes is 1 for the small-code kernel, 3 for the nine-plane one, 0 before any call."""

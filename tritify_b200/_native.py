@@ -49,6 +49,7 @@ SIGNATURES = {
     "ktmoe_linear_noalloc": ([_i32, _vp, _vp, _i64, _i64, _i64, _vp, _vp], ctypes.c_int),
     "ktmoe_linear_last_gemm": ([_vp, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(_i32)], ctypes.c_int),
     "ktmoe_wire_size": ([_i32, _i64, ctypes.POINTER(_u64)], ctypes.c_int),
+    "ktmoe_check_wait_expiry": ([_vp], ctypes.c_int),
     "ktmoe_layer_expert_forward": ([_vp, _vp, _i64, KtmoeScale, _vp, _i32, _vp, _vp], ctypes.c_int),
     "ktmoe_layer_forward_with_experts": ([_vp, _vp, _i64, KtmoeScale, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ktmoe_wire_encode": ([_vp, _i64, _vp, _i32, KtmoeScale, _vp, _u64, ctypes.POINTER(_u64)], ctypes.c_int),

@@ -2197,6 +2197,40 @@ int ktmoe_layer_set_ep_capacity(ktmoe_layer* L, int64_t max_tokens_per_rank) {
     return KTMOE_OK;
 }
 
+int ktmoe_check_wait_expiry(ktmoe_ctx* ctx) {
+    if (!ctx) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    cudaStream_t st = ctx->stream;
+    // two "ranks" whose regions are both this GPU's memory: rank 0 runs the exchange, rank 1 never does, so the wait
+    // for rank 1's flag expires; every access stays inside these two allocations
+    DevBuf a, b, words;
+    struct Release {
+        DevBuf* bufs[3];
+        ~Release() {
+            for (DevBuf* d : bufs) d->release();
+        }
+    } release{{&a, &b, &words}};
+    CK(a.ensure(sizeof(ep::Box)));
+    CK(b.ensure(sizeof(ep::Box)));
+    CK(words.ensure(3 * sizeof(unsigned long long)));  // [0] seq, [1] the word sent, [2] the maximum received
+    CK(cudaMemsetAsync(a.p, 0, sizeof(ep::Box), st));
+    CK(cudaMemsetAsync(b.p, 0, sizeof(ep::Box), st));
+    const unsigned long long init[3] = {1, 7, 0};
+    CK(cudaMemcpyAsync(words.p, init, sizeof(init), cudaMemcpyHostToDevice, st));
+    ep::Peers P{};
+    P.base[0] = a.as<unsigned char>();
+    P.base[1] = b.as<unsigned char>();
+    P.world = 2;
+    P.rank = 0;
+    P.seq = words.as<unsigned long long>();
+    ep::exchange_kernel<<<1, 32, 0, st>>>(P, ep::P_MERGE, words.as<unsigned long long>() + 1, 1, nullptr,
+                                          words.as<unsigned long long>() + 2, ctx->d_err);
+    CKL(ctx);
+    CK(cudaStreamSynchronize(st));
+    return check_err_word(ctx);  // KTMOE_ERR_KERNEL with the wait's code; the error word is cleared
+}
+
 int ktmoe_layer_destroy(ktmoe_layer* L) {
     if (!L) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
