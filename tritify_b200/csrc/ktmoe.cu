@@ -78,6 +78,26 @@ struct DevBuf {
     }
 };
 
+// Pinned host memory, grown on demand (the staging of small LinearBackend transfers).
+struct HostBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    cudaError_t ensure(size_t want) {
+        if (want <= bytes) return cudaSuccess;
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaHostAlloc(&p, want, cudaHostAllocDefault);
+        if (e == cudaSuccess) bytes = want;
+        return e;
+    }
+    void release() {
+        if (p) cudaFreeHost(p);
+        p = nullptr;
+        bytes = 0;
+    }
+};
+
 // Digit planes: [groups][3][rows_pad][k_pad] int8.
 struct Planes {
     int8_t* ptr = nullptr;
@@ -111,6 +131,9 @@ struct ktmoe_ctx {
     std::mutex mu;
     // LinearBackend scratch
     DevBuf lin_xi, lin_wi, lin_xp, lin_xr, lin_wp, lin_y, lin_bad;
+    // pinned staging of a call's activations and result up to LIN_STAGE_MAX bytes each: a copy through pageable
+    // memory costs the driver's own staging and a blocking wait per transfer, which dominate decode-sized calls
+    HostBuf lin_hx, lin_hy;
     // resident weights (linear_weights)
     std::unordered_map<uint64_t, Resident*> cache;
     uint64_t budget = 0, resident = 0, tick = 0;
@@ -1733,6 +1756,8 @@ int ktmoe_close(ktmoe_ctx* ctx) {
     ctx->lin_wp.release();
     ctx->lin_y.release();
     ctx->lin_bad.release();
+    ctx->lin_hx.release();
+    ctx->lin_hy.release();
     cudaFree(ctx->d_err);
     cudaStreamDestroy(ctx->stream);
     if (ctx->side) cudaStreamDestroy(ctx->side);
@@ -1776,6 +1801,8 @@ int ktmoe_resident_bytes(ktmoe_ctx* ctx, uint64_t* bytes) {
     *bytes = ctx->resident;
     return KTMOE_OK;
 }
+
+constexpr size_t LIN_STAGE_MAX = 256u << 10;
 
 static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t* x, const int32_t* w, int64_t rows,
                        int64_t out, int64_t k, int64_t* y) {
@@ -1875,7 +1902,17 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     CK(ctx->lin_xi.ensure((size_t)(rows * k) * 4));
     CK(ctx->lin_xp.ensure((size_t)(3 * rows_pad * k_pad)));
     CK(ctx->lin_y.ensure((size_t)(rows * out) * 8));
-    CK(cudaMemcpyAsync(ctx->lin_xi.p, x, (size_t)(rows * k) * 4, cudaMemcpyHostToDevice, st));
+    const size_t x_bytes = (size_t)(rows * k) * 4, y_bytes = (size_t)(rows * out) * 8;
+    const bool stage_x = x_bytes <= LIN_STAGE_MAX && ctx->lin_hx.ensure(x_bytes) == cudaSuccess;
+    const bool stage_y = y_bytes <= LIN_STAGE_MAX && ctx->lin_hy.ensure(y_bytes) == cudaSuccess;
+    cudaGetLastError();  // a failed pinned allocation only means the pageable path
+    if (stage_x) {
+        CK(cudaStreamSynchronize(st));  // an earlier call that failed may have left its copy from the staging in flight
+        std::memcpy(ctx->lin_hx.p, x, x_bytes);
+        CK(cudaMemcpyAsync(ctx->lin_xi.p, ctx->lin_hx.p, x_bytes, cudaMemcpyHostToDevice, st));
+    } else {
+        CK(cudaMemcpyAsync(ctx->lin_xi.p, x, x_bytes, cudaMemcpyHostToDevice, st));
+    }
     // with small weights, the activations are also written as one raw plane and their range decides the kernel
     const bool try_small = small_enabled && small_w;
     if (try_small) CK(ctx->lin_xr.ensure((size_t)(rows_pad * k_pad)));
@@ -1909,8 +1946,9 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     CK(cudaMemcpyAsync(ctx->h_status, ctx->lin_bad.p, 8, cudaMemcpyDeviceToHost, st));
     ctx->h_status[3] = 0;
     CK(cudaMemcpyAsync(ctx->h_status + 3, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
-    CK(cudaMemcpyAsync(y, ctx->lin_y.p, (size_t)(rows * out) * 8, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(stage_y ? ctx->lin_hy.p : (void*)y, ctx->lin_y.p, y_bytes, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
+    if (stage_y) std::memcpy(y, ctx->lin_hy.p, y_bytes);
     if (ctx->h_status[3] != 0) {
         const int code = (int)(uint32_t)ctx->h_status[3];
         CK(cudaMemset(ctx->d_err, 0, sizeof(int)));
