@@ -137,3 +137,26 @@ def test_seam_errors(ctx):
     want = m.forward_int(x)  # the layer stays usable
     got = m.forward_int_with_experts(x, lambda ids, row: m.expert_outputs(row, np.array([ids]))[0])
     assert got.scale == want.scale and (got.data == want.data).all()
+
+
+def test_seam_with_zero_input_and_empty_routes(ctx, oracle):
+    """A zero input (zero codes, zero scale): the callback sees ids -1 exactly for the rows whose route is empty
+    (sumc <= 0), and the result equals the plain forward and the oracle."""
+    c = cases.CASES["tiny_sigmoid_shared"]
+    m = cases.build_layer(c, ctx)
+    x = tb.IntTensor(np.zeros(c.T * c.d, np.int32), (c.T, c.d), tb.Scale.ZERO)
+    want = m.forward_int(x)
+    o = cases.build_oracle(c, oracle)
+    wy, ws = o.forward(x.data.reshape(c.T, c.d), (0, 0))
+    assert (want.scale.mant, want.scale.shift) == ws and (want.data.reshape(wy.shape) == wy).all()
+    seen = []
+
+    def fn(ids, xr, xs):
+        seen.append(ids.copy())
+        return m.device_layer().expert_forward(xr, ids.shape[0], xs, ids)
+
+    y, ys = m.device_layer().forward_with_experts(x.data, c.T, x.scale, fn)
+    assert ys == want.scale and (y == want.data).all()
+    _, _, sumc = o.route(x.data.reshape(c.T, c.d), (0, 0))
+    for t in range(c.T):
+        assert (seen[0][t] < 0).all() == (sumc[t] <= 0)
