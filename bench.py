@@ -458,8 +458,7 @@ def run_linear_bench_ours(args, w, name):
     torch.cuda.set_device(local)
     ctx = tb.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream())
-    _, bf16, peak_kind = measured_peaks()
-    hbm, _, _ = measured_peaks()
+    hbm, _, peak_kind = measured_peaks()
     rows_out, tot_mac, tot_us, tot_gemm_us, h2d, d2h = [], 0, 0.0, 0.0, 0, 0
     launches0 = ctx.launch_count()
     lm = None

@@ -183,7 +183,7 @@ int ktmoe_layer_forward_with_experts(ktmoe_layer* layer, const int32_t* x, int64
 /* Failure detection, checked without a fault: runs the expert-parallel peer-exchange kernel against two regions of
  * this GPU's own memory standing for two ranks, the second of which never takes part, so the kernel's bounded wait for
  * it expires (about 2 s) and the call returns KTMOE_ERR_KERNEL, as a forward whose peer stopped does. The context
- * stays usable afterwards. */
+ * stays usable afterwards. No counterpart in the reference (its CPU path has no waits). */
 int ktmoe_check_wait_expiry(ktmoe_ctx* ctx);
 /* Kernel launches of this library on the context since open (the device work is all this library's own kernels). */
 int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
