@@ -27,7 +27,8 @@ from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 
 __all__ = [
     "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
-    "B200Linear", "Context", "DeviceLayer", "device_count", "synth_normal", "lcg_uniform", "table", "KtmoeError",
+    "B200Linear", "Context", "DeviceLayer", "MoeStack", "device_count", "synth_normal", "lcg_uniform", "table",
+    "KtmoeError",
     "ep_unique_id",
 ]
 
@@ -387,6 +388,14 @@ class DeviceLayer:
                                                ctypes.c_void_p(y_ptr), ctypes.c_void_p(y_scale_ptr),
                                                ctypes.c_void_p(stream) if stream else None))
 
+    def block_forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int,
+                          stream: int = 0) -> None:
+        """The block x + moe(rms_norm(x)) on device buffers (raw pointers), stream-ordered, not synchronised."""
+        self.ctx.check(lib().ktmoe_block_forward_dev(self._h, ctypes.c_void_p(x_ptr), rows,
+                                                     ctypes.c_void_p(x_scale_ptr), ctypes.c_void_p(y_ptr),
+                                                     ctypes.c_void_p(y_scale_ptr),
+                                                     ctypes.c_void_p(stream) if stream else None))
+
     def route(self, x: np.ndarray, rows: int, x_scale: Scale):
         x = np.ascontiguousarray(x, dtype=np.int32).reshape(-1)
         ex = np.empty(rows * self.top_k, dtype=np.int32)
@@ -616,6 +625,69 @@ class MoeMlp:
     def route_trace(self, x: IntTensor) -> List[List[int]]:
         """Module::route_trace (layers.rs:1089-1100)."""
         return [r.experts for r in self.route(x)]
+
+
+class MoeStack:
+    """A stack of MoE decoder-block FFN halves with attention excluded (the shape of a GLM-4.5-Air-style model's 45
+    MoE layers): for each layer l, x ← add(x, moe_l(rms_norm_l(x))) (kt-core model.rs:175-181), the residual stream
+    staying on the device between layers in two ping-pong buffers. Every layer is a :class:`DeviceLayer` with its norm
+    set (``set_norm``), all on one context; each layer's block is one ``ktmoe_block_forward_dev`` on that context's
+    stream (with the layer's CUDA graphs when enabled: the buffers a layer sees are the same on every call)."""
+
+    def __init__(self, layers: Sequence[DeviceLayer]):
+        if not layers:
+            raise ValueError("a stack needs at least one layer")
+        self.layers = list(layers)
+        self.ctx = self.layers[0].ctx
+        self.d_model = self.layers[0].d_model
+        if any(L.ctx is not self.ctx or L.d_model != self.d_model for L in self.layers):
+            raise ValueError("the layers of a stack share one context and one d_model")
+        self._bufs = None
+
+    def _buffers(self, rows: int):
+        """Four int32 [rows·d] buffers and their scales: the input, two ping-pong, the output. Kept across calls, so a
+        layer sees the same pointers every time (its CUDA graphs are reused)."""
+        import torch  # device memory for the residual stream (plumbing only)
+
+        if self._bufs is None or self._bufs[0] < rows:
+            dev = torch.device("cuda", self.ctx.device)
+            n = max(1, rows) * self.d_model
+            self._bufs = (rows, [torch.empty(n, dtype=torch.int32, device=dev) for _ in range(4)],
+                          [torch.zeros(2, dtype=torch.int64, device=dev) for _ in range(4)])
+        return self._bufs
+
+    def forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int) -> None:
+        """Device buffers (raw pointers; a Scale is 16 bytes {i64 mant, i32 shift}); ordered on the context's stream,
+        not synchronised."""
+        _, xb, sb = self._buffers(rows)
+        src, src_s = x_ptr, x_scale_ptr
+        for i, L in enumerate(self.layers):
+            last = i == len(self.layers) - 1
+            dst = y_ptr if last else xb[1 + i % 2].data_ptr()
+            dst_s = y_scale_ptr if last else sb[1 + i % 2].data_ptr()
+            L.block_forward_dev(src, rows, src_s, dst, dst_s)
+            src, src_s = dst, dst_s
+
+    def forward(self, x: IntTensor) -> IntTensor:
+        """Host tensors in and out (synchronous)."""
+        import torch
+
+        d = self.d_model
+        if len(x) % d != 0:
+            raise ValueError("stack input length must be a multiple of d_model")
+        rows = len(x) // d
+        _, xb, sb = self._buffers(rows)
+        n = rows * d
+        xb[0][:n].copy_(torch.from_numpy(np.ascontiguousarray(x.data, dtype=np.int32)))
+        sb[0].copy_(torch.tensor([x.scale.mant, x.scale.shift & 0xFFFFFFFF], dtype=torch.int64))
+        torch.cuda.synchronize(xb[0].device)  # the uploads ran on torch's stream; the layers run on the context's
+        self.forward_dev(xb[0].data_ptr(), rows, sb[0].data_ptr(), xb[3].data_ptr(), sb[3].data_ptr())
+        self.ctx.sync()
+        y = xb[3][:n].cpu().numpy().copy()
+        s = sb[3].cpu().numpy()
+        shift = int(s[1]) & 0xFFFFFFFF
+        shift = shift - (1 << 32) if shift >= 1 << 31 else shift
+        return IntTensor(y, (d,) if rows == 1 else (rows, d), Scale(int(s[0]), shift))
 
 
 def scale_from_f64(x: float) -> Scale:

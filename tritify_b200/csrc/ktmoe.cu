@@ -1640,6 +1640,7 @@ int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, in
         return KTMOE_OK;
     }
     if (L->graph_cache.size() >= 16) {
+        cudaStreamSynchronize(L->graph_cache.front().st);  // no launch of the evicted graph is still in flight
         cudaGraphExecDestroy(L->graph_cache.front().exec);
         L->graph_cache.erase(L->graph_cache.begin());
     }
