@@ -111,6 +111,7 @@ class ClockSampler:
         self.index = index
         self.proc = None
         self.lines = []
+        self.started = threading.Event()
 
     def __enter__(self):
         try:
@@ -119,6 +120,8 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi takes a moment to start: let its first sample arrive (bounded) before the timed region
+            self.started.wait(timeout=3.0)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -126,6 +129,8 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.started.set()
+        self.started.set()
 
     def __exit__(self, *a):
         if self.proc:
