@@ -2,9 +2,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-A step is one forward of one MoE layer over one batch of synthetic tokens (the reference has no
-normal RNG, so inputs come from the build-defined splitmix64 + Box-Muller generator). The default workload is BASELINE
-config 4, the largest configuration that fits one GPU: a Mixtral-8x7B-shaped layer (d_model 4096, 8 experts of
+A step is one forward of one MoE layer over one batch of synthetic tokens (the benchmark's named configurations; the
+reference has no normal RNG, so inputs come from the build-defined splitmix64 + Box-Muller generator). The default
+workload is the largest configuration that fits one GPU: a Mixtral-8x7B-shaped layer (d_model 4096, 8 experts of
 d_ff 14336, top-2, norm_topk), 8192 prefill tokens. ``value`` is device-timed tokens/s with inputs resident in HBM;
 ``e2e`` is the same metric through the public C ABI call (ktmoe_forward) with pinned host buffers, so every step
 includes the host-to-device copy of the tokens and the device-to-host read of the result. ``--impl reference`` times
@@ -29,23 +29,23 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 WORKLOADS = {
-    # BASELINE config 4 (i): Mixtral-8x7B-shaped, uniform router N(0, 0.02), prefill 8192 tokens.
+    # Mixtral-8x7B-shaped, uniform router N(0, 0.02), prefill 8192 tokens; one expert per GPU at 8 GPUs.
     "mixtral_prefill": dict(d=4096, E=8, f=14336, k=2, T=8192, norm=True, sigmoid=False, shared=0, wseed=1, xseed=0),
-    # BASELINE config 4 (ii): the same layer with a router bias (QuantLinear::with_bias on the router) fitted so that
+    # The same layer with a router bias (QuantLinear::with_bias on the router) fitted so that
     # the top-2 selections follow Zipf(1.2) over the experts; with one expert per GPU the hottest GPU bounds the step.
     "mixtral_zipf": dict(d=4096, E=8, f=14336, k=2, T=8192, norm=True, sigmoid=False, shared=0, wseed=1, xseed=0,
                          zipf=1.2),
-    # the CPU-parity layer.
+    # The CPU-parity layer: d 2048, 64 experts of d_ff 1408, top-8, softmax without norm_topk, 512 tokens.
     "config1": dict(d=2048, E=64, f=1408, k=8, T=512, norm=False, sigmoid=False, shared=0, wseed=1, xseed=0),
-    # BASELINE config 3: Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
+    # Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
     "qwen_prefill": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
     "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0,
                         decode=True),
-    # BASELINE config 5, one layer: GLM-4.5-Air-shaped, sigmoid router with selection bias N(0, 0.02), shared expert.
+    # One layer of the GLM-4.5-Air-shaped stack: sigmoid router with selection bias N(0, 0.02), shared expert.
     "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3,
                        decode=True),
     "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
-    # the standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
+    # The standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
     # activations uniform in [-127, 127] from the reference's LCG, seed 2 (1 GPU).
     "gemm4096": dict(gemm=True, M=4096, N=4096, K=4096, seed=2),
     # The reference's LinearBackend benchmark shapes (kt-runtime/examples/cuda_bench.rs:59-66): an OLMoE-sized prefill,

@@ -46,7 +46,7 @@ CASES = {
         Case("tiny_sigmoid_raw_shared_one_row", d=64, E=16, f=48, k=4, T=1, norm=False, sigmoid=True, shared=40,
              wseed=21, xseed=22),
         Case("small_shared_softmax", d=256, E=32, f=192, k=6, T=48, norm=True, shared=384, wseed=23, xseed=24),
-        # BASELINE config 1 (the CPU-parity layer): d=2048, E=64, f=1408, k=8, T=512, softmax, norm_topk=false,
+        # The CPU-parity layer: d=2048, E=64, f=1408, k=8, T=512, softmax, norm_topk=false,
         # hidden N(0,1) seed 0, weights N(0,0.02) seed 1.
         Case("config1", d=2048, E=64, f=1408, k=8, T=512, norm=False, wseed=1, xseed=0),
         Case("config1_norm_topk", d=2048, E=64, f=1408, k=8, T=512, norm=True, wseed=1, xseed=0),

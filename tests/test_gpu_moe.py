@@ -63,7 +63,7 @@ def test_small_cases_equal_the_oracle(ctx, oracle, name):
 @pytest.mark.parametrize("pair", ["1", "0"])
 @pytest.mark.parametrize("name", ["config1", "config1_norm_topk"])
 def test_config1_is_bit_identical_to_the_golden_hash(ctx, name, pair, monkeypatch):
-    """d=2048, E=64, f=1408, k=8, T=512 — same SHA-256 as the CPU integer path, with the expert
+    """The CPU-parity layer: d=2048, E=64, f=1408, k=8, T=512 — same SHA-256 as the CPU integer path, with the expert
     GEMMs on SM pairs (64 rows per expert on average) and, with KTMOE_PAIR=0, on single SMs."""
     monkeypatch.setenv("KTMOE_PAIR", pair)
     c = cases.CASES[name]

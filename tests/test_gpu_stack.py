@@ -1,6 +1,6 @@
-"""A stack of MoE block FFN halves, x ← add(x, moe_l(rms_norm_l(x))) for each layer l (kt-core model.rs:175-181, the
-shape of BASELINE config 5 with attention excluded), with the residual stream on the device between layers, against the
-oracle's layer-by-layer loop; with and without the layers' CUDA graphs."""
+"""A stack of MoE block FFN halves, x ← add(x, moe_l(rms_norm_l(x))) for each layer l (kt-core model.rs:175-181; the
+shape of a GLM-4.5-Air-style model's MoE layers with attention excluded), with the residual stream on the device
+between layers, against the oracle's layer-by-layer loop; with and without the layers' CUDA graphs."""
 
 import dataclasses
 import os
