@@ -598,7 +598,11 @@ def run_ours(args, w, name):
     # the exchange of an expert-parallel layer: peer memory over NVLink (default) or NCCL (KTMOE_EP=nccl)
     transport = os.environ.get("KTMOE_EP", "peer") if world > 1 else None
     if transport == "peer":
-        dev.set_ep_capacity(T)
+        try:
+            dev.set_ep_capacity(T)  # collective: every rank gets the same outcome
+        except tb.KtmoeError as e:
+            log(f"[bench] the peer transport could not be set up ({e}); exchanging over NCCL")
+            transport = "nccl (peer set-up failed)"
     log(f"[bench] {name}: layer resident in {time.perf_counter() - t_build:.1f} s")
 
     stream = torch.cuda.ExternalStream(ctx.stream())
