@@ -844,6 +844,73 @@ void ko_linear(const int32_t* x, const int32_t* w, size_t rows, size_t out, size
     if (!r.empty()) std::memcpy(y, r.data(), r.size() * 8);
 }
 
+// ── the digit algorithm as a second, independent GEMM (kt-cuda's host executor) ──
+// kt-cuda/src/digits.rs:40-52 (split): a code |v| <= WLEVELS is three balanced base-81 digits, low digit first, each
+// the remainder of (r + 40) mod 81 shifted back by 40, the rest carried exactly. Returns false beyond ±WLEVELS.
+static bool split_digits(int32_t v, int8_t d[3]) {
+    if (v > (int32_t)WLEVELS || v < -(int32_t)WLEVELS) return false;
+    int32_t r = v;
+    for (int i = 0; i < 3; ++i) {
+        int32_t m = (r + 40) % 81;
+        if (m < 0) m += 81;  // rem_euclid
+        d[i] = (int8_t)(m - 40);
+        r = (r - (m - 40)) / 81;
+    }
+    return r == 0;
+}
+
+// kt-cuda/src/host.rs:47-76 (dot_tiles) without the tile layout: nine int32 sums s[i][j] = Σ x_i·w_j that wrap as the
+// hardware's accumulators do, added into i64 with weight 81^(i+j) every `flush` terms (digits.rs:16-19: KT_FLUSH tiles
+// of 16 terms), so the result equals the plain i64 dot product exactly when the flush bound holds.
+void ko_linear_digits(const int32_t* x, const int32_t* w, size_t rows, size_t out, size_t k, size_t flush, int64_t* y) {
+    static const int64_t SCALE[5] = {1, 81, 81 * 81, 81 * 81 * 81, 81LL * 81 * 81 * 81};
+    std::vector<int8_t> xd(rows * k * 3), wd(out * k * 3);
+    for (size_t i = 0; i < rows * k; ++i) split_digits(x[i], &xd[i * 3]);
+    for (size_t i = 0; i < out * k; ++i) split_digits(w[i], &wd[i * 3]);
+    if (flush == 0) flush = k ? k : 1;
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t o = 0; o < out; ++o) {
+            int64_t acc = 0;
+            for (size_t k0 = 0; k0 < k; k0 += flush) {
+                const size_t k1 = std::min(k, k0 + flush);
+                uint32_t s[3][3] = {};
+                for (size_t t = k0; t < k1; ++t) {
+                    const int8_t* a = &xd[(r * k + t) * 3];
+                    const int8_t* b = &wd[(o * k + t) * 3];
+                    for (int i = 0; i < 3; ++i)
+                        for (int j = 0; j < 3; ++j) s[i][j] += (uint32_t)(int32_t)(a[i] * b[j]);
+                }
+                for (int i = 0; i < 3; ++i)
+                    for (int j = 0; j < 3; ++j) acc += SCALE[i + j] * (int64_t)(int32_t)s[i][j];
+            }
+            y[r * out + o] = acc;
+        }
+}
+
+// The reduced-plane decomposition of the library's small-code GEMM (this build's, not the reference's): x in
+// [-127, 127] as one raw int8 plane, w in [-3280, 3280] as its two low balanced digits (the third is zero there);
+// two wrapping int32 sums s_j = Σ x·w_j per flush of `flush` terms, recombined as s_0 + 81·s_1.
+void ko_linear_small(const int32_t* x, const int32_t* w, size_t rows, size_t out, size_t k, size_t flush, int64_t* y) {
+    std::vector<int8_t> wd(out * k * 3);
+    for (size_t i = 0; i < out * k; ++i) split_digits(w[i], &wd[i * 3]);
+    if (flush == 0) flush = k ? k : 1;
+    for (size_t r = 0; r < rows; ++r)
+        for (size_t o = 0; o < out; ++o) {
+            int64_t acc = 0;
+            for (size_t k0 = 0; k0 < k; k0 += flush) {
+                const size_t k1 = std::min(k, k0 + flush);
+                uint32_t s0 = 0, s1 = 0;
+                for (size_t t = k0; t < k1; ++t) {
+                    const int32_t a = x[r * k + t];
+                    s0 += (uint32_t)(a * wd[(o * k + t) * 3]);
+                    s1 += (uint32_t)(a * wd[(o * k + t) * 3 + 1]);
+                }
+                acc += (int64_t)(int32_t)s0 + 81 * (int64_t)(int32_t)s1;
+            }
+            y[r * out + o] = acc;
+        }
+}
+
 // The equality-gate corpus (crates/02-runtime/kt-runtime/src/gate.rs:26-56). ko_corpus_case(i, ...) returns the
 // shape of case i (or -1 past the end); with non-null buffers it also writes its operands.
 int ko_corpus_case(int i, size_t* rows, size_t* out, size_t* k, int32_t* x, int32_t* w) {

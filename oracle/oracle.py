@@ -66,6 +66,8 @@ def lib():
             "ko_quantize_bias": ([f32p, sz, i64p, p(KoScale)], ctypes.c_int),
             "ko_from_reals_f32": ([f32p, sz, ctypes.c_int64, i32p, p(KoScale)], None),
             "ko_linear": ([i32p, i32p, sz, sz, sz, i64p], None),
+            "ko_linear_digits": ([i32p, i32p, sz, sz, sz, sz, i64p], None),
+            "ko_linear_small": ([i32p, i32p, sz, sz, sz, sz, i64p], None),
             "ko_corpus_case": ([ctypes.c_int, p(sz), p(sz), p(sz), i32p, i32p], ctypes.c_int),
             "ko_moe_new": ([sz, sz, sz, sz, f32p, f32p, f32p, ctypes.c_int, f32p, sz, f32p], ctypes.c_void_p),
             "ko_moe_free": ([ctypes.c_void_p], None),
@@ -184,6 +186,28 @@ def linear(x: np.ndarray, w: np.ndarray, rows: int, out: int, k: int) -> np.ndar
     w = np.ascontiguousarray(w, dtype=np.int32)
     y = np.empty(rows * out, dtype=np.int64)
     lib().ko_linear(_p(x, ctypes.c_int32), _p(w, ctypes.c_int32), rows, out, k, _p(y, ctypes.c_int64))
+    return y
+
+
+KT_FLUSH_TERMS = 83886 * 16  # kt-cuda/src/digits.rs:16-19: KT_FLUSH tiles of 16 terms
+SMALL_FLUSH_TERMS = 422733  # the small-code GEMM's split: floor((2^31 - 1) / (127 · 40))
+
+
+def linear_digits(x: np.ndarray, w: np.ndarray, rows: int, out: int, k: int, flush: int = KT_FLUSH_TERMS):
+    """The reference's digit algorithm (kt-cuda host executor): nine wrapping int32 plane sums flushed into i64."""
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.int32)
+    y = np.empty(rows * out, dtype=np.int64)
+    lib().ko_linear_digits(_p(x, ctypes.c_int32), _p(w, ctypes.c_int32), rows, out, k, flush, _p(y, ctypes.c_int64))
+    return y
+
+
+def linear_small(x: np.ndarray, w: np.ndarray, rows: int, out: int, k: int, flush: int = SMALL_FLUSH_TERMS):
+    """The library's (1, 2)-plane decomposition for |x| <= 127, |w| <= 3280: two wrapping int32 sums flushed into i64."""
+    x = np.ascontiguousarray(x, dtype=np.int32)
+    w = np.ascontiguousarray(w, dtype=np.int32)
+    y = np.empty(rows * out, dtype=np.int64)
+    lib().ko_linear_small(_p(x, ctypes.c_int32), _p(w, ctypes.c_int32), rows, out, k, flush, _p(y, ctypes.c_int64))
     return y
 
 
