@@ -1,10 +1,12 @@
 // ktmoe: tritify's integer MoE layer and its exact linear accumulate on B200, behind the C ABI of include/ktmoe.h.
 //
-// Host side: contexts (device + stream + resident weights), TMA tensor maps, the launch sequence of one layer
-// forward, and the offline f64 preparation entry points. Device side: digit_gemm.cuh (the tcgen05 digit-plane GEMM)
-// and moe_kernels.cuh (routing, dispatch, SwiGLU/requant, combine, merge, shared expert). There is no CPU compute
-// path: every result comes from the kernels in this library, and a context on a device that is not sm_100 fails to
-// open.
+// Host side: contexts (device + stream + resident weights), TMA tensor maps, the launch sequence of one layer forward
+// and of the decoder block around it, the expert-parallel exchange (NCCL, or peer memory through ep_peer.cuh), the
+// seam entry points for experts on other hosts, and the offline f64 preparation entry points. Device side:
+// digit_gemm.cuh and digit_gemm_pair.cuh (the tcgen05 digit-plane GEMMs, nine-plane and small-code), moe_kernels.cuh
+// (routing, dispatch, SwiGLU/requant, combine, merge, shared expert, RmsNorm, add). The activation wire format is in
+// wire.cpp. There is no CPU compute path: every result comes from the kernels in this library, and a context on a
+// device that is not sm_100 fails to open.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
