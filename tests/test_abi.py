@@ -39,3 +39,22 @@ def test_no_device_here_is_reported_not_crashed():
         pytest.skip("a GPU is present")
     h = ctypes.c_void_p()
     assert tb.lib().ktmoe_open(0, ctypes.byref(h)) == _native.ERR_NO_DEVICE
+
+
+def declared_arities():
+    """name -> number of parameters, from each `ret ktmoe_name(params);` declaration of the header."""
+    text = open(os.path.join(ROOT, "include", "ktmoe.h")).read()
+    text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(ktmoe_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text):
+        params = " ".join(m.group(2).split())
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_the_binding_passes_as_many_arguments_as_the_header_declares():
+    arity = declared_arities()
+    assert len(arity) >= 25
+    for name, (argtypes, _) in _native.SIGNATURES.items():
+        assert name in arity, name
+        assert len(argtypes) == arity[name], f"{name}: header {arity[name]} parameters, binding {len(argtypes)}"
