@@ -37,10 +37,18 @@ WORKLOADS = {
                          zipf=1.2),
     # The CPU-parity layer: d 2048, 64 experts of d_ff 1408, top-8, softmax without norm_topk, 512 tokens.
     "config1": dict(d=2048, E=64, f=1408, k=8, T=512, norm=False, sigmoid=False, shared=0, wseed=1, xseed=0),
-    # Qwen1.5-MoE-A2.7B-shaped, unweighted shared expert (the reference's only shared form).
-    "qwen_prefill": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0),
-    "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1, xseed=0,
-                        decode=True),
+    # Qwen1.5-MoE-A2.7B-shaped as the benchmark writes it: the shared expert behind a sigmoid gate (shared_expert_gate,
+    # an extension: the reference refuses gated shared experts, so its parity rests on the oracle's restatement of
+    # this build's definition) ...
+    "qwen_prefill": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632, gated=True,
+                         wseed=1, xseed=0),
+    "qwen_decode": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, gated=True, wseed=1,
+                        xseed=0, decode=True),
+    # ... and with the reference's own unweighted shared expert (bit parity with the reference's path).
+    "qwen_prefill_unweighted": dict(d=2048, E=60, f=1408, k=4, T=4096, norm=True, sigmoid=False, shared=5632,
+                                    wseed=1, xseed=0),
+    "qwen_decode_unweighted": dict(d=2048, E=60, f=1408, k=4, T=64, norm=True, sigmoid=False, shared=5632, wseed=1,
+                                   xseed=0, decode=True),
     # One layer of the GLM-4.5-Air-shaped stack: sigmoid router with selection bias N(0, 0.02), shared expert.
     "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3,
                        decode=True),
@@ -63,10 +71,14 @@ def linear_bench_shapes():
     return shapes
 
 
-def linear_bench_codes(tb, m, n, k):
-    """cuda_bench.rs:13-21: x = codes(m·k, 1 + m), w = codes(n·k, 2 + n), uniform in [-WLEVELS, WLEVELS]."""
-    lv = tb.WLEVELS
-    return tb.lcg_uniform(1 + m, -lv, lv, m * k), tb.lcg_uniform(2 + n, -lv, lv, n * k)
+WLEVELS = 265720  # (3^12 - 1) / 2, the 12-trit code range (layers.rs:15-16)
+
+
+def linear_bench_codes(lcg, m, n, k):
+    """cuda_bench.rs:13-21: x = codes(m·k, 1 + m), w = codes(n·k, 2 + n), uniform in [-WLEVELS, WLEVELS]. ``lcg`` is
+    the reference's test LCG (seed, lo, hi, n) -> int32 array: the product's in our arm, the oracle's in the
+    reference arm."""
+    return lcg(1 + m, -WLEVELS, WLEVELS, m * k), lcg(2 + n, -WLEVELS, WLEVELS, n * k)
 GEMM_METRIC = "exact int64 GEMM throughput (2·M·N·K code ops/s), bit-exact; % int8 tensor peak"
 METRIC = "MoE-layer tokens/s at 1/2/4/8 B200, bit-exact; % HBM / int8 tensor peak"
 P_PLANES = 9  # int8 plane products per code product (3 balanced base-81 digits each side)
@@ -170,18 +182,17 @@ def measured_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def zipf_router_bias(w, tokens=2048, iters=300):
+def zipf_router_bias(w, synth, tokens=2048, iters=300):
     """A router bias (f32, one per expert) under which the top-k selections of the workload's tokens are distributed
     as Zipf(s) over the experts: expert e is chosen with frequency proportional to (e + 1)^-s. Fitted on the float
     logits of the first ``tokens`` tokens (x·W_router^T + b, the generator's f32 values in f64 arithmetic) by repeated
     corrections b_e += log(target_e / observed_e); deterministic. The integer path routes on the quantised codes, so
-    its frequencies follow the target closely but not exactly; the bench reports the observed load."""
-    import tritify_b200 as tb
-
+    its frequencies follow the target closely but not exactly; the bench reports the observed load. ``synth`` is the
+    generator (seed, sigma, n, offset) -> f32 array."""
     d, E, k, s = w["d"], w["E"], w["k"], w["zipf"]
     n = min(tokens, w["T"])
-    x = tb.synth_normal(w["xseed"], 1.0, n * d).reshape(n, d).astype(np.float64)
-    wr = tb.synth_normal(w["wseed"], 0.02, E * d).reshape(E, d).astype(np.float64)
+    x = synth(w["xseed"], 1.0, n * d, 0).reshape(n, d).astype(np.float64)
+    wr = synth(w["wseed"], 0.02, E * d, 0).reshape(E, d).astype(np.float64)
     logits = x @ wr.T
     target = np.arange(1, E + 1, dtype=np.float64) ** -s
     target /= target.sum()
@@ -213,7 +224,8 @@ def build_product_layer(w, ctx, ep=None):
     router = q(0, E, d)
     rbias = None
     if w.get("zipf"):
-        rbias = tb.QuantLinear("router", router[0], router[1], E, d).with_bias(zipf_router_bias(w)).bias
+        rbias = tb.QuantLinear("router", router[0], router[1], E, d).with_bias(
+            zipf_router_bias(w, lambda sd, sg, n, o: tb.synth_normal(sd, sg, n, offset=o))).bias
     dev.set_router(router[0], router[1], rbias)
     base = E * d
     for e in dev.experts:
@@ -222,6 +234,8 @@ def build_product_layer(w, ctx, ep=None):
     if fs:
         o = base + E * 3 * f * d
         dev.set_shared(q(o, fs, d), q(o + fs * d, fs, d), q(o + 2 * fs * d, d, fs))
+        if w.get("gated"):
+            dev.set_shared_gate(q(o + 3 * fs * d, 1, d))  # shared_expert_gate [1, d], next in the stream
     if w["sigmoid"]:
         b = tb.synth_normal(w["wseed"] + 2, 0.02, E)
         codes = np.empty(E, dtype=np.int64)
@@ -232,24 +246,25 @@ def build_product_layer(w, ctx, ep=None):
 
 
 def build_oracle_layer(w, O):
-    import tritify_b200 as tb
-
+    """The workload's layer in the CPU oracle (the reference's path restated), built from the same generator bytes by
+    the oracle's own generator and quantiser: nothing of the product library is loaded."""
     d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
     off = 0
 
     def take(n):
         nonlocal off
-        a = tb.synth_normal(w["wseed"], 0.02, n, offset=off)
+        a = O.synth_normal(w["wseed"], 0.02, n, offset=off)
         off += n
         return a
 
     router = take(E * d)
     experts = take(E * 3 * f * d)
     shared = take(3 * fs * d) if fs else None
-    sbias = tb.synth_normal(w["wseed"] + 2, 0.02, E) if w["sigmoid"] else None
-    rbias = zipf_router_bias(w) if w.get("zipf") else None
+    gate = take(d) if fs and w.get("gated") else None
+    sbias = O.synth_normal(w["wseed"] + 2, 0.02, E) if w["sigmoid"] else None
+    rbias = zipf_router_bias(w, lambda sd, sg, n, o: O.synth_normal(sd, sg, n, offset=o)) if w.get("zipf") else None
     return O.MoeOracle(d, E, f, w["k"], router, experts, router_bias=rbias, norm_topk=w["norm"], sigmoid_bias=sbias,
-                       shared_hidden=fs, shared_w=shared)
+                       shared_hidden=fs, shared_w=shared, shared_gate_w=gate)
 
 
 def make_x(w, rows=None):
@@ -259,13 +274,44 @@ def make_x(w, rows=None):
     return tb.IntTensor.from_reals(tb.synth_normal(w["xseed"], 1.0, T * w["d"]).reshape(T, w["d"]))
 
 
+def oracle_x(w, O):
+    """The workload's tokens through the oracle's entry quantiser (IntTensor::from_reals, tensor.rs:106-116):
+    (codes [T, d], (mant, shift))."""
+    xi, xs = O.from_reals_f32(O.synth_normal(w["xseed"], 1.0, w["T"] * w["d"]))
+    return xi.reshape(w["T"], w["d"]), xs
+
+
+def workload_config(w, name):
+    """The workload-identifying config, the same in both arms."""
+    return {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
+            "shared_gate": "sigmoid (extension)" if w.get("gated") else None,
+            "router_bias": f"zipf({w['zipf']})" if w.get("zipf") else None,
+            "l2": "working set (weight planes) larger than L2, no flush"}
+
+
+GOLDEN_PATH = os.path.join(ROOT, "tests", "golden", "bench_golden.json")
+
+
+def golden_parity(name, out_hash, w):
+    """Compare a run's output hashes with the CPU oracle's committed golden for this workload (tests/golden/
+    bench_golden.json, made by tests/golden/make_bench_golden.py): "golden", "MISMATCH" or "no golden" (a workload
+    without a committed golden, or token/expert counts overridden on the command line)."""
+    try:
+        g = json.load(open(GOLDEN_PATH)).get("workloads", {}).get(name)
+    except (OSError, ValueError):
+        g = None
+    if g is None or g.get("T") != w.get("T") or g.get("E") != w.get("E"):
+        return "no golden"
+    want = g["output"]
+    same = all(out_hash.get(k) == want.get(k) for k in ("data_sha256", "repro_sha256"))
+    return "golden" if same else "MISMATCH"
+
+
 def cpu_sample(w, seconds_target: float, O, max_rows=None):
     """Time the oracle (the reference's CPU path, restated) on a bounded sample of the workload's tokens."""
     O.lib().ko_set_max_threads(0)  # every host core, as the reference's default (TRITIFY_THREADS unset)
     m = build_oracle_layer(w, O)
-    x = make_x(w)
-    xi = x.data.reshape(w["T"], w["d"])
-    xs = (x.scale.mant, x.scale.shift)
+    xi, xs = oracle_x(w, O)
     t0 = time.perf_counter()
     m.forward(xi[:2], xs)
     per_tok = max((time.perf_counter() - t0) / 2, 1e-6)
@@ -295,7 +341,7 @@ def run_reference(args, w, name):
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")}},
+        "config": workload_config(w, name), "parallelism": f"ep{world}",
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
@@ -314,14 +360,13 @@ def lcg_state_after(seed: int, n: int) -> int:
     return (acc_a * seed + acc_c) % m
 
 
-def gemm_codes(w):
+def gemm_codes(w, lcg):
     """One stream of the reference's test LCG with the config's seed (as gate.rs:446-459 draws its corpus): first the
-    weights w [M][K] uniform in [-2048, 2047], then the activations x [N][K] uniform in [-127, 127]."""
-    import tritify_b200 as tb
-
+    weights w [M][K] uniform in [-2048, 2047], then the activations x [N][K] uniform in [-127, 127]. ``lcg`` as in
+    linear_bench_codes."""
     nw = w["M"] * w["K"]
-    wt = tb.lcg_uniform(w["seed"], -2048, 2047, nw)
-    x = tb.lcg_uniform(lcg_state_after(w["seed"], nw), -127, 127, w["N"] * w["K"])
+    wt = lcg(w["seed"], -2048, 2047, nw)
+    x = lcg(lcg_state_after(w["seed"], nw), -127, 127, w["N"] * w["K"])
     return x, wt
 
 
@@ -349,7 +394,7 @@ def run_gemm_reference(args, w, name):
 
     O.build()
     O.lib().ko_set_max_threads(0)
-    x, wt = gemm_codes(w)
+    x, wt = gemm_codes(w, O.lcg_uniform)
     M, K = w["M"], w["K"]
     rows = gemm_cpu_sample(w, 150.0 / max(1, args.steps + args.warmup), O, x, wt)
     for _ in range(args.warmup):
@@ -382,7 +427,7 @@ def run_gemm_ours(args, w, name):
         return  # a 1-GPU workload: other ranks idle
     torch.cuda.set_device(local)
     M, N, K = w["M"], w["N"], w["K"]
-    x, wt = gemm_codes(w)
+    x, wt = gemm_codes(w, tb.lcg_uniform)
     ctx = tb.Context(local)
     stream = torch.cuda.ExternalStream(ctx.stream())
     launches0 = None
@@ -404,12 +449,11 @@ def run_gemm_ours(args, w, name):
     launches = ctx.launch_count() - launches0
     step_ms = e0.elapsed_time(e1) / args.steps
     g_ms = sum(gemm_ms) / len(gemm_ms)
-    # spot check: 16 output columns equal their exact dot products
-    cols = np.random.default_rng(7).choice(M, 16, replace=False)
-    Y = y.reshape(N, M)
-    X = x.reshape(N, K).astype(np.int64)
-    if not (Y[:, cols] == X @ wt.reshape(M, K)[cols].astype(np.int64).T).all():
-        raise SystemExit("gemm4096: the result differs from the exact product")
+    # the whole int64 result against the CPU oracle's committed golden hash (tests/golden/bench_golden.json)
+    import hashlib
+
+    y_sha = hashlib.sha256(np.ascontiguousarray(y, dtype="<i8").tobytes()).hexdigest()
+    parity = golden_parity(name, {"data_sha256": y_sha, "repro_sha256": y_sha}, w)
     ops = 2.0 * M * N * K
     _, bf16, peak_kind = measured_peaks()
     int8_peak = 2.0 * bf16
@@ -427,6 +471,7 @@ def run_gemm_ours(args, w, name):
         "warmup": args.warmup, "ms_per_step": g_ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int64", "data": "synthetic", "config": gemm_config(w, name),
         "activation_planes": pl, "clocks": clk.summary(), "gpu_launches": launches,
+        "parity": parity, "output": {"y_int64_sha256": y_sha},
         "e2e": {"value": ops / (step_ms * 1e-3) / 1e12, "unit": "TOPS", "ms_per_step": step_ms,
                 "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 8},
         "roofline": {"bound": "tensor", "achieved": int8_ops / (g_ms * 1e-3) / 1e12, "peak": int8_peak,
@@ -446,6 +491,13 @@ def run_gemm_ours(args, w, name):
                                "kind": "port", "sample": f"first {rows} of {N} activation rows, one call (C++ "
                                                          f"restatement of the reference's CPU linear, all cores)"}
     print(json.dumps(res), flush=True)
+    if parity == "MISMATCH":
+        raise SystemExit(f"{name}: the output differs from the CPU oracle's golden hash")
+
+
+def linear_bench_config(name):
+    return {"workload": name, "shapes": "cuda_bench.rs:59-66", "codes": "test LCG, full range +-WLEVELS",
+            "l2": "the LM head's 408 MB of planes exceed L2; the smaller shapes run from L2 (as in the reference)"}
 
 
 def run_linear_bench_ours(args, w, name):
@@ -469,7 +521,7 @@ def run_linear_bench_ours(args, w, name):
     lm = None
     with ClockSampler(smi_index(local)) as clk:
         for i, (m, n, k, label) in enumerate(linear_bench_shapes()):
-            x, wt = linear_bench_codes(tb, m, n, k)
+            x, wt = linear_bench_codes(tb.lcg_uniform, m, n, k)
             for _ in range(args.warmup):
                 y = ctx.linear(x, wt, m, n, k, weight_id=1000 + i)
             cols = np.arange(n) if n <= 2048 else np.random.default_rng(i).choice(n, 256, replace=False)
@@ -505,8 +557,7 @@ def run_linear_bench_ours(args, w, name):
         "metric": LINEAR_METRIC, "value": tot_mac / tot_gemm_us, "unit": "MMAC/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": tot_gemm_us * 1e-3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
-        "config": {"workload": name, "shapes": "cuda_bench.rs:59-66", "codes": "test LCG, full range +-WLEVELS",
-                   "l2": "the LM head's 408 MB of planes exceed L2; the smaller shapes run from L2 (as in the reference)"},
+        "config": linear_bench_config(name),
         "shapes": rows_out, "clocks": clk.summary(), "gpu_launches": launches,
         "e2e": {"value": tot_mac / tot_us, "unit": "MMAC/s", "ms_per_step": tot_us * 1e-3,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -521,7 +572,7 @@ def run_linear_bench_ours(args, w, name):
         O.lib().ko_set_max_threads(0)
         mac, sec = 0, 0.0
         for (m, n, k, label) in linear_bench_shapes():
-            x, wt = linear_bench_codes(tb, m, n, k)
+            x, wt = linear_bench_codes(tb.lcg_uniform, m, n, k)
             t0 = time.perf_counter()
             O.linear(x, wt, m, n, k)
             sec += time.perf_counter() - t0
@@ -535,14 +586,13 @@ def run_linear_bench_reference(args, w, name):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import tritify_b200 as tb
     from oracle import oracle as O
 
     O.build()
     O.lib().ko_set_max_threads(0)
     shapes, mac, sec = [], 0, 0.0
     for (m, n, k, label) in linear_bench_shapes():
-        x, wt = linear_bench_codes(tb, m, n, k)
+        x, wt = linear_bench_codes(O.lcg_uniform, m, n, k)
         O.linear(x, wt, m, n, k)
         t0 = time.perf_counter()
         for _ in range(args.steps):
@@ -556,8 +606,7 @@ def run_linear_bench_reference(args, w, name):
         "impl": "reference", "metric": LINEAR_METRIC, "value": v, "unit": "MMAC/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int64", "data": "synthetic",
-        "config": {"workload": name, "shapes": "cuda_bench.rs:59-66", "codes": "test LCG, full range +-WLEVELS"},
-        "shapes": shapes,
+        "config": linear_bench_config(name), "shapes": shapes,
         "cpu_baseline": {"value": v, "unit": "MMAC/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": "every shape, `steps` calls each (C++ restatement of the reference's Portable "
                                    "linear)"},
@@ -644,6 +693,8 @@ def run_ours(args, w, name):
                 "repro_sha256": hashlib.sha256(np.int64(ys_ref.mant).astype("<i8").tobytes()
                                                + np.int32(ys_ref.shift).astype("<i4").tobytes() + y_bytes).hexdigest(),
                 "scale": [int(ys_ref.mant), int(ys_ref.shift)]}
+
+    parity = golden_parity(name, out_hash, w)
 
     # per-expert load of this routing (rows each expert receives), summed over the ranks
     ex, _, _ = dev.route(x.data, T, x.scale)
@@ -750,10 +801,10 @@ def run_ours(args, w, name):
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
-        "config": {"workload": name, **{k: w[k] for k in ("d", "E", "f", "k", "T", "norm", "sigmoid", "shared")},
-                   "router_bias": f"zipf({w['zipf']})" if w.get("zipf") else None,
-                   "parallelism": f"ep{world}", "ep_transport": transport, "cuda_graphs": graphs, "tokens_per_rank": T, "l2": "working set (weight planes) larger than L2, no flush",
-                   "bit_exact_vs_host_api": ok_exact, "output": out_hash},
+        "config": workload_config(w, name), "parallelism": f"ep{world}",
+        "parity": parity, "output": out_hash,
+        "run": {"ep_transport": transport, "cuda_graphs": graphs, "tokens_per_rank": T,
+                "graphed_forward_equals_host_api": ok_exact},
         "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4 + 16 * world,
                 "d2h_bytes_per_step": T_all * d * 4 + 16 * world},
         "gpu_launches": launches,
@@ -783,6 +834,8 @@ def run_ours(args, w, name):
                                "sample": f"first {rows} of {T_all} tokens, one forward (C++ restatement of the "
                                          f"reference CPU path, its own thread policy over all cores)"}
     print(json.dumps(res), flush=True)
+    if parity == "MISMATCH" or not ok_exact:
+        raise SystemExit(f"{name}: the output differs from the CPU oracle's golden hash or from the host-API forward")
 
 
 def main():

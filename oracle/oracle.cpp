@@ -15,6 +15,7 @@
 // Build: oracle/Makefile (g++ -O3 -ffp-contract=off: the reference's f64 steps are never fused into FMAs).
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -327,10 +328,15 @@ static size_t resolve_threads(size_t nblocks) {
 
 static size_t isqrt_usize(size_t v) { return (size_t)isqrt_u128((u128)v); }
 
+// Set inside the workers of ko_moe_forward_par, which already spread tokens over the cores: their linears run on the
+// calling thread. The partition of a linear never changes its values (each output is one exact i64 dot product).
+static thread_local bool tl_serial = false;
+
 // backend.rs:74-94 — plan_threads.
 static const size_t WORK_PER_SPAWN = size_t(1) << 17;
 static const size_t SERIAL_BELOW = size_t(1) << 20;
 static size_t plan_threads(size_t elems, size_t work) {
+    if (tl_serial) return 1;
     if (work < SERIAL_BELOW) return 1;
     return std::max<size_t>(1, std::min(resolve_threads(elems), isqrt_usize(work / WORK_PER_SPAWN)));
 }
@@ -616,6 +622,9 @@ struct MoeMlp {
     CodeLut exp_code = exp_table();
     std::unique_ptr<SigmoidScore> sigmoid;
     std::unique_ptr<SwiGluMlp> shared;
+    // Extension (the reference refuses it, crates/03-models/kt-model-moe/src/lib.rs:152-154, :276-288): Qwen2-MoE's
+    // sigmoid-gated shared expert, shared_expert_gate [1, dim]. Off unless set.
+    std::unique_ptr<QuantLinear> shared_gate;
 
     size_t dim() const { return router.in_features; }
 
@@ -731,7 +740,36 @@ struct MoeMlp {
     IntTensor add_shared(IntTensor routed, const IntTensor& x) const {
         if (!shared) return routed;
         IntTensor y = shared->forward_int(x);
+        if (shared_gate) y = gate_shared(y, x);
         return add(routed, y);
+    }
+
+    // The gated shared expert (an extension defined by this build in the reference's own terms; parity with the
+    // reference is unpinned because the reference has no such path). The gate is a QuantLinear [1, dim] on the whole
+    // input (layers.rs:275-328: tensor-global xmax and ymax), its logit per token goes through the sigmoid CodeLut
+    // of the GLM router (router.rs:37-51, code_at(index(logit, scale)), codes in units of 2^-20), and each token's
+    // shared output row is multiplied by its code and requantised over the whole tensor, as SwiGLU forms and
+    // requantises h (layers.rs:618-638): v = code_t·y[t, j] (i64), gmax = max |v|, data = requant_dyn(v, L, gmax),
+    // scale = from_ratio(gmax, L)·y.scale·code_scale. The result is then added to the routed output with add.
+    IntTensor gate_shared(const IntTensor& y, const IntTensor& x) const {
+        const IntTensor logit = shared_gate->forward_int(x);
+        const size_t rows = logit.len();
+        const size_t d = rows ? y.len() / rows : 0;
+        static const CodeLut sig = sigmoid_table();
+        std::vector<int64_t> v(y.len(), 0);
+        int64_t gmax = 0;
+        for (size_t t = 0; t < rows; ++t) {
+            const int64_t c = sig.code_at(sig.index(logit.data[t], logit.scale));
+            for (size_t j = 0; j < d; ++j) {
+                v[t * d + j] = c * (int64_t)y.data[t * d + j];
+                gmax = std::max<int64_t>(gmax, std::llabs(v[t * d + j]));
+            }
+        }
+        if (gmax == 0) return zeros(y.len(), y.shape);
+        IntTensor o{std::vector<int32_t>(y.len()), y.shape,
+                    Scale::from_ratio((u128)gmax, (u128)ACT_LEVELS).mul(y.scale).mul(sig.code_scale)};
+        for (size_t i = 0; i < v.size(); ++i) o.data[i] = requant_dyn(v[i], ACT_LEVELS, gmax);
+        return o;
     }
 
     // layers.rs:1070-1073
@@ -992,7 +1030,19 @@ void* ko_moe_new(size_t dim, size_t n_experts, size_t hidden, size_t top_k, cons
 
 void ko_moe_free(void* p) { delete (MoeMlp*)p; }
 
-// Which = 0 router, 1 gate, 2 up, 3 down (expert e), 4/5/6 shared gate/up/down. Copies the codes, returns the scale.
+// The extension's shared-expert gate (Qwen2-MoE shared_expert_gate, [1, dim] f32), quantised by QuantLinear::
+// from_weights (layers.rs:225-244); a null `w` removes it. Only with a shared expert.
+void ko_moe_set_shared_gate(void* p, const float* w) {
+    MoeMlp* m = (MoeMlp*)p;
+    if (!w) {
+        m->shared_gate.reset();
+        return;
+    }
+    m->shared_gate.reset(new QuantLinear(QuantLinear::from_weights(w, 1, m->dim())));
+}
+
+// Which = 0 router, 1 gate, 2 up, 3 down (expert e), 4/5/6 shared gate/up/down, 7 the shared-expert gate [1, dim].
+// Copies the codes, returns the scale.
 ko_scale ko_moe_weights(void* p, int which, size_t e, int32_t* codes) {
     MoeMlp* m = (MoeMlp*)p;
     const QuantLinear* q = which == 0   ? &m->router
@@ -1001,7 +1051,8 @@ ko_scale ko_moe_weights(void* p, int which, size_t e, int32_t* codes) {
                            : which == 3 ? &m->experts[e].down
                            : which == 4 ? &m->shared->gate
                            : which == 5 ? &m->shared->up
-                                        : &m->shared->down;
+                           : which == 6 ? &m->shared->down
+                                        : m->shared_gate.get();
     if (codes) std::memcpy(codes, q->w_codes.data(), q->w_codes.size() * 4);
     return to_c(q->w_scale);
 }
@@ -1028,6 +1079,81 @@ void ko_moe_forward(void* p, const int32_t* x, size_t rows, ko_scale xs, int32_t
     IntTensor o = m->forward_int(t);
     std::memcpy(y, o.data.data(), o.data.size() * 4);
     *ys = to_c(o.scale);
+}
+
+// The same Module::forward_int with the per-token work (layers.rs:997-1000: route, experts, combine of one row,
+// forward_one_int) spread over `threads` host threads, each token on one thread, then the merge and the shared expert
+// exactly as forward_int does them. Every per-token output depends on that token's row alone, so the result is the
+// serial one bit for bit (checked against ko_moe_forward in the tests); it exists so that the golden outputs of the
+// full-size workloads take minutes rather than an hour.
+void ko_moe_forward_par(void* p, const int32_t* x, size_t rows, ko_scale xs, int32_t* y, ko_scale* ys,
+                        size_t threads) {
+    MoeMlp* m = (MoeMlp*)p;
+    size_t d = m->dim();
+    IntTensor t{std::vector<int32_t>(x, x + rows * d), rows == 1 ? std::vector<size_t>{d} : std::vector<size_t>{rows, d},
+                from_c(xs)};
+    IntTensor routed;
+    if (rows <= 1) {
+        routed = m->forward_one_int(t);
+    } else {
+        std::vector<IntTensor> outs(rows);
+        std::atomic<size_t> next{0};
+        auto work = [&]() {
+            tl_serial = true;
+            for (size_t r; (r = next.fetch_add(1)) < rows;) outs[r] = m->forward_one_int(MoeMlp::row_of(t, r, d));
+            tl_serial = false;
+        };
+        if (threads == 0) threads = std::max<unsigned>(1, std::thread::hardware_concurrency());
+        std::vector<std::thread> ts;
+        for (size_t i = 1; i < threads; ++i) ts.emplace_back(work);
+        work();
+        for (auto& th : ts) th.join();
+        routed = MoeMlp::merge_rows(outs, outs[0].len());
+    }
+    IntTensor o = m->add_shared(std::move(routed), t);
+    std::memcpy(y, o.data.data(), o.data.size() * 4);
+    *ys = to_c(o.scale);
+}
+
+// The build-defined synthetic generator (the reference has no normal RNG), restated here so that the checker's inputs
+// never come from the product library: element i of stream `seed` takes two uniforms from splitmix64 (Steele, Lea
+// and Flood, 2014: state seed + (j+1)·0x9E3779B97F4A7C15, then the xor-shift-multiply finaliser) at positions 2i and
+// 2i+1, u = (bits >> 11)·2^-53 with u1 moved into (0, 1], then the Box-Muller transform sqrt(-2 ln u1)·cos(2π u2) in
+// f64 (host libm), rounded to f32 and multiplied by sigma in f32.
+void ko_synth_normal(uint64_t seed, float sigma, uint64_t offset, size_t n, float* out) {
+    auto mix = [](uint64_t s, uint64_t j) {
+        uint64_t v = s + (j + 1) * 0x9E3779B97F4A7C15ULL;
+        v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        v = (v ^ (v >> 27)) * 0x94D049BB133111EBULL;
+        return v ^ (v >> 31);
+    };
+    const double inv53 = 1.0 / 9007199254740992.0;
+    auto run = [&](size_t lo, size_t hi) {
+        for (size_t j = lo; j < hi; ++j) {
+            const uint64_t i = offset + j;
+            const double u1 = 1.0 - (double)(mix(seed, 2 * i) >> 11) * inv53;
+            const double u2 = (double)(mix(seed, 2 * i + 1) >> 11) * inv53;
+            const double r = std::sqrt(-2.0 * std::log(u1));
+            out[j] = (float)(r * std::cos(6.283185307179586 * u2)) * sigma;
+        }
+    };
+    const size_t nt = n < (size_t(1) << 20) ? 1 : std::max<unsigned>(1, std::thread::hardware_concurrency());
+    std::vector<std::thread> ts;
+    const size_t chunk = (n + nt - 1) / nt;
+    for (size_t s = chunk; s < n; s += chunk) ts.emplace_back(run, s, std::min(n, s + chunk));
+    run(0, std::min(n, chunk));
+    for (auto& th : ts) th.join();
+}
+
+// The reference's test LCG (crates/02-runtime/kt-runtime/src/gate.rs:29-36; kt-core/src/tests.rs:15-24):
+// s ← s·6364136223846793005 + 1442695040888963407 (mod 2^64), value = (s >> 33) mod (hi − lo + 1) + lo.
+void ko_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, size_t n, int32_t* out) {
+    uint64_t s = seed;
+    const uint64_t range = (uint64_t)(hi - lo + 1);
+    for (size_t i = 0; i < n; ++i) {
+        s = s * 6364136223846793005ULL + 1442695040888963407ULL;
+        out[i] = (int32_t)((int64_t)((s >> 33) % range) + lo);
+    }
 }
 
 // The routed part only, for a subset of tokens (per-token outputs before the merge), for stage-level checks:

@@ -71,11 +71,15 @@ def lib():
             "ko_corpus_case": ([ctypes.c_int, p(sz), p(sz), p(sz), i32p, i32p], ctypes.c_int),
             "ko_moe_new": ([sz, sz, sz, sz, f32p, f32p, f32p, ctypes.c_int, f32p, sz, f32p], ctypes.c_void_p),
             "ko_moe_free": ([ctypes.c_void_p], None),
+            "ko_moe_set_shared_gate": ([ctypes.c_void_p, f32p], None),
             "ko_moe_weights": ([ctypes.c_void_p, ctypes.c_int, sz, i32p], KoScale),
             "ko_moe_router_bias": ([ctypes.c_void_p, i64p, p(KoScale)], ctypes.c_int),
             "ko_moe_sigmoid_bias": ([ctypes.c_void_p, i64p], ctypes.c_int),
             "ko_moe_forward": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_tokens": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
+            "ko_moe_forward_par": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale), sz], None),
+            "ko_synth_normal": ([ctypes.c_uint64, ctypes.c_float, ctypes.c_uint64, sz, f32p], None),
+            "ko_lcg_uniform": ([ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, sz, i32p], None),
             "ko_moe_forward_with_local_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_with_given_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale), i32p,
                                                    p(KoScale)], None),
@@ -211,6 +215,21 @@ def linear_small(x: np.ndarray, w: np.ndarray, rows: int, out: int, k: int, flus
     return y
 
 
+def synth_normal(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray:
+    """Elements [offset, offset + n) of the build-defined N(0, sigma) stream ``seed`` (splitmix64 + Box-Muller in f64,
+    rounded to f32), computed by the oracle itself."""
+    out = np.empty(n, dtype=np.float32)
+    lib().ko_synth_normal(seed, sigma, offset, n, _p(out, ctypes.c_float))
+    return out
+
+
+def lcg_uniform(seed: int, lo: int, hi: int, n: int) -> np.ndarray:
+    """Uniform integers in [lo, hi] from the reference's test LCG (gate.rs:29-36)."""
+    out = np.empty(n, dtype=np.int32)
+    lib().ko_lcg_uniform(seed, lo, hi, n, _p(out, ctypes.c_int32))
+    return out
+
+
 def corpus():
     """The reference's equality-gate corpus: a list of (label, rows, out, k, x, w)."""
     labels = ["k=1", "odd tail", "k=33", "k=1023", "k=4099 (long)", "threaded 8×512×2048", "extremes ±WLEVELS",
@@ -231,7 +250,7 @@ class MoeOracle:
     """The reference MoeMlp (layers.rs:661-1106) restated on the CPU, built from f32 weights."""
 
     def __init__(self, dim, n_experts, hidden, top_k, router_w, expert_w, *, router_bias=None, norm_topk=False,
-                 sigmoid_bias=None, shared_hidden=0, shared_w=None):
+                 sigmoid_bias=None, shared_hidden=0, shared_w=None, shared_gate_w=None):
         self.dim, self.n_experts, self.hidden, self.top_k = dim, n_experts, hidden, top_k
         self.shared_hidden = shared_hidden
         keep = []
@@ -245,6 +264,9 @@ class MoeOracle:
 
         self._h = lib().ko_moe_new(dim, n_experts, hidden, top_k, f(router_w), f(router_bias), f(expert_w),
                                    1 if norm_topk else 0, f(sigmoid_bias), shared_hidden, f(shared_w))
+        if shared_gate_w is not None:
+            # the extension: Qwen2-MoE's sigmoid-gated shared expert (shared_expert_gate [1, dim])
+            lib().ko_moe_set_shared_gate(self._h, f(shared_gate_w))
 
     def __del__(self):
         if getattr(self, "_h", None):
@@ -254,7 +276,7 @@ class MoeOracle:
     def weights(self, which: int, e: int = 0):
         shapes = {0: (self.n_experts, self.dim), 1: (self.hidden, self.dim), 2: (self.hidden, self.dim),
                   3: (self.dim, self.hidden), 4: (self.shared_hidden, self.dim), 5: (self.shared_hidden, self.dim),
-                  6: (self.dim, self.shared_hidden)}
+                  6: (self.dim, self.shared_hidden), 7: (1, self.dim)}
         codes = np.empty(shapes[which], dtype=np.int32)
         s = lib().ko_moe_weights(self._h, which, e, _p(codes, ctypes.c_int32))
         return codes, s.tup()
@@ -279,6 +301,15 @@ class MoeOracle:
         y = np.empty(rows * self.dim, dtype=np.int32)
         s = KoScale()
         lib().ko_moe_forward(self._h, _p(x, ctypes.c_int32), rows, S(xs), _p(y, ctypes.c_int32), ctypes.byref(s))
+        return y.reshape(rows, self.dim), s.tup()
+
+    def forward_par(self, x, xs, threads: int = 0):
+        """forward() with the tokens spread over host threads (0 = every core); the same bits as forward()."""
+        x, rows = self._x(x)
+        y = np.empty(rows * self.dim, dtype=np.int32)
+        s = KoScale()
+        lib().ko_moe_forward_par(self._h, _p(x, ctypes.c_int32), rows, S(xs), _p(y, ctypes.c_int32), ctypes.byref(s),
+                                 threads)
         return y.reshape(rows, self.dim), s.tup()
 
     def forward_tokens(self, x, xs):

@@ -3,7 +3,7 @@
 Inputs come from the build-defined generator (tritify_b200.synth_normal: splitmix64 + Box-Muller, f32) because the
 reference has no normal RNG. Weights of one case form one stream (seed ``wseed``, sigma 0.02) consumed tensor by
 tensor in the order router [E, d], then for each expert gate [f, d], up [f, d], down [d, f], then the shared expert's
-gate, up, down. Hidden states are N(0, 1) from seed ``xseed``. Router bias (QuantLinear::with_bias) and the sigmoid
+gate, up, down, then (gated cases) the shared-expert gate [d]. Hidden states are N(0, 1) from seed ``xseed``. Router bias (QuantLinear::with_bias) and the sigmoid
 selection bias come from seeds ``wseed + 1`` and ``wseed + 2``.
 """
 
@@ -29,6 +29,7 @@ class Case:
     sigmoid: bool = False
     shared: int = 0
     router_bias: bool = False
+    gated: bool = False  # the shared expert behind a sigmoid gate (extension; Qwen2-MoE shared_expert_gate)
     wseed: int = 1
     xseed: int = 0
     bias_sigma: float = 0.05
@@ -46,6 +47,14 @@ CASES = {
         Case("tiny_sigmoid_raw_shared_one_row", d=64, E=16, f=48, k=4, T=1, norm=False, sigmoid=True, shared=40,
              wseed=21, xseed=22),
         Case("small_shared_softmax", d=256, E=32, f=192, k=6, T=48, norm=True, shared=384, wseed=23, xseed=24),
+        # f % 4 != 0: the SwiGLU element pass takes its block-per-row form
+        Case("tiny_odd_hidden", d=64, E=6, f=50, k=2, T=11, wseed=25, xseed=26),
+        # the gated shared expert (extension), with a softmax and a sigmoid router, one row and several
+        Case("tiny_gated_shared", d=64, E=8, f=48, k=2, T=9, norm=True, shared=64, gated=True, wseed=27, xseed=28),
+        Case("tiny_gated_shared_one_row", d=64, E=16, f=48, k=4, T=1, norm=True, sigmoid=True, shared=40, gated=True,
+             wseed=29, xseed=30),
+        Case("small_gated_shared", d=256, E=32, f=192, k=4, T=48, norm=True, shared=512, gated=True, wseed=31,
+             xseed=32),
         # The CPU-parity layer: d=2048, E=64, f=1408, k=8, T=512, softmax, norm_topk=false,
         # hidden N(0,1) seed 0, weights N(0,0.02) seed 1.
         Case("config1", d=2048, E=64, f=1408, k=8, T=512, norm=False, wseed=1, xseed=0),
@@ -55,11 +64,12 @@ CASES = {
 
 
 def weight_count(c: Case) -> int:
-    return c.E * c.d + c.E * 3 * c.f * c.d + 3 * c.shared * c.d
+    return c.E * c.d + c.E * 3 * c.f * c.d + 3 * c.shared * c.d + (c.d if c.gated else 0)
 
 
 def make_weights(c: Case):
-    """(router_w [E,d], expert_w flat [E·3·f·d], router_bias or None, sigmoid_bias or None, shared_w or None)."""
+    """(router_w [E,d], expert_w flat [E·3·f·d], router_bias or None, sigmoid_bias or None, shared_w or None,
+    shared_gate_w [d] or None)."""
     off = 0
 
     def take(n):
@@ -71,9 +81,10 @@ def make_weights(c: Case):
     router = take(c.E * c.d).reshape(c.E, c.d)
     experts = take(c.E * 3 * c.f * c.d)
     shared = take(3 * c.shared * c.d) if c.shared else None
+    gate = take(c.d) if c.shared and c.gated else None
     rbias = tb.synth_normal(c.wseed + 1, 1.0, c.E) if c.router_bias else None
     sbias = tb.synth_normal(c.wseed + 2, c.bias_sigma, c.E) if c.sigmoid else None
-    return router, experts, rbias, sbias, shared
+    return router, experts, rbias, sbias, shared, gate
 
 
 def make_x(c: Case) -> np.ndarray:
@@ -98,7 +109,7 @@ def out_hashes(y: np.ndarray, scale) -> dict:
 
 def build_layer(c: Case, ctx=None) -> "tb.MoeMlp":
     """The reference-shaped layer, built through the product's own host mirror (QuantLinear::from_weights etc.)."""
-    router_w, expert_w, rbias, sbias, shared_w = make_weights(c)
+    router_w, expert_w, rbias, sbias, shared_w, gate_w = make_weights(c)
     router = tb.QuantLinear.from_weights("router", router_w, c.E, c.d).with_bias(rbias)
     per = 3 * c.f * c.d
     experts = []
@@ -119,10 +130,12 @@ def build_layer(c: Case, ctx=None) -> "tb.MoeMlp":
             tb.QuantLinear.from_weights("gate", shared_w[:sd], c.shared, c.d),
             tb.QuantLinear.from_weights("up", shared_w[sd:2 * sd], c.shared, c.d),
             tb.QuantLinear.from_weights("down", shared_w[2 * sd:], c.d, c.shared)))
+        if c.gated:
+            m = m.with_shared_expert_gate(tb.QuantLinear.from_weights("shared_expert_gate", gate_w, 1, c.d))
     return m
 
 
 def build_oracle(c: Case, O):
-    router_w, expert_w, rbias, sbias, shared_w = make_weights(c)
+    router_w, expert_w, rbias, sbias, shared_w, gate_w = make_weights(c)
     return O.MoeOracle(c.d, c.E, c.f, c.k, router_w, expert_w, router_bias=rbias, norm_topk=c.norm,
-                       sigmoid_bias=sbias, shared_hidden=c.shared, shared_w=shared_w)
+                       sigmoid_bias=sbias, shared_hidden=c.shared, shared_w=shared_w, shared_gate_w=gate_w)

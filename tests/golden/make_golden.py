@@ -44,13 +44,14 @@ REFERENCE_LITERALS = {
 }
 
 SMALL = ["tiny_softmax", "tiny_softmax_norm_one_row", "tiny_softmax_37rows", "tiny_router_bias",
-         "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row", "small_shared_softmax"]
+         "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row", "small_shared_softmax", "tiny_odd_hidden",
+         "tiny_gated_shared", "tiny_gated_shared_one_row", "small_gated_shared"]
 LARGE = ["config1", "config1_norm_topk"]
 
 
 def case_entry(c):
     t0 = time.time()
-    router_w, expert_w, rbias, sbias, shared_w = cases.make_weights(c)
+    router_w, expert_w, rbias, sbias, shared_w, gate_w = cases.make_weights(c)
     x = cases.make_x(c)
     xi, xs = O.from_reals_f32(x)
     m = cases.build_oracle(c, O)
@@ -59,7 +60,8 @@ def case_entry(c):
     entry = {
         "params": {k: getattr(c, k) for k in c.__dataclass_fields__},
         "weights_f32_sha256": cases.sha(np.concatenate([router_w.reshape(-1), expert_w] +
-                                                       ([shared_w] if shared_w is not None else []))),
+                                                       ([shared_w] if shared_w is not None else []) +
+                                                       ([gate_w] if gate_w is not None else []))),
         "x_f32_sha256": cases.sha(x),
         "x_int": {"data_sha256": cases.sha(xi.astype("<i4")), "scale": list(xs)},
         "output": cases.out_hashes(y, ys),

@@ -32,7 +32,7 @@ def test_gemm_codes_are_one_lcg_stream():
         s = (s * 6364136223846793005 + 1442695040888963407) % (1 << 64)
     assert bench.lcg_state_after(2, 777) == s
     w = dict(M=32, N=16, K=64, seed=2)
-    x, wt = bench.gemm_codes(w)
+    x, wt = bench.gemm_codes(w, tb.lcg_uniform)
     assert (wt == tb.lcg_uniform(2, -2048, 2047, 32 * 64)).all()
     assert x.min() >= -127 and x.max() <= 127 and wt.min() >= -2048 and wt.max() <= 2047
     # the activations continue the same stream: drawing the weights' count first lands on the same state
@@ -43,6 +43,6 @@ def test_linear_bench_shapes_are_the_references():
     shapes = [(m, n, k) for m, n, k, _ in bench.linear_bench_shapes()]
     assert shapes[:3] == [(8, 2048, 2048), (1, 4864, 896), (1, 151_936, 896)]
     assert shapes[3:] == [(r, 2048, 2048) for r in (1, 2, 4, 8, 16, 32, 64)]
-    x, w = bench.linear_bench_codes(tb, 1, 4864, 896)
+    x, w = bench.linear_bench_codes(tb.lcg_uniform, 1, 4864, 896)
     assert (x == tb.lcg_uniform(2, -tb.WLEVELS, tb.WLEVELS, 896)).all()
     assert (w[:5] == tb.lcg_uniform(4866, -tb.WLEVELS, tb.WLEVELS, 5)).all()

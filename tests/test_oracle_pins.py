@@ -166,3 +166,60 @@ def test_rmsnorm_tracks_float_like_the_reference(oracle):
     ref = x64 / np.sqrt((x64 ** 2).mean(axis=1, keepdims=True) + 1e-6) * w.astype(np.float64)
     got = y.astype(np.float64).reshape(rows, dim) * ys[0] * 2.0 ** (-ys[1])
     assert np.abs(got - ref).max() <= np.abs(ref).max() * 1e-2
+
+
+def _gate_case(oracle, gate_w, sigmoid=False):
+    """A small layer with a shared expert, optionally behind the sigmoid gate (the extension). Every token's first
+    feature is +8, so a gate that weighs only that feature gives every token a logit of the same sign."""
+    d, E, f, k, fs, T = 64, 8, 48, 2, 40, 6
+    w = oracle.synth_normal(41, 0.02, E * d + E * 3 * f * d + 3 * fs * d)
+    router, experts, shared = w[:E * d], w[E * d:E * d + E * 3 * f * d], w[E * d + E * 3 * f * d:]
+    sbias = oracle.synth_normal(43, 0.05, E) if sigmoid else None
+    m = oracle.MoeOracle(d, E, f, k, router, experts, norm_topk=True, sigmoid_bias=sbias, shared_hidden=fs,
+                         shared_w=shared, shared_gate_w=gate_w)
+    x = oracle.synth_normal(42, 1.0, T * d).reshape(T, d)
+    x[:, 0] = 8.0
+    xi, xs = oracle.from_reals_f32(x)
+    return m.forward(xi, xs)
+
+
+@pytest.mark.parametrize("sigmoid", [False, True])
+def test_a_saturated_shared_gate_is_the_ungated_layer(oracle, sigmoid):
+    """The gated shared expert (extension; the reference refuses it, kt-model-moe/src/lib.rs:152-154) is pinned by an
+    exact property of its definition: a gate whose logit is beyond +16 for every token reads the sigmoid table's last
+    entry, round(sigmoid(16)·2^20) = 2^20, so the gated tensor is requant_dyn(2^20·y, L, 2^20·L) = y at scale
+    ratio(2^48)·y.scale·2^-20 = y.scale — the ungated layer's bits exactly."""
+    gw = np.zeros(64, np.float32)
+    gw[0] = 50.0  # logit ~ 8·50 = 400 for every token
+    gated = _gate_case(oracle, gw, sigmoid=sigmoid)
+    plain = _gate_case(oracle, None, sigmoid=sigmoid)
+    assert (gated[0] == plain[0]).all() and gated[1] == plain[1]
+    # a gate inside the table's range changes the result, deterministically
+    g = oracle.synth_normal(44, 0.02, 64)
+    a, b = _gate_case(oracle, g, sigmoid=sigmoid), _gate_case(oracle, g, sigmoid=sigmoid)
+    assert (a[0] == b[0]).all() and a[1] == b[1]
+    assert not ((a[0] == plain[0]).all() and a[1] == plain[1])
+
+
+def test_oracle_generator_and_lcg_equal_the_products(oracle):
+    """The oracle's copy of the build-defined normal generator and of the reference's test LCG give the product
+    library's bytes, so the reference arm of the benchmark and the goldens need nothing of the product."""
+    import tritify_b200 as tb
+
+    for seed, sigma, n, off in [(1, 0.02, 1 << 21, 0), (0, 1.0, 1000, 17), (3, 1.0, 3 << 20, 123456789)]:
+        a = oracle.synth_normal(seed, sigma, n, offset=off)
+        b = tb.synth_normal(seed, sigma, n, offset=off)
+        assert (a.view(np.uint32) == b.view(np.uint32)).all()
+    assert (oracle.lcg_uniform(2, -2048, 2047, 100000) == tb.lcg_uniform(2, -2048, 2047, 100000)).all()
+
+
+def test_token_parallel_forward_equals_the_serial_forward(oracle):
+    """MoeOracle.forward_par (tokens spread over threads, used for the full-size goldens) gives forward's bits."""
+    import cases
+
+    for name in ["small_shared_softmax", "tiny_sigmoid_shared", "tiny_gated_shared", "tiny_softmax_norm_one_row"]:
+        c = cases.CASES[name]
+        xi, xs = oracle.from_reals_f32(cases.make_x(c))
+        m = cases.build_oracle(c, oracle)
+        a, b = m.forward(xi, xs), m.forward_par(xi, xs, 3)
+        assert (a[0] == b[0]).all() and a[1] == b[1], name
