@@ -131,6 +131,13 @@ int ktmoe_layer_set_expert(ktmoe_layer* layer, int32_t e, const int32_t* gate, k
 /* The shared expert (layers.rs:741-745): gate/up [shared_d_ff][d_model], down [d_model][shared_d_ff]. */
 int ktmoe_layer_set_shared(ktmoe_layer* layer, const int32_t* gate, ktmoe_scale gate_scale, const int32_t* up,
                            ktmoe_scale up_scale, const int32_t* down, ktmoe_scale down_scale);
+/* Extension, off by default: Qwen2-MoE's sigmoid-gated shared expert. The reference refuses this configuration
+ * (crates/03-models/kt-model-moe/src/lib.rs:152-154, :276-288); this library defines it in the reference's terms:
+ * `codes` [d_model] are shared_expert_gate's QuantLinear::from_weights codes (a [1][d_model] linear, layers.rs:225-244)
+ * at `w_scale`; per token the gate's integer logit (QuantLinear::forward_int over the whole input) picks a code of
+ * the sigmoid CodeLut (router.rs:37-51), the shared output row is multiplied by it and the tensor requantised
+ * (requant_dyn at the tensor's max) before add. NULL codes turn the gate off. Needs a shared expert. */
+int ktmoe_layer_set_shared_gate(ktmoe_layer* layer, const int32_t* codes, ktmoe_scale w_scale);
 /* Module::forward_int: x [rows][d_model] at x_scale -> y [rows][d_model] at *y_scale. Host buffers; synchronous. */
 int ktmoe_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
                   ktmoe_scale* y_scale);

@@ -18,7 +18,8 @@ GOLDEN = json.load(open(os.path.join(HERE, "golden", "golden.json")))
 import cases  # noqa: E402
 
 SMALL = ["tiny_softmax", "tiny_softmax_norm_one_row", "tiny_softmax_37rows", "tiny_router_bias",
-         "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row", "small_shared_softmax"]
+         "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row", "small_shared_softmax", "tiny_odd_hidden",
+         "tiny_gated_shared", "tiny_gated_shared_one_row", "small_gated_shared"]
 
 
 def _diff(a, b):

@@ -346,6 +346,17 @@ class DeviceLayer:
                                                     _p(u, ctypes.c_int32), up[1]._c(), _p(d, ctypes.c_int32),
                                                     down[1]._c()))
 
+    def set_shared_gate(self, gate: Optional[tuple]) -> None:
+        """Extension: gate the shared expert with a sigmoid of a [1, d_model] linear's integer logit (Qwen2-MoE's
+        shared_expert_gate); ``gate = (codes [d_model], Scale)`` or None to turn it off."""
+        if gate is None:
+            self.ctx.check(lib().ktmoe_layer_set_shared_gate(self._h, None, KtmoeScale(0, 0)))
+            return
+        c = np.ascontiguousarray(gate[0], dtype=np.int32).reshape(-1)
+        if c.size != self.d_model:
+            raise ValueError("the shared-expert gate has d_model codes")
+        self.ctx.check(lib().ktmoe_layer_set_shared_gate(self._h, _p(c, ctypes.c_int32), gate[1]._c()))
+
     def set_norm(self, w_codes: np.ndarray, w_scale: Scale, eps_scale: Scale) -> None:
         """The block's FFN input RmsNorm (RmsNorm::new codes and scales) for block_forward."""
         w = np.ascontiguousarray(w_codes, dtype=np.int32)
@@ -514,6 +525,7 @@ class MoeMlp:
         self.norm_topk_prob = False
         self.sigmoid_bias_codes: Optional[np.ndarray] = None
         self.shared: Optional[SwiGluMlp] = None
+        self.shared_gate: Optional[QuantLinear] = None
         self._ctx = ctx
         self._dev: Optional[DeviceLayer] = None
 
@@ -541,6 +553,18 @@ class MoeMlp:
     def dim(self) -> int:
         return self.router.in_features
 
+    def with_shared_expert_gate(self, gate: "QuantLinear") -> "MoeMlp":
+        """Extension (the reference refuses it, kt-model-moe/src/lib.rs:152-154): Qwen2-MoE's sigmoid-gated shared
+        expert. ``gate`` is shared_expert_gate as a QuantLinear [1, dim]; each token's shared output is scaled by the
+        sigmoid code of the gate's integer logit and requantised before the add."""
+        if self.shared is None:
+            raise ValueError("with_shared_expert_gate needs a shared expert")
+        if gate.out_features != 1 or gate.in_features != self.dim:
+            raise ValueError("the shared-expert gate is a [1, dim] linear")
+        self.shared_gate = gate
+        self._dev = None
+        return self
+
     def n_experts(self) -> int:
         return self.router.out_features
 
@@ -565,6 +589,8 @@ class MoeMlp:
                 s = self.shared
                 dev.set_shared((s.gate.w_codes, s.gate.w_scale), (s.up.w_codes, s.up.w_scale),
                                (s.down.w_codes, s.down.w_scale))
+                if self.shared_gate is not None:
+                    dev.set_shared_gate((self.shared_gate.w_codes, self.shared_gate.w_scale))
             self._dev = dev
         return self._dev
 

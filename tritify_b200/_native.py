@@ -72,6 +72,7 @@ SIGNATURES = {
     "ktmoe_layer_set_sigmoid_bias": ([_vp, _i64p], ctypes.c_int),
     "ktmoe_layer_set_expert": ([_vp, _i32, _i32p, KtmoeScale, _i32p, KtmoeScale, _i32p, KtmoeScale], ctypes.c_int),
     "ktmoe_layer_set_shared": ([_vp, _i32p, KtmoeScale, _i32p, KtmoeScale, _i32p, KtmoeScale], ctypes.c_int),
+    "ktmoe_layer_set_shared_gate": ([_vp, _i32p, KtmoeScale], ctypes.c_int),
     "ktmoe_forward": ([_vp, _i32p, _i64, KtmoeScale, _i32p, _P(KtmoeScale)], ctypes.c_int),
     "ktmoe_forward_dev": ([_vp, _vp, _i64, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ktmoe_sync": ([_vp, _vp], ctypes.c_int),

@@ -30,6 +30,7 @@ constexpr int MAXW = 8;
 enum Point : int {
     P_COUNTS = 0, P_DISPATCH, P_RETURN, P_REC, P_MERGE, P_SX, P_SYG, P_SHMAX, P_SYD, P_ADD,
     P_TOK, P_NREC, P_NMAX, P_RADD,  // the block around the layer: row counts, the norm's record and max, the residual add
+    P_GYMAX, P_GATED,               // the gated shared expert: the gate logits' max, the gated output's max
     NPOINT
 };
 enum : int { ERR_WAIT = 21, ERR_BOUNDS = 22 };

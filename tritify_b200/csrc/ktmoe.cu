@@ -531,6 +531,10 @@ struct ktmoe_layer {
     Scale router_ws{0, 0}, router_bscale{0, 0};
     bool has_rbias = false;
     DevBuf b_rbias, b_sigbias;
+    // extension: the sigmoid-gated shared expert (ktmoe_layer_set_shared_gate); the gate's codes zero-padded to d_pad
+    bool sgate_set = false;
+    DevBuf b_sgate, sg_acc, sg_code, y_gated;
+    Scale sgate_ws{0, 0};
     // device scales: [0,E) gate, [E,2E) up, [2E,3E) down, then shared gate, up, down
     DevBuf b_wsc;
     std::vector<Scale> h_wsc;
@@ -584,9 +588,12 @@ enum ScalarSlot {
     SL_ADD = 5,      // Scale[4]: add scratch
     SL_SCD = 9,      // Scale: shared down c
     SL_YROUTED = 10, // Scale: routed scale (with shared)
-    SL_NSCALES = 12
+    SL_GATED = 12,   // Scale: the gated shared output's scale
+    SL_ADD2 = 13,    // Scale[3]: add(routed, gated) plan {common, fa, fb}
+    SL_NSCALES = 16
 };
-enum U64Slot { U_MERGE_GMAX = 0, U_GXMAX, U_SYG, U_SYU, U_SHMAX, U_SYD, U_ADDGMAX, U_NTILES_PAD, U_N };
+enum U64Slot { U_MERGE_GMAX = 0, U_GXMAX, U_SYG, U_SYU, U_SHMAX, U_SYD, U_ADDGMAX, U_GYMAX, U_GATEDMAX, U_NTILES_PAD,
+               U_N };
 // the two n-tile counts live in the two 32-bit halves of U_NTILES_PAD
 
 Scale* scal_scale(ktmoe_layer* L, int slot) { return L->scal.as<Scale>() + slot; }
@@ -668,6 +675,11 @@ int ensure_scratch(ktmoe_layer* L, int64_t T) {
         CK(L->acc_sgu.ensure(T * 2 * fs * 8));
         CK(L->hs_planes.ensure(3 * T_pad * L->fs_pad));
         CK(L->acc_sd.ensure(T * d * 8));
+        if (L->sgate_set) {
+            CK(L->sg_acc.ensure(T * 8));
+            CK(L->sg_code.ensure(T * 8));
+            CK(L->y_gated.ensure(T * d * 4));
+        }
     }
     L->cap = T;
     return KTMOE_OK;
@@ -890,7 +902,28 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     sa.phase = 0;
     mk::swiglu_plan_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
     CKL(ctx);
-    {
+    // a cluster per row with h in registers (mk::swiglu_cluster_kernel); KTMOE_SWIGLU_CLUSTER=0 keeps the block-per-row
+    // kernel below, which also takes rows the cluster form cannot (f % 4 != 0, or wider than 8 CTAs hold)
+    const char* ce = getenv("KTMOE_SWIGLU_CLUSTER");
+    const bool use_cluster = !(ce && ce[0] == '0');
+    constexpr int SG = 4, SNT = 128;  // groups of four elements per thread, threads per CTA
+    int csize = 1;
+    while (csize < 8 && (int64_t)csize * SG * SNT * 4 < L->f_pad) csize *= 2;
+    if (use_cluster && f % 4 == 0 && (int64_t)csize * SG * SNT * 4 >= L->f_pad) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(R * csize));
+        cfg.blockDim = dim3(SNT);
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)csize;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<SG, SNT>, sa));
+        CKL(ctx);
+    } else {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
         const size_t sm = h_smem ? (size_t)L->swiglu_smem : 0;
         static const int unroll = [] {
@@ -1296,6 +1329,41 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         if (int r = run_gemm(ctx, st, s)) return r;
     }
     if (int r = allreduce_max(L, scal_u64(L, U_SYD), 1, st, ep::P_SYD)) return r;
+    if (!L->sgate_set) return KTMOE_OK;
+
+    // the sigmoid gate of the shared expert (extension): gate logits from the same input planes, their sigmoid
+    // codes, then the shared output scaled per token and requantised over the whole tensor (all ranks)
+    if (T > 0) {
+        mk::gate_logit_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(L->xs_planes.as<int8_t>(), (int)T,
+                                                                       (int)L->d_pad, T_pad, L->b_sgate.as<int32_t>(),
+                                                                       L->sg_acc.as<int64_t>(), scal_u64(L, U_GYMAX));
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_GYMAX), 1, st, ep::P_GYMAX)) return r;
+    mk::GateArgs ga;
+    ga.s_acc = L->acc_sd.as<int64_t>();
+    ga.s_ymax = scal_u64(L, U_SYD);
+    ga.s_cd = scal_scale(L, SL_SCD);
+    ga.code = L->sg_code.as<int64_t>();
+    ga.T = (int)T;
+    ga.d = (int)d;
+    ga.gmax = scal_u64(L, U_GATEDMAX);
+    ga.code_scale = S(L->tabs[2].code_scale);
+    ga.y = L->y_gated.as<int32_t>();
+    ga.y_scale = scal_scale(L, SL_GATED);
+    if (T > 0) {
+        mk::gate_code_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(
+            L->sg_acc.as<int64_t>(), (int)T, scal_u64(L, U_GYMAX), scal_scale(L, SL_GSQX), L->sgate_ws, lut(L, 2),
+            L->sg_code.as<int64_t>());
+        CKL(ctx);
+        mk::gated_max_kernel<<<(unsigned)T, 256, 0, st>>>(ga);
+        CKL(ctx);
+    }
+    if (int r = allreduce_max(L, scal_u64(L, U_GATEDMAX), 1, st, ep::P_GATED)) return r;
+    if (T > 0) {
+        mk::gated_final_kernel<<<(unsigned)T, 256, 0, st>>>(ga);
+        CKL(ctx);
+    }
     return KTMOE_OK;
 }
 
@@ -1460,6 +1528,26 @@ int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset
     }
     const int64_t n = T * d;
     const unsigned red_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
+    if (L->sgate_set) {  // add(routed, gated shared output) of two int32 tensors
+        Scale* plan = scal_scale(L, SL_ADD2);
+        if (T > 0) {
+            mk::add2_prepare_kernel<<<1, 1, 0, st>>>(routed_scale, scal_scale(L, SL_GATED), plan);
+            CKL(ctx);
+            mk::add2_max_kernel<<<red_blocks, 256, 0, st>>>(routed, L->y_gated.as<int32_t>(), n, plan,
+                                                            scal_u64(L, U_ADDGMAX));
+            CKL(ctx);
+        }
+        if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st, ep::P_ADD)) return r;
+        if (T > 0) {
+            mk::add2_final_kernel<<<red_blocks, 256, 0, st>>>(routed, L->y_gated.as<int32_t>(), n, plan,
+                                                              scal_u64(L, U_ADDGMAX), y_dev);
+            CKL(ctx);
+            mk::gmax_scale_kernel<<<1, 1, 0, st>>>(plan, scal_u64(L, U_ADDGMAX), ys_dev);
+            CKL(ctx);
+        }
+        MARK(L, st);
+        return KTMOE_OK;
+    }
     // a rank without tokens still needs the shared down c for nothing: only ranks with rows produce output
     mk::AddArgs aa;
     aa.a = routed;
@@ -2374,6 +2462,30 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
     L->h_wsc[3 * L->E_local + 2] = S(down_scale);
     if (int r = push_scales(L)) return r;
     L->shared_set = true;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_set_shared_gate(ktmoe_layer* L, const int32_t* codes, ktmoe_scale w_scale) {
+    if (!L) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (L->fs <= 0) return fail(ctx, KTMOE_ERR_ARG, "the layer has no shared expert to gate");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);
+    if (int r = set_device(ctx)) return r;
+    if (!codes) {
+        L->sgate_set = false;
+        return KTMOE_OK;
+    }
+    for (int64_t k = 0; k < L->d; ++k)
+        if (codes[k] > (int32_t)kt::WLEVELS || codes[k] < -(int32_t)kt::WLEVELS)
+            return fail(ctx, KTMOE_ERR_RANGE, "shared-expert gate codes beyond +-WLEVELS");
+    std::vector<int32_t> padded((size_t)L->d_pad, 0);
+    std::copy(codes, codes + L->d, padded.begin());
+    CK(L->b_sgate.ensure(L->d_pad * 4));
+    CK(cudaMemcpy(L->b_sgate.p, padded.data(), L->d_pad * 4, cudaMemcpyHostToDevice));
+    L->sgate_ws = S(w_scale);
+    L->sgate_set = true;
+    L->cap = 0;  // the next forward allocates the gate's scratch
     return KTMOE_OK;
 }
 

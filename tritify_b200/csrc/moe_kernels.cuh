@@ -602,6 +602,135 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
     }
 }
 
+// ── Phase 0 on a thread-block cluster: one routed row per cluster, h in registers ──
+// The C CTAs of a cluster (C = %cluster_nctarank, at most 8) split the row's f_pad / 4 groups of four elements;
+// thread t of CTA c owns groups gt, gt + C·NT, ... (gt = c·NT + t), at most G of them. Each thread loads all of its
+// gate and up accumulators first (16-byte loads, coalesced across the warp), turns them into h = silu_code(g)·u in
+// registers (the LUT reads of a thread issued together), and reduces max |h|: over the CTA with warp shuffles, then
+// over the cluster by writing each CTA's partial into slot c of every CTA's shared memory (distributed shared
+// memory) between two cluster barriers. The down linear's digit planes are then written from the registers. Per
+// element 16 bytes are read and 3 written, and h never leaves the SM, so a wide expert needs no row buffer: a row
+// of 14336 elements is spread over 7 CTAs of 128 threads. Requires f % 4 == 0 (so the accumulator rows are 16-byte
+// aligned) and f_pad <= 4·G·NT·8.
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_size() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store v into the shared-memory word `local` (this CTA's address) of CTA `rank` of the cluster.
+__device__ __forceinline__ void st_cluster_u64(uint64_t* local, uint32_t rank, uint64_t v) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(ra), "l"(v) : "memory");
+}
+
+template <int G, int NT>
+__global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs a) {
+    __shared__ uint64_t red[32];
+    __shared__ uint64_t part[8];
+    const int r = (int)cluster_id_x();
+    if (r >= swiglu_rows(a)) return;  // the same for every CTA of the cluster: no barrier is left waiting
+    const uint32_t C = cluster_size(), rank = cluster_rank();
+    cluster_arrive_relaxed();  // every CTA of the cluster has started before any writes into another's memory
+    const int f = a.f, ngroups = a.f_pad >> 2;
+    const int gt = (int)rank * NT + (int)threadIdx.x, stride = (int)C * NT;
+    const int64_t* accg = a.acc + (long long)r * 2 * f;
+    const int64_t* accu = accg + f;
+    const SwigluScales q = a.plans[r];
+
+    longlong2 gv[G][2], uv[G][2];
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+        const int k = (gt + i * stride) << 2;
+        if (k < f) {
+            gv[i][0] = __ldcs((const longlong2*)(accg + k));
+            gv[i][1] = __ldcs((const longlong2*)(accg + k + 2));
+            uv[i][0] = __ldcs((const longlong2*)(accu + k));
+            uv[i][1] = __ldcs((const longlong2*)(accu + k + 2));
+        } else {
+            gv[i][0] = gv[i][1] = uv[i][0] = uv[i][1] = make_longlong2(0, 0);
+        }
+    }
+    int64_t h[G][4];
+    uint64_t hm = 0;
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+        const int64_t gg[4] = {gv[i][0].x, gv[i][0].y, gv[i][1].x, gv[i][1].y};
+        const int64_t uu[4] = {uv[i][0].x, uv[i][0].y, uv[i][1].x, uv[i][1].y};
+        int32_t g32[4], u32[4];
+        int64_t idx[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            g32[j] = q.mg ? kt::requant_row(gg[j], q.rg) : 0;
+            u32[j] = q.mu ? kt::requant_row(uu[j], q.ru) : 0;
+            idx[j] = kt::apply_row(q.is, g32[j]) - a.silu.lo_index;
+        }
+        int64_t code[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t ix = idx[j] < 0 ? 0 : (idx[j] >= LUT_N ? LUT_N - 1 : idx[j]);
+            code[j] = a.silu.codes32 ? (int64_t)__ldg(a.silu.codes32 + ix) : __ldg(a.silu.codes + ix);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int64_t c = code[j];
+            if (idx[j] < 0)
+                c = 0;
+            else if (idx[j] >= LUT_N)
+                c = kt::apply_row(q.idf, g32[j]);  // identity right tail, in code units
+            const int32_t c32 = (int32_t)c;
+            const int64_t v = c32 == c ? (int64_t)c32 * (int64_t)u32[j] : c * (int64_t)u32[j];
+            h[i][j] = v;
+            hm = max(hm, uabs64(v));
+        }
+    }
+    // max |h| over the row: the CTA, then the cluster through distributed shared memory
+    const uint64_t bm = block_max_u64(hm, red);
+    cluster_wait_acquire();  // (the relaxed arrive above) every CTA is running
+    if (threadIdx.x == 0)
+        for (uint32_t c = 0; c < C; ++c) st_cluster_u64(&part[rank], c, bm);
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    uint64_t hmu = 0;
+    for (uint32_t c = 0; c < C; ++c) hmu = max(hmu, part[c]);
+    const int64_t hmax = (int64_t)hmu;
+    const kt::ReqDiv rh = kt::make_req(hmax);
+    int8_t* p0 = a.planes + (long long)r * a.f_pad;
+    int8_t* p1 = p0 + a.R_pad * a.f_pad;
+    int8_t* p2 = p1 + a.R_pad * a.f_pad;
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+        const int gi = gt + i * stride;
+        if (gi >= ngroups) continue;
+        const int k = gi << 2;
+        int32_t qv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qv[j] = (k + j < f && hmax > 0) ? kt::quant_to_act(kt::requant_row(h[i][j], rh)) : 0;
+        store_digits4(p0 + k, p1 + k, p2 + k, qv);
+    }
+    if (rank == 0 && threadIdx.x == 0) a.row_hmax[r] = hmu;
+}
+
 // Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase; one plan).
 __global__ void swiglu_global_kernel(const SwigluArgs a) {
     __shared__ uint64_t red[32];
@@ -1073,6 +1202,113 @@ __global__ void add2_final_kernel(const int32_t* __restrict__ a, const int32_t* 
     const kt::ReqDiv rg = kt::make_req(gmax);
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         y[i] = zero ? 0 : kt::requant_row(kt::apply_row(fa, a[i]) + kt::apply_row(fb, b[i]), rg);
+}
+
+// ───────────── extension: the sigmoid-gated shared expert (Qwen2-MoE's shared_expert_gate) ─────────────
+// The reference refuses this path (crates/03-models/kt-model-moe/src/lib.rs:152-154); it is defined here in the
+// reference's own terms and restated in the CPU oracle: gate = QuantLinear [1, d] on the whole input (tensor-global
+// xmax and ymax, layers.rs:275-328), code_t = sigmoid CodeLut at the token's logit (router.rs:37-51), and the shared
+// output y becomes requant_dyn(code_t·y[t, j], L, max |.|) at scale ratio(gmax)·y.scale·code_scale before add.
+
+// Gate logit accumulators acc[t] = sum_k qx[t, k]·w[k] from the shared expert's input planes, which hold the
+// tensor-global quant_to of x — the gate linear's own input quantisation (layers.rs:297-298). One warp per token,
+// 16 elements per lane step (w is zero-padded to d_pad like the planes); max |acc| into *ymax.
+__global__ void gate_logit_kernel(const int8_t* __restrict__ planes, int T, int d_pad, long long R_pad,
+                                  const int32_t* __restrict__ w, int64_t* __restrict__ acc,
+                                  unsigned long long* __restrict__ ymax) {
+    const int t = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (t >= T) return;
+    const int8_t* p0 = planes + (long long)t * d_pad;
+    const int8_t* p1 = p0 + R_pad * d_pad;
+    const int8_t* p2 = p1 + R_pad * d_pad;
+    int64_t s = 0;
+    for (int k = lane * 16; k < d_pad; k += 32 * 16) {
+        const int4 a0 = __ldg((const int4*)(p0 + k)), a1 = __ldg((const int4*)(p1 + k)), a2 = __ldg((const int4*)(p2 + k));
+        const int8_t* b0 = (const int8_t*)&a0;
+        const int8_t* b1 = (const int8_t*)&a1;
+        const int8_t* b2 = (const int8_t*)&a2;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int32_t q = (int32_t)b0[j] + 81 * (int32_t)b1[j] + 6561 * (int32_t)b2[j];
+            s += (int64_t)q * (int64_t)__ldg(w + k + j);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) {
+        acc[t] = s;
+        if (s) atomicMax(ymax, (unsigned long long)uabs64(s));
+    }
+}
+
+// One thread per token: the gate linear's output (logit = requant_dyn(acc, L, ymax) at ratio(ymax)·s_qx·w_scale, or
+// zeros when that scale or ymax is zero, layers.rs:300-326) and its sigmoid code code_at(index(logit, scale)).
+__global__ void gate_code_kernel(const int64_t* __restrict__ acc, int T, const unsigned long long* __restrict__ ymax_p,
+                                 const Scale* __restrict__ sqx, Scale w_scale, Lut sig, int64_t* __restrict__ code) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const int64_t ymax = (int64_t)*ymax_p;
+    const Scale c = kt::scale_mul(*sqx, w_scale);
+    const bool zero = c.mant == 0 || ymax == 0;
+    const Scale ls = zero ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), c);
+    const int32_t logit = zero ? 0 : kt::requant_act(acc[t], ymax);
+    int64_t idx = kt::scale_apply(kt::scale_mul(ls, sig.inv_step), (int64_t)logit) - sig.lo_index;
+    idx = idx < 0 ? 0 : (idx > LUT_N - 1 ? LUT_N - 1 : idx);
+    code[t] = sig.codes[idx];
+}
+
+struct GateArgs {
+    const int64_t* s_acc;  // shared down accumulators [T][d]
+    const unsigned long long* s_ymax;
+    const Scale* s_cd;       // shared down c
+    const int64_t* code;     // [T] sigmoid codes
+    int T, d;
+    unsigned long long* gmax;  // pass 1 out / pass 2 in
+    Scale code_scale;          // the sigmoid table's code scale (2^-20)
+    int32_t* y;                // [T][d] the gated shared output
+    Scale* y_scale;
+};
+
+// The shared expert's output element i (SwiGluMlp's down QuantLinear: requant_dyn(acc, L, ymax), zero when its
+// scale is zero) times the token's code.
+__device__ __forceinline__ int64_t gated_value(const GateArgs& p, bool live, const kt::ReqDiv& ry, int64_t c,
+                                               int64_t acc) {
+    return live ? c * (int64_t)kt::requant_row(acc, ry) : 0;
+}
+
+// Pass 1 (one block per token): max |code_t·y[t, j]| into *gmax.
+__global__ void gated_max_kernel(const GateArgs p) {
+    __shared__ uint64_t red[32];
+    const int t = blockIdx.x;
+    if (t >= p.T) return;
+    const int64_t ymax = (int64_t)*p.s_ymax;
+    const bool live = ymax != 0 && p.s_cd->mant != 0;
+    const kt::ReqDiv ry = kt::make_req(ymax);
+    const int64_t c = p.code[t];
+    const int64_t* a = p.s_acc + (long long)t * p.d;
+    uint64_t m = 0;
+    for (int j = threadIdx.x; j < p.d; j += blockDim.x) m = max(m, uabs64(gated_value(p, live, ry, c, a[j])));
+    m = block_max_u64(m, red);
+    if (threadIdx.x == 0 && m) atomicMax(p.gmax, (unsigned long long)m);
+}
+
+// Pass 2: y[t, j] = requant_dyn(code_t·y_s[t, j], L, gmax); scale = ratio(gmax)·y_s.scale·code_scale.
+__global__ void gated_final_kernel(const GateArgs p) {
+    const int t = blockIdx.x;
+    if (t >= p.T) return;
+    const int64_t ymax = (int64_t)*p.s_ymax, gmax = (int64_t)*p.gmax;
+    const Scale cd = *p.s_cd;
+    const bool live = ymax != 0 && cd.mant != 0;
+    const kt::ReqDiv ry = kt::make_req(ymax), rg = kt::make_req(gmax);
+    const int64_t c = p.code[t];
+    const int64_t* a = p.s_acc + (long long)t * p.d;
+    int32_t* y = p.y + (long long)t * p.d;
+    for (int j = threadIdx.x; j < p.d; j += blockDim.x)
+        y[j] = gmax ? kt::requant_row(gated_value(p, live, ry, c, a[j]), rg) : 0;
+    if (t == 0 && threadIdx.x == 0) {
+        const Scale ys = live ? kt::scale_mul(kt::ratio_act(ymax), cd) : kt::scale_zero();
+        *p.y_scale = gmax == 0 ? kt::scale_zero() : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), ys), p.code_scale);
+    }
 }
 
 // The first global row of this rank from every rank's row count ([world] u64, rank order).

@@ -36,6 +36,11 @@ constexpr size_t kScratchBytes = size_t(64) << 20;
 constexpr size_t kControlBytes = 256;
 static __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
+// Every accepted shape has 3·k_pad·(rows_pad + out_pad) <= kScratchBytes with rows_pad >= 64 and out_pad >= 128, so
+// k_pad stays below the longest K whose int32 diagonal sums cannot overflow (dg::K_EXACT_MAX): the K-chunk loop in
+// ktmoe_linear_noalloc makes exactly one pass at this array size and would split K only if the array grew.
+static_assert(kScratchBytes / (3 * (64 + 128)) < (size_t)dg::K_EXACT_MAX, "the scratch cap keeps K within one chunk");
+
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 unsigned char* g_scratch_dev[kMaxDevices] = {};  // the array's device address, per device (null until set up)
@@ -171,7 +176,8 @@ extern "C" int ktmoe_linear_noalloc(int32_t device, const int32_t* x, const int3
         pack_planes<<<(unsigned)out, 128, 0, st>>>(w, out, (int)k, (int)k_pad, out_pad, wp, bad);
         if (cudaGetLastError() != cudaSuccess) status = KTMOE_ERR_CUDA;
     }
-    // one weight group, one activation group; K is split into chunks whose int32 plane sums cannot overflow
+    // one weight group, one activation group; K is split into chunks whose int32 plane sums cannot overflow (one
+    // chunk at this array size, see the static_assert above)
     const int BN = rows >= 40 ? 48 : 16;
     CUtensorMap ma, mb;
     if (status == KTMOE_OK) status = make_map(&ma, wp, k_pad, 3 * out_pad, dg::BM);
