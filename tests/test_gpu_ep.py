@@ -67,6 +67,8 @@ def _worker(rank, world, port, name, mode, transport, outdir):
     if c.shared:
         s = m.shared
         dev.set_shared((s.gate.w_codes, s.gate.w_scale), (s.up.w_codes, s.up.w_scale), (s.down.w_codes, s.down.w_scale))
+        if m.shared_gate is not None:
+            dev.set_shared_gate((m.shared_gate.w_codes, m.shared_gate.w_scale))
     block = mode.endswith(":block")
     mode = mode.split(":")[0]
     if block:
@@ -94,7 +96,8 @@ def _worker(rank, world, port, name, mode, transport, outdir):
 @pytest.mark.parametrize("transport", ["nccl", "peer", "peer_graphs"])
 @pytest.mark.parametrize("name,mode", [("tiny_softmax_37rows", "even"), ("small_shared_softmax", "even"),
                                        ("tiny_sigmoid_shared", "first_empty"), ("config1", "even"),
-                                       ("tiny_sigmoid_raw_shared_one_row", "first_empty")])
+                                       ("tiny_sigmoid_raw_shared_one_row", "first_empty"),
+                                       ("small_gated_shared", "even"), ("tiny_gated_shared", "first_empty")])
 def test_expert_parallel_equals_one_gpu(tmp_path, name, mode, transport):
     import torch
     import torch.multiprocessing as mp

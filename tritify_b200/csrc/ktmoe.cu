@@ -902,11 +902,16 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     sa.phase = 0;
     mk::swiglu_plan_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
     CKL(ctx);
-    // a cluster per row with h in registers (mk::swiglu_cluster_kernel); KTMOE_SWIGLU_CLUSTER=0 keeps the block-per-row
-    // kernel below, which also takes rows the cluster form cannot (f % 4 != 0, or wider than 8 CTAs hold)
+    // KTMOE_SWIGLU_CLUSTER=1: a cluster per row with h in registers (mk::swiglu_cluster_kernel). The block-per-row
+    // kernel below is the default: it spreads a row's per-row work over more elements per thread, and measured faster
+    // on the Mixtral rows (2.37 against 2.54 ms); it also takes rows the cluster form cannot (f % 4 != 0, wider than
+    // 8 CTAs hold).
     const char* ce = getenv("KTMOE_SWIGLU_CLUSTER");
-    const bool use_cluster = !(ce && ce[0] == '0');
-    constexpr int SG = 4, SNT = 128;  // groups of four elements per thread, threads per CTA
+    const bool use_cluster = ce && ce[0] == '1';
+    // groups of four elements per thread x threads per CTA: 4 x 128 (KTMOE_SWIGLU_SHAPE=4x128) or 2 x 256
+    const char* se = getenv("KTMOE_SWIGLU_SHAPE");
+    const bool wide = !(se && se[0] == '4');
+    const int SG = wide ? 2 : 4, SNT = wide ? 256 : 128;
     int csize = 1;
     while (csize < 8 && (int64_t)csize * SG * SNT * 4 < L->f_pad) csize *= 2;
     if (use_cluster && f % 4 == 0 && (int64_t)csize * SG * SNT * 4 >= L->f_pad) {
@@ -921,7 +926,10 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
-        CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<SG, SNT>, sa));
+        if (wide)
+            CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<2, 256>, sa));
+        else
+            CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<4, 128>, sa));
         CKL(ctx);
     } else {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;

@@ -447,7 +447,71 @@ struct SwigluScales {
     int64_t mg, mu;  // requant divisors (0: that output is all zero)
     kt::ReqDiv rg, ru;
     kt::ApplyPlan is, idf;
+    int fast;  // the row meets the conditions of the lean element path (swiglu_fast_ok)
 };
+
+// ── the lean element path ──
+// A row takes it when both requant divisors admit the certified double path (2^22 <= max < 2^52), the SiLU index
+// plan is tight with a shift of at least 32 and keeps every index magnitude below 2^30 for |g| <= 2^28, the identity
+// tail keeps every code below 2^31, and the table's codes are held as int32. Every step is the exact arithmetic of
+// the general path, written for 32-bit registers where the plan's bounds allow; a certified estimate that lands too
+// near an integer falls back to the exact integer path for that element.
+constexpr double RQ_MAGIC = 6755399441055744.0;    // 1.5·2^52: an add rounded down leaves floor(y) in the low bits
+constexpr double RQ_EPS = 4.76837158203125e-07;    // 2^-21
+
+// floor(av·inv + 1/2) for 0 <= av <= den < 2^52 with inv = RN(2^28/den) and den >= 2^22: the one-rounding FMA is within
+// 2^-25 + 2^-25 + 1/(2·den) < 2^-22 of t = (av·2^28 + floor(den/2))/den (the bound of kt::requant_row's double path,
+// tightened by the fused multiply-add), and t is a multiple of 1/den, so y further than 2^-21 from an integer has
+// t's floor. Returns false (q unusable) otherwise.
+__device__ __forceinline__ bool req_mag(double av, double inv, uint32_t& q) {
+    const double y = __fma_rn(av, inv, 0.5);
+    const double m = __dadd_rd(y, RQ_MAGIC);
+    q = (uint32_t)__double2loint(m);
+    const double fr = y - (m - RQ_MAGIC);
+    return fabs(fr - 0.5) < 0.5 - RQ_EPS;
+}
+
+__device__ __forceinline__ bool swiglu_fast_ok(const SwigluScales& q, const Lut& silu) {
+    if (!(q.mg > 0 && q.mu > 0 && q.rg.dbl && q.ru.dbl && q.is.tight && q.idf.tight && silu.codes32)) return false;
+    if (q.is.shift < 32) return false;
+    const uint64_t imax = ((uint64_t(1) << 28) * q.is.mant + q.is.half) >> q.is.shift;
+    const uint64_t tmax = ((uint64_t(1) << 28) * q.idf.mant + q.idf.half) >> q.idf.shift;
+    const int64_t base = -silu.lo_index;
+    return imax < (uint64_t(1) << 30) && tmax < (uint64_t(1) << 31) && base >= 0 && base < (int64_t(1) << 30);
+}
+
+// h = silu_code(g)·u of one element on the lean path (the same integers as swiglu_h).
+__device__ __forceinline__ int64_t swiglu_h_fast(const SwigluScales& q, const int32_t* __restrict__ lut32, int32_t base,
+                                                 int64_t accg, int64_t accu) {
+    uint32_t qg, qu;
+    const bool okg = req_mag(fabs((double)accg), q.rg.inv28, qg);
+    const bool oku = req_mag(fabs((double)accu), q.ru.inv28, qu);
+    int32_t g = accg < 0 ? -(int32_t)qg : (int32_t)qg;
+    int32_t u = accu < 0 ? -(int32_t)qu : (int32_t)qu;
+    if (!okg) g = kt::requant_row(accg, q.rg);
+    if (!oku) u = kt::requant_row(accu, q.ru);
+    // CodeLut::index = is.apply(g) - lo_index; with shift >= 32 the rounding shift reads the product's high word
+    const uint32_t ag = (uint32_t)(g < 0 ? -g : g);
+    const uint32_t r = (uint32_t)(((uint64_t)ag * q.is.mant + q.is.half) >> 32) >> (q.is.shift - 32);
+    const int32_t idx = g < 0 ? base - (int32_t)r : base + (int32_t)r;
+    int32_t c = __ldg(lut32 + min(max(idx, 0), LUT_N - 1));
+    if (idx < 0)
+        c = 0;
+    else if (idx >= LUT_N)
+        c = (int32_t)kt::apply_row(q.idf, g);  // identity right tail, in code units (< 2^31 by the plan)
+    return (int64_t)c * (int64_t)u;
+}
+
+// quant_to_act(requant_row(h, rh)) on the lean path (rh.dbl): both roundings on magnitudes, the sign applied once.
+__device__ __forceinline__ int32_t down_code_fast(int64_t h, const kt::ReqDiv& rh) {
+    uint32_t q;
+    if (!req_mag(fabs((double)h), rh.inv28, q)) {
+        const int32_t e = kt::requant_row(h, rh);
+        q = (uint32_t)(e < 0 ? -e : e);
+    }
+    const uint32_t t = (uint32_t)(((uint64_t)q * (uint64_t)kt::WLEVELS + (uint64_t(1) << 27)) >> 28);
+    return h < 0 ? -(int32_t)t : (int32_t)t;
+}
 
 struct SwigluArgs {
     int64_t* acc;  // [rows][2f]: gate in [0, f), up in [f, 2f); in the tensor-global mode the gate half holds h
@@ -491,6 +555,7 @@ __device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t
     q.mu = cu.mant == 0 ? 0 : gmax_u;
     q.rg = kt::make_req(q.mg);
     q.ru = kt::make_req(q.mu);
+    q.fast = swiglu_fast_ok(q, a.silu) ? 1 : 0;
     return q;
 }
 
@@ -548,6 +613,15 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
     int8_t* p1 = p0 + a.R_pad * a.f_pad;
     int8_t* p2 = p1 + a.R_pad * a.f_pad;
     const kt::ReqDiv rh = kt::make_req(hmax);
+    if (rh.dbl) {  // the lean path (2^22 <= hmax < 2^52)
+        for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
+            int32_t q[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) q[j] = k4 + j < a.f ? down_code_fast(h[k4 + j], rh) : 0;
+            store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+        }
+        return;
+    }
     for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
         int32_t q[4];
 #pragma unroll
@@ -576,6 +650,23 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
         uint64_t hm = 0;
         // the loads of a step are issued before its arithmetic
         int k = threadIdx.x;
+        if (q.fast) {
+            const int32_t base = (int32_t)-a.silu.lo_index;
+            for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
+                int64_t gv[U], uv[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    gv[j] = accg[k + j * blockDim.x];
+                    uv[j] = accu[k + j * blockDim.x];
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int64_t v = swiglu_h_fast(q, a.silu.codes32, base, gv[j], uv[j]);
+                    h[k + j * blockDim.x] = v;
+                    hm = max(hm, uabs64(v));
+                }
+            }
+        }
         for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
             int64_t gv[U], uv[U];
 #pragma unroll
@@ -645,7 +736,7 @@ __device__ __forceinline__ void st_cluster_u64(uint64_t* local, uint32_t rank, u
 }
 
 template <int G, int NT>
-__global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs a) {
+__global__ void __launch_bounds__(NT, 2048 / (NT * G)) swiglu_cluster_kernel(const SwigluArgs a) {
     __shared__ uint64_t red[32];
     __shared__ uint64_t part[8];
     const int r = (int)cluster_id_x();
@@ -656,8 +747,8 @@ __global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs 
     const int gt = (int)rank * NT + (int)threadIdx.x, stride = (int)C * NT;
     const int64_t* accg = a.acc + (long long)r * 2 * f;
     const int64_t* accu = accg + f;
-    const SwigluScales q = a.plans[r];
 
+    // the accumulators' loads go out first; the row's plan is read while they are in flight
     longlong2 gv[G][2], uv[G][2];
 #pragma unroll
     for (int i = 0; i < G; ++i) {
@@ -671,8 +762,22 @@ __global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs 
             gv[i][0] = gv[i][1] = uv[i][0] = uv[i][1] = make_longlong2(0, 0);
         }
     }
+    const SwigluScales q = a.plans[r];
     int64_t h[G][4];
     uint64_t hm = 0;
+    if (q.fast) {
+        const int32_t base = (int32_t)-a.silu.lo_index;
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+            const int64_t gg[4] = {gv[i][0].x, gv[i][0].y, gv[i][1].x, gv[i][1].y};
+            const int64_t uu[4] = {uv[i][0].x, uv[i][0].y, uv[i][1].x, uv[i][1].y};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                h[i][j] = swiglu_h_fast(q, a.silu.codes32, base, gg[j], uu[j]);
+                hm = max(hm, uabs64(h[i][j]));
+            }
+        }
+    } else {
 #pragma unroll
     for (int i = 0; i < G; ++i) {
         const int64_t gg[4] = {gv[i][0].x, gv[i][0].y, gv[i][1].x, gv[i][1].y};
@@ -704,6 +809,7 @@ __global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs 
             hm = max(hm, uabs64(v));
         }
     }
+    }
     // max |h| over the row: the CTA, then the cluster through distributed shared memory
     const uint64_t bm = block_max_u64(hm, red);
     cluster_wait_acquire();  // (the relaxed arrive above) every CTA is running
@@ -724,8 +830,14 @@ __global__ void __launch_bounds__(NT, 4) swiglu_cluster_kernel(const SwigluArgs 
         if (gi >= ngroups) continue;
         const int k = gi << 2;
         int32_t qv[4];
+        if (rh.dbl) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) qv[j] = (k + j < f && hmax > 0) ? kt::quant_to_act(kt::requant_row(h[i][j], rh)) : 0;
+            for (int j = 0; j < 4; ++j) qv[j] = k + j < f ? down_code_fast(h[i][j], rh) : 0;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                qv[j] = (k + j < f && hmax > 0) ? kt::quant_to_act(kt::requant_row(h[i][j], rh)) : 0;
+        }
         store_digits4(p0 + k, p1 + k, p2 + k, qv);
     }
     if (rank == 0 && threadIdx.x == 0) a.row_hmax[r] = hmu;
@@ -742,10 +854,19 @@ __global__ void swiglu_global_kernel(const SwigluArgs a) {
     if (a.phase == 1) {
         const SwigluScales q = a.plans[0];
         uint64_t hm = 0;
-        for (int k = threadIdx.x; k < f; k += blockDim.x) {
-            const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
-            accg[k] = v;
-            hm = max(hm, uabs64(v));
+        if (q.fast) {
+            const int32_t base = (int32_t)-a.silu.lo_index;
+            for (int k = threadIdx.x; k < f; k += blockDim.x) {
+                const int64_t v = swiglu_h_fast(q, a.silu.codes32, base, accg[k], accu[k]);
+                accg[k] = v;
+                hm = max(hm, uabs64(v));
+            }
+        } else {
+            for (int k = threadIdx.x; k < f; k += blockDim.x) {
+                const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
+                accg[k] = v;
+                hm = max(hm, uabs64(v));
+            }
         }
         hm = block_max_u64(hm, red);
         if (threadIdx.x == 0 && hm) atomicMax(a.g_hmax, (unsigned long long)hm);
