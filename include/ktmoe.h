@@ -197,8 +197,10 @@ int ktmoe_launch_count(ktmoe_ctx* ctx, uint64_t* n);
 
 /* Per-stage timing with CUDA events on the forward's stream (tracing; off by default). With it on, every forward
  * records one event per stage boundary; ktmoe_layer_stage_times waits for them, returns the summed milliseconds per
- * stage over the timed forwards (stages: 0 quantise+route, 1 dispatch, 2 gate/up GEMM, 3 SwiGLU, 4 down GEMM,
- * 5 combine, 6 merge, 7 shared expert + add; n_stages >= 8) and forgets them. */
+ * stage over the timed forwards (stages: 0 quantise+route, 1 dispatch (permute; with expert parallelism also the
+ * counts exchange and the sends), 2 exchange in (the wait for the rows other ranks send; empty on one GPU), 3 gate/up
+ * GEMM, 4 SwiGLU, 5 down GEMM, 6 exchange out (expert outputs back to their home ranks; empty on one GPU),
+ * 7 combine, 8 merge, 9 shared expert + add; n_stages >= 10) and forgets them. */
 int ktmoe_layer_set_timing(ktmoe_layer* layer, int32_t enable);
 /* CUDA graphs for the forward (off by default): with it on, the first forward with given buffers, row count and
  * stream runs normally and is then captured; later forwards with the same ones launch the graph (fewer launch

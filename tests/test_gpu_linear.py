@@ -164,18 +164,28 @@ def test_small_codes_equal_the_cpu_path(ctx, oracle, rows, out, k):
     assert ctx.last_gemm()[1] == 3
 
 
-def test_small_codes_at_the_standalone_gemm_size(ctx):
-    """M = N = K = 4096, 12-bit weight codes uniform in [-2048, 2047] and int8 activations in [-127, 127]: every row
-    sum equals x · (sum of the weight rows), and 64 random output columns equal their exact dot products."""
-    n = 4096
-    rng = np.random.default_rng(2)
-    x, w = _small_codes(rng, n, n, n)
-    y = ctx.linear(x, w, n, n, n).reshape(n, n)
-    X = x.reshape(n, n).astype(np.int64)
-    W = w.reshape(n, n).astype(np.int64)
-    assert (y.sum(axis=1) == X @ W.sum(axis=0)).all()
-    cols = rng.choice(n, 64, replace=False)
-    assert (y[:, cols] == X @ W[cols].T).all()
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_small_codes_at_the_standalone_gemm_size(ctx, pair, monkeypatch):
+    """The standalone GEMM as the benchmark runs it: M = N = K = 4096, 12-bit weight codes uniform in [-2048, 2047]
+    then int8 activations in [-127, 127], one stream of the reference's test LCG seeded 2. The whole exact int64
+    result hashes to the CPU oracle's golden (tests/golden/bench_golden.json, the oracle's Portable linear), on SM
+    pairs and on single SMs."""
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import bench
+
+    monkeypatch.setenv("KTMOE_PAIR", pair)
+    g = json.load(open(os.path.join(root, "tests", "golden", "bench_golden.json")))["workloads"]["gemm4096"]
+    w = bench.WORKLOADS["gemm4096"]
+    x, wt = bench.gemm_codes(w, tb.lcg_uniform)
+    assert hashlib.sha256(np.ascontiguousarray(x, dtype="<i4").tobytes()).hexdigest() == g["x_sha256"]
+    assert hashlib.sha256(np.ascontiguousarray(wt, dtype="<i4").tobytes()).hexdigest() == g["w_sha256"]
+    n = w["M"]
+    y = ctx.linear(x, wt, n, n, n)
+    assert ctx.last_gemm()[1] == 1  # the (1, 2)-plane kernels
+    assert hashlib.sha256(np.ascontiguousarray(y, dtype="<i8").tobytes()).hexdigest() == g["output"]["data_sha256"]
 
 
 @pytest.mark.parametrize("rows,out,k", [(300, 1000, 4096), (256, 256, 128), (1000, 384, 3000), (129, 130, 200)])

@@ -469,16 +469,17 @@ class DeviceLayer:
         self.ctx.check(status)
         return y, Scale._of(ys)
 
-    STAGES = ["route", "dispatch", "gemm_gate_up", "swiglu", "gemm_down", "combine", "merge", "shared"]
+    STAGES = ["route", "dispatch", "exchange_in", "gemm_gate_up", "swiglu", "gemm_down", "exchange_out", "combine",
+              "merge", "shared"]
 
     def set_timing(self, enable: bool) -> None:
         self.ctx.check(lib().ktmoe_layer_set_timing(self._h, 1 if enable else 0))
 
     def stage_times(self):
         """(per-stage milliseconds summed over the timed forwards, number of timed forwards)."""
-        ms = (ctypes.c_double * 8)()
+        ms = (ctypes.c_double * len(self.STAGES))()
         n = ctypes.c_int32()
-        self.ctx.check(lib().ktmoe_layer_stage_times(self._h, ms, 8, ctypes.byref(n)))
+        self.ctx.check(lib().ktmoe_layer_stage_times(self._h, ms, len(self.STAGES), ctypes.byref(n)))
         return dict(zip(self.STAGES, list(ms))), n.value
 
     def debug_fetch(self, which: int, rows: int):

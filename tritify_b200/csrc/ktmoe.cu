@@ -695,7 +695,12 @@ bool layer_complete(const ktmoe_layer* L) {
 }
 
 // Stage boundaries recorded when timing is on (see ktmoe_layer_stage_times).
-enum Stage { ST_ROUTE = 0, ST_DISPATCH, ST_GEMM_GU, ST_SWIGLU, ST_GEMM_DOWN, ST_COMBINE, ST_MERGE, ST_SHARED, ST_N };
+// ST_XIN (the wait for the rows other ranks send) and ST_XOUT (the return of expert outputs to their home ranks) are
+// empty on one GPU: every path records the same boundaries.
+enum Stage {
+    ST_ROUTE = 0, ST_DISPATCH, ST_XIN, ST_GEMM_GU, ST_SWIGLU, ST_GEMM_DOWN, ST_XOUT, ST_COMBINE, ST_MERGE, ST_SHARED,
+    ST_N
+};
 
 int mark(ktmoe_layer* L, cudaStream_t st) {
     if (!L->timing) return KTMOE_OK;
@@ -1063,6 +1068,7 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     // the exchange of rows: three digit planes and the s_qx words
     CK(L->ep_recv_planes.ensure(3 * Rr_pad * L->d_pad));
     CK(L->ep_meta_recv.ensure(std::max<int64_t>(Rr, 1) * 16));
+    MARK(L, st);
     NK(ncclGroupStart());
     for (int64_t q = 0; q < G; ++q) {
         for (int p = 0; p < 3; ++p) {
@@ -1143,6 +1149,7 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         }
     }
     NK(ncclGroupEnd());
+    MARK(L, st);
     if (T > 0) {
         mk::CombineYArgs ca;
         ca.y = L->ep_y_back.as<int32_t>();
@@ -1197,6 +1204,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         pr.P, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
         L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(), ctx->d_err);
     CKL(ctx);
+    MARK(L, st);
     ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_DISPATCH, ctx->d_err);
     CKL(ctx);
     MARK(L, st);
@@ -1226,6 +1234,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     xr.row_expert = pr.recv_expert.as<int>();
     xr.row_sqx = pr.recv_sqx.as<Scale>();
     if (int r = run_experts(L, xr, st)) return r;
+    MARK(L, st);
     ep::return_kernel<<<(unsigned)(ctx->num_sms * 8), 256, 0, st>>>(pr.P, pr.rows_recv.as<int>(),
                                                                    L->acc_d.as<int64_t>(),
                                                                    L->rowmax_d.as<unsigned long long>(),
@@ -1410,6 +1419,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         const int BN2 = pick_bn_long_k((double)R / (double)E, f, true);
         if (int r = plan_and_permute(L, T, BN, BN2, st)) return r;
         MARK(L, st);
+        MARK(L, st);  // no exchange on one GPU
         ExpertRows xr;
         xr.B = Planes{L->xg_planes.as<int8_t>(), 1, R_pad, d, L->d_pad};
         xr.n_rows = R;
@@ -1431,6 +1441,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         xr.row_sqx = L->tok_sqx.as<Scale>();
         if (int r = run_experts(L, xr, st)) return r;
         MARK(L, st);
+        MARK(L, st);  // no exchange on one GPU
         mk::CombineArgs ca;
         ca.acc_d = L->acc_d.as<int64_t>();
         ca.ymax_d = L->rowmax_d.as<unsigned long long>();
