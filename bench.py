@@ -53,6 +53,13 @@ WORKLOADS = {
     "glm_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3,
                        decode=True),
     "glm_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, wseed=1, xseed=3),
+    # The GLM-4.5-Air-shaped stack (45 MoE blocks: RmsNorm, the layer, the residual add; attention excluded), the
+    # experts sharded over the GPUs, every layer's weights generated and quantised on its GPUs from the portable stream
+    # (layer l: seed lseed + 4l); about 301 GB of digit planes, so it needs several GPUs.
+    "glm_stack_decode": dict(d=4096, E=128, f=1408, k=8, T=128, norm=True, sigmoid=True, shared=1408, xseed=3,
+                             decode=True, stack=45, lseed=1000),
+    "glm_stack_prefill": dict(d=4096, E=128, f=1408, k=8, T=16384, norm=True, sigmoid=True, shared=1408, xseed=3,
+                              stack=45, lseed=1000),
     # The standalone digit-plane GEMM, M = N = K = 4096, weights uniform in [-2048, 2047] and
     # activations uniform in [-127, 127] from the reference's LCG, seed 2 (1 GPU).
     "gemm4096": dict(gemm=True, M=4096, N=4096, K=4096, seed=2),
@@ -305,6 +312,58 @@ def golden_parity(name, out_hash, w):
     want = g["output"]
     same = all(out_hash.get(k) == want.get(k) for k in ("data_sha256", "repro_sha256"))
     return "golden" if same else "MISMATCH"
+
+
+STACK_EPS = 1e-5  # the blocks' RmsNorm epsilon (GLM-4.5-Air's rms_norm_eps); the norm weight is all ones
+STACK_CHECK_LAYERS = 2  # the leading layers whose output every stack run checks against the oracle's golden
+
+
+def stack_seed(w, layer: int) -> int:
+    """The portable weight stream of one layer of a stack (its sigmoid bias uses seed + 2, never another layer's)."""
+    return w["lseed"] + 4 * layer
+
+
+def portable_oracle_layer(w, O, seed):
+    """One layer in the CPU oracle from the portable stream ``seed``, in the order the library synthesises it on the
+    GPU (ktmoe_layer_synth_weights): router, experts' gate/up/down, shared gate/up/down, [shared-expert gate]; a
+    sigmoid router's selection bias from seed + 2 at sigma 0.02."""
+    d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
+    gated = bool(fs and w.get("gated"))
+    router = O.synth_normal_portable(seed, 0.02, E * d, 0)
+    experts = O.synth_normal_portable(seed, 0.02, E * 3 * f * d, E * d)
+    o = E * d + E * 3 * f * d
+    shared = O.synth_normal_portable(seed, 0.02, 3 * fs * d, o) if fs else None
+    gate = O.synth_normal_portable(seed, 0.02, d, o + 3 * fs * d) if gated else None
+    sbias = O.synth_normal_portable(seed + 2, 0.02, E) if w["sigmoid"] else None
+    return O.MoeOracle(d, E, f, w["k"], router, experts, norm_topk=w["norm"], sigmoid_bias=sbias, shared_hidden=fs,
+                       shared_w=shared, shared_gate_w=gate)
+
+
+def stack_oracle(w, O, n_layers):
+    """The oracle's layer loop (kt-core model.rs:175-181 with attention excluded): x <- add(x, moe_l(rms_norm(x))) for
+    the first n_layers layers of the stack; returns (codes [T, d], (mant, shift))."""
+    xi, xs = oracle_x(w, O)
+    ones = np.ones(w["d"], np.float32)
+    for layer in range(n_layers):
+        m = portable_oracle_layer(w, O, stack_seed(w, layer))
+        xn, xns, _, _, _ = O.rmsnorm(ones, STACK_EPS, xi, xs)
+        moe, ms = m.forward_par(xn.reshape(w["T"], w["d"]), xns)
+        del m
+        y, xs = O.add(xi.reshape(-1), xs, moe.reshape(-1), ms)
+        xi = y.reshape(w["T"], w["d"])
+    return xi, xs
+
+
+def stack_bytes_per_gpu(w, world):
+    """Digit-plane bytes one GPU holds for the stack (planes padded as the library pads them)."""
+    up = lambda v, m: (v + m - 1) // m * m  # noqa: E731
+    d, E, f, fs = w["d"], w["E"], w["f"], w["shared"]
+    rows = lambda r: up(r, 256) if r > 128 else 128  # noqa: E731
+    el = -(-E // world)
+    per = 3 * (el * (rows(2 * f) * up(d, 128) + rows(d) * up(f, 128)) + rows(E) * up(d, 128))
+    if fs:
+        per += 3 * (rows(2 * fs) * up(d, 128) + rows(d) * up(fs, 128))
+    return w["stack"] * per
 
 
 def cpu_sample(w, seconds_target: float, O, max_rows=None):
@@ -838,6 +897,256 @@ def run_ours(args, w, name):
         raise SystemExit(f"{name}: the output differs from the CPU oracle's golden hash or from the host-API forward")
 
 
+def run_stack_reference(args, w, name):
+    """The reference's CPU path for the stack: one block of the stack (RmsNorm, the layer, the residual add, in the
+    oracle) on a bounded sample of the tokens per step; every layer has the same shape and cost, so a step's time for
+    the whole stack is the block's time times the layer count."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as O
+
+    O.build()
+    O.lib().ko_set_max_threads(0)
+    L = w["stack"]
+    m = portable_oracle_layer(w, O, stack_seed(w, 0))
+    xi, xs = oracle_x(w, O)
+    ones = np.ones(w["d"], np.float32)
+
+    def block(rows):
+        xn, xns, _, _, _ = O.rmsnorm(ones, STACK_EPS, xi[:rows], xs)
+        moe, ms = m.forward(xn.reshape(rows, w["d"]), xns)
+        return O.add(xi[:rows].reshape(-1), xs, moe.reshape(-1), ms)
+
+    t0 = time.perf_counter()
+    block(2)
+    per_tok = max((time.perf_counter() - t0) / 2, 1e-6)
+    rows = int(max(1, min(w["T"], 150.0 / max(1, args.steps + args.warmup) / per_tok)))
+    for _ in range(args.warmup):
+        block(rows)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        block(rows)
+    dt = (time.perf_counter() - t0) / args.steps * L
+    v = rows / dt
+    sample = (f"first {rows} of {w['T']} tokens through one block per step, times {L} layers (C++ restatement of "
+              f"the reference CPU path)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+        "config": {**workload_config(w, name), "layers": L, "block": "rms_norm + moe + residual add",
+                   "weights": "portable N(0, 0.02) stream per layer, generated and quantised on the GPU"},
+        "parallelism": f"ep{world}",
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_stack(args, w, name):
+    """Config 5: the stack of MoE blocks over the GPUs of one node (expert parallel, peer-memory exchange), one
+    DeviceLayer per rank holding every layer as a weight slot. Each run first checks the leading STACK_CHECK_LAYERS
+    layers' output against the CPU oracle's golden, then times whole steps through all the layers."""
+    import ctypes
+    import datetime
+    import hashlib
+
+    import torch
+
+    import tritify_b200 as tb
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    need = stack_bytes_per_gpu(w, world)
+    total = torch.cuda.get_device_properties(local).total_memory
+    if need > 0.8 * total:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "workload": name, "n_gpus": world,
+                              "error": f"the stack's {need / 1e9:.0f} GB of planes per GPU do not fit "
+                                       f"{total / 1e9:.0f} GB: run it on more GPUs"}), flush=True)
+        raise SystemExit(2)
+    ep = None
+    if dist is not None:
+        nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            nid.copy_(torch.frombuffer(bytearray(tb.ep_unique_id()), dtype=torch.uint8))
+        dist.broadcast(nid, 0)
+        ep = (rank, world, bytes(nid.cpu().numpy().tobytes()))
+    d, T_all, L = w["d"], w["T"], w["stack"]
+    if T_all % world:
+        raise SystemExit(f"{T_all} tokens do not split evenly over {world} ranks")
+    T = T_all // world
+    ctx = tb.Context(local)
+    t0 = time.perf_counter()
+    dev = tb.DeviceLayer(ctx, d, w["E"], w["f"], w["k"], w["norm"], w["sigmoid"], w["shared"], ep=ep)
+    dev.set_depth(L)
+    norm = tb.QuantLinear.from_weights("norm", np.ones(d, np.float32), 1, d)
+    for layer in range(L):
+        dev.select(layer)
+        dev.synth_weights(stack_seed(w, layer), 0.02, 0.02, bool(w.get("gated")))
+        dev.set_norm(norm.w_codes, norm.w_scale, tb.scale_from_f64(STACK_EPS))
+    transport = None
+    if world > 1:
+        dev.set_ep_capacity(T)  # collective
+        transport = "peer"
+    dev.set_graphs(True)
+    log(f"[bench] {name}: {L} layers synthesised on the GPU in {time.perf_counter() - t0:.1f} s "
+        f"({need / 1e9:.1f} GB of planes per GPU)")
+
+    x_full = make_x(w)
+    x = tb.IntTensor(x_full.data.reshape(T_all, d)[rank * T:(rank + 1) * T], (T, d), x_full.scale)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    xd = torch.from_numpy(x.data.copy()).cuda()
+    xs_d = torch.tensor([x.scale.mant, x.scale.shift & 0xFFFFFFFF], dtype=torch.int64).cuda()
+    yd = torch.empty_like(xd)
+    ys_d = torch.zeros(2, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def gather_hash(y, ys):
+        y_all = y.clone()
+        if dist is not None:
+            parts = [torch.empty_like(y_all) for _ in range(world)]
+            dist.all_gather(parts, y_all)
+            y_all = torch.cat(parts)
+        b = y_all.cpu().numpy().astype("<i4").tobytes()
+        mant, shift = int(ys[0]), int(ys[1]) & 0xFFFFFFFF
+        shift = shift - (1 << 32) if shift >= 1 << 31 else shift
+        head = np.int64(mant).astype("<i8").tobytes() + np.int32(shift).astype("<i4").tobytes()
+        return {"data_sha256": hashlib.sha256(b).hexdigest(), "repro_sha256": hashlib.sha256(head + b).hexdigest(),
+                "scale": [mant, shift]}
+
+    # parity: the leading layers against the oracle's golden
+    head = tb.MoeStack([dev.slot(i) for i in range(min(STACK_CHECK_LAYERS, L))])
+    head.forward_dev(xd.data_ptr(), T, xs_d.data_ptr(), yd.data_ptr(), ys_d.data_ptr())
+    ctx.sync()
+    head_hash = gather_hash(yd, ys_d.cpu())
+    try:
+        g = json.load(open(GOLDEN_PATH)).get("workloads", {}).get(name)
+    except (OSError, ValueError):
+        g = None
+    parity = "no golden" if g is None else ("golden" if all(head_hash[k] == g["output"][k] for k in
+                                                            ("data_sha256", "repro_sha256")) else "MISMATCH")
+
+    stack = tb.MoeStack([dev.slot(i) for i in range(L)])
+
+    def step():
+        stack.forward_dev(xd.data_ptr(), T, xs_d.data_ptr(), yd.data_ptr(), ys_d.data_ptr())
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    ctx.sync()
+    barrier()
+    launches0 = ctx.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(smi_index(local)) as clk:
+        barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        end.synchronize()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    launches = ctx.launch_count() - launches0
+    out_hash = gather_hash(yd, ys_d.cpu())
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # per-stage split of one layer's forward (every layer has the same shape): timed forwards, uncaptured
+    dev.set_timing(True)
+    dev.stage_times()
+    for _ in range(max(1, args.steps // 2)):
+        step()
+    ctx.sync()
+    stages, nfw = dev.stage_times()
+    dev.set_timing(False)
+    barrier()
+    stage_ms = {k: v / max(1, nfw) for k, v in stages.items()}
+
+    # e2e: pinned host tokens in, the stack, the result back, every step
+    xh = torch.empty(T * d, dtype=torch.int32, pin_memory=True)
+    xh.numpy()[:] = x.data
+    yh = torch.empty(T * d, dtype=torch.int32, pin_memory=True)
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            xd.copy_(xh, non_blocking=True)
+            step()
+            yh.copy_(yd, non_blocking=True)
+
+    e2e_step()
+    ctx.sync()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_steps = max(3, args.steps // 2)
+    barrier()
+    e_start.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e_end.record(stream)
+    e_end.synchronize()
+    e2e_ms = e_start.elapsed_time(e_end) / e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    hbm, bf16, peak_kind = measured_peaks()
+    E, f, fs, k = w["E"], w["f"], w["shared"], w["k"]
+    if w.get("decode"):
+        # every step streams each layer's planes once: the experts the routing touches (at 128 tokens x top-8 over
+        # 128 experts, all of them but about 0.04 per layer on average), the router and the shared expert
+        per_gpu = [3 * L * ((r + 1) * E // world - r * E // world) * 3 * d * f + 3 * L * (E * d + 3 * d * fs)
+                   + 2 * L * T * d * 4 for r in range(world)]
+        hb = max(per_gpu)
+        roofline = {"bound": "hbm", "achieved": hb / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                    "frac": hb / (ms * 1e-3) / 1e9 / hbm, "traffic": None, "kernel": "the whole stack step (decode)",
+                    "bytes_per_gpu": per_gpu, "peak_source": f"{peak_kind} HBM copy bandwidth",
+                    "assumption": "every expert of every layer touched"}
+    else:
+        ops = 2.0 * P_PLANES * L * T_all * (k * 3 * d * f + 3 * d * fs + E * d) / world
+        roofline = {"bound": "tensor", "achieved": ops / (ms * 1e-3) / 1e12, "peak": 2.0 * bf16,
+                    "unit": "TOPS (int8)", "frac": ops / (ms * 1e-3) / 1e12 / (2.0 * bf16), "traffic": None,
+                    "kernel": "the whole stack step, per GPU (routed + shared + router plane products)",
+                    "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
+                    "plane_products": P_PLANES}
+    res = {
+        "metric": METRIC, "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8x9 (exact int64)", "data": "synthetic",
+        "config": {**workload_config(w, name), "layers": L, "block": "rms_norm + moe + residual add",
+                   "weights": "portable N(0, 0.02) stream per layer, generated and quantised on the GPU"},
+        "parallelism": f"ep{world}", "parity": parity, "parity_layers": min(STACK_CHECK_LAYERS, L),
+        "output": out_hash, "head_output": head_hash,
+        "run": {"ep_transport": transport, "cuda_graphs": True, "tokens_per_rank": T,
+                "planes_gb_per_gpu": need / 1e9},
+        "e2e": {"value": T_all / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": T_all * d * 4,
+                "d2h_bytes_per_step": T_all * d * 4},
+        "gpu_launches": launches, "roofline": roofline, "stage_ms_per_layer": stage_ms, "clocks": clk.summary(),
+    }
+    stack = head = None
+    dev = None
+    ctx.sync()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+        if parity == "MISMATCH":
+            raise SystemExit(f"{name}: the first layers differ from the CPU oracle's golden")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -848,6 +1157,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--tokens", type=int, default=0, help="override the workload's token count (small profiling cases)")
     ap.add_argument("--experts", type=int, default=0, help="override the workload's expert count (small profiling cases)")
+    ap.add_argument("--layers", type=int, default=0, help="override a stack workload's layer count")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = dict(WORKLOADS[args.workload])
@@ -856,6 +1166,16 @@ def main():
         return
     if w.get("linear_bench"):
         (run_linear_bench_reference if args.impl == "reference" else run_linear_bench_ours)(args, w, args.workload)
+        return
+    if w.get("stack"):
+        if args.tokens:
+            w["T"] = args.tokens
+        if args.layers:
+            w["stack"] = args.layers
+        if args.impl == "reference":
+            run_stack_reference(args, w, args.workload)
+        else:
+            run_stack(args, w, args.workload)
         return
     if args.tokens:
         w["T"] = args.tokens

@@ -138,6 +138,20 @@ int ktmoe_layer_set_shared(ktmoe_layer* layer, const int32_t* gate, ktmoe_scale 
  * the sigmoid CodeLut (router.rs:37-51), the shared output row is multiplied by it and the tensor requantised
  * (requant_dyn at the tensor's max) before add. NULL codes turn the gate off. Needs a shared expert. */
 int ktmoe_layer_set_shared_gate(ktmoe_layer* layer, const int32_t* codes, ktmoe_scale w_scale);
+/* A stack of layers of one shape in one object (a decoder's MoE blocks, model.rs:175-186, attention excluded): the
+ * layer holds n_layers weight slots that share its scratch, tables and expert-parallel exchange. Slot 0 keeps the
+ * weights set so far; ktmoe_layer_select(layer, i) makes slot i the one that the setters write and the forwards read
+ * (a host-side swap, no device work). Set the depth once, before the first forward. */
+int ktmoe_layer_set_depth(ktmoe_layer* layer, int32_t n_layers);
+int ktmoe_layer_select(ktmoe_layer* layer, int32_t slot);
+/* Fill the selected slot on the device, for layers too large to quantise on the host: weights N(0, sigma) from the
+ * portable stream `seed` (ktmoe_synth_normal_portable), in the order router [E][d], expert e's gate [f][d], up [f][d],
+ * down [d][f] for every e, then the shared expert's gate, up, down and, with shared_gate, its gate [1][d]; this rank
+ * draws only its own experts' ranges. Each matrix is quantised per tensor as QuantLinear::from_weights does it
+ * (layers.rs:225-244): the same codes and scales as the host quantiser on the same f32 values. A sigmoid router also
+ * gets its selection bias: E values of the stream seed + 2 at sigmoid_bias_sigma, coded round(b * 2^20). Synchronous. */
+int ktmoe_layer_synth_weights(ktmoe_layer* layer, uint64_t seed, float sigma, float sigmoid_bias_sigma,
+                              int32_t shared_gate);
 /* Module::forward_int: x [rows][d_model] at x_scale -> y [rows][d_model] at *y_scale. Host buffers; synchronous. */
 int ktmoe_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
                   ktmoe_scale* y_scale);
@@ -225,6 +239,13 @@ int ktmoe_table(int32_t kind, int64_t* codes, ktmoe_scale* inv_step, int64_t* lo
 /* Synthetic inputs defined by this build: elements [offset, offset + n) of the N(0, sigma) stream `seed` (splitmix64
  * + Box-Muller in f64, cast to f32), and the reference's LCG uniform integers in [lo, hi]. */
 int ktmoe_synth_normal(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out);
+/* The portable normal stream (tritify_b200/csrc/synth.cuh): the same splitmix64 uniforms as ktmoe_synth_normal, the
+ * Box-Muller deviate with this library's own logarithm and cosine from correctly rounded IEEE operations only, so the
+ * host and the device give identical bits (libm's log and cos differ between them in the last place). The _dev form
+ * writes device memory on the context's stream and returns when it is done. */
+int ktmoe_synth_normal_portable(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out);
+int ktmoe_synth_normal_portable_dev(ktmoe_ctx* ctx, uint64_t seed, float sigma, uint64_t offset, int64_t n,
+                                    float* out_dev);
 int ktmoe_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, int64_t n, int32_t* out);
 
 /* ── wire format: IntTensor::to_bytes / IntTensor::from_bytes (kt-core/src/tensor.rs:51-100) ──

@@ -1145,6 +1145,84 @@ void ko_synth_normal(uint64_t seed, float sigma, uint64_t offset, size_t n, floa
     for (auto& th : ts) th.join();
 }
 
+// The portable normal stream this build defines for weights generated on the GPU (the product's synth.cuh): the same
+// splitmix64 uniforms as ko_synth_normal, the Box-Muller deviate with a logarithm and a cosine built from IEEE
+// add/mul/div/sqrt only, in a fixed order (this file is compiled with -ffp-contract=off), so the GPU's weights can be
+// regenerated here bit for bit. ln(u) = e·ln2 + 2·atanh((m-1)/(m+1)) for u = m·2^e, m in [sqrt(1/2), sqrt(2)), the
+// atanh series to s^23; cos(2πu) from the quadrant of 4u and the Taylor series of cos and sin on [0, π/4].
+static double portable_ln(double u) {
+    static const double inv_odd[11] = {0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3,
+                                       0x1.c71c71c71c71cp-4, 0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4,
+                                       0x1.1111111111111p-4, 0x1.e1e1e1e1e1e1ep-5, 0x1.af286bca1af28p-5,
+                                       0x1.8618618618618p-5, 0x1.642c8590b2164p-5};  // 1/3, 1/5, ..., 1/23
+    uint64_t bits;
+    std::memcpy(&bits, &u, 8);
+    int e = (int)((bits >> 52) & 0x7ff) - 1023;
+    const uint64_t mb = (bits & ((uint64_t(1) << 52) - 1)) | (uint64_t(1023) << 52);
+    double m;
+    std::memcpy(&m, &mb, 8);
+    if (m > 0x1.6a09e667f3bcdp+0) {
+        m = m * 0.5;
+        e = e + 1;
+    }
+    const double s = (m - 1.0) / (m + 1.0), s2 = s * s;
+    double p = inv_odd[10];
+    for (int k = 9; k >= 0; --k) p = p * s2 + inv_odd[k];
+    return (double)e * 0x1.62e42fefa39efp-1 + 2.0 * (s + s * (s2 * p));
+}
+
+static double portable_cos_2pi(double u) {
+    static const double cos_c[9] = {-0x1.0000000000000p-1, 0x1.5555555555555p-5,  -0x1.6c16c16c16c17p-10,
+                                    0x1.a01a01a01a01ap-16, -0x1.27e4fb7789f5cp-22, 0x1.1eed8eff8d898p-29,
+                                    -0x1.93974a8c07c9dp-37, 0x1.ae7f3e733b81fp-45, -0x1.6827863b97d97p-53};
+    static const double sin_c[9] = {-0x1.5555555555555p-3, 0x1.1111111111111p-7,  -0x1.a01a01a01a01ap-13,
+                                    0x1.71de3a556c734p-19, -0x1.ae64567f544e4p-26, 0x1.6124613a86d09p-33,
+                                    -0x1.ae7f3e733b81fp-41, 0x1.952c77030ad4ap-49, -0x1.2f49b46814157p-57};
+    const double t = u * 4.0;
+    const int quadrant = (int)t;
+    const double r = t - (double)quadrant;
+    const bool first_half = r <= 0.5;
+    const double a = (first_half ? r : 1.0 - r) * 0x1.921fb54442d18p+0;
+    const double a2 = a * a;
+    double c = cos_c[8], sv = sin_c[8];
+    for (int k = 7; k >= 0; --k) {
+        c = c * a2 + cos_c[k];
+        sv = sv * a2 + sin_c[k];
+    }
+    const double cos_a = 1.0 + a2 * c, sin_a = a + a * (a2 * sv);
+    const double cp = first_half ? cos_a : sin_a, sp = first_half ? sin_a : cos_a;
+    switch (quadrant) {
+        case 0: return cp;
+        case 1: return -sp;
+        case 2: return -cp;
+        default: return sp;
+    }
+}
+
+void ko_synth_normal_portable(uint64_t seed, float sigma, uint64_t offset, size_t n, float* out) {
+    auto mix = [](uint64_t sd, uint64_t j) {
+        uint64_t v = sd + (j + 1) * 0x9E3779B97F4A7C15ULL;
+        v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ULL;
+        v = (v ^ (v >> 27)) * 0x94D049BB133111EBULL;
+        return v ^ (v >> 31);
+    };
+    auto run = [&](size_t lo, size_t hi) {
+        for (size_t j = lo; j < hi; ++j) {
+            const uint64_t i = offset + j;
+            const double u1 = 1.0 - (double)(mix(seed, 2 * i) >> 11) * 0x1p-53;
+            const double u2 = (double)(mix(seed, 2 * i + 1) >> 11) * 0x1p-53;
+            const double z = std::sqrt(-2.0 * portable_ln(u1)) * portable_cos_2pi(u2);
+            out[j] = (float)z * sigma;
+        }
+    };
+    const size_t nt = n < (size_t(1) << 20) ? 1 : std::max<unsigned>(1, std::thread::hardware_concurrency());
+    const size_t chunk = (n + nt - 1) / nt;
+    std::vector<std::thread> ts;
+    for (size_t s0 = chunk; s0 < n; s0 += chunk) ts.emplace_back(run, s0, std::min(n, s0 + chunk));
+    run(0, std::min(n, chunk));
+    for (auto& th : ts) th.join();
+}
+
 // The reference's test LCG (crates/02-runtime/kt-runtime/src/gate.rs:29-36; kt-core/src/tests.rs:15-24):
 // s ← s·6364136223846793005 + 1442695040888963407 (mod 2^64), value = (s >> 33) mod (hi − lo + 1) + lo.
 void ko_lcg_uniform(uint64_t seed, int64_t lo, int64_t hi, size_t n, int32_t* out) {

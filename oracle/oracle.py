@@ -79,6 +79,7 @@ def lib():
             "ko_moe_forward_tokens": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_par": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale), sz], None),
             "ko_synth_normal": ([ctypes.c_uint64, ctypes.c_float, ctypes.c_uint64, sz, f32p], None),
+            "ko_synth_normal_portable": ([ctypes.c_uint64, ctypes.c_float, ctypes.c_uint64, sz, f32p], None),
             "ko_lcg_uniform": ([ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64, sz, i32p], None),
             "ko_moe_forward_with_local_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale)], None),
             "ko_moe_forward_with_given_experts": ([ctypes.c_void_p, i32p, sz, KoScale, i32p, p(KoScale), i32p,
@@ -220,6 +221,14 @@ def synth_normal(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray
     rounded to f32), computed by the oracle itself."""
     out = np.empty(n, dtype=np.float32)
     lib().ko_synth_normal(seed, sigma, offset, n, _p(out, ctypes.c_float))
+    return out
+
+
+def synth_normal_portable(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray:
+    """Elements [offset, offset + n) of the portable N(0, sigma) stream (own ln and cos from IEEE operations), the one
+    the GPU library generates weights with on the device."""
+    out = np.empty(n, dtype=np.float32)
+    lib().ko_synth_normal_portable(seed, sigma, offset, n, _p(out, ctypes.c_float))
     return out
 
 

@@ -69,6 +69,18 @@ def layer_entry(name: str) -> dict:
     return entry
 
 
+def stack_entry(name: str) -> dict:
+    """The leading bench.STACK_CHECK_LAYERS blocks of a stack workload, their weights from the portable stream the GPU
+    synthesises them from."""
+    w = dict(bench.WORKLOADS[name])
+    t0 = time.time()
+    n = min(bench.STACK_CHECK_LAYERS, w["stack"])
+    y, ys = bench.stack_oracle(w, O, n)
+    print(f"{name}: first {n} layers {out_hashes(y, ys)['data_sha256'][:16]} ({time.time() - t0:.0f} s)", flush=True)
+    return {"T": w["T"], "E": w["E"], "layers_checked": n, "config": bench.workload_config(w, name),
+            "output": out_hashes(y, ys), "oracle_seconds": round(time.time() - t0, 1)}
+
+
 def gemm_entry(name: str) -> dict:
     w = dict(bench.WORKLOADS[name])
     t0 = time.time()
@@ -84,14 +96,16 @@ def gemm_entry(name: str) -> dict:
 
 
 def main():
-    names = sys.argv[1:] or (LAYER_WORKLOADS + ["gemm4096"])
+    names = sys.argv[1:] or (LAYER_WORKLOADS + ["gemm4096", "glm_stack_decode", "glm_stack_prefill"])
     out = {"about": "CPU-oracle golden hashes of bench.py's workloads (python tests/golden/make_bench_golden.py); "
                     "output.data_sha256 is verify::hash_int of the whole output, repro_sha256 binds the scale.",
            "workloads": {}}
     if os.path.exists(PATH):
         out["workloads"].update(json.load(open(PATH)).get("workloads", {}))
     for n in names:
-        out["workloads"][n] = gemm_entry(n) if bench.WORKLOADS[n].get("gemm") else layer_entry(n)
+        kind = bench.WORKLOADS[n]
+        out["workloads"][n] = gemm_entry(n) if kind.get("gemm") else stack_entry(n) if kind.get("stack") else \
+            layer_entry(n)
         with open(PATH, "w") as fh:
             json.dump(out, fh, indent=1, sort_keys=True)
     print("wrote", PATH)

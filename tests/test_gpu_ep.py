@@ -149,3 +149,74 @@ def test_expert_parallel_block_equals_the_oracle(tmp_path, oracle, name, mode, t
             scales.add((int(z["mant"]), int(z["shift"])))
     assert scales == {ws}
     assert (np.concatenate(ys) == want).all()
+
+
+STACK = dict(d=256, E=16, f=192, k=4, T=24, norm=True, sigmoid=True, shared=128, xseed=7, stack=3, lseed=500)
+
+
+def _stack_worker(rank, world, port, outdir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(HERE))
+    import bench
+
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    nid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        nid.copy_(torch.frombuffer(bytearray(tb.ep_unique_id()), dtype=torch.uint8))
+    dist.broadcast(nid, 0)
+    w = STACK
+    ctx = tb.Context(rank)
+    dev = tb.DeviceLayer(ctx, w["d"], w["E"], w["f"], w["k"], w["norm"], w["sigmoid"], w["shared"],
+                         ep=(rank, world, bytes(nid.cpu().numpy().tobytes())))
+    dev.set_depth(w["stack"])
+    norm = tb.QuantLinear.from_weights("norm", np.ones(w["d"], np.float32), 1, w["d"])
+    for i in range(w["stack"]):
+        dev.select(i)
+        dev.synth_weights(bench.stack_seed(w, i))  # each rank draws only its own experts
+        dev.set_norm(norm.w_codes, norm.w_scale, tb.scale_from_f64(bench.STACK_EPS))
+    sizes = _splits(w["T"], world, "even")
+    dev.set_ep_capacity(max(sizes))
+    dev.set_graphs(True)
+    x = tb.IntTensor.from_reals(tb.synth_normal(w["xseed"], 1.0, w["T"] * w["d"]))
+    start, rows = sum(sizes[:rank]), sizes[rank]
+    xr = tb.IntTensor(x.data.reshape(w["T"], w["d"])[start:start + rows].reshape(-1), (rows, w["d"]), x.scale)
+    stack = tb.MoeStack([dev.slot(i) for i in range(w["stack"])])
+    for _ in range(3):
+        y = stack.forward(xr)
+    np.savez(os.path.join(outdir, f"rank{rank}.npz"), y=y.data, mant=y.scale.mant, shift=y.scale.shift, rows=rows)
+    stack = dev = None
+    ctx.sync()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_expert_parallel_slot_stack_equals_the_oracle(tmp_path, oracle):
+    """A stack of three blocks held as weight slots, the experts spread over the GPUs and synthesised there, the
+    exchange over peer memory with CUDA graphs: the ranks' rows together equal the oracle's layer loop."""
+    import torch
+    import torch.multiprocessing as mp
+
+    sys.path.insert(0, os.path.dirname(HERE))
+    import bench
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("expert parallelism needs two or more GPUs")
+    mp.spawn(_stack_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    want, ws = bench.stack_oracle(STACK, oracle, STACK["stack"])
+    ys, scales = [], set()
+    for r in range(world):
+        z = np.load(tmp_path / f"rank{r}.npz")
+        if int(z["rows"]) > 0:
+            ys.append(z["y"].reshape(-1))
+            scales.add((int(z["mant"]), int(z["shift"])))
+    assert scales == {ws}
+    assert (np.concatenate(ys) == want.reshape(-1)).all()

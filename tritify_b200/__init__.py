@@ -27,7 +27,7 @@ from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 
 __all__ = [
     "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
-    "B200Linear", "Context", "DeviceLayer", "MoeStack", "device_count", "synth_normal", "lcg_uniform", "table",
+    "B200Linear", "Context", "DeviceLayer", "LayerSlot", "MoeStack", "device_count", "synth_normal", "synth_normal_portable", "lcg_uniform", "table",
     "KtmoeError",
     "ep_unique_id",
 ]
@@ -357,6 +357,25 @@ class DeviceLayer:
             raise ValueError("the shared-expert gate has d_model codes")
         self.ctx.check(lib().ktmoe_layer_set_shared_gate(self._h, _p(c, ctypes.c_int32), gate[1]._c()))
 
+    def set_depth(self, n_layers: int) -> None:
+        """Hold ``n_layers`` weight slots (a stack of layers of this shape sharing one scratch and exchange)."""
+        self.ctx.check(lib().ktmoe_layer_set_depth(self._h, int(n_layers)))
+
+    def select(self, slot: int) -> None:
+        """Make weight slot ``slot`` the one the setters write and the forwards read."""
+        self.ctx.check(lib().ktmoe_layer_select(self._h, int(slot)))
+
+    def slot(self, i: int) -> "LayerSlot":
+        """Layer ``i`` of this stack of slots, for :class:`MoeStack`."""
+        return LayerSlot(self, i)
+
+    def synth_weights(self, seed: int, sigma: float = 0.02, sigmoid_bias_sigma: float = 0.02,
+                      shared_gate: bool = False) -> None:
+        """Generate and quantise the selected slot's weights on the GPU from the portable stream ``seed`` (router,
+        experts, shared expert, optional shared-expert gate; a sigmoid router's bias from ``seed + 2``)."""
+        self.ctx.check(lib().ktmoe_layer_synth_weights(self._h, int(seed), float(sigma), float(sigmoid_bias_sigma),
+                                                       1 if shared_gate else 0))
+
     def set_norm(self, w_codes: np.ndarray, w_scale: Scale, eps_scale: Scale) -> None:
         """The block's FFN input RmsNorm (RmsNorm::new codes and scales) for block_forward."""
         w = np.ascontiguousarray(w_codes, dtype=np.int32)
@@ -654,6 +673,24 @@ class MoeMlp:
         return [r.experts for r in self.route(x)]
 
 
+class LayerSlot:
+    """Layer ``slot`` of a DeviceLayer that holds a stack of weight slots (``DeviceLayer.set_depth``): its forwards
+    select the slot, then run on the shared layer (a host-side swap: the launches read the slot's weights)."""
+
+    def __init__(self, dev: "DeviceLayer", slot: int):
+        self.dev, self.slot = dev, int(slot)
+        self.ctx, self.d_model = dev.ctx, dev.d_model
+
+    def block_forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int,
+                          stream: int = 0) -> None:
+        self.dev.select(self.slot)
+        self.dev.block_forward_dev(x_ptr, rows, x_scale_ptr, y_ptr, y_scale_ptr, stream)
+
+    def forward_dev(self, x_ptr: int, rows: int, x_scale_ptr: int, y_ptr: int, y_scale_ptr: int, stream: int = 0) -> None:
+        self.dev.select(self.slot)
+        self.dev.forward_dev(x_ptr, rows, x_scale_ptr, y_ptr, y_scale_ptr, stream)
+
+
 class MoeStack:
     """A stack of MoE decoder-block FFN halves with attention excluded (the shape of a GLM-4.5-Air-style model's 45
     MoE layers): for each layer l, x ← add(x, moe_l(rms_norm_l(x))) (kt-core model.rs:175-181), the residual stream
@@ -661,7 +698,8 @@ class MoeStack:
     set (``set_norm``), all on one context; each layer's block is one ``ktmoe_block_forward_dev`` on that context's
     stream (with the layer's CUDA graphs when enabled: the buffers a layer sees are the same on every call)."""
 
-    def __init__(self, layers: Sequence[DeviceLayer]):
+    def __init__(self, layers: Sequence):
+        """``layers``: DeviceLayers, or the LayerSlots of one DeviceLayer with several weight slots."""
         if not layers:
             raise ValueError("a stack needs at least one layer")
         self.layers = list(layers)
@@ -736,6 +774,14 @@ def synth_normal(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray
     cast to f32)."""
     out = np.empty(n, dtype=np.float32)
     check(lib().ktmoe_synth_normal(seed, sigma, offset, n, _p(out, ctypes.c_float)))
+    return out
+
+
+def synth_normal_portable(seed: int, sigma: float, n: int, offset: int = 0) -> np.ndarray:
+    """Elements [offset, offset + n) of the portable N(0, sigma) stream (ktmoe_synth_normal_portable): the stream
+    ``DeviceLayer.synth_weights`` draws on the GPU, here on the host with identical bits."""
+    out = np.empty(n, dtype=np.float32)
+    check(lib().ktmoe_synth_normal_portable(seed, sigma, offset, n, _p(out, ctypes.c_float)))
     return out
 
 

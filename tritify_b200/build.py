@@ -20,7 +20,7 @@ LIB = os.path.join(PKG, "libktmoe.so")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 SOURCES_CU = ["ktmoe.cu", "noalloc.cu"]
 SOURCES_CPP = ["host_prep.cpp", "wire.cpp"]
-HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "digit_gemm_pair.cuh", "moe_kernels.cuh", "ep_peer.cuh",
+HEADERS = ["fixed_point.cuh", "digit_gemm.cuh", "digit_gemm_pair.cuh", "moe_kernels.cuh", "ep_peer.cuh", "synth.cuh",
            "host_prep.h"]
 
 

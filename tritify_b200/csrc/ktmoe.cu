@@ -29,6 +29,7 @@
 #include "host_prep.h"
 #include "ktmoe.h"
 #include "moe_kernels.cuh"
+#include "synth.cuh"
 
 using kt::Scale;
 
@@ -502,6 +503,25 @@ int check_err_word(ktmoe_ctx* ctx) {
 
 // ───────────────────────────── the layer ─────────────────────────────
 
+// The weights of one layer of a stack (ktmoe_layer_set_depth): every buffer and scale the forward reads that differs
+// from one layer to the next. The selected slot's weights live in the layer's own fields (ktmoe_layer_select swaps
+// them in and out); scratch, tables and the expert-parallel exchange are shared by all slots.
+struct WeightSet {
+    Planes w_router, w_gu, w_dn, w_sgu, w_sdn;
+    DevBuf b_router, b_gu, b_dn, b_sgu, b_sdn, b_rbias, b_sigbias, b_wsc, b_norm, b_sgate;
+    std::vector<Scale> h_wsc;
+    std::vector<char> expert_set;
+    Scale router_ws{0, 0}, router_bscale{0, 0}, norm_ws{0, 0}, norm_eps{0, 0}, sgate_ws{0, 0};
+    bool has_rbias = false, router_set = false, shared_set = false, sigbias_set = false, norm_set = false,
+         sgate_set = false;
+};
+
+static void release_weights(WeightSet& w) {
+    DevBuf* bufs[] = {&w.b_router, &w.b_gu, &w.b_dn, &w.b_sgu, &w.b_sdn, &w.b_rbias, &w.b_sigbias, &w.b_wsc,
+                      &w.b_norm, &w.b_sgate};
+    for (DevBuf* b : bufs) b->release();
+}
+
 struct ktmoe_layer {
     ktmoe_ctx* ctx = nullptr;
     ktmoe_layer_config cfg{};
@@ -571,10 +591,15 @@ struct ktmoe_layer {
         cudaGraphExec_t exec;
         uint64_t launches;  // this library's kernels in the graph
         bool block;         // the block forward (norm, layer, residual add) rather than the layer alone
+        int slot;           // the weight slot it ran with
     };
     bool graphs = false;
     std::vector<Graph> graph_cache;
     std::vector<cudaEvent_t> events;
+    // a stack of layers in one object (ktmoe_layer_set_depth): slots[active] is empty while its weights are in the
+    // fields above
+    std::vector<WeightSet> slots;
+    int active = 0;
 };
 
 namespace {
@@ -627,7 +652,7 @@ void graphs_clear(ktmoe_layer* L) {
 
 int ensure_scratch(ktmoe_layer* L, int64_t T) {
     ktmoe_ctx* ctx = L->ctx;
-    if (T <= L->cap && L->cap > 0) return KTMOE_OK;
+    if (T <= L->cap && L->cap > 0 && (!L->sgate_set || L->y_gated.bytes >= (size_t)(T * L->d * 4))) return KTMOE_OK;
     graphs_clear(L);  // the scratch moves: graphs that name it are stale
     const int64_t d = L->d, E = L->E, K = L->K, fs = L->fs;
     T = std::max<int64_t>(T, 1);
@@ -1712,7 +1737,8 @@ int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, in
     auto once = [&]() { return block ? stage_block(L, T, x, xs, y, ys, st) : stage_forward(L, T, x, xs, y, ys, st); };
     if (!L->graphs || L->timing || (L->world > 1 && !L->peer.on)) return once();
     for (auto& g : L->graph_cache)
-        if (g.x == x && g.xs == xs && g.y == y && g.ys == ys && g.T == T && g.st == st && g.block == block) {
+        if (g.x == x && g.xs == xs && g.y == y && g.ys == ys && g.T == T && g.st == st && g.block == block &&
+            g.slot == L->active) {
             CK(cudaGraphLaunch(g.exec, st));
             ctx->launches += g.launches;
             return KTMOE_OK;
@@ -1748,12 +1774,12 @@ int run_forward(ktmoe_layer* L, int64_t T, const int32_t* x, const Scale* xs, in
         L->graphs = false;
         return KTMOE_OK;
     }
-    if (L->graph_cache.size() >= 16) {
+    if (L->graph_cache.size() >= std::max<size_t>(16, 2 * L->slots.size() + 4)) {
         cudaStreamSynchronize(L->graph_cache.front().st);  // no launch of the evicted graph is still in flight
         cudaGraphExecDestroy(L->graph_cache.front().exec);
         L->graph_cache.erase(L->graph_cache.begin());
     }
-    L->graph_cache.push_back({x, xs, y, ys, T, st, exec, n, block});
+    L->graph_cache.push_back({x, xs, y, ys, T, st, exec, n, block, L->active});
     return KTMOE_OK;
 }
 
@@ -2394,12 +2420,14 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                       &L->hs_planes, &L->acc_sd, &L->swiglu_plans, &L->row_hmax, &L->shared_plan,
                       &L->cp_n, &L->cp_common, &L->cp_row, &L->cp_ec, &L->cp_ry, &L->cp_f};
     for (DevBuf* b : bufs) b->release();
-    DevBuf* blk_bufs[] = {&L->b_norm, &L->blk_c, &L->blk_xn, &L->blk_m, &L->blk_sc, &L->blk_u64, &L->blk_off};
+    DevBuf* blk_bufs[] = {&L->b_norm, &L->blk_c, &L->blk_xn, &L->blk_m, &L->blk_sc, &L->blk_u64, &L->blk_off,
+                          &L->b_sgate, &L->sg_acc, &L->sg_code, &L->y_gated};
     for (DevBuf* b : blk_bufs) b->release();
     DevBuf* ep_bufs[] = {&L->ep_counts, &L->ep_counts_all, &L->ep_meta_send, &L->ep_meta_recv, &L->ep_recv_planes,
                          &L->ep_recv_sqx, &L->ep_recv_row_expert, &L->ep_y_send, &L->ep_ys_send, &L->ep_y_back,
                          &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
     for (DevBuf* b : ep_bufs) b->release();
+    for (WeightSet& w : L->slots) release_weights(w);
     graphs_clear(L);
     peer_close(L, L->peer.on);  // an expert-parallel layer is destroyed on every rank
     if (L->comm) ncclCommDestroy(L->comm);
@@ -2481,6 +2509,236 @@ int ktmoe_layer_set_shared(ktmoe_layer* L, const int32_t* gate, ktmoe_scale gate
     L->h_wsc[3 * L->E_local + 2] = S(down_scale);
     if (int r = push_scales(L)) return r;
     L->shared_set = true;
+    return KTMOE_OK;
+}
+
+// ── a stack of layers in one object: weight slots that share the scratch and the exchange ──
+namespace {
+
+void swap_weights(ktmoe_layer* L, WeightSet& w) {
+    using std::swap;
+    swap(L->w_router, w.w_router);
+    swap(L->w_gu, w.w_gu);
+    swap(L->w_dn, w.w_dn);
+    swap(L->w_sgu, w.w_sgu);
+    swap(L->w_sdn, w.w_sdn);
+    swap(L->b_router, w.b_router);
+    swap(L->b_gu, w.b_gu);
+    swap(L->b_dn, w.b_dn);
+    swap(L->b_sgu, w.b_sgu);
+    swap(L->b_sdn, w.b_sdn);
+    swap(L->b_rbias, w.b_rbias);
+    swap(L->b_sigbias, w.b_sigbias);
+    swap(L->b_wsc, w.b_wsc);
+    swap(L->b_norm, w.b_norm);
+    swap(L->b_sgate, w.b_sgate);
+    swap(L->h_wsc, w.h_wsc);
+    swap(L->expert_set, w.expert_set);
+    swap(L->router_ws, w.router_ws);
+    swap(L->router_bscale, w.router_bscale);
+    swap(L->norm_ws, w.norm_ws);
+    swap(L->norm_eps, w.norm_eps);
+    swap(L->sgate_ws, w.sgate_ws);
+    swap(L->has_rbias, w.has_rbias);
+    swap(L->router_set, w.router_set);
+    swap(L->shared_set, w.shared_set);
+    swap(L->sigbias_set, w.sigbias_set);
+    swap(L->norm_set, w.norm_set);
+    swap(L->sgate_set, w.sgate_set);
+}
+
+// One matrix [rows][k] of the portable normal stream `seed` from element `offset`, quantised per tensor as
+// QuantLinear::from_weights does it (layers.rs:225-244) and packed into group g of P from row row0; its Scale out.
+int synth_matrix(ktmoe_ctx* ctx, uint64_t seed, float sigma, uint64_t offset, const Planes& P, int64_t g, int64_t rows,
+                 int64_t k, int64_t row0, DevBuf& fbuf, DevBuf& cbuf, DevBuf& wbuf, Scale* scale) {
+    cudaStream_t st = ctx->stream;
+    const int64_t n = rows * k;
+    CK(fbuf.ensure((size_t)n * 4));
+    CK(cbuf.ensure((size_t)n * 4));
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, ctx->num_sms * 8));
+    sy::portable_normal_kernel<<<grid, 256, 0, st>>>(seed, sigma, offset, n, fbuf.as<float>());
+    CKL(ctx);
+    CK(cudaMemsetAsync(wbuf.p, 0, 4, st));  // the peak; word 1 counts codes out of range over the whole layer
+    sy::absmax_f32_kernel<<<grid, 256, 0, st>>>(fbuf.as<float>(), n, wbuf.as<unsigned>());
+    CKL(ctx);
+    unsigned pbits = 0;
+    CK(cudaMemcpyAsync(&pbits, wbuf.p, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    float peak;
+    std::memcpy(&peak, &pbits, 4);
+    if (peak == 0.0f) {
+        CK(cudaMemsetAsync(cbuf.p, 0, (size_t)n * 4, st));
+        *scale = Scale{0, 0};
+    } else {
+        const double step = (double)peak / (double)kt::WLEVELS;
+        sy::quantize_kernel<<<grid, 256, 0, st>>>(fbuf.as<float>(), n, step, cbuf.as<int32_t>());
+        CKL(ctx);
+        *scale = S(hp::scale_from_f64(step));
+    }
+    int8_t* base = P.ptr + (g * 3) * P.rows_pad * P.k_pad + row0 * P.k_pad;
+    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, st>>>(cbuf.as<int32_t>(), rows, (int)k, (int)P.k_pad, P.rows_pad,
+                                                          base, wbuf.as<unsigned long long>() + 1);
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+}  // namespace
+
+int ktmoe_layer_set_depth(ktmoe_layer* L, int32_t n_layers) {
+    if (!L || n_layers < 1) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (!L->slots.empty()) return fail(ctx, KTMOE_ERR_ARG, "the layer's depth is already set");
+    if (int r = set_device(ctx)) return r;
+    graphs_clear(L);
+    L->slots.resize((size_t)n_layers);  // slot 0 is the weights already in the layer
+    for (int32_t i = 1; i < n_layers; ++i) {
+        WeightSet& w = L->slots[(size_t)i];
+        if (int r = alloc_planes(ctx, w.b_router, w.w_router, 1, L->E, L->d)) return r;
+        if (int r = alloc_planes(ctx, w.b_gu, w.w_gu, L->E_local, 2 * L->f, L->d)) return r;
+        if (int r = alloc_planes(ctx, w.b_dn, w.w_dn, L->E_local, L->d, L->f)) return r;
+        if (L->fs > 0) {
+            if (int r = alloc_planes(ctx, w.b_sgu, w.w_sgu, 1, 2 * L->fs, L->d)) return r;
+            if (int r = alloc_planes(ctx, w.b_sdn, w.w_sdn, 1, L->d, L->fs)) return r;
+        }
+        w.h_wsc.assign(3 * L->E_local + 3, Scale{0, 0});
+        w.expert_set.assign(L->E_local, 0);
+        CK(w.b_wsc.ensure(w.h_wsc.size() * sizeof(Scale)));
+        CK(w.b_rbias.ensure(L->E * 8));
+        CK(w.b_sigbias.ensure(L->E * 8));
+    }
+    L->active = 0;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_select(ktmoe_layer* L, int32_t slot) {
+    if (!L) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    const int32_t n = std::max<int32_t>(1, (int32_t)L->slots.size());
+    if (slot < 0 || slot >= n) return fail(ctx, KTMOE_ERR_ARG, "no such weight slot");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (slot == L->active) return KTMOE_OK;
+    swap_weights(L, L->slots[(size_t)L->active]);  // the current weights back into their slot
+    swap_weights(L, L->slots[(size_t)slot]);
+    L->active = slot;
+    return KTMOE_OK;
+}
+
+int ktmoe_layer_synth_weights(ktmoe_layer* L, uint64_t seed, float sigma, float sigmoid_bias_sigma,
+                              int32_t shared_gate) {
+    if (!L || !(sigma > 0.0f)) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (shared_gate && L->fs <= 0) return fail(ctx, KTMOE_ERR_ARG, "the layer has no shared expert to gate");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    graphs_clear(L);
+    if (int r = set_device(ctx)) return r;
+    const int64_t d = L->d, E = L->E, f = L->f, fs = L->fs;
+    DevBuf fbuf, cbuf, wbuf;
+    auto done = [&](int r) {
+        fbuf.release();
+        cbuf.release();
+        wbuf.release();
+        return r;
+    };
+    CK(wbuf.ensure(16));
+    CK(cudaMemsetAsync(wbuf.p, 0, 16, ctx->stream));
+    Scale sc{0, 0};
+    // one stream: router [E][d], expert e's gate [f][d], up [f][d], down [d][f], then the shared expert's gate, up,
+    // down, then the shared expert's gate [1][d]; this rank draws only its own experts' ranges
+    if (int r = synth_matrix(ctx, seed, sigma, 0, L->w_router, 0, E, d, 0, fbuf, cbuf, wbuf, &sc)) return done(r);
+    L->router_ws = sc;
+    L->has_rbias = false;
+    const uint64_t base = (uint64_t)(E * d), per = (uint64_t)(3 * f * d);
+    for (int64_t le = 0; le < L->E_local; ++le) {
+        const uint64_t o = base + (uint64_t)(L->e_begin + le) * per;
+        if (int r = synth_matrix(ctx, seed, sigma, o, L->w_gu, le, f, d, 0, fbuf, cbuf, wbuf, &sc)) return done(r);
+        L->h_wsc[le] = sc;
+        if (int r = synth_matrix(ctx, seed, sigma, o + f * d, L->w_gu, le, f, d, f, fbuf, cbuf, wbuf, &sc))
+            return done(r);
+        L->h_wsc[L->E_local + le] = sc;
+        if (int r = synth_matrix(ctx, seed, sigma, o + 2 * f * d, L->w_dn, le, d, f, 0, fbuf, cbuf, wbuf, &sc))
+            return done(r);
+        L->h_wsc[2 * L->E_local + le] = sc;
+        L->expert_set[le] = 1;
+    }
+    if (fs > 0) {
+        const uint64_t o = base + (uint64_t)E * per;
+        if (int r = synth_matrix(ctx, seed, sigma, o, L->w_sgu, 0, fs, d, 0, fbuf, cbuf, wbuf, &sc)) return done(r);
+        L->h_wsc[3 * L->E_local] = sc;
+        if (int r = synth_matrix(ctx, seed, sigma, o + fs * d, L->w_sgu, 0, fs, d, fs, fbuf, cbuf, wbuf, &sc))
+            return done(r);
+        L->h_wsc[3 * L->E_local + 1] = sc;
+        if (int r = synth_matrix(ctx, seed, sigma, o + 2 * fs * d, L->w_sdn, 0, d, fs, 0, fbuf, cbuf, wbuf, &sc))
+            return done(r);
+        L->h_wsc[3 * L->E_local + 2] = sc;
+        L->shared_set = true;
+        L->sgate_set = false;
+        if (shared_gate) {
+            // the gate's d codes through the same device quantiser, then into the gate buffer (zero-padded to d_pad)
+            CK(fbuf.ensure((size_t)d * 4));
+            CK(cbuf.ensure((size_t)L->d_pad * 4));
+            sy::portable_normal_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(
+                seed, sigma, o + 3 * fs * d, d, fbuf.as<float>());
+            CKL(ctx);
+            CK(cudaMemsetAsync(wbuf.p, 0, 4, ctx->stream));
+            sy::absmax_f32_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(fbuf.as<float>(), d,
+                                                                                         wbuf.as<unsigned>());
+            CKL(ctx);
+            unsigned pbits = 0;
+            CK(cudaMemcpyAsync(&pbits, wbuf.p, 4, cudaMemcpyDeviceToHost, ctx->stream));
+            CK(cudaStreamSynchronize(ctx->stream));
+            float peak;
+            std::memcpy(&peak, &pbits, 4);
+            CK(cudaMemsetAsync(cbuf.p, 0, (size_t)L->d_pad * 4, ctx->stream));
+            L->sgate_ws = Scale{0, 0};
+            if (peak > 0.0f) {
+                const double step = (double)peak / (double)kt::WLEVELS;
+                sy::quantize_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(fbuf.as<float>(), d, step,
+                                                                                            cbuf.as<int32_t>());
+                CKL(ctx);
+                L->sgate_ws = S(hp::scale_from_f64(step));
+            }
+            CK(L->b_sgate.ensure(L->d_pad * 4));
+            CK(cudaMemcpyAsync(L->b_sgate.p, cbuf.p, L->d_pad * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+            L->sgate_set = true;
+        }
+    }
+    L->router_set = true;
+    if (L->cfg.router_score == 1) {
+        // the sigmoid selection bias: E values of the portable stream seed + 2, coded round(b·2^20) (router.rs:35-51)
+        std::vector<float> b((size_t)E);
+        for (int64_t e = 0; e < E; ++e) b[(size_t)e] = sy::portable_normal(seed + 2, sigmoid_bias_sigma, (uint64_t)e);
+        std::vector<int64_t> codes((size_t)E);
+        hp::code_sigmoid_bias(b.data(), (size_t)E, codes.data());
+        CK(cudaMemcpyAsync(L->b_sigbias.p, codes.data(), E * 8, cudaMemcpyHostToDevice, ctx->stream));
+        L->sigbias_set = true;
+    }
+    CK(cudaMemcpyAsync(L->b_wsc.p, L->h_wsc.data(), L->h_wsc.size() * sizeof(Scale), cudaMemcpyHostToDevice,
+                       ctx->stream));
+    CK(cudaStreamSynchronize(ctx->stream));
+    unsigned long long nbad = 0;
+    CK(cudaMemcpy(&nbad, wbuf.as<unsigned long long>() + 1, 8, cudaMemcpyDeviceToHost));
+    if (nbad) return done(fail(ctx, KTMOE_ERR_RANGE, "a synthesised code lies outside +-WLEVELS"));
+    if (L->sgate_set) L->cap = 0;  // the next forward allocates the gate's scratch
+    return done(KTMOE_OK);
+}
+
+int ktmoe_synth_normal_portable(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out) {
+    if (n < 0 || (n > 0 && !out)) return KTMOE_ERR_ARG;
+    for (int64_t j = 0; j < n; ++j) out[j] = sy::portable_normal(seed, sigma, offset + (uint64_t)j);
+    return KTMOE_OK;
+}
+
+int ktmoe_synth_normal_portable_dev(ktmoe_ctx* ctx, uint64_t seed, float sigma, uint64_t offset, int64_t n,
+                                    float* out_dev) {
+    if (!ctx || n < 0 || (n > 0 && !out_dev)) return KTMOE_ERR_ARG;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (n == 0) return KTMOE_OK;
+    const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, ctx->num_sms * 8));
+    sy::portable_normal_kernel<<<grid, 256, 0, ctx->stream>>>(seed, sigma, offset, n, out_dev);
+    CKL(ctx);
+    CK(cudaStreamSynchronize(ctx->stream));
     return KTMOE_OK;
 }
 
