@@ -181,6 +181,32 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+GEMM_SOURCES = ["tritify_b200/csrc/digit_gemm.cuh", "tritify_b200/csrc/digit_gemm_pair.cuh"]
+
+
+def gemm_sources_sha16():
+    """The first 16 hex digits of the SHA-256 of the GEMM kernels' sources, joined: a committed ncu figure is only
+    valid for the sources it was captured with."""
+    import hashlib
+
+    return "/".join(hashlib.sha256(open(os.path.join(ROOT, p), "rb").read()).hexdigest()[:16] for p in GEMM_SOURCES)
+
+
+def profile_traffic(path, key):
+    """(bytes, source) of a per-launch DRAM figure committed in a profiles/ summary, or (None, why) when the summary
+    was captured with other GEMM sources than the ones built now."""
+    import re
+
+    text = open(path).read()
+    m = re.search(key + r":\s*(\d+)", text)
+    src = re.search(r"gemm_sources_sha16:\s*([0-9a-f/]+)", text)
+    if not m:
+        return None, None
+    if not src or src.group(1) != gemm_sources_sha16():
+        return None, f"stale: {os.path.basename(path)} was captured with other GEMM sources"
+    return int(m.group(1)), f"{os.path.basename(path)} (GEMM sources {src.group(1)})"
+
+
 def measured_peaks():
     try:
         p = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -518,13 +544,10 @@ def run_gemm_ours(args, w, name):
     int8_peak = 2.0 * bf16
     pl = planes.pop() if len(planes) == 1 else -1
     int8_ops = ops * (2 if pl == 1 else 9)  # int8 plane products per code product: (1, 2) planes or (3, 3)
-    traffic = None
+    traffic, traffic_source = None, None
     tpath = os.path.join(ROOT, "profiles", f"digit_gemm_{name}.md")
     if os.path.exists(tpath):
-        import re
-
-        m = re.search(r"dram_bytes_per_launch:\s*(\d+)", open(tpath).read())
-        traffic = int(m.group(1)) if m else None
+        traffic, traffic_source = profile_traffic(tpath, "dram_bytes_per_launch")
     res = {
         "metric": GEMM_METRIC, "value": ops / (g_ms * 1e-3) / 1e12, "unit": "TOPS", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": g_ms, "higher_is_better": True, "scaling": "strong",
@@ -535,6 +558,7 @@ def run_gemm_ours(args, w, name):
                 "h2d_bytes_per_step": N * K * 4, "d2h_bytes_per_step": N * M * 8},
         "roofline": {"bound": "tensor", "achieved": int8_ops / (g_ms * 1e-3) / 1e12, "peak": int8_peak,
                      "unit": "TOPS (int8)", "frac": int8_ops / (g_ms * 1e-3) / 1e12 / int8_peak, "traffic": traffic,
+                     "traffic_source": traffic_source,
                      "kernel": "digit_gemm", "peak_kind": f"2 x bf16 dense, {peak_kind}"},
     }
     if not args.no_cpu:
@@ -834,13 +858,10 @@ def run_ours(args, w, name):
     int8_peak = 2.0 * bf16  # dense int8 : bf16 = 2 : 1 on B200
     achieved = gu_ops / (gu_ms * 1e-3) / 1e12
     # DRAM bytes per gate/up launch from the committed ncu summary of this workload (null when none is committed)
-    traffic = None
+    traffic, traffic_source = None, None
     tpath = os.path.join(ROOT, "profiles", f"digit_gemm_{name}.md")
     if os.path.exists(tpath) and not args.tokens and not args.experts and world == 1:
-        import re
-
-        m = re.search(r"gemm_gate_up_dram_bytes_per_launch:\s*(\d+)", open(tpath).read())
-        traffic = int(m.group(1)) if m else None
+        traffic, traffic_source = profile_traffic(tpath, "gemm_gate_up_dram_bytes_per_launch")
 
     value = T_all / (ms * 1e-3)
     if w.get("decode"):
@@ -853,7 +874,8 @@ def run_ours(args, w, name):
                     "peak_source": f"{peak_kind} HBM copy bandwidth"}
     else:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": int8_peak, "unit": "TOPS (int8)",
-                    "frac": achieved / int8_peak, "traffic": traffic, "kernel": "digit_gemm gate/up",
+                    "frac": achieved / int8_peak, "traffic": traffic, "traffic_source": traffic_source,
+                    "kernel": "digit_gemm gate/up",
                     "peak_source": f"2 x {peak_kind} bf16 {bf16:.0f} TF/s (B200 dense int8:bf16 = 2:1)",
                     "ops_per_launch": gu_ops, "plane_products": P_PLANES}
     res = {
