@@ -59,12 +59,15 @@ def test_decode_and_config1_workloads_equal_the_golden(ctx, name, monkeypatch):
     # both SwiGLU element kernels: a block per row, and a cluster per row with h in registers (both thread shapes)
     _run(ctx, name, monkeypatch, [{"KTMOE_SWIGLU_CLUSTER": "0"},
                                   {"KTMOE_SWIGLU_CLUSTER": "1", "KTMOE_SWIGLU_SHAPE": "2x256"},
-                                  {"KTMOE_SWIGLU_CLUSTER": "1", "KTMOE_SWIGLU_SHAPE": "4x128"}])
+                                  {"KTMOE_SWIGLU_CLUSTER": "1", "KTMOE_SWIGLU_SHAPE": "4x128"},
+                                  {"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_PAIR_ZERO_MMA": "1"},
+                                  {"KTMOE_PAIR_ZERO_MMA": "0"}])
 
 
 @pytest.mark.parametrize("name", ["qwen_prefill", "mixtral_prefill", "mixtral_zipf", "glm_prefill"])
 def test_prefill_workloads_equal_the_golden(ctx, name, monkeypatch):
-    variants = [{"KTMOE_SWIGLU_CLUSTER": "0"}]
+    # the pair GEMM with the epilogue zeroing the accumulator, and with the clearing MMA
+    variants = [{"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_PAIR_ZERO_MMA": "0"}, {"KTMOE_PAIR_ZERO_MMA": "1"}]
     if name == "mixtral_prefill":
         variants.append({"KTMOE_SWIGLU_CLUSTER": "1"})  # the 14336-wide rows on 8-CTA clusters as well
     _run(ctx, name, monkeypatch, variants)

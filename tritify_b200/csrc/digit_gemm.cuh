@@ -65,6 +65,9 @@ struct GemmArgs {
     // Split K: k_splits > 1 blocks share a tile, each over its own K range, and add their partial results into `out`
     // with 64-bit atomics (integer sums: exact in any order; `out` starts at zero; no fused row maxima).
     int k_splits;
+    // Pair kernel only: 1 clears diagonals 2-4 of a tile's accumulator with one MMA of a zero B operand at its first
+    // K step, so the epilogue releases TMEM without zeroing it (0: the epilogue zeroes diagonals 3-4).
+    int zero_mma;
 };
 
 // PX, PW: digit planes of the activations and the weights per stage (3, 3 for any code; 1, 2 for small codes).

@@ -13,7 +13,9 @@
 // (CTA 0 only). One accumulator buffer (5·64 = 320 of 512 columns): the epilogue loads its whole share of the
 // accumulator into registers, zeroes diagonals 3 and 4 (the next tile's first K step overwrites 0-2 and accumulates
 // into 3-4), and releases TMEM before it recombines and stores, so the MMAs of the next tile wait only for the
-// TMEM reads. No load uses cluster multicast; every wait is bounded as in the one-SM kernel.
+// TMEM reads. With args.zero_mma the MMA issuer clears diagonals 2-4 itself at a tile's first K step (one MMA whose
+// B operand is an all-zero tile in shared memory, 1/384 of the tile's tensor work) and the epilogue skips its TMEM
+// stores, which shortens the time the accumulator is held. No load uses cluster multicast; every wait is bounded as in the one-SM kernel.
 #pragma once
 
 #include "digit_gemm.cuh"
@@ -34,7 +36,8 @@ constexpr int B_STAGE = HALF_ROWS * BK;                // 12 KB
 constexpr int CTA_STAGE_BYTES = 3 * A_PLANE + B_STAGE;  // what one CTA's copies of a stage bring
 constexpr int ACC_COLS = NDIAG * BN;                   // 320
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = 1024 + STAGES * CTA_STAGE_BYTES + 256;
+constexpr int ZERO_B = B_STAGE;                        // an all-zero B tile: the operand of the clearing MMA
+constexpr int SMEM_BYTES = 1024 + STAGES * CTA_STAGE_BYTES + ZERO_B + 256;
 static_assert(SMEM_BYTES <= 232448, "shared memory per block");
 static_assert(B_STAGE % 1024 == 0 && A_PLANE % 1024 == 0, "swizzle atoms stay 1024-byte aligned");
 
@@ -183,7 +186,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;                                  // [STAGES][3][128 rows][BK]
     uint8_t* sB = smem + STAGES * 3 * A_PLANE;           // [STAGES][96 rows][BK]
-    uint64_t* full = (uint64_t*)(smem + STAGES * CTA_STAGE_BYTES);
+    uint8_t* sZ = smem + STAGES * CTA_STAGE_BYTES;       // [96 rows][BK] of zeros
+    uint64_t* full = (uint64_t*)(sZ + ZERO_B);
     uint64_t* empty = full + STAGES;
     uint64_t* acc_full = empty + STAGES;   // this CTA's accumulator half is complete (commit from CTA 0)
     uint64_t* acc_empty = acc_full + 1;    // CTA 0: both CTAs' epilogues have read the accumulator (16 warp arrivals)
@@ -200,6 +204,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = args.num_k_blocks;
 
+    const bool zero_mma = args.zero_mma != 0;
+    if (zero_mma) {
+        // the clearing MMA reads this tile through the async proxy: write it, then make it visible there
+        for (int i = threadIdx.x; i < ZERO_B / 16; i += blockDim.x) ((uint4*)sZ)[i] = make_uint4(0, 0, 0, 0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -284,6 +294,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
                     asm volatile("tcgen05.fence::after_thread_sync;");
                     const uint32_t a_base = smem_u32(sA + s * 3 * A_PLANE);
                     const uint32_t b_base = smem_u32(sB + s * B_STAGE);
+                    if (zero_mma && kb == 0)  // diagonals 2-4 := A·0; plane 0 then overwrites 0-2, planes 1-2 add
+                        umma_i8_pair(tmem + 2 * BN, smem_desc_sw128(a_base), smem_desc_sw128(smem_u32(sZ)), id, 0u);
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; ++kk) {
                         const uint64_t bd = smem_desc_sw128(b_base + kk * UMMA_K);
@@ -306,12 +318,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
         // Epilogue: warp w reads TMEM lanes 32·(w%4).. (weight rows) and columns 32·(w/4).. (activation rows).
         const int quad = warp & 3, chalf = warp >> 2;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-        // Before the first tile: zero diagonals 3 and 4 and release the accumulator.
-        tmem_st16_zero(lane_base + 3 * BN + chalf * 32);
-        tmem_st16_zero(lane_base + 3 * BN + chalf * 32 + 16);
-        tmem_st16_zero(lane_base + 4 * BN + chalf * 32);
-        tmem_st16_zero(lane_base + 4 * BN + chalf * 32 + 16);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        // Before the first tile: zero diagonals 3 and 4 (unless the MMAs clear them) and release the accumulator.
+        if (!zero_mma) {
+            tmem_st16_zero(lane_base + 3 * BN + chalf * 32);
+            tmem_st16_zero(lane_base + 3 * BN + chalf * 32 + 16);
+            tmem_st16_zero(lane_base + 4 * BN + chalf * 32);
+            tmem_st16_zero(lane_base + 4 * BN + chalf * 32 + 16);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
         asm volatile("tcgen05.fence::before_thread_sync;");
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(acc_empty_leader);
@@ -341,11 +355,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[c * 16 + j] = kt::recombine(s0[j], s1[j], s2[j], s3[j], s4[j]);
                 }
-                tmem_st16_zero(lane_base + 3 * BN + chalf * 32);
-                tmem_st16_zero(lane_base + 3 * BN + chalf * 32 + 16);
-                tmem_st16_zero(lane_base + 4 * BN + chalf * 32);
-                tmem_st16_zero(lane_base + 4 * BN + chalf * 32 + 16);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                if (!zero_mma) {
+                    tmem_st16_zero(lane_base + 3 * BN + chalf * 32);
+                    tmem_st16_zero(lane_base + 3 * BN + chalf * 32 + 16);
+                    tmem_st16_zero(lane_base + 4 * BN + chalf * 32);
+                    tmem_st16_zero(lane_base + 4 * BN + chalf * 32 + 16);
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                }
             }
             // the accumulator is in registers: the next tile's MMAs may start
             asm volatile("tcgen05.fence::before_thread_sync;");
@@ -372,13 +388,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
             if (do_max) {
                 const int n = chalf * 32 + lane;  // the column whose maximum this lane ends up holding
                 const bool one_slot = __all_sync(0xffffffffu, my_slot == __shfl_sync(0xffffffffu, my_slot, 0));
-#pragma unroll 1
-                for (int sl = 0; sl < 2; ++sl) {
-                    if (one_slot && sl != my_slot) continue;
-                    unsigned long long bv[32];
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) bv[j] = my_slot == sl ? av[j] : 0ull;
-                    unsigned long long mx = lane_max_transpose(bv, lane);
+                auto publish = [&](unsigned long long mx, int sl) {
                     if (n >= ti.n_valid) mx = 0;
                     if (args.rowmax_stride == 0) {
                         // one word for the whole output: reduce the warp's columns first (one atomic per warp)
@@ -390,6 +400,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
                         if (lane == 0 && mx) atomicMax(args.rowmax + sl, mx);
                     } else if (mx) {
                         atomicMax(args.rowmax + (long long)(ti.row0 + n) * args.rowmax_stride + sl, mx);
+                    }
+                };
+                if (one_slot) {
+                    // the warp's 32 weight rows lie on one side of rowmax_split (the usual case): reduce in place
+                    publish(lane_max_transpose(av, lane), my_slot);
+                } else {
+#pragma unroll 1
+                    for (int sl = 0; sl < 2; ++sl) {
+                        unsigned long long bv[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) bv[j] = my_slot == sl ? av[j] : 0ull;
+                        publish(lane_max_transpose(bv, lane), sl);
                     }
                 }
             }

@@ -399,6 +399,10 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         a.rowmax_stride = g.rowmax_stride;
         a.rowmax_split = (int)std::min<int64_t>(g.rowmax_split, INT32_MAX);
         a.k_splits = ks;
+        {
+            const char* ze = getenv("KTMOE_PAIR_ZERO_MMA");
+            a.zero_mma = (ze && ze[0] == '1') ? 1 : 0;
+        }
         if (pair) {
             r = launch_gemm_pair(ctx, st, ma, mb, m_tiles * group_n * n_groups, a);
             if (r) return r;
