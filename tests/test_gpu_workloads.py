@@ -70,4 +70,5 @@ def test_prefill_workloads_equal_the_golden(ctx, name, monkeypatch):
     variants = [{"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_PAIR_ZERO_MMA": "0"}, {"KTMOE_PAIR_ZERO_MMA": "1"}]
     if name == "mixtral_prefill":
         variants.append({"KTMOE_SWIGLU_CLUSTER": "1"})  # the 14336-wide rows on 8-CTA clusters as well
+        variants.append({"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_SWIGLU_U": "2"})  # and two elements per thread step
     _run(ctx, name, monkeypatch, variants)
