@@ -1055,8 +1055,11 @@ def run_stack(args, w, name):
         g = json.load(open(GOLDEN_PATH)).get("workloads", {}).get(name)
     except (OSError, ValueError):
         g = None
-    parity = "no golden" if g is None else ("golden" if all(head_hash[k] == g["output"][k] for k in
-                                                            ("data_sha256", "repro_sha256")) else "MISMATCH")
+    if g is None or g.get("T") != T_all or L < g.get("layers_checked", STACK_CHECK_LAYERS):
+        parity = "no golden"
+    else:
+        parity = "golden" if all(head_hash[k] == g["output"][k] for k in ("data_sha256", "repro_sha256")) \
+            else "MISMATCH"
 
     stack = tb.MoeStack([dev.slot(i) for i in range(L)])
 
