@@ -1105,21 +1105,29 @@ def run_stack(args, w, name):
     xh.numpy()[:] = x.data
     yh = torch.empty(T * d, dtype=torch.int32, pin_memory=True)
 
+    # the copies run on torch's stream (whose lifetime torch owns) and are ordered against the library's stream by
+    # events: the stack waits for the tokens, the read-back waits for the stack
+    torch_stream = torch.cuda.current_stream()
+    ev_in, ev_out = torch.cuda.Event(), torch.cuda.Event()
+
     def e2e_step():
-        with torch.cuda.stream(stream):
-            xd.copy_(xh, non_blocking=True)
-            step()
-            yh.copy_(yd, non_blocking=True)
+        xd.copy_(xh, non_blocking=True)
+        ev_in.record(torch_stream)
+        stream.wait_event(ev_in)
+        step()
+        ev_out.record(stream)
+        torch_stream.wait_event(ev_out)
+        yh.copy_(yd, non_blocking=True)
 
     e2e_step()
-    ctx.sync()
+    torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_steps = max(3, args.steps // 2)
     barrier()
-    e_start.record(stream)
+    e_start.record(torch_stream)
     for _ in range(e_steps):
         e2e_step()
-    e_end.record(stream)
+    e_end.record(torch_stream)
     e_end.synchronize()
     e2e_ms = e_start.elapsed_time(e_end) / e_steps
     if dist is not None:
@@ -1162,10 +1170,12 @@ def run_stack(args, w, name):
     }
     stack = head = None
     dev = None
+    torch.cuda.synchronize()
     ctx.sync()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+    ctx.close()  # after every torch tensor that ran on its stream is done
     if rank == 0:
         print(json.dumps(res), flush=True)
         if parity == "MISMATCH":
