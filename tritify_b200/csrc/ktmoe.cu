@@ -1297,6 +1297,14 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
 
 // The shared expert on the whole tensor (layers.rs:758-780; its QuantLinears see the whole [rows, dim] input, so its
 // maxima are global): everything up to the down accumulators and their max, on stream `st`.
+// The token tile of one of the shared expert's GEMMs (one matrix of M weight rows over all T tokens): the SM pair
+// when its 256-row tiles give at least half as many clusters as there are SMs, otherwise the one-SM kernel, which
+// splits K across the idle SMs when its own tiles are too few (decode: the Qwen shared down GEMM went from 16 CTAs).
+int shared_bn(const ktmoe_ctx* ctx, int64_t M, int64_t T) {
+    const int64_t pair_clusters = (M + dg::pair::BM2 - 1) / dg::pair::BM2 * ((T + dg::pair::BN - 1) / dg::pair::BN);
+    return pick_bn((double)T, 2 * pair_clusters >= ctx->num_sms);
+}
+
 int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t d = L->d, fs = L->fs;
@@ -1321,7 +1329,7 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
         s.out = L->acc_sgu.as<int64_t>();
         s.ld_out = 2 * fs;
-        s.BN = pick_bn((double)T, true);
+        s.BN = shared_bn(ctx, 2 * fs, T);
         s.grid_y = (T + s.BN - 1) / s.BN;
         s.single_rows = T;
         s.rowmax = scal_u64(L, U_SYG);  // [U_SYG] gate, [U_SYU] up: maxima over the whole tensor
@@ -1367,6 +1375,8 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         s.A = L->w_sdn;
         s.M_valid = d;
         s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
+        s.BN = shared_bn(ctx, d, T);
+        s.grid_y = (T + s.BN - 1) / s.BN;
         s.out = L->acc_sd.as<int64_t>();
         s.ld_out = d;
         s.rowmax = scal_u64(L, U_SYD);
