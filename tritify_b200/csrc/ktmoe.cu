@@ -880,6 +880,20 @@ struct ExpertRows {
     const int* n_rows_dev = nullptr;  // rows counted on the device (n_rows is then an upper bound)
 };
 
+// The SwiGLU element pass for wide rows (h beyond one block's shared-memory budget): KTMOE_SWIGLU_SLICE=1 splits a row
+// over a cluster of swiglu_slices(L) CTAs with h in shared memory (mk::swiglu_slice_kernel).
+bool swiglu_slice_enabled() {
+    const char* e = getenv("KTMOE_SWIGLU_SLICE");
+    return e && e[0] == '1';
+}
+
+// The fewest CTAs (a power of two, at most 8) whose slices of f_pad elements hold h in 60 KB each; 0 if none does.
+int swiglu_slices(const ktmoe_layer* L) {
+    for (int c = 1; c <= 8; c *= 2)
+        if (L->f_pad % (4 * c) == 0 && (L->f_pad / c) * 8 <= 60 * 1024) return c;
+    return 0;
+}
+
 int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
     const int64_t d = L->d, f = L->f, R = x.n_rows;
@@ -964,6 +978,30 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
             CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<2, 256>, sa));
         else
             CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<4, 128>, sa));
+        CKL(ctx);
+    } else if (swiglu_slice_enabled() && L->swiglu_smem == 0 && swiglu_slices(L) > 0) {
+        // a wide row (h does not fit one block's budget) split over a cluster, h in shared memory
+        const int C = swiglu_slices(L);
+        const size_t smem = (size_t)(L->f_pad / C) * 8;
+        static bool attr_set[64] = {};
+        if (!attr_set[ctx->device & 63]) {
+            CK(cudaFuncSetAttribute(mk::swiglu_slice_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)(60 * 1024)));
+            attr_set[ctx->device & 63] = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(R * C));
+        cfg.blockDim = dim3(256);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = (unsigned)C;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        CK(cudaLaunchKernelEx(&cfg, mk::swiglu_slice_kernel<4>, sa));
         CKL(ctx);
     } else {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
@@ -1297,12 +1335,14 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
 
 // The shared expert on the whole tensor (layers.rs:758-780; its QuantLinears see the whole [rows, dim] input, so its
 // maxima are global): everything up to the down accumulators and their max, on stream `st`.
-// The token tile of one of the shared expert's GEMMs (one matrix of M weight rows over all T tokens): the SM pair
-// when its 256-row tiles give at least half as many clusters as there are SMs, otherwise the one-SM kernel, which
-// splits K across the idle SMs when its own tiles are too few (decode: the Qwen shared down GEMM went from 16 CTAs).
+// The token tile of one of the shared expert's GEMMs (one matrix of M weight rows over all T tokens). Routing the
+// decode-sized ones to the one-SM kernel with split K when the pair's tiles fill few SMs measured no faster (Qwen
+// decode: shared stage 0.170 against 0.159 ms; the split adds a memset, atomics and a row-max pass), so the pair
+// keeps every launch of 64 tokens and more.
 int shared_bn(const ktmoe_ctx* ctx, int64_t M, int64_t T) {
-    const int64_t pair_clusters = (M + dg::pair::BM2 - 1) / dg::pair::BM2 * ((T + dg::pair::BN - 1) / dg::pair::BN);
-    return pick_bn((double)T, 2 * pair_clusters >= ctx->num_sms);
+    (void)ctx;
+    (void)M;
+    return pick_bn((double)T, true);
 }
 
 int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {

@@ -843,6 +843,78 @@ __global__ void __launch_bounds__(NT, 2048 / (NT * G)) swiglu_cluster_kernel(con
     if (rank == 0 && threadIdx.x == 0) a.row_hmax[r] = hmu;
 }
 
+// ── Phase 0 for wide rows on a cluster, h in shared memory ──
+// Row r = %clusterid.x is split into C = %cluster_nctarank contiguous slices of f_pad / C elements (f_pad is a multiple
+// of 128, so every slice is a multiple of 4 long); CTA c keeps its slice's h in dynamic shared memory (f_pad / C · 8
+// bytes: 57 KB for Mixtral's 14336 on 2 CTAs, which leaves room for 3 CTAs per SM), so phase 2 reads h from shared
+// memory instead of back from L2. The row's max |h| is reduced over the CTA, then over the cluster through distributed
+// shared memory between two cluster barriers. U elements per thread per step as in swiglu_rows_kernel.
+template <int U>
+__global__ void __launch_bounds__(256, 3) swiglu_slice_kernel(const SwigluArgs a) {
+    extern __shared__ int64_t hs[];
+    __shared__ uint64_t red[32];
+    __shared__ uint64_t part[8];
+    const int r = (int)cluster_id_x();
+    if (r >= swiglu_rows(a)) return;  // the same for every CTA of the cluster
+    const uint32_t C = cluster_size(), rank = cluster_rank();
+    cluster_arrive_relaxed();
+    const int f = a.f, slice = a.f_pad / (int)C, k0 = (int)rank * slice;
+    const int k_end = min(f, k0 + slice);  // the slice's data elements [k0, k_end); the rest is padding
+    const int64_t* accg = a.acc + (long long)r * 2 * f;
+    const int64_t* accu = accg + f;
+    const SwigluScales q = a.plans[r];
+    uint64_t hm = 0;
+    int k = k0 + threadIdx.x;
+    if (q.fast) {
+        const int32_t base = (int32_t)-a.silu.lo_index;
+        for (; k + (U - 1) * (int)blockDim.x < k_end; k += U * blockDim.x) {
+            int64_t gv[U], uv[U];
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                gv[j] = __ldcs(accg + k + j * blockDim.x);
+                uv[j] = __ldcs(accu + k + j * blockDim.x);
+            }
+#pragma unroll
+            for (int j = 0; j < U; ++j) {
+                const int64_t v = swiglu_h_fast(q, a.silu.codes32, base, gv[j], uv[j]);
+                hs[k - k0 + j * blockDim.x] = v;
+                hm = max(hm, uabs64(v));
+            }
+        }
+    }
+    for (; k < k_end; k += blockDim.x) {
+        const int64_t v = swiglu_h(a, q, accg[k], accu[k]);
+        hs[k - k0] = v;
+        hm = max(hm, uabs64(v));
+    }
+    const uint64_t bm = block_max_u64(hm, red);  // its barriers also publish hs
+    cluster_wait_acquire();
+    if (threadIdx.x == 0)
+        for (uint32_t c = 0; c < C; ++c) st_cluster_u64(&part[rank], c, bm);
+    cluster_arrive_release();
+    cluster_wait_acquire();
+    uint64_t hmu = 0;
+    for (uint32_t c = 0; c < C; ++c) hmu = max(hmu, part[c]);
+    const int64_t hmax = (int64_t)hmu;
+    const kt::ReqDiv rh = kt::make_req(hmax);
+    int8_t* p0 = a.planes + (long long)r * a.f_pad;
+    int8_t* p1 = p0 + a.R_pad * a.f_pad;
+    int8_t* p2 = p1 + a.R_pad * a.f_pad;
+    for (int k4 = k0 + threadIdx.x * 4; k4 < k0 + slice; k4 += blockDim.x * 4) {
+        int32_t qv[4];
+        if (rh.dbl) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) qv[j] = k4 + j < f ? down_code_fast(hs[k4 + j - k0], rh) : 0;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                qv[j] = (k4 + j < f && hmax > 0) ? kt::quant_to_act(kt::requant_row(hs[k4 + j - k0], rh)) : 0;
+        }
+        store_digits4(p0 + k4, p1 + k4, p2 + k4, qv);
+    }
+    if (rank == 0 && threadIdx.x == 0) a.row_hmax[r] = hmu;
+}
+
 // Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase; one plan).
 __global__ void swiglu_global_kernel(const SwigluArgs a) {
     __shared__ uint64_t red[32];
