@@ -155,6 +155,16 @@ int ktmoe_layer_synth_weights(ktmoe_layer* layer, uint64_t seed, float sigma, fl
 /* Module::forward_int: x [rows][d_model] at x_scale -> y [rows][d_model] at *y_scale. Host buffers; synchronous. */
 int ktmoe_forward(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
                   ktmoe_scale* y_scale);
+/* The same, asynchronous: enqueues the upload of x (and x_scale), the forward and the download of y (and the scale
+ * into *y_scale) and returns at once. Two calls can be in flight: the layer keeps two slots of device buffers, an
+ * upload and a download stream, so one call's copies overlap the forward of the one before or after it (PCIe runs both
+ * ways at once). A call waits only for the call two back, which used the same slot. x must stay unchanged and y and
+ * *y_scale unread until ktmoe_forward_async_wait returns; give pinned host memory, or the copies stage through the
+ * driver and overlap nothing. No counterpart in the reference (its CPU path has no copies). */
+int ktmoe_forward_async(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                        ktmoe_scale* y_scale);
+/* Wait for every ktmoe_forward_async of the layer; the first error of any of them. */
+int ktmoe_forward_async_wait(ktmoe_layer* layer);
 /* The same on device buffers, ordered on `stream` (NULL: the context stream) and not synchronised: x_dev and y_dev
  * hold rows x d_model int32, x_scale_dev and y_scale_dev one ktmoe_scale each. Kernel errors surface on the next
  * ktmoe_sync. */

@@ -202,3 +202,34 @@ def test_graph_replays_equal_the_uncaptured_forward(ctx, name):
             assert (y.data == want[0].data).all() and y.scale == want[0].scale
     finally:
         dev.set_graphs(False)
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_async_forwards_equal_the_synchronous_ones(ctx, graphs):
+    """ktmoe_forward_async: five back-to-back calls on different inputs (and row counts) from pinned host buffers, two
+    in flight at a time, then one wait; every output and scale equals the synchronous ktmoe_forward's."""
+    import dataclasses
+
+    import torch
+
+    c = cases.CASES["small_shared_softmax"]
+    dev = cases.build_layer(c, ctx).device_layer()
+    dev.set_graphs(graphs)
+    inputs, want = [], []
+    for i, rows in enumerate([c.T, c.T, c.T - 5, c.T, 7]):
+        ci = dataclasses.replace(c, T=rows, xseed=c.xseed + 100 + i)
+        x = tb.IntTensor.from_reals(cases.make_x(ci))
+        inputs.append((x, rows))
+        want.append(dev.forward(x.data, rows, x.scale))
+    xh = [torch.from_numpy(x.data.copy()).pin_memory() for x, _ in inputs]
+    yh = [torch.empty(rows * c.d, dtype=torch.int32).pin_memory() for _, rows in inputs]
+    ys = [tb.KtmoeScale() for _ in inputs]
+    try:
+        for (x, rows), xb, yb, sc in zip(inputs, xh, yh, ys):
+            dev.forward_async(xb.data_ptr(), rows, x.scale, yb.data_ptr(), sc)
+        dev.forward_async_wait()
+        for (y, s), yb, sc in zip(want, yh, ys):
+            assert (int(sc.mant), int(sc.shift)) == (s.mant, s.shift)
+            assert (yb.numpy() == y).all()
+    finally:
+        dev.set_graphs(False)

@@ -403,6 +403,16 @@ class DeviceLayer:
                                            ctypes.byref(ys)))
         return y, Scale._of(ys)
 
+    def forward_async(self, x_ptr: int, rows: int, x_scale: Scale, y_ptr: int, y_scale: "KtmoeScale") -> None:
+        """ktmoe_forward_async on host buffers given as raw pointers (pinned memory for the copies to overlap): returns
+        at once; ``y`` and ``y_scale`` hold the result after ``forward_async_wait``."""
+        self.ctx.check(lib().ktmoe_forward_async(self._h, ctypes.cast(x_ptr, ctypes.POINTER(ctypes.c_int32)), rows,
+                                                 x_scale._c(), ctypes.cast(y_ptr, ctypes.POINTER(ctypes.c_int32)),
+                                                 ctypes.byref(y_scale)))
+
+    def forward_async_wait(self) -> None:
+        self.ctx.check(lib().ktmoe_forward_async_wait(self._h))
+
     def set_graphs(self, enable: bool) -> None:
         """Capture the forward in CUDA graphs (per buffers, rows and stream) and replay them."""
         self.ctx.check(lib().ktmoe_layer_set_graphs(self._h, 1 if enable else 0))

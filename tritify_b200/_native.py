@@ -73,6 +73,8 @@ SIGNATURES = {
     "ktmoe_layer_set_expert": ([_vp, _i32, _i32p, KtmoeScale, _i32p, KtmoeScale, _i32p, KtmoeScale], ctypes.c_int),
     "ktmoe_layer_set_shared": ([_vp, _i32p, KtmoeScale, _i32p, KtmoeScale, _i32p, KtmoeScale], ctypes.c_int),
     "ktmoe_layer_set_shared_gate": ([_vp, _i32p, KtmoeScale], ctypes.c_int),
+    "ktmoe_forward_async": ([_vp, _i32p, _i64, KtmoeScale, _i32p, ctypes.POINTER(KtmoeScale)], ctypes.c_int),
+    "ktmoe_forward_async_wait": ([_vp], ctypes.c_int),
     "ktmoe_layer_set_depth": ([_vp, _i32], ctypes.c_int),
     "ktmoe_layer_select": ([_vp, _i32], ctypes.c_int),
     "ktmoe_layer_synth_weights": ([_vp, _u64, ctypes.c_float, ctypes.c_float, _i32], ctypes.c_int),

@@ -604,6 +604,18 @@ struct ktmoe_layer {
     // fields above
     std::vector<WeightSet> slots;
     int active = 0;
+    // asynchronous host-buffer forwards (ktmoe_forward_async): two slots of device buffers, an upload and a download
+    // stream ordered against the context stream by events, so one call's copies overlap another's forward
+    struct Async {
+        bool init = false;
+        cudaStream_t up = nullptr, down = nullptr;
+        DevBuf x[2], y[2], sc;  // sc: per slot {x scale, y scale}
+        HostBuf hsc;            // pinned: per slot {x scale, y scale}
+        cudaEvent_t ev_up[2] = {}, ev_fwd[2] = {}, ev_down[2] = {};
+        bool pending[2] = {false, false};
+        ktmoe_scale* ys_out[2] = {nullptr, nullptr};
+        uint64_t calls = 0;
+    } as;
 };
 
 namespace {
@@ -2459,6 +2471,10 @@ int ktmoe_check_wait_expiry(ktmoe_ctx* ctx) {
     return check_err_word(ctx);  // KTMOE_ERR_KERNEL with the wait's code; the error word is cleared
 }
 
+namespace {
+void async_release(ktmoe_layer* L);  // the asynchronous forwards' streams, events and buffers (defined below)
+}
+
 int ktmoe_layer_destroy(ktmoe_layer* L) {
     if (!L) return KTMOE_ERR_ARG;
     ktmoe_ctx* ctx = L->ctx;
@@ -2482,6 +2498,7 @@ int ktmoe_layer_destroy(ktmoe_layer* L) {
                          &L->ep_ys_back, &L->ep_tiles, &L->ep_runs, &L->ep_rec, &L->ep_recs, &L->ep_best_idx};
     for (DevBuf* b : ep_bufs) b->release();
     for (WeightSet& w : L->slots) release_weights(w);
+    async_release(L);
     graphs_clear(L);
     peer_close(L, L->peer.on);  // an expert-parallel layer is destroyed on every rank
     if (L->comm) ncclCommDestroy(L->comm);
@@ -2859,6 +2876,112 @@ int ktmoe_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_
     if (int r = check_err_word(ctx)) return r;
     *y_scale = C(ys);
     return KTMOE_OK;
+}
+
+// ── asynchronous host-buffer forwards ──
+namespace {
+
+int async_init(ktmoe_layer* L) {
+    ktmoe_ctx* ctx = L->ctx;
+    auto& a = L->as;
+    if (a.init) return KTMOE_OK;
+    CK(cudaStreamCreateWithFlags(&a.up, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&a.down, cudaStreamNonBlocking));
+    for (int s = 0; s < 2; ++s) {
+        CK(cudaEventCreateWithFlags(&a.ev_up[s], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&a.ev_fwd[s], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&a.ev_down[s], cudaEventDisableTiming));
+    }
+    CK(a.sc.ensure(4 * sizeof(Scale)));
+    CK(a.hsc.ensure(4 * sizeof(Scale)));
+    a.init = true;
+    return KTMOE_OK;
+}
+
+// Complete slot s's call: wait for its download, hand its output scale to the caller.
+int async_finish(ktmoe_layer* L, int s) {
+    ktmoe_ctx* ctx = L->ctx;
+    auto& a = L->as;
+    if (!a.pending[s]) return KTMOE_OK;
+    a.pending[s] = false;
+    CK(cudaEventSynchronize(a.ev_down[s]));
+    const Scale ys = ((const Scale*)a.hsc.p)[2 * s + 1];
+    if (a.ys_out[s]) *a.ys_out[s] = C(ys);
+    return KTMOE_OK;
+}
+
+void async_release(ktmoe_layer* L) {
+    auto& a = L->as;
+    if (!a.init) return;
+    if (a.up) cudaStreamSynchronize(a.up);
+    if (a.down) cudaStreamSynchronize(a.down);
+    for (int s = 0; s < 2; ++s) {
+        cudaEventDestroy(a.ev_up[s]);
+        cudaEventDestroy(a.ev_fwd[s]);
+        cudaEventDestroy(a.ev_down[s]);
+        a.x[s].release();
+        a.y[s].release();
+    }
+    a.sc.release();
+    a.hsc.release();
+    cudaStreamDestroy(a.up);
+    cudaStreamDestroy(a.down);
+    a.init = false;
+}
+
+}  // namespace
+
+int ktmoe_forward_async(ktmoe_layer* L, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* y,
+                        ktmoe_scale* y_scale) {
+    if (!L || !y_scale || rows < 0 || (rows == 0 && L->world == 1)) return KTMOE_ERR_ARG;
+    if (L->peer.on && rows > L->peer.cap_T) return fail(L->ctx, KTMOE_ERR_ARG, "more rows than the EP capacity");
+    if (rows > 0 && (!x || !y)) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    if (!layer_complete(L)) return fail(ctx, KTMOE_ERR_STATE, "a weight of the layer is not set");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (int r = async_init(L)) return r;
+    auto& a = L->as;
+    const int s = (int)(a.calls++ & 1);
+    if (int r = async_finish(L, s)) return r;  // the call two back used this slot
+    if (int r = ensure_scratch(L, rows)) return r;
+    const size_t n = (size_t)(rows * L->d);
+    CK(a.x[s].ensure(std::max<size_t>(n, 1) * 4));
+    CK(a.y[s].ensure(std::max<size_t>(n, 1) * 4));
+    Scale* hsc = (Scale*)a.hsc.p + 2 * s;
+    Scale* dsc = a.sc.as<Scale>() + 2 * s;
+    hsc[0] = S(x_scale);
+    // upload: tokens and scale into slot s
+    if (n) CK(cudaMemcpyAsync(a.x[s].p, x, n * 4, cudaMemcpyHostToDevice, a.up));
+    CK(cudaMemcpyAsync(dsc, hsc, sizeof(Scale), cudaMemcpyHostToDevice, a.up));
+    CK(cudaEventRecord(a.ev_up[s], a.up));
+    // the forward, after the upload, on the context stream (after every earlier forward)
+    CK(cudaStreamWaitEvent(ctx->stream, a.ev_up[s], 0));
+    if (int r = run_forward(L, rows, a.x[s].as<int32_t>(), dsc, a.y[s].as<int32_t>(), dsc + 1, ctx->stream)) return r;
+    CK(cudaEventRecord(a.ev_fwd[s], ctx->stream));
+    // download: result and scale, after the forward
+    CK(cudaStreamWaitEvent(a.down, a.ev_fwd[s], 0));
+    if (n) CK(cudaMemcpyAsync(y, a.y[s].p, n * 4, cudaMemcpyDeviceToHost, a.down));
+    CK(cudaMemcpyAsync(hsc + 1, dsc + 1, sizeof(Scale), cudaMemcpyDeviceToHost, a.down));
+    CK(cudaEventRecord(a.ev_down[s], a.down));
+    a.pending[s] = true;
+    a.ys_out[s] = y_scale;
+    return KTMOE_OK;
+}
+
+int ktmoe_forward_async_wait(ktmoe_layer* L) {
+    if (!L) return KTMOE_ERR_ARG;
+    ktmoe_ctx* ctx = L->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (int r = set_device(ctx)) return r;
+    if (!L->as.init) return KTMOE_OK;
+    int status = KTMOE_OK;
+    for (int k = 0; k < 2; ++k) {
+        const int s = (int)((L->as.calls + k) & 1);  // the older call first
+        if (int r = async_finish(L, s)) status = status ? status : r;
+    }
+    if (int r = check_err_word(ctx)) status = status ? status : r;
+    return status;
 }
 
 int ktmoe_layer_set_norm(ktmoe_layer* L, const int32_t* w_codes, ktmoe_scale w_scale, ktmoe_scale eps_scale) {
