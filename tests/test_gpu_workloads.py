@@ -71,6 +71,8 @@ def test_prefill_workloads_equal_the_golden(ctx, name, monkeypatch):
     if name == "mixtral_prefill":
         variants.append({"KTMOE_SWIGLU_CLUSTER": "1"})  # the 14336-wide rows on 8-CTA clusters as well
         variants.append({"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_SWIGLU_U": "2"})  # and two elements per thread step
+        variants.append({"KTMOE_SWIGLU_V": "1", "KTMOE_SWIGLU_U": "4"})  # the first lean element path
+        variants.append({"KTMOE_SWIGLU_V": "2"})
         # and split over a 2-CTA cluster with h in shared memory
         variants.append({"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_SWIGLU_U": "4", "KTMOE_SWIGLU_SLICE": "1"})
     _run(ctx, name, monkeypatch, variants)

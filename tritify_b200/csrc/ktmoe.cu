@@ -1018,20 +1018,25 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     } else {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
         const size_t sm = h_smem ? (size_t)L->swiglu_smem : 0;
-        // elements per thread per step (KTMOE_SWIGLU_U = 1, 2 or 4): 4 measured fastest on the Mixtral rows (2.07 ms
-        // against 2.31-2.41 ms at 2): more loads of a row in flight per thread
+        // steps per thread (KTMOE_SWIGLU_U = 1, 2 or 4) of one element (the first lean path) or one pair (v2): v2 at 2
+        // measured 1.82-1.86 ms on the Mixtral rows with the fewest instructions (113 M against 120 M at 4 on a
+        // 2048-row capture); the first lean path wanted 4 (2.07-2.28 ms)
         const char* ue = getenv("KTMOE_SWIGLU_U");
-        const int uv = ue ? atoi(ue) : 4;
-        const int unroll = (uv == 1 || uv == 2 || uv == 4) ? uv : 4;
+        const int uv = ue ? atoi(ue) : 2;
+        const int unroll = (uv == 1 || uv == 2 || uv == 4) ? uv : 2;
         // a block per row (rows beyond a device-side count leave at once): blocks that wait at a row's barrier
         // are replaced by new ones, which keeps the SMs busier than blocks walking several rows (ncu: 617 vs 696 us)
         const unsigned grid = (unsigned)R;
+        // KTMOE_SWIGLU_V=1: the first lean element path; 2 (default): magnitudes and signs apart, a cheaper
+        // certificate, element pairs through 16-byte loads and stores
+        const char* ve = getenv("KTMOE_SWIGLU_V");
+        const int v2 = (ve && ve[0] == '1') ? 0 : 1;
         if (unroll == 1)
-            mk::swiglu_rows_kernel<1><<<grid, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<1><<<grid, 256, sm, st>>>(sa, h_smem, v2);
         else if (unroll == 4)
-            mk::swiglu_rows_kernel<4><<<grid, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<4><<<grid, 256, sm, st>>>(sa, h_smem, v2);
         else
-            mk::swiglu_rows_kernel<2><<<grid, 256, sm, st>>>(sa, h_smem);
+            mk::swiglu_rows_kernel<2><<<grid, 256, sm, st>>>(sa, h_smem, v2);
         CKL(ctx);
     }
     mk::down_c_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);

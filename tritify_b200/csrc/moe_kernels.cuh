@@ -502,6 +502,55 @@ __device__ __forceinline__ int64_t swiglu_h_fast(const SwigluScales& q, const in
     return (int64_t)c * (int64_t)u;
 }
 
+// The same floor as req_mag from two one-rounding estimates 2^-21 below and above: z = av·inv is within 2^-25 of
+// av·2^28/den, and t lies in [z + 1/2 - 2^-25 - 1/(2·den), z + 1/2 + 2^-25]; RN(z + 1/2 ∓ 2^-21) err by at most 2^-25,
+// so the low estimate is below t and the high one above it, and equal floors (read from the low words after an add
+// of 1.5·2^52 rounded down) certify floor(t). One FMA and one add fewer than req_mag's test of the fraction.
+__device__ __forceinline__ bool req_mag2(double av, double inv, uint32_t& q) {
+    const double lo = __dadd_rd(__fma_rn(av, inv, 0.5 - RQ_EPS), RQ_MAGIC);
+    const double hi = __dadd_rd(__fma_rn(av, inv, 0.5 + RQ_EPS), RQ_MAGIC);
+    q = (uint32_t)__double2loint(lo);
+    return __double2loint(lo) == __double2loint(hi);
+}
+
+// swiglu_h_fast with magnitudes and signs kept apart: g is never formed as a signed value (the SiLU index needs
+// only its magnitude and sign), and |h| = |code|·|u| comes from one 32x32->64 product for the row maximum.
+__device__ __forceinline__ int64_t swiglu_h_fast2(const SwigluScales& q, const int32_t* __restrict__ lut32,
+                                                  int32_t base, int64_t accg, int64_t accu, uint64_t& habs) {
+    uint32_t qg, qu;
+    const bool okg = req_mag2(fabs((double)accg), q.rg.inv28, qg);
+    const bool oku = req_mag2(fabs((double)accu), q.ru.inv28, qu);
+    const bool gneg = accg < 0, uneg = accu < 0;
+    if (!okg) {
+        const int32_t e = kt::requant_row(accg, q.rg);
+        qg = (uint32_t)(e < 0 ? -e : e);
+    }
+    if (!oku) {
+        const int32_t e = kt::requant_row(accu, q.ru);
+        qu = (uint32_t)(e < 0 ? -e : e);
+    }
+    const uint32_t r = (uint32_t)(((uint64_t)qg * q.is.mant + q.is.half) >> 32) >> (q.is.shift - 32);
+    const int32_t idx = gneg ? base - (int32_t)r : base + (int32_t)r;
+    int32_t c = __ldg(lut32 + min(max(idx, 0), LUT_N - 1));
+    if (idx < 0)
+        c = 0;
+    else if (idx >= LUT_N)
+        c = (int32_t)kt::apply_row(q.idf, gneg ? -(int32_t)qg : (int32_t)qg);  // identity right tail
+    habs = (uint64_t)(uint32_t)(c < 0 ? -c : c) * (uint64_t)qu;
+    return (int64_t)c * (int64_t)(uneg ? -(int32_t)qu : (int32_t)qu);
+}
+
+// down_code_fast with the req_mag2 certificate.
+__device__ __forceinline__ int32_t down_code_fast2(int64_t h, const kt::ReqDiv& rh) {
+    uint32_t q;
+    if (!req_mag2(fabs((double)h), rh.inv28, q)) {
+        const int32_t e = kt::requant_row(h, rh);
+        q = (uint32_t)(e < 0 ? -e : e);
+    }
+    const uint32_t t = (uint32_t)(((uint64_t)q * (uint64_t)kt::WLEVELS + (uint64_t(1) << 27)) >> 28);
+    return h < 0 ? -(int32_t)t : (int32_t)t;
+}
+
 // quant_to_act(requant_row(h, rh)) on the lean path (rh.dbl): both roundings on magnitudes, the sign applied once.
 __device__ __forceinline__ int32_t down_code_fast(int64_t h, const kt::ReqDiv& rh) {
     uint32_t q;
@@ -608,11 +657,29 @@ __global__ void down_c_kernel(const SwigluArgs a) {
 }
 
 // hint = requant_dyn(h, L, hmax) has max |.| = L exactly, so the down linear's quant_to divides by 2^28.
-__device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, const int64_t* h, int64_t hmax) {
+__device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, const int64_t* h, int64_t hmax,
+                                                  bool v2 = false) {
     int8_t* p0 = a.planes + (long long)r * a.f_pad;
     int8_t* p1 = p0 + a.R_pad * a.f_pad;
     int8_t* p2 = p1 + a.R_pad * a.f_pad;
     const kt::ReqDiv rh = kt::make_req(hmax);
+    if (rh.dbl && v2 && (((uintptr_t)h) & 15) == 0) {  // the lean path, four elements from two 16-byte loads
+        for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
+            int32_t q[4];
+            if (k4 + 3 < a.f) {
+                const longlong2 h0 = *(const longlong2*)(h + k4), h1 = *(const longlong2*)(h + k4 + 2);
+                q[0] = down_code_fast2(h0.x, rh);
+                q[1] = down_code_fast2(h0.y, rh);
+                q[2] = down_code_fast2(h1.x, rh);
+                q[3] = down_code_fast2(h1.y, rh);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) q[j] = k4 + j < a.f ? down_code_fast2(h[k4 + j], rh) : 0;
+            }
+            store_digits4(p0 + k4, p1 + k4, p2 + k4, q);
+        }
+        return;
+    }
     if (rh.dbl) {  // the lean path (2^22 <= hmax < 2^52)
         for (int k4 = threadIdx.x * 4; k4 < a.f_pad; k4 += blockDim.x * 4) {
             int32_t q[4];
@@ -637,7 +704,7 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
 // `h_smem`. U independent elements per thread per step. The row's scales come from swiglu_plan_kernel; its max |h|
 // goes to row_hmax.
 template <int U>
-__global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem) {
+__global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem, int v2) {
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
     const int n = swiglu_rows(a);
@@ -650,6 +717,36 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
         uint64_t hm = 0;
         // the loads of a step are issued before its arithmetic
         int k = threadIdx.x;
+        if (q.fast && v2 && (f & 1) == 0 && (((uintptr_t)accg | (uintptr_t)h) & 15) == 0) {
+            // element pairs: 16-byte loads of g and u, a 16-byte store of h
+            const int32_t base = (int32_t)-a.silu.lo_index;
+            const int npairs = f >> 1;
+            int p = threadIdx.x;
+            for (; p < npairs; p += U * blockDim.x) {
+                longlong2 gv[U], uv[U];
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int pj = p + j * blockDim.x;
+                    if (pj < npairs) {
+                        gv[j] = __ldcs((const longlong2*)(accg + 2 * pj));
+                        uv[j] = __ldcs((const longlong2*)(accu + 2 * pj));
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < U; ++j) {
+                    const int pj = p + j * blockDim.x;
+                    if (pj < npairs) {
+                        uint64_t a0, a1;
+                        longlong2 hv;
+                        hv.x = swiglu_h_fast2(q, a.silu.codes32, base, gv[j].x, uv[j].x, a0);
+                        hv.y = swiglu_h_fast2(q, a.silu.codes32, base, gv[j].y, uv[j].y, a1);
+                        *(longlong2*)(h + 2 * pj) = hv;
+                        hm = max(hm, max(a0, a1));
+                    }
+                }
+            }
+            k = f;
+        }
         if (q.fast) {
             const int32_t base = (int32_t)-a.silu.lo_index;
             for (; k + (U - 1) * (int)blockDim.x < f; k += U * blockDim.x) {
@@ -687,7 +784,7 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
             hm = max(hm, uabs64(v));
         }
         const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
-        write_down_planes(a, r, h, hmax);
+        write_down_planes(a, r, h, hmax, v2 != 0);
         if (threadIdx.x == 0) a.row_hmax[r] = (unsigned long long)hmax;
         __syncthreads();  // h (and red) are reused by the next row
     }
