@@ -551,6 +551,13 @@ __device__ __forceinline__ int32_t down_code_fast2(int64_t h, const kt::ReqDiv& 
     return h < 0 ? -(int32_t)t : (int32_t)t;
 }
 
+// requant_row(v, r) for a divisor with r.dbl, through the req_mag2 certificate (exact integer path on a miss).
+__device__ __forceinline__ int32_t requant_fast(int64_t v, const kt::ReqDiv& r) {
+    uint32_t q;
+    if (!req_mag2(fabs((double)v), r.inv28, q)) return kt::requant_row(v, r);
+    return v < 0 ? -(int32_t)q : (int32_t)q;
+}
+
 // quant_to_act(requant_row(h, rh)) on the lean path (rh.dbl): both roundings on magnitudes, the sign applied once.
 __device__ __forceinline__ int32_t down_code_fast(int64_t h, const kt::ReqDiv& rh) {
     uint32_t q;
@@ -1026,9 +1033,9 @@ __global__ void swiglu_global_kernel(const SwigluArgs a) {
         if (q.fast) {
             const int32_t base = (int32_t)-a.silu.lo_index;
             for (int k = threadIdx.x; k < f; k += blockDim.x) {
-                const int64_t v = swiglu_h_fast(q, a.silu.codes32, base, accg[k], accu[k]);
-                accg[k] = v;
-                hm = max(hm, uabs64(v));
+                uint64_t av;
+                accg[k] = swiglu_h_fast2(q, a.silu.codes32, base, accg[k], accu[k], av);
+                hm = max(hm, av);
             }
         } else {
             for (int k = threadIdx.x; k < f; k += blockDim.x) {
@@ -1042,7 +1049,7 @@ __global__ void swiglu_global_kernel(const SwigluArgs a) {
         return;
     }
     const int64_t hmax = (int64_t)*a.g_hmax;
-    write_down_planes(a, r, accg, hmax);
+    write_down_planes(a, r, accg, hmax, true);
     if (r == 0 && threadIdx.x == 0) a.row_cd[0] = down_c(a, a.plans[0].us, hmax, 0);
 }
 
@@ -1141,6 +1148,12 @@ __global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, co
         f_s[threadIdx.x] = p.f[q];
     }
     __syncthreads();
+    // the lean path when every live slot's divisor admits the certified double path, its rescale is tight and its code
+    // fits 31 bits: the rescaled value (|requant| <= 2^28 times a factor of about 1 at most, the common scale being
+    // the largest) then fits 32 bits and the weighting is one widening multiply
+    bool lean = true;
+    for (int j = 0; j < n; ++j)
+        lean = lean && ry_s[j].dbl && f_s[j].tight && ec_s[j] >= 0 && ec_s[j] < (int64_t(1) << 31);
     uint64_t gm = 0;
     for (int d0 = threadIdx.x; d0 < D; d0 += CE * blockDim.x) {
         int64_t acc[CE];
@@ -1157,8 +1170,14 @@ __global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, co
                 const int d = d0 + u * blockDim.x;
                 v[u] = d < D ? __ldg(b + d) : 0;
             }
+            if (lean) {
 #pragma unroll
-            for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, kt::requant_row(v[u], ry));
+                for (int u = 0; u < CE; ++u)
+                    acc[u] += (int64_t)(int32_t)ec * (int64_t)(int32_t)kt::apply_row(f, requant_fast(v[u], ry));
+            } else {
+#pragma unroll
+                for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, kt::requant_row(v[u], ry));
+            }
         }
 #pragma unroll
         for (int u = 0; u < CE; ++u) {
@@ -1172,7 +1191,11 @@ __global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, co
     gm = block_max_u64(gm, red);
     const int64_t gmax = (int64_t)gm;
     const kt::ReqDiv rg = kt::make_req(gmax);
-    for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
+    if (rg.dbl) {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = requant_fast(acc_s[d], rg);
+    } else {
+        for (int d = threadIdx.x; d < D; d += blockDim.x) o[d] = gmax ? kt::requant_row(acc_s[d], rg) : 0;
+    }
     if (threadIdx.x == 0) {
         const int64_t sumc = a.sumc[t];
         a.out_scale[t] = gmax == 0 ? kt::scale_zero()
@@ -1265,10 +1288,17 @@ __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* _
             int4 r = make_int4(0, 0, 0, 0);
             if (!zero) {
                 const int4 v = __ldg((const int4*)(ot + d));
-                r.x = kt::requant_row(kt::apply_row(f, v.x), rg);
-                r.y = kt::requant_row(kt::apply_row(f, v.y), rg);
-                r.z = kt::requant_row(kt::apply_row(f, v.z), rg);
-                r.w = kt::requant_row(kt::apply_row(f, v.w), rg);
+                if (rg.dbl) {  // the certified double path through the two-estimate test
+                    r.x = requant_fast(kt::apply_row(f, v.x), rg);
+                    r.y = requant_fast(kt::apply_row(f, v.y), rg);
+                    r.z = requant_fast(kt::apply_row(f, v.z), rg);
+                    r.w = requant_fast(kt::apply_row(f, v.w), rg);
+                } else {
+                    r.x = kt::requant_row(kt::apply_row(f, v.x), rg);
+                    r.y = kt::requant_row(kt::apply_row(f, v.y), rg);
+                    r.z = kt::requant_row(kt::apply_row(f, v.z), rg);
+                    r.w = kt::requant_row(kt::apply_row(f, v.w), rg);
+                }
             }
             *(int4*)(yt + d) = r;
         }
