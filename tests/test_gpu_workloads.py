@@ -61,13 +61,19 @@ def test_decode_and_config1_workloads_equal_the_golden(ctx, name, monkeypatch):
                                   {"KTMOE_SWIGLU_CLUSTER": "1", "KTMOE_SWIGLU_SHAPE": "2x256"},
                                   {"KTMOE_SWIGLU_CLUSTER": "1", "KTMOE_SWIGLU_SHAPE": "4x128"},
                                   {"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_PAIR_ZERO_MMA": "1"},
-                                  {"KTMOE_PAIR_ZERO_MMA": "0"}])
+                                  {"KTMOE_PAIR_ZERO_MMA": "0"},
+                                  {"KTMOE_COMBINE": "0"},  # the thread-per-token plan and a CTA per token
+                                  {"KTMOE_COMBINE": "1"},  # a warp plan inside each token's cluster of CTAs
+                                  {"KTMOE_SWIGLU_INLINE": "0"},  # the SwiGLU row plans and down c as kernels
+                                  {"KTMOE_SWIGLU_INLINE": "1"}])  # and inside the row kernel
 
 
 @pytest.mark.parametrize("name", ["qwen_prefill", "mixtral_prefill", "mixtral_zipf", "glm_prefill"])
 def test_prefill_workloads_equal_the_golden(ctx, name, monkeypatch):
     # the pair GEMM with the epilogue zeroing the accumulator, and with the clearing MMA
     variants = [{"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_PAIR_ZERO_MMA": "0"}, {"KTMOE_PAIR_ZERO_MMA": "1"}]
+    # the combine's thread-per-token plan kernel, then back to the warp-per-token one
+    variants += [{"KTMOE_COMBINE": "0"}, {"KTMOE_COMBINE": "1"}]
     if name == "mixtral_prefill":
         variants.append({"KTMOE_SWIGLU_CLUSTER": "1"})  # the 14336-wide rows on 8-CTA clusters as well
         variants.append({"KTMOE_SWIGLU_CLUSTER": "0", "KTMOE_SWIGLU_U": "2"})  # and two elements per thread step

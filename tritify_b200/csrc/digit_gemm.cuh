@@ -254,6 +254,7 @@ template <int BN, int STAGES, int ACC, int PX = 3, int PW = 3>
 __global__ void __launch_bounds__(THREADS, 1)
     digit_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const GemmArgs args) {
+    kt::pdl_enter();
     using C = Cfg<BN, STAGES, ACC, PX, PW>;
     constexpr int NDIAG_USED = C::DIAGS;
     constexpr uint32_t TX_BYTES = (uint32_t)C::STAGE_BYTES;  // what one stage's copies bring
@@ -532,6 +533,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // output). One block per row (grid-stride); the words start at zero.
 static __global__ void rowmax_kernel(const int64_t* __restrict__ out, long long ld, int rows, int M_valid, int split,
                               unsigned long long* __restrict__ rowmax, int stride) {
+    kt::pdl_enter();
     __shared__ unsigned long long red[2][32];
     for (int r = blockIdx.x; r < rows; r += gridDim.x) {
         unsigned long long v[2] = {0ull, 0ull};

@@ -181,6 +181,7 @@ struct TileIter2 {
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair::THREADS, 1)
     digit_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const GemmArgs args) {
+    kt::pdl_enter();
     using namespace pair;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -479,6 +480,7 @@ __device__ __forceinline__ bool tile_of(const GemmArgs& a, int per_group, int li
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pair_small::THREADS, 1)
     digit_gemm_pair_small_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                                  const GemmArgs args) {
+    kt::pdl_enter();
     using namespace pair;
     namespace ps = pair_small;
     extern __shared__ uint8_t smem_raw[];

@@ -103,6 +103,7 @@ __device__ __forceinline__ bool wait_flag(const Peers& P, int point, int src, un
 // `all` and/or their maxima in `mx` (in place allowed: mx may equal src).
 __global__ void exchange_kernel(const Peers P, int point, const unsigned long long* src, int n, unsigned long long* all,
                                 unsigned long long* mx, int* err) {
+    kt::pdl_enter();
     const unsigned long long seq = *P.seq;
     __shared__ unsigned long long v[4];
     __shared__ int ok;
@@ -133,6 +134,7 @@ __global__ void exchange_kernel(const Peers P, int point, const unsigned long lo
 // Publish this rank's counts (E experts + its token count) into counts[rank] of every rank, raise P_COUNTS, wait for
 // all ranks. One block.
 __global__ void counts_exchange_kernel(const Peers P, const int* __restrict__ expert_count, int T, int* err) {
+    kt::pdl_enter();
     const unsigned long long seq = *P.seq;
     const int E1 = P.E + 1;
     for (int q = 0; q < P.world; ++q) {
@@ -154,6 +156,7 @@ __global__ void ep_plan_kernel(const Peers P, const int* __restrict__ expert_off
                                int* __restrict__ group_end, int* __restrict__ rows_recv, mk::TileTable ta,
                                mk::TileTable tb, int* __restrict__ tok_offset, int* __restrict__ tok_total,
                                int* err) {
+    kt::pdl_enter();
     extern __shared__ int sh[];  // [E] total rows per expert over all sources, [E] rows of lower sources
     int* tot = sh;
     int* below = sh + P.E;
@@ -240,6 +243,7 @@ __global__ void dispatch_kernel(const Peers P, int R, const int* __restrict__ ro
                                 const int* __restrict__ row_expert, int K, const int8_t* __restrict__ tok_planes,
                                 long long T_pad, const Scale* __restrict__ tok_sqx, const int* __restrict__ dst_base,
                                 int* ctr, int* err) {
+    kt::pdl_enter();
     const unsigned long long seq = *P.seq;
     const int n16 = P.d_pad / 16;
     const int lane = threadIdx.x & 31;
@@ -273,16 +277,18 @@ __global__ void dispatch_kernel(const Peers P, int R, const int* __restrict__ ro
 }
 
 // A new forward: the next sequence number (one thread).
-__global__ void seq_bump_kernel(const Peers P) { *P.seq += 1; }
+__global__ void seq_bump_kernel(const Peers P) { kt::pdl_enter(); *P.seq += 1; }
 
 // Wait for `point` from every rank (one block, >= world threads).
 __global__ void wait_all_kernel(const Peers P, int point, int* err) {
+    kt::pdl_enter();
     if ((int)threadIdx.x < P.world) wait_flag(P, point, threadIdx.x, *P.seq, err);
 }
 
 // The owner's per-row s_qx and local expert from the meta of its received rows.
 __global__ void meta_unpack_kernel(const Peers P, const int* __restrict__ rows_recv, Scale* __restrict__ row_sqx,
                                    int* __restrict__ row_expert_local) {
+    kt::pdl_enter();
     const int n = *rows_recv;
     const long long* m = P.meta(P.rank);
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < n; r += gridDim.x * blockDim.x) {
@@ -297,6 +303,7 @@ __global__ void meta_unpack_kernel(const Peers P, const int* __restrict__ rows_r
 __global__ void return_kernel(const Peers P, const int* __restrict__ rows_recv,
                               const int64_t* __restrict__ acc, const unsigned long long* __restrict__ ymax_row,
                               const Scale* __restrict__ row_cd, int* ctr, int* err) {
+    kt::pdl_enter();
     const unsigned long long seq = *P.seq;
     const int n = *rows_recv;
     const int D = P.d;

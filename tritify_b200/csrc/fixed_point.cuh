@@ -18,6 +18,17 @@
 
 namespace kt {
 
+#ifdef __CUDACC__
+// The first statement of every kernel of this library. Programmatic dependent launch: a kernel launched with the
+// programmatic-serialization attribute may be scheduled once the blocks of the kernel before it on its stream have
+// exited; griddepcontrol.wait holds it until that kernel has completed and its writes are visible (a no-op for a
+// kernel launched without the attribute). Only launch and set-up overlap; as every kernel waits before it can
+// complete, completion keeps the stream's order. (No early launch_dependents: blocks of the next kernel parked on
+// the SMs measured slower, 0.442 against 0.395 ms on Qwen-shaped decode, taking room from the shared expert's
+// kernels on the side stream.)
+__device__ __forceinline__ void pdl_enter() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+#endif
+
 typedef __int128 i128;
 typedef unsigned __int128 u128;
 

@@ -166,6 +166,65 @@ int fail_cuda(ktmoe_ctx* ctx, cudaError_t e, const char* what) {
         if (e__ != cudaSuccess) return fail_cuda(ctx, e__, "kernel launch"); \
     } while (0)
 
+// Programmatic dependent launch of this library's kernels (every one begins with kt::pdl_enter(), which waits for
+// the kernel before it on the stream): a kernel is scheduled while its predecessor finishes, which hides most of the
+// gap between two dependent launches. KTMOE_PDL=0, read once, launches them plainly.
+bool pdl_on() {
+    static const bool on = [] {
+        const char* e = getenv("KTMOE_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// One launch of `kernel` on clusters of `cluster` CTAs along x (1: no cluster attribute).
+template <typename... KArgs, typename... Args>
+int launch_kc(ktmoe_ctx* ctx, cudaStream_t st, dim3 grid, dim3 block, size_t smem, unsigned cluster,
+              void (*kernel)(KArgs...), Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl_on()) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = cluster;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+    CKL(ctx);
+    return KTMOE_OK;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_k(ktmoe_ctx* ctx, cudaStream_t st, dim3 grid, dim3 block, size_t smem, void (*kernel)(KArgs...),
+             Args&&... args) {
+    return launch_kc(ctx, st, grid, block, smem, 1u, kernel, std::forward<Args>(args)...);
+}
+
+// KLAUNCH(stream, grid, block, shared bytes, (kernel), args...): launch_k, returning its status on failure; one
+// statement (safe under an unbraced if / else).
+#define KLAUNCH(...)                                                   \
+    do {                                                               \
+        if (int r_kl__ = launch_k(ctx, __VA_ARGS__)) return r_kl__;    \
+    } while (0)
+// KLAUNCHC(stream, grid, block, shared bytes, cluster size, (kernel), args...): the same through launch_kc.
+#define KLAUNCHC(...)                                                  \
+    do {                                                               \
+        if (int r_kl__ = launch_kc(ctx, __VA_ARGS__)) return r_kl__;   \
+    } while (0)
+
 int make_map(ktmoe_ctx* ctx, CUtensorMap* map, const void* base, int64_t k_pad, int64_t rows_total, int box_rows) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(ctx, KTMOE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -190,8 +249,7 @@ int launch_gemm_t(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, const 
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM_BYTES));
         attr_set[ctx->device & 63] = true;
     }
-    dg::digit_gemm_kernel<BN, ST, ACC, PX, PW><<<grid, dg::THREADS, Cf::SMEM_BYTES, st>>>(ma, mb, args);
-    CKL(ctx);
+    KLAUNCH(st, grid, dg::THREADS, Cf::SMEM_BYTES, (dg::digit_gemm_kernel<BN, ST, ACC, PX, PW>), ma, mb, args);
     return KTMOE_OK;
 }
 
@@ -229,9 +287,8 @@ int launch_gemm_pair(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& ma, con
         ctx->pair_clusters = std::min(n, ctx->num_sms / 2);
     }
     const int64_t clusters = std::min<int64_t>(slots, ctx->pair_clusters);
-    dg::digit_gemm_pair_kernel<<<dim3((unsigned)(2 * clusters)), dg::pair::THREADS, dg::pair::SMEM_BYTES, st>>>(ma, mb,
-                                                                                                              args);
-    CKL(ctx);
+    KLAUNCH(st, dim3((unsigned)(2 * clusters)), dg::pair::THREADS, dg::pair::SMEM_BYTES, (dg::digit_gemm_pair_kernel),
+            ma, mb, args);
     return KTMOE_OK;
 }
 
@@ -289,9 +346,8 @@ int launch_gemm_pair_small(ktmoe_ctx* ctx, cudaStream_t st, const CUtensorMap& m
         clusters_of[dev] = std::min(n, ctx->num_sms / 2);
     }
     const int64_t clusters = std::min<int64_t>(slots, clusters_of[dev]);
-    dg::digit_gemm_pair_small_kernel<<<dim3((unsigned)(2 * clusters)), ps::THREADS, ps::SMEM_BYTES, st>>>(mx, mw,
-                                                                                                      args);
-    CKL(ctx);
+    KLAUNCH(st, dim3((unsigned)(2 * clusters)), ps::THREADS, ps::SMEM_BYTES, (dg::digit_gemm_pair_small_kernel), mx, mw,
+            args);
     return KTMOE_OK;
 }
 
@@ -430,10 +486,9 @@ int run_gemm(ktmoe_ctx* ctx, cudaStream_t st, const GemmCall& g) {
         if (r) return r;
     }
     if (ks > 1 && g.rowmax) {
-        dg::rowmax_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>(g.single_rows, ctx->num_sms * 4)), 256, 0,
-                            st>>>(g.out, g.ld_out, (int)g.single_rows, (int)g.M_valid,
-                                  (int)std::min<int64_t>(g.rowmax_split, INT32_MAX), g.rowmax, g.rowmax_stride);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)std::max<int64_t>(1, std::min<int64_t>(g.single_rows, ctx->num_sms * 4)), 256, 0,
+                (dg::rowmax_kernel), g.out, g.ld_out, (int)g.single_rows, (int)g.M_valid,
+                (int)std::min<int64_t>(g.rowmax_split, INT32_MAX), g.rowmax, g.rowmax_stride);
     }
     return KTMOE_OK;
 }
@@ -470,6 +525,7 @@ int pick_bn_small(double rows) {
 }
 
 __global__ void sqx_kernel(const unsigned long long* gxmax, const Scale* x_scale, Scale* out) {
+    kt::pdl_enter();
     const int64_t xm = (int64_t)*gxmax;
     *out = xm > 0 ? kt::scale_mul(kt::from_ratio((kt::u128)(uint64_t)xm, (kt::u128)kt::WLEVELS), *x_scale)
                   : kt::scale_zero();
@@ -770,10 +826,8 @@ mk::Lut lut(const ktmoe_layer* L, int kind) {
 // Each token row's quantiser (xmax, quant_to, the digit planes, s_qx): tok_planes, tok_xmax, tok_sqx.
 int stage_quant(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs_dev, cudaStream_t st) {
     ktmoe_ctx* ctx = L->ctx;
-    mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)L->d, (int)L->d_pad, round_up(T, 64),
-                                                        L->tok_planes.as<int8_t>(), L->tok_xmax.as<int64_t>(),
-                                                        L->tok_sqx.as<Scale>(), xs_dev, nullptr);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)T, 256, 0, (mk::quant_rows_kernel), x_dev, (int)T, (int)L->d, (int)L->d_pad, round_up(T, 64),
+            L->tok_planes.as<int8_t>(), L->tok_xmax.as<int64_t>(), L->tok_sqx.as<Scale>(), xs_dev, nullptr);
     return KTMOE_OK;
 }
 
@@ -814,8 +868,7 @@ int stage_route(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs
     ra.sumc = L->sumc.as<int64_t>();
     ra.logits_out = L->logits.as<int32_t>();
     ra.logit_scale_out = L->logit_scale.as<Scale>();
-    mk::route_kernel<<<(unsigned)((T + 3) / 4), 128, 0, st>>>(ra);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)((T + 3) / 4), 128, 0, (mk::route_kernel), ra);
     return KTMOE_OK;
 }
 
@@ -836,8 +889,7 @@ int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t 
     if (L->world == 1) return KTMOE_OK;
     ktmoe_ctx* ctx = L->ctx;
     if (L->peer.on) {
-        ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, point, p, (int)n, nullptr, p, ctx->d_err);
-        CKL(ctx);
+        KLAUNCH(st, 1, 32, 0, (ep::exchange_kernel), L->peer.P, point, p, (int)n, nullptr, p, ctx->d_err);
         return KTMOE_OK;
     }
     NK(ncclAllReduce(p, p, n, ncclUint64, ncclMax, L->comm, st));
@@ -855,24 +907,19 @@ int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st
         return KTMOE_OK;
     }
     const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
-    mk::plan_count_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, E * 4, st>>>(L->top_e.as<int32_t>(), R, (int)E,
-                                                                             L->counts.as<int>());
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)nchunks, mk::PLAN_THREADS, E * 4, (mk::plan_count_kernel), L->top_e.as<int32_t>(), R, (int)E,
+            L->counts.as<int>());
     const int scan_threads = (int)std::min<int64_t>(1024, round_up(E, 32));
-    mk::plan_scan_kernel<<<1, scan_threads, 3 * E * 4, st>>>(
-        L->counts.as<int>(), (int)nchunks, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(),
-        L->group_end.as<int>(), L->expert_count.as<int>(),
-        mk::TileTable{BN, L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L)},
-        mk::TileTable{BN2, L->tile_group2.as<int>(), L->tile_row02.as<int>(), n_tiles2_ptr(L)});
-    CKL(ctx);
-    mk::plan_assign_kernel<<<(unsigned)nchunks, mk::PLAN_THREADS, (E + (mk::PLAN_THREADS / 32) * E) * 4, st>>>(
-        L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
-        L->row_assign.as<int>(), L->row_expert.as<int>());
-    CKL(ctx);
+    KLAUNCH(st, 1, scan_threads, 3 * E * 4, (mk::plan_scan_kernel), L->counts.as<int>(), (int)nchunks, (int)E,
+            L->chunk_off.as<int>(), L->expert_off.as<int>(), L->group_end.as<int>(), L->expert_count.as<int>(),
+            mk::TileTable{BN, L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L)},
+            mk::TileTable{BN2, L->tile_group2.as<int>(), L->tile_row02.as<int>(), n_tiles2_ptr(L)});
+    KLAUNCH(st, (unsigned)nchunks, mk::PLAN_THREADS, (E + (mk::PLAN_THREADS / 32) * E) * 4, (mk::plan_assign_kernel),
+            L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
+            L->row_assign.as<int>(), L->row_expert.as<int>());
     if (!permute) return KTMOE_OK;
-    mk::permute_planes_kernel<<<(unsigned)R, 128, 0, st>>>(L->tok_planes.as<int8_t>(), T_pad, L->xg_planes.as<int8_t>(),
-                                                         R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)R, 128, 0, (mk::permute_planes_kernel), L->tok_planes.as<int8_t>(), T_pad,
+            L->xg_planes.as<int8_t>(), R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
     return KTMOE_OK;
 }
 
@@ -904,6 +951,15 @@ int swiglu_slices(const ktmoe_layer* L) {
     for (int c = 1; c <= 8; c *= 2)
         if (L->f_pad % (4 * c) == 0 && (L->f_pad / c) * 8 <= 60 * 1024) return c;
     return 0;
+}
+
+// Routed rows up to which swiglu_rows_kernel computes each row's plan itself (KTMOE_SWIGLU_INLINE=0: never): one wave
+// of its blocks (three per SM). Every wave waits on its rows' plans, so beyond one the plan kernel wins (ms per
+// forward, inline against not: 256 rows 0.389 against 0.399, 1024 rows 1.233 against 1.234, 4096 rows 0.620 against
+// 0.600).
+int64_t swiglu_inline_rows(const ktmoe_ctx* ctx) {
+    const char* e = getenv("KTMOE_SWIGLU_INLINE");
+    return (e && e[0] == '0') ? 0 : 3 * (int64_t)ctx->num_sms;
 }
 
 int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
@@ -960,8 +1016,6 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     sa.row_hmax = L->row_hmax.as<unsigned long long>();
     sa.rows_dev = x.n_rows_dev;
     sa.phase = 0;
-    mk::swiglu_plan_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
-    CKL(ctx);
     // KTMOE_SWIGLU_CLUSTER=1: a cluster per row with h in registers (mk::swiglu_cluster_kernel). The block-per-row
     // kernel below is the default: it spreads a row's per-row work over more elements per thread, and measured faster
     // on the Mixtral rows (2.37 against 2.54 ms); it also takes rows the cluster form cannot (f % 4 != 0, wider than
@@ -974,24 +1028,21 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     const int SG = wide ? 2 : 4, SNT = wide ? 256 : 128;
     int csize = 1;
     while (csize < 8 && (int64_t)csize * SG * SNT * 4 < L->f_pad) csize *= 2;
-    if (use_cluster && f % 4 == 0 && (int64_t)csize * SG * SNT * 4 >= L->f_pad) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(R * csize));
-        cfg.blockDim = dim3(SNT);
-        cfg.stream = st;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = (unsigned)csize;
-        at[0].val.clusterDim.y = 1;
-        at[0].val.clusterDim.z = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
+    const bool cluster_path = use_cluster && f % 4 == 0 && (int64_t)csize * SG * SNT * 4 >= L->f_pad;
+    const bool slice_path = !cluster_path && swiglu_slice_enabled() && L->swiglu_smem == 0 && swiglu_slices(L) > 0;
+    // with few rows the row kernel computes each row's plan and down c itself (two launches fewer); with many the
+    // plan kernel runs first, so that no row's loads wait on its plan
+    sa.inline_plan = (!cluster_path && !slice_path && R <= swiglu_inline_rows(ctx)) ? 1 : 0;
+    if (!sa.inline_plan) {
+        KLAUNCH(st, (unsigned)((R + 127) / 128), 128, 0, (mk::swiglu_plan_kernel), sa);
+    }
+    if (cluster_path) {
+        const dim3 grid((unsigned)(R * csize));
         if (wide)
-            CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<2, 256>, sa));
+            KLAUNCHC(st, grid, SNT, 0, (unsigned)csize, (mk::swiglu_cluster_kernel<2, 256>), sa);
         else
-            CK(cudaLaunchKernelEx(&cfg, mk::swiglu_cluster_kernel<4, 128>, sa));
-        CKL(ctx);
-    } else if (swiglu_slice_enabled() && L->swiglu_smem == 0 && swiglu_slices(L) > 0) {
+            KLAUNCHC(st, grid, SNT, 0, (unsigned)csize, (mk::swiglu_cluster_kernel<4, 128>), sa);
+    } else if (slice_path) {
         // a wide row (h does not fit one block's budget) split over a cluster, h in shared memory
         const int C = swiglu_slices(L);
         const size_t smem = (size_t)(L->f_pad / C) * 8;
@@ -1001,20 +1052,7 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
                                     (int)(60 * 1024)));
             attr_set[ctx->device & 63] = true;
         }
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((unsigned)(R * C));
-        cfg.blockDim = dim3(256);
-        cfg.dynamicSmemBytes = smem;
-        cfg.stream = st;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = (unsigned)C;
-        at[0].val.clusterDim.y = 1;
-        at[0].val.clusterDim.z = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = 1;
-        CK(cudaLaunchKernelEx(&cfg, mk::swiglu_slice_kernel<4>, sa));
-        CKL(ctx);
+        KLAUNCHC(st, (unsigned)(R * C), 256, smem, (unsigned)C, (mk::swiglu_slice_kernel<4>), sa);
     } else {
         const int h_smem = L->swiglu_smem > 0 ? 1 : 0;
         const size_t sm = h_smem ? (size_t)L->swiglu_smem : 0;
@@ -1032,15 +1070,15 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
         const char* ve = getenv("KTMOE_SWIGLU_V");
         const int v2 = (ve && ve[0] == '1') ? 0 : 1;
         if (unroll == 1)
-            mk::swiglu_rows_kernel<1><<<grid, 256, sm, st>>>(sa, h_smem, v2);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<1>), sa, h_smem, v2);
         else if (unroll == 4)
-            mk::swiglu_rows_kernel<4><<<grid, 256, sm, st>>>(sa, h_smem, v2);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<4>), sa, h_smem, v2);
         else
-            mk::swiglu_rows_kernel<2><<<grid, 256, sm, st>>>(sa, h_smem, v2);
-        CKL(ctx);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<2>), sa, h_smem, v2);
     }
-    mk::down_c_kernel<<<(unsigned)((R + 127) / 128), 128, 0, st>>>(sa);
-    CKL(ctx);
+    if (!sa.inline_plan) {
+        KLAUNCH(st, (unsigned)((R + 127) / 128), 128, 0, (mk::down_c_kernel), sa);
+    }
     MARK(L, st);
 
     g.A = L->w_dn;
@@ -1061,6 +1099,55 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
     return KTMOE_OK;
 }
 
+// KTMOE_COMBINE=0: the thread-per-token plan kernel (combine_plan_kernel / combine_y_plan_kernel) at every size, in
+// place of the warp-per-token plans; for comparison only, the results are the same. Read per call.
+bool combine_tok_enabled() {
+    const char* e = getenv("KTMOE_COMBINE");
+    return !(e && e[0] == '0');
+}
+
+// Below this many tokens each token's CTAs compute its plan themselves (combine_tok_kernel, one launch); from it on
+// a warp-per-token plan kernel runs first and a CTA per token reads it (combine_kernel / combine_y_kernel), so that
+// the plan does not hold up the loads of every token's CTA.
+constexpr int64_t COMBINE_FUSED_T = 1024;
+
+// The CTAs per token of combine_tok_kernel: the largest power of two up to 8 that keeps the launch to one wave (three
+// CTAs per SM, the kernel's launch bound), as every CTA spends the plan's latency before its loads.
+int combine_cluster(const ktmoe_ctx* ctx, int64_t T) {
+    int C = 1;
+    while (C < 8 && T * C * 2 <= 3 * (int64_t)ctx->num_sms) C *= 2;
+    return C;
+}
+
+// The combine of T > 0 tokens (layers.rs:893-923) into tok_out / tok_scale: Y = false from the down accumulators
+// (mk::CombineArgs), Y = true from expert outputs given as IntTensors (mk::CombineYArgs). The plan goes through `cp`
+// unless the token's CTAs compute it.
+template <bool Y, class A>
+int launch_combine(ktmoe_layer* L, const A& a, const mk::CombinePlan& cp, int64_t T, cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t d = L->d;
+    const bool tok = combine_tok_enabled();
+    if (tok && T < COMBINE_FUSED_T) {
+        const int C = combine_cluster(ctx, T);
+        const size_t smem = (size_t)((d + C - 1) / C) * 8;
+        KLAUNCHC(st, (unsigned)(T * C), 256, smem, (unsigned)C, (mk::combine_tok_kernel<Y, A>), a);
+        return KTMOE_OK;
+    }
+    if (tok) {
+        KLAUNCH(st, (unsigned)((T + 7) / 8), 256, 0, (mk::combine_plan_warp_kernel<Y, A>), a, cp);
+    } else if constexpr (Y) {
+        KLAUNCH(st, (unsigned)((T + 127) / 128), 128, 0, (mk::combine_y_plan_kernel), a, cp);
+    } else {
+        KLAUNCH(st, (unsigned)((T + 127) / 128), 128, 0, (mk::combine_plan_kernel), a, cp);
+    }
+    if constexpr (Y) {
+        KLAUNCH(st, (unsigned)T, 256, d * 8, (mk::combine_y_kernel), a, cp);
+    } else {
+        KLAUNCH(st, (unsigned)T, 256, d * 8, (mk::combine_kernel), a, cp);
+    }
+    return KTMOE_OK;
+}
+
 // Expert parallelism: exchange the home rank's expert-sorted rows with the experts' owners, run the local experts on
 // what arrives, return their outputs (i32 + Scale per row) and combine at home. Grouped ncclSend/ncclRecv over the
 // world; every rank takes the same collective steps.
@@ -1073,10 +1160,8 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     // per-row s_qx for the owners, and this rank's per-expert counts (+ its token count) for everyone
     CK(L->ep_meta_send.ensure(std::max<int64_t>(R, 1) * 16));
     if (R > 0) {
-        mk::pack_meta_kernel<<<(unsigned)((R + 255) / 256), 256, 0, st>>>(L->row_assign.as<int>(), (int)K,
-                                                                        L->tok_sqx.as<Scale>(), (int)R,
-                                                                        L->ep_meta_send.as<int64_t>());
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)((R + 255) / 256), 256, 0, (mk::pack_meta_kernel), L->row_assign.as<int>(), (int)K,
+                L->tok_sqx.as<Scale>(), (int)R, L->ep_meta_send.as<int64_t>());
     }
     CK(L->ep_counts.ensure((E + 1) * 4));
     CK(L->ep_counts_all.ensure(G * (E + 1) * 4));
@@ -1178,13 +1263,11 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     CK(L->ep_recv_sqx.ensure(std::max<int64_t>(Rr, 1) * sizeof(Scale)));
     CK(L->ep_recv_row_expert.ensure(std::max<int64_t>(Rr, 1) * 4));
     if (Rr > 0) {
-        mk::meta_to_scale_kernel<<<(unsigned)((Rr + 255) / 256), 256, 0, st>>>(L->ep_meta_recv.as<int64_t>(), (int)Rr,
-                                                                             L->ep_recv_sqx.as<Scale>());
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)((Rr + 255) / 256), 256, 0, (mk::meta_to_scale_kernel), L->ep_meta_recv.as<int64_t>(),
+                (int)Rr, L->ep_recv_sqx.as<Scale>());
         const int* runs = td + 3 * na + 3 * nb + 2;
-        mk::runs_to_rows_kernel<<<(unsigned)n_runs, 128, 0, st>>>(runs, runs + n_runs, runs + 2 * n_runs, (int)n_runs,
-                                                                 L->ep_recv_row_expert.as<int>());
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)n_runs, 128, 0, (mk::runs_to_rows_kernel), runs, runs + n_runs, runs + 2 * n_runs,
+                (int)n_runs, L->ep_recv_row_expert.as<int>());
     }
     ExpertRows xr;
     xr.B = Planes{L->ep_recv_planes.as<int8_t>(), 1, Rr_pad, d, L->d_pad};
@@ -1209,10 +1292,9 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     CK(L->ep_y_send.ensure(std::max<int64_t>(Rr, 1) * d * 4));
     CK(L->ep_ys_send.ensure(std::max<int64_t>(Rr, 1) * sizeof(Scale)));
     if (Rr > 0) {
-        mk::expert_out_kernel<<<(unsigned)Rr, 256, 0, st>>>(L->acc_d.as<int64_t>(), L->rowmax_d.as<unsigned long long>(),
-                                                           L->row_cd.as<Scale>(), (int)Rr, (int)d,
-                                                           L->ep_y_send.as<int32_t>(), L->ep_ys_send.as<Scale>());
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)Rr, 256, 0, (mk::expert_out_kernel), L->acc_d.as<int64_t>(),
+                L->rowmax_d.as<unsigned long long>(), L->row_cd.as<Scale>(), (int)Rr, (int)d,
+                L->ep_y_send.as<int32_t>(), L->ep_ys_send.as<Scale>());
     }
     MARK(L, st);
 
@@ -1248,10 +1330,7 @@ int ep_routed(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         ca.out_scale = L->tok_scale.as<Scale>();
         const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
                                  L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
-        mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
-        CKL(ctx);
-        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        CKL(ctx);
+        if (int r = launch_combine<true>(L, ca, cp, T, st)) return r;
     }
     MARK(L, st);
     return KTMOE_OK;
@@ -1273,30 +1352,25 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         CK(cudaMemsetAsync(L->expert_count.p, 0, E * 4, st));
         CK(cudaMemsetAsync(L->expert_off.p, 0, E * 4, st));
     }
-    ep::counts_exchange_kernel<<<1, 256, 0, st>>>(pr.P, L->expert_count.as<int>(), (int)T, ctx->d_err);
-    CKL(ctx);
+    KLAUNCH(st, 1, 256, 0, (ep::counts_exchange_kernel), pr.P, L->expert_count.as<int>(), (int)T, ctx->d_err);
     int* tiles = pr.tiles.as<int>();
     const int64_t tmax = pr.cap_rows / 16 + L->E_local + 1;
     const mk::TileTable ta{BN, tiles, tiles + tmax, tiles + 4 * tmax};
     const mk::TileTable tb{BN2, tiles + 2 * tmax, tiles + 3 * tmax, tiles + 4 * tmax + 1};
     int* tok_info = pr.tok_info.as<int>();  // [0] this rank's first token, [1] the layer's tokens
-    ep::ep_plan_kernel<<<1, 256, 2 * E * 4, st>>>(pr.P, L->expert_off.as<int>(), pr.dst_base.as<int>(),
-                                                   pr.group_end.as<int>(), pr.rows_recv.as<int>(), ta, tb, tok_info,
-                                                   tok_info + 1, ctx->d_err);
-    CKL(ctx);
-    ep::dispatch_kernel<<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, ctx->num_sms * 8)), 256, 0, st>>>(
-        pr.P, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K, L->tok_planes.as<int8_t>(), T_pad,
-        L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(), ctx->d_err);
-    CKL(ctx);
+    KLAUNCH(st, 1, 256, 2 * E * 4, (ep::ep_plan_kernel), pr.P, L->expert_off.as<int>(), pr.dst_base.as<int>(),
+            pr.group_end.as<int>(), pr.rows_recv.as<int>(), ta, tb, tok_info, tok_info + 1, ctx->d_err);
+    KLAUNCH(st, (unsigned)std::max<int64_t>(1, std::min<int64_t>((R + 7) / 8, ctx->num_sms * 8)), 256, 0,
+            (ep::dispatch_kernel), pr.P, (int)R, L->row_assign.as<int>(), L->row_expert.as<int>(), (int)K,
+            L->tok_planes.as<int8_t>(), T_pad, L->tok_sqx.as<Scale>(), pr.dst_base.as<int>(), pr.ctr.as<int>(),
+            ctx->d_err);
     MARK(L, st);
-    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_DISPATCH, ctx->d_err);
-    CKL(ctx);
+    KLAUNCH(st, 1, 32, 0, (ep::wait_all_kernel), pr.P, ep::P_DISPATCH, ctx->d_err);
     MARK(L, st);
 
     // the owner side: this rank's experts on the rows that arrived (their count is on the device)
-    ep::meta_unpack_kernel<<<(unsigned)std::min<int64_t>((pr.cap_rows + 255) / 256, ctx->num_sms * 4), 256, 0, st>>>(
-        pr.P, pr.rows_recv.as<int>(), pr.recv_sqx.as<Scale>(), pr.recv_expert.as<int>());
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)std::min<int64_t>((pr.cap_rows + 255) / 256, ctx->num_sms * 4), 256, 0,
+            (ep::meta_unpack_kernel), pr.P, pr.rows_recv.as<int>(), pr.recv_sqx.as<Scale>(), pr.recv_expert.as<int>());
     ExpertRows xr;
     xr.B = Planes{(int8_t*)((unsigned char*)pr.region.p + pr.P.off_planes), 1, pr.cap_rows, d, L->d_pad};
     xr.n_rows = pr.cap_rows;
@@ -1319,13 +1393,10 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
     xr.row_sqx = pr.recv_sqx.as<Scale>();
     if (int r = run_experts(L, xr, st)) return r;
     MARK(L, st);
-    ep::return_kernel<<<(unsigned)(ctx->num_sms * 8), 256, 0, st>>>(pr.P, pr.rows_recv.as<int>(),
-                                                                   L->acc_d.as<int64_t>(),
-                                                                   L->rowmax_d.as<unsigned long long>(),
-                                                                   L->row_cd.as<Scale>(), pr.ctr.as<int>(), ctx->d_err);
-    CKL(ctx);
-    ep::wait_all_kernel<<<1, 32, 0, st>>>(pr.P, ep::P_RETURN, ctx->d_err);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)(ctx->num_sms * 8), 256, 0, (ep::return_kernel), pr.P, pr.rows_recv.as<int>(),
+            L->acc_d.as<int64_t>(), L->rowmax_d.as<unsigned long long>(), L->row_cd.as<Scale>(), pr.ctr.as<int>(),
+            ctx->d_err);
+    KLAUNCH(st, 1, 32, 0, (ep::wait_all_kernel), pr.P, ep::P_RETURN, ctx->d_err);
     MARK(L, st);
     if (T > 0) {
         mk::CombineYArgs ca;
@@ -1341,10 +1412,7 @@ int ep_routed_peer(ktmoe_layer* L, int64_t T, cudaStream_t st) {
         ca.out_scale = L->tok_scale.as<Scale>();
         const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
                                  L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
-        mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
-        CKL(ctx);
-        mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        CKL(ctx);
+        if (int r = launch_combine<true>(L, ca, cp, T, st)) return r;
     }
     MARK(L, st);
     return KTMOE_OK;
@@ -1369,18 +1437,14 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     const int64_t n = T * d;
     const unsigned red_blocks = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
     if (T > 0) {
-        mk::absmax_i32_kernel<<<red_blocks, 256, 0, st>>>(x_dev, n, scal_u64(L, U_GXMAX));
-        CKL(ctx);
+        KLAUNCH(st, red_blocks, 256, 0, (mk::absmax_i32_kernel), x_dev, n, scal_u64(L, U_GXMAX));
     }
     if (int r = allreduce_max(L, scal_u64(L, U_GXMAX), 1, st, ep::P_SX)) return r;
-    sqx_kernel<<<1, 1, 0, st>>>(scal_u64(L, U_GXMAX), xs_dev, scal_scale(L, SL_GSQX));
-    CKL(ctx);
+    KLAUNCH(st, 1, 1, 0, (sqx_kernel), scal_u64(L, U_GXMAX), xs_dev, scal_scale(L, SL_GSQX));
     GemmCall s;
     if (T > 0) {
-        mk::quant_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
-                                                            L->xs_planes.as<int8_t>(), nullptr, nullptr, xs_dev,
-                                                            scal_u64(L, U_GXMAX));
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::quant_rows_kernel), x_dev, (int)T, (int)d, (int)L->d_pad, T_pad,
+                L->xs_planes.as<int8_t>(), nullptr, nullptr, xs_dev, scal_u64(L, U_GXMAX));
         s.A = L->w_sgu;
         s.M_valid = 2 * fs;
         s.B = Planes{L->xs_planes.as<int8_t>(), 1, T_pad, d, L->d_pad};
@@ -1418,17 +1482,14 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     CK(L->shared_plan.ensure(sizeof(mk::SwigluScales)));
     sh.plans = L->shared_plan.as<mk::SwigluScales>();
     sh.phase = 1;
-    mk::swiglu_plan_kernel<<<1, 32, 0, st>>>(sh);
-    CKL(ctx);
+    KLAUNCH(st, 1, 32, 0, (mk::swiglu_plan_kernel), sh);
     if (T > 0) {
-        mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::swiglu_global_kernel), sh);
     }
     if (int r = allreduce_max(L, scal_u64(L, U_SHMAX), 1, st, ep::P_SHMAX)) return r;
     sh.phase = 2;
     if (T > 0) {
-        mk::swiglu_global_kernel<<<(unsigned)T, 256, 0, st>>>(sh);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::swiglu_global_kernel), sh);
         s.A = L->w_sdn;
         s.M_valid = d;
         s.B = Planes{L->hs_planes.as<int8_t>(), 1, T_pad, fs, L->fs_pad};
@@ -1447,10 +1508,8 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     // the sigmoid gate of the shared expert (extension): gate logits from the same input planes, their sigmoid
     // codes, then the shared output scaled per token and requantised over the whole tensor (all ranks)
     if (T > 0) {
-        mk::gate_logit_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(L->xs_planes.as<int8_t>(), (int)T,
-                                                                       (int)L->d_pad, T_pad, L->b_sgate.as<int32_t>(),
-                                                                       L->sg_acc.as<int64_t>(), scal_u64(L, U_GYMAX));
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)((T + 7) / 8), 256, 0, (mk::gate_logit_kernel), L->xs_planes.as<int8_t>(), (int)T,
+                (int)L->d_pad, T_pad, L->b_sgate.as<int32_t>(), L->sg_acc.as<int64_t>(), scal_u64(L, U_GYMAX));
     }
     if (int r = allreduce_max(L, scal_u64(L, U_GYMAX), 1, st, ep::P_GYMAX)) return r;
     mk::GateArgs ga;
@@ -1465,17 +1524,13 @@ int shared_expert(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     ga.y = L->y_gated.as<int32_t>();
     ga.y_scale = scal_scale(L, SL_GATED);
     if (T > 0) {
-        mk::gate_code_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(
-            L->sg_acc.as<int64_t>(), (int)T, scal_u64(L, U_GYMAX), scal_scale(L, SL_GSQX), L->sgate_ws, lut(L, 2),
-            L->sg_code.as<int64_t>());
-        CKL(ctx);
-        mk::gated_max_kernel<<<(unsigned)T, 256, 0, st>>>(ga);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)((T + 127) / 128), 128, 0, (mk::gate_code_kernel), L->sg_acc.as<int64_t>(), (int)T,
+                scal_u64(L, U_GYMAX), scal_scale(L, SL_GSQX), L->sgate_ws, lut(L, 2), L->sg_code.as<int64_t>());
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::gated_max_kernel), ga);
     }
     if (int r = allreduce_max(L, scal_u64(L, U_GATEDMAX), 1, st, ep::P_GATED)) return r;
     if (T > 0) {
-        mk::gated_final_kernel<<<(unsigned)T, 256, 0, st>>>(ga);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::gated_final_kernel), ga);
     }
     return KTMOE_OK;
 }
@@ -1491,7 +1546,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
     const int64_t T_pad = round_up(std::max<int64_t>(T, 1), 64), R_pad = round_up(std::max<int64_t>(R, 1), 64);
     CK(cudaMemsetAsync(scal_u64(L, 0), 0, U_N * 8, st));
     if (L->peer.on && bump) {
-        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);  // a new forward for every exchange below
+        KLAUNCH(st, 1, 1, 0, (ep::seq_bump_kernel), L->peer.P);  // a new forward for every exchange below
         CKL(ctx);
     }
     // the shared expert depends only on x: it runs on the side stream while the routed experts run on st (not with
@@ -1552,10 +1607,7 @@ int stage_forward(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* 
         ca.out_scale = L->tok_scale.as<Scale>();
         const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
                                  L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
-        mk::combine_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
-        CKL(ctx);
-        mk::combine_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-        CKL(ctx);
+        if (int r = launch_combine<false>(L, ca, cp, T, st)) return r;
         MARK(L, st);
     } else if (L->peer.on) {
         if (int r = ep_routed_peer(L, T, st)) return r;
@@ -1582,54 +1634,43 @@ int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset
     Scale* routed_scale = fs > 0 ? scal_scale(L, SL_YROUTED) : ys_dev;
     if (T_total == 1) {
         if (T == 1) {
-            mk::copy_row_kernel<<<(unsigned)((d + 255) / 256), 256, 0, st>>>(
-                L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(), (int)d, routed, routed_scale);
-            CKL(ctx);
+            KLAUNCH(st, (unsigned)((d + 255) / 256), 256, 0, (mk::copy_row_kernel), L->tok_out.as<int32_t>(),
+                    L->tok_scale.as<Scale>(), (int)d, routed, routed_scale);
         }
     } else {
         if (L->world == 1) {
-            mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, 0, scal_scale(L, SL_COMMON),
-                                                        nullptr);
-            CKL(ctx);
+            KLAUNCH(st, 1, 1024, 0, (mk::common_scale_kernel), L->tok_scale.as<Scale>(), (int)T, 0,
+                    scal_scale(L, SL_COMMON), nullptr, nullptr);
         } else {
             CK(L->ep_rec.ensure(3 * 8));
             CK(L->ep_recs.ensure(L->world * 3 * 8));
             CK(L->ep_best_idx.ensure(4));
             if (T > 0) {
-                mk::common_scale_kernel<<<1, 1024, 0, st>>>(L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
-                                                            scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
-                                                            tok_info);
-                CKL(ctx);
-                mk::scale_record_kernel<<<1, 1, 0, st>>>(scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
-                                                         L->ep_rec.as<int64_t>());
-                CKL(ctx);
+                KLAUNCH(st, 1, 1024, 0, (mk::common_scale_kernel), L->tok_scale.as<Scale>(), (int)T, (int)tok_offset,
+                        scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(), tok_info);
+                KLAUNCH(st, 1, 1, 0, (mk::scale_record_kernel), scal_scale(L, SL_COMMON), L->ep_best_idx.as<int>(),
+                        L->ep_rec.as<int64_t>());
             } else {
-                mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
-                CKL(ctx);
+                KLAUNCH(st, 1, 1, 0, (mk::empty_record_kernel), L->ep_rec.as<int64_t>());
             }
             if (L->peer.on) {
-                ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_REC, L->ep_rec.as<unsigned long long>(),
-                                                      3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
-                CKL(ctx);
+                KLAUNCH(st, 1, 32, 0, (ep::exchange_kernel), L->peer.P, ep::P_REC, L->ep_rec.as<unsigned long long>(),
+                        3, L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
             } else {
                 NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
             }
-            mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, scal_scale(L, SL_COMMON));
-            CKL(ctx);
+            KLAUNCH(st, 1, 1, 0, (mk::reduce_records_kernel), L->ep_recs.as<int64_t>(), L->world,
+                    scal_scale(L, SL_COMMON));
         }
         if (T > 0) {
-            mk::merge_max_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
-                                                            (int)T, (int)d, scal_scale(L, SL_COMMON),
-                                                            scal_u64(L, U_MERGE_GMAX));
-            CKL(ctx);
+            KLAUNCH(st, (unsigned)T, 256, 0, (mk::merge_max_kernel), L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
+                    (int)T, (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX));
         }
         if (int r = allreduce_max(L, scal_u64(L, U_MERGE_GMAX), 1, st, ep::P_MERGE)) return r;
         if (T > 0) {
-            mk::merge_final_kernel<<<(unsigned)T, 256, 0, st>>>(L->tok_out.as<int32_t>(), L->tok_scale.as<Scale>(),
-                                                              (int)T, (int)d, scal_scale(L, SL_COMMON),
-                                                              scal_u64(L, U_MERGE_GMAX), routed, routed_scale,
-                                                              tok_info ? tok_info + 1 : nullptr);
-            CKL(ctx);
+            KLAUNCH(st, (unsigned)T, 256, 0, (mk::merge_final_kernel), L->tok_out.as<int32_t>(),
+                    L->tok_scale.as<Scale>(), (int)T, (int)d, scal_scale(L, SL_COMMON), scal_u64(L, U_MERGE_GMAX),
+                    routed, routed_scale, tok_info ? tok_info + 1 : nullptr);
         }
     }
     MARK(L, st);
@@ -1646,19 +1687,15 @@ int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset
     if (L->sgate_set) {  // add(routed, gated shared output) of two int32 tensors
         Scale* plan = scal_scale(L, SL_ADD2);
         if (T > 0) {
-            mk::add2_prepare_kernel<<<1, 1, 0, st>>>(routed_scale, scal_scale(L, SL_GATED), plan);
-            CKL(ctx);
-            mk::add2_max_kernel<<<red_blocks, 256, 0, st>>>(routed, L->y_gated.as<int32_t>(), n, plan,
-                                                            scal_u64(L, U_ADDGMAX));
-            CKL(ctx);
+            KLAUNCH(st, 1, 1, 0, (mk::add2_prepare_kernel), routed_scale, scal_scale(L, SL_GATED), plan);
+            KLAUNCH(st, red_blocks, 256, 0, (mk::add2_max_kernel), routed, L->y_gated.as<int32_t>(), n, plan,
+                    scal_u64(L, U_ADDGMAX));
         }
         if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st, ep::P_ADD)) return r;
         if (T > 0) {
-            mk::add2_final_kernel<<<red_blocks, 256, 0, st>>>(routed, L->y_gated.as<int32_t>(), n, plan,
-                                                              scal_u64(L, U_ADDGMAX), y_dev);
-            CKL(ctx);
-            mk::gmax_scale_kernel<<<1, 1, 0, st>>>(plan, scal_u64(L, U_ADDGMAX), ys_dev);
-            CKL(ctx);
+            KLAUNCH(st, red_blocks, 256, 0, (mk::add2_final_kernel), routed, L->y_gated.as<int32_t>(), n, plan,
+                    scal_u64(L, U_ADDGMAX), y_dev);
+            KLAUNCH(st, 1, 1, 0, (mk::gmax_scale_kernel), plan, scal_u64(L, U_ADDGMAX), ys_dev);
         }
         MARK(L, st);
         return KTMOE_OK;
@@ -1676,21 +1713,18 @@ int merge_and_add(ktmoe_layer* L, int64_t T, int64_t T_total, int64_t tok_offset
     aa.y = y_dev;
     aa.y_scale = ys_dev;
     if (T > 0) {
-        mk::add_prepare_kernel<<<1, 1, 0, st>>>(aa);
-        CKL(ctx);
-        mk::add_max_kernel<<<red_blocks, 256, 0, st>>>(aa);
-        CKL(ctx);
+        KLAUNCH(st, 1, 1, 0, (mk::add_prepare_kernel), aa);
+        KLAUNCH(st, red_blocks, 256, 0, (mk::add_max_kernel), aa);
     }
     if (int r = allreduce_max(L, scal_u64(L, U_ADDGMAX), 1, st, ep::P_ADD)) return r;
     if (T > 0) {
-        mk::add_final_kernel<<<red_blocks, 256, 0, st>>>(aa);
-        CKL(ctx);
+        KLAUNCH(st, red_blocks, 256, 0, (mk::add_final_kernel), aa);
     }
     MARK(L, st);
     return KTMOE_OK;
 }
 
-__global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { *p = v; }
+__global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { kt::pdl_enter(); *p = v; }
 
 int ensure_block(ktmoe_layer* L, int64_t T) {
     ktmoe_ctx* ctx = L->ctx;
@@ -1724,78 +1758,63 @@ int stage_block(ktmoe_layer* L, int64_t T, const int32_t* x_dev, const Scale* xs
     int32_t* m = L->blk_m.as<int32_t>();
     CK(cudaMemsetAsync(u, 0, 2 * 8, st));
     if (L->peer.on) {
-        ep::seq_bump_kernel<<<1, 1, 0, st>>>(L->peer.P);
-        CKL(ctx);
+        KLAUNCH(st, 1, 1, 0, (ep::seq_bump_kernel), L->peer.P);
     }
     const int* off = nullptr;
     if (L->world > 1) {
         // every rank's row count, for this rank's first global row (the tie rule of the common scale)
-        set_u64_kernel<<<1, 1, 0, st>>>(u + 2, (unsigned long long)T);
-        CKL(ctx);
+        KLAUNCH(st, 1, 1, 0, (set_u64_kernel), u + 2, (unsigned long long)T);
         if (L->peer.on) {
-            ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_TOK, u + 2, 1, u + 3, nullptr, ctx->d_err);
-            CKL(ctx);
+            KLAUNCH(st, 1, 32, 0, (ep::exchange_kernel), L->peer.P, ep::P_TOK, u + 2, 1, u + 3, nullptr, ctx->d_err);
         } else {
             NK(ncclAllGather(u + 2, u + 3, 1, ncclUint64, L->comm, st));
         }
-        mk::row_offset_kernel<<<1, 1, 0, st>>>(u + 3, L->rank, L->blk_off.as<int>());
-        CKL(ctx);
+        KLAUNCH(st, 1, 1, 0, (mk::row_offset_kernel), u + 3, L->rank, L->blk_off.as<int>());
         off = L->blk_off.as<int>();
     }
     if (T > 0) {
-        mk::rms_rows_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, (int)T, (int)d, xs_dev, L->norm_ws, L->norm_eps, c);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::rms_rows_kernel), x_dev, (int)T, (int)d, xs_dev, L->norm_ws, L->norm_eps,
+                c);
     }
     if (L->world == 1) {
-        mk::common_scale_kernel<<<1, 1024, 0, st>>>(c, (int)T, 0, sc, nullptr);
-        CKL(ctx);
+        KLAUNCH(st, 1, 1024, 0, (mk::common_scale_kernel), c, (int)T, 0, sc, nullptr, nullptr);
     } else {
         if (T > 0) {
-            mk::common_scale_kernel<<<1, 1024, 0, st>>>(c, (int)T, 0, sc, L->ep_best_idx.as<int>(), off);
-            CKL(ctx);
-            mk::scale_record_kernel<<<1, 1, 0, st>>>(sc, L->ep_best_idx.as<int>(), L->ep_rec.as<int64_t>());
-            CKL(ctx);
+            KLAUNCH(st, 1, 1024, 0, (mk::common_scale_kernel), c, (int)T, 0, sc, L->ep_best_idx.as<int>(), off);
+            KLAUNCH(st, 1, 1, 0, (mk::scale_record_kernel), sc, L->ep_best_idx.as<int>(), L->ep_rec.as<int64_t>());
         } else {
-            mk::empty_record_kernel<<<1, 1, 0, st>>>(L->ep_rec.as<int64_t>());
-            CKL(ctx);
+            KLAUNCH(st, 1, 1, 0, (mk::empty_record_kernel), L->ep_rec.as<int64_t>());
         }
         if (L->peer.on) {
-            ep::exchange_kernel<<<1, 32, 0, st>>>(L->peer.P, ep::P_NREC, L->ep_rec.as<unsigned long long>(), 3,
-                                                  L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
-            CKL(ctx);
+            KLAUNCH(st, 1, 32, 0, (ep::exchange_kernel), L->peer.P, ep::P_NREC, L->ep_rec.as<unsigned long long>(), 3,
+                    L->ep_recs.as<unsigned long long>(), nullptr, ctx->d_err);
         } else {
             NK(ncclAllGather(L->ep_rec.p, L->ep_recs.p, 3, ncclInt64, L->comm, st));
         }
-        mk::reduce_records_kernel<<<1, 1, 0, st>>>(L->ep_recs.as<int64_t>(), L->world, sc);
-        CKL(ctx);
+        KLAUNCH(st, 1, 1, 0, (mk::reduce_records_kernel), L->ep_recs.as<int64_t>(), L->world, sc);
     }
     if (T > 0) {
-        mk::rms_max_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc, u);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::rms_max_kernel), x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc,
+                u);
     }
     if (int r = allreduce_max(L, u, 1, st, ep::P_NMAX)) return r;
     if (T > 0) {
-        mk::rms_final_kernel<<<(unsigned)T, 256, 0, st>>>(x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc, u, xn);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)T, 256, 0, (mk::rms_final_kernel), x_dev, L->b_norm.as<int32_t>(), (int)T, (int)d, c, sc,
+                u, xn);
     }
-    mk::gmax_scale_kernel<<<1, 1, 0, st>>>(sc, u, sc + 2);
-    CKL(ctx);
+    KLAUNCH(st, 1, 1, 0, (mk::gmax_scale_kernel), sc, u, sc + 2);
     if (int r = stage_forward(L, T, xn, sc + 2, m, sc + 3, st, false)) return r;
     const int64_t n = T * d;
     const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>(1184, (n + 255) / 256));
-    mk::add2_prepare_kernel<<<1, 1, 0, st>>>(xs_dev, sc + 3, sc + 4);
-    CKL(ctx);
+    KLAUNCH(st, 1, 1, 0, (mk::add2_prepare_kernel), xs_dev, sc + 3, sc + 4);
     if (T > 0) {
-        mk::add2_max_kernel<<<rb, 256, 0, st>>>(x_dev, m, n, sc + 4, u + 1);
-        CKL(ctx);
+        KLAUNCH(st, rb, 256, 0, (mk::add2_max_kernel), x_dev, m, n, sc + 4, u + 1);
     }
     if (int r = allreduce_max(L, u + 1, 1, st, ep::P_RADD)) return r;
     if (T > 0) {
-        mk::add2_final_kernel<<<rb, 256, 0, st>>>(x_dev, m, n, sc + 4, u + 1, y_dev);
-        CKL(ctx);
+        KLAUNCH(st, rb, 256, 0, (mk::add2_final_kernel), x_dev, m, n, sc + 4, u + 1, y_dev);
     }
-    mk::gmax_scale_kernel<<<1, 1, 0, st>>>(sc + 4, u + 1, ys_dev);
-    CKL(ctx);
+    KLAUNCH(st, 1, 1, 0, (mk::gmax_scale_kernel), sc + 4, u + 1, ys_dev);
     return KTMOE_OK;
 }
 
@@ -1864,9 +1883,8 @@ int upload_matrix(ktmoe_ctx* ctx, const Planes& P, int64_t g, const int32_t* cod
     CK(cudaMemsetAsync(bad.p, 0, 8, ctx->stream));
     CK(cudaMemcpyAsync(tmp.p, codes, (size_t)rows * k * 4, cudaMemcpyHostToDevice, ctx->stream));
     int8_t* base = P.ptr + (g * 3) * P.rows_pad * P.k_pad + row0 * P.k_pad;
-    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, ctx->stream>>>(tmp.as<int32_t>(), rows, (int)k, (int)P.k_pad,
-                                                                   P.rows_pad, base, bad.as<unsigned long long>());
-    CKL(ctx);
+    KLAUNCH(ctx->stream, (unsigned)rows, 128, 0, (mk::pack_codes_kernel), tmp.as<int32_t>(), rows, (int)k, (int)P.k_pad,
+            P.rows_pad, base, bad.as<unsigned long long>(), nullptr, 0, nullptr);
     unsigned long long hbad = 0;
     CK(cudaMemcpyAsync(&hbad, bad.p, 8, cudaMemcpyDeviceToHost, ctx->stream));
     CK(cudaStreamSynchronize(ctx->stream));
@@ -2084,9 +2102,8 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
         CK(cudaMemsetAsync(target->p, 0, wbytes, st));
         CK(ctx->lin_wi.ensure((size_t)(out * k) * 4));
         CK(cudaMemcpyAsync(ctx->lin_wi.p, w, (size_t)(out * k) * 4, cudaMemcpyHostToDevice, st));
-        mk::pack_codes_kernel<<<(unsigned)out, 128, 0, st>>>(ctx->lin_wi.as<int32_t>(), out, (int)k, (int)k_pad, out_pad,
-                                                            target->as<int8_t>(), counters, counters + 1, 3280);
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)out, 128, 0, (mk::pack_codes_kernel), ctx->lin_wi.as<int32_t>(), out, (int)k, (int)k_pad,
+                out_pad, target->as<int8_t>(), counters, counters + 1, 3280, nullptr);
         CK(cudaMemcpyAsync(hbad_w, ctx->lin_bad.p, 16, cudaMemcpyDeviceToHost, st));
         CK(cudaStreamSynchronize(st));
         small_w = hbad_w[1] == 0;
@@ -2123,11 +2140,9 @@ static int linear_impl(ktmoe_ctx* ctx, const uint64_t* weight_id, const int32_t*
     // with small weights, the activations are also written as one raw plane and their range decides the kernel
     const bool try_small = small_enabled && small_w;
     if (try_small) CK(ctx->lin_xr.ensure((size_t)(rows_pad * k_pad)));
-    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, st>>>(ctx->lin_xi.as<int32_t>(), rows, (int)k, (int)k_pad, rows_pad,
-                                                         ctx->lin_xp.as<int8_t>(), counters,
-                                                         try_small ? counters + 2 : nullptr, 127,
-                                                         try_small ? ctx->lin_xr.as<int8_t>() : nullptr);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)rows, 128, 0, (mk::pack_codes_kernel), ctx->lin_xi.as<int32_t>(), rows, (int)k, (int)k_pad,
+            rows_pad, ctx->lin_xp.as<int8_t>(), counters, try_small ? counters + 2 : nullptr, 127,
+            try_small ? ctx->lin_xr.as<int8_t>() : nullptr);
     bool small = false;
     if (try_small) {
         CK(cudaMemcpyAsync(ctx->h_status + 2, counters + 2, 8, cudaMemcpyDeviceToHost, st));
@@ -2276,6 +2291,11 @@ static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank,
             return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
         if (cudaFuncSetAttribute(mk::combine_y_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(L->d * 8)) !=
             cudaSuccess)
+            return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
+        if (cudaFuncSetAttribute(mk::combine_tok_kernel<false, mk::CombineArgs>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess ||
+            cudaFuncSetAttribute(mk::combine_tok_kernel<true, mk::CombineYArgs>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, cs) != cudaSuccess)
             return bail(fail(ctx, KTMOE_ERR_CUDA, "combine shared memory"));
     }
     if (world > 1) {
@@ -2469,9 +2489,8 @@ int ktmoe_check_wait_expiry(ktmoe_ctx* ctx) {
     P.world = 2;
     P.rank = 0;
     P.seq = words.as<unsigned long long>();
-    ep::exchange_kernel<<<1, 32, 0, st>>>(P, ep::P_MERGE, words.as<unsigned long long>() + 1, 1, nullptr,
-                                          words.as<unsigned long long>() + 2, ctx->d_err);
-    CKL(ctx);
+    KLAUNCH(st, 1, 32, 0, (ep::exchange_kernel), P, ep::P_MERGE, words.as<unsigned long long>() + 1, 1, nullptr,
+            words.as<unsigned long long>() + 2, ctx->d_err);
     CK(cudaStreamSynchronize(st));
     return check_err_word(ctx);  // KTMOE_ERR_KERNEL with the wait's code; the error word is cleared
 }
@@ -2632,11 +2651,9 @@ int synth_matrix(ktmoe_ctx* ctx, uint64_t seed, float sigma, uint64_t offset, co
     CK(fbuf.ensure((size_t)n * 4));
     CK(cbuf.ensure((size_t)n * 4));
     const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, ctx->num_sms * 8));
-    sy::portable_normal_kernel<<<grid, 256, 0, st>>>(seed, sigma, offset, n, fbuf.as<float>());
-    CKL(ctx);
+    KLAUNCH(st, grid, 256, 0, (sy::portable_normal_kernel), seed, sigma, offset, n, fbuf.as<float>());
     CK(cudaMemsetAsync(wbuf.p, 0, 4, st));  // the peak; word 1 counts codes out of range over the whole layer
-    sy::absmax_f32_kernel<<<grid, 256, 0, st>>>(fbuf.as<float>(), n, wbuf.as<unsigned>());
-    CKL(ctx);
+    KLAUNCH(st, grid, 256, 0, (sy::absmax_f32_kernel), fbuf.as<float>(), n, wbuf.as<unsigned>());
     unsigned pbits = 0;
     CK(cudaMemcpyAsync(&pbits, wbuf.p, 4, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
@@ -2647,14 +2664,12 @@ int synth_matrix(ktmoe_ctx* ctx, uint64_t seed, float sigma, uint64_t offset, co
         *scale = Scale{0, 0};
     } else {
         const double step = (double)peak / (double)kt::WLEVELS;
-        sy::quantize_kernel<<<grid, 256, 0, st>>>(fbuf.as<float>(), n, step, cbuf.as<int32_t>());
-        CKL(ctx);
+        KLAUNCH(st, grid, 256, 0, (sy::quantize_kernel), fbuf.as<float>(), n, step, cbuf.as<int32_t>());
         *scale = S(hp::scale_from_f64(step));
     }
     int8_t* base = P.ptr + (g * 3) * P.rows_pad * P.k_pad + row0 * P.k_pad;
-    mk::pack_codes_kernel<<<(unsigned)rows, 128, 0, st>>>(cbuf.as<int32_t>(), rows, (int)k, (int)P.k_pad, P.rows_pad,
-                                                          base, wbuf.as<unsigned long long>() + 1);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)rows, 128, 0, (mk::pack_codes_kernel), cbuf.as<int32_t>(), rows, (int)k, (int)P.k_pad,
+            P.rows_pad, base, wbuf.as<unsigned long long>() + 1, nullptr, 0, nullptr);
     return KTMOE_OK;
 }
 
@@ -2753,13 +2768,11 @@ int ktmoe_layer_synth_weights(ktmoe_layer* L, uint64_t seed, float sigma, float 
             // the gate's d codes through the same device quantiser, then into the gate buffer (zero-padded to d_pad)
             CK(fbuf.ensure((size_t)d * 4));
             CK(cbuf.ensure((size_t)L->d_pad * 4));
-            sy::portable_normal_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(
-                seed, sigma, o + 3 * fs * d, d, fbuf.as<float>());
-            CKL(ctx);
+            KLAUNCH(ctx->stream, (unsigned)((d + 255) / 256), 256, 0, (sy::portable_normal_kernel), seed, sigma,
+                    o + 3 * fs * d, d, fbuf.as<float>());
             CK(cudaMemsetAsync(wbuf.p, 0, 4, ctx->stream));
-            sy::absmax_f32_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(fbuf.as<float>(), d,
-                                                                                         wbuf.as<unsigned>());
-            CKL(ctx);
+            KLAUNCH(ctx->stream, (unsigned)((d + 255) / 256), 256, 0, (sy::absmax_f32_kernel), fbuf.as<float>(), d,
+                    wbuf.as<unsigned>());
             unsigned pbits = 0;
             CK(cudaMemcpyAsync(&pbits, wbuf.p, 4, cudaMemcpyDeviceToHost, ctx->stream));
             CK(cudaStreamSynchronize(ctx->stream));
@@ -2769,9 +2782,8 @@ int ktmoe_layer_synth_weights(ktmoe_layer* L, uint64_t seed, float sigma, float 
             L->sgate_ws = Scale{0, 0};
             if (peak > 0.0f) {
                 const double step = (double)peak / (double)kt::WLEVELS;
-                sy::quantize_kernel<<<(unsigned)((d + 255) / 256), 256, 0, ctx->stream>>>(fbuf.as<float>(), d, step,
-                                                                                            cbuf.as<int32_t>());
-                CKL(ctx);
+                KLAUNCH(ctx->stream, (unsigned)((d + 255) / 256), 256, 0, (sy::quantize_kernel), fbuf.as<float>(), d,
+                        step, cbuf.as<int32_t>());
                 L->sgate_ws = S(hp::scale_from_f64(step));
             }
             CK(L->b_sgate.ensure(L->d_pad * 4));
@@ -2812,8 +2824,7 @@ int ktmoe_synth_normal_portable_dev(ktmoe_ctx* ctx, uint64_t seed, float sigma, 
     if (int r = set_device(ctx)) return r;
     if (n == 0) return KTMOE_OK;
     const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, ctx->num_sms * 8));
-    sy::portable_normal_kernel<<<grid, 256, 0, ctx->stream>>>(seed, sigma, offset, n, out_dev);
-    CKL(ctx);
+    KLAUNCH(ctx->stream, grid, 256, 0, (sy::portable_normal_kernel), seed, sigma, offset, n, out_dev);
     CK(cudaStreamSynchronize(ctx->stream));
     return KTMOE_OK;
 }
@@ -3146,11 +3157,9 @@ int ktmoe_layer_expert_forward(ktmoe_layer* L, const int32_t* x, int64_t rows, k
         xr.row_expert = L->row_expert.as<int>();
         xr.row_sqx = L->tok_sqx.as<Scale>();
         if (int r = run_experts(L, xr, st)) return r;
-        mk::seam_out_kernel<<<(unsigned)R, 256, 0, st>>>(
-            L->acc_d.as<int64_t>(), L->rowmax_d.as<unsigned long long>(), L->row_cd.as<Scale>(),
-            L->row_assign.as<int>(), (int)R, (int)d, (int)K, Kc, n_ids, j0, L->seam_ids.as<int32_t>(),
-            L->seam_y.as<int32_t>(), L->seam_ys.as<Scale>());
-        CKL(ctx);
+        KLAUNCH(st, (unsigned)R, 256, 0, (mk::seam_out_kernel), L->acc_d.as<int64_t>(),
+                L->rowmax_d.as<unsigned long long>(), L->row_cd.as<Scale>(), L->row_assign.as<int>(), (int)R, (int)d,
+                (int)K, Kc, n_ids, j0, L->seam_ids.as<int32_t>(), L->seam_y.as<int32_t>(), L->seam_ys.as<Scale>());
         // te is reused by the next chunk: its copy must have left the host buffer first
         CK(cudaStreamSynchronize(st));
     }
@@ -3213,8 +3222,8 @@ int ktmoe_layer_forward_with_experts(ktmoe_layer* L, const int32_t* x, int64_t r
     CK(cudaMemcpyAsync(L->sumc.p, sumc.data(), (size_t)T * 8, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(L->seam_y.p, ye.data(), (size_t)(R * d) * 4, cudaMemcpyHostToDevice, st));
     CK(cudaMemcpyAsync(L->seam_ys.p, ys_h.data(), (size_t)R * sizeof(Scale), cudaMemcpyHostToDevice, st));
-    mk::iota_kernel<<<(unsigned)std::min<int64_t>((R + 255) / 256, 1024), 256, 0, st>>>(L->slot_row.as<int>(), R);
-    CKL(ctx);
+    KLAUNCH(st, (unsigned)std::min<int64_t>((R + 255) / 256, 1024), 256, 0, (mk::iota_kernel), L->slot_row.as<int>(),
+            R);
     mk::CombineYArgs ca;
     ca.y = L->seam_y.as<int32_t>();
     ca.ys = L->seam_ys.as<Scale>();
@@ -3228,10 +3237,7 @@ int ktmoe_layer_forward_with_experts(ktmoe_layer* L, const int32_t* x, int64_t r
     ca.out_scale = L->tok_scale.as<Scale>();
     const mk::CombinePlan cp{L->cp_n.as<int>(), L->cp_common.as<Scale>(), L->cp_row.as<int>(),
                              L->cp_ec.as<int64_t>(), L->cp_ry.as<kt::ReqDiv>(), L->cp_f.as<kt::ApplyPlan>()};
-    mk::combine_y_plan_kernel<<<(unsigned)((T + 127) / 128), 128, 0, st>>>(ca, cp);
-    CKL(ctx);
-    mk::combine_y_kernel<<<(unsigned)T, 256, d * 8, st>>>(ca, cp);
-    CKL(ctx);
+    if (int r = launch_combine<true>(L, ca, cp, T, st)) return r;
     if (int r = merge_and_add(L, T, T, 0, L->x_in.as<int32_t>(), scal_scale(L, SL_XSCALE), L->y_out.as<int32_t>(),
                               scal_scale(L, SL_YSCALE), st, false))
         return r;

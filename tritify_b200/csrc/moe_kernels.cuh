@@ -72,6 +72,7 @@ __device__ __forceinline__ void store_digits4(int8_t* p0, int8_t* p1, int8_t* p2
 __global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K, int K_pad, long long R_pad,
                                   int8_t* __restrict__ planes, int64_t* __restrict__ row_xmax, Scale* __restrict__ row_sqx,
                                   const Scale* __restrict__ x_scale, const unsigned long long* __restrict__ gxmax) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const int r = blockIdx.x;
     if (r >= rows) return;
@@ -122,6 +123,7 @@ __global__ void quant_rows_kernel(const int32_t* __restrict__ x, int rows, int K
 
 // Global max |x| over n values (atomicMax into *out, which the caller zeroes).
 __global__ void absmax_i32_kernel(const int32_t* __restrict__ v, long long n, unsigned long long* out) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     uint64_t m = 0;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
@@ -133,6 +135,7 @@ __global__ void absmax_i32_kernel(const int32_t* __restrict__ v, long long n, un
 // Global max |v| over the columns [c0, c0 + cols) of rows x ld int64 (atomicMax into *out).
 __global__ void absmax_i64_cols_kernel(const int64_t* __restrict__ v, int rows, long long ld, int c0, int cols,
                                        unsigned long long* out) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     uint64_t m = 0;
     const long long n = (long long)rows * cols;
@@ -166,6 +169,7 @@ constexpr int ROUTE_MAX_PER_LANE = 16;  // E <= 512
 
 // One warp per token.
 __global__ void route_kernel(const RouteArgs a) {
+    kt::pdl_enter();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= a.rows) return;
@@ -312,6 +316,7 @@ constexpr int PLAN_CHUNK = 2048;  // assignments per chunk
 constexpr int PLAN_THREADS = 256;
 
 __global__ void plan_count_kernel(const int32_t* __restrict__ top_e, long long n_assign, int E, int* __restrict__ counts) {
+    kt::pdl_enter();
     extern __shared__ int hist[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
     __syncthreads();
@@ -336,6 +341,7 @@ struct TileTable {
 __global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, int E, int* __restrict__ chunk_off,
                                  int* __restrict__ expert_off, int* __restrict__ group_end,
                                  int* __restrict__ expert_count, TileTable ta, TileTable tb) {
+    kt::pdl_enter();
     extern __shared__ int sh[];
     int* tot = sh;             // [E]
     int* toff_a = sh + E;      // [E] tile offsets, table a
@@ -383,6 +389,7 @@ __global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, i
 __global__ void plan_assign_kernel(const int32_t* __restrict__ top_e, long long n_assign, int E,
                                    const int* __restrict__ chunk_off, const int* __restrict__ expert_off,
                                    int* __restrict__ slot_row, int* __restrict__ row_assign, int* __restrict__ row_expert) {
+    kt::pdl_enter();
     extern __shared__ int sm[];
     const int nw = blockDim.x >> 5;
     int* running = sm;           // [E]
@@ -427,6 +434,7 @@ __global__ void plan_assign_kernel(const int32_t* __restrict__ top_e, long long 
 __global__ void permute_planes_kernel(const int8_t* __restrict__ src, long long src_R_pad, int8_t* __restrict__ dst,
                                       long long dst_R_pad, int K_pad, const int* __restrict__ row_assign, int top_k,
                                       int n_rows) {
+    kt::pdl_enter();
     const int r = blockIdx.x;
     if (r >= n_rows) return;
     const int t = row_assign[r] / top_k;
@@ -593,6 +601,9 @@ struct SwigluArgs {
     unsigned long long* g_hmax;  // tensor-global mode: phase 1 reduces max |h| here, phase 2 reads it
     int phase;  // 0: per-row (routed, one kernel); 1: global h pass; 2: global quantise pass
     const int* rows_dev;  // routed rows counted on the device (rows is then an upper bound), or nullptr
+    // swiglu_rows_kernel only: each row's block computes the row's plan (thread 0, before its loads) and its down
+    // linear's c (thread 0, at the end) itself, in place of swiglu_plan_kernel and down_c_kernel
+    int inline_plan;
 };
 
 __device__ __forceinline__ int swiglu_rows(const SwigluArgs& a) { return a.rows_dev ? *a.rows_dev : a.rows; }
@@ -618,6 +629,7 @@ __device__ __forceinline__ SwigluScales swiglu_scales(const SwigluArgs& a, int t
 // The per-row scale plans, one thread per row (one thread in the tensor-global mode), so that the element kernels
 // start without a serial prologue.
 __global__ void swiglu_plan_kernel(const SwigluArgs a) {
+    kt::pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (a.ymax_stride == 0) {
         if (r == 0) a.plans[0] = swiglu_scales(a, 0, 0, (int64_t)a.ymax[0], (int64_t)a.ymax[1]);
@@ -657,6 +669,7 @@ __device__ __forceinline__ Scale down_c(const SwigluArgs& a, Scale us, int64_t h
 
 // Per routed row: the down linear's c from the row's plan and max |h|, one thread per row.
 __global__ void down_c_kernel(const SwigluArgs a) {
+    kt::pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= swiglu_rows(a)) return;
     const int e = a.row_expert ? a.row_expert[r] : 0;
@@ -708,18 +721,30 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
 }
 
 // Phase 0: blocks walk the routed rows (row r, r + gridDim.x, ...); h stays in shared memory (dynamic, f int64) when
-// `h_smem`. U independent elements per thread per step. The row's scales come from swiglu_plan_kernel; its max |h|
-// goes to row_hmax.
+// `h_smem`. U independent elements per thread per step. The row's scales come from swiglu_plan_kernel, or with
+// a.inline_plan from thread 0 of the row's block (then also the down linear's c, at the end); its max |h| goes to
+// row_hmax.
 template <int U>
 __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem, int v2) {
+    kt::pdl_enter();
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
+    __shared__ SwigluScales q_s;
     const int n = swiglu_rows(a);
     const int f = a.f;
     for (int r = blockIdx.x; r < n; r += gridDim.x) {
         int64_t* accg = a.acc + (long long)r * 2 * f;
         const int64_t* accu = accg + f;
-        const SwigluScales q = a.plans[r];
+        if (a.inline_plan) {
+            if (threadIdx.x == 0) {
+                const int e = a.row_expert ? a.row_expert[r] : 0;
+                const int t = a.row_assign ? a.row_assign[r] / a.top_k : r;
+                q_s = swiglu_scales(a, t, e, (int64_t)a.ymax[(long long)r * a.ymax_stride],
+                                    (int64_t)a.ymax[(long long)r * a.ymax_stride + 1]);
+            }
+            __syncthreads();
+        }
+        const SwigluScales q = a.inline_plan ? q_s : a.plans[r];
         int64_t* h = h_smem ? hs : accg;
         uint64_t hm = 0;
         // the loads of a step are issued before its arithmetic
@@ -792,8 +817,11 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
         }
         const int64_t hmax = (int64_t)block_max_u64(hm, red);  // its barriers also publish h
         write_down_planes(a, r, h, hmax, v2 != 0);
-        if (threadIdx.x == 0) a.row_hmax[r] = (unsigned long long)hmax;
-        __syncthreads();  // h (and red) are reused by the next row
+        if (threadIdx.x == 0) {
+            a.row_hmax[r] = (unsigned long long)hmax;
+            if (a.inline_plan) a.row_cd[r] = down_c(a, q.us, hmax, a.row_expert ? a.row_expert[r] : 0);
+        }
+        __syncthreads();  // h, red and q_s are reused by the next row
     }
 }
 
@@ -841,6 +869,7 @@ __device__ __forceinline__ void st_cluster_u64(uint64_t* local, uint32_t rank, u
 
 template <int G, int NT>
 __global__ void __launch_bounds__(NT, 2048 / (NT * G)) swiglu_cluster_kernel(const SwigluArgs a) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     __shared__ uint64_t part[8];
     const int r = (int)cluster_id_x();
@@ -955,6 +984,7 @@ __global__ void __launch_bounds__(NT, 2048 / (NT * G)) swiglu_cluster_kernel(con
 // shared memory between two cluster barriers. U elements per thread per step as in swiglu_rows_kernel.
 template <int U>
 __global__ void __launch_bounds__(256, 3) swiglu_slice_kernel(const SwigluArgs a) {
+    kt::pdl_enter();
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
     __shared__ uint64_t part[8];
@@ -1021,6 +1051,7 @@ __global__ void __launch_bounds__(256, 3) swiglu_slice_kernel(const SwigluArgs a
 
 // Phases 1 and 2: the shared expert, whose maxima are over the whole tensor (one block per row each phase; one plan).
 __global__ void swiglu_global_kernel(const SwigluArgs a) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const int r = blockIdx.x;
     if (r >= a.rows) return;
@@ -1053,6 +1084,21 @@ __global__ void swiglu_global_kernel(const SwigluArgs a) {
     if (r == 0 && threadIdx.x == 0) a.row_cd[0] = down_c(a, a.plans[0].us, hmax, 0);
 }
 
+// A common scale is the LAST item whose scale value is maximal (fold `if b.ge(a) {b} else {a}`, over a token's slots
+// in combine and over the tokens in merge): a reduction over (exact value, index), the larger index winning ties,
+// gives the same item for any partition.
+struct ScaleIdx {
+    Scale s;
+    int idx;
+};
+
+__device__ __forceinline__ ScaleIdx better(ScaleIdx x, ScaleIdx y) {
+    const bool xy = kt::scale_ge(x.s, y.s), yx = kt::scale_ge(y.s, x.s);
+    if (xy && !yx) return x;
+    if (yx && !xy) return y;
+    return x.idx > y.idx ? x : y;
+}
+
 // ───────────── combine: one token's selected experts → its output (layers.rs:893-923) ─────────────
 struct CombineArgs {
     const int64_t* acc_d;  // [rows][dim] down accumulators (expert-sorted rows)
@@ -1082,6 +1128,7 @@ struct CombinePlan {
 // One thread per token: ys_i = ratio_act(ymax_i)·c_i (zero when c_i or ymax_i is zero, layers.rs:300-302,
 // :321-326), common = the last of the largest (fold with ge, layers.rs:898), and the live slots' plans.
 __global__ void combine_plan_kernel(const CombineArgs a, const CombinePlan p) {
+    kt::pdl_enter();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= a.T) return;
     const int K = a.top_k;
@@ -1123,6 +1170,7 @@ __global__ void combine_plan_kernel(const CombineArgs a, const CombinePlan p) {
 constexpr int CE = 8;
 
 __global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, const CombinePlan p) {
+    kt::pdl_enter();
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
     __shared__ kt::ReqDiv ry_s[COMBINE_MAX_K];
@@ -1205,23 +1253,11 @@ __global__ void __launch_bounds__(256, 3) combine_kernel(const CombineArgs a, co
 }
 
 // ───────────── merge: per-token outputs → one tensor at one scale (layers.rs:1001-1019 / :866-886) ─────────────
-// The common scale is the LAST token whose scale value is maximal (fold `if b.ge(a) {b} else {a}`): a reduction over
-// (exact value, token index), larger index winning ties, gives the same token for any partition.
-struct ScaleIdx {
-    Scale s;
-    int idx;
-};
-
-__device__ __forceinline__ ScaleIdx better(ScaleIdx x, ScaleIdx y) {
-    const bool xy = kt::scale_ge(x.s, y.s), yx = kt::scale_ge(y.s, x.s);
-    if (xy && !yx) return x;
-    if (yx && !xy) return y;
-    return x.idx > y.idx ? x : y;
-}
 
 // One block: common scale over `n` scales (index offset idx0), result + its reciprocal into out[0..1].
 __global__ void common_scale_kernel(const Scale* __restrict__ scales, int n, int idx0, Scale* __restrict__ out,
                                     int* __restrict__ out_idx, const int* __restrict__ idx0_dev = nullptr) {
+    kt::pdl_enter();
     __shared__ ScaleIdx sm[1024];
     if (idx0_dev) idx0 = *idx0_dev;
     ScaleIdx b{kt::scale_zero(), -1};
@@ -1243,6 +1279,7 @@ __global__ void common_scale_kernel(const Scale* __restrict__ scales, int n, int
 // Pass 1 of the merge: max over all tokens of |f_t.apply(o_t[d])| (atomicMax into *gmax).
 __global__ void merge_max_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ o_scale, int T, int D,
                                  const Scale* __restrict__ common, unsigned long long* __restrict__ gmax) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const int t = blockIdx.x;
     if (t >= T) return;
@@ -1269,6 +1306,7 @@ __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* _
                                    const Scale* __restrict__ common, const unsigned long long* __restrict__ gmax_p,
                                    int32_t* __restrict__ y, Scale* __restrict__ y_scale,
                                    const int* __restrict__ t_total = nullptr) {
+    kt::pdl_enter();
     const int t = blockIdx.x;
     if (t >= T) return;
     if (t_total && *t_total == 1) {
@@ -1311,6 +1349,7 @@ __global__ void merge_final_kernel(const int32_t* __restrict__ o, const Scale* _
 // One token (rows == 1): the routed output is the combine output itself (layers.rs:992-994).
 __global__ void copy_row_kernel(const int32_t* __restrict__ o, const Scale* __restrict__ os, int D, int32_t* __restrict__ y,
                                 Scale* __restrict__ ys) {
+    kt::pdl_enter();
     for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < D; d += gridDim.x * blockDim.x) y[d] = o[d];
     if (blockIdx.x == 0 && threadIdx.x == 0) *ys = os[0];
 }
@@ -1332,6 +1371,7 @@ struct AddArgs {
 };
 
 __global__ void add_prepare_kernel(const AddArgs p) {
+    kt::pdl_enter();
     const int64_t ymax = (int64_t)*p.s_ymax;
     const Scale cd = *p.s_cd;
     const Scale ss = (cd.mant == 0 || ymax == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(ymax), cd);
@@ -1369,6 +1409,7 @@ __device__ __forceinline__ void add_sum4(const AddArgs& p, long long i, const kt
 }
 
 __global__ void add_max_kernel(const AddArgs p) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const kt::ApplyPlan fa = kt::make_apply(p.scratch[2]), fb = kt::make_apply(p.scratch[3]);
     const int64_t ymax = (int64_t)*p.s_ymax;
@@ -1390,6 +1431,7 @@ __global__ void add_max_kernel(const AddArgs p) {
 }
 
 __global__ void add_final_kernel(const AddArgs p) {
+    kt::pdl_enter();
     const kt::ApplyPlan fa = kt::make_apply(p.scratch[2]), fb = kt::make_apply(p.scratch[3]);
     const Scale common = p.scratch[1];
     const int64_t ymax = (int64_t)*p.s_ymax;
@@ -1422,6 +1464,7 @@ __global__ void add_final_kernel(const AddArgs p) {
 // One block per row: the row's C (the sum of squares in 128 bits, as the reference's i128).
 __global__ void rms_rows_kernel(const int32_t* __restrict__ x, int rows, int dim, const Scale* __restrict__ x_scale,
                                 Scale w_scale, Scale eps_scale, Scale* __restrict__ c) {
+    kt::pdl_enter();
     __shared__ unsigned long long part[2][256];
     const int r = blockIdx.x;
     if (r >= rows) return;
@@ -1446,6 +1489,7 @@ __global__ void rms_rows_kernel(const int32_t* __restrict__ x, int rows, int dim
 __global__ void rms_max_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ wcodes, int rows, int dim,
                                const Scale* __restrict__ c, const Scale* __restrict__ common,
                                unsigned long long* __restrict__ gmax) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const int r = blockIdx.x;
     if (r >= rows || common[0].mant == 0) return;
@@ -1462,6 +1506,7 @@ __global__ void rms_max_kernel(const int32_t* __restrict__ x, const int32_t* __r
 __global__ void rms_final_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ wcodes, int rows, int dim,
                                  const Scale* __restrict__ c, const Scale* __restrict__ common,
                                  const unsigned long long* __restrict__ gmax_p, int32_t* __restrict__ y) {
+    kt::pdl_enter();
     const int r = blockIdx.x;
     if (r >= rows) return;
     const int64_t gmax = (int64_t)*gmax_p;
@@ -1481,6 +1526,7 @@ __global__ void rms_final_kernel(const int32_t* __restrict__ x, const int32_t* _
 // The scale of a dynamic requant over a whole tensor: from_ratio(gmax, L)·common (zero when either is).
 __global__ void gmax_scale_kernel(const Scale* __restrict__ common, const unsigned long long* __restrict__ gmax_p,
                                   Scale* __restrict__ out) {
+    kt::pdl_enter();
     const int64_t gmax = (int64_t)*gmax_p;
     *out = (common[0].mant == 0 || gmax == 0) ? kt::scale_zero() : kt::scale_mul(kt::ratio_act(gmax), common[0]);
 }
@@ -1489,6 +1535,7 @@ __global__ void gmax_scale_kernel(const Scale* __restrict__ common, const unsign
 // fb.apply(b); one dynamic requant over the tensor. `plan` holds {common, fa, fb}.
 __global__ void add2_prepare_kernel(const Scale* __restrict__ a_scale, const Scale* __restrict__ b_scale,
                                     Scale* __restrict__ plan) {
+    kt::pdl_enter();
     const Scale as = *a_scale, bs = *b_scale;
     const Scale common = kt::scale_ge(as, bs) ? as : bs;
     plan[0] = common;
@@ -1503,6 +1550,7 @@ __global__ void add2_prepare_kernel(const Scale* __restrict__ a_scale, const Sca
 
 __global__ void add2_max_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ b, long long n,
                                 const Scale* __restrict__ plan, unsigned long long* __restrict__ gmax) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const kt::ApplyPlan fa = kt::make_apply(plan[1]), fb = kt::make_apply(plan[2]);
     uint64_t m = 0;
@@ -1516,6 +1564,7 @@ __global__ void add2_max_kernel(const int32_t* __restrict__ a, const int32_t* __
 __global__ void add2_final_kernel(const int32_t* __restrict__ a, const int32_t* __restrict__ b, long long n,
                                   const Scale* __restrict__ plan, const unsigned long long* __restrict__ gmax_p,
                                   int32_t* __restrict__ y) {
+    kt::pdl_enter();
     const kt::ApplyPlan fa = kt::make_apply(plan[1]), fb = kt::make_apply(plan[2]);
     const int64_t gmax = (int64_t)*gmax_p;
     const bool zero = plan[0].mant == 0 || gmax == 0;
@@ -1536,6 +1585,7 @@ __global__ void add2_final_kernel(const int32_t* __restrict__ a, const int32_t* 
 __global__ void gate_logit_kernel(const int8_t* __restrict__ planes, int T, int d_pad, long long R_pad,
                                   const int32_t* __restrict__ w, int64_t* __restrict__ acc,
                                   unsigned long long* __restrict__ ymax) {
+    kt::pdl_enter();
     const int t = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     if (t >= T) return;
     const int8_t* p0 = planes + (long long)t * d_pad;
@@ -1565,6 +1615,7 @@ __global__ void gate_logit_kernel(const int8_t* __restrict__ planes, int T, int 
 // zeros when that scale or ymax is zero, layers.rs:300-326) and its sigmoid code code_at(index(logit, scale)).
 __global__ void gate_code_kernel(const int64_t* __restrict__ acc, int T, const unsigned long long* __restrict__ ymax_p,
                                  const Scale* __restrict__ sqx, Scale w_scale, Lut sig, int64_t* __restrict__ code) {
+    kt::pdl_enter();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= T) return;
     const int64_t ymax = (int64_t)*ymax_p;
@@ -1598,6 +1649,7 @@ __device__ __forceinline__ int64_t gated_value(const GateArgs& p, bool live, con
 
 // Pass 1 (one block per token): max |code_t·y[t, j]| into *gmax.
 __global__ void gated_max_kernel(const GateArgs p) {
+    kt::pdl_enter();
     __shared__ uint64_t red[32];
     const int t = blockIdx.x;
     if (t >= p.T) return;
@@ -1614,6 +1666,7 @@ __global__ void gated_max_kernel(const GateArgs p) {
 
 // Pass 2: y[t, j] = requant_dyn(code_t·y_s[t, j], L, gmax); scale = ratio(gmax)·y_s.scale·code_scale.
 __global__ void gated_final_kernel(const GateArgs p) {
+    kt::pdl_enter();
     const int t = blockIdx.x;
     if (t >= p.T) return;
     const int64_t ymax = (int64_t)*p.s_ymax, gmax = (int64_t)*p.gmax;
@@ -1633,6 +1686,7 @@ __global__ void gated_final_kernel(const GateArgs p) {
 
 // The first global row of this rank from every rank's row count ([world] u64, rank order).
 __global__ void row_offset_kernel(const unsigned long long* __restrict__ counts, int rank, int* __restrict__ offset) {
+    kt::pdl_enter();
     int o = 0;
     for (int q = 0; q < rank; ++q) o += (int)counts[q];
     *offset = o;
@@ -1647,6 +1701,7 @@ __global__ void row_offset_kernel(const unsigned long long* __restrict__ counts,
 // meta[pos] = s_qx of the token of expert-sorted row pos (as {mant, shift} int64 pairs).
 __global__ void pack_meta_kernel(const int* __restrict__ row_assign, int top_k, const Scale* __restrict__ tok_sqx,
                                  int n_rows, int64_t* __restrict__ meta) {
+    kt::pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
     const Scale s = tok_sqx[row_assign[r] / top_k];
@@ -1655,6 +1710,7 @@ __global__ void pack_meta_kernel(const int* __restrict__ row_assign, int top_k, 
 }
 
 __global__ void meta_to_scale_kernel(const int64_t* __restrict__ meta, int n_rows, Scale* __restrict__ out) {
+    kt::pdl_enter();
     const int r = blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= n_rows) return;
     out[r] = Scale{meta[2 * (long long)r], (int32_t)meta[2 * (long long)r + 1]};
@@ -1663,6 +1719,7 @@ __global__ void meta_to_scale_kernel(const int64_t* __restrict__ meta, int n_row
 // row_expert for received rows: run i covers rows [start[i], start[i] + count[i]) of local expert group[i].
 __global__ void runs_to_rows_kernel(const int* __restrict__ start, const int* __restrict__ count,
                                     const int* __restrict__ group, int n_runs, int* __restrict__ row_expert) {
+    kt::pdl_enter();
     const int i = blockIdx.x;
     if (i >= n_runs) return;
     for (int j = threadIdx.x; j < count[i]; j += blockDim.x) row_expert[start[i] + j] = group[i];
@@ -1672,6 +1729,7 @@ __global__ void runs_to_rows_kernel(const int* __restrict__ start, const int* __
 __global__ void expert_out_kernel(const int64_t* __restrict__ acc, const unsigned long long* __restrict__ ymax_d,
                                   const Scale* __restrict__ row_cd, int n_rows, int D, int32_t* __restrict__ y,
                                   Scale* __restrict__ ys) {
+    kt::pdl_enter();
     const int r = blockIdx.x;
     if (r >= n_rows) return;
     const int64_t ymax = (int64_t)ymax_d[r];
@@ -1691,6 +1749,7 @@ __global__ void seam_out_kernel(const int64_t* __restrict__ acc, const unsigned 
                                 const Scale* __restrict__ row_cd, const int* __restrict__ row_assign, int n_rows, int D,
                                 int K, int Kc, int n_ids, int j0, const int32_t* __restrict__ ids,
                                 int32_t* __restrict__ y, Scale* __restrict__ ys) {
+    kt::pdl_enter();
     const int r = blockIdx.x;
     if (r >= n_rows) return;
     const int a = row_assign[r], t = a / K, slot = a % K;
@@ -1706,6 +1765,7 @@ __global__ void seam_out_kernel(const int64_t* __restrict__ acc, const unsigned 
 }
 
 __global__ void iota_kernel(int* __restrict__ p, long long n) {
+    kt::pdl_enter();
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         p[i] = (int)i;
 }
@@ -1725,6 +1785,7 @@ struct CombineYArgs {
 // One thread per token: the plan of combine from expert outputs given as IntTensors (their scales are final, so each
 // live slot needs only its rescale to the common scale); the same CombinePlan layout (ry unused).
 __global__ void combine_y_plan_kernel(const CombineYArgs a, const CombinePlan p) {
+    kt::pdl_enter();
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= a.T) return;
     const int K = a.top_k;
@@ -1760,6 +1821,7 @@ __global__ void combine_y_plan_kernel(const CombineYArgs a, const CombinePlan p)
 // combine (layers.rs:893-923) from expert outputs given as IntTensors (y rows + scales), row = slot_row[t·K + i]: one
 // block per token from its plan, each thread CE elements per chunk, one slot's plan at a time.
 __global__ void __launch_bounds__(256, 3) combine_y_kernel(const CombineYArgs a, const CombinePlan p) {
+    kt::pdl_enter();
     extern __shared__ int64_t acc_s[];  // [dim]
     __shared__ uint64_t red[32];
     __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
@@ -1822,9 +1884,191 @@ __global__ void __launch_bounds__(256, 3) combine_y_kernel(const CombineYArgs a,
     }
 }
 
+// ───────────── combine with a warp per token's plan, one token over a cluster ─────────────
+// The same arithmetic as combine_plan_kernel / combine_kernel (Y = false: the down accumulators) and
+// combine_y_plan_kernel / combine_y_kernel (Y = true: expert outputs given as IntTensors), arranged for latency:
+// the plan is one warp per token with lane i on slot i (top_k <= 32), and a token's output row is split over a
+// cluster of C CTAs whose row maximum is reduced through distributed shared memory.
+
+// One token's plan by one warp, written at p's pointers (offset by the caller): the slot scales (the expert outputs'
+// own for Y, else ratio_act(ymax)·c, zero when either is zero: layers.rs:300-302, :321-326), common = the last of the
+// largest as a warp reduction over (value, slot) (the fold of layers.rs:898), and the live slots packed to the front
+// in slot order by their rank in the ballot. *p.n = -1 when the token's output is zero (sumc <= 0 or every slot zero).
+template <bool Y, class A>
+__device__ __forceinline__ void combine_plan_warp(const A& a, int t, const CombinePlan& p) {
+    const int lane = threadIdx.x & 31, K = a.top_k;
+    if (a.sumc[t] <= 0) {
+        if (lane == 0) *p.n = -1;
+        return;
+    }
+    const bool in = lane < K;
+    const int row = in ? a.slot_row[(long long)t * K + lane] : 0;
+    Scale ys = kt::scale_zero();
+    int64_t ym = 0;
+    if (in) {
+        if constexpr (Y) {
+            ys = a.ys[row];
+        } else {
+            ym = (int64_t)a.ymax_d[row];
+            const Scale cd = a.row_cd[row];
+            if (cd.mant != 0 && ym != 0) ys = kt::scale_mul(kt::ratio_act(ym), cd);
+        }
+    }
+    ScaleIdx b{ys, in ? lane : -1};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ScaleIdx w;
+        w.s.mant = __shfl_xor_sync(0xffffffffu, b.s.mant, o);
+        w.s.shift = __shfl_xor_sync(0xffffffffu, b.s.shift, o);
+        w.idx = __shfl_xor_sync(0xffffffffu, b.idx, o);
+        b = better(b, w);
+    }
+    const Scale common = b.s;
+    if (common.mant == 0) {
+        if (lane == 0) *p.n = -1;
+        return;
+    }
+    const bool live = in && ys.mant != 0;
+    const unsigned m = __ballot_sync(0xffffffffu, live);
+    if (live) {
+        const int o = __popc(m & ((1u << lane) - 1u));
+        p.row[o] = row;
+        p.ec[o] = a.top_ec[(long long)t * K + lane];
+        if constexpr (!Y) p.ry[o] = kt::make_req(ym);
+        p.f[o] = kt::make_apply(kt::scale_mul(ys, kt::scale_recip(common)));
+    }
+    if (lane == 0) {
+        *p.n = __popc(m);
+        *p.common = common;
+    }
+}
+
+// The plan of every token into global memory, a warp per token, for combine_kernel / combine_y_kernel (where tokens
+// are many and a plan inside every token's CTA would hold up its loads).
+template <bool Y, class A>
+__global__ void combine_plan_warp_kernel(const A a, const CombinePlan p) {
+    kt::pdl_enter();
+    const int t = (int)((blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5);
+    if (t >= a.T) return;  // the same for the whole warp
+    const long long q = (long long)t * a.top_k;
+    combine_plan_warp<Y>(a, t, CombinePlan{p.n + t, p.common + t, p.row + q, p.ec + q, Y ? nullptr : p.ry + q, p.f + q});
+}
+
+// Token t = %clusterid.x over the C = %cluster_nctarank CTAs of its cluster (C <= 8; a plain launch is a cluster of
+// one): CTA c owns the output elements [c·S, min(D, (c+1)·S)), S = ceil(D / C), and the slice's accumulators in
+// shared memory (S int64). Warp 0 of every CTA computes the token's plan (the same one). The row maximum: the CTA's,
+// then each CTA stores it into slot c of every CTA's `part` between two cluster barriers (the first, relaxed, arrive
+// is made before the loads so that every CTA has started by the time it is waited on), and each takes the max of
+// its C slots. Every CTA of a cluster takes the same branch at the zero-token test, so no cluster barrier is left
+// waiting. For few tokens (decode); with many, combine_plan_warp_kernel and combine_kernel / combine_y_kernel.
+template <bool Y, class A>
+__global__ void __launch_bounds__(256, 3) combine_tok_kernel(const A a) {
+    kt::pdl_enter();
+    extern __shared__ int64_t acc_s[];  // [S]
+    __shared__ uint64_t red[32];
+    __shared__ uint64_t part[8];
+    __shared__ kt::ReqDiv ry_s[COMBINE_MAX_K];
+    __shared__ kt::ApplyPlan f_s[COMBINE_MAX_K];
+    __shared__ int64_t ec_s[COMBINE_MAX_K];
+    __shared__ int row_s[COMBINE_MAX_K];
+    __shared__ int n_s;
+    __shared__ Scale common_s;
+    const uint32_t C = cluster_size(), c = cluster_rank();
+    const int t = (int)cluster_id_x();
+    if (t >= a.T) return;  // the same for every CTA of the cluster
+    const int D = a.dim;
+    const int S = (D + (int)C - 1) / (int)C;
+    const int d_lo = min(D, (int)c * S), d_hi = min(D, d_lo + S);
+    if (threadIdx.x < 32) combine_plan_warp<Y>(a, t, CombinePlan{&n_s, &common_s, row_s, ec_s, ry_s, f_s});
+    __syncthreads();
+    const int n = n_s;
+    int32_t* o = a.out + (long long)t * D;
+    if (n < 0) {
+        for (int d = d_lo + threadIdx.x; d < d_hi; d += blockDim.x) o[d] = 0;
+        if (c == 0 && threadIdx.x == 0) a.out_scale[t] = kt::scale_zero();
+        return;
+    }
+    if (C > 1) cluster_arrive_relaxed();
+    bool lean = !Y;
+    if constexpr (!Y) {
+        for (int j = 0; j < n; ++j)
+            lean = lean && ry_s[j].dbl && f_s[j].tight && ec_s[j] >= 0 && ec_s[j] < (int64_t(1) << 31);
+    }
+    uint64_t gm = 0;
+    for (int d0 = d_lo + threadIdx.x; d0 < d_hi; d0 += CE * blockDim.x) {
+        int64_t acc[CE];
+#pragma unroll
+        for (int u = 0; u < CE; ++u) acc[u] = 0;
+        for (int j = 0; j < n; ++j) {
+            const kt::ApplyPlan f = f_s[j];
+            const int64_t ec = ec_s[j];
+            if constexpr (Y) {
+                const int32_t* b = a.y + (long long)row_s[j] * D;
+                int32_t v[CE];
+#pragma unroll
+                for (int u = 0; u < CE; ++u) {
+                    const int d = d0 + u * blockDim.x;
+                    v[u] = d < d_hi ? __ldg(b + d) : 0;
+                }
+#pragma unroll
+                for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, v[u]);
+            } else {
+                const kt::ReqDiv ry = ry_s[j];
+                const int64_t* b = a.acc_d + (long long)row_s[j] * D;
+                int64_t v[CE];
+#pragma unroll
+                for (int u = 0; u < CE; ++u) {
+                    const int d = d0 + u * blockDim.x;
+                    v[u] = d < d_hi ? __ldg(b + d) : 0;
+                }
+                if (lean) {
+#pragma unroll
+                    for (int u = 0; u < CE; ++u)
+                        acc[u] += (int64_t)(int32_t)ec * (int64_t)(int32_t)kt::apply_row(f, requant_fast(v[u], ry));
+                } else {
+#pragma unroll
+                    for (int u = 0; u < CE; ++u) acc[u] += ec * kt::apply_row(f, kt::requant_row(v[u], ry));
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CE; ++u) {
+            const int d = d0 + u * blockDim.x;
+            if (d < d_hi) {
+                acc_s[d - d_lo] = acc[u];
+                gm = max(gm, uabs64(acc[u]));
+            }
+        }
+    }
+    gm = block_max_u64(gm, red);
+    if (C > 1) {
+        cluster_wait_acquire();  // (the relaxed arrive above) every CTA of the cluster is running
+        if (threadIdx.x < C) st_cluster_u64(&part[c], threadIdx.x, gm);
+        cluster_arrive_release();
+        cluster_wait_acquire();
+        gm = 0;
+        for (uint32_t k = 0; k < C; ++k) gm = max(gm, part[k]);
+    }
+    const int64_t gmax = (int64_t)gm;
+    const kt::ReqDiv rg = kt::make_req(gmax);
+    if (rg.dbl) {
+        for (int d = d_lo + threadIdx.x; d < d_hi; d += blockDim.x) o[d] = requant_fast(acc_s[d - d_lo], rg);
+    } else {
+        for (int d = d_lo + threadIdx.x; d < d_hi; d += blockDim.x)
+            o[d] = gmax ? kt::requant_row(acc_s[d - d_lo], rg) : 0;
+    }
+    if (c == 0 && threadIdx.x == 0) {
+        const int64_t sumc = a.sumc[t];
+        a.out_scale[t] = gmax == 0 ? kt::scale_zero()
+                                   : kt::scale_mul(kt::scale_mul(kt::ratio_act(gmax), common_s),
+                                                   kt::from_ratio(1, (kt::u128)(uint64_t)sumc));
+    }
+}
+
 // This rank's best (common-scale candidate, global token index) as an int64 record {mant, shift, index}.
 __global__ void scale_record_kernel(const Scale* __restrict__ best, const int* __restrict__ best_idx,
                                     int64_t* __restrict__ rec) {
+    kt::pdl_enter();
     rec[0] = best[0].mant;
     rec[1] = best[0].shift;
     rec[2] = *best_idx;
@@ -1832,6 +2076,7 @@ __global__ void scale_record_kernel(const Scale* __restrict__ best, const int* _
 
 // The record of a rank without tokens: no candidate ({0, 0, -1}).
 __global__ void empty_record_kernel(int64_t* __restrict__ rec) {
+    kt::pdl_enter();
     rec[0] = 0;
     rec[1] = 0;
     rec[2] = -1;
@@ -1839,6 +2084,7 @@ __global__ void empty_record_kernel(int64_t* __restrict__ rec) {
 
 // The common scale over the ranks' records (in rank order; the index decides ties, so the order does not matter).
 __global__ void reduce_records_kernel(const int64_t* __restrict__ recs, int n, Scale* __restrict__ out) {
+    kt::pdl_enter();
     ScaleIdx b{kt::scale_zero(), -1};
     for (int i = 0; i < n; ++i)
         b = better(b, ScaleIdx{Scale{recs[3 * i], (int32_t)recs[3 * i + 1]}, (int)recs[3 * i + 2]});
@@ -1854,6 +2100,7 @@ __global__ void pack_codes_kernel(const int32_t* __restrict__ codes, long long r
                                   int8_t* __restrict__ planes, unsigned long long* __restrict__ bad,
                                   unsigned long long* __restrict__ big = nullptr, int32_t big_lim = 0,
                                   int8_t* __restrict__ raw = nullptr) {
+    kt::pdl_enter();
     const long long r = blockIdx.x;
     if (r >= rows) return;
     const int32_t* c = codes + r * K;

@@ -135,12 +135,14 @@ KT_HD float portable_normal(uint64_t seed, float sigma, uint64_t i) {
 
 #ifdef __CUDACC__
 __global__ void portable_normal_kernel(uint64_t seed, float sigma, uint64_t offset, long long n, float* __restrict__ out) {
+    kt::pdl_enter();
     for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x)
         out[j] = portable_normal(seed, sigma, offset + (uint64_t)j);
 }
 
 // max |w| as the bits of a non-negative float (their integer order is their numeric order).
 __global__ void absmax_f32_kernel(const float* __restrict__ w, long long n, unsigned* __restrict__ out) {
+    kt::pdl_enter();
     unsigned m = 0;
     for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x)
         m = max(m, __float_as_uint(w[j]) & 0x7fffffffu);
@@ -152,6 +154,7 @@ __global__ void absmax_f32_kernel(const float* __restrict__ w, long long n, unsi
 // QuantLinear::from_weights' codes (layers.rs:225-244): clamp(round(w / step), ±WLEVELS), the division and the
 // rounding (half away from zero) in f64 as on the host.
 __global__ void quantize_kernel(const float* __restrict__ w, long long n, double step, int32_t* __restrict__ codes) {
+    kt::pdl_enter();
     for (long long j = blockIdx.x * (long long)blockDim.x + threadIdx.x; j < n; j += (long long)gridDim.x * blockDim.x) {
         double c = round(__ddiv_rn((double)w[j], step));
         c = c > (double)kt::WLEVELS ? (double)kt::WLEVELS : (c < -(double)kt::WLEVELS ? -(double)kt::WLEVELS : c);
