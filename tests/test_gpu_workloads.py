@@ -65,7 +65,9 @@ def test_decode_and_config1_workloads_equal_the_golden(ctx, name, monkeypatch):
                                   {"KTMOE_COMBINE": "0"},  # the thread-per-token plan and a CTA per token
                                   {"KTMOE_COMBINE": "1"},  # a warp plan inside each token's cluster of CTAs
                                   {"KTMOE_SWIGLU_INLINE": "0"},  # the SwiGLU row plans and down c as kernels
-                                  {"KTMOE_SWIGLU_INLINE": "1"}])  # and inside the row kernel
+                                  {"KTMOE_SWIGLU_INLINE": "1"},  # and inside the row kernel
+                                  {"KTMOE_PLAN_ONE": "0"},  # the routing plan as count, scan and assign kernels
+                                  {"KTMOE_PLAN_ONE": "1"}])  # and as one launch
 
 
 @pytest.mark.parametrize("name", ["qwen_prefill", "mixtral_prefill", "mixtral_zipf", "glm_prefill"])

@@ -896,6 +896,16 @@ int allreduce_max(ktmoe_layer* L, unsigned long long* p, size_t n, cudaStream_t 
     return KTMOE_OK;
 }
 
+// KTMOE_PLAN_ONE=0: the three-kernel routing plan (count, scan, assign) also for one chunk; the same result. Read per
+// call.
+bool plan_one_enabled() {
+    const char* e = getenv("KTMOE_PLAN_ONE");
+    return !(e && e[0] == '0');
+}
+
+int plan_chunks(ktmoe_layer* L, int64_t R, int64_t nchunks, const mk::TileTable& ta, const mk::TileTable& tb,
+                cudaStream_t st);
+
 // Dispatch plan of the home rank: a stable counting sort of the T·K (token, slot) rows by expert, the tile tables of
 // the grouped GEMMs (widths BN and BN2) and the rows' digit planes gathered in that order (xg_planes).
 int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st, bool permute = true) {
@@ -907,19 +917,35 @@ int plan_and_permute(ktmoe_layer* L, int64_t T, int BN, int BN2, cudaStream_t st
         return KTMOE_OK;
     }
     const int64_t nchunks = (R + mk::PLAN_CHUNK - 1) / mk::PLAN_CHUNK;
+    const mk::TileTable ta{BN, L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L)};
+    const mk::TileTable tb{BN2, L->tile_group2.as<int>(), L->tile_row02.as<int>(), n_tiles2_ptr(L)};
+    if (nchunks == 1 && E <= mk::PLAN_ONE_MAX_E && plan_one_enabled()) {
+        // one chunk (every decode batch): count, scan, tile tables and assignment in one launch
+        KLAUNCH(st, 1, mk::PLAN_ONE_THREADS, 0, (mk::plan_one_chunk_kernel), L->top_e.as<int32_t>(), (int)R, (int)E,
+                L->chunk_off.as<int>(), L->expert_off.as<int>(), L->group_end.as<int>(), L->expert_count.as<int>(),
+                ta, tb, L->slot_row.as<int>(), L->row_assign.as<int>(), L->row_expert.as<int>());
+    } else {
+        if (int r = plan_chunks(L, R, nchunks, ta, tb, st)) return r;
+    }
+    if (!permute) return KTMOE_OK;
+    KLAUNCH(st, (unsigned)R, 128, 0, (mk::permute_planes_kernel), L->tok_planes.as<int8_t>(), T_pad,
+            L->xg_planes.as<int8_t>(), R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
+    return KTMOE_OK;
+}
+
+// The routing plan over several chunks of PLAN_CHUNK rows: per-chunk counts, the scan, the assignment.
+int plan_chunks(ktmoe_layer* L, int64_t R, int64_t nchunks, const mk::TileTable& ta, const mk::TileTable& tb,
+                cudaStream_t st) {
+    ktmoe_ctx* ctx = L->ctx;
+    const int64_t E = L->E;
     KLAUNCH(st, (unsigned)nchunks, mk::PLAN_THREADS, E * 4, (mk::plan_count_kernel), L->top_e.as<int32_t>(), R, (int)E,
             L->counts.as<int>());
     const int scan_threads = (int)std::min<int64_t>(1024, round_up(E, 32));
     KLAUNCH(st, 1, scan_threads, 3 * E * 4, (mk::plan_scan_kernel), L->counts.as<int>(), (int)nchunks, (int)E,
-            L->chunk_off.as<int>(), L->expert_off.as<int>(), L->group_end.as<int>(), L->expert_count.as<int>(),
-            mk::TileTable{BN, L->tile_group.as<int>(), L->tile_row0.as<int>(), n_tiles_ptr(L)},
-            mk::TileTable{BN2, L->tile_group2.as<int>(), L->tile_row02.as<int>(), n_tiles2_ptr(L)});
+            L->chunk_off.as<int>(), L->expert_off.as<int>(), L->group_end.as<int>(), L->expert_count.as<int>(), ta, tb);
     KLAUNCH(st, (unsigned)nchunks, mk::PLAN_THREADS, (E + (mk::PLAN_THREADS / 32) * E) * 4, (mk::plan_assign_kernel),
             L->top_e.as<int32_t>(), R, (int)E, L->chunk_off.as<int>(), L->expert_off.as<int>(), L->slot_row.as<int>(),
             L->row_assign.as<int>(), L->row_expert.as<int>());
-    if (!permute) return KTMOE_OK;
-    KLAUNCH(st, (unsigned)R, 128, 0, (mk::permute_planes_kernel), L->tok_planes.as<int8_t>(), T_pad,
-            L->xg_planes.as<int8_t>(), R_pad, (int)L->d_pad, L->row_assign.as<int>(), (int)K, (int)R);
     return KTMOE_OK;
 }
 

@@ -338,6 +338,97 @@ struct TileTable {
     int* n_tiles;
 };
 
+// The exclusive scan over experts of (rows, tiles of width ta.BN, tiles of width tb.BN) from the per-expert totals
+// `tot`, by the whole block (blockDim.x a multiple of 32, at most 1024): thread i owns the experts [i·per, (i+1)·per)
+// and the threads' sums are scanned with warp shuffles, then over the warps. Writes expert_off, expert_count and
+// group_end, the offsets into shared off_s (may be nullptr), toff_a and toff_b, and both tile counts. Ends with a
+// barrier.
+__device__ __forceinline__ void plan_offsets(const int* __restrict__ tot, int E, const TileTable& ta,
+                                             const TileTable& tb, int* __restrict__ expert_off,
+                                             int* __restrict__ expert_count, int* __restrict__ group_end,
+                                             int* __restrict__ off_s, int* __restrict__ toff_a, int* __restrict__ toff_b) {
+    __shared__ int wsum[3][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per = (E + (int)blockDim.x - 1) / (int)blockDim.x;
+    const int e0 = min(E, (int)threadIdx.x * per), e1 = min(E, e0 + per);
+    int s0 = 0, s1 = 0, s2 = 0;
+    for (int e = e0; e < e1; ++e) {
+        s0 += tot[e];
+        s1 += (tot[e] + ta.BN - 1) / ta.BN;
+        s2 += (tot[e] + tb.BN - 1) / tb.BN;
+    }
+    int i0 = s0, i1 = s1, i2 = s2;  // inclusive over the warp's lanes
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int a0 = __shfl_up_sync(0xffffffffu, i0, o), a1 = __shfl_up_sync(0xffffffffu, i1, o),
+                  a2 = __shfl_up_sync(0xffffffffu, i2, o);
+        if (lane >= o) {
+            i0 += a0;
+            i1 += a1;
+            i2 += a2;
+        }
+    }
+    if (lane == 31) {
+        wsum[0][warp] = i0;
+        wsum[1][warp] = i1;
+        wsum[2][warp] = i2;
+    }
+    __syncthreads();
+    if (warp == 0) {  // inclusive over the warps
+        int w0 = lane < nw ? wsum[0][lane] : 0, w1 = lane < nw ? wsum[1][lane] : 0, w2 = lane < nw ? wsum[2][lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a0 = __shfl_up_sync(0xffffffffu, w0, o), a1 = __shfl_up_sync(0xffffffffu, w1, o),
+                      a2 = __shfl_up_sync(0xffffffffu, w2, o);
+            if (lane >= o) {
+                w0 += a0;
+                w1 += a1;
+                w2 += a2;
+            }
+        }
+        wsum[0][lane] = w0;
+        wsum[1][lane] = w1;
+        wsum[2][lane] = w2;
+    }
+    __syncthreads();
+    int r = i0 - s0 + (warp ? wsum[0][warp - 1] : 0);
+    int qa = i1 - s1 + (warp ? wsum[1][warp - 1] : 0);
+    int qb = i2 - s2 + (warp ? wsum[2][warp - 1] : 0);
+    for (int e = e0; e < e1; ++e) {
+        expert_off[e] = r;
+        if (off_s) off_s[e] = r;
+        expert_count[e] = tot[e];
+        toff_a[e] = qa;
+        toff_b[e] = qb;
+        r += tot[e];
+        group_end[e] = r;
+        qa += (tot[e] + ta.BN - 1) / ta.BN;
+        qb += (tot[e] + tb.BN - 1) / tb.BN;
+    }
+    if (threadIdx.x == 0) {
+        *ta.n_tiles = wsum[1][nw - 1];
+        *tb.n_tiles = wsum[2][nw - 1];
+    }
+    __syncthreads();
+}
+
+// The tile tables of both widths from the scanned offsets: expert e's tiles at toff[e], in row order.
+__device__ __forceinline__ void plan_tiles(const int* __restrict__ tot, int E, const int* __restrict__ off,
+                                           const int* __restrict__ toff_a, const int* __restrict__ toff_b,
+                                           const TileTable& ta, const TileTable& tb) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        const int na = (tot[e] + ta.BN - 1) / ta.BN, nb = (tot[e] + tb.BN - 1) / tb.BN;
+        for (int i = 0; i < na; ++i) {
+            ta.tile_group[toff_a[e] + i] = e;
+            ta.tile_row0[toff_a[e] + i] = off[e] + i * ta.BN;
+        }
+        for (int i = 0; i < nb; ++i) {
+            tb.tile_group[toff_b[e] + i] = e;
+            tb.tile_row0[toff_b[e] + i] = off[e] + i * tb.BN;
+        }
+    }
+}
+
 __global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, int E, int* __restrict__ chunk_off,
                                  int* __restrict__ expert_off, int* __restrict__ group_end,
                                  int* __restrict__ expert_count, TileTable ta, TileTable tb) {
@@ -355,33 +446,8 @@ __global__ void plan_scan_kernel(const int* __restrict__ counts, int n_chunks, i
         tot[e] = run;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int off = 0, tiles_a = 0, tiles_b = 0;
-        for (int e = 0; e < E; ++e) {
-            expert_off[e] = off;
-            expert_count[e] = tot[e];
-            off += tot[e];
-            group_end[e] = off;
-            toff_a[e] = tiles_a;
-            toff_b[e] = tiles_b;
-            tiles_a += (tot[e] + ta.BN - 1) / ta.BN;
-            tiles_b += (tot[e] + tb.BN - 1) / tb.BN;
-        }
-        *ta.n_tiles = tiles_a;
-        *tb.n_tiles = tiles_b;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        const int na = (tot[e] + ta.BN - 1) / ta.BN, nb = (tot[e] + tb.BN - 1) / tb.BN;
-        for (int i = 0; i < na; ++i) {
-            ta.tile_group[toff_a[e] + i] = e;
-            ta.tile_row0[toff_a[e] + i] = expert_off[e] + i * ta.BN;
-        }
-        for (int i = 0; i < nb; ++i) {
-            tb.tile_group[toff_b[e] + i] = e;
-            tb.tile_row0[toff_b[e] + i] = expert_off[e] + i * tb.BN;
-        }
-    }
+    plan_offsets(tot, E, ta, tb, expert_off, expert_count, group_end, nullptr, toff_a, toff_b);
+    plan_tiles(tot, E, expert_off, toff_a, toff_b, ta, tb);
 }
 
 // Stable positions: assignment a = t·k + i goes to expert_off[e] + chunk_off[chunk][e] + (rank among the same expert
@@ -421,6 +487,65 @@ __global__ void plan_assign_kernel(const int32_t* __restrict__ top_e, long long 
         for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
             int s = 0;
             for (int w = 0; w < nw; ++w) {
+                s += wcnt[w * E + ee];
+                wcnt[w * E + ee] = 0;
+            }
+            running[ee] += s;
+        }
+        __syncthreads();
+    }
+}
+
+// The routing plan of one chunk (n_assign <= PLAN_CHUNK, E <= PLAN_ONE_MAX_E) in one launch of one block: the counts
+// (plan_count_kernel), the offsets and tile tables (plan_scan_kernel; the chunk offsets are all zero) and the stable
+// assignment (plan_assign_kernel, the same per-warp ranks), with the offsets kept in shared memory between them.
+constexpr int PLAN_ONE_THREADS = 512;
+constexpr int PLAN_ONE_MAX_E = 256;
+
+__global__ void __launch_bounds__(PLAN_ONE_THREADS)
+    plan_one_chunk_kernel(const int32_t* __restrict__ top_e, int n_assign, int E, int* __restrict__ chunk_off,
+                          int* __restrict__ expert_off, int* __restrict__ group_end, int* __restrict__ expert_count,
+                          TileTable ta, TileTable tb, int* __restrict__ slot_row, int* __restrict__ row_assign,
+                          int* __restrict__ row_expert) {
+    kt::pdl_enter();
+    constexpr int NW = PLAN_ONE_THREADS / 32;
+    __shared__ int hist[PLAN_ONE_MAX_E], off_s[PLAN_ONE_MAX_E], toff_a[PLAN_ONE_MAX_E], toff_b[PLAN_ONE_MAX_E],
+        running[PLAN_ONE_MAX_E];
+    __shared__ int wcnt[NW * PLAN_ONE_MAX_E];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        hist[e] = 0;
+        running[e] = 0;
+        chunk_off[e] = 0;
+    }
+    for (int i = threadIdx.x; i < NW * E; i += blockDim.x) wcnt[i] = 0;
+    __syncthreads();
+    for (int j = threadIdx.x; j < n_assign; j += blockDim.x) atomicAdd(&hist[top_e[j]], 1);
+    __syncthreads();
+    plan_offsets(hist, E, ta, tb, expert_off, expert_count, group_end, off_s, toff_a, toff_b);
+    plan_tiles(hist, E, off_s, toff_a, toff_b, ta, tb);
+    for (int r0 = 0; r0 < n_assign; r0 += blockDim.x) {
+        const int a = r0 + (int)threadIdx.x;
+        const bool valid = a < n_assign;
+        const int e = valid ? top_e[a] : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const unsigned lt = (1u << lane) - 1u;
+        const int rank_w = __popc(peers & lt);
+        const bool leader = (peers & lt) == 0;
+        if (valid && leader) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        if (valid) {
+            int before = running[e];
+            for (int w = 0; w < warp; ++w) before += wcnt[w * E + e];
+            const int pos = off_s[e] + before + rank_w;
+            slot_row[a] = pos;
+            row_assign[pos] = a;
+            row_expert[pos] = e;
+        }
+        __syncthreads();
+        for (int ee = threadIdx.x; ee < E; ee += blockDim.x) {
+            int s = 0;
+            for (int w = 0; w < NW; ++w) {
                 s += wcnt[w * E + ee];
                 wcnt[w * E + ee] = 0;
             }
