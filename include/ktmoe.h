@@ -88,7 +88,8 @@ int ktmoe_linear_last_gemm(ktmoe_ctx* ctx, double* ms, int32_t* act_planes);
  * reference. x [rows][k], w [out][k] (int32 codes) and y [rows][out] (int64) are DEVICE buffers on `device`; the
  * call allocates nothing: its scratch is a 64 MiB file-scope device array that every GPU running this entry point
  * holds until exit; the first call on a device looks up its address and loads this entry point's kernels there
- * (make that first call before any stream capture). Limit: 256 + 3*ceil64(rows)*ceil128(k) (rounded up to 256) + 3*ceil128(out)*ceil128(k) <= 64 MiB, else
+ * (make that first call before any stream capture; a first call on a capturing stream returns KTMOE_ERR_ARG).
+ * Limit: 256 + 3*ceil64(rows)*ceil128(k) (rounded up to 256) + 3*ceil128(out)*ceil128(k) <= 64 MiB, else
  * KTMOE_ERR_UNSUPPORTED. Calls on one device share the array and keep the last call's contents; calls whose GPU work
  * overlaps on one device race, so serialise them. Synchronous: returns when the work on `stream` (NULL: the legacy
  * default stream) is done. */

@@ -90,3 +90,35 @@ def test_noalloc_linear_rejects_sizes_beyond_its_scratch():
     assert _call(xb, wb, 1, 1, 2, yb) == _native.ERR_RANGE
     ok = torch.tensor([1, 2], dtype=torch.int32, device="cuda")
     assert _call(ok, wb, 1, 1, 2, yb) == _native.OK and int(yb[0]) == 11
+
+
+@pytest.mark.gpu
+def test_noalloc_first_call_on_a_capturing_stream_is_refused():
+    """The first call on a device loads this entry point's kernels there, which a stream capture cannot record: on a
+    capturing stream that call returns KTMOE_ERR_ARG and leaves the device set up for nothing, and the next call
+    outside the capture sets it up and computes. Run in a fresh process, where no call has set the device up yet."""
+    import subprocess
+    import sys
+
+    code = r"""
+import ctypes, torch
+import tritify_b200 as tb
+from tritify_b200 import _native
+x = torch.tensor([1, 2, 3, 4], dtype=torch.int32, device="cuda")
+y = torch.zeros(1, dtype=torch.int64, device="cuda")
+def call(stream):
+    return tb.lib().ktmoe_linear_noalloc(0, ctypes.c_void_p(x.data_ptr()), ctypes.c_void_p(x.data_ptr()), 1, 1, 4,
+                                         ctypes.c_void_p(y.data_ptr()), stream)
+s = torch.cuda.Stream()
+g = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g, stream=s):
+    rc = call(ctypes.c_void_p(s.cuda_stream))
+assert rc == _native.ERR_ARG, rc
+del g
+torch.cuda.synchronize()
+assert call(None) == _native.OK and int(y[0]) == 30
+print("capture guard ok")
+"""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "capture guard ok" in r.stdout, r.stdout + r.stderr

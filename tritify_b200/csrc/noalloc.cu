@@ -10,12 +10,13 @@
 //
 // The array is part of this file's device code: every GPU on which this entry point runs holds it (64 MiB) until the
 // process exits. Its address is looked up once per device with cudaGetSymbolAddress, by the first call on that device,
-// which also loads this entry point's kernels there (so that first call should come before any CUDA stream capture). All calls on one device share that device's array
-// and it keeps the last call's contents, so two calls whose GPU work overlaps on one device (two streams, or two host
-// threads) race and must be serialised by the caller; calls on different devices use different copies. The call is
-// synchronous: it returns after its work on `stream` has finished. The control words are cleared at the
-// start of every call; the planes need no clearing, because every byte a product reads is written first (rows past
-// the data are only read into output columns the epilogue discards).
+// which also loads this entry point's kernels there (so that first call should come before any CUDA stream capture; a
+// first call on a stream that is being captured returns KTMOE_ERR_ARG). All calls on one device share that device's
+// array and it keeps the last call's contents, so two calls whose GPU work overlaps on one device (two streams, or two
+// host threads) race and must be serialised by the caller; calls on different devices use different copies. The call
+// is synchronous: it returns after its work on `stream` has finished. The control words are cleared at the start of
+// every call; the planes need no clearing, because every byte a product reads is written first (rows past the data
+// are only read into output columns the epilogue discards).
 //
 // Shares the digit-plane GEMM of digit_gemm.cuh with ktmoe_linear; the existing entry points are unchanged.
 
@@ -150,16 +151,24 @@ extern "C" int ktmoe_linear_noalloc(int32_t device, const int32_t* x, const int3
     if (cudaSetDevice(device) != cudaSuccess) return KTMOE_ERR_NO_DEVICE;
     int status = KTMOE_OK;
     unsigned char* base = nullptr;
+    cudaStream_t st = (cudaStream_t)stream;
     {
         std::lock_guard<std::mutex> lk(g_mu);
         if (!g_scratch_dev[device]) {
+            // the set-up loads code onto the device, which a stream being captured would not record: a first call
+            // under capture is refused (KTMOE_ERR_ARG) instead of failing part-way through
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
             unsigned char* p = nullptr;
-            status = setup_device(&p);
+            if (cudaStreamIsCapturing(st, &cs) != cudaSuccess)
+                status = KTMOE_ERR_CUDA;
+            else if (cs != cudaStreamCaptureStatusNone)
+                status = KTMOE_ERR_ARG;
+            else
+                status = setup_device(&p);
             if (status == KTMOE_OK) g_scratch_dev[device] = p;
         }
         base = g_scratch_dev[device];
     }
-    cudaStream_t st = (cudaStream_t)stream;
     if (k == 0) {  // empty sums
         const bool ok = status == KTMOE_OK && cudaMemsetAsync(y, 0, (size_t)(rows * out) * 8, st) == cudaSuccess &&
                         cudaStreamSynchronize(st) == cudaSuccess;
