@@ -980,12 +980,12 @@ int swiglu_slices(const ktmoe_layer* L) {
 }
 
 // Routed rows up to which swiglu_rows_kernel computes each row's plan itself (KTMOE_SWIGLU_INLINE=0: never): one wave
-// of its blocks (three per SM). Every wave waits on its rows' plans, so beyond one the plan kernel wins (ms per
-// forward, inline against not: 256 rows 0.389 against 0.399, 1024 rows 1.233 against 1.234, 4096 rows 0.620 against
-// 0.600).
+// of its blocks (four per SM). Every wave waits on its rows' plans, so beyond one the plan kernel wins (ms per
+// forward, inline against not, measured at three blocks per SM: 256 rows 0.389 against 0.399, 1024 rows 1.233
+// against 1.234, 4096 rows 0.620 against 0.600).
 int64_t swiglu_inline_rows(const ktmoe_ctx* ctx) {
     const char* e = getenv("KTMOE_SWIGLU_INLINE");
-    return (e && e[0] == '0') ? 0 : 3 * (int64_t)ctx->num_sms;
+    return (e && e[0] == '0') ? 0 : 4 * (int64_t)ctx->num_sms;
 }
 
 int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
@@ -1095,12 +1095,19 @@ int run_experts(ktmoe_layer* L, const ExpertRows& x, cudaStream_t st) {
         // certificate, element pairs through 16-byte loads and stores
         const char* ve = getenv("KTMOE_SWIGLU_V");
         const int v2 = (ve && ve[0] == '1') ? 0 : 1;
+        // KTMOE_SWIGLU_PF=n: thread 0 prefetches the row's accumulators n block steps ahead into L2 (default 2; 0:
+        // none): on the Mixtral rows 1-2% faster than none
+        const char* pe = getenv("KTMOE_SWIGLU_PF");
+        const int pf = pe ? std::max(0, std::min(16, atoi(pe))) : 2;
+        // two pairs per thread step compiled for four resident blocks per SM (64 registers, a few spills): the pass
+        // is latency bound, and against three blocks of 80 registers it measured 11-17% faster on those rows
+        // (Mixtral 1.94 -> 1.73 ms, GLM 2.29 -> 1.91, Qwen 0.262 -> 0.220)
         if (unroll == 1)
-            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<1>), sa, h_smem, v2);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<1, 3>), sa, h_smem, v2, pf);
         else if (unroll == 4)
-            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<4>), sa, h_smem, v2);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<4, 3>), sa, h_smem, v2, pf);
         else
-            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<2>), sa, h_smem, v2);
+            KLAUNCH(st, grid, 256, sm, (mk::swiglu_rows_kernel<2, 4>), sa, h_smem, v2, pf);
     }
     if (!sa.inline_plan) {
         KLAUNCH(st, (unsigned)((R + 127) / 128), 128, 0, (mk::down_c_kernel), sa);
@@ -2303,11 +2310,11 @@ static int layer_create(ktmoe_ctx* ctx, const ktmoe_layer_config* cfg, int rank,
     if (L->f * 8 <= 24 * 1024) {
         L->swiglu_smem = L->f * 8;
         if (L->swiglu_smem > 48 * 1024 &&
-            (cudaFuncSetAttribute(mk::swiglu_rows_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            (cudaFuncSetAttribute(mk::swiglu_rows_kernel<1, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)L->swiglu_smem) != cudaSuccess ||
-             cudaFuncSetAttribute(mk::swiglu_rows_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+             cudaFuncSetAttribute(mk::swiglu_rows_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)L->swiglu_smem) != cudaSuccess ||
-             cudaFuncSetAttribute(mk::swiglu_rows_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+             cudaFuncSetAttribute(mk::swiglu_rows_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)L->swiglu_smem) != cudaSuccess))
             return bail(fail(ctx, KTMOE_ERR_CUDA, "SwiGLU shared memory"));
     }

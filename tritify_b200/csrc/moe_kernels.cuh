@@ -845,12 +845,18 @@ __device__ __forceinline__ void write_down_planes(const SwigluArgs& a, int r, co
     }
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) at `p` into L2: a hint, nothing waits on it.
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Phase 0: blocks walk the routed rows (row r, r + gridDim.x, ...); h stays in shared memory (dynamic, f int64) when
-// `h_smem`. U independent elements per thread per step. The row's scales come from swiglu_plan_kernel, or with
-// a.inline_plan from thread 0 of the row's block (then also the down linear's c, at the end); its max |h| goes to
-// row_hmax.
-template <int U>
-__global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a, int h_smem, int v2) {
+// `h_smem`. U independent elements per thread per step, compiled for MINB resident blocks per SM. The row's scales
+// come from swiglu_plan_kernel, or with a.inline_plan from thread 0 of the row's block (then also the down linear's c,
+// at the end); its max |h| goes to row_hmax. pf > 0 (element pairs): thread 0 keeps the gate and up accumulators of
+// the block's next pf steps on their way into L2, so the other threads' loads meet fewer DRAM latencies.
+template <int U, int MINB>
+__global__ void __launch_bounds__(256, MINB) swiglu_rows_kernel(const SwigluArgs a, int h_smem, int v2, int pf) {
     kt::pdl_enter();
     extern __shared__ int64_t hs[];
     __shared__ uint64_t red[32];
@@ -878,8 +884,22 @@ __global__ void __launch_bounds__(256, 3) swiglu_rows_kernel(const SwigluArgs a,
             // element pairs: 16-byte loads of g and u, a 16-byte store of h
             const int32_t base = (int32_t)-a.silu.lo_index;
             const int npairs = f >> 1;
+            const int step = U * blockDim.x;  // pairs per step of the block
+            // pf > 0: thread 0 keeps the gate and up accumulators of the block's next pf steps on their way to L2
+            if (pf > 0 && threadIdx.x == 0) {
+                for (int p0 = 0; p0 < min(pf * step, npairs); p0 += step) {
+                    const int n = min(step, npairs - p0);
+                    prefetch_l2(accg + 2 * p0, (unsigned)n * 16);
+                    prefetch_l2(accu + 2 * p0, (unsigned)n * 16);
+                }
+            }
             int p = threadIdx.x;
-            for (; p < npairs; p += U * blockDim.x) {
+            for (; p < npairs; p += step) {
+                if (pf > 0 && threadIdx.x == 0 && p + pf * step < npairs) {
+                    const int p0 = p + pf * step, n = min(step, npairs - p0);
+                    prefetch_l2(accg + 2 * p0, (unsigned)n * 16);
+                    prefetch_l2(accu + 2 * p0, (unsigned)n * 16);
+                }
                 longlong2 gv[U], uv[U];
 #pragma unroll
                 for (int j = 0; j < U; ++j) {
