@@ -58,3 +58,79 @@ def test_the_binding_passes_as_many_arguments_as_the_header_declares():
     for name, (argtypes, _) in _native.SIGNATURES.items():
         assert name in arity, name
         assert len(argtypes) == arity[name], f"{name}: header {arity[name]} parameters, binding {len(argtypes)}"
+
+
+# Entry points whose all-zero call is empty work, not an error (nothing to generate, no rows); the string and handle
+# getters return a string or NULL; every other entry point must refuse null handles and buffers with KTMOE_ERR_ARG.
+EMPTY_OK = {"ktmoe_lcg_uniform", "ktmoe_linear_noalloc", "ktmoe_synth_normal", "ktmoe_synth_normal_portable"}
+NOT_STATUS = {"ktmoe_error_string", "ktmoe_last_error", "ktmoe_stream"}
+
+_NULL_SWEEP = r"""
+import ctypes, sys
+sys.path.insert(0, sys.argv[1])
+import tritify_b200 as tb
+from tritify_b200 import _native
+L = tb.lib()
+ints = (ctypes.c_int, ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_uint32, ctypes.c_size_t,
+        ctypes.c_uint8, ctypes.c_int8, ctypes.c_long, ctypes.c_ulong, ctypes.c_longlong, ctypes.c_ulonglong)
+for name in sorted(_native.SIGNATURES):
+    argtypes, _ = _native.SIGNATURES[name]
+    args = []
+    for t in argtypes:
+        if t in (ctypes.c_double, ctypes.c_float):
+            args.append(0.0)
+        elif isinstance(t, type) and issubclass(t, ctypes.Structure):
+            args.append(t())
+        elif t in ints:
+            args.append(0)
+        else:
+            args.append(None)
+    print("CALL", name, flush=True)
+    print("RESULT", name, repr(getattr(L, name)(*args)), flush=True)
+"""
+
+
+def test_every_entry_point_refuses_null_handles_without_crashing():
+    """Each exported function, called with null pointers and zero sizes (in a child process, so that a crash names
+    the function it happened in), returns KTMOE_ERR_ARG, or OK where the call is empty work; none touches the
+    missing objects. The C ABI never aborts its host (the reference's Rust contract turns statuses into panics)."""
+    import subprocess
+    import sys
+
+    r = subprocess.run([sys.executable, "-c", _NULL_SWEEP, ROOT], capture_output=True, text=True, timeout=600)
+    calls = [ln.split()[1] for ln in r.stdout.splitlines() if ln.startswith("CALL")]
+    assert r.returncode == 0, f"crashed in {calls[-1] if calls else '?'}: {r.stderr[-2000:]}"
+    results = {}
+    for ln in r.stdout.splitlines():
+        if ln.startswith("RESULT"):
+            _, name, val = ln.split(" ", 2)
+            results[name] = val
+    assert set(results) == set(_native.SIGNATURES)
+    for name, val in results.items():
+        if name in NOT_STATUS:
+            continue
+        want = str(_native.OK) if name in EMPTY_OK else str(_native.ERR_ARG)
+        assert val == want, f"{name}: status {val}, expected {want}"
+
+
+def test_noalloc_argument_and_size_checks_come_before_any_device_call():
+    """ktmoe_linear_noalloc validates its arguments and its scratch limit on the host first, so these answers hold
+    on any machine: bad device or sizes -> KTMOE_ERR_ARG, missing buffers -> KTMOE_ERR_ARG, planes beyond the 64 MiB
+    array -> KTMOE_ERR_UNSUPPORTED, no rows -> OK."""
+    f = tb.lib().ktmoe_linear_noalloc
+    one = ctypes.c_void_p(16)  # never dereferenced: every case below returns before touching memory
+    assert f(-1, one, one, 4, 4, 4, one, None) == _native.ERR_ARG
+    assert f(64, one, one, 4, 4, 4, one, None) == _native.ERR_ARG
+    assert f(0, one, one, -1, 4, 4, one, None) == _native.ERR_ARG
+    assert f(0, one, one, 4, -1, 4, one, None) == _native.ERR_ARG
+    assert f(0, one, one, 4, 4, -1, one, None) == _native.ERR_ARG
+    assert f(0, one, one, 4, 4, 4, None, None) == _native.ERR_ARG
+    assert f(0, None, one, 4, 4, 4, one, None) == _native.ERR_ARG
+    assert f(0, one, None, 4, 4, 4, one, None) == _native.ERR_ARG
+    assert f(0, one, one, 0, 4, 4, one, None) == _native.OK
+    # 3*4096*4096 + 3*4096*4096 bytes of planes: far above the array
+    assert f(0, one, one, 4096, 4096, 4096, one, None) == _native.ERR_UNSUPPORTED
+    # just above the limit: rows_pad 64, out_pad 128, k_pad = k rounded to 128; 3*k_pad*(64+128) + 256 > 64 MiB
+    k = 116608
+    assert 3 * k * (64 + 128) + 256 > (64 << 20)
+    assert f(0, one, one, 1, 1, k, one, None) == _native.ERR_UNSUPPORTED
