@@ -70,3 +70,36 @@ void fp_isqrt(uint64_t hi, uint64_t lo, uint64_t* out_hi, uint64_t* out_lo) {
 extern "C" {
 int64_t fp_apply_row_wide(fp_scale s, int64_t v) { return kt::apply_row_wide(kt::make_apply(S(s)), v); }
 }
+
+extern "C" {
+// The certified requant of a magnitude as the lean element paths call it: av = |v| converted to double, inv = the
+// row divisor's RN(2^28/den) from make_req; which = 1 (req_mag) or 2 (req_mag2). ok[i] = the certificate held.
+void fp_req_mag_n(const int64_t* av, const int64_t* den, int which, uint32_t* q, uint8_t* ok, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        const kt::ReqDiv r = kt::make_req(den[i]);
+        uint32_t qq = 0;
+        const bool k = which == 1 ? kt::req_mag((double)av[i], r.inv28, qq) : kt::req_mag2((double)av[i], r.inv28, qq);
+        q[i] = qq;
+        ok[i] = k ? 1 : 0;
+    }
+}
+
+// floor((av·2^28 + floor(den/2)) / den) in 128-bit integers: the value the certificate must give.
+void fp_req_exact_n(const int64_t* av, const int64_t* den, int64_t* q, int64_t n) {
+    for (int64_t i = 0; i < n; ++i) {
+        const kt::u128 num = ((kt::u128)(uint64_t)av[i] << 28) + (kt::u128)(uint64_t)(den[i] / 2);
+        q[i] = (int64_t)(num / (kt::u128)(uint64_t)den[i]);
+    }
+}
+
+// The down linear's input code on the lean path, (q·WLEVELS + 2^27) >> 28 on a magnitude q, against quant_to_act(q)
+// for every q in [0, 2^28]: the count of differences.
+int64_t fp_down_code_mismatches() {
+    int64_t bad = 0;
+    for (uint32_t q = 0; q <= (1u << 28); ++q) {
+        const uint32_t t = (uint32_t)(((uint64_t)q * (uint64_t)kt::WLEVELS + (uint64_t(1) << 27)) >> 28);
+        bad += (int32_t)t != kt::quant_to_act((int32_t)q);
+    }
+    return bad;
+}
+}

@@ -48,6 +48,10 @@ def fp(tmp_path_factory):
     L.fp_apply_row.restype = ctypes.c_int64
     L.fp_requant_act_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
     L.fp_quant_to_n.argtypes = [P(ctypes.c_int32), P(ctypes.c_int64), P(ctypes.c_int32), ctypes.c_int64]
+    L.fp_req_mag_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), ctypes.c_int, P(ctypes.c_uint32),
+                               P(ctypes.c_uint8), ctypes.c_int64]
+    L.fp_req_exact_n.argtypes = [P(ctypes.c_int64), P(ctypes.c_int64), P(ctypes.c_int64), ctypes.c_int64]
+    L.fp_down_code_mismatches.restype = ctypes.c_int64
     return L
 
 
@@ -260,3 +264,65 @@ def test_apply_row_wide_equals_the_oracle(fp, oracle):
                        oracle.from_ratio(next(g) % (1 << 40) + 1, next(g) % (1 << 20) + 1))
         val = int(next(g) % (1 << 50)) - (1 << 49)
         assert fp.fp_apply_row_wide(FpScale(*s), val) == oracle.apply(s, val)
+
+
+def _req_mag(fp, av, den, which):
+    P = ctypes.POINTER
+    n = len(av)
+    q = np.zeros(n, dtype=np.uint32)
+    ok = np.zeros(n, dtype=np.uint8)
+    fp.fp_req_mag_n(av.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)), which,
+                    q.ctypes.data_as(P(ctypes.c_uint32)), ok.ctypes.data_as(P(ctypes.c_uint8)), n)
+    exact = np.zeros(n, dtype=np.int64)
+    fp.fp_req_exact_n(av.ctypes.data_as(P(ctypes.c_int64)), den.ctypes.data_as(P(ctypes.c_int64)),
+                      exact.ctypes.data_as(P(ctypes.c_int64)), n)
+    return q.astype(np.int64), ok.astype(bool), exact
+
+
+def _near_integer_cases(rng, n):
+    """(av, den) whose quotient t = (av·2^28 + floor(den/2)) / den lies within a few 1/den of an integer, from both
+    sides: for odd den, av = (delta - floor(den/2)) · 2^-28 mod den puts the numerator at delta mod den."""
+    av, den = [], []
+    for _ in range(n):
+        e = int(rng.integers(22, 52))
+        d = int(rng.integers(1 << e, min(1 << (e + 1), 1 << 52))) | 1
+        delta = int(rng.choice([0, 1, 2, 3, -1, -2, -3]))
+        a = ((delta - d // 2) * pow(1 << 28, -1, d)) % d
+        av.append(a)
+        den.append(d)
+    return np.array(av, dtype=np.int64), np.array(den, dtype=np.int64)
+
+
+@pytest.mark.parametrize("which", [1, 2])
+def test_certified_magnitude_requant_is_exact_or_declines(fp, which):
+    """req_mag / req_mag2 (the lean SwiGLU, combine and down-input paths; the same source the kernels compile, with
+    the device's fused multiply-add and round-down add taken from the host's IEEE operations) either certify the exact
+    floor((|v|·2^28 + floor(den/2)) / den) or decline, for every divisor the lean paths admit (2^22 <= den < 2^52,
+    |v| <= den): random magnitudes decline about once in 10^5, quotients placed on and next to integers always
+    decline or are exact, and the ends |v| = 0 and |v| = den are exact."""
+    rng = np.random.default_rng(28 + which)
+    n = 400_000
+    e = rng.integers(22, 52, size=n)
+    den = np.minimum((rng.random(n) + 1.0) * np.exp2(e), float((1 << 52) - 1)).astype(np.int64)
+    av = (rng.random(n) * den).astype(np.int64)
+    av = np.minimum(av, den)
+    q, ok, exact = _req_mag(fp, av, den, which)
+    assert (q[ok] == exact[ok]).all()
+    assert (~ok).sum() <= 20  # the near-integer band is 2^-20 wide: about 0.4 expected in 400 000
+
+    av2, den2 = _near_integer_cases(rng, 20_000)
+    q2, ok2, exact2 = _req_mag(fp, av2, den2, which)
+    assert (q2[ok2] == exact2[ok2]).all()
+    assert (~ok2).mean() > 0.9  # t within 3/den of an integer: far inside the band the certificate refuses
+
+    ends_den = np.array([1 << 22, (1 << 22) + 1, 3 << 30, (1 << 52) - 1] * 2, dtype=np.int64)
+    ends_av = np.concatenate([np.zeros(4, dtype=np.int64), ends_den[:4]])
+    q3, ok3, exact3 = _req_mag(fp, ends_av, ends_den, which)
+    assert ok3.all() and (q3 == exact3).all()
+    assert (exact3[4:] == 1 << 28).all()
+
+
+def test_lean_down_code_equals_quant_to_act_for_every_magnitude(fp):
+    """The lean paths quantise the down linear's input as (q·WLEVELS + 2^27) >> 28 on |requant| = q, then apply the
+    sign; for all 2^28 + 1 magnitudes that equals quant_to_act (layers.rs:23-31 with xmax = 2^28)."""
+    assert fp.fp_down_code_mismatches() == 0

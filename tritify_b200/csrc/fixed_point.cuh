@@ -317,6 +317,64 @@ KT_HD int32_t requant_act(int64_t v, int64_t den) {
     return (int32_t)r;
 }
 
+// ───── one-rounding double operations ─────
+// The device's own IEEE operations (fused multiply-add, an add rounded toward minus infinity, the low word of a
+// double); host builds (the tests' harness) get the same results from the C library's fma, a round-to-nearest sum
+// stepped down one ulp when its exact error (TwoSum, no multiplications) shows it rounded up, and a bit copy.
+KT_HD double fma_rn(double a, double b, double c) {
+#ifdef __CUDA_ARCH__
+    return __fma_rn(a, b, c);
+#else
+    return __builtin_fma(a, b, c);
+#endif
+}
+
+KT_HD double add_rd(double a, double b) {
+#ifdef __CUDA_ARCH__
+    return __dadd_rd(a, b);
+#else
+    const double s = a + b, bb = s - a, err = (a - (s - bb)) + (b - bb);
+    return err < 0 ? __builtin_nextafter(s, -__builtin_inf()) : s;
+#endif
+}
+
+KT_HD uint32_t lo_word(double x) {
+#ifdef __CUDA_ARCH__
+    return (uint32_t)__double2loint(x);
+#else
+    uint64_t u;
+    __builtin_memcpy(&u, &x, sizeof(u));
+    return (uint32_t)u;
+#endif
+}
+
+// ───── certified requant of a magnitude (the lean element paths) ─────
+constexpr double RQ_MAGIC = 6755399441055744.0;  // 1.5·2^52: an add rounded down leaves floor(y) in the low bits
+constexpr double RQ_EPS = 4.76837158203125e-07;  // 2^-21
+
+// floor(av·inv + 1/2) for 0 <= av <= den < 2^52 with inv = RN(2^28/den) and den >= 2^22: the one-rounding FMA is within
+// 2^-25 + 2^-25 + 1/(2·den) < 2^-22 of t = (av·2^28 + floor(den/2))/den (the bound of requant_row's double path,
+// tightened by the fused multiply-add), and t is a multiple of 1/den, so y further than 2^-21 from an integer has
+// t's floor. Returns false (q unusable) otherwise.
+KT_HD bool req_mag(double av, double inv, uint32_t& q) {
+    const double y = fma_rn(av, inv, 0.5);
+    const double m = add_rd(y, RQ_MAGIC);
+    q = lo_word(m);
+    const double fr = y - (m - RQ_MAGIC);
+    return __builtin_fabs(fr - 0.5) < 0.5 - RQ_EPS;
+}
+
+// The same floor as req_mag from two one-rounding estimates 2^-21 below and above: z = av·inv is within 2^-25 of
+// av·2^28/den, and t lies in [z + 1/2 - 2^-25 - 1/(2·den), z + 1/2 + 2^-25]; RN(z + 1/2 ∓ 2^-21) err by at most 2^-25,
+// so the low estimate is below t and the high one above it, and equal floors (read from the low words after an add
+// of 1.5·2^52 rounded down) certify floor(t). One FMA and one add fewer than req_mag's test of the fraction.
+KT_HD bool req_mag2(double av, double inv, uint32_t& q) {
+    const double lo = add_rd(fma_rn(av, inv, 0.5 - RQ_EPS), RQ_MAGIC);
+    const double hi = add_rd(fma_rn(av, inv, 0.5 + RQ_EPS), RQ_MAGIC);
+    q = lo_word(lo);
+    return lo_word(lo) == lo_word(hi);
+}
+
 // ───── per-row plans for the hot loops ─────
 // floor(y) for 0 <= y < 2^31 as a double and as an integer. On the device one add rounded toward minus infinity
 // of 1.5·2^52 leaves floor(y) in the low mantissa bits (FP64 pipe only, no conversion instruction).

@@ -589,20 +589,8 @@ struct SwigluScales {
 // tail keeps every code below 2^31, and the table's codes are held as int32. Every step is the exact arithmetic of
 // the general path, written for 32-bit registers where the plan's bounds allow; a certified estimate that lands too
 // near an integer falls back to the exact integer path for that element.
-constexpr double RQ_MAGIC = 6755399441055744.0;    // 1.5·2^52: an add rounded down leaves floor(y) in the low bits
-constexpr double RQ_EPS = 4.76837158203125e-07;    // 2^-21
-
-// floor(av·inv + 1/2) for 0 <= av <= den < 2^52 with inv = RN(2^28/den) and den >= 2^22: the one-rounding FMA is within
-// 2^-25 + 2^-25 + 1/(2·den) < 2^-22 of t = (av·2^28 + floor(den/2))/den (the bound of kt::requant_row's double path,
-// tightened by the fused multiply-add), and t is a multiple of 1/den, so y further than 2^-21 from an integer has
-// t's floor. Returns false (q unusable) otherwise.
-__device__ __forceinline__ bool req_mag(double av, double inv, uint32_t& q) {
-    const double y = __fma_rn(av, inv, 0.5);
-    const double m = __dadd_rd(y, RQ_MAGIC);
-    q = (uint32_t)__double2loint(m);
-    const double fr = y - (m - RQ_MAGIC);
-    return fabs(fr - 0.5) < 0.5 - RQ_EPS;
-}
+using kt::req_mag;   // the certified requant of a magnitude (fixed_point.cuh, where the host tests also reach it)
+using kt::req_mag2;
 
 __device__ __forceinline__ bool swiglu_fast_ok(const SwigluScales& q, const Lut& silu) {
     if (!(q.mg > 0 && q.mu > 0 && q.rg.dbl && q.ru.dbl && q.is.tight && q.idf.tight && silu.codes32)) return false;
@@ -633,17 +621,6 @@ __device__ __forceinline__ int64_t swiglu_h_fast(const SwigluScales& q, const in
     else if (idx >= LUT_N)
         c = (int32_t)kt::apply_row(q.idf, g);  // identity right tail, in code units (< 2^31 by the plan)
     return (int64_t)c * (int64_t)u;
-}
-
-// The same floor as req_mag from two one-rounding estimates 2^-21 below and above: z = av·inv is within 2^-25 of
-// av·2^28/den, and t lies in [z + 1/2 - 2^-25 - 1/(2·den), z + 1/2 + 2^-25]; RN(z + 1/2 ∓ 2^-21) err by at most 2^-25,
-// so the low estimate is below t and the high one above it, and equal floors (read from the low words after an add
-// of 1.5·2^52 rounded down) certify floor(t). One FMA and one add fewer than req_mag's test of the fraction.
-__device__ __forceinline__ bool req_mag2(double av, double inv, uint32_t& q) {
-    const double lo = __dadd_rd(__fma_rn(av, inv, 0.5 - RQ_EPS), RQ_MAGIC);
-    const double hi = __dadd_rd(__fma_rn(av, inv, 0.5 + RQ_EPS), RQ_MAGIC);
-    q = (uint32_t)__double2loint(lo);
-    return __double2loint(lo) == __double2loint(hi);
 }
 
 // swiglu_h_fast with magnitudes and signs kept apart: g is never formed as a signed value (the SiLU index needs
