@@ -90,3 +90,17 @@ def test_norm_codes_and_eps_equal_the_references_quantiser(oracle):
     assert (q.w_codes.reshape(-1) == wc).all() and (q.w_scale.mant, q.w_scale.shift) == ws
     e = tb.scale_from_f64(1e-6)
     assert (e.mant, e.shift) == es
+
+
+def test_portable_generator_on_the_host_equals_the_oracle(oracle):
+    """The portable N(0, sigma) stream that the stack workloads generate on the GPU: the library's host form
+    (ktmoe_synth_normal_portable) equals the oracle's restatement bit for bit, at any offset, and a window read at an
+    offset equals the same elements of a longer read."""
+    for seed, sigma, n, off in [(1, 0.02, 4097, 0), (3, 1.0, 1 << 16, 12345), (7, 0.02, 1000, (1 << 33) + 5)]:
+        a = tb.synth_normal_portable(seed, sigma, n, off)
+        b = oracle.synth_normal_portable(seed, sigma, n, off)
+        assert a.dtype == np.float32 and (a.view("u4") == b.view("u4")).all()
+    long = tb.synth_normal_portable(11, 1.0, 5000, 100)
+    assert (tb.synth_normal_portable(11, 1.0, 1000, 2100).view("u4") == long[2000:3000].view("u4")).all()
+    big = tb.synth_normal_portable(13, 1.0, 1 << 20)
+    assert abs(float(big.mean())) < 5e-3 and abs(float(big.std()) - 1.0) < 5e-3
