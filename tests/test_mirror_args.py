@@ -1,0 +1,68 @@
+"""The Python mirror of the reference's operators refuses what the reference asserts against, with the reference's
+messages, before anything reaches a device (so these run on the CPU): layers.rs:226 and :248 (QuantLinear weights and
+bias lengths), :591-592 (SwiGluMlp shapes), :680-681 and :699 (MoeMlp top_k and router width), :736 (one selection
+bias per expert), :990 (MoE input a multiple of dim). The reference panics; the mirror raises ValueError."""
+
+import numpy as np
+import pytest
+
+import tritify_b200 as tb
+
+
+def _lin(name, out_f, in_f, seed=1):
+    return tb.QuantLinear.from_weights(name, tb.synth_normal(seed, 0.02, out_f * in_f), out_f, in_f)
+
+
+def _expert(d, f, seed):
+    return tb.SwiGluMlp(f"e{seed}", _lin("g", f, d, seed), _lin("u", f, d, seed + 1), _lin("d", d, f, seed + 2))
+
+
+def test_quant_linear_lengths():
+    with pytest.raises(ValueError, match="weights are not out·in"):
+        tb.QuantLinear.from_weights("w", np.zeros(7, np.float32), 2, 4)
+    q = _lin("r", 4, 8)
+    with pytest.raises(ValueError, match="r: bias len mismatch"):
+        q.with_bias(np.ones(3, np.float32))
+    assert q.with_bias(None) is q
+
+
+def test_swiglu_shapes():
+    d, f = 8, 4
+    with pytest.raises(ValueError, match="gate/up hidden mismatch"):
+        tb.SwiGluMlp("s", _lin("g", f, d), _lin("u", f + 1, d), _lin("d", d, f))
+    with pytest.raises(ValueError, match="down input != hidden"):
+        tb.SwiGluMlp("s", _lin("g", f, d), _lin("u", f, d), _lin("d", d, f + 1))
+
+
+def test_moe_top_k_router_width_and_selection_bias():
+    d, f, E = 8, 4, 3
+    experts = [_expert(d, f, 10 * i) for i in range(E)]
+    router = _lin("router", E, d)
+    for k in (0, E + 1):
+        with pytest.raises(ValueError, match=r"top_k in 1\.\.=E"):
+            tb.MoeMlp("m", router, experts, k)
+        with pytest.raises(ValueError, match=r"top_k in 1\.\.=E"):
+            tb.MoeMlp.remote("m", router, k)
+    with pytest.raises(ValueError, match="router out_features != number of experts"):
+        tb.MoeMlp("m", _lin("router", E + 1, d), experts, 2)
+    m = tb.MoeMlp("m", router, experts, 2)
+    with pytest.raises(ValueError, match="m: one selection bias per expert"):
+        m.with_sigmoid_router(np.zeros(E + 1, np.float32))
+    with pytest.raises(ValueError, match="with_shared_expert_gate needs a shared expert"):
+        m.with_shared_expert_gate(_lin("sg", 1, d))
+    m.with_shared_expert(_expert(d, f, 99))
+    with pytest.raises(ValueError, match=r"the shared-expert gate is a \[1, dim\] linear"):
+        m.with_shared_expert_gate(_lin("sg", 2, d))
+
+
+def test_moe_input_must_be_rows_of_dim():
+    d, f, E = 8, 4, 2
+    m = tb.MoeMlp("m", _lin("router", E, d), [_expert(d, f, 3), _expert(d, f, 7)], 1)
+    x = tb.IntTensor(np.zeros(d + 1, np.int32), (d + 1,), tb.Scale.ZERO)
+    with pytest.raises(ValueError, match="m: MoE input length must be a multiple of dim"):
+        m.forward_int(x)
+    with pytest.raises(ValueError, match="m: MoE input length must be a multiple of dim"):
+        m.forward_int_with_experts(x, lambda ids, row: [])
+    r = tb.MoeMlp.remote("m", _lin("router", E, d), 1)
+    with pytest.raises(RuntimeError, match="the routed experts are remote"):
+        r.forward_int(tb.IntTensor(np.zeros(d, np.int32), (d,), tb.Scale.ZERO))
