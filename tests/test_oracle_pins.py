@@ -223,3 +223,59 @@ def test_token_parallel_forward_equals_the_serial_forward(oracle):
         m = cases.build_oracle(c, oracle)
         a, b = m.forward(xi, xs), m.forward_par(xi, xs, 3)
         assert (a[0] == b[0]).all() and a[1] == b[1], name
+
+
+def test_the_selection_bias_moves_the_choice_but_not_the_weights(oracle):
+    """tests_glm.rs:178-199 (kt-core): with a sigmoid router, a selection bias larger than any sigma difference puts
+    an expert the unbiased route left out into the top-k; every chosen expert's weight is still its sigma code
+    without the bias (CodeLut::index, clamped read); with norm_topk_prob the weights' sum is sumc, without it sumc is
+    2^20 (the raw scores)."""
+    d, E, f, k = 32, 16, 8, 4
+    rng = np.random.default_rng(0x53)
+    router_w = (rng.standard_normal((E, d)) * 0.5).astype(np.float32)
+    experts = (rng.standard_normal(E * 3 * f * d) * 0.02).astype(np.float32)
+    xi, xs = oracle.from_reals_f32(rng.standard_normal((1, d)).astype(np.float32))
+
+    def moe(bias, norm):
+        return oracle.MoeOracle(d, E, f, k, router_w, experts, norm_topk=norm, sigmoid_bias=bias)
+
+    plain = moe(np.zeros(E, np.float32), True)
+    ex0, _, _ = plain.route(xi, xs)
+    outsider = next(e for e in range(E) if e not in set(ex0[0].tolist()))
+    b = np.zeros(E, np.float32)
+    b[outsider] = 1.5
+    ex1, ec1, sumc1 = moe(b, True).route(xi, xs)
+    assert outsider in ex1[0].tolist(), "the bias must move the choice"
+    logits, ls = plain.router_logits(xi, xs)
+    codes = oracle.table(2)[0]
+    for e, c in zip(ex1[0].tolist(), ec1[0].tolist()):
+        idx = oracle.table_index(2, int(logits[0, e]), ls[0])
+        assert c == int(codes[min(max(idx, 0), len(codes) - 1)]), f"expert {e}: its weight is its sigma code"
+    assert sumc1[0] == ec1[0].sum()
+    _, _, sumc2 = moe(b, False).route(xi, xs)
+    assert sumc2[0] == 1 << 20
+
+
+def test_sigmoid_codes_track_the_float_sigmoid_and_clamp(oracle):
+    """tests_glm.rs:137-154 (kt-core): a logit's sigma code (CodeLut over [-16, 16] with 2^16 entries, clamped read)
+    is within one table step of sigma(real)·2^20 (sigma' <= 1/4, so one step moves the code by at most step/4·2^20,
+    plus one for the index's rounding), and past the table the codes are 0 and 2^20."""
+    import math
+
+    k = float(1 << 20)
+    step = 2.0 * 16.0 / ((1 << 16) - 1)
+    scale = oracle.from_f64(1.0 / 4096.0)
+    codes = oracle.table(2)[0]
+
+    def code(v, s):
+        return int(codes[min(max(oracle.table_index(2, v, s), 0), len(codes) - 1)])
+
+    for l in range(-80_000, 80_001, 997):
+        for v in (l, -l, 0, int(l / 3)):
+            c = code(v, scale)
+            real = v / 4096.0
+            want = k / (1.0 + math.exp(-real))
+            assert abs(c - want) <= step / 4.0 * k + 1.0, (real, c, want)
+            assert 0 <= c <= 1 << 20
+    one = oracle.from_f64(1.0)
+    assert (code(-(1 << 20), one), code(1 << 20, one)) == (0, 1 << 20)
