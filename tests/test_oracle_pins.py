@@ -279,3 +279,81 @@ def test_sigmoid_codes_track_the_float_sigmoid_and_clamp(oracle):
             assert 0 <= c <= 1 << 20
     one = oracle.from_f64(1.0)
     assert (code(-(1 << 20), one), code(1 << 20, one)) == (0, 1 << 20)
+
+
+# ── the reference's float-tracking tests (kt-core tests.rs), on their own inputs ──
+def _ref_uniforms(seed, n):
+    """tests.rs:15-24: the test LCG and unif = ((s >> 40) / 2^24 · 2 - 1) as f32, n draws after `seed`; returns the
+    values and the state."""
+    s, out = seed, np.empty(n, np.float32)
+    for i in range(n):
+        s = (s * 6364136223846793005 + 1442695040888963407) & ((1 << 64) - 1)
+        out[i] = np.float32((s >> 40) / float(1 << 24) * 2.0 - 1.0)
+    return out, s
+
+
+def _real(scale):
+    return scale[0] * 2.0 ** (-scale[1])
+
+
+def _linear_ref(x, codes, ws):
+    """QuantLinear::forward_ref (layers.rs:330-348): f64 sums of x·(code·w_scale), cast to f32."""
+    return (x.astype(np.float64) @ (codes.astype(np.float64) * _real(ws)).T).astype(np.float32)
+
+
+def _swiglu_ref(x, g, u, dn):
+    """SwiGluMlp::forward_ref (layers.rs:642-648)."""
+    gf, uf = _linear_ref(x, *g).astype(np.float64), _linear_ref(x, *u).astype(np.float64)
+    act = (gf / (1.0 + np.exp(-gf)) * uf).astype(np.float32)
+    return _linear_ref(act, *dn)
+
+
+def test_swiglu_tracks_float_like_the_reference(oracle):
+    """tests.rs:94-111 (swiglu_tracks_float_and_is_deterministic): dim 64, hidden 128, the test LCG at 0x9999 for the
+    gate, up and down weights and the probe; the integer SwiGLU is deterministic and within 2% of the float path's
+    peak."""
+    dim, hidden = 64, 128
+    w, s = _ref_uniforms(0x9999, 3 * hidden * dim)
+    p, _ = _ref_uniforms(s, dim)
+    m = oracle.MoeOracle(dim, 1, hidden, 1, np.zeros((1, dim), np.float32), w)
+    xi, xs = oracle.from_reals_f32(p)
+    y, ys = m.expert(0, xi.reshape(-1), xs)
+    y2, ys2 = m.expert(0, xi.reshape(-1), xs)
+    assert (y == y2).all() and ys == ys2
+    x = (xi.reshape(1, dim).astype(np.float64) * _real(xs)).astype(np.float32)
+    ref = _swiglu_ref(x, m.weights(1), m.weights(2), m.weights(3)).reshape(-1)
+    got = y.astype(np.float64) * _real(ys)
+    assert np.abs(got - ref).max() <= np.abs(ref).max() * 2e-2
+
+
+def test_moe_tracks_float_without_a_routing_flip_like_the_reference(oracle):
+    """tests.rs:113-154 (moe_mlp_tracks_float_sparse_and_deterministic): dim 64, hidden 96, 8 experts, top-2, softmax
+    router normalised over all experts, weights and probe from the test LCG at 0x30E1; the integer and float routers
+    choose the same experts, the integer layer is deterministic and within 3% of MoeMlp::forward_ref's peak."""
+    dim, hidden, E, k = 64, 96, 8, 2
+    vals, s = _ref_uniforms(0x30E1, E * dim + E * 3 * hidden * dim)
+    p, _ = _ref_uniforms(s, dim)
+    router_w, experts = vals[:E * dim], vals[E * dim:]
+    m = oracle.MoeOracle(dim, E, hidden, k, router_w, experts)
+    xi, xs = oracle.from_reals_f32(p)
+    y, ys = m.forward(xi, xs)
+    y2, ys2 = m.forward(xi, xs)
+    assert (y == y2).all() and ys == ys2
+
+    x = (xi.reshape(1, dim).astype(np.float64) * _real(xs)).astype(np.float32)
+    logits = _linear_ref(x, *m.weights(0))[0]
+    order = sorted(range(E), key=lambda e: (-float(logits[e]), e))[:k]
+    li, _ = m.router_logits(xi, xs)
+    order_int = sorted(range(E), key=lambda e: (-int(li[0, e]), e))[:k]
+    assert order == order_int, "a routing flip between the integer and the float router"
+    ex, _, _ = m.route(xi, xs)
+    assert ex[0].tolist() == order_int
+
+    exps = np.exp((logits - logits.max()).astype(np.float64))
+    out = np.zeros(dim)
+    for e in order:
+        ye = _swiglu_ref(x, m.weights(1, e), m.weights(2, e), m.weights(3, e))[0]
+        out += exps[e] / exps.sum() * ye.astype(np.float64)
+    ref = out.astype(np.float32)
+    got = y.reshape(-1).astype(np.float64) * _real(ys)
+    assert np.abs(got - ref).max() <= np.abs(ref).max() * 3e-2
