@@ -188,6 +188,12 @@ int ktmoe_scale_from_f64(double x, ktmoe_scale* out);
 /* MoeMlp::route for each row: experts [rows][top_k] (top-k order), ec [rows][top_k] codes, sumc [rows]. */
 int ktmoe_route(ktmoe_layer* layer, const int32_t* x, int64_t rows, ktmoe_scale x_scale, int32_t* experts,
                 int64_t* ec, int64_t* sumc);
+/* MoeRoute::margin (layers.rs:816-820, computed at :844-848) of softmax routes, on the host: from each row's router
+ * logits [rows][n_experts] (ktmoe_layer_debug_fetch 0 after ktmoe_route), their scales [rows] (fetch 1) and the
+ * route's experts [rows][top_k], margins[r] = the strongest excluded expert's exp code over the weakest selected
+ * one's, 0 when that is 0. A read-only diagnostic of how decisive each cut is; a sigmoid route's margin is 0. */
+int ktmoe_route_margins(const int32_t* logits, int64_t rows, int32_t n_experts, const ktmoe_scale* scales,
+                        const int32_t* experts, int32_t top_k, double* margins);
 /* ── the expert-parallel seam: MoeMlp::forward_int_with_experts (layers.rs:945-984) with the experts elsewhere ──
  * A layer whose routed experts live on other hosts (MoeMlp::remote, layers.rs:694-712) routes, combines, merges and
  * adds its shared expert here, and gets the expert outputs through a callback; a worker holding experts computes

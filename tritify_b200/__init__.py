@@ -28,6 +28,7 @@ from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 __all__ = [
     "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
     "B200Linear", "Context", "DeviceLayer", "LayerSlot", "MoeStack", "device_count", "synth_normal", "synth_normal_portable", "lcg_uniform", "table",
+    "route_margins",
     "KtmoeError",
     "ep_unique_id",
 ]
@@ -279,11 +280,29 @@ class SwiGluMlp:
 
 @dataclass
 class MoeRoute:
-    """MoeRoute (layers.rs:812-821): the selected experts in top-k order, their codes and the normaliser."""
+    """MoeRoute (layers.rs:812-821): the selected experts in top-k order, their codes, the normaliser and the
+    boundary margin (the strongest excluded expert's exp code over the weakest selected one's, in (0, 1]; 0 for a
+    sigmoid router or a zero weakest code): a read-only diagnostic of how decisive the cut is."""
 
     experts: List[int]
     ec: List[int]
     sumc: int
+    margin: float = 0.0
+
+
+def route_margins(logits: np.ndarray, scales: Sequence["Scale"], experts: np.ndarray) -> np.ndarray:
+    """MoeRoute::margin of softmax routes (ktmoe_route_margins, on the host): router logits [rows][E] with their
+    per-row scales and the routes' experts [rows][k] -> margins [rows]."""
+    lg = np.ascontiguousarray(logits, dtype=np.int32)
+    ex = np.ascontiguousarray(experts, dtype=np.int32)
+    rows, n_experts = lg.shape
+    if ex.shape[0] != rows or len(scales) != rows:
+        raise ValueError("route_margins: one scale and one route per row of logits")
+    sc = (KtmoeScale * max(rows, 1))(*[s._c() for s in scales])
+    out = np.zeros(rows, dtype=np.float64)
+    check(lib().ktmoe_route_margins(_p(lg, ctypes.c_int32), rows, n_experts, sc, _p(ex, ctypes.c_int32),
+                                    ex.shape[1], _p(out, ctypes.c_double)))
+    return out
 
 
 class DeviceLayer:
@@ -566,7 +585,7 @@ class MoeMlp:
 
     def with_sigmoid_router(self, bias: np.ndarray) -> "MoeMlp":
         b = np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
-        if b.size != len(self.experts):
+        if b.size != self.n_experts():
             raise ValueError(f"{self.name}: one selection bias per expert")
         codes = np.empty(b.size, dtype=np.int64)
         check(lib().ktmoe_code_sigmoid_bias(_p(b, ctypes.c_float), b.size, _p(codes, ctypes.c_int64)))
@@ -673,10 +692,16 @@ class MoeMlp:
         return IntTensor(y, shape, ys)
 
     def route(self, x: IntTensor) -> List[MoeRoute]:
-        """MoeMlp::route (layers.rs:826-862) for each row of ``x``."""
+        """MoeMlp::route (layers.rs:826-862) for each row of ``x``; a softmax route's margin comes from the route's
+        router logits (fetched from the device) on the host."""
         rows = len(x) // self.dim
-        ex, ec, sumc = self.device_layer().route(x.data, rows, x.scale)
-        return [MoeRoute([int(v) for v in ex[t]], [int(v) for v in ec[t]], int(sumc[t])) for t in range(rows)]
+        dev = self.device_layer()
+        ex, ec, sumc = dev.route(x.data, rows, x.scale)
+        margins = np.zeros(rows)
+        if self.sigmoid_bias_codes is None and rows > 0:
+            margins = route_margins(dev.debug_fetch(0, rows), dev.debug_fetch(1, rows), ex)
+        return [MoeRoute([int(v) for v in ex[t]], [int(v) for v in ec[t]], int(sumc[t]), float(margins[t]))
+                for t in range(rows)]
 
     def route_trace(self, x: IntTensor) -> List[List[int]]:
         """Module::route_trace (layers.rs:1089-1100)."""

@@ -84,6 +84,7 @@ SIGNATURES = {
     "ktmoe_forward_dev": ([_vp, _vp, _i64, _vp, _vp, _vp, _vp], ctypes.c_int),
     "ktmoe_sync": ([_vp, _vp], ctypes.c_int),
     "ktmoe_route": ([_vp, _i32p, _i64, KtmoeScale, _i32p, _i64p, _i64p], ctypes.c_int),
+    "ktmoe_route_margins": ([_i32p, _i64, _i32, _P(KtmoeScale), _i32p, _i32, _P(ctypes.c_double)], ctypes.c_int),
     "ktmoe_launch_count": ([_vp, _P(_u64)], ctypes.c_int),
     "ktmoe_layer_debug_fetch": ([_vp, _i32, _vp, _i64], ctypes.c_int),
     "ktmoe_layer_set_timing": ([_vp, _i32], ctypes.c_int),

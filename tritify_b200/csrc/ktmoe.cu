@@ -3383,6 +3383,46 @@ int ktmoe_table(int32_t kind, int64_t* codes, ktmoe_scale* inv_step, int64_t* lo
     return KTMOE_OK;
 }
 
+// MoeRoute::margin of softmax routes (layers.rs:831-849): per row, every expert's exp code (CodeLut::index of
+// logit - lmax at the row's logit scale, layers.rs:837-838: 0 below the table, the clamped code above it), then the
+// strongest code left out of the route over the weakest chosen one, 0 when that is 0. Host only, exact integers up
+// to the final division.
+int ktmoe_route_margins(const int32_t* logits, int64_t rows, int32_t n_experts, const ktmoe_scale* scales,
+                        const int32_t* experts, int32_t top_k, double* margins) {
+    if (rows < 0 || n_experts <= 0 || top_k <= 0 || top_k > n_experts) return KTMOE_ERR_ARG;
+    if (rows > 0 && (!logits || !scales || !experts || !margins)) return KTMOE_ERR_ARG;
+    static const hp::HTable t = [] {
+        hp::HTable x;
+        hp::build_table(0, &x);
+        return x;
+    }();
+    const int64_t n = (int64_t)t.codes.size();
+    std::vector<int64_t> ecs(n_experts);
+    std::vector<char> chosen(n_experts);
+    for (int64_t r = 0; r < rows; ++r) {
+        const int32_t* lg = logits + r * n_experts;
+        int32_t lmax = INT32_MIN;
+        for (int32_t j = 0; j < n_experts; ++j) lmax = std::max(lmax, lg[j]);
+        const Scale s = kt::scale_mul(S(scales[r]), S(t.inv_step));
+        for (int32_t j = 0; j < n_experts; ++j) {
+            const int64_t idx = kt::scale_apply(s, (int64_t)lg[j] - lmax) - t.lo_index;
+            ecs[j] = idx < 0 ? 0 : t.codes[(size_t)std::min(idx, n - 1)];
+        }
+        std::fill(chosen.begin(), chosen.end(), 0);
+        int64_t weakest = INT64_MAX, strongest = 0;
+        for (int32_t i = 0; i < top_k; ++i) {
+            const int32_t e = experts[r * top_k + i];
+            if (e < 0 || e >= n_experts) return KTMOE_ERR_ARG;
+            chosen[e] = 1;
+            weakest = std::min(weakest, ecs[e]);
+        }
+        for (int32_t j = 0; j < n_experts; ++j)
+            if (!chosen[j]) strongest = std::max(strongest, ecs[j]);
+        margins[r] = weakest > 0 ? (double)strongest / (double)weakest : 0.0;
+    }
+    return KTMOE_OK;
+}
+
 int ktmoe_synth_normal(uint64_t seed, float sigma, uint64_t offset, int64_t n, float* out) {
     if (n < 0 || (n > 0 && !out)) return KTMOE_ERR_ARG;
     hp::synth_normal(seed, sigma, offset, (size_t)n, out);
