@@ -66,3 +66,14 @@ def test_moe_input_must_be_rows_of_dim():
     r = tb.MoeMlp.remote("m", _lin("router", E, d), 1)
     with pytest.raises(RuntimeError, match="the routed experts are remote"):
         r.forward_int(tb.IntTensor(np.zeros(d, np.int32), (d,), tb.Scale.ZERO))
+
+
+def test_a_remote_layer_takes_one_selection_bias_per_router_output():
+    """layers.rs:736 compares the bias with n_experts() (the router's width), so a router-only layer whose experts
+    are elsewhere takes a sigmoid router too."""
+    d, E = 8, 6
+    r = tb.MoeMlp.remote("r", _lin("router", E, d), 2)
+    r.with_sigmoid_router(np.zeros(E, np.float32))
+    assert r.sigmoid_bias_codes is not None and r.sigmoid_bias_codes.size == E
+    with pytest.raises(ValueError, match="r: one selection bias per expert"):
+        tb.MoeMlp.remote("r", _lin("router", E, d), 2).with_sigmoid_router(np.zeros(E - 1, np.float32))
