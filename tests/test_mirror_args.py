@@ -77,3 +77,20 @@ def test_a_remote_layer_takes_one_selection_bias_per_router_output():
     assert r.sigmoid_bias_codes is not None and r.sigmoid_bias_codes.size == E
     with pytest.raises(ValueError, match="r: one selection bias per expert"):
         tb.MoeMlp.remote("r", _lin("router", E, d), 2).with_sigmoid_router(np.zeros(E - 1, np.float32))
+
+
+def test_router_score_shared_expert_and_router_codes(oracle):
+    """MoeMlp::router_score / shared_expert / router_codes (layers.rs:747-755, :784-788) on the mirror: the score
+    function and its coded bias, the shared expert as set, and the router's exp code table (the oracle's, read-only)."""
+    d, f, E = 8, 4, 3
+    m = tb.MoeMlp("m", _lin("router", E, d), [_expert(d, f, 10 * i) for i in range(E)], 2)
+    assert m.router_score().kind == "softmax" and m.router_score().bias_codes is None
+    assert m.shared_expert() is None
+    b = np.array([0.5, -0.25, 0.0], np.float32)
+    m.with_sigmoid_router(b)
+    sc = m.router_score()
+    assert sc.kind == "sigmoid" and sc.bias_codes.tolist() == [1 << 19, -(1 << 18), 0]
+    s = _expert(d, f, 77)
+    assert m.with_shared_expert(s).shared_expert() is s
+    codes = m.router_codes()
+    assert (codes == oracle.table(0)[0]).all() and not codes.flags.writeable

@@ -26,7 +26,7 @@ from . import _native
 from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 
 __all__ = [
-    "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute",
+    "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute", "RouterScore",
     "B200Linear", "Context", "DeviceLayer", "LayerSlot", "MoeStack", "device_count", "synth_normal", "synth_normal_portable", "lcg_uniform", "table",
     "route_margins",
     "KtmoeError",
@@ -288,6 +288,15 @@ class MoeRoute:
     ec: List[int]
     sumc: int
     margin: float = 0.0
+
+
+@dataclass
+class RouterScore:
+    """RouterScore (router.rs:21-26, the router's score function): ``kind`` "softmax" or "sigmoid"; a sigmoid router
+    carries its selection bias coded as round(b·2^20) (SigmoidScore::new, router.rs:37-51)."""
+
+    kind: str
+    bias_codes: Optional[np.ndarray]
 
 
 def route_margins(logits: np.ndarray, scales: Sequence["Scale"], experts: np.ndarray) -> np.ndarray:
@@ -619,6 +628,23 @@ class MoeMlp:
 
     def is_remote(self) -> bool:
         return not self.experts
+
+    def router_score(self) -> "RouterScore":
+        """MoeMlp::router_score (layers.rs:747-750): softmax, or sigmoid with the coded selection bias."""
+        if self.sigmoid_bias_codes is None:
+            return RouterScore("softmax", None)
+        return RouterScore("sigmoid", self.sigmoid_bias_codes.copy())
+
+    def shared_expert(self) -> Optional[SwiGluMlp]:
+        """MoeMlp::shared_expert (layers.rs:752-755)."""
+        return self.shared
+
+    def router_codes(self) -> np.ndarray:
+        """MoeMlp::router_codes (layers.rs:784-788): the router's softmax code table (read-only); every routing code
+        is one of its entries or 0."""
+        codes = table(0)[0]
+        codes.setflags(write=False)
+        return codes
 
     def device_layer(self) -> DeviceLayer:
         if self._dev is None:
