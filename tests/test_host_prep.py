@@ -104,3 +104,17 @@ def test_portable_generator_on_the_host_equals_the_oracle(oracle):
     assert (tb.synth_normal_portable(11, 1.0, 1000, 2100).view("u4") == long[2000:3000].view("u4")).all()
     big = tb.synth_normal_portable(13, 1.0, 1 << 20)
     assert abs(float(big.mean())) < 5e-3 and abs(float(big.std()) - 1.0) < 5e-3
+
+
+def test_int_tensor_helpers_follow_the_reference(oracle):
+    """IntTensor::vector / is_empty / max_abs_data / to_f32 / quantize_probe (tensor.rs:22-49, :119-123) on the
+    mirror; quantize_probe is from_reals of the f32 values (the oracle's entry quantiser)."""
+    v = tb.IntTensor.vector(np.array([3, -7, 2], np.int32), tb.Scale(3, 2))
+    assert v.shape == (3,) and not v.is_empty() and v.max_abs_data() == 7
+    assert v.to_f32().tolist() == [2.25, -5.25, 1.5]
+    assert tb.IntTensor.vector(np.zeros(0, np.int32), tb.Scale.ZERO).is_empty()
+    assert tb.IntTensor.vector(np.array([-(2 ** 31)], np.int32), tb.Scale(1, 0)).max_abs_data() == 2 ** 31
+    x = tb.synth_normal(21, 1.0, 257)
+    p = tb.IntTensor.quantize_probe(x)
+    xi, xs = oracle.from_reals_f32(x)
+    assert p.shape == (257,) and (p.data == xi.reshape(-1)).all() and (p.scale.mant, p.scale.shift) == xs

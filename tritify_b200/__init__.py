@@ -77,6 +77,28 @@ class IntTensor:
         return int(self.data.size)
 
     @staticmethod
+    def vector(data: np.ndarray, scale: Scale) -> "IntTensor":
+        """IntTensor::vector (tensor.rs:22-25): a 1-D tensor."""
+        d = np.ascontiguousarray(data, dtype=np.int32).reshape(-1)
+        return IntTensor(d, (d.size,), scale)
+
+    def is_empty(self) -> bool:
+        return self.data.size == 0
+
+    def max_abs_data(self) -> int:
+        """IntTensor::max_abs_data (tensor.rs:46-49): the largest |data| (0 when empty)."""
+        return int(np.abs(self.data.astype(np.int64)).max()) if self.data.size else 0
+
+    def to_f32(self) -> np.ndarray:
+        """IntTensor::to_f32 (tensor.rs:35-38): data · scale in f64, then rounded to f32."""
+        return (self.data.astype(np.float64) * self.scale.to_f64()).astype(np.float32)
+
+    @staticmethod
+    def quantize_probe(x: np.ndarray, levels: int = ACT_LEVELS) -> "IntTensor":
+        """IntTensor::quantize_probe (tensor.rs:119-123): from_reals of an f32 vector, 1-D."""
+        return IntTensor.from_reals(np.ascontiguousarray(x, dtype=np.float32).reshape(-1), levels)
+
+    @staticmethod
     def from_reals(values: np.ndarray, levels: int = ACT_LEVELS) -> "IntTensor":
         """IntTensor::from_reals (tensor.rs:106-116) at ACT_LEVELS, on f32 values."""
         if levels != ACT_LEVELS:
