@@ -118,3 +118,18 @@ def test_int_tensor_helpers_follow_the_reference(oracle):
     p = tb.IntTensor.quantize_probe(x)
     xi, xs = oracle.from_reals_f32(x)
     assert p.shape == (257,) and (p.data == xi.reshape(-1)).all() and (p.scale.mant, p.scale.shift) == xs
+
+
+def test_hash_int_and_repro_hash_are_the_reference_hashes():
+    """verify::hash_int (verify.rs:35-41) and repro.rs's logits_hash (kt-convert/src/repro.rs:34-42) on the mirror:
+    config 1's golden output hashes, and a scale change moves only the repro form."""
+    import cases
+
+    g = GOLDEN["cases"]["config1"]["x_int"]
+    t = tb.IntTensor.from_reals(cases.make_x(cases.CASES["config1"]))
+    assert tb.hash_int(t) == g["data_sha256"]
+    want = cases.out_hashes(t.data, t.scale)
+    assert tb.repro_hash(t) == want["repro_sha256"]
+    u = tb.IntTensor(t.data, t.shape, tb.Scale(t.scale.mant + 1, t.scale.shift))
+    assert tb.hash_int(u) == tb.hash_int(t) and tb.repro_hash(u) != tb.repro_hash(t)
+    assert tb.hash_int(tb.IntTensor.vector(np.zeros(0, np.int32), tb.Scale.ZERO)) == hashlib.sha256(b"").hexdigest()

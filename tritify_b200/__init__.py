@@ -16,6 +16,7 @@ reference's own offline f64 preparation (weight and entry quantisers, code table
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import threading
 from dataclasses import dataclass
 from typing import Callable, List, Optional, Sequence
@@ -28,7 +29,7 @@ from ._native import KtmoeError, KtmoeLayerConfig, KtmoeScale, check, lib
 __all__ = [
     "WLEVELS", "ACT_LEVELS", "ROUTER_CODE_BITS", "Scale", "IntTensor", "QuantLinear", "SwiGluMlp", "MoeMlp", "MoeRoute", "RouterScore",
     "B200Linear", "Context", "DeviceLayer", "LayerSlot", "MoeStack", "device_count", "synth_normal", "synth_normal_portable", "lcg_uniform", "table",
-    "route_margins",
+    "route_margins", "hash_int", "repro_hash",
     "KtmoeError",
     "ep_unique_id",
 ]
@@ -139,6 +140,22 @@ class IntTensor:
                                       data.size, ctypes.byref(used)))
         t = IntTensor(data, shape.tolist(), Scale._of(s))
         return (t, used.value) if with_length else t
+
+
+def hash_int(t: "IntTensor") -> str:
+    """verify::hash_int (verify.rs:35-41): SHA-256 of the tensor's i32 data, little-endian (the scale is not hashed),
+    as 64 hex digits: the reference's parity hash."""
+    return hashlib.sha256(np.ascontiguousarray(t.data, dtype="<i4").tobytes()).hexdigest()
+
+
+def repro_hash(t: "IntTensor") -> str:
+    """The repro form of the hash (logits_hash, kt-convert/src/repro.rs:34-42), which also binds the scale: SHA-256
+    of mant (i64 LE), shift (i32 LE) and the data (i32 LE)."""
+    h = hashlib.sha256()
+    h.update(np.int64(t.scale.mant).astype("<i8").tobytes())
+    h.update(np.int32(t.scale.shift).astype("<i4").tobytes())
+    h.update(np.ascontiguousarray(t.data, dtype="<i4").tobytes())
+    return h.hexdigest()
 
 
 def device_count() -> int:
