@@ -86,7 +86,8 @@ def test_tables_match_golden_and_end_codes(oracle):
 
 @pytest.mark.parametrize("name", ["tiny_softmax", "tiny_softmax_norm_one_row", "tiny_softmax_37rows",
                                   "tiny_router_bias", "tiny_sigmoid_shared", "tiny_sigmoid_raw_shared_one_row",
-                                  "small_shared_softmax"])
+                                  "small_shared_softmax", "tiny_odd_hidden", "tiny_gated_shared",
+                                  "tiny_gated_shared_one_row", "small_gated_shared"])
 def test_oracle_reproduces_golden_cases(oracle, name):
     import cases
 
@@ -357,3 +358,20 @@ def test_moe_tracks_float_without_a_routing_flip_like_the_reference(oracle):
     ref = out.astype(np.float32)
     got = y.reshape(-1).astype(np.float64) * _real(ys)
     assert np.abs(got - ref).max() <= np.abs(ref).max() * 3e-2
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name", ["config1", "config1_norm_topk"])
+def test_oracle_reproduces_the_config1_goldens(oracle, name):
+    """BASELINE config 1 (512 tokens, 64 experts of 1408, top-8) through the oracle's token-parallel forward (equal
+    to the serial one, test above) over every host core: the committed output and route hashes again."""
+    import cases
+
+    c = cases.CASES[name]
+    g = GOLDEN["cases"][name]
+    x = cases.make_x(c)
+    assert cases.sha(x) == g["x_f32_sha256"]
+    xi, xs = oracle.from_reals_f32(x)
+    m = cases.build_oracle(c, oracle)
+    y, ys = m.forward_par(xi, xs)
+    assert cases.out_hashes(y, ys) == g["output"]
