@@ -46,3 +46,18 @@ def test_linear_bench_shapes_are_the_references():
     x, w = bench.linear_bench_codes(tb.lcg_uniform, 1, 4864, 896)
     assert (x == tb.lcg_uniform(2, -tb.WLEVELS, tb.WLEVELS, 896)).all()
     assert (w[:5] == tb.lcg_uniform(4866, -tb.WLEVELS, tb.WLEVELS, 5)).all()
+
+
+def test_committed_goldens_describe_the_workloads_bench_runs():
+    """Every workload with a committed golden (tests/golden/bench_golden.json) still has the configuration the golden
+    was made for, so a bench line's parity verdict compares like with like."""
+    import json
+
+    g = json.load(open(os.path.join(ROOT, "tests", "golden", "bench_golden.json")))["workloads"]
+    assert {"mixtral_prefill", "glm_decode", "glm_prefill", "qwen_decode", "qwen_prefill", "config1"} <= set(g)
+    for name, rec in g.items():
+        w = bench.WORKLOADS[name]
+        cfg = bench.gemm_config(w, name) if w.get("gemm") else bench.workload_config(w, name)
+        assert cfg == rec["config"], name
+        if not w.get("gemm"):
+            assert (w["T"], w["E"]) == (rec["T"], rec["E"]), name
