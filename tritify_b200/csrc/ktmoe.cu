@@ -5,8 +5,9 @@
 // seam entry points for experts on other hosts, and the offline f64 preparation entry points. Device side:
 // digit_gemm.cuh and digit_gemm_pair.cuh (the tcgen05 digit-plane GEMMs, nine-plane and small-code), moe_kernels.cuh
 // (routing, dispatch, SwiGLU/requant, combine, merge, shared expert, RmsNorm, add). The activation wire format is in
-// wire.cpp. There is no CPU compute path: every result comes from the kernels in this library, and a context on a
-// device that is not sm_100 fails to open.
+// wire.cpp. There is no CPU compute path: every result comes from the kernels in this library (only the routes'
+// read-only margin diagnostic is worked out on the host, from logits the kernels produced), and a context on a device
+// that is not sm_100 fails to open.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
