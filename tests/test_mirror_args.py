@@ -94,3 +94,19 @@ def test_router_score_shared_expert_and_router_codes(oracle):
     assert m.with_shared_expert(s).shared_expert() is s
     codes = m.router_codes()
     assert (codes == oracle.table(0)[0]).all() and not codes.flags.writeable
+
+
+def test_a_stack_takes_layers_of_one_context_and_one_width():
+    """MoeStack (the block loop of model.rs:175-186 without attention) refuses an empty list and layers that do not
+    share one context and one d_model; the check reads only those two attributes, so stand-ins serve here."""
+    from types import SimpleNamespace as L
+
+    with pytest.raises(ValueError, match="a stack needs at least one layer"):
+        tb.MoeStack([])
+    c0, c1 = object(), object()
+    with pytest.raises(ValueError, match="share one context and one d_model"):
+        tb.MoeStack([L(ctx=c0, d_model=8), L(ctx=c0, d_model=16)])
+    with pytest.raises(ValueError, match="share one context and one d_model"):
+        tb.MoeStack([L(ctx=c0, d_model=8), L(ctx=c1, d_model=8)])
+    s = tb.MoeStack([L(ctx=c0, d_model=8), L(ctx=c0, d_model=8)])
+    assert len(s.layers) == 2 and s.d_model == 8 and s.ctx is c0
